@@ -1,0 +1,215 @@
+"""brian2-atlas_b200: B200 engine for Brian2 Atlas AtlasIR simulations.
+
+Host-side mirror of the reference's runner interface.  The reference frontend
+runs its engine as a subprocess (`b2-runner MODEL.json OUTDIR`,
+brian2-rust/python/brian2_rust/device.py:1316-1365); this package exposes the
+same operation in-process over the C ABI of lib/libb2gpu.so (include/b2gpu.h):
+
+    run_model(model_json_bytes, outdir)    # == b2-runner MODEL.json OUTDIR
+    Engine(model_json_bytes).step(ticks)    # == Runtime::new / Runtime::step
+    runner_path()                           # B2_RUNNER drop-in binary
+
+Every operation runs the compiled CUDA engine; there is no CPU fallback.  If
+the library has not been built (`python brian2-atlas_b200/build.py`), loading
+fails with an error instead of degrading.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+_PKG = Path(__file__).resolve().parent
+LIBRARY = _PKG / "lib" / "libb2gpu.so"
+RUNNER = _PKG / "bin" / "b2gpu-runner"
+_lib = None
+
+
+class B2GpuError(RuntimeError):
+    """An engine call failed; the message is the engine's error text."""
+
+
+class Options(ctypes.Structure):
+    _fields_ = [("struct_size", ctypes.c_uint32), ("device", ctypes.c_int32), ("chunk_ticks", ctypes.c_uint32),
+                ("use_graphs", ctypes.c_uint32), ("ring_capacity", ctypes.c_uint64)]
+
+
+class Stats(ctypes.Structure):
+    _fields_ = [("ticks", ctypes.c_uint64), ("synaptic_events", ctypes.c_uint64), ("spikes", ctypes.c_uint64),
+                ("kernel_launches", ctypes.c_uint64), ("launches_per_tick", ctypes.c_uint64),
+                ("simulation_seconds", ctypes.c_double), ("build_seconds", ctypes.c_double),
+                ("compile_seconds", ctypes.c_double), ("device_seconds", ctypes.c_double),
+                ("h2d_bytes", ctypes.c_uint64), ("d2h_bytes", ctypes.c_uint64)]
+
+
+class KernelTime(ctypes.Structure):
+    _fields_ = [("name", ctypes.c_char * 64), ("launches", ctypes.c_uint64), ("total_ms", ctypes.c_double)]
+
+
+def library() -> ctypes.CDLL:
+    """Load libb2gpu.so (raises if it was not built)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIBRARY.exists():
+        raise B2GpuError(f"{LIBRARY} is missing; run `python brian2-atlas_b200/build.py`")
+    lib = ctypes.CDLL(str(LIBRARY))
+    c = ctypes
+    sig = {
+        "b2g_default_options": (None, [c.POINTER(Options)]),
+        "b2g_create": (c.c_void_p, [c.c_char_p, c.c_size_t, c.POINTER(Options), c.c_char_p, c.c_size_t]),
+        "b2g_step": (c.c_int, [c.c_void_p, c.c_uint64, c.POINTER(c.c_int), c.c_char_p, c.c_size_t]),
+        "b2g_write_results": (c.c_int, [c.c_void_p, c.c_char_p, c.c_char_p, c.c_size_t]),
+        "b2g_get_stats": (c.c_int, [c.c_void_p, c.POINTER(Stats), c.c_char_p, c.c_size_t]),
+        "b2g_read_state": (c.c_int, [c.c_void_p, c.c_uint32, c.c_char_p, c.c_void_p, c.c_size_t,
+                                     c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
+        "b2g_spikes": (c.c_int, [c.c_void_p, c.c_uint32, c.c_uint64, c.c_void_p, c.c_size_t,
+                                 c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
+        "b2g_generated_source": (c.c_int, [c.c_void_p, c.c_char_p, c.c_size_t, c.POINTER(c.c_size_t)]),
+        "b2g_codegen": (c.c_int, [c.c_char_p, c.c_size_t, c.c_char_p, c.c_size_t, c.POINTER(c.c_size_t),
+                                  c.c_char_p, c.c_size_t]),
+        "b2g_profile": (c.c_int, [c.c_void_p, c.c_uint64, c.POINTER(KernelTime), c.c_size_t,
+                                  c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
+        "b2g_destroy": (None, [c.c_void_p]),
+        "b2g_version": (c.c_char_p, []),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def _err():
+    return ctypes.create_string_buffer(4096)
+
+
+def version() -> str:
+    return library().b2g_version().decode()
+
+
+def codegen(model_json: bytes) -> str:
+    """Compile a model's plan for sm_100a without a GPU and return the source."""
+    lib = library()
+    err, need = _err(), ctypes.c_size_t(0)
+    if lib.b2g_codegen(model_json, len(model_json), None, 0, ctypes.byref(need), err, len(err)):
+        raise B2GpuError(err.value.decode())
+    buf = ctypes.create_string_buffer(need.value)
+    if lib.b2g_codegen(model_json, len(model_json), buf, need, ctypes.byref(need), err, len(err)):
+        raise B2GpuError(err.value.decode())
+    return buf.value.decode()
+
+
+class Engine:
+    """One AtlasIR run on one GPU (mirrors the reference `Runtime`)."""
+
+    def __init__(self, model_json: bytes, device: int = -1, chunk_ticks: int = 0, use_graphs: bool = True,
+                 ring_capacity: int = 0):
+        lib = library()
+        opt = Options()
+        lib.b2g_default_options(ctypes.byref(opt))
+        opt.device = device
+        if chunk_ticks:
+            opt.chunk_ticks = chunk_ticks
+        opt.use_graphs = 1 if use_graphs else 0
+        opt.ring_capacity = ring_capacity
+        err = _err()
+        self._h = lib.b2g_create(model_json, len(model_json), ctypes.byref(opt), err, len(err))
+        if not self._h:
+            raise B2GpuError(err.value.decode())
+        self._lib = lib
+
+    def _call(self, name, *args):
+        err = _err()
+        if getattr(self._lib, name)(self._h, *args, err, len(err)):
+            raise B2GpuError(err.value.decode())
+
+    def step(self, max_ticks: int = 2 ** 63) -> bool:
+        done = ctypes.c_int(0)
+        self._call("b2g_step", ctypes.c_uint64(max_ticks), ctypes.byref(done))
+        return bool(done.value)
+
+    def run(self) -> None:
+        while not self.step():
+            pass
+
+    def write_results(self, outdir) -> None:
+        self._call("b2g_write_results", str(outdir).encode())
+
+    def stats(self) -> dict:
+        s = Stats()
+        self._call("b2g_get_stats", ctypes.byref(s))
+        return {name: getattr(s, name) for name, _ in Stats._fields_}
+
+    def read_state(self, population: int, name: str) -> bytes:
+        need = ctypes.c_size_t(0)
+        self._call("b2g_read_state", population, name.encode(), None, 0, ctypes.byref(need))
+        buf = ctypes.create_string_buffer(need.value)
+        self._call("b2g_read_state", population, name.encode(), buf, need, ctypes.byref(need))
+        return buf.raw[:need.value]
+
+    def spikes(self, population: int, tick: int) -> list:
+        count = ctypes.c_size_t(0)
+        self._call("b2g_spikes", population, ctypes.c_uint64(tick), None, 0, ctypes.byref(count))
+        buf = (ctypes.c_uint32 * max(count.value, 1))()
+        self._call("b2g_spikes", population, ctypes.c_uint64(tick), buf, count.value, ctypes.byref(count))
+        return list(buf[:count.value])
+
+    def profile(self, ticks: int) -> list:
+        """Advance `ticks` ticks with per-kernel CUDA-event timing."""
+        out = (KernelTime * 64)()
+        count = ctypes.c_size_t(0)
+        self._call("b2g_profile", ctypes.c_uint64(ticks), out, 64, ctypes.byref(count))
+        return [{"name": out[i].name.decode(), "launches": out[i].launches, "total_ms": out[i].total_ms}
+                for i in range(min(count.value, 64))]
+
+    def generated_source(self) -> str:
+        need = ctypes.c_size_t(0)
+        self._lib.b2g_generated_source(self._h, None, 0, ctypes.byref(need))
+        buf = ctypes.create_string_buffer(need.value)
+        self._lib.b2g_generated_source(self._h, buf, need, ctypes.byref(need))
+        return buf.value.decode()
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            self._lib.b2g_destroy(self._h)
+            self._h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+    def __del__(self):
+        self.close()
+
+
+def run_model(model_json: bytes, outdir, device: int = -1) -> dict:
+    """Run a whole model and write results.bin/events.bin/summary.json into the
+    new directory `outdir` (the b2-runner contract: the directory must not
+    exist beforehand)."""
+    outdir = Path(outdir)
+    if outdir.exists():
+        raise B2GpuError("output directory already exists; choose a new directory")
+    with Engine(model_json, device=device) as eng:
+        eng.run()
+        outdir.mkdir(parents=True)
+        eng.write_results(outdir)
+        return eng.stats()
+
+
+def runner_path() -> Path:
+    """Path of the b2-runner drop-in binary (export it as B2_RUNNER)."""
+    if not RUNNER.exists():
+        raise B2GpuError(f"{RUNNER} is missing; run `python brian2-atlas_b200/build.py`")
+    return RUNNER
+
+
+def package_dir() -> Path:
+    return _PKG
+
+
+__all__ = ["Engine", "B2GpuError", "run_model", "codegen", "version", "library", "runner_path", "LIBRARY",
+           "RUNNER"]

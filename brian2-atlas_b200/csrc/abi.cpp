@@ -1,0 +1,240 @@
+// extern "C" boundary of libb2gpu.so (declarations and reference mapping in
+// include/b2gpu.h).
+#include "../../include/b2gpu.h"
+
+#include <sys/stat.h>
+
+#include <chrono>
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <string>
+
+#include "common/dump.hpp"
+#include "common/ir.hpp"
+#include "engine/engine.hpp"
+
+struct b2g_engine {
+  std::unique_ptr<b2gpu::Engine> engine;
+  bool failed = false;
+};
+
+namespace {
+
+void set_error(char* error, size_t cap, const std::string& msg) {
+  if (!error || cap == 0) return;
+  size_t n = std::min(cap - 1, msg.size());
+  std::memcpy(error, msg.data(), n);
+  error[n] = '\0';
+}
+
+template <class F>
+int guarded(b2g_engine* e, char* error, size_t cap, F f) {
+  if (!e) {
+    set_error(error, cap, "null engine");
+    return 1;
+  }
+  if (e->failed) {
+    set_error(error, cap, "execution failed; create a new executor");
+    return 1;
+  }
+  try {
+    f();
+    set_error(error, cap, "");
+    return 0;
+  } catch (const std::exception& ex) {
+    e->failed = true;
+    set_error(error, cap, ex.what());
+    return 1;
+  }
+}
+
+b2gpu::Options to_options(const b2g_options* o) {
+  b2gpu::Options opt;
+  if (!o) return opt;
+  opt.device = o->device;
+  if (o->chunk_ticks) opt.chunk_ticks = o->chunk_ticks;
+  opt.use_graphs = o->use_graphs != 0;
+  opt.ring_capacity = o->ring_capacity;
+  return opt;
+}
+
+}  // namespace
+
+extern "C" {
+
+void b2g_default_options(b2g_options* o) {
+  if (!o) return;
+  std::memset(o, 0, sizeof(*o));
+  o->struct_size = sizeof(b2g_options);
+  o->device = -1;
+  o->chunk_ticks = 128;
+  o->use_graphs = 1;
+}
+
+b2g_engine* b2g_create(const char* json, size_t len, const b2g_options* options, char* error, size_t cap) {
+  try {
+    if (!json) throw b2ir::Error("null model document");
+    if (options && options->struct_size < sizeof(b2g_options)) throw b2ir::Error("b2g_options.struct_size too small");
+    b2ir::Model m = b2ir::load_model(json, len);
+    auto e = std::make_unique<b2g_engine>();
+    e->engine = std::make_unique<b2gpu::Engine>(m, to_options(options));
+    set_error(error, cap, "");
+    return e.release();
+  } catch (const std::exception& ex) {
+    set_error(error, cap, ex.what());
+    return nullptr;
+  }
+}
+
+int b2g_step(b2g_engine* e, uint64_t max_ticks, int* finished, char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    bool done = e->engine->step(max_ticks);
+    if (finished) *finished = done ? 1 : 0;
+  });
+}
+
+int b2g_write_results(b2g_engine* e, const char* outdir, char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    if (!outdir) throw b2ir::Error("null output directory");
+    auto t0 = std::chrono::steady_clock::now();
+    b2dump::ResultSet r = e->engine->results();
+    auto sizes = b2dump::write_dumps(r, outdir);
+    double dump_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    b2gpu::Stats s = e->engine->stats();
+    std::string summary = b2dump::summary_json(r, sizes.first, sizes.second, s.simulation_seconds, dump_seconds);
+    std::ofstream f(std::string(outdir) + "/summary.json");
+    f << summary;
+    if (!f) throw b2ir::Error("cannot write summary.json");
+  });
+}
+
+int b2g_get_stats(const b2g_engine* e, b2g_stats* out, char* error, size_t cap) {
+  return guarded(const_cast<b2g_engine*>(e), error, cap, [&] {
+    if (!out) throw b2ir::Error("null stats");
+    b2gpu::Stats s = e->engine->stats();
+    out->ticks = s.ticks;
+    out->synaptic_events = s.synaptic_events;
+    out->spikes = s.spikes;
+    out->kernel_launches = s.kernel_launches;
+    out->launches_per_tick = s.launches_per_tick;
+    out->simulation_seconds = s.simulation_seconds;
+    out->build_seconds = s.build_seconds;
+    out->compile_seconds = s.compile_seconds;
+    out->device_seconds = s.device_seconds;
+    out->h2d_bytes = s.h2d_bytes;
+    out->d2h_bytes = s.d2h_bytes;
+  });
+}
+
+int b2g_profile(b2g_engine* e, uint64_t ticks, b2g_kernel_time* out, size_t capacity, size_t* count, char* error,
+                size_t cap) {
+  return guarded(e, error, cap, [&] {
+    auto times = e->engine->profile(ticks);
+    if (count) *count = times.size();
+    for (size_t i = 0; i < times.size() && out && i < capacity; ++i) {
+      std::memset(out[i].name, 0, sizeof(out[i].name));
+      std::strncpy(out[i].name, times[i].name.c_str(), sizeof(out[i].name) - 1);
+      out[i].launches = times[i].launches;
+      out[i].total_ms = times[i].total_ms;
+    }
+  });
+}
+
+int b2g_read_state(b2g_engine* e, uint32_t population, const char* name, void* dst, size_t capacity, size_t* needed,
+                   char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    std::vector<uint8_t> bytes;
+    e->engine->read_state(population, name ? name : "", bytes);
+    if (needed) *needed = bytes.size();
+    if (dst) {
+      if (capacity < bytes.size()) throw b2ir::Error("destination buffer too small");
+      std::memcpy(dst, bytes.data(), bytes.size());
+    }
+  });
+}
+
+int b2g_spikes(b2g_engine* e, uint32_t population, uint64_t tick, uint32_t* dst, size_t capacity, size_t* count,
+               char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    std::vector<uint32_t> ids = e->engine->spikes_at(population, tick);
+    if (count) *count = ids.size();
+    if (dst) {
+      if (capacity < ids.size()) throw b2ir::Error("destination buffer too small");
+      std::memcpy(dst, ids.data(), ids.size() * 4);
+    }
+  });
+}
+
+int b2g_generated_source(const b2g_engine* e, char* dst, size_t capacity, size_t* needed) {
+  if (!e || !e->engine) return 1;
+  const std::string& s = e->engine->generated_source();
+  if (needed) *needed = s.size() + 1;
+  if (dst) {
+    if (capacity < s.size() + 1) return 1;
+    std::memcpy(dst, s.c_str(), s.size() + 1);
+  }
+  return 0;
+}
+
+int b2g_codegen(const char* json, size_t len, char* dst, size_t capacity, size_t* needed, char* error, size_t cap) {
+  try {
+    if (!json) throw b2ir::Error("null model document");
+    b2ir::Model m = b2ir::load_model(json, len);
+    b2gpu::Options opt;
+    opt.dry_run = true;
+    b2gpu::Engine engine(m, opt);
+    const std::string& s = engine.generated_source();
+    if (needed) *needed = s.size() + 1;
+    if (dst) {
+      if (capacity < s.size() + 1) throw b2ir::Error("destination buffer too small");
+      std::memcpy(dst, s.c_str(), s.size() + 1);
+    }
+    set_error(error, cap, "");
+    return 0;
+  } catch (const std::exception& ex) {
+    set_error(error, cap, ex.what());
+    return 1;
+  }
+}
+
+void b2g_destroy(b2g_engine* e) { delete e; }
+
+const char* b2g_version(void) { return "brian2-atlas-b200 0.1 (abi 1, sm_100a)"; }
+
+int b2g_run_cli(int argc, const char* const* argv) {
+  try {
+    b2ir::check(argc == 3, "usage: b2-runner MODEL.json OUTPUT_DIRECTORY | b2-runner --validate MODEL.json");
+    std::string first = argv[1];
+    if (first == "--validate") {
+      b2ir::Model m = b2ir::load_model_file(argv[2]);
+      (void)m;
+      std::printf("validated AtlasIR\n");
+      return 0;
+    }
+    b2ir::check(first.rfind("--", 0) != 0, "unknown b2-runner option");
+    struct stat st;
+    b2ir::check(stat(argv[2], &st) != 0, "output directory already exists; choose a new directory");
+    b2ir::Model m = b2ir::load_model_file(argv[1]);
+    b2gpu::Options opt;
+    b2gpu::Engine engine(m, opt);
+    engine.step(UINT64_MAX);
+    b2ir::check(mkdir(argv[2], 0777) == 0, "cannot create output directory");
+    auto t0 = std::chrono::steady_clock::now();
+    b2dump::ResultSet r = engine.results();
+    auto sizes = b2dump::write_dumps(r, argv[2]);
+    double dump_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    b2gpu::Stats s = engine.stats();
+    std::ofstream(std::string(argv[2]) + "/summary.json")
+        << b2dump::summary_json(r, sizes.first, sizes.second, s.simulation_seconds, dump_seconds);
+    std::printf("completed %zu populations for %llu neurons\n", r.populations.size(),
+                (unsigned long long)r.neuron_count);
+    return 0;
+  } catch (const std::exception& ex) {
+    std::fprintf(stderr, "b2-runner: %s\n", ex.what());
+    return 1;
+  }
+}
+
+}  // extern "C"

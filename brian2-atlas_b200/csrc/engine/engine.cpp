@@ -1,0 +1,1663 @@
+// B200 engine: plan construction, kernel generation, device state, tick loop.
+// Reference semantics: brian2-rust/src/executor.rs `Runtime::new` (:3473-3901)
+// and `Runtime::advance` (:3927-4360).
+#include "engine.hpp"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <functional>
+#include <set>
+#include <sstream>
+#include <unordered_set>
+
+#include "cuda_util.hpp"
+#include "topology.hpp"
+
+namespace b2gpu {
+
+extern const char* const kDeviceLibSource;  // device_lib.cuh, embedded at build time
+
+using b2ir::check;
+using b2ir::Error;
+
+// ------------------------------------------------------------------ buffers
+DeviceBuffer::DeviceBuffer(size_t n) : bytes(n) {
+  if (n) B2_CUDA(cudaMalloc(&ptr, n));
+}
+DeviceBuffer::~DeviceBuffer() {
+  if (ptr) cudaFree(ptr);
+}
+DeviceBuffer::DeviceBuffer(DeviceBuffer&& o) noexcept : ptr(o.ptr), bytes(o.bytes) {
+  o.ptr = nullptr;
+  o.bytes = 0;
+}
+DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
+  if (this != &o) {
+    if (ptr) cudaFree(ptr);
+    ptr = o.ptr;
+    bytes = o.bytes;
+    o.ptr = nullptr;
+    o.bytes = 0;
+  }
+  return *this;
+}
+
+namespace {
+
+constexpr unsigned kThreads = 256;
+constexpr uint32_t kErrNonfinite = 0x1, kErrTimestep = 0x2, kErrBinomial = 0x4, kErrPoisson = 0x8,
+                   kErrRing = 0x10, kErrLookback = 0x20, kErrIntDiv = 0x40, kErrTimedArray = 0x80,
+                   kErrCast = 0x100, kErrExchange = 0x200;
+
+std::string error_message(uint32_t e) {
+  if (e & kErrNonfinite) return "non-finite numeric value";
+  if (e & kErrTimestep) return "timestep outside Brian2 int64 range";
+  if (e & kErrBinomial) return "invalid binomial probability";
+  if (e & kErrPoisson) return "invalid poisson lambda";
+  if (e & kErrIntDiv) return "integer division by zero";
+  if (e & kErrTimedArray) return "TimedArray index/value outside supported range";
+  if (e & kErrCast) return "unsupported cast source";
+  if (e & kErrRing) return "spike ring overflow (raise the ring capacity)";
+  if (e & kErrLookback) return "spike compaction look-back timed out";
+  if (e & kErrExchange) return "spike exchange failed";
+  return "device error";
+}
+
+std::string sanitize(const std::string& s) {
+  std::string o;
+  for (char c : s) o.push_back(std::isalnum((unsigned char)c) ? c : '_');
+  return o.substr(0, 40);
+}
+
+uint64_t next_pow2(uint64_t v) {
+  uint64_t p = 1;
+  while (p < v) p <<= 1;
+  return p;
+}
+
+std::string u64lit(uint64_t v) { return std::to_string(v) + "ull"; }
+
+struct NodeEffects {
+  std::set<std::string> reads, writes;
+};
+
+bool conflicts(const NodeEffects& a, const NodeEffects& b) {
+  for (const auto& w : a.writes)
+    if (b.reads.count(w) || b.writes.count(w)) return true;
+  for (const auto& w : b.writes)
+    if (a.reads.count(w)) return true;
+  return false;
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ impl
+struct Engine::Impl {
+  b2ir::Model m;
+  Options opt;
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  cudaLibrary_t module = nullptr;
+  std::vector<DeviceBuffer> owned;
+  std::vector<uint64_t> ptrs;  // device pointer table (__constant__ g_ptr)
+  DeviceBuffer ctl;
+  std::string source;
+  Stats st;
+
+  // ---- populations
+  struct Slot {  // one state variable of a population
+    DType dtype;
+    int ptr;
+  };
+  struct EventStreamDev {
+    size_t pop = 0, event = 0;
+    uint64_t cap = 0, mask = 0;
+    int ring = -1, tick_start = -1, status = -1, ticket = -1;
+    bool produced = false, ascending = true;
+    size_t max_delay = 0;  // deepest consumer delay
+    // host copy of drained spikes
+    std::vector<uint32_t> ids;
+    std::vector<uint64_t> starts;  // host positions per tick: starts[rel] .. starts[rel+1]
+    uint64_t drained_pos = 0;
+  };
+  struct PopDev {
+    size_t count = 0, start_tick = 0, end_tick = 0, steps = 0;
+    double dt = 0.0;
+    std::vector<Slot> states;
+    int lastspike = -1, not_refractory = -1;
+    uint64_t period_ticks = 0;
+    bool fixed_refractory = false;
+    std::map<std::string, int> param_ptr;      // per-neuron parameter arrays
+    std::map<std::string, double> param_const; // scalar or uniform parameters
+    std::vector<int> stream_of_event;          // event index -> event stream id
+    bool has_spike_monitor = false;
+    // state monitor
+    int mon_records = -1;
+    std::vector<int> mon_samples;  // per monitor variable
+    std::vector<DType> mon_dtypes;
+    uint64_t mon_ticks = 0, mon_first_tick = 0;
+    // spike generator
+    int gen_offsets = -1, gen_ids = -1;
+  };
+  std::vector<PopDev> pops;
+  std::vector<EventStreamDev> streams;
+
+  // ---- synapses
+  struct AtomicAdd {
+    size_t state = 0;           // post state index
+    double addend = 0.0;
+    bool gated = false;         // only where the target's not_refractory is set
+  };
+  struct PathwayDev {
+    size_t synapse = 0, index = 0;
+    bool is_pre = true;
+    size_t endpoint_pop = 0, other_pop = 0;
+    size_t endpoint_start = 0, endpoint_count = 0;
+    int stream = -1;
+    int offsets = -1, row_other = -1, row_edge = -1, row_delay = -1;  // CSR
+    bool uniform = true;
+    size_t delay = 0, max_delay = 0;
+    int delivered_slot = 0;
+    enum class Mode { Atomic, EdgeParallel, Serial } mode = Mode::Serial;
+    std::vector<AtomicAdd> atomic_adds;
+    int pend_offsets = -1, pend_items = -1;
+    bool has_pending = false;
+  };
+  struct SynDev {
+    uint64_t edges = 0;
+    std::vector<Slot> states;
+    std::map<std::string, int> param_ptr;
+    std::map<std::string, double> param_const;
+    std::vector<PathwayDev> pathways;
+    bool identity_edges = true;  // row position == edge id for pre CSR
+  };
+  std::vector<SynDev> syns;
+  int delivered_ptr = -1;
+  size_t delivered_count = 0;
+
+  // ---- kernels
+  struct Op {
+    std::string name;
+    cudaKernel_t fn = nullptr;
+    unsigned grid = 1, block = kThreads;
+  };
+  std::vector<Op> ops;
+  std::vector<std::string> kernel_sources;
+  cudaGraphExec_t graph_exec = nullptr;
+  uint32_t graph_ticks = 0;
+  cudaEvent_t ev_start = nullptr, ev_stop = nullptr;
+
+  // ---- run state
+  size_t start_tick = 0, steps = 0, cur_rel = 0;
+  double dt = 0.0;
+  bool failed = false;
+
+  Impl(const b2ir::Model& model, const Options& o) : m(model), opt(o) {}
+
+  ~Impl() {
+    if (ev_start) cudaEventDestroy(ev_start);
+    if (ev_stop) cudaEventDestroy(ev_stop);
+    if (graph_exec) cudaGraphExecDestroy(graph_exec);
+    if (module) cudaLibraryUnload(module);
+    owned.clear();
+    ctl = DeviceBuffer();
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  int add_ptr(void* p) {
+    ptrs.push_back(reinterpret_cast<uint64_t>(p));
+    return int(ptrs.size() - 1);
+  }
+  int alloc(size_t bytes) {
+    if (opt.dry_run) return add_ptr(reinterpret_cast<void*>(uintptr_t(0x100000) * (ptrs.size() + 1)));
+    owned.emplace_back(std::max<size_t>(bytes, 16));
+    return add_ptr(owned.back().ptr);
+  }
+  int upload(const void* host, size_t bytes) {
+    int k = alloc(bytes);
+    if (bytes && !opt.dry_run)
+      B2_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(ptrs[size_t(k)]), host, bytes, cudaMemcpyHostToDevice, stream));
+    return k;
+  }
+  void memset_dev(int k, size_t bytes) {
+    if (!opt.dry_run) B2_CUDA(cudaMemsetAsync(dptr(k), 0, bytes, stream));
+  }
+  int adopt(DeviceBuffer&& b) {
+    owned.push_back(std::move(b));
+    return add_ptr(owned.back().ptr);
+  }
+  void* dptr(int k) const { return reinterpret_cast<void*>(ptrs[size_t(k)]); }
+
+  // ================================================================ checks
+  void check_capabilities() {
+    check(m.clocks.size() == 1, "the GPU engine supports models with a single clock");
+    dt = m.clocks[0].dt;
+    start_tick = m.run_clocks[0].start_tick;
+    steps = m.run_clocks[0].steps;
+    for (const auto& p : m.populations) {
+      check(p.linked_variable_count == 0, "linked variables are not supported by the GPU engine");
+      check(!p.spatial, "spatial neurons are not supported by the GPU engine");
+      check(p.rate_monitor_count == 0, "rate monitors are not supported by the GPU engine");
+      check(p.event_monitors.empty(), "event monitors are not supported by the GPU engine yet");
+      check(p.steps == steps, "population steps must match the run clock");
+      for (const auto& c : p.code_objects) check(!c.adaptive, "adaptive integrators are not supported by the GPU engine");
+    }
+    for (const auto& s : m.synapses) {
+      check(!s.source_synapse && !s.target_synapse, "synapse-to-synapse projections are not supported by the GPU engine");
+      check(s.linked_variable_count == 0, "synaptic linked variables are not supported by the GPU engine");
+      check(s.state_monitor_count == 0, "synapse state monitors are not supported by the GPU engine");
+      for (const auto& c : s.code_objects)
+        check(c.kind == "synapses" || c.kind == "synapses_post",
+              "synapse code object kind '" + c.kind + "' is not supported by the GPU engine");
+    }
+    for (const auto& si : m.synapse_instances)
+      check(si.topology.kind != b2ir::Topology::Kind::BinaryCsr, "binary_csr topology is not supported by the GPU engine yet");
+    check(opt.world_size == 1, "multi-GPU partitioning is configured through the distributed runner");
+  }
+
+  // ================================================================ populations
+  void build_populations() {
+    for (size_t p = 0; p < m.populations.size(); ++p) {
+      const auto& def = m.populations[p];
+      const auto& inst = m.population_instances[p];
+      PopDev pd;
+      pd.count = def.count;
+      pd.start_tick = start_tick;
+      pd.steps = def.steps;
+      pd.end_tick = start_tick + def.steps;
+      pd.dt = def.dt;
+      for (const auto& s : def.states) {
+        const auto& arr = inst.initial_state.at(s.name);
+        std::vector<uint8_t> bytes(arr.size() * b2ir::dtype_bytes(s.dtype));
+        for (size_t i = 0; i < arr.size(); ++i) std::memcpy(&bytes[i * b2ir::dtype_bytes(s.dtype)], &arr.raw[i], b2ir::dtype_bytes(s.dtype));
+        pd.states.push_back({s.dtype, upload(bytes.data(), bytes.size())});
+      }
+      if (inst.refractory) {
+        pd.lastspike = upload(inst.refractory->initial_lastspike.data(), def.count * 8);
+        pd.not_refractory = upload(inst.refractory->initial_not_refractory.data(), def.count);
+        pd.period_ticks = inst.refractory->period_ticks;
+        pd.fixed_refractory = def.refractory && def.refractory->mode == "fixed";
+      }
+      for (const auto& s : def.parameters) {
+        const auto& arr = inst.parameters.at(s.name);
+        bool uniform = true;
+        for (size_t i = 1; i < arr.size(); ++i) uniform &= arr.raw[i] == arr.raw[0];
+        if (s.index_domain == b2ir::IndexDomain::Scalar || uniform) {
+          pd.param_const[s.name] = arr.as_f64(0);
+        } else {
+          std::vector<double> v(arr.size());
+          for (size_t i = 0; i < arr.size(); ++i) v[i] = arr.as_f64(i);
+          pd.param_ptr[s.name] = upload(v.data(), v.size() * 8);
+        }
+      }
+      pd.stream_of_event.assign(def.events.size(), -1);
+      for (size_t e = 0; e < def.events.size(); ++e) {
+        EventStreamDev es;
+        es.pop = p;
+        es.event = e;
+        pd.stream_of_event[e] = int(streams.size());
+        streams.push_back(std::move(es));
+      }
+      for (const auto& node : m.schedule)
+        if (node.owner_kind == b2ir::OwnerKind::Population && node.owner_index == p &&
+            node.operation == b2ir::ScheduleOp::SpikeMonitor)
+          pd.has_spike_monitor = true;
+      // state monitor buffers
+      if (!def.state_monitors.empty() && !def.monitor.record.empty() && !def.monitor.variables.empty()) {
+        std::vector<uint32_t> rec(def.monitor.record.begin(), def.monitor.record.end());
+        for (auto r : rec) check(r < def.count, "state monitor record index out of range");
+        pd.mon_records = upload(rec.data(), rec.size() * 4);
+        uint64_t window = std::min<uint64_t>(def.monitor.window_steps, def.steps);
+        pd.mon_ticks = window;
+        pd.mon_first_tick = pd.end_tick - window;
+        for (const auto& name : def.monitor.variables) {
+          DType d = DType::F64;
+          bool found = false;
+          for (const auto& s : def.states) if (s.name == name) { d = s.dtype; found = true; }
+          for (const auto& s : def.parameters) if (s.name == name) { d = s.dtype; found = true; }
+          check(found, "monitor symbol missing from population");
+          pd.mon_dtypes.push_back(d);
+          pd.mon_samples.push_back(alloc(window * rec.size() * b2ir::dtype_bytes(d)));
+        }
+      }
+      if (inst.spike_generator) {
+        // Precompute each tick's fired list with the reference cursor rule
+        // (emit_spike_generator, executor.rs:3008-3036).
+        const auto& g = *inst.spike_generator;
+        std::vector<uint64_t> offs(def.steps + 1, 0);
+        std::vector<uint32_t> ids;
+        size_t cursor = 0;
+        for (size_t k = 0; k < def.steps; ++k) {
+          size_t tick = start_tick + k;
+          while (cursor < g.spike_ticks.size() && g.spike_ticks[cursor] < tick) ++cursor;
+          while (cursor < g.spike_ticks.size() && g.spike_ticks[cursor] == tick) {
+            check(g.spike_indices[cursor] < def.count, "spike generator index out of range");
+            ids.push_back(uint32_t(g.spike_indices[cursor++]));
+          }
+          offs[k + 1] = ids.size();
+        }
+        pd.gen_offsets = upload(offs.data(), offs.size() * 8);
+        pd.gen_ids = upload(ids.data(), std::max<size_t>(ids.size(), 1) * 4);
+      }
+      pops.push_back(std::move(pd));
+    }
+  }
+
+  // ================================================================ synapses
+  void build_synapses() {
+    std::vector<uint64_t> delivered_init;
+    for (size_t s = 0; s < m.synapses.size(); ++s) {
+      const auto& def = m.synapses[s];
+      const auto& inst = m.synapse_instances[s];
+      SynDev sd;
+      const auto& topo = inst.topology;
+      std::vector<uint32_t> src_h, tgt_h;  // explicit only
+      std::map<std::string, std::vector<double>> generated_params;
+      std::vector<std::vector<size_t>> delays;
+      bool procedural = topo.kind != b2ir::Topology::Kind::Explicit;
+      if (!procedural) {
+        src_h = inst.source;
+        tgt_h = inst.target;
+        sd.edges = src_h.size();
+        for (const auto& pw : inst.pathways) delays.push_back(pw.delay_ticks);
+      } else {
+        sd.edges = topo.edge_count;
+        for (const auto& pw : inst.pathways) {
+          check(!pw.delay_initializer, "procedural delay initializers are not supported by the GPU engine yet");
+          delays.push_back(pw.delay_ticks);
+        }
+      }
+      // synapse states
+      for (const auto& sym : def.states) {
+        auto it = inst.initial_state.find(sym.name);
+        check(it != inst.initial_state.end() && it->second.size() == sd.edges,
+              "synapse state '" + sym.name + "' has the wrong length");
+        size_t w = b2ir::dtype_bytes(sym.dtype);
+        std::vector<uint8_t> bytes(sd.edges * w);
+        for (size_t i = 0; i < sd.edges; ++i) std::memcpy(&bytes[i * w], &it->second.raw[i], w);
+        sd.states.push_back({sym.dtype, upload(bytes.data(), bytes.size())});
+      }
+      // parameters (per-edge arrays indexed by edge id)
+      for (const auto& sym : def.parameters) {
+        auto init = topo.initializers.find(sym.name);
+        if (procedural && init != topo.initializers.end()) {
+          const auto& in = init->second;
+          check(in.kind == b2ir::Initializer::Kind::Uniform, "clipped-normal initializers are not supported by the GPU engine yet");
+          int k = alloc(sd.edges * 8);
+          if (!opt.dry_run)
+            uniform_initializer_device(static_cast<double*>(dptr(k)), sd.edges, topo.seed, in.stream, *in.minimum,
+                                       *in.maximum, 0, stream);
+          sd.param_ptr[sym.name] = k;
+          continue;
+        }
+        const auto& arr = inst.parameters.at(sym.name);
+        bool uniform = true;
+        for (size_t i = 1; i < arr.size(); ++i) uniform &= arr.raw[i] == arr.raw[0];
+        if (sym.index_domain == b2ir::IndexDomain::Scalar || uniform) {
+          check(arr.size() > 0, "empty parameter '" + sym.name + "'");
+          sd.param_const[sym.name] = arr.as_f64(0);
+        } else {
+          check(arr.size() == sd.edges, "synapse parameter '" + sym.name + "' has the wrong length");
+          std::vector<double> v(arr.size());
+          for (size_t i = 0; i < arr.size(); ++i) v[i] = arr.as_f64(i);
+          sd.param_ptr[sym.name] = upload(v.data(), v.size() * 8);
+        }
+      }
+      // pathways
+      for (size_t k = 0; k < inst.pathways.size(); ++k) {
+        const auto& pw = inst.pathways[k];
+        PathwayDev pd;
+        pd.synapse = s;
+        pd.index = k;
+        pd.is_pre = pw.kind == "pre";
+        pd.endpoint_pop = pd.is_pre ? def.source_population : def.target_population;
+        pd.other_pop = pd.is_pre ? def.target_population : def.source_population;
+        pd.endpoint_start = pd.is_pre ? def.source_start : def.target_start;
+        pd.endpoint_count = pd.is_pre ? def.source_count : def.target_count;
+        const auto& endpoint = m.populations[pd.endpoint_pop];
+        auto ev = std::find(endpoint.events.begin(), endpoint.events.end(), pw.event);
+        check(ev != endpoint.events.end(), "pathway event missing from endpoint");
+        pd.stream = pops[pd.endpoint_pop].stream_of_event[size_t(ev - endpoint.events.begin())];
+        const auto& d = delays[k];
+        check(!d.empty(), "pathway has no delay");
+        pd.uniform = std::all_of(d.begin(), d.end(), [&](size_t x) { return x == d[0]; });
+        pd.delay = d[0];
+        pd.max_delay = *std::max_element(d.begin(), d.end());
+        if (!pd.uniform) check(d.size() == sd.edges, "per-edge delay array has the wrong length");
+        // CSR over the endpoint (source for pre, target for post), rows in
+        // edge creation order (stable counting sort).
+        if (!procedural) {
+          const auto& idx = pd.is_pre ? src_h : tgt_h;
+          const auto& other = pd.is_pre ? tgt_h : src_h;
+          std::vector<uint64_t> offs(pd.endpoint_count + 1, 0);
+          for (uint32_t i : idx) offs[i + 1]++;
+          for (size_t i = 0; i < pd.endpoint_count; ++i) offs[i + 1] += offs[i];
+          std::vector<uint64_t> next(offs.begin(), offs.end() - 1);
+          std::vector<uint32_t> row_other(idx.size()), row_edge(idx.size());
+          std::vector<uint16_t> row_delay;
+          if (!pd.uniform) row_delay.resize(idx.size());
+          bool identity = true;
+          for (size_t e = 0; e < idx.size(); ++e) {
+            uint64_t pos = next[idx[e]]++;
+            row_other[pos] = other[e];
+            row_edge[pos] = uint32_t(e);
+            identity &= pos == e;
+            if (!pd.uniform) {
+              check(d[e] < 65535, "per-edge delay exceeds 65534 ticks");
+              row_delay[pos] = uint16_t(d[e]);
+            }
+          }
+          check(idx.size() <= UINT32_MAX, "explicit edge count must fit u32");
+          pd.offsets = upload(offs.data(), offs.size() * 8);
+          pd.row_other = upload(row_other.data(), std::max<size_t>(row_other.size(), 1) * 4);
+          if (!identity) pd.row_edge = upload(row_edge.data(), std::max<size_t>(row_edge.size(), 1) * 4);
+          if (!pd.uniform) pd.row_delay = upload(row_delay.data(), std::max<size_t>(row_delay.size(), 1) * 2);
+        } else {
+          check(pd.is_pre, "procedural topologies support on_pre pathways only");
+          check(pd.uniform, "procedural topologies with per-edge delays are not supported by the GPU engine yet");
+          if (opt.dry_run) {
+            pd.offsets = alloc(0);
+            pd.row_other = alloc(0);
+          } else {
+            DeviceBuffer offs, rows;
+            uint64_t local_edges = 0;
+            if (topo.kind == b2ir::Topology::Kind::FixedIndegree)
+              build_fixed_indegree_csr(def.source_count, def.target_count, topo.indegree, topo.seed, 0,
+                                       def.target_count, offs, rows, local_edges, stream);
+            else
+              build_fixed_total_csr(def.source_count, def.target_count, topo.edge_count, topo.seed, 0,
+                                    def.target_count, offs, rows, local_edges, stream);
+            check(local_edges == sd.edges, "procedural edge count mismatch");
+            pd.offsets = adopt(std::move(offs));
+            pd.row_other = adopt(std::move(rows));
+          }
+        }
+        // pending (continuation) events: CSR by consumption tick
+        if (!pw.pending.empty()) {
+          check(pd.uniform, "pending events on per-edge-delay pathways are not supported by the GPU engine yet");
+          size_t slots = std::min(pd.max_delay + 1, endpoint.steps);
+          std::vector<std::vector<uint32_t>> per(steps);
+          for (const auto& ev2 : pw.pending) {
+            size_t slot = ev2.delivery_tick % slots;
+            size_t first = start_tick + ((slot + slots - start_tick % slots) % slots);
+            if (first >= start_tick + steps) continue;
+            check(ev2.item <= UINT32_MAX, "pending item out of range");
+            per[first - start_tick].push_back(uint32_t(ev2.item));
+          }
+          std::vector<uint64_t> offs(steps + 1, 0);
+          std::vector<uint32_t> items;
+          for (size_t t = 0; t < steps; ++t) {
+            items.insert(items.end(), per[t].begin(), per[t].end());
+            offs[t + 1] = items.size();
+          }
+          pd.pend_offsets = upload(offs.data(), offs.size() * 8);
+          pd.pend_items = upload(items.data(), std::max<size_t>(items.size(), 1) * 4);
+          pd.has_pending = !items.empty();
+        }
+        pd.delivered_slot = int(delivered_count++);
+        StreamUse(pd.stream, pd.max_delay);
+        sd.pathways.push_back(std::move(pd));
+      }
+      syns.push_back(std::move(sd));
+    }
+    delivered_init.assign(std::max<size_t>(delivered_count, 1), 0);
+    delivered_ptr = upload(delivered_init.data(), delivered_init.size() * 8);
+  }
+
+  void StreamUse(int s, size_t delay) { streams[size_t(s)].max_delay = std::max(streams[size_t(s)].max_delay, delay); }
+
+  void build_streams() {
+    for (auto& es : streams) {
+      const PopDev& pd = pops[es.pop];
+      uint64_t want = opt.ring_capacity ? opt.ring_capacity
+                                        : uint64_t(std::max<size_t>(pd.count, 1)) * (opt.chunk_ticks + es.max_delay + 2);
+      es.cap = next_pow2(std::max<uint64_t>(want, 1024));
+      es.mask = es.cap - 1;
+      es.ring = alloc(es.cap * 4);
+      es.tick_start = alloc((steps + 1) * 8);
+      memset_dev(es.tick_start, 8);
+      size_t tiles = (pd.count + kThreads - 1) / kThreads;
+      es.status = alloc(std::max<size_t>(tiles, 1) * 8);
+      memset_dev(es.status, std::max<size_t>(tiles, 1) * 8);
+      es.ticket = alloc(8);
+      memset_dev(es.ticket, 8);
+      es.starts.assign(1, 0);
+    }
+  }
+
+  // ================================================================ inputs
+  std::map<std::string, Input> population_inputs(size_t p, std::map<std::string, WriteTarget>& writable) {
+    const auto& def = m.populations[p];
+    const PopDev& pd = pops[p];
+    std::map<std::string, Input> in;
+    in["dt"] = Input::constant(def.dt, DType::F64);
+    in["t"] = Input::make(Input::Kind::Time);
+    in["N"] = Input::constant(double(def.count), DType::Index);
+    in["i"] = Input::make(Input::Kind::Index, Domain::Neuron);
+    for (size_t s = 0; s < def.states.size(); ++s) {
+      in[def.states[s].name] = Input::make(Input::Kind::State, Domain::Neuron, s, def.states[s].dtype);
+      writable[def.states[s].name] = WriteTarget{WriteTarget::Kind::Neuron, s};
+    }
+    if (pd.lastspike >= 0) {
+      in["lastspike"] = Input::make(Input::Kind::LastSpike);
+      in["not_refractory"] = Input::make(Input::Kind::Available, Domain::Neuron);
+      writable["not_refractory"] = WriteTarget{WriteTarget::Kind::Available, 0};
+    }
+    for (size_t k = 0; k < def.parameters.size(); ++k) {
+      const auto& sym = def.parameters[k];
+      auto c = pd.param_const.find(sym.name);
+      if (c != pd.param_const.end()) in[sym.name] = Input::constant(c->second, sym.dtype);
+      else in[sym.name] = Input::make(Input::Kind::Parameter, Domain::Neuron, k, sym.dtype);
+    }
+    return in;
+  }
+
+  std::map<std::string, Input> synapse_inputs(size_t s, bool is_pre, std::map<std::string, WriteTarget>& writable) {
+    const auto& def = m.synapses[s];
+    const SynDev& sd = syns[s];
+    const auto& src = m.populations[def.source_population];
+    const auto& tgt = m.populations[def.target_population];
+    std::map<std::string, Input> in;
+    in["dt"] = Input::constant((is_pre ? src : tgt).dt, DType::F64);
+    in["t"] = Input::make(Input::Kind::Time);
+    in["N"] = Input::constant(double(sd.edges), DType::Index);
+    in["N_pre"] = Input::constant(double(def.source_count), DType::Index);
+    in["N_post"] = Input::constant(double(def.target_count), DType::Index);
+    in["i"] = Input::make(Input::Kind::Index, Domain::Pre);
+    in["j"] = Input::make(Input::Kind::Index, Domain::Post);
+    for (size_t k = 0; k < def.states.size(); ++k) {
+      in[def.states[k].name] = Input::make(Input::Kind::SynapseState, Domain::Edge, k, def.states[k].dtype);
+    }
+    auto index_of = [](const std::vector<b2ir::Symbol>& syms, const std::string& name) {
+      for (size_t k = 0; k < syms.size(); ++k)
+        if (syms[k].name == name) return k;
+      throw Error("alias to unknown state '" + name + "'");
+    };
+    if (is_pre) {
+      for (const auto& [alias, state] : def.pre_state_aliases) {
+        size_t k = index_of(src.states, state);
+        in[alias] = Input::make(Input::Kind::PreState, Domain::Pre, k, src.states[k].dtype);
+        writable[alias] = WriteTarget{WriteTarget::Kind::PreNeuron, k};
+      }
+    } else {
+      for (const auto& [alias, state] : def.pre_state_aliases) {
+        size_t k = index_of(src.states, state);
+        in[alias] = Input::make(Input::Kind::PreState, Domain::Pre, k, src.states[k].dtype);
+      }
+    }
+    for (const auto& [alias, state] : def.post_state_aliases) {
+      size_t k = index_of(tgt.states, state);
+      in[alias] = Input::make(Input::Kind::PostState, Domain::Post, k, tgt.states[k].dtype);
+      writable[alias] = WriteTarget{WriteTarget::Kind::Neuron, k};
+    }
+    for (size_t k = 0; k < def.states.size(); ++k)
+      writable[def.states[k].name] = WriteTarget{WriteTarget::Kind::Synapse, k};
+    if (pops[def.target_population].lastspike >= 0)
+      in["not_refractory_post"] = Input::make(Input::Kind::Available, Domain::Post);
+    for (size_t k = 0; k < def.parameters.size(); ++k) {
+      const auto& sym = def.parameters[k];
+      auto c = sd.param_const.find(sym.name);
+      if (c != sd.param_const.end()) in[sym.name] = Input::constant(c->second, sym.dtype);
+      else in[sym.name] = Input::make(Input::Kind::Parameter, Domain::Edge, k, sym.dtype);
+    }
+    return in;
+  }
+
+  // ================================================================ codegen helpers
+  std::string P(int k, const char* type) const { return "((" + std::string(type) + "*)g_ptr[" + std::to_string(k) + "])"; }
+
+  // Neuron-domain context: state slots sv<k>, refractory slots ls/nr.
+  EmitContext neuron_ctx(size_t p) {
+    EmitContext c;
+    const PopDev& pd = pops[p];
+    const auto& def = m.populations[p];
+    c.load = [this, p, &def](const Input& in) -> std::string {
+      const PopDev& pd2 = pops[p];
+      switch (in.kind) {
+        case Input::Kind::State: return widen(def.states[in.index].dtype, "sv" + std::to_string(in.index));
+        case Input::Kind::Parameter: return P(pd2.param_ptr.at(def.parameters[in.index].name), "const double") + "[i]";
+        case Input::Kind::Index: return "((double)i)";
+        case Input::Kind::LastSpike: return "ls";
+        case Input::Kind::Available: return "(nr ? 1.0 : 0.0)";
+        default: throw Error("input kind not available in a neuron program");
+      }
+    };
+    (void)pd;
+    c.seed = u64lit(m.rng_seed);
+    c.tick = "tick";
+    c.time = "t";
+    c.index_for_domain[int(Domain::Neuron)] = "(u64)i";
+    c.index_for_domain[int(Domain::Pre)] = "(u64)i";
+    c.index_for_domain[int(Domain::Post)] = "(u64)i";
+    c.index_for_domain[int(Domain::Edge)] = "(u64)i";
+    return c;
+  }
+
+  // Slots a set of neuron programs touch (state indices).
+  std::set<size_t> slots_used(const std::vector<const Program*>& progs) {
+    std::set<size_t> out;
+    for (const Program* pr : progs) {
+      for (const auto& b : pr->bindings)
+        if (b.second.kind == Input::Kind::State) out.insert(b.second.index);
+      for (const auto& w : pr->writes)
+        if (w.first.kind == WriteTarget::Kind::Neuron) out.insert(w.first.index);
+    }
+    return out;
+  }
+  std::set<size_t> slots_written(const std::vector<const Program*>& progs) {
+    std::set<size_t> out;
+    for (const Program* pr : progs)
+      for (const auto& w : pr->writes)
+        if (w.first.kind == WriteTarget::Kind::Neuron) out.insert(w.first.index);
+    return out;
+  }
+  bool writes_available(const std::vector<const Program*>& progs) {
+    for (const Program* pr : progs)
+      for (const auto& w : pr->writes)
+        if (w.first.kind == WriteTarget::Kind::Available) return true;
+    return false;
+  }
+
+  std::string commits(const Program& pr, size_t p, const std::string& prefix) {
+    std::ostringstream o;
+    const auto& def = m.populations[p];
+    for (const auto& [w, r] : pr.writes) {
+      if (w.kind == WriteTarget::Kind::Neuron)
+        o << "  sv" << w.index << " = " << narrow(def.states[w.index].dtype, reg_expr(pr, r, prefix)) << ";\n";
+      else if (w.kind == WriteTarget::Kind::Available)
+        o << "  nr = (u8)(" << reg_expr(pr, r, prefix) << " != 0.0);\n";
+    }
+    return o.str();
+  }
+
+  std::string kernel_head(const std::string& name) {
+    return "extern \"C\" __global__ void __launch_bounds__(" + std::to_string(kThreads) + ") " + name +
+           "(RunCtl* __restrict__ ctl, u32 k) {\n  u32 err = 0;\n  const u64 tick = ctl->tick_base + k;\n"
+           "  const u64 rel = tick - " + u64lit(start_tick) + ";\n  const double t = (double)tick * " +
+           double_literal(dt) + ";\n  (void)rel; (void)t;\n";
+  }
+  static std::string kernel_tail() { return "  if (err) atomicOr(&ctl->error, err);\n}\n"; }
+
+  // ================================================================ step kernels
+  // Population step: optional update U, optional threshold X (with ascending
+  // compaction into the event ring), optional reset R on fired lanes.
+  std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
+                           bool x_is_spike, const Program* R) {
+    const auto& def = m.populations[p];
+    const PopDev& pd = pops[p];
+    std::vector<const Program*> progs;
+    for (const Program* pr : {U, X, R})
+      if (pr) progs.push_back(pr);
+    std::set<size_t> used = slots_used(progs), written = slots_written(progs);
+    bool refr = pd.lastspike >= 0;
+    std::ostringstream o;
+    o << kernel_head(name);
+    const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
+    size_t tiles = std::max<size_t>(1, (pd.count + kThreads - 1) / kThreads);
+    if (X) {
+      o << "  __shared__ u32 s_warp[" << kThreads / 32 + 1 << "];\n  __shared__ u64 s_base;\n  __shared__ u32 s_tile;\n";
+      o << "  if (threadIdx.x == 0) s_tile = (u32)(atomicAdd((unsigned long long*)" << P(es->ticket, "u64") << ", 1ull) % "
+        << tiles << "ull);\n  __syncthreads();\n  const u32 tile = s_tile;\n";
+      o << "  const u32 i = tile * " << kThreads << "u + threadIdx.x;\n";
+    } else {
+      o << "  const u32 i = blockIdx.x * " << kThreads << "u + threadIdx.x;\n";
+    }
+    o << "  const bool active = i < " << pd.count << "u;\n";
+    for (size_t s : used) {
+      const char* ct = storage_ctype(def.states[s].dtype);
+      o << "  " << ct << " sv" << s << " = active ? " << P(pops[p].states[s].ptr, ct) << "[i] : (" << ct << ")0;\n";
+    }
+    if (refr) {
+      o << "  double ls = active ? " << P(pd.lastspike, "double") << "[i] : 0.0;\n";
+      o << "  u8 nr = active ? " << P(pd.not_refractory, "u8") << "[i] : (u8)0;\n";
+    }
+    o << "  bool fired = false;\n  (void)fired;\n";
+    EmitContext ctx = neuron_ctx(p);
+    o << "  if (active) {\n";
+    if (U) {
+      if (refr && pd.fixed_refractory)
+        o << "  nr = (u8)(b2_timestep(t - ls, " << double_literal(pd.dt) << ", err) >= " << u64lit(pd.period_ticks) << ");\n";
+      o << "  {\n" << emit_program(*U, ctx, "u_") << commits(*U, p, "u_") << "  }\n";
+    }
+    if (X) {
+      o << "  {\n" << emit_program(*X, ctx, "h_");
+      o << "  fired = " << reg_expr(*X, size_t(X->condition), "h_") << " != 0.0";
+      if (x_is_spike && refr) o << " && nr";
+      o << ";\n";
+      o << commits(*X, p, "h_") << "  }\n";
+      if (x_is_spike && refr) o << "  if (fired) { ls = t; nr = 0; }\n";
+    }
+    o << "  }\n";
+    if (X) {
+      o << "  u32 block_total = 0;\n";
+      o << "  const u32 off = b2_compact_offsets<" << kThreads << ">(fired, tick, tile, " << P(es->status, "u64")
+        << ", s_warp, &s_base, err, &block_total);\n";
+      o << "  const u64* ts = " << P(es->tick_start, "u64") << ";\n";
+      o << "  const u64 tick_base_pos = ts[rel];\n";
+      o << "  if (fired) " << P(es->ring, "u32") << "[(tick_base_pos + s_base + off) & " << u64lit(es->mask) << "] = i;\n";
+      o << "  if (tile == " << tiles - 1 << "u && threadIdx.x == 0) {\n";
+      o << "    const u64 end = tick_base_pos + s_base + block_total;\n";
+      o << "    " << P(es->tick_start, "u64") << "[rel + 1] = end;\n";
+      o << "    if (end - ctl->ring_floor > " << u64lit(es->cap) << ") err |= " << kErrRing << "u;\n";
+      o << "  }\n";
+    }
+    if (R) {
+      o << "  if (active && fired) {\n" << emit_program(*R, ctx, "r_") << commits(*R, p, "r_") << "  }\n";
+    }
+    o << "  if (active) {\n";
+    for (size_t s : written) {
+      const char* ct = storage_ctype(def.states[s].dtype);
+      o << "    " << P(pops[p].states[s].ptr, ct) << "[i] = sv" << s << ";\n";
+    }
+    if (refr && (X || (U && pd.fixed_refractory) || writes_available(progs))) {
+      if (X && x_is_spike) o << "    if (fired) " << P(pd.lastspike, "double") << "[i] = ls;\n";
+      o << "    " << P(pd.not_refractory, "u8") << "[i] = nr;\n";
+    }
+    o << "  }\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
+  // Reset over the tick's fired list (one thread per spike).
+  std::string gen_reset(const std::string& name, size_t p, const Program& R, int stream_id) {
+    const auto& def = m.populations[p];
+    const EventStreamDev& es = streams[size_t(stream_id)];
+    std::vector<const Program*> progs{&R};
+    std::set<size_t> used = slots_used(progs), written = slots_written(progs);
+    bool refr = pops[p].lastspike >= 0;
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  const u64* ts = " << P(es.tick_start, "u64") << ";\n  const u64 a = ts[rel], b = ts[rel + 1];\n";
+    o << "  for (u64 j = a + blockIdx.x * (u64)blockDim.x + threadIdx.x; j < b; j += (u64)gridDim.x * blockDim.x) {\n";
+    o << "    const u32 i = " << P(es.ring, "const u32") << "[j & " << u64lit(es.mask) << "];\n";
+    for (size_t s : used) {
+      const char* ct = storage_ctype(def.states[s].dtype);
+      o << "    " << ct << " sv" << s << " = " << P(pops[p].states[s].ptr, ct) << "[i];\n";
+    }
+    if (refr) o << "    double ls = " << P(pops[p].lastspike, "double") << "[i];\n    u8 nr = " << P(pops[p].not_refractory, "u8") << "[i];\n    (void)ls; (void)nr;\n";
+    EmitContext ctx = neuron_ctx(p);
+    o << "  {\n" << emit_program(R, ctx, "r_") << commits(R, p, "r_") << "  }\n";
+    for (size_t s : written) {
+      const char* ct = storage_ctype(def.states[s].dtype);
+      o << "    " << P(pops[p].states[s].ptr, ct) << "[i] = sv" << s << ";\n";
+    }
+    if (refr && writes_available(progs)) o << "    " << P(pops[p].not_refractory, "u8") << "[i] = nr;\n";
+    o << "  }\n" << kernel_tail();
+    return o.str();
+  }
+
+  std::string gen_state_monitor(const std::string& name, size_t p) {
+    const auto& def = m.populations[p];
+    const PopDev& pd = pops[p];
+    size_t nrec = def.monitor.record.size(), nvar = def.monitor.variables.size();
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  if (tick < " << u64lit(pd.mon_first_tick) << ") return;\n";
+    o << "  const u64 row = tick - " << u64lit(pd.mon_first_tick) << ";\n";
+    o << "  const u32 x = blockIdx.x * blockDim.x + threadIdx.x;\n  if (x >= " << nrec * nvar << "u) return;\n";
+    o << "  const u32 var = x / " << nrec << "u, r = x % " << nrec << "u;\n";
+    o << "  const u32 i = " << P(pd.mon_records, "const u32") << "[r];\n  (void)i;\n";
+    for (size_t v = 0; v < nvar; ++v) {
+      const std::string& vname = def.monitor.variables[v];
+      DType d = pd.mon_dtypes[v];
+      const char* ct = storage_ctype(d);
+      std::string value;
+      bool is_state = false;
+      for (size_t s = 0; s < def.states.size(); ++s)
+        if (def.states[s].name == vname) {
+          value = P(pd.states[s].ptr, ct) + "[i]";
+          is_state = true;
+        }
+      if (!is_state) {
+        auto c = pd.param_const.find(vname);
+        std::string reg = c != pd.param_const.end() ? double_literal(c->second)
+                                                    : P(pd.param_ptr.at(vname), "const double") + "[i]";
+        value = narrow(d, reg);
+      }
+      o << "  if (var == " << v << "u) " << P(pd.mon_samples[v], ct) << "[row * " << nrec << "ull + r] = " << value << ";\n";
+    }
+    o << kernel_tail();
+    return o.str();
+  }
+
+  std::string gen_event_source(const std::string& name, size_t p, int stream_id) {
+    const PopDev& pd = pops[p];
+    const EventStreamDev& es = streams[size_t(stream_id)];
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  const u64* go = " << P(pd.gen_offsets, "const u64") << ";\n  const u64 a = go[rel], b = go[rel + 1];\n";
+    o << "  const u64 base = " << P(es.tick_start, "u64") << "[rel];\n";
+    o << "  for (u64 j = a + threadIdx.x; j < b; j += blockDim.x) " << P(es.ring, "u32") << "[(base + j - a) & "
+      << u64lit(es.mask) << "] = " << P(pd.gen_ids, "const u32") << "[j];\n";
+    o << "  if (threadIdx.x == 0) {\n    " << P(es.tick_start, "u64") << "[rel + 1] = base + (b - a);\n";
+    o << "    if (base + (b - a) - ctl->ring_floor > " << u64lit(es.cap) << ") err |= " << kErrRing << "u;\n  }\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
+  std::string gen_empty_stream(const std::string& name, int stream_id) {
+    const EventStreamDev& es = streams[size_t(stream_id)];
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  if (threadIdx.x == 0) " << P(es.tick_start, "u64") << "[rel + 1] = " << P(es.tick_start, "u64") << "[rel];\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
+  // ---------------------------------------------------------------- pathways
+  EmitContext event_ctx(size_t s, const PathwayDev& pw) {
+    EmitContext c;
+    const auto& def = m.synapses[s];
+    c.load = [this, s, &def](const Input& in) -> std::string {
+      const SynDev& sd = syns[s];
+      const auto& src = m.populations[def.source_population];
+      const auto& tgt = m.populations[def.target_population];
+      switch (in.kind) {
+        case Input::Kind::PreState: {
+          DType d = src.states[in.index].dtype;
+          return widen(d, P(pops[def.source_population].states[in.index].ptr, storage_ctype(d)) + "[src_state]");
+        }
+        case Input::Kind::PostState: {
+          DType d = tgt.states[in.index].dtype;
+          return widen(d, P(pops[def.target_population].states[in.index].ptr, storage_ctype(d)) + "[tgt_state]");
+        }
+        case Input::Kind::SynapseState: {
+          DType d = def.states[in.index].dtype;
+          return widen(d, P(sd.states[in.index].ptr, storage_ctype(d)) + "[edge]");
+        }
+        case Input::Kind::Parameter:
+          return P(sd.param_ptr.at(def.parameters[in.index].name), "const double") + "[edge]";
+        case Input::Kind::Index: return in.domain == Domain::Pre ? "((double)src)" : "((double)tgt)";
+        case Input::Kind::Available: {
+          int nrp = in.domain == Domain::Post ? pops[def.target_population].not_refractory
+                                              : pops[def.source_population].not_refractory;
+          check(nrp >= 0, "not_refractory read without refractory state");
+          return "(" + P(nrp, "const u8") + "[" + (in.domain == Domain::Post ? "tgt_state" : "src_state") + "] ? 1.0 : 0.0)";
+        }
+        default: throw Error("input kind not available in a pathway program");
+      }
+    };
+    (void)pw;
+    c.seed = u64lit(m.rng_seed);
+    c.tick = "tick";
+    c.time = "t";
+    c.index_for_domain[int(Domain::Neuron)] = "edge";
+    c.index_for_domain[int(Domain::Pre)] = "(u64)src";
+    c.index_for_domain[int(Domain::Post)] = "(u64)tgt";
+    c.index_for_domain[int(Domain::Edge)] = "edge";
+    return c;
+  }
+
+  std::string gen_pathway_body(const std::string& fname, size_t s, const PathwayDev& pw, const Program& pr) {
+    const auto& def = m.synapses[s];
+    const SynDev& sd = syns[s];
+    std::ostringstream o;
+    o << "__device__ __forceinline__ void " << fname
+      << "(u32 src, u32 tgt, u64 edge, u64 tick, double t, u32& err) {\n";
+    o << "  const u64 src_state = (u64)src + " << def.source_start << "ull;\n";
+    o << "  const u64 tgt_state = (u64)tgt + " << def.target_start << "ull;\n";
+    o << "  (void)src_state; (void)tgt_state; (void)t; (void)tick;\n";
+    o << emit_program(pr, event_ctx(s, pw), "e_");
+    const auto& src = m.populations[def.source_population];
+    const auto& tgt = m.populations[def.target_population];
+    for (const auto& [w, r] : pr.writes) {
+      std::string v = reg_expr(pr, r, "e_");
+      switch (w.kind) {
+        case WriteTarget::Kind::Neuron: {
+          DType d = tgt.states[w.index].dtype;
+          o << "  " << P(pops[def.target_population].states[w.index].ptr, storage_ctype(d)) << "[tgt_state] = " << narrow(d, v) << ";\n";
+          break;
+        }
+        case WriteTarget::Kind::PreNeuron: {
+          DType d = src.states[w.index].dtype;
+          o << "  " << P(pops[def.source_population].states[w.index].ptr, storage_ctype(d)) << "[src_state] = " << narrow(d, v) << ";\n";
+          break;
+        }
+        case WriteTarget::Kind::Synapse: {
+          DType d = def.states[w.index].dtype;
+          o << "  " << P(sd.states[w.index].ptr, storage_ctype(d)) << "[edge] = " << narrow(d, v) << ";\n";
+          break;
+        }
+        case WriteTarget::Kind::Available: break;
+      }
+    }
+    o << "}\n";
+    return o.str();
+  }
+
+  // Classify the delivery of one pathway (see PathwayDev::Mode).
+  void classify_pathway(PathwayDev& pw, const Program& pr) {
+    const auto& def = m.synapses[pw.synapse];
+    bool only_post = true, only_syn = true;
+    for (const auto& [w, r] : pr.writes) {
+      only_post &= w.kind == WriteTarget::Kind::Neuron;
+      only_syn &= w.kind == WriteTarget::Kind::Synapse;
+    }
+    if (pw.has_pending || !pw.uniform) {
+      pw.mode = PathwayDev::Mode::Serial;
+      return;
+    }
+    if (only_post && !pr.writes.empty() && pw.is_pre) {
+      // x_post = x_post + c with a plan-time constant c, optionally rounded to
+      // f32 and optionally gated by the target's not_refractory flag (which
+      // this pathway does not write).  Every event reaching one target then
+      // applies the same map, so the result does not depend on the order in
+      // which hardware atomics land and equals the sequential reference fold.
+      bool ok = true;
+      std::set<size_t> seen;
+      std::vector<AtomicAdd> adds;
+      size_t consumed = 0;
+      auto producer_of = [&](size_t r) -> const Instr* {
+        for (const auto& in : pr.vector)
+          if (in.output == r) return &in;
+        return nullptr;
+      };
+      for (const auto& [w, r0] : pr.writes) {
+        DType d = m.populations[def.target_population].states[w.index].dtype;
+        auto post_reg = pr.post_state_register(w.index);
+        const Instr* in = producer_of(r0);
+        if (!in || !post_reg || seen.count(w.index) || !(d == DType::F64 || d == DType::F32)) {
+          ok = false;
+          break;
+        }
+        seen.insert(w.index);
+        long cond = -1;
+        if (in->op == IOp::Select) {
+          const Input* g = in->guard >= 0 ? pr.binding_of(size_t(in->guard)) : nullptr;
+          if (!g || g->kind != Input::Kind::Available || g->domain != Domain::Post || in->right != *post_reg) {
+            ok = false;
+            break;
+          }
+          cond = in->guard;
+          ++consumed;
+          in = producer_of(in->left);
+        }
+        if (in && in->op == IOp::RoundF32 && in->guard == cond && d == DType::F32) {
+          ++consumed;
+          in = producer_of(in->left);
+        }
+        if (!in || in->guard != cond) {
+          ok = false;
+          break;
+        }
+        const RegInfo& L = pr.regs[in->left];
+        const RegInfo& R = pr.regs[in->right];
+        double c;
+        if (in->op == IOp::Add && in->left == *post_reg && R.kind == RegKind::Const && R.finite) c = R.value;
+        else if (in->op == IOp::Add && in->right == *post_reg && L.kind == RegKind::Const && L.finite) c = L.value;
+        else if (in->op == IOp::Sub && in->left == *post_reg && R.kind == RegKind::Const && R.finite) c = -R.value;
+        else {
+          ok = false;
+          break;
+        }
+        ++consumed;
+        adds.push_back({w.index, c, cond >= 0});
+      }
+      // Any other lane work (reads of other state, draws) disqualifies.
+      size_t lane_instrs = 0;
+      for (const auto& in : pr.vector)
+        if (pr.regs[in.output].kind != RegKind::Const) ++lane_instrs;
+      if (ok && lane_instrs == consumed) {
+        pw.mode = PathwayDev::Mode::Atomic;
+        pw.atomic_adds = adds;
+        return;
+      }
+    }
+    if (only_syn && !pr.writes.empty()) {
+      pw.mode = PathwayDev::Mode::EdgeParallel;
+      return;
+    }
+    pw.mode = PathwayDev::Mode::Serial;
+  }
+
+  // Spike-list traversal shared by pathway kernels: warp per fired endpoint,
+  // lanes over its CSR row.
+  std::string gen_pathway_kernel(const std::string& name, const std::string& body_fn, const PathwayDev& pw) {
+    const auto& def = m.synapses[pw.synapse];
+    const EventStreamDev& es = streams[size_t(pw.stream)];
+    const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
+    const bool full = lo == 0 && hi == m.populations[pw.endpoint_pop].count;
+    std::ostringstream o;
+    o << kernel_head(name);
+    std::string edge_of_q = pw.row_edge >= 0 ? "(u64)" + P(pw.row_edge, "const u32") + "[q]" : "q";
+    if (pw.mode == PathwayDev::Mode::Serial) {
+      // Canonical order: pending items first, then emission ticks oldest
+      // first, sources ascending, row (creation) order (executor.rs:2326-2378).
+      o << "  if (blockIdx.x != 0 || threadIdx.x != 0) return;\n";
+      o << "  const u64* off = " << P(pw.offsets, "const u64") << ";\n";
+      o << "  const u32* other = " << P(pw.row_other, "const u32") << ";\n";
+      o << "  u64 events = 0;\n";
+      std::string call_pre = pw.is_pre ? body_fn + "(ep, other[q], e, tick, t, err);" : body_fn + "(other[q], ep, e, tick, t, err);";
+      auto deliver_row = [&](const std::string& filter) {
+        std::ostringstream r;
+        r << "      for (u64 q = off[ep]; q < off[ep + 1]; ++q) {\n";
+        if (!filter.empty()) r << "        if (!(" << filter << ")) continue;\n";
+        r << "        const u64 e = " << edge_of_q << ";\n        " << call_pre << "\n        ++events;\n      }\n";
+        return r.str();
+      };
+      if (pw.has_pending) {
+        // Pending items were queued before any runtime push, so they come first
+        // in their slot; with a uniform delay an item is an endpoint index.
+        o << "  { const u64* po = " << P(pw.pend_offsets, "const u64") << "; const u32* pi = " << P(pw.pend_items, "const u32") << ";\n";
+        o << "    for (u64 x = po[rel]; x < po[rel + 1]; ++x) {\n";
+        o << "      const u32 ep = pi[x];\n" << deliver_row("");
+        o << "    }\n  }\n";
+      }
+      o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n";
+      o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
+      if (pw.uniform) {
+        o << "  if ((i64)rel - " << pw.delay << "ll >= 0) {\n    const u64 te = rel - " << pw.delay << "ull;\n";
+        o << "    for (u64 j = ts[te]; j < ts[te + 1]; ++j) {\n      const u32 s = ring[j & " << u64lit(es.mask) << "];\n";
+        if (!full) o << "      if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
+        o << "      const u32 ep = s - " << lo << "u;\n" << deliver_row("") << "    }\n  }\n";
+      } else {
+        o << "  const u16* dl = " << P(pw.row_delay, "const u16") << ";\n";
+        o << "  for (i64 te = (i64)rel - " << pw.max_delay << "ll; te <= (i64)rel; ++te) {\n    if (te < 0) continue;\n";
+        o << "    const u64 lag = rel - (u64)te;\n";
+        o << "    for (u64 j = ts[te]; j < ts[te + 1]; ++j) {\n      const u32 s = ring[j & " << u64lit(es.mask) << "];\n";
+        if (!full) o << "      if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
+        o << "      const u32 ep = s - " << lo << "u;\n" << deliver_row("dl[q] == lag") << "    }\n  }\n";
+      }
+      o << "  if (events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + " << pw.delivered_slot << ", events);\n";
+      o << kernel_tail();
+      return o.str();
+    }
+    // Parallel traversal: one warp per fired endpoint of tick rel - delay.
+    o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n  const u64 te = rel - " << pw.delay << "ull;\n";
+    o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
+    o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
+    o << "  const u64* off = " << P(pw.offsets, "const u64") << ";\n  const u32* other = " << P(pw.row_other, "const u32") << ";\n";
+    o << "  const u32 lane = threadIdx.x & 31u;\n";
+    o << "  const u64 warp = ((u64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;\n";
+    o << "  const u64 nwarps = ((u64)gridDim.x * blockDim.x) >> 5;\n  u64 events = 0;\n";
+    o << "  for (u64 j = a + warp; j < b; j += nwarps) {\n    const u32 s = ring[j & " << u64lit(es.mask) << "];\n";
+    if (!full) o << "    if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
+    o << "    const u32 ep = s - " << lo << "u;\n    const u64 r0 = off[ep], r1 = off[ep + 1];\n";
+    o << "    for (u64 q = r0 + lane; q < r1; q += 32) {\n";
+    if (pw.mode == PathwayDev::Mode::Atomic) {
+      const auto& tgt = m.populations[def.target_population];
+      o << "      const u64 tgt_state = (u64)other[q] + " << def.target_start << "ull;\n";
+      for (const auto& a : pw.atomic_adds) {
+        DType d = tgt.states[a.state].dtype;
+        int ptr = pops[def.target_population].states[a.state].ptr;
+        std::string gate = a.gated ? "if (" + P(pops[def.target_population].not_refractory, "const u8") + "[tgt_state]) " : "";
+        if (d == DType::F64) {
+          o << "      " << gate << "{ const double old = atomicAdd(" << P(ptr, "double") << " + tgt_state, "
+            << double_literal(a.addend) << "); if (!b2_finite(old + " << double_literal(a.addend) << ")) err |= "
+            << kErrNonfinite << "u; }\n";
+        } else {
+          o << "      " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tgt_state, "
+            << double_literal(a.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
+        }
+      }
+    } else {
+      o << "      const u64 e = " << edge_of_q << ";\n";
+      if (pw.is_pre) o << "      " << body_fn << "(ep, other[q], e, tick, t, err);\n";
+      else o << "      " << body_fn << "(other[q], ep, e, tick, t, err);\n";
+    }
+    o << "    }\n    events += r1 - r0;\n  }\n";
+    o << "  if (lane == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
+      << pw.delivered_slot << ", events);\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
+  // ================================================================ plan
+  NodeEffects effects_of(const b2ir::ScheduleNode& node) {
+    NodeEffects e;
+    e.reads.insert(node.effects.reads.begin(), node.effects.reads.end());
+    e.writes.insert(node.effects.writes.begin(), node.effects.writes.end());
+    if (node.operation == b2ir::ScheduleOp::CodeObject && node.owner_kind == b2ir::OwnerKind::Population) {
+      const auto& def = m.populations[node.owner_index];
+      const auto& code = def.code_objects[node.item_index];
+      if (def.refractory) {
+        std::string ls = "population/" + std::to_string(node.owner_index) + "/refractory/lastspike";
+        std::string nr = "population/" + std::to_string(node.owner_index) + "/refractory/not_refractory";
+        if (code.kind == "threshold" && code.event_name && *code.event_name == "spike") {
+          e.reads.insert(nr);
+          e.writes.insert(ls);
+          e.writes.insert(nr);
+        } else if (code.kind == "state_update" && def.refractory->mode == "fixed") {
+          e.reads.insert(ls);
+          e.writes.insert(nr);
+        }
+      }
+    }
+    return e;
+  }
+
+  std::vector<Program> programs;  // owned programs (stable addresses via reserve)
+
+  void build_plan() {
+    const auto& nodes = m.schedule;
+    check(!nodes.empty(), "model has no schedule");
+    std::vector<NodeEffects> eff;
+    for (const auto& n : nodes) eff.push_back(effects_of(n));
+    programs.reserve(nodes.size() * 2 + 8);
+    std::vector<bool> done(nodes.size(), false);
+    std::ostringstream src;
+    src << "// generated by brian2-atlas_b200 for one AtlasIR model\n";
+    src << kDeviceLibSource << "\n";
+    src << "__constant__ u64 g_ptr[PTR_COUNT_PLACEHOLDER];\n\n";
+    std::ostringstream bodies, kernels;
+    int kid = 0;
+    auto name_for = [&](const std::string& base) { return "b2_" + std::to_string(kid++) + "_" + sanitize(base); };
+    auto code_of = [&](const b2ir::ScheduleNode& n) -> const b2ir::CodeObject& {
+      return n.owner_kind == b2ir::OwnerKind::Population ? m.populations[n.owner_index].code_objects[n.item_index]
+                                                         : m.synapses[n.owner_index].code_objects[n.item_index];
+    };
+    auto compile_pop = [&](size_t p, const b2ir::CodeObject& c) -> const Program* {
+      std::map<std::string, WriteTarget> writable;
+      auto inputs = population_inputs(p, writable);
+      programs.push_back(Program::compile(c, inputs, writable, m.functions));
+      return &programs.back();
+    };
+    // Can node `mover` move from position `from` to just after position `to`
+    // (to < from) past every not-yet-consumed node in between?
+    auto can_hoist = [&](size_t to, size_t from) {
+      for (size_t y = to + 1; y < from; ++y)
+        if (!done[y] && conflicts(eff[from], eff[y])) return false;
+      return true;
+    };
+    std::vector<bool> stream_produced(streams.size(), false);
+    for (size_t idx = 0; idx < nodes.size(); ++idx) {
+      if (done[idx]) continue;
+      const auto& node = nodes[idx];
+      done[idx] = true;
+      if (node.owner_kind == b2ir::OwnerKind::Population) {
+        size_t p = node.owner_index;
+        const auto& def = m.populations[p];
+        switch (node.operation) {
+          case b2ir::ScheduleOp::StateMonitor: {
+            if (pops[p].mon_records < 0) break;
+            std::string nm = name_for(def.name + "_statemon");
+            kernels << gen_state_monitor(nm, p);
+            size_t n = def.monitor.record.size() * def.monitor.variables.size();
+            ops.push_back({nm, nullptr, unsigned((n + kThreads - 1) / kThreads), kThreads});
+            // several monitor nodes of one population record once per tick
+            for (size_t y = idx + 1; y < nodes.size(); ++y)
+              if (nodes[y].operation == b2ir::ScheduleOp::StateMonitor && nodes[y].owner_kind == b2ir::OwnerKind::Population &&
+                  nodes[y].owner_index == p && can_hoist(idx, y))
+                done[y] = true;
+            break;
+          }
+          case b2ir::ScheduleOp::SpikeMonitor: break;  // read from the drained spike ring
+          case b2ir::ScheduleOp::EventMonitor: throw Error("event monitors are not supported by the GPU engine yet");
+          case b2ir::ScheduleOp::EventSource: {
+            check(pops[p].gen_offsets >= 0, "event source without spike generator");
+            std::string nm = name_for(def.name + "_generator");
+            kernels << gen_event_source(nm, p, pops[p].stream_of_event[0]);
+            stream_produced[size_t(pops[p].stream_of_event[0])] = true;
+            ops.push_back({nm, nullptr, 1, kThreads});
+            break;
+          }
+          case b2ir::ScheduleOp::CodeObject: {
+            const auto& code = def.code_objects[node.item_index];
+            if (code.kind == "state_update" || code.kind == "threshold") {
+              const Program* U = nullptr;
+              const Program* X = nullptr;
+              const Program* R = nullptr;
+              size_t x_event = 0;
+              bool x_spike = false;
+              size_t x_pos = idx;
+              if (code.kind == "state_update") {
+                U = compile_pop(p, code);
+                // fuse the population's next threshold
+                for (size_t y = idx + 1; y < nodes.size(); ++y) {
+                  const auto& n2 = nodes[y];
+                  if (done[y] || n2.owner_kind != b2ir::OwnerKind::Population || n2.owner_index != p ||
+                      n2.operation != b2ir::ScheduleOp::CodeObject)
+                    continue;
+                  const auto& c2 = code_of(n2);
+                  if (c2.kind == "threshold" && can_hoist(idx, y)) {
+                    X = compile_pop(p, c2);
+                    done[y] = true;
+                    x_pos = y;
+                    x_event = size_t(std::find(def.events.begin(), def.events.end(), *c2.event_name) - def.events.begin());
+                    x_spike = *c2.event_name == "spike";
+                  }
+                  break;
+                }
+              } else {
+                X = compile_pop(p, code);
+                x_event = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
+                x_spike = *code.event_name == "spike";
+              }
+              if (X) {
+                check(x_event < def.events.size(), "threshold event is unknown");
+                stream_produced[size_t(pops[p].stream_of_event[x_event])] = true;
+                // fuse the matching reset when it can move up to the threshold
+                for (size_t y = x_pos + 1; y < nodes.size(); ++y) {
+                  const auto& n2 = nodes[y];
+                  if (done[y] || n2.owner_kind != b2ir::OwnerKind::Population || n2.owner_index != p ||
+                      n2.operation != b2ir::ScheduleOp::CodeObject)
+                    continue;
+                  const auto& c2 = code_of(n2);
+                  if (c2.kind == "reset" && c2.event_name && *c2.event_name == def.events[x_event]) {
+                    bool movable = true;
+                    for (size_t z = idx + 1; z < y; ++z)
+                      if (!done[z] && conflicts(eff[y], eff[z])) movable = false;
+                    if (movable) {
+                      R = compile_pop(p, c2);
+                      done[y] = true;
+                    }
+                    break;
+                  }
+                }
+              }
+              std::string nm = name_for(def.name + (X ? "_step" : "_update"));
+              kernels << gen_pop_step(nm, p, U, X, x_event, x_spike, R);
+              ops.push_back({nm, nullptr, unsigned(std::max<size_t>(1, (def.count + kThreads - 1) / kThreads)), kThreads});
+            } else if (code.kind == "reset") {
+              const Program* R = compile_pop(p, code);
+              size_t e = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
+              check(e < def.events.size(), "reset event is unknown");
+              std::string nm = name_for(def.name + "_reset");
+              kernels << gen_reset(nm, p, *R, pops[p].stream_of_event[e]);
+              ops.push_back({nm, nullptr, 148 * 4, kThreads});
+            } else if (code.kind == "poisson_input" || code.kind == "run_regularly" || code.kind == "subexpression_update") {
+              const Program* pr = compile_pop(p, code);
+              std::string nm = name_for(def.name + "_" + code.kind);
+              kernels << gen_pop_step(nm, p, pr, nullptr, 0, false, nullptr);
+              ops.push_back({nm, nullptr, unsigned(std::max<size_t>(1, (def.count + kThreads - 1) / kThreads)), kThreads});
+            } else {
+              throw Error("population code object kind '" + code.kind + "' is not supported by the GPU engine");
+            }
+            break;
+          }
+        }
+      } else {
+        check(node.operation == b2ir::ScheduleOp::CodeObject, "synapse monitors are not supported by the GPU engine");
+        size_t s = node.owner_index;
+        const auto& code = code_of(node);
+        check(bool(code.pathway_name), "scheduled pathway has no name");
+        const auto& pws = m.synapse_instances[s].pathways;
+        size_t pos = pws.size();
+        for (size_t k = 0; k < pws.size(); ++k)
+          if (pws[k].name == *code.pathway_name) pos = k;
+        check(pos < pws.size(), "scheduled pathway has no runtime instance");
+        PathwayDev& pw = syns[s].pathways[pos];
+        std::map<std::string, WriteTarget> writable;
+        auto inputs = synapse_inputs(s, pw.is_pre, writable);
+        programs.push_back(Program::compile(code, inputs, writable, m.functions));
+        const Program& pr = programs.back();
+        classify_pathway(pw, pr);
+        std::string base = sanitize(code.name);
+        std::string body = "b2_body_" + std::to_string(kid) + "_" + base;
+        if (pw.mode != PathwayDev::Mode::Atomic) bodies << gen_pathway_body(body, s, pw, pr);
+        const char* mode = pw.mode == PathwayDev::Mode::Atomic ? "_atomic"
+                           : pw.mode == PathwayDev::Mode::EdgeParallel ? "_edges" : "_serial";
+        std::string nm = name_for(code.name + mode);
+        kernels << gen_pathway_kernel(nm, body, pw);
+        ops.push_back({nm, nullptr, pw.mode == PathwayDev::Mode::Serial ? 1u : 148u * 8u,
+                       pw.mode == PathwayDev::Mode::Serial ? 32u : kThreads});
+      }
+    }
+    for (size_t sidx = 0; sidx < streams.size(); ++sidx) {
+      streams[sidx].produced = stream_produced[sidx];
+      if (!stream_produced[sidx]) {
+        std::string nm = name_for("empty_stream");
+        kernels << gen_empty_stream(nm, int(sidx));
+        ops.push_back({nm, nullptr, 1, 32});
+      }
+    }
+    src << bodies.str() << "\n" << kernels.str();
+    source = src.str();
+    std::string placeholder = "PTR_COUNT_PLACEHOLDER";
+    source.replace(source.find(placeholder), placeholder.size(), std::to_string(std::max<size_t>(ptrs.size(), 1)));
+  }
+
+  // ================================================================ compile
+  void compile_module() {
+    auto t0 = std::chrono::steady_clock::now();
+    nvrtcProgram prog;
+    B2_NVRTC(nvrtcCreateProgram(&prog, source.c_str(), "b2_model.cu", 0, nullptr, nullptr));
+    int major = 10, minor = 0;  // dry runs compile for sm_100a
+    if (!opt.dry_run) {
+      B2_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+      B2_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+    }
+    std::string arch = "--gpu-architecture=sm_" + std::to_string(major) + std::to_string(minor) + (major >= 9 ? "a" : "");
+    const char* opts[] = {arch.c_str(), "--std=c++17", "--fmad=false", "--prec-div=true", "--prec-sqrt=true",
+                          "--ftz=false", "-default-device", "-lineinfo"};
+    nvrtcResult res = nvrtcCompileProgram(prog, int(sizeof(opts) / sizeof(opts[0])), opts);
+    size_t log_size = 0;
+    nvrtcGetProgramLogSize(prog, &log_size);
+    std::string log(log_size, '\0');
+    if (log_size) nvrtcGetProgramLog(prog, log.data());
+    if (res != NVRTC_SUCCESS) {
+      nvrtcDestroyProgram(&prog);
+      throw Error("kernel compilation failed: " + log.substr(0, 4000));
+    }
+    size_t cubin_size = 0;
+    B2_NVRTC(nvrtcGetCUBINSize(prog, &cubin_size));
+    std::vector<char> cubin(cubin_size);
+    B2_NVRTC(nvrtcGetCUBIN(prog, cubin.data()));
+    nvrtcDestroyProgram(&prog);
+    st.compile_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    cubin_bytes = cubin.size();
+    if (opt.dry_run) return;
+    B2_CUDA(cudaLibraryLoadData(&module, cubin.data(), nullptr, nullptr, 0, nullptr, nullptr, 0));
+    void* table = nullptr;
+    size_t table_bytes = 0;
+    B2_CUDA(cudaLibraryGetGlobal(&table, &table_bytes, module, "g_ptr"));
+    check(table_bytes >= ptrs.size() * 8, "pointer table size mismatch");
+    B2_CUDA(cudaStreamSynchronize(stream));
+    if (!ptrs.empty()) B2_CUDA(cudaMemcpy(table, ptrs.data(), ptrs.size() * 8, cudaMemcpyHostToDevice));
+    for (auto& op : ops) B2_CUDA(cudaLibraryGetKernel(&op.fn, module, op.name.c_str()));
+  }
+  size_t cubin_bytes = 0;
+
+  // ================================================================ run loop
+  void launch_tick(uint32_t k) {
+    void* ctl_ptr = ctl.ptr;
+    for (auto& op : ops) {
+      void* args[] = {&ctl_ptr, &k};
+      B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(op.fn), dim3(op.grid), dim3(op.block), args, 0, stream));
+    }
+  }
+
+  void ensure_graph(uint32_t ticks) {
+    if (graph_exec && graph_ticks == ticks) return;
+    if (graph_exec) {
+      cudaGraphExecDestroy(graph_exec);
+      graph_exec = nullptr;
+    }
+    cudaGraph_t graph;
+    B2_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+    for (uint32_t k = 0; k < ticks; ++k) launch_tick(k);
+    B2_CUDA(cudaStreamEndCapture(stream, &graph));
+    B2_CUDA(cudaGraphInstantiate(&graph_exec, graph, 0));
+    cudaGraphDestroy(graph);
+    graph_ticks = ticks;
+  }
+
+  uint64_t tick_host_ = 0;  // pageable staging: the copy is complete when the call returns
+  uint64_t floor_host_ = 0;
+
+  void drain(size_t rel0, size_t rel1) {
+    for (auto& es : streams) {
+      std::vector<uint64_t> ts(rel1 - rel0 + 1);
+      B2_CUDA(cudaMemcpy(ts.data(), static_cast<uint64_t*>(dptr(es.tick_start)) + rel0, ts.size() * 8, cudaMemcpyDeviceToHost));
+      st.d2h_bytes += ts.size() * 8 + (ts.back() - ts.front()) * 4;
+      check(ts[0] == es.drained_pos, "spike ring bookkeeping mismatch");
+      uint64_t a = ts.front(), b = ts.back();
+      size_t old = es.ids.size();
+      es.ids.resize(old + (b - a));
+      uint64_t pos = a;
+      while (pos < b) {
+        uint64_t idx = pos & es.mask;
+        uint64_t n = std::min<uint64_t>(b - pos, es.cap - idx);
+        B2_CUDA(cudaMemcpy(es.ids.data() + old + (pos - a), static_cast<uint32_t*>(dptr(es.ring)) + idx, n * 4,
+                           cudaMemcpyDeviceToHost));
+        pos += n;
+      }
+      for (size_t k = 1; k < ts.size(); ++k) es.starts.push_back(ts[k]);
+      es.drained_pos = b;
+    }
+  }
+
+  void update_floor(size_t rel_now) {
+    // Oldest ring position any consumer may still read next chunk.
+    uint64_t floor = UINT64_MAX;
+    for (auto& es : streams) {
+      size_t back = rel_now > es.max_delay ? rel_now - es.max_delay : 0;
+      floor = std::min<uint64_t>(floor, es.starts.size() > back ? es.starts[back] : 0);
+    }
+    if (floor == UINT64_MAX) floor = 0;
+    floor_host_ = floor;
+    B2_CUDA(cudaMemcpy(static_cast<char*>(ctl.ptr) + 16, &floor_host_, 8, cudaMemcpyHostToDevice));
+    st.h2d_bytes += 8;
+  }
+
+  // Per-kernel timing: direct launches bracketed by events (no graph).
+  std::vector<KernelTime> profile(uint64_t ticks) {
+    check(!opt.dry_run && !failed, "profiling needs a live engine");
+    std::vector<KernelTime> out(ops.size());
+    for (size_t i = 0; i < ops.size(); ++i) out[i].name = ops[i].name;
+    std::vector<cudaEvent_t> evs(ops.size() + 1);
+    for (auto& e : evs) B2_CUDA(cudaEventCreate(&e));
+    uint64_t remaining = std::min<uint64_t>(ticks, steps - cur_rel);
+    while (remaining > 0) {
+      uint32_t n = uint32_t(std::min<uint64_t>(remaining, opt.chunk_ticks));
+      tick_host_ = start_tick + cur_rel;
+      B2_CUDA(cudaMemcpyAsync(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice, stream));
+      for (uint32_t k = 0; k < n; ++k) {
+        void* ctl_ptr = ctl.ptr;
+        B2_CUDA(cudaEventRecord(evs[0], stream));
+        for (size_t i = 0; i < ops.size(); ++i) {
+          void* args[] = {&ctl_ptr, &k};
+          B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(ops[i].fn), dim3(ops[i].grid), dim3(ops[i].block),
+                                   args, 0, stream));
+          B2_CUDA(cudaEventRecord(evs[i + 1], stream));
+        }
+        B2_CUDA(cudaEventSynchronize(evs.back()));
+        for (size_t i = 0; i < ops.size(); ++i) {
+          float ms = 0.f;
+          B2_CUDA(cudaEventElapsedTime(&ms, evs[i], evs[i + 1]));
+          out[i].total_ms += ms;
+          out[i].launches += 1;
+        }
+      }
+      st.kernel_launches += uint64_t(n) * ops.size();
+      check_error();
+      drain(cur_rel, cur_rel + n);
+      cur_rel += n;
+      remaining -= n;
+      update_floor(cur_rel);
+    }
+    for (auto& e : evs) cudaEventDestroy(e);
+    st.ticks = cur_rel;
+    return out;
+  }
+
+  void check_error() {
+    uint32_t err = 0;
+    B2_CUDA(cudaMemcpy(&err, static_cast<char*>(ctl.ptr) + 8, 4, cudaMemcpyDeviceToHost));
+    if (err) {
+      failed = true;
+      throw Error(error_message(err));
+    }
+  }
+
+  bool step(uint64_t max_ticks) {
+    check(!opt.dry_run, "a dry-run engine cannot step");
+    check(!failed, "execution failed; create a new executor");
+    check(max_ticks > 0, "step requires a positive tick budget");
+    auto t0 = std::chrono::steady_clock::now();
+    try {
+      uint64_t remaining = std::min<uint64_t>(max_ticks, steps - cur_rel);
+      while (remaining > 0) {
+        uint32_t n = uint32_t(std::min<uint64_t>(remaining, opt.chunk_ticks));
+        tick_host_ = start_tick + cur_rel;
+        B2_CUDA(cudaMemcpyAsync(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice, stream));
+        st.h2d_bytes += 8;
+        if (opt.use_graphs && n == opt.chunk_ticks) ensure_graph(n);
+        B2_CUDA(cudaEventRecord(ev_start, stream));
+        if (opt.use_graphs && n == opt.chunk_ticks) {
+          B2_CUDA(cudaGraphLaunch(graph_exec, stream));
+        } else {
+          for (uint32_t k = 0; k < n; ++k) launch_tick(k);
+        }
+        B2_CUDA(cudaEventRecord(ev_stop, stream));
+        st.kernel_launches += uint64_t(n) * ops.size();
+        B2_CUDA(cudaStreamSynchronize(stream));
+        float ms = 0.f;
+        B2_CUDA(cudaEventElapsedTime(&ms, ev_start, ev_stop));
+        st.device_seconds += double(ms) * 1e-3;
+        check_error();
+        drain(cur_rel, cur_rel + n);
+        cur_rel += n;
+        remaining -= n;
+        update_floor(cur_rel);
+      }
+    } catch (...) {
+      failed = true;
+      st.simulation_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+      throw;
+    }
+    st.simulation_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    st.ticks = cur_rel;
+    return cur_rel >= steps;
+  }
+
+  // ================================================================ results
+  std::vector<uint8_t> read_bytes(int k, size_t bytes) {
+    std::vector<uint8_t> out(bytes);
+    if (bytes) B2_CUDA(cudaMemcpy(out.data(), dptr(k), bytes, cudaMemcpyDeviceToHost));
+    return out;
+  }
+
+  b2dump::ResultSet results() {
+    check(!failed && cur_rel >= steps, "results require a completed execution");
+    B2_CUDA(cudaStreamSynchronize(stream));
+    b2dump::ResultSet r;
+    r.neuron_count = m.neuron_count;
+    r.final_time = m.run_start + m.run_duration;
+    for (size_t p = 0; p < m.populations.size(); ++p) {
+      const auto& def = m.populations[p];
+      const PopDev& pd = pops[p];
+      r.has_events |= !def.events.empty() || !def.event_monitors.empty();
+      b2dump::PopulationResult pr;
+      pr.count = def.count;
+      pr.steps = def.steps;
+      pr.record_count = def.monitor.record.size();
+      pr.variable_count = def.monitor.variables.size();
+      for (size_t v = 0; v < def.monitor.variables.size(); ++v) {
+        b2dump::Column c;
+        c.dtype = pd.mon_dtypes.empty() ? DType::F64 : pd.mon_dtypes[v];
+        if (pd.mon_records >= 0)
+          c.bytes = read_bytes(pd.mon_samples[v], pd.mon_ticks * def.monitor.record.size() * b2ir::dtype_bytes(c.dtype));
+        pr.samples.push_back(std::move(c));
+      }
+      uint64_t window_first = pd.end_tick - std::min<uint64_t>(def.monitor.window_steps, pd.end_tick);
+      pr.event_history.resize(def.events.size());
+      for (size_t e = 0; e < def.events.size(); ++e) {
+        const EventStreamDev& es = streams[size_t(pd.stream_of_event[e])];
+        for (size_t rel = 0; rel < steps; ++rel) {
+          uint64_t tick = start_tick + rel;
+          if (tick < window_first) continue;
+          for (uint64_t x = es.starts[rel]; x < es.starts[rel + 1]; ++x)
+            pr.event_history[e].push_back({tick, es.ids[x]});
+        }
+      }
+      pr.counts.assign(def.count, 0);
+      auto spike_it = std::find(def.events.begin(), def.events.end(), "spike");
+      if (spike_it != def.events.end()) {
+        size_t e = size_t(spike_it - def.events.begin());
+        const EventStreamDev& es = streams[size_t(pd.stream_of_event[e])];
+        if (pd.has_spike_monitor) {
+          pr.spikes = pr.event_history[e];
+          for (const auto& sp : pr.spikes) pr.counts[sp.second]++;
+        }
+        if (steps > 0)
+          for (uint64_t x = es.starts[steps - 1]; x < es.starts[steps]; ++x) pr.last_fired.push_back(es.ids[x]);
+      }
+      for (size_t s = 0; s < def.states.size(); ++s) {
+        b2dump::Column c;
+        c.dtype = def.states[s].dtype;
+        c.bytes = read_bytes(pd.states[s].ptr, def.count * b2ir::dtype_bytes(c.dtype));
+        pr.states.push_back(std::move(c));
+      }
+      if (pd.lastspike >= 0) {
+        pr.has_refractory = true;
+        auto ls = read_bytes(pd.lastspike, def.count * 8);
+        pr.lastspike.resize(def.count);
+        std::memcpy(pr.lastspike.data(), ls.data(), ls.size());
+        pr.not_refractory = read_bytes(pd.not_refractory, def.count);
+      }
+      r.populations.push_back(std::move(pr));
+    }
+    std::vector<uint64_t> delivered(std::max<size_t>(delivered_count, 1));
+    B2_CUDA(cudaMemcpy(delivered.data(), dptr(delivered_ptr), delivered.size() * 8, cudaMemcpyDeviceToHost));
+    for (size_t s = 0; s < m.synapses.size(); ++s) {
+      const auto& def = m.synapses[s];
+      const SynDev& sd = syns[s];
+      b2dump::SynapseResult sr;
+      sr.edge_count = sd.edges;
+      for (size_t k = 0; k < def.states.size(); ++k) {
+        b2dump::Column c;
+        c.dtype = def.states[k].dtype;
+        c.bytes = read_bytes(sd.states[k].ptr, sd.edges * b2ir::dtype_bytes(c.dtype));
+        sr.states.push_back(std::move(c));
+      }
+      for (const auto& pw : sd.pathways) sr.delivered += delivered[size_t(pw.delivered_slot)];
+      r.synapses.push_back(std::move(sr));
+    }
+    return r;
+  }
+
+  void build() {
+    auto t0 = std::chrono::steady_clock::now();
+    check_capabilities();
+    if (!opt.dry_run) {
+      if (opt.device >= 0) B2_CUDA(cudaSetDevice(opt.device));
+      B2_CUDA(cudaGetDevice(&device));
+      B2_CUDA(cudaFree(nullptr));  // establish the primary context
+      B2_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+      B2_CUDA(cudaEventCreate(&ev_start));
+      B2_CUDA(cudaEventCreate(&ev_stop));
+      ctl = DeviceBuffer(64);
+      B2_CUDA(cudaMemsetAsync(ctl.ptr, 0, 64, stream));
+    }
+    build_populations();
+    build_synapses();
+    build_streams();
+    build_plan();
+    compile_module();
+    if (!opt.dry_run) B2_CUDA(cudaStreamSynchronize(stream));
+    st.launches_per_tick = ops.size();
+    st.build_seconds = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  }
+};
+
+// ------------------------------------------------------------------ facade
+Engine::Engine(const b2ir::Model& model, const Options& options) : impl_(std::make_unique<Impl>(model, options)) {
+  impl_->build();
+}
+Engine::~Engine() = default;
+bool Engine::step(uint64_t max_ticks) { return impl_->step(max_ticks); }
+bool Engine::finished() const { return impl_->cur_rel >= impl_->steps; }
+b2dump::ResultSet Engine::results() { return impl_->results(); }
+Stats Engine::stats() const {
+  Stats s = impl_->st;
+  uint64_t spikes = 0;
+  for (const auto& es : impl_->streams) spikes += es.ids.size();
+  s.spikes = spikes;
+  if (!impl_->opt.dry_run && impl_->delivered_ptr >= 0 && impl_->delivered_count) {
+    std::vector<uint64_t> d(impl_->delivered_count);
+    if (cudaMemcpy(d.data(), impl_->dptr(impl_->delivered_ptr), d.size() * 8, cudaMemcpyDeviceToHost) == cudaSuccess)
+      for (auto x : d) s.synaptic_events += x;
+  }
+  return s;
+}
+const std::string& Engine::generated_source() const { return impl_->source; }
+
+void Engine::read_state(size_t population, const std::string& name, std::vector<uint8_t>& out) {
+  check(population < impl_->m.populations.size(), "population index out of range");
+  const auto& def = impl_->m.populations[population];
+  for (size_t s = 0; s < def.states.size(); ++s)
+    if (def.states[s].name == name) {
+      out = impl_->read_bytes(impl_->pops[population].states[s].ptr, def.count * b2ir::dtype_bytes(def.states[s].dtype));
+      return;
+    }
+  throw Error("unknown state '" + name + "'");
+}
+
+std::vector<KernelTime> Engine::profile(uint64_t ticks) { return impl_->profile(ticks); }
+
+std::vector<uint32_t> Engine::spikes_at(size_t population, uint64_t tick) const {
+  check(population < impl_->m.populations.size(), "population index out of range");
+  const auto& def = impl_->m.populations[population];
+  auto it = std::find(def.events.begin(), def.events.end(), "spike");
+  check(it != def.events.end(), "population has no spike event");
+  const auto& es = impl_->streams[size_t(impl_->pops[population].stream_of_event[size_t(it - def.events.begin())])];
+  check(tick >= impl_->start_tick && tick - impl_->start_tick + 1 < es.starts.size(), "tick not simulated yet");
+  size_t rel = tick - impl_->start_tick;
+  return std::vector<uint32_t>(es.ids.begin() + long(es.starts[rel]), es.ids.begin() + long(es.starts[rel + 1]));
+}
+
+}  // namespace b2gpu

@@ -1,0 +1,29 @@
+// Device construction of procedural projections (see topology.cu).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "engine.hpp"
+
+namespace b2gpu {
+
+// Source-major CSR of a fixed in-degree projection restricted to the targets
+// [t_lo, t_hi): offsets[S+1] (u64) and row_targets[] (u32, target indices
+// local to the target range), rows in ascending target order.
+void build_fixed_indegree_csr(uint64_t S, uint64_t T, uint64_t K, uint64_t seed, uint64_t t_lo, uint64_t t_hi,
+                              DeviceBuffer& offsets, DeviceBuffer& row_targets, uint64_t& local_edges,
+                              cudaStream_t stream);
+
+// Same for a fixed-total projection (edges sampled with replacement).
+void build_fixed_total_csr(uint64_t S, uint64_t T, uint64_t E, uint64_t seed, uint64_t t_lo, uint64_t t_hi,
+                           DeviceBuffer& offsets, DeviceBuffer& row_targets, uint64_t& local_edges,
+                           cudaStream_t stream);
+
+// Uniform per-edge initializer (large_topology.rs:129-142) for edge ids
+// edge_base .. edge_base+n-1.
+void uniform_initializer_device(double* out, uint64_t n, uint64_t seed, uint64_t stream_id, double lo, double hi,
+                                uint64_t edge_base, cudaStream_t stream);
+
+}  // namespace b2gpu

@@ -1,0 +1,409 @@
+// Device library prepended to every generated model translation unit (compiled
+// by NVRTC for sm_100a with -fmad=false, so every a*b+c stays two IEEE
+// roundings, as in the reference's non-fused CPU arithmetic).
+//
+// Contents:
+//   * RunCtl: the per-run control block in device memory (tick cursor, error
+//     word, spike-ring counters) that CUDA-graph-replayed kernels read.
+//   * counter RNG (splitmix64 counters), restated from the reference
+//     brian2-rust/src/executor.rs:190-336.
+//   * Brian2 timestep() (brian2-rust/src/model.rs:981-992).
+//   * block-ascending spike compaction with decoupled look-back (Merrill &
+//     Garland, "Single-pass Parallel Prefix Scan with Decoupled Look-back",
+//     NVIDIA tech report NVR-2016-002): warp ballot + popc, a shared-memory
+//     block scan, and a bounded look-back over tile status words so the spike
+//     list of a tick comes out globally ascending in one pass.
+#pragma once
+
+typedef unsigned long long u64;
+typedef long long i64;
+typedef unsigned int u32;
+typedef int i32;
+typedef unsigned short u16;
+typedef unsigned char u8;
+
+// Error bits OR-ed into RunCtl::error; the host maps them to messages.
+#define B2_ERR_NONFINITE 0x1u
+#define B2_ERR_TIMESTEP 0x2u
+#define B2_ERR_BINOMIAL 0x4u
+#define B2_ERR_POISSON 0x8u
+#define B2_ERR_RING 0x10u
+#define B2_ERR_LOOKBACK 0x20u
+#define B2_ERR_INTDIV 0x40u
+#define B2_ERR_TIMEDARRAY 0x80u
+#define B2_ERR_CAST 0x100u
+#define B2_ERR_EXCHANGE 0x200u
+
+struct RunCtl {
+  u64 tick_base;      // absolute tick of graph step k == 0
+  u32 error;          // OR of B2_ERR_* bits
+  u32 pad0;
+  u64 ring_floor;     // oldest ring position the host still needs
+  u64 tile_ticket;    // monotonically increasing compaction tile ticket
+};
+
+__device__ __forceinline__ double b2_bits(u64 r) { return __longlong_as_double((i64)r); }
+__device__ __forceinline__ u64 b2_raw(double v) { return (u64)__double_as_longlong(v); }
+__device__ __forceinline__ bool b2_finite(double v) { return isfinite(v); }
+
+// ---------------------------------------------------------------- RNG
+__device__ __forceinline__ u64 b2_mix64(u64 v) {
+  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+  v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+  return v ^ (v >> 31);
+}
+
+__device__ __forceinline__ double b2_uniform_draw(u64 seed, u64 stream, u64 tick, u64 index, u64 draw) {
+  u64 c = seed ^ (stream * 0x9e3779b97f4a7c15ull) ^ (tick * 0xd1b54a32d192ed03ull) ^
+          (index * 0x94d049bb133111ebull) ^ (draw * 0x369dea0f31a53f85ull);
+  return (double)(b2_mix64(c) >> 11) * (1.0 / 9007199254740992.0);
+}
+
+__device__ __forceinline__ double b2_uniform(u64 seed, u64 stream, u64 tick, u64 index) {
+  return b2_uniform_draw(seed, stream, tick, index, 0);
+}
+
+// Marsaglia polar method on pair index/2 (executor.rs:209-222).
+__device__ double b2_normal(u64 seed, u64 stream, u64 tick, u64 index) {
+  u64 pair = index >> 1;
+  u64 draw = 0;
+  for (int guard = 0; guard < 1 << 20; ++guard) {
+    double x1 = 2.0 * b2_uniform_draw(seed, stream, tick, pair, draw) - 1.0;
+    double x2 = 2.0 * b2_uniform_draw(seed, stream, tick, pair, draw + 1) - 1.0;
+    double r = x1 * x1 + x2 * x2;
+    if (r < 1.0 && r != 0.0) {
+      double f = sqrt(-2.0 * log(r) / r);
+      return f * ((index & 1) == 0 ? x1 : x2);
+    }
+    draw += 2;
+  }
+  return 0.0;
+}
+
+// Binomial inversion with the per-pathway constants precomputed on the host in
+// glibc f64 (probability, q, q^n, restart bound), so the device loop is pure
+// IEEE arithmetic and bit-identical to executor.rs:224-268.
+__device__ double b2_binomial_inv(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
+                                  double probability, double q, double qn, double bound,
+                                  bool reverse) {
+  u64 draw = 0;
+  for (int restarts = 0; restarts < 1 << 16; ++restarts) {
+    u64 x = 0;
+    double px = qn;
+    double u = b2_uniform_draw(seed, stream, tick, index, draw);
+    while (true) {
+      if (u <= px) return (double)(reverse ? n - x : x);
+      x += 1;
+      if ((double)x > bound) {
+        draw += 1;
+        break;
+      }
+      u -= px;
+      px = ((double)(n - x + 1) * probability * px) / ((double)x * q);
+    }
+  }
+  return 0.0;
+}
+
+// General binomial with a per-lane probability (device libm for q^n).
+__device__ double b2_binomial(u64 seed, u64 stream, u64 tick, u64 index, u64 n, double p,
+                              bool approximate) {
+  if (p <= 0.0) return 0.0;
+  if (p >= 1.0) return (double)n;
+  double nf = (double)n;
+  double loc = nf * p;
+  double complement = nf * (1.0 - p);
+  if (approximate && loc > 5.0 && complement > 5.0)
+    return b2_normal(seed, stream, tick, index) * sqrt(loc * (1.0 - p)) + loc;
+  bool reverse = p > 0.5;
+  double probability = reverse ? 1.0 - p : p;
+  double q = 1.0 - probability;
+  double qn = exp(nf * log(q));
+  double bound = fmin(nf, nf * probability + 10.0 * sqrt(nf * probability * q + 1.0));
+  return b2_binomial_inv(seed, stream, tick, index, n, probability, q, qn, bound, reverse);
+}
+
+__device__ double b2_log_gamma_positive(double value) {
+  const double c[8] = {676.5203681218851,    -1259.1392167224028, 771.3234287776531,
+                       -176.6150291621406,   12.507343278686905,  -0.13857109526572012,
+                       9.984369578019572e-6, 1.5056327351493116e-7};
+  double z = value - 1.0;
+  double x = 0.9999999999998099;
+  for (int i = 0; i < 8; ++i) x += c[i] / (z + (double)i + 1.0);
+  double t = z + 7.5;
+  return 0.9189385332046727 + (z + 0.5) * log(t) - t + log(x);
+}
+
+// Knuth product below 10, Hoermann PTRS above (executor.rs:290-336).
+__device__ double b2_poisson(u64 seed, u64 stream, u64 tick, u64 index, double lambda) {
+  if (lambda == 0.0) return 0.0;
+  if (!isfinite(lambda) || !(lambda >= 0.0 && lambda <= 1.0e12)) return __longlong_as_double(0x7ff8000000000000ll);
+  if (lambda < 10.0) {
+    double limit = exp(-lambda);
+    double product = 1.0;
+    for (u64 sample = 0; sample < (1ull << 24); ++sample) {
+      product *= b2_uniform_draw(seed, stream, tick, index, sample);
+      if (product <= limit) return (double)sample;
+    }
+    return 0.0;
+  }
+  double root = sqrt(lambda);
+  double b = 0.931 + 2.53 * root;
+  double a = -0.059 + 0.02483 * b;
+  double inverse_alpha = 1.1239 + 1.1328 / (b - 3.4);
+  double squeeze = 0.9277 - 3.6224 / (b - 2.0);
+  u64 draw = 0;
+  for (int guard = 0; guard < 1 << 20; ++guard) {
+    double u = b2_uniform_draw(seed, stream, tick, index, draw) - 0.5;
+    double v = b2_uniform_draw(seed, stream, tick, index, draw + 1);
+    draw += 2;
+    double us = 0.5 - fabs(u);
+    double candidate = floor((2.0 * a / us + b) * u + lambda + 0.43);
+    if (us >= 0.07 && v <= squeeze) return candidate;
+    if (candidate < 0.0 || (us < 0.013 && v > us)) continue;
+    double left = log(v * inverse_alpha / (a / (us * us) + b));
+    double right = -lambda + candidate * log(lambda) - b2_log_gamma_positive(candidate + 1.0);
+    if (left <= right) return candidate;
+  }
+  return 0.0;
+}
+
+// Brian2 timestep(): floor((t + 1e-3 dt) / dt) with range checks.
+__device__ __forceinline__ u64 b2_timestep(double time, double dt, u32& err) {
+  double steps = (time + 1e-3 * dt) / dt;
+  if (!(time >= 0.0 && isfinite(dt) && dt > 0.0 && isfinite(steps) && steps < 9223372036854775808.0)) {
+    err |= B2_ERR_TIMESTEP;
+    return 0;
+  }
+  return (u64)steps;
+}
+
+__device__ __forceinline__ double b2_timestep_reg(double time, double dt, u32& err) {
+  u64 v = b2_timestep(time, dt, err);
+  if (v > 9007199254740992ull) {
+    err |= B2_ERR_TIMESTEP;
+    return 0.0;
+  }
+  return (double)v;
+}
+
+__device__ __forceinline__ double b2_binomial_checked(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
+                                                      double p, bool approximate, u32& err) {
+  if (!(isfinite(p) && p >= 0.0 && p <= 1.0)) {
+    err |= B2_ERR_BINOMIAL;
+    return 0.0;
+  }
+  return b2_binomial(seed, stream, tick, index, n, p, approximate);
+}
+
+// ---------------------------------------------------------------- scalar ops
+// Per-op rules of the reference evaluate() (executor.rs:5932-6158).
+__device__ __forceinline__ double b2_exprel(double a) {
+  if (fabs(a) < 1e-16) return 1.0;
+  if (a > 717.0) return __longlong_as_double(0x7ff0000000000000ll);
+  return expm1(a) / a;
+}
+__device__ __forceinline__ double b2_trunc(double a) {
+  return fabs(a) <= 9007199254740992.0 ? trunc(a) : __longlong_as_double(0x7ff8000000000000ll);
+}
+__device__ __forceinline__ double b2_round_f32(double a) {
+  float f = (float)a;
+  return isfinite(f) ? (double)f : __longlong_as_double(0x7ff8000000000000ll);
+}
+__device__ __forceinline__ double b2_fmod_floor(double a, double b) { return a - b * floor(a / b); }
+__device__ __forceinline__ double b2_tick_offset(double a, i64 offset) {
+  double r = a + (double)offset;
+  return fabs(r) <= 9007199254740992.0 ? r : __longlong_as_double(0x7ff8000000000000ll);
+}
+
+// ---------------------------------------------------------------- casts
+// Rust `as` float -> int casts saturate and send NaN to 0.
+__device__ __forceinline__ i64 b2_f2i64(double x) {
+  if (isnan(x)) return 0;
+  if (x <= -9223372036854775808.0) return (i64)0x8000000000000000ull;
+  if (x >= 9223372036854775808.0) return 0x7fffffffffffffffll;
+  return (i64)x;
+}
+__device__ __forceinline__ u64 b2_f2u64(double x) {
+  if (isnan(x) || x <= 0.0) return 0;
+  if (x >= 18446744073709551616.0) return 0xffffffffffffffffull;
+  return (u64)x;
+}
+__device__ __forceinline__ i32 b2_f2i32(double x) {
+  i64 v = b2_f2i64(x);
+  return v < -2147483648ll ? (i32)0x80000000u : v > 2147483647ll ? 2147483647 : (i32)v;
+}
+__device__ __forceinline__ u32 b2_f2u32(double x) {
+  u64 v = b2_f2u64(x);
+  return v > 0xffffffffull ? 0xffffffffu : (u32)v;
+}
+
+template <class T>
+__device__ __forceinline__ T b2_floor_mod(T a, T b) {
+  T q = a / b, r = a % b;
+  T fq = (r != 0 && ((r < 0) != (b < 0))) ? (T)(q - 1) : q;
+  return (T)(a - fq * b);
+}
+template <class T>
+__device__ __forceinline__ T b2_floor_div(T a, T b) {
+  T q = a / b, r = a % b;
+  return (r != 0 && ((r < 0) != (b < 0))) ? (T)(q - 1) : q;
+}
+
+// Integer register ops (integer_unary_value / integer_binary_value,
+// executor.rs:5831-5930).  dtype: 0 i32, 1 i64, 2 u32, 3 u64; op: 0 add,
+// 1 sub, 2 mul, 3 floor-mod, 4 floor-div, 5 gt, 6 ge, 7 lt, 8 le.
+__device__ __forceinline__ double b2_int_neg(int dtype, double a) {
+  u64 r = b2_raw(a);
+  return dtype == 0 ? b2_bits((u64)(u32)(0u - (u32)r)) : b2_bits(0ull - r);
+}
+__device__ __forceinline__ double b2_int_abs(int dtype, double a) {
+  u64 r = b2_raw(a);
+  if (dtype == 0) {
+    i32 v = (i32)(u32)r;
+    return b2_bits((u64)(v < 0 ? (0u - (u32)v) : (u32)v));
+  }
+  i64 v = (i64)r;
+  return b2_bits(v < 0 ? 0ull - (u64)v : (u64)v);
+}
+template <class S, class U>
+__device__ __forceinline__ double b2_int_signed(int op, S a, S b, S minv, u32& err, bool narrow) {
+  u64 out;
+  switch (op) {
+    case 5: return a > b ? 1.0 : 0.0;
+    case 6: return a >= b ? 1.0 : 0.0;
+    case 7: return a < b ? 1.0 : 0.0;
+    case 8: return a <= b ? 1.0 : 0.0;
+    case 0: out = (u64)(U)((U)a + (U)b); break;
+    case 1: out = (u64)(U)((U)a - (U)b); break;
+    case 2: out = (u64)(U)((U)a * (U)b); break;
+    case 3:
+      if (b == 0) { err |= B2_ERR_INTDIV; return 0.0; }
+      out = (u64)(U)((a == minv && b == (S)-1) ? (S)0 : b2_floor_mod<S>(a, b));
+      break;
+    default:
+      if (b == 0) { err |= B2_ERR_INTDIV; return 0.0; }
+      out = (u64)(U)((a == minv && b == (S)-1) ? minv : b2_floor_div<S>(a, b));
+      break;
+  }
+  return b2_bits(narrow ? (u64)(u32)out : out);
+}
+template <class U>
+__device__ __forceinline__ double b2_int_unsigned(int op, U a, U b, u32& err) {
+  switch (op) {
+    case 5: return a > b ? 1.0 : 0.0;
+    case 6: return a >= b ? 1.0 : 0.0;
+    case 7: return a < b ? 1.0 : 0.0;
+    case 8: return a <= b ? 1.0 : 0.0;
+    case 0: return b2_bits((u64)(U)(a + b));
+    case 1: return b2_bits((u64)(U)(a - b));
+    case 2: return b2_bits((u64)(U)(a * b));
+    case 3:
+      if (b == 0) { err |= B2_ERR_INTDIV; return 0.0; }
+      return b2_bits((u64)(a % b));
+    default:
+      if (b == 0) { err |= B2_ERR_INTDIV; return 0.0; }
+      return b2_bits((u64)(a / b));
+  }
+}
+__device__ __forceinline__ double b2_int_binary(int dtype, int op, double a, double b, u32& err) {
+  u64 x = b2_raw(a), y = b2_raw(b);
+  switch (dtype) {
+    case 0: return b2_int_signed<i32, u32>(op, (i32)(u32)x, (i32)(u32)y, (i32)0x80000000u, err, true);
+    case 1: return b2_int_signed<i64, u64>(op, (i64)x, (i64)y, (i64)0x8000000000000000ull, err, false);
+    case 2: return b2_int_unsigned<u32>(op, (u32)x, (u32)y, err);
+    default: return b2_int_unsigned<u64>(op, x, y, err);
+  }
+}
+
+// ---------------------------------------------------------------- atomics
+// f32 state commit `(float)((double)old + add)`, applied as one atomic step.
+// Every event of a constant-weight pathway applies the same map, so the final
+// value is independent of the order in which the updates land.
+// Returns false when the rounded result is not finite (the reference raises).
+__device__ __forceinline__ bool b2_atomic_add_f32_via_f64(float* addr, double add) {
+  u32* a = (u32*)addr;
+  u32 old = *((volatile u32*)a), assumed;
+  float next;
+  do {
+    assumed = old;
+    next = (float)((double)__uint_as_float(assumed) + add);
+    old = atomicCAS(a, assumed, __float_as_uint(next));
+  } while (old != assumed);
+  return isfinite(next);
+}
+
+// ---------------------------------------------------------------- look-back
+__device__ __forceinline__ u64 b2_ld_acquire(const u64* p) {
+  u64 v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void b2_st_release(u64* p, u64 v) {
+  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+// Tile status word: [63:40] tick tag, [39:38] flag (1 aggregate, 2 inclusive
+// prefix), [37:0] count.  The tick tag makes stale words of earlier ticks
+// invisible, so the status array never needs clearing.
+#define B2_TAG(tick) (((tick) + 1ull) & 0xffffffull)
+__device__ __forceinline__ u64 b2_status(u64 tick, u64 flag, u64 value) {
+  return (B2_TAG(tick) << 40) | (flag << 38) | (value & ((1ull << 38) - 1));
+}
+
+// Block-level exclusive offsets of `fired` lanes and the block's global base
+// in the tick's ascending spike list.  `tile` is this block's position in
+// neuron order (taken from a ticket, so every predecessor tile has already
+// started and will publish).  Returns the block-global exclusive offset of this
+// lane; *block_total/*base are broadcast.  Waits are bounded: on timeout the
+// error bit is raised and the block continues with base 0.
+template <int THREADS>
+__device__ __forceinline__ u32 b2_compact_offsets(bool fired, u64 tick, u32 tile, u64* status,
+                                                  u32* s_warp, u64* s_base, u32& err,
+                                                  u32* block_total_out) {
+  const u32 lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  u32 ballot = __ballot_sync(0xffffffffu, fired);
+  u32 within = __popc(ballot & ((1u << lane) - 1u));
+  if (lane == 0) s_warp[warp] = __popc(ballot);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    u32 acc = 0;
+    for (int w = 0; w < THREADS / 32; ++w) {
+      u32 c = s_warp[w];
+      s_warp[w] = acc;
+      acc += c;
+    }
+    s_warp[THREADS / 32] = acc;
+    u64 base = 0;
+    if (tile == 0) {
+      b2_st_release(&status[0], b2_status(tick, 2, acc));
+    } else {
+      b2_st_release(&status[tile], b2_status(tick, 1, acc));
+      u64 running = 0;
+      int j = (int)tile - 1;
+      u32 spins = 0;
+      const u64 tag = B2_TAG(tick);
+      while (j >= 0) {
+        u64 s = b2_ld_acquire(&status[j]);
+        if ((s >> 40) != tag || ((s >> 38) & 3ull) == 0) {
+          if (++spins > (1u << 24)) {
+            err |= B2_ERR_LOOKBACK;
+            running = 0;
+            break;
+          }
+          if (spins > 64) __nanosleep(64);
+          continue;
+        }
+        running += s & ((1ull << 38) - 1);
+        if (((s >> 38) & 3ull) == 2) break;
+        --j;
+      }
+      base = running;
+      b2_st_release(&status[tile], b2_status(tick, 2, running + acc));
+    }
+    *s_base = base;
+  }
+  __syncthreads();
+  *block_total_out = s_warp[THREADS / 32];
+  return s_warp[warp] + within;
+}

@@ -1,0 +1,121 @@
+/*
+ * b2gpu: C ABI of the B200 engine for AtlasIR (`atlasir-v1`) simulations.
+ *
+ * Drop-in boundary for the reference's execution core.  The reference runs its
+ * engine as the `b2-runner MODEL.json OUTDIR` subprocess
+ * (brian2-rust/src/model.rs:4596-4677, main.rs:2-7) over the Rust
+ * `Runtime` (brian2-rust/src/executor.rs:3473-4824).  The entry points below
+ * map one to one onto that runtime, and follow the in-tree C ABI precedent for
+ * GPU offload (brian2-rust/python/brian2_rust/mpi_runtime/gpu_cuda.cpp:17-51,
+ * loaded with dlopen/dlsym in mpi_runtime/gpu.rs:17-49):
+ *   - an opaque handle; constructors return NULL on failure;
+ *   - a caller-owned error buffer (char *error, size_t capacity), always
+ *     NUL-terminated when capacity > 0;
+ *   - int return codes: 0 success, non-zero failure;
+ *   - plain C types only; one host thread per engine.
+ * A failed engine is poisoned like the reference `Runtime` (executor.rs:
+ * 3917-3925): every later call fails until it is destroyed.
+ */
+#ifndef B2GPU_H
+#define B2GPU_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2G_ABI_VERSION 1
+
+typedef struct b2g_engine b2g_engine;
+
+typedef struct b2g_options {
+  uint32_t struct_size;   /* sizeof(b2g_options); lets the struct grow compatibly */
+  int32_t device;         /* CUDA device ordinal, -1 for the current device */
+  uint32_t chunk_ticks;   /* ticks per CUDA-graph replay, 0 for the default (128) */
+  uint32_t use_graphs;    /* 1: replay captured graphs (default), 0: direct launches */
+  uint64_t ring_capacity; /* spike-ring entries per event stream, 0 for automatic */
+} b2g_options;
+
+typedef struct b2g_stats {
+  uint64_t ticks;              /* ticks simulated so far */
+  uint64_t synaptic_events;    /* summary.json `synaptic_events` so far */
+  uint64_t spikes;             /* events recorded on every stream so far */
+  uint64_t kernel_launches;    /* launches of the engine's kernels so far */
+  uint64_t launches_per_tick;  /* kernels per tick in the compiled plan */
+  double simulation_seconds;   /* wall time inside b2g_step */
+  double build_seconds;        /* b2g_create: device state, topology, compile */
+  double compile_seconds;      /* NVRTC share of build_seconds */
+  double device_seconds;       /* CUDA-event time of the tick kernels */
+  uint64_t h2d_bytes;          /* host->device bytes moved by b2g_step */
+  uint64_t d2h_bytes;          /* device->host bytes moved by b2g_step (spike drain) */
+} b2g_stats;
+
+typedef struct b2g_kernel_time {
+  char name[64];
+  uint64_t launches;
+  double total_ms;
+} b2g_kernel_time;
+
+/* Fill `options` with defaults (struct_size set). */
+void b2g_default_options(b2g_options* options);
+
+/* Validate and load an AtlasIR document and build the device plan.
+ * Replaces `Runtime::new` (executor.rs:3473) after `Model::validate`
+ * (model.rs:3203).  Unsupported models fail here, before any result file
+ * exists (brian2-rust/AtlasIR.md:66-70). */
+b2g_engine* b2g_create(const char* json, size_t json_len, const b2g_options* options, char* error,
+                       size_t error_capacity);
+
+/* Advance at most `max_ticks` ticks; *finished is set to 1 when the run is
+ * complete.  Replaces `Runtime::step` (executor.rs:3917). */
+int b2g_step(b2g_engine* engine, uint64_t max_ticks, int* finished, char* error, size_t error_capacity);
+
+/* Write results.bin (B2DMP001 v3), events.bin (B2EVT001, when the model has
+ * event streams) and summary.json into the existing directory `outdir`.
+ * Replaces `Runtime::write_results` plus the file writing of `execute`
+ * (executor.rs:4749-4824). */
+int b2g_write_results(b2g_engine* engine, const char* outdir, char* error, size_t error_capacity);
+
+int b2g_get_stats(const b2g_engine* engine, b2g_stats* stats, char* error, size_t error_capacity);
+
+/* Advance `ticks` ticks launching every kernel directly, bracketed by CUDA
+ * events on the engine's stream; fills up to `capacity` per-kernel records
+ * (launch count, summed milliseconds) and sets *count.  No reference
+ * counterpart: measurement support for the roofline report. */
+int b2g_profile(b2g_engine* engine, uint64_t ticks, b2g_kernel_time* out, size_t capacity, size_t* count,
+                char* error, size_t error_capacity);
+
+/* Copy the raw storage bytes of a population state array (dtype width x
+ * count); *needed receives the size.  Passing dst=NULL queries the size. */
+int b2g_read_state(b2g_engine* engine, uint32_t population, const char* name, void* dst, size_t capacity,
+                   size_t* needed, char* error, size_t error_capacity);
+
+/* Ascending spike indices of `population` at absolute `tick`. */
+int b2g_spikes(b2g_engine* engine, uint32_t population, uint64_t tick, uint32_t* dst, size_t capacity,
+               size_t* count, char* error, size_t error_capacity);
+
+/* The generated CUDA source of the compiled plan (diagnostics). */
+int b2g_generated_source(const b2g_engine* engine, char* dst, size_t capacity, size_t* needed);
+
+/* Build the plan of a model and compile its generated kernels for sm_100a
+ * without a GPU; copies the generated source to dst (NULL queries *needed).
+ * Same validation and capability errors as b2g_create. */
+int b2g_codegen(const char* json, size_t json_len, char* dst, size_t capacity, size_t* needed, char* error,
+                size_t error_capacity);
+
+void b2g_destroy(b2g_engine* engine);
+
+const char* b2g_version(void);
+
+/* The complete `b2-runner` command line (argv[0] is ignored):
+ *   MODEL.json OUTDIR | --validate MODEL.json
+ * Same exit codes, stdout line and stderr prefix as model.rs:4596-4677. */
+int b2g_run_cli(int argc, const char* const* argv);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B2GPU_H */

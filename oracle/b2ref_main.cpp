@@ -18,6 +18,16 @@
 
 int main(int argc, char** argv) {
   try {
+    if (argc == 5 && std::strcmp(argv[1], "--timed") == 0) {
+      // b2ref --timed WARMUP_TICKS TIMED_TICKS MODEL.json
+      b2ir::Model m = b2ir::load_model_file(argv[4]);
+      oracle::TimedSample s = oracle::timed_sample(m, std::stoull(argv[2]), std::stoull(argv[3]));
+      std::printf("{\"ticks\": %llu, \"synaptic_events\": %llu, \"spikes\": %llu, \"seconds\": %.9f, "
+                  "\"build_seconds\": %.6f}\n",
+                  (unsigned long long)s.ticks, (unsigned long long)s.synaptic_events,
+                  (unsigned long long)s.spikes, s.seconds, s.build_seconds);
+      return 0;
+    }
     if (argc == 4 && std::strcmp(argv[1], "--sample") == 0) {
       uint64_t k = std::stoull(argv[2]);
       b2ir::Model m = b2ir::load_model_file(argv[3]);

@@ -1631,6 +1631,32 @@ struct Runtime {
 
 }  // namespace
 
+TimedSample timed_sample(const Model& model, uint64_t warmup, uint64_t timed) {
+  TimedSample s;
+  auto t0 = std::chrono::steady_clock::now();
+  Runtime rt(model);
+  auto t1 = std::chrono::steady_clock::now();
+  s.build_seconds = std::chrono::duration<double>(t1 - t0).count();
+  rt.advance(warmup);
+  auto count = [&](uint64_t& events, uint64_t& spikes) {
+    events = spikes = 0;
+    for (const auto& syn : rt.synapses)
+      for (const auto& pw : syn.pathways) events += pw.topology.delivered;
+    for (const auto& p : rt.populations)
+      for (const auto& h : p.event_history) spikes += h.size();
+  };
+  uint64_t e0, s0, e1, s1;
+  count(e0, s0);
+  auto t2 = std::chrono::steady_clock::now();
+  s.ticks = rt.advance(timed);
+  auto t3 = std::chrono::steady_clock::now();
+  count(e1, s1);
+  s.seconds = std::chrono::duration<double>(t3 - t2).count();
+  s.synaptic_events = e1 - e0;
+  s.spikes = s1 - s0;
+  return s;
+}
+
 b2dump::ResultSet execute(const Model& model, RunStats* stats, uint64_t max_ticks) {
   for (const auto& p : model.populations)
     check(p.rate_monitor_count == 0, "rate monitors are outside the oracle's subset");

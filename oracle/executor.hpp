@@ -24,4 +24,12 @@ struct RunStats {
 b2dump::ResultSet execute(const b2ir::Model& model, RunStats* stats = nullptr,
                           uint64_t max_ticks = UINT64_MAX);
 
+// Timing harness for the CPU baseline: build once, run `warmup` ticks, then
+// time `timed` ticks; returns the synaptic events and spikes of the timed part.
+struct TimedSample {
+  uint64_t ticks = 0, synaptic_events = 0, spikes = 0;
+  double build_seconds = 0.0, seconds = 0.0;
+};
+TimedSample timed_sample(const b2ir::Model& model, uint64_t warmup, uint64_t timed);
+
 }  // namespace oracle

@@ -1,0 +1,297 @@
+"""Generate the committed AtlasIR fixtures from the reference's own frontend.
+
+Run in a container that has the reference checkout (default /root/reference):
+
+    python tests/golden/make_fixtures.py [--reference /root/reference]
+
+What it writes (all under tests/golden/):
+  reference-v1/        the reference's golden b2-runner run, copied verbatim
+                       (brian2-rust/tests/fixtures/reference-v1/): model.json,
+                       results.bin, events.bin, summary.json
+  models/*.json[.gz]   AtlasIR documents lowered by the reference's
+                       brian2_rust.export.lower_network (export.py:2540) from
+                       small versions of the benchmark networks (CUBA, COBAHH,
+                       STDP, Brunel, CUBA + PoissonInput on a fixed in-degree
+                       topology) and the full-size CUBA 4k config
+  brian_numpy/*.npz    spikes and final state of the same networks run by
+                       Brian2's numpy runtime (the reference's cross-backend
+                       gate, brian2-rust/examples/cuba.py:140-160)
+
+The reference frontend needs two local build steps that this script performs
+in tests/golden/_frontend/ (git-ignored): a `pyparsing` alias onto pip's
+vendored copy, and a copy of brian2/ with its two Cython extensions built.
+"""
+from __future__ import annotations
+
+import argparse
+import gzip
+import json
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+FRONTEND = HERE / "_frontend"
+
+
+def prepare_frontend(reference: Path) -> None:
+    shim = FRONTEND / "shim"
+    shim.mkdir(parents=True, exist_ok=True)
+    (shim / "pyparsing.py").write_text(
+        "import sys\nimport pip._vendor.pyparsing as _p\nsys.modules[__name__] = _p\n")
+    src = FRONTEND / "src"
+    if not (src / "brian2" / "synapses").exists():
+        shutil.copytree(reference / "brian2", src / "brian2")
+        for p in (src / "brian2").rglob("*"):
+            p.chmod(0o755 if p.is_dir() else 0o644)
+    setup = src / "build_ext.py"
+    setup.write_text(
+        "import numpy\nfrom setuptools import setup, Extension\nfrom Cython.Build import cythonize\n"
+        "exts=[Extension('brian2.synapses.cythonspikequeue',['brian2/synapses/cythonspikequeue.pyx'],"
+        "include_dirs=[numpy.get_include()]),\n"
+        "Extension('brian2.memory.cythondynamicarray',['brian2/memory/cythondynamicarray.pyx'],"
+        "include_dirs=[numpy.get_include(),'brian2/devices/cpp_standalone/brianlib'])]\n"
+        "setup(name='b2', ext_modules=cythonize(exts, language_level=3), script_args=['build_ext','--inplace'])\n")
+    if not list((src / "brian2" / "synapses").glob("cythonspikequeue*.so")):
+        subprocess.run([sys.executable, "build_ext.py"], cwd=src, check=True, capture_output=True)
+    sys.path[:0] = [str(shim), str(src), str(reference / "brian2-rust" / "python")]
+
+
+def write_model(model: dict, name: str) -> Path:
+    out = HERE / "models"
+    out.mkdir(exist_ok=True)
+    text = json.dumps(model, sort_keys=True, separators=(",", ":"))
+    if len(text) > 1_000_000:
+        path = out / f"{name}.json.gz"
+        with gzip.open(path, "wt") as f:
+            f.write(text)
+    else:
+        path = out / f"{name}.json"
+        path.write_text(text)
+    return path
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    args = ap.parse_args()
+    reference = Path(args.reference)
+    golden = reference / "brian2-rust" / "tests" / "fixtures" / "reference-v1"
+    dst = HERE / "reference-v1"
+    dst.mkdir(exist_ok=True)
+    for name in ("model.json", "reference/results.bin", "reference/events.bin", "reference/summary.json"):
+        shutil.copyfile(golden / name, dst / Path(name).name)
+
+    prepare_frontend(reference)
+    import numpy as np
+    import brian2 as b
+    import brian2_rust  # noqa: F401  (registers the atlas device)
+    from brian2_rust.export import lower_network
+
+    b.prefs.codegen.target = "numpy"
+    (HERE / "brian_numpy").mkdir(exist_ok=True)
+
+    # ---------------------------------------------------------------- CUBA
+    def cuba(n, p, ticks, seed, numpy_run):
+        b.start_scope()
+        taum, taue, taui = 20 * b.ms, 5 * b.ms, 10 * b.ms
+        Vt, Vr, El = -50 * b.mV, -60 * b.mV, -49 * b.mV
+        eqs = """
+        dv/dt  = (ge+gi-(v-El))/taum : volt (unless refractory)
+        dge/dt = -ge/taue : volt
+        dgi/dt = -gi/taui : volt
+        """
+        clock = b.Clock(dt=0.1 * b.ms, name="clock")
+        P = b.NeuronGroup(n, eqs, threshold="v>Vt", reset="v = Vr", refractory=5 * b.ms, method="exact",
+                          name="neurons", clock=clock)
+        rng = np.random.default_rng(seed)
+        P.v = Vr + rng.random(n) * (Vt - Vr)
+        we, wi = (60 * 0.27 / 10) * b.mV, (-20 * 4.5 / 10) * b.mV
+        Ce = b.Synapses(P, P, on_pre="ge += we", name="exc", clock=clock)
+        Ci = b.Synapses(P, P, on_pre="gi += wi", name="inh", clock=clock)
+        ne = int(n * 0.8)
+        mask = rng.random((n, n)) < p
+        src, tgt = np.nonzero(mask)
+        e = src < ne
+        Ce.connect(i=src[e], j=tgt[e])
+        Ci.connect(i=src[~e], j=tgt[~e])
+        spikes = b.SpikeMonitor(P, name="spikes")
+        trace = b.StateMonitor(P, ["v", "ge"], record=[0, 1, n // 2], name="trace", clock=clock)
+        net = b.Network(P, Ce, Ci, spikes, trace)
+        ns = dict(taum=taum, taue=taue, taui=taui, Vt=Vt, Vr=Vr, El=El, we=we, wi=wi)
+        model = lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+        if numpy_run:
+            net.run(ticks * 0.1 * b.ms, namespace=ns)
+            return model, dict(spike_i=np.array(spikes.i[:]), spike_t=np.array(spikes.t / b.second),
+                               v=np.array(P.v[:] / b.volt), ge=np.array(P.ge[:] / b.volt),
+                               trace_v=np.array(trace.v / b.volt))
+        return model, None
+
+    model, ref = cuba(400, 0.1, 1000, 1, True)
+    write_model(model, "cuba_small")
+    np.savez_compressed(HERE / "brian_numpy" / "cuba_small.npz", **ref)
+    model, _ = cuba(4000, 0.02, 10000, 1, False)
+    write_model(model, "cuba_4k")
+
+    # ---------------------------------------------------------------- COBAHH
+    def cobahh(n, p, ticks, seed, numpy_run):
+        b.start_scope()
+        area = 20000 * b.umetre ** 2
+        Cm = (1 * b.ufarad * b.cm ** -2) * area
+        gl = (5e-5 * b.siemens * b.cm ** -2) * area
+        El, EK, ENa = -60 * b.mV, -90 * b.mV, 50 * b.mV
+        g_na = (100 * b.msiemens * b.cm ** -2) * area
+        g_kd = (30 * b.msiemens * b.cm ** -2) * area
+        VT, taue, taui, Ee, Ei = -63 * b.mV, 5 * b.ms, 10 * b.ms, 0 * b.mV, -80 * b.mV
+        we, wi = 6 * b.nS, 67 * b.nS
+        eqs = b.Equations("""
+        dv/dt = (gl*(El-v)+ge*(Ee-v)+gi*(Ei-v)-g_na*(m*m*m)*h*(v-ENa)-g_kd*(n*n*n*n)*(v-EK))/Cm : volt
+        dm/dt = alpha_m*(1-m)-beta_m*m : 1
+        dn/dt = alpha_n*(1-n)-beta_n*n : 1
+        dh/dt = alpha_h*(1-h)-beta_h*h : 1
+        dge/dt = -ge*(1./taue) : siemens
+        dgi/dt = -gi*(1./taui) : siemens
+        alpha_m = 0.32*(mV**-1)*4*mV/exprel((13*mV-v+VT)/(4*mV))/ms : Hz
+        beta_m = 0.28*(mV**-1)*5*mV/exprel((v-VT-40*mV)/(5*mV))/ms : Hz
+        alpha_h = 0.128*exp((17*mV-v+VT)/(18*mV))/ms : Hz
+        beta_h = 4./(1+exp((40*mV-v+VT)/(5*mV)))/ms : Hz
+        alpha_n = 0.032*(mV**-1)*5*mV/exprel((15*mV-v+VT)/(5*mV))/ms : Hz
+        beta_n = .5*exp((10*mV-v+VT)/(40*mV))/ms : Hz
+        """)
+        clock = b.Clock(dt=0.1 * b.ms, name="clock")
+        P = b.NeuronGroup(n, model=eqs, threshold="v>-20*mV", refractory=3 * b.ms, method="exponential_euler",
+                          name="neurons", clock=clock)
+        ne = int(n * 0.8)
+        Ce = b.Synapses(P[:ne], P, on_pre="ge+=we", name="exc", clock=clock)
+        Ci = b.Synapses(P[ne:], P, on_pre="gi+=wi", name="inh", clock=clock)
+        rng = np.random.default_rng(seed)
+        mask = rng.random((n, n)) < p
+        src, tgt = np.nonzero(mask)
+        e = src < ne
+        Ce.connect(i=src[e], j=tgt[e])
+        Ci.connect(i=src[~e] - ne, j=tgt[~e])
+        P.v = El + rng.normal(0, 5, n) * b.mV
+        P.ge = (rng.normal(0, 1.5, n) + 4) * 10 * b.nS
+        P.gi = (rng.normal(0, 12, n) + 20) * 10 * b.nS
+        spikes = b.SpikeMonitor(P, name="spikes")
+        net = b.Network(P, Ce, Ci, spikes)
+        ns = dict(area=area, Cm=Cm, gl=gl, El=El, EK=EK, ENa=ENa, g_na=g_na, g_kd=g_kd, VT=VT, taue=taue,
+                  taui=taui, Ee=Ee, Ei=Ei, we=we, wi=wi)
+        model = lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+        if numpy_run:
+            net.run(ticks * 0.1 * b.ms, namespace=ns)
+            return model, dict(spike_i=np.array(spikes.i[:]), spike_t=np.array(spikes.t / b.second),
+                               v=np.array(P.v[:] / b.volt))
+        return model, None
+
+    model, ref = cobahh(400, 0.1, 1000, 2, True)
+    write_model(model, "cobahh_small")
+    np.savez_compressed(HERE / "brian_numpy" / "cobahh_small.npz", **ref)
+    model, _ = cobahh(4000, 0.02, 10000, 2, False)
+    write_model(model, "cobahh_4k")
+
+    # ---------------------------------------------------------------- STDP
+    def stdp(n_in, n_out, indegree, ticks, seed):
+        b.start_scope()
+        taum, taupre, taupost = 10 * b.ms, 20 * b.ms, 20 * b.ms
+        Ee, vt, vr, El, taue = 0 * b.mV, -54 * b.mV, -60 * b.mV, -74 * b.mV, 5 * b.ms
+        gmax, dApre = 0.01, 0.01
+        dApost = -dApre * taupre / taupost * 1.05
+        dApost *= gmax
+        dApre *= gmax
+        clock = b.Clock(dt=0.1 * b.ms, name="clock")
+        inputs = b.PoissonGroup(n_in, rates=15 * b.Hz, name="inputs", clock=clock)
+        neurons = b.NeuronGroup(n_out, "dv/dt = (ge * (Ee-v) + El - v) / taum : volt\ndge/dt = -ge / taue : 1",
+                                threshold="v>vt", reset="v = vr", method="euler", name="neurons", clock=clock)
+        neurons.v = vr
+        S = b.Synapses(inputs, neurons,
+                       """w : 1
+                          dApre/dt = -Apre / taupre : 1 (event-driven)
+                          dApost/dt = -Apost / taupost : 1 (event-driven)""",
+                       on_pre="ge += w\nApre += dApre\nw = clip(w + Apost, 0, gmax)",
+                       on_post="Apost += dApost\nw = clip(w + Apre, 0, gmax)", name="stdp", clock=clock)
+        rng = np.random.default_rng(seed)
+        src = np.concatenate([rng.choice(n_in, indegree, replace=False) for _ in range(n_out)])
+        tgt = np.repeat(np.arange(n_out), indegree)
+        S.connect(i=src, j=tgt)
+        S.w = rng.random(len(src)) * gmax
+        spikes = b.SpikeMonitor(neurons, name="spikes")
+        net = b.Network(inputs, neurons, S, spikes)
+        ns = dict(taum=taum, taupre=taupre, taupost=taupost, Ee=Ee, vt=vt, vr=vr, El=El, taue=taue, gmax=gmax,
+                  dApre=dApre, dApost=dApost)
+        return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+
+    write_model(stdp(1000, 20, 1000, 2000, 5), "stdp_small")
+
+    # ---------------------------------------------------------------- Brunel (f32 v, delay 1.5 ms)
+    def brunel(n, indegree, ticks, seed):
+        b.start_scope()
+        b.set_device("atlas", build_on_run=False)
+        dev = b.get_device()
+        tau, theta, reset, J = 20 * b.ms, 20 * b.mV, 10 * b.mV, 0.1 * b.mV
+        n_e = int(n * 0.8)
+        c_e = int(indegree * 0.8)
+        c_i = indegree - c_e
+        nu_thr = theta / (J * c_e * tau)
+        clock = b.Clock(dt=0.1 * b.ms, name="clock")
+        P = b.NeuronGroup(n, "dv/dt = -v/tau : volt (unless refractory)", threshold="v > theta", reset="v = reset",
+                          refractory=2 * b.ms, name="neurons", dtype={"v": np.float32}, clock=clock)
+        rng = np.random.default_rng(seed)
+        P.v = rng.random(n) * theta
+        syns = []
+        for name, src, k, w, s in (("excitatory", P[:n_e], c_e, J, seed + 1),
+                                   ("inhibitory", P[n_e:], c_i, -5 * J, seed + 2)):
+            S = b.Synapses(src, P, "weight : volt (constant, shared)", on_pre="v_post += weight",
+                           delay=1.5 * b.ms, name=f"{name}_synapses", clock=clock)
+            dev.connect_fixed_indegree(S, k, seed=s)
+            S.weight = w
+            syns.append(S)
+        ext = b.PoissonInput(P, "v", N=c_e, rate=2 * nu_thr, weight=J)
+        spikes = b.SpikeMonitor(P, name="spikes")
+        net = b.Network(P, *syns, ext, spikes)
+        model = lower_network(net, ticks * 0.1 * b.ms, namespace=dict(tau=tau, theta=theta, reset=reset),
+                              rng_seed=seed)
+        b.set_device("runtime")
+        return model
+
+    write_model(brunel(2000, 200, 1000, 4), "brunel_small")
+
+    # ---------------------------------------------------------------- CUBA on fixed in-degree + PoissonInput (C2 shape)
+    def cuba_poisson(n, indegree, ticks, seed):
+        b.start_scope()
+        b.set_device("atlas", build_on_run=False)
+        dev = b.get_device()
+        taum, taue, taui = 20 * b.ms, 5 * b.ms, 10 * b.ms
+        Vt, Vr, El = -50 * b.mV, -60 * b.mV, -49 * b.mV
+        eqs = """
+        dv/dt  = (ge+gi-(v-El))/taum : volt (unless refractory)
+        dge/dt = -ge/taue : volt
+        dgi/dt = -gi/taui : volt
+        """
+        clock = b.Clock(dt=0.1 * b.ms, name="clock")
+        P = b.NeuronGroup(n, eqs, threshold="v>Vt", reset="v = Vr", refractory=5 * b.ms, method="exact",
+                          name="neurons", clock=clock)
+        rng = np.random.default_rng(seed)
+        P.v = Vr + rng.random(n) * (Vt - Vr)
+        we, wi = (60 * 0.27 / 10) * b.mV, (-20 * 4.5 / 10) * b.mV
+        ne = int(n * 0.8)
+        Ce = b.Synapses(P[:ne], P, on_pre="ge += we", name="exc", clock=clock)
+        Ci = b.Synapses(P[ne:], P, on_pre="gi += wi", name="inh", clock=clock)
+        dev.connect_fixed_indegree(Ce, int(indegree * 0.8), seed=seed + 1)
+        dev.connect_fixed_indegree(Ci, indegree - int(indegree * 0.8), seed=seed + 2)
+        ext = b.PoissonInput(P, "ge", N=100, rate=10 * b.Hz, weight=we)
+        spikes = b.SpikeMonitor(P, name="spikes")
+        net = b.Network(P, Ce, Ci, ext, spikes)
+        model = lower_network(net, ticks * 0.1 * b.ms,
+                              namespace=dict(taum=taum, taue=taue, taui=taui, Vt=Vt, Vr=Vr, El=El, we=we, wi=wi),
+                              rng_seed=seed)
+        b.set_device("runtime")
+        return model
+
+    write_model(cuba_poisson(1000, 100, 1000, 3), "cuba_poisson_small")
+    print("fixtures written under", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,96 @@
+"""The C ABI boundary and the plan compiler, without a GPU.
+
+* libb2gpu.so loads and exports every entry point include/b2gpu.h declares.
+* b2g_codegen builds the plan of each fixture model and compiles the generated
+  kernels for sm_100a with NVRTC (no GPU involved).
+* The plan picks the delivery strategy the reference semantics allow
+  (atomic only for constant-addend pathways) and fuses update/threshold/reset.
+* Unsupported models fail at creation with a capability message, before any
+  result file exists (brian2-rust/AtlasIR.md:66-70).
+"""
+from __future__ import annotations
+
+import gzip
+import json
+import re
+
+import pytest
+
+from conftest import GOLDEN, MODELS, ROOT
+
+
+def declared_symbols():
+    text = (ROOT / "include" / "b2gpu.h").read_text()
+    return sorted(set(re.findall(r"\b(b2g_[a-z_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg.library()
+    names = declared_symbols()
+    assert "b2g_create" in names and "b2g_step" in names and "b2g_run_cli" in names
+    for name in names:
+        assert hasattr(lib, name), name
+
+
+def test_version(pkg):
+    assert "sm_100a" in pkg.version()
+
+
+def kernels(src):
+    return re.findall(r"__global__ void __launch_bounds__\(\d+\) (\w+)", src)
+
+
+def load(name):
+    path = MODELS / f"{name}.json"
+    if path.exists():
+        return path.read_bytes()
+    with gzip.open(MODELS / f"{name}.json.gz", "rb") as f:
+        return f.read()
+
+
+@pytest.mark.parametrize("name,expected", [
+    ("cuba_small", ["statemon", "step", "exc_pre_atomic", "inh_pre_atomic"]),
+    ("cuba_poisson_small", ["step", "exc_pre_atomic", "inh_pre_atomic", "poisson_input"]),
+    ("brunel_small", ["step", "excitatory_synapses_pre_atomic", "inhibitory_synapses_pre_atomic",
+                      "poisson_input", "reset"]),
+    ("cobahh_small", ["step", "exc_pre_atomic", "inh_pre_atomic"]),
+    ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_serial", "stdp_post_edges"]),
+])
+def test_codegen_plan(pkg, name, expected):
+    src = pkg.codegen(load(name))
+    names = kernels(src)
+    assert len(names) == len(expected), names
+    for kernel, suffix in zip(names, expected):
+        assert kernel.endswith(suffix), (kernel, suffix)
+
+
+def test_codegen_golden_fixture(pkg):
+    src = pkg.codegen((GOLDEN / "reference-v1" / "model.json").read_bytes())
+    names = kernels(src)
+    # per-edge delays 1-4 ticks and per-edge weights: ordered (serial) delivery
+    assert sum(n.endswith("_serial") for n in names) == 4
+    assert sum(n.endswith("_step") for n in names) == 2
+
+
+def test_exact_linear_update_is_pure_arithmetic(pkg):
+    """CUBA's exp(-dt/tau) terms fold to host constants computed with glibc, so
+    the per-neuron update issues no device transcendental."""
+    src = pkg.codegen(load("cuba_small"))
+    step = src[src.index("neurons_step"):]
+    step = step[:step.index("b2_compact_offsets")]
+    assert "exp(" not in step and "log(" not in step
+
+
+def test_unsupported_model_fails_before_results(pkg, tmp_path):
+    doc = json.loads(load("cuba_small"))
+    doc["definition"]["clocks"].append(dict(doc["definition"]["clocks"][0], name="second"))
+    doc["run"]["clocks"].append(dict(doc["run"]["clocks"][0]))
+    with pytest.raises(pkg.B2GpuError, match="single clock"):
+        pkg.codegen(json.dumps(doc).encode())
+
+
+def test_malformed_document_is_rejected(pkg):
+    with pytest.raises(pkg.B2GpuError, match="JSON"):
+        pkg.codegen(b"{not json")
+    with pytest.raises(pkg.B2GpuError, match="schema"):
+        pkg.codegen(json.dumps({"schema": "other"}).encode())

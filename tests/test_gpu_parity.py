@@ -1,0 +1,163 @@
+"""GPU engine against the oracle and the reference's golden output (needs a GPU).
+
+Bar: byte-identical results.bin / events.bin where every per-lane operation is
+exact IEEE arithmetic (CUBA, Brunel, CUBA+PoissonInput and the golden fixture:
+their transcendentals fold to host constants computed with glibc).  Models
+with per-neuron device transcendentals (COBAHH's exp/exprel, STDP's trace
+decay) must keep identical spike rasters over the first 50 ms and agree on
+firing statistics after that; states within 1e-12 relative while the rasters
+agree.
+"""
+from __future__ import annotations
+
+import json
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, MODELS, model_file, run_oracle
+from b2results import load_model, read_results
+
+pytestmark = pytest.mark.gpu
+
+EXACT = ["cuba_small", "cuba_poisson_small", "brunel_small"]
+
+
+def gpu_run(pkg, model_path, outdir, **kw):
+    data = model_path.read_bytes()
+    with pkg.Engine(data, device=0, **kw) as eng:
+        eng.run()
+        outdir.mkdir()
+        eng.write_results(outdir)
+        return eng.stats()
+
+
+def assert_same_files(a, b):
+    assert (a / "results.bin").read_bytes() == (b / "results.bin").read_bytes()
+    ea, eb = a / "events.bin", b / "events.bin"
+    assert ea.exists() == eb.exists()
+    if ea.exists():
+        assert ea.read_bytes() == eb.read_bytes()
+
+
+def test_golden_fixture_bytes(pkg, tmp_path):
+    """The reference's golden b2-runner run, reproduced on the GPU byte for byte."""
+    out = tmp_path / "gpu"
+    gpu_run(pkg, GOLDEN / "reference-v1" / "model.json", out)
+    assert (out / "results.bin").read_bytes() == (GOLDEN / "reference-v1" / "results.bin").read_bytes()
+    assert (out / "events.bin").read_bytes() == (GOLDEN / "reference-v1" / "events.bin").read_bytes()
+    summary = json.loads((out / "summary.json").read_text())
+    assert summary["spike_count"] == 155 and summary["synaptic_events"] == 1238
+
+
+@pytest.mark.parametrize("name", EXACT)
+def test_exact_models_match_oracle(pkg, oracle, tmp_path, name):
+    path = model_file(name, tmp_path)
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
+def test_cuba_4k_full_second(pkg, oracle, tmp_path):
+    """Config 0 (CUBA 4000 neurons, ~320k synapses, 10,000 ticks)."""
+    path = model_file("cuba_4k", tmp_path)
+    stats = gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+    assert stats["ticks"] == 10000
+
+
+def raster_until(spikes, tick):
+    return spikes[spikes[:, 0] < tick]
+
+
+@pytest.mark.parametrize("name,tolerance", [("cobahh_small", 1e-12), ("stdp_small", 1e-12)])
+def test_transcendental_models(pkg, oracle, tmp_path, name, tolerance):
+    path = model_file(name, tmp_path)
+    model = load_model(path)
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    g = read_results(tmp_path / "gpu", model)
+    r = read_results(tmp_path / "ref", model)
+    for pg, pr in zip(g.populations, r.populations):
+        np.testing.assert_array_equal(raster_until(pg.spikes, 500), raster_until(pr.spikes, 500))
+        if len(pr.spikes) > 100:
+            assert abs(len(pg.spikes) - len(pr.spikes)) <= 0.01 * len(pr.spikes)
+    assert g.delivered == r.delivered or abs(sum(g.delivered) - sum(r.delivered)) <= 0.01 * sum(r.delivered)
+
+
+def test_cobahh_4k_raster(pkg, oracle, tmp_path):
+    """Config 1 (COBAHH 4000 neurons, exponential Euler): early raster exact,
+    whole-run firing rate within 1%."""
+    path = model_file("cobahh_4k", tmp_path)
+    model = load_model(path)
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    g = read_results(tmp_path / "gpu", model).populations[0]
+    r = read_results(tmp_path / "ref", model).populations[0]
+    np.testing.assert_array_equal(raster_until(g.spikes, 500), raster_until(r.spikes, 500))
+    assert abs(len(g.spikes) - len(r.spikes)) <= 0.01 * len(r.spikes)
+
+
+@pytest.mark.parametrize("kw", [dict(chunk_ticks=1), dict(chunk_ticks=7), dict(use_graphs=False)])
+def test_chunking_and_graphs_do_not_change_results(pkg, oracle, tmp_path, kw):
+    path = MODELS / "cuba_poisson_small.json"
+    gpu_run(pkg, path, tmp_path / "gpu", **kw)
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
+def test_stepwise_api_and_state_readback(pkg, oracle, tmp_path):
+    path = MODELS / "cuba_small.json"
+    model = load_model(path)
+    run_oracle(oracle, path, tmp_path / "ref")
+    ref = read_results(tmp_path / "ref", model)
+    with pkg.Engine(path.read_bytes(), device=0) as eng:
+        assert eng.step(250) is False
+        assert eng.stats()["ticks"] == 250
+        eng.run()
+        v = np.frombuffer(eng.read_state(0, "v"), dtype=np.float64)
+        np.testing.assert_array_equal(v, ref.populations[0].states["v"])
+        last = ref.populations[0].spikes
+        tick = int(last[-1, 0])
+        assert eng.spikes(0, tick) == [int(i) for t, i in last if t == tick]
+
+
+def test_nonfinite_state_raises_instead_of_faulting(pkg):
+    """A value the reference would reject (overflow to inf) sets the device
+    error word; the host raises and poisons the engine."""
+    doc = load_model(MODELS / "cuba_small.json")
+    v = doc["instance"]["populations"][0]["initial_state"]["v"]
+    v[0] = "7fefffffffffffff"  # DBL_MAX: the exact-linear update overflows
+    with pkg.Engine(json.dumps(doc).encode(), device=0) as eng:
+        with pytest.raises(pkg.B2GpuError, match="non-finite"):
+            eng.run()
+        with pytest.raises(pkg.B2GpuError, match="create a new executor"):
+            eng.step(1)
+
+
+def test_scaled_cuba_fixed_indegree_matches_oracle(pkg, oracle, tmp_path):
+    """Config 2's network shape at 20k neurons (in-degree 1000, 2e7 synapses
+    generated on the device) against the oracle's host-side generation."""
+    import importlib
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    template = json.loads((MODELS / "cuba_poisson_small.json").read_text())
+    doc = synthetic.cuba_fixed_indegree(template, n=20000, indegree=1000, ticks=300, seed=9)
+    path = tmp_path / "c2_20k.json"
+    path.write_bytes(synthetic.encode(doc))
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
+def test_cli_runner_drop_in(pkg, oracle, tmp_path):
+    """b2gpu-runner honours the b2-runner argv/output contract."""
+    import subprocess
+    path = MODELS / "cuba_small.json"
+    proc = subprocess.run([str(pkg.runner_path()), str(path), str(tmp_path / "gpu")], capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr
+    assert proc.stdout.startswith("completed 1 populations for 400 neurons")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+    again = subprocess.run([str(pkg.runner_path()), str(path), str(tmp_path / "gpu")], capture_output=True, text=True)
+    assert again.returncode == 1 and again.stderr.startswith("b2-runner: ")

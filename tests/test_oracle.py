@@ -1,0 +1,78 @@
+"""The CPU oracle against the reference's own pins (no GPU needed).
+
+1. The golden b2-runner run (brian2-rust/tests/fixtures/reference-v1): the
+   oracle must reproduce results.bin and events.bin byte for byte and the
+   summary counts (155 spikes, 1,238 synaptic events).
+2. Brian2's numpy runtime on the same lowered networks (the reference's
+   cross-backend gate, brian2-rust/examples/cuba.py:140-160): identical spike
+   rasters, states within the gate's tolerance.
+3. Planted mistakes: a corrupted oracle output must fail the comparison
+   (the reference tests its gates the same way, tests/test_gpu_comparison.py:55-71).
+"""
+from __future__ import annotations
+
+import json
+import shutil
+
+import numpy as np
+import pytest
+
+from conftest import GOLDEN, MODELS, model_file, run_oracle
+from b2results import load_model, read_results
+
+
+def test_golden_results_bytes(oracle, tmp_path):
+    out = run_oracle(oracle, GOLDEN / "reference-v1" / "model.json", tmp_path / "out")
+    assert (out / "results.bin").read_bytes() == (GOLDEN / "reference-v1" / "results.bin").read_bytes()
+    assert (out / "events.bin").read_bytes() == (GOLDEN / "reference-v1" / "events.bin").read_bytes()
+    ours = json.loads((out / "summary.json").read_text())
+    ref = json.loads((GOLDEN / "reference-v1" / "summary.json").read_text())
+    for key in ("dump_bytes", "event_dump_bytes", "spike_count", "synaptic_events", "neuron_count",
+                "population_count", "final_time_seconds", "schema"):
+        assert ours[key] == ref[key], key
+
+
+def test_golden_comparison_detects_corruption(oracle, tmp_path):
+    out = run_oracle(oracle, GOLDEN / "reference-v1" / "model.json", tmp_path / "out")
+    data = bytearray((out / "results.bin").read_bytes())
+    data[len(data) // 2] ^= 1
+    assert bytes(data) != (GOLDEN / "reference-v1" / "results.bin").read_bytes()
+
+
+@pytest.mark.parametrize("name,rtol", [("cuba_small", 1e-12), ("cobahh_small", 1e-9)])
+def test_oracle_matches_brian_numpy(oracle, tmp_path, name, rtol):
+    model_path = model_file(name, tmp_path)
+    out = run_oracle(oracle, model_path, tmp_path / "out")
+    res = read_results(out, load_model(model_path))
+    ref = np.load(GOLDEN / "brian_numpy" / f"{name}.npz")
+    spikes = res.populations[0].spikes
+    ticks = np.rint(ref["spike_t"] / 1e-4).astype(np.int64)
+    order = np.lexsort((ref["spike_i"], ticks))
+    assert len(spikes) == len(ticks)
+    np.testing.assert_array_equal(spikes[:, 0], ticks[order])
+    np.testing.assert_array_equal(spikes[:, 1], ref["spike_i"][order])
+    np.testing.assert_allclose(res.populations[0].states["v"], ref["v"], rtol=rtol, atol=1e-18)
+
+
+def test_oracle_rejects_existing_output_dir(oracle, tmp_path):
+    import subprocess
+    (tmp_path / "exists").mkdir()
+    proc = subprocess.run([str(oracle), str(MODELS / "cuba_small.json"), str(tmp_path / "exists")],
+                          capture_output=True, text=True)
+    assert proc.returncode == 1
+    assert "already exists" in proc.stderr
+
+
+def test_oracle_synaptic_events_equal_outdegree_of_spikes(oracle, tmp_path):
+    """summary.synaptic_events == sum of out-degrees of the delivered spikes
+    (the reference's check in brian2-rust/examples/cuba.py:120-123)."""
+    model_path = MODELS / "cuba_small.json"
+    model = load_model(model_path)
+    out = run_oracle(oracle, model_path, tmp_path / "out")
+    res = read_results(out, model)
+    spikes = res.populations[0].spikes
+    total = 0
+    for syn in model["instance"]["synapses"]:
+        outdeg = np.bincount(np.asarray(syn["source"]), minlength=model["definition"]["populations"][0]["count"])
+        total += int(outdeg[spikes[:, 1]].sum())
+    assert sum(res.delivered) == total

@@ -48,6 +48,13 @@ DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
 namespace {
 
 constexpr unsigned kThreads = 256;
+constexpr unsigned kNpt = 4;                    // neurons per thread in neuron kernels
+constexpr unsigned kTile = kThreads * kNpt;     // neurons per block (one compaction tile)
+
+constexpr uint64_t kRowChunk = 256;            // CSR row entries per scatter work item
+static_assert(kNpt * (kThreads / 32) <= 32, "one warp scans the per-(kk, warp) spike counts");
+
+size_t tiles_for(size_t count) { return std::max<size_t>(1, (count + kTile - 1) / kTile); }
 constexpr uint32_t kErrNonfinite = 0x1, kErrTimestep = 0x2, kErrBinomial = 0x4, kErrPoisson = 0x8,
                    kErrRing = 0x10, kErrLookback = 0x20, kErrIntDiv = 0x40, kErrTimedArray = 0x80,
                    kErrCast = 0x100, kErrExchange = 0x200;
@@ -160,6 +167,7 @@ struct Engine::Impl {
     int offsets = -1, row_other = -1, row_edge = -1, row_delay = -1;  // CSR
     bool uniform = true;
     size_t delay = 0, max_delay = 0;
+    uint64_t max_row = 0;  // longest CSR row (sizes the scatter work split)
     int delivered_slot = 0;
     enum class Mode { Atomic, EdgeParallel, Serial } mode = Mode::Serial;
     std::vector<AtomicAdd> atomic_adds;
@@ -451,6 +459,7 @@ struct Engine::Impl {
             }
           }
           check(idx.size() <= UINT32_MAX, "explicit edge count must fit u32");
+          for (size_t i = 0; i < pd.endpoint_count; ++i) pd.max_row = std::max<uint64_t>(pd.max_row, offs[i + 1] - offs[i]);
           pd.offsets = upload(offs.data(), offs.size() * 8);
           pd.row_other = upload(row_other.data(), std::max<size_t>(row_other.size(), 1) * 4);
           if (!identity) pd.row_edge = upload(row_edge.data(), std::max<size_t>(row_edge.size(), 1) * 4);
@@ -471,6 +480,10 @@ struct Engine::Impl {
               build_fixed_total_csr(def.source_count, def.target_count, topo.edge_count, topo.seed, 0,
                                     def.target_count, offs, rows, local_edges, stream);
             check(local_edges == sd.edges, "procedural edge count mismatch");
+            std::vector<uint64_t> host_offs(def.source_count + 1);
+            B2_CUDA(cudaMemcpy(host_offs.data(), offs.ptr, host_offs.size() * 8, cudaMemcpyDeviceToHost));
+            for (size_t i = 0; i < def.source_count; ++i)
+              pd.max_row = std::max<uint64_t>(pd.max_row, host_offs[i + 1] - host_offs[i]);
             pd.offsets = adopt(std::move(offs));
             pd.row_other = adopt(std::move(rows));
           }
@@ -519,9 +532,9 @@ struct Engine::Impl {
       es.ring = alloc(es.cap * 4);
       es.tick_start = alloc((steps + 1) * 8);
       memset_dev(es.tick_start, 8);
-      size_t tiles = (pd.count + kThreads - 1) / kThreads;
-      es.status = alloc(std::max<size_t>(tiles, 1) * 8);
-      memset_dev(es.status, std::max<size_t>(tiles, 1) * 8);
+      size_t tiles = tiles_for(pd.count);
+      es.status = alloc(tiles * 8);
+      memset_dev(es.status, tiles * 8);
       es.ticket = alloc(8);
       memset_dev(es.ticket, 8);
       es.starts.assign(1, 0);
@@ -686,6 +699,13 @@ struct Engine::Impl {
   // compaction into the event ring), optional reset R on fired lanes.
   std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
                            bool x_is_spike, const Program* R) {
+    // One block owns a tile of kTile consecutive neurons; thread t handles
+    // neurons tile*kTile + kk*kThreads + t for kk < kNpt, so every load and
+    // store is coalesced and each thread keeps kNpt independent neurons in
+    // flight.  Fired lanes are counted per (kk, warp) with ballots; the
+    // block's base in the tick's ascending spike list comes from a
+    // warp-parallel decoupled look-back over the tiles (ticket order == neuron
+    // order), so the list is globally ascending after one pass.
     const auto& def = m.populations[p];
     const PopDev& pd = pops[p];
     std::vector<const Program*> progs;
@@ -696,27 +716,32 @@ struct Engine::Impl {
     std::ostringstream o;
     o << kernel_head(name);
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
-    size_t tiles = std::max<size_t>(1, (pd.count + kThreads - 1) / kThreads);
+    size_t tiles = tiles_for(pd.count);
+    constexpr unsigned W = kThreads / 32;
     if (X) {
-      o << "  __shared__ u32 s_warp[" << kThreads / 32 + 1 << "];\n  __shared__ u64 s_base;\n  __shared__ u32 s_tile;\n";
+      o << "  __shared__ u32 s_ballot[" << kNpt * W << "];\n  __shared__ u32 s_off[" << kNpt * W + 1 << "];\n";
+      o << "  __shared__ u64 s_base;\n  __shared__ u32 s_tile;\n";
       o << "  if (threadIdx.x == 0) s_tile = (u32)(atomicAdd((unsigned long long*)" << P(es->ticket, "u64") << ", 1ull) % "
         << tiles << "ull);\n  __syncthreads();\n  const u32 tile = s_tile;\n";
-      o << "  const u32 i = tile * " << kThreads << "u + threadIdx.x;\n";
+      o << "  u32 fired_bits = 0;\n";
     } else {
-      o << "  const u32 i = blockIdx.x * " << kThreads << "u + threadIdx.x;\n";
+      o << "  const u32 tile = blockIdx.x;\n";
     }
+    o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
+    EmitContext ctx = neuron_ctx(p);
+    o << "#pragma unroll\n  for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
+    o << "  const u32 i = tile * " << kTile << "u + kk * " << kThreads << "u + threadIdx.x;\n";
     o << "  const bool active = i < " << pd.count << "u;\n";
+    o << "  bool fired = false;\n  (void)fired;\n";
+    o << "  if (active) {\n";
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
-      o << "  " << ct << " sv" << s << " = active ? " << P(pops[p].states[s].ptr, ct) << "[i] : (" << ct << ")0;\n";
+      o << "  " << ct << " sv" << s << " = " << P(pops[p].states[s].ptr, ct) << "[i];\n";
     }
     if (refr) {
-      o << "  double ls = active ? " << P(pd.lastspike, "double") << "[i] : 0.0;\n";
-      o << "  u8 nr = active ? " << P(pd.not_refractory, "u8") << "[i] : (u8)0;\n";
+      o << "  double ls = " << P(pd.lastspike, "double") << "[i];\n";
+      o << "  u8 nr = " << P(pd.not_refractory, "u8") << "[i];\n  (void)ls;\n";
     }
-    o << "  bool fired = false;\n  (void)fired;\n";
-    EmitContext ctx = neuron_ctx(p);
-    o << "  if (active) {\n";
     if (U) {
       if (refr && pd.fixed_refractory)
         o << "  nr = (u8)(b2_timestep(t - ls, " << double_literal(pd.dt) << ", err) >= " << u64lit(pd.period_ticks) << ");\n";
@@ -730,33 +755,49 @@ struct Engine::Impl {
       o << commits(*X, p, "h_") << "  }\n";
       if (x_is_spike && refr) o << "  if (fired) { ls = t; nr = 0; }\n";
     }
-    o << "  }\n";
-    if (X) {
-      o << "  u32 block_total = 0;\n";
-      o << "  const u32 off = b2_compact_offsets<" << kThreads << ">(fired, tick, tile, " << P(es->status, "u64")
-        << ", s_warp, &s_base, err, &block_total);\n";
-      o << "  const u64* ts = " << P(es->tick_start, "u64") << ";\n";
-      o << "  const u64 tick_base_pos = ts[rel];\n";
-      o << "  if (fired) " << P(es->ring, "u32") << "[(tick_base_pos + s_base + off) & " << u64lit(es->mask) << "] = i;\n";
-      o << "  if (tile == " << tiles - 1 << "u && threadIdx.x == 0) {\n";
-      o << "    const u64 end = tick_base_pos + s_base + block_total;\n";
-      o << "    " << P(es->tick_start, "u64") << "[rel + 1] = end;\n";
-      o << "    if (end - ctl->ring_floor > " << u64lit(es->cap) << ") err |= " << kErrRing << "u;\n";
-      o << "  }\n";
-    }
-    if (R) {
-      o << "  if (active && fired) {\n" << emit_program(*R, ctx, "r_") << commits(*R, p, "r_") << "  }\n";
-    }
-    o << "  if (active) {\n";
+    if (R) o << "  if (fired) {\n" << emit_program(*R, ctx, "r_") << commits(*R, p, "r_") << "  }\n";
     for (size_t s : written) {
       const char* ct = storage_ctype(def.states[s].dtype);
-      o << "    " << P(pops[p].states[s].ptr, ct) << "[i] = sv" << s << ";\n";
+      o << "  " << P(pops[p].states[s].ptr, ct) << "[i] = sv" << s << ";\n";
     }
     if (refr && (X || (U && pd.fixed_refractory) || writes_available(progs))) {
-      if (X && x_is_spike) o << "    if (fired) " << P(pd.lastspike, "double") << "[i] = ls;\n";
-      o << "    " << P(pd.not_refractory, "u8") << "[i] = nr;\n";
+      if (X && x_is_spike) o << "  if (fired) " << P(pd.lastspike, "double") << "[i] = ls;\n";
+      o << "  " << P(pd.not_refractory, "u8") << "[i] = nr;\n";
     }
-    o << "  }\n";
+    o << "  }\n";  // active
+    if (X) {
+      o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
+      o << "  if (lane == 0) s_ballot[kk * " << W << "u + warp] = b;\n";
+      o << "  fired_bits |= (fired ? 1u : 0u) << kk;\n";
+    }
+    o << "  }\n";  // kk loop
+    if (X) {
+      o << "  __syncthreads();\n";
+      o << "  if (warp == 0) {\n";
+      o << "    // exclusive scan of the " << kNpt * W << " (kk, warp) counts in neuron order\n";
+      o << "    u32 c = lane < " << kNpt * W << "u ? __popc(s_ballot[lane]) : 0u;\n";
+      o << "    u32 x = c;\n";
+      o << "#pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { u32 y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= (u32)d) x += y; }\n";
+      o << "    if (lane < " << kNpt * W << "u) s_off[lane] = x - c;\n";
+      o << "    const u32 total = __shfl_sync(0xffffffffu, x, 31);\n";
+      o << "    const u64 prefix = b2_lookback(tick, tile, " << P(es->status, "u64") << ", (u64)total, err);\n";
+      o << "    if (lane == 0) {\n";
+      o << "      const u64 base = " << P(es->tick_start, "u64") << "[rel] + prefix;\n";
+      o << "      s_base = base;\n";
+      o << "      if (tile == " << tiles - 1 << "u) {\n";
+      o << "        " << P(es->tick_start, "u64") << "[rel + 1] = base + total;\n";
+      o << "        if (base + total - ctl->ring_floor > " << u64lit(es->cap) << ") err |= " << kErrRing << "u;\n";
+      o << "      }\n    }\n  }\n";
+      o << "  __syncthreads();\n";
+      o << "  if (fired_bits) {\n    u32* ring = " << P(es->ring, "u32") << ";\n";
+      o << "#pragma unroll\n    for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
+      o << "      if ((fired_bits >> kk) & 1u) {\n";
+      o << "        const u32 slot = kk * " << W << "u + warp;\n";
+      o << "        const u64 pos = s_base + s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u));\n";
+      o << "        ring[pos & " << u64lit(es->mask) << "] = tile * " << kTile << "u + kk * " << kThreads
+        << "u + threadIdx.x;\n";
+      o << "      }\n    }\n  }\n";
+    }
     o << kernel_tail();
     return o.str();
   }
@@ -1065,29 +1106,37 @@ struct Engine::Impl {
       o << kernel_tail();
       return o.str();
     }
-    // Parallel traversal: one warp per fired endpoint of tick rel - delay.
+    // Parallel traversal.  Work item = (fired endpoint, row chunk of
+    // kRowChunk entries); blocks stride over items, threads over the chunk, so
+    // a tick's events spread across the whole GPU instead of one warp per
+    // spike.  Constant-addend updates are fire-and-forget reductions
+    // (red.global.add): their result is re-checked for finiteness by the next
+    // reader of the state (every neuron program checks every operation).
+    const uint64_t chunks = std::max<uint64_t>(1, (pw.max_row + kRowChunk - 1) / kRowChunk);
     o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n  const u64 te = rel - " << pw.delay << "ull;\n";
     o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
     o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
     o << "  const u64* off = " << P(pw.offsets, "const u64") << ";\n  const u32* other = " << P(pw.row_other, "const u32") << ";\n";
-    o << "  const u32 lane = threadIdx.x & 31u;\n";
-    o << "  const u64 warp = ((u64)blockIdx.x * blockDim.x + threadIdx.x) >> 5;\n";
-    o << "  const u64 nwarps = ((u64)gridDim.x * blockDim.x) >> 5;\n  u64 events = 0;\n";
-    o << "  for (u64 j = a + warp; j < b; j += nwarps) {\n    const u32 s = ring[j & " << u64lit(es.mask) << "];\n";
+    o << "  u64 events = 0;\n";
+    o << "  const u64 items = (b - a) * " << chunks << "ull;\n";
+    o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
+    o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
+    o << "    const u32 s = ring[j & " << u64lit(es.mask) << "];\n";
     if (!full) o << "    if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
     o << "    const u32 ep = s - " << lo << "u;\n    const u64 r0 = off[ep], r1 = off[ep + 1];\n";
-    o << "    for (u64 q = r0 + lane; q < r1; q += 32) {\n";
+    o << "    if (c == 0 && threadIdx.x == 0) events += r1 - r0;\n";
+    o << "    const u64 q0 = r0 + c * " << kRowChunk << "ull;\n    if (q0 >= r1) continue;\n";
+    o << "    const u64 q1 = q0 + " << kRowChunk << "ull < r1 ? q0 + " << kRowChunk << "ull : r1;\n";
+    o << "#pragma unroll 4\n    for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
     if (pw.mode == PathwayDev::Mode::Atomic) {
       const auto& tgt = m.populations[def.target_population];
-      o << "      const u64 tgt_state = (u64)other[q] + " << def.target_start << "ull;\n";
+      o << "      const u64 tgt_state = (u64)__ldg(other + q) + " << def.target_start << "ull;\n";
       for (const auto& a : pw.atomic_adds) {
         DType d = tgt.states[a.state].dtype;
         int ptr = pops[def.target_population].states[a.state].ptr;
         std::string gate = a.gated ? "if (" + P(pops[def.target_population].not_refractory, "const u8") + "[tgt_state]) " : "";
         if (d == DType::F64) {
-          o << "      " << gate << "{ const double old = atomicAdd(" << P(ptr, "double") << " + tgt_state, "
-            << double_literal(a.addend) << "); if (!b2_finite(old + " << double_literal(a.addend) << ")) err |= "
-            << kErrNonfinite << "u; }\n";
+          o << "      " << gate << "atomicAdd(" << P(ptr, "double") << " + tgt_state, " << double_literal(a.addend) << ");\n";
         } else {
           o << "      " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tgt_state, "
             << double_literal(a.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
@@ -1098,8 +1147,8 @@ struct Engine::Impl {
       if (pw.is_pre) o << "      " << body_fn << "(ep, other[q], e, tick, t, err);\n";
       else o << "      " << body_fn << "(other[q], ep, e, tick, t, err);\n";
     }
-    o << "    }\n    events += r1 - r0;\n  }\n";
-    o << "  if (lane == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
+    o << "    }\n  }\n";
+    o << "  if (threadIdx.x == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
       << pw.delivered_slot << ", events);\n";
     o << kernel_tail();
     return o.str();
@@ -1250,7 +1299,7 @@ struct Engine::Impl {
               }
               std::string nm = name_for(def.name + (X ? "_step" : "_update"));
               kernels << gen_pop_step(nm, p, U, X, x_event, x_spike, R);
-              ops.push_back({nm, nullptr, unsigned(std::max<size_t>(1, (def.count + kThreads - 1) / kThreads)), kThreads});
+              ops.push_back({nm, nullptr, unsigned(tiles_for(def.count)), kThreads});
             } else if (code.kind == "reset") {
               const Program* R = compile_pop(p, code);
               size_t e = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
@@ -1262,7 +1311,7 @@ struct Engine::Impl {
               const Program* pr = compile_pop(p, code);
               std::string nm = name_for(def.name + "_" + code.kind);
               kernels << gen_pop_step(nm, p, pr, nullptr, 0, false, nullptr);
-              ops.push_back({nm, nullptr, unsigned(std::max<size_t>(1, (def.count + kThreads - 1) / kThreads)), kThreads});
+              ops.push_back({nm, nullptr, unsigned(tiles_for(def.count)), kThreads});
             } else {
               throw Error("population code object kind '" + code.kind + "' is not supported by the GPU engine");
             }

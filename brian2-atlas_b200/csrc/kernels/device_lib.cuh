@@ -351,6 +351,60 @@ __device__ __forceinline__ u64 b2_status(u64 tick, u64 flag, u64 value) {
   return (B2_TAG(tick) << 40) | (flag << 38) | (value & ((1ull << 38) - 1));
 }
 
+__device__ __forceinline__ u64 b2_warp_sum_u64(u64 v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Decoupled look-back run by one full warp: publishes this tile's aggregate,
+// then inspects 32 predecessors per step (nearest first) until it meets an
+// inclusive prefix, and publishes its own.  Returns the exclusive prefix in
+// every lane.  Every predecessor took its ticket earlier, so it is running and
+// publishes its aggregate before it looks back itself; waits are bounded and
+// raise B2_ERR_LOOKBACK instead of hanging.
+__device__ u64 b2_lookback(u64 tick, u32 tile, u64* status, u64 aggregate, u32& err) {
+  const u32 lane = threadIdx.x & 31;
+  if (tile == 0) {
+    if (lane == 0) b2_st_release(&status[0], b2_status(tick, 2, aggregate));
+    return 0;
+  }
+  if (lane == 0) b2_st_release(&status[tile], b2_status(tick, 1, aggregate));
+  const u64 tag = B2_TAG(tick);
+  u64 running = 0;
+  i64 end = (i64)tile - 1;
+  u32 spins = 0;
+  while (true) {
+    const i64 idx = end - (i64)lane;
+    u32 flag = 2;
+    u64 val = 0;
+    if (idx >= 0) {
+      const u64 s = b2_ld_acquire(&status[idx]);
+      flag = ((s >> 40) == tag) ? (u32)((s >> 38) & 3ull) : 0u;
+      val = s & ((1ull << 38) - 1);
+    }
+    if (__ballot_sync(0xffffffffu, flag == 0)) {
+      if (++spins > (1u << 22)) {
+        err |= B2_ERR_LOOKBACK;
+        running = 0;
+        break;
+      }
+      if (spins > 16) __nanosleep(32);
+      continue;
+    }
+    const u32 prefix_lanes = __ballot_sync(0xffffffffu, flag == 2);
+    if (prefix_lanes) {
+      const u32 first = __ffs(prefix_lanes) - 1;
+      running += b2_warp_sum_u64(lane <= first ? val : 0ull);
+      break;
+    }
+    running += b2_warp_sum_u64(val);
+    end -= 32;
+  }
+  if (lane == 0) b2_st_release(&status[tile], b2_status(tick, 2, running + aggregate));
+  return running;
+}
+
 // Block-level exclusive offsets of `fired` lanes and the block's global base
 // in the tick's ascending spike list.  `tile` is this block's position in
 // neuron order (taken from a ticket, so every predecessor tile has already

@@ -127,8 +127,12 @@ def test_nonfinite_state_raises_instead_of_faulting(pkg):
     """A value the reference would reject (overflow to inf) sets the device
     error word; the host raises and poisons the engine."""
     doc = load_model(MODELS / "cuba_small.json")
-    v = doc["instance"]["populations"][0]["initial_state"]["v"]
-    v[0] = "7fefffffffffffff"  # DBL_MAX: the exact-linear update overflows
+    # ge <- ge * ge with ge0 = 1e200 overflows to +inf on the first tick
+    update = doc["definition"]["populations"][0]["code_objects"][0]
+    for st in update["vector"]:
+        if st["target"] == "ge":
+            st["value"] = {"op": "mul", "left": {"op": "load", "name": "ge"}, "right": {"op": "load", "name": "ge"}}
+    doc["instance"]["populations"][0]["initial_state"]["ge"][5] = "6974e718d7d7625a"  # 1e200
     with pkg.Engine(json.dumps(doc).encode(), device=0) as eng:
         with pytest.raises(pkg.B2GpuError, match="non-finite"):
             eng.run()

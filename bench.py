@@ -162,6 +162,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--neurons", type=int, default=N_NEURONS)
+    ap.add_argument("--indegree", type=int, default=INDEGREE)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -176,7 +177,7 @@ def main():
     pkg = importlib.import_module("brian2-atlas_b200")
     total_ticks = (args.warmup + args.steps) * TICKS_PER_STEP
     t0 = time.time()
-    model = build_model(args.neurons, INDEGREE, total_ticks + 400)
+    model = build_model(args.neurons, args.indegree, total_ticks + 400)
     t_json = time.time() - t0
     eng = pkg.Engine(model, device=local_rank)
     del model
@@ -250,7 +251,7 @@ def main():
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded; definition layer lowered by the reference frontend)",
         "config": {"workload": "config 2: CUBA 1M neurons, fixed in-degree 1000 (1e9 synapses), Poisson 100x10 Hz",
-                   "neurons": args.neurons, "indegree": INDEGREE, "synapses": args.neurons * INDEGREE,
+                   "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
                    "ticks_per_step": TICKS_PER_STEP, "dt_s": DT, "parallelism": "single GPU",
                    "l2": "256 MiB buffer written between timed steps; per-tick neuron state (56 MB) stays "
                          "L2-resident within a step"},

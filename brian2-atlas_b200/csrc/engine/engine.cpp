@@ -122,7 +122,7 @@ struct Engine::Impl {
   struct EventStreamDev {
     size_t pop = 0, event = 0;
     uint64_t cap = 0, mask = 0;
-    int ring = -1, tick_start = -1, status = -1, ticket = -1;
+    int ring = -1, tick_start = -1, status = -1, gstatus = -1, ticket = -1;
     bool produced = false, ascending = true;
     size_t max_delay = 0;  // deepest consumer delay
     // host copy of drained spikes
@@ -535,6 +535,9 @@ struct Engine::Impl {
       size_t tiles = tiles_for(pd.count);
       es.status = alloc(tiles * 8);
       memset_dev(es.status, tiles * 8);
+      size_t groups = (tiles + 31) / 32;
+      es.gstatus = alloc(groups * 8);
+      memset_dev(es.gstatus, groups * 8);
       es.ticket = alloc(8);
       memset_dev(es.ticket, 8);
       es.starts.assign(1, 0);
@@ -698,21 +701,30 @@ struct Engine::Impl {
   // Population step: optional update U, optional threshold X (with ascending
   // compaction into the event ring), optional reset R on fired lanes.
   std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
-                           bool x_is_spike, const Program* R) {
+                           bool x_is_spike, const Program* R, const std::vector<const Program*>& deferred = {},
+                           bool flush = false) {
     // One block owns a tile of kTile consecutive neurons; thread t handles
-    // neurons tile*kTile + kk*kThreads + t for kk < kNpt, so every load and
-    // store is coalesced and each thread keeps kNpt independent neurons in
-    // flight.  Fired lanes are counted per (kk, warp) with ballots; the
-    // block's base in the tick's ascending spike list comes from a
-    // warp-parallel decoupled look-back over the tiles (ticket order == neuron
-    // order), so the list is globally ascending after one pass.
+    // neurons tile*kTile + kk*kThreads + t for kk < kNpt: all loads of the
+    // kNpt neurons are issued before any arithmetic (memory-level
+    // parallelism), every access is coalesced, and the fired lanes are
+    // counted per (kk, warp) with ballots.  The tile's base in the tick's
+    // ascending spike list comes from a chain-free two-level prefix over the
+    // tiles (ticket order == neuron order).
+    //
+    // `deferred` programs are trailing neuron maps of the previous tick (e.g.
+    // PoissonInput) that the schedule analysis moved to the start of this
+    // kernel; they run with the previous tick's t and RNG counter.  A flush
+    // kernel applies the last tick's copy at the end of a run or before a
+    // state read, and marks it done so the next prologue skips it.
     const auto& def = m.populations[p];
     const PopDev& pd = pops[p];
-    std::vector<const Program*> progs;
+    std::vector<const Program*> progs(deferred.begin(), deferred.end());
     for (const Program* pr : {U, X, R})
       if (pr) progs.push_back(pr);
     std::set<size_t> used = slots_used(progs), written = slots_written(progs);
     bool refr = pd.lastspike >= 0;
+    bool touch_refr = refr && (X || (U && pd.fixed_refractory && !flush) || writes_available(progs));
+    bool read_refr = refr;
     std::ostringstream o;
     o << kernel_head(name);
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
@@ -728,22 +740,46 @@ struct Engine::Impl {
       o << "  const u32 tile = blockIdx.x;\n";
     }
     o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
+    if (!deferred.empty()) {
+      o << "  const bool run_deferred = rel > 0 && " << P(deferred_flags, "const u64") << "[" << p << "] != tick - 1;\n";
+      o << "  const u64 tick_prev = tick - 1;\n  const double t_prev = (double)tick_prev * " << double_literal(dt) << ";\n";
+      o << "  (void)t_prev;\n";
+    }
+    // ---- load phase
+    auto ld = [&](int ptr, const char* ct) { return "__ldg(" + P(ptr, ct) + " + i)"; };
+    for (size_t s : used) {
+      const char* ct = storage_ctype(def.states[s].dtype);
+      o << "  " << ct << " sva" << s << "[" << kNpt << "];\n";
+    }
+    if (read_refr) o << "  double lsa[" << kNpt << "];\n  u8 nra[" << kNpt << "];\n";
+    o << "#pragma unroll\n  for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
+    o << "    const u32 i = tile * " << kTile << "u + kk * " << kThreads << "u + threadIdx.x;\n";
+    o << "    if (i < " << pd.count << "u) {\n";
+    for (size_t s : used) {
+      const char* ct = storage_ctype(def.states[s].dtype);
+      o << "      sva" << s << "[kk] = " << ld(pops[p].states[s].ptr, ct) << ";\n";
+    }
+    if (read_refr)
+      o << "      lsa[kk] = " << ld(pd.lastspike, "const double") << ";\n      nra[kk] = " << ld(pd.not_refractory, "const u8") << ";\n";
+    o << "    }\n  }\n";
+    // ---- compute / store phase
     EmitContext ctx = neuron_ctx(p);
+    EmitContext prev_ctx = ctx;
+    prev_ctx.tick = "tick_prev";
+    prev_ctx.time = "t_prev";
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
     o << "  const u32 i = tile * " << kTile << "u + kk * " << kThreads << "u + threadIdx.x;\n";
     o << "  const bool active = i < " << pd.count << "u;\n";
     o << "  bool fired = false;\n  (void)fired;\n";
     o << "  if (active) {\n";
-    for (size_t s : used) {
-      const char* ct = storage_ctype(def.states[s].dtype);
-      o << "  " << ct << " sv" << s << " = " << P(pops[p].states[s].ptr, ct) << "[i];\n";
-    }
-    if (refr) {
-      o << "  double ls = " << P(pd.lastspike, "double") << "[i];\n";
-      o << "  u8 nr = " << P(pd.not_refractory, "u8") << "[i];\n  (void)ls;\n";
+    for (size_t s : used) o << "  " << storage_ctype(def.states[s].dtype) << " sv" << s << " = sva" << s << "[kk];\n";
+    if (read_refr) o << "  double ls = lsa[kk];\n  u8 nr = nra[kk];\n  (void)ls;\n";
+    for (size_t d = 0; d < deferred.size(); ++d) {
+      std::string pre = "d" + std::to_string(d) + "_";
+      o << "  if (run_deferred) {\n" << emit_program(*deferred[d], prev_ctx, pre) << commits(*deferred[d], p, pre) << "  }\n";
     }
     if (U) {
-      if (refr && pd.fixed_refractory)
+      if (refr && pd.fixed_refractory && !flush)
         o << "  nr = (u8)(b2_timestep(t - ls, " << double_literal(pd.dt) << ", err) >= " << u64lit(pd.period_ticks) << ");\n";
       o << "  {\n" << emit_program(*U, ctx, "u_") << commits(*U, p, "u_") << "  }\n";
     }
@@ -760,7 +796,7 @@ struct Engine::Impl {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "  " << P(pops[p].states[s].ptr, ct) << "[i] = sv" << s << ";\n";
     }
-    if (refr && (X || (U && pd.fixed_refractory) || writes_available(progs))) {
+    if (touch_refr) {
       if (X && x_is_spike) o << "  if (fired) " << P(pd.lastspike, "double") << "[i] = ls;\n";
       o << "  " << P(pd.not_refractory, "u8") << "[i] = nr;\n";
     }
@@ -771,16 +807,17 @@ struct Engine::Impl {
       o << "  fired_bits |= (fired ? 1u : 0u) << kk;\n";
     }
     o << "  }\n";  // kk loop
+    if (flush) o << "  if (blockIdx.x == 0 && threadIdx.x == 0) " << P(deferred_flags, "u64") << "[" << p << "] = tick;\n";
     if (X) {
       o << "  __syncthreads();\n";
       o << "  if (warp == 0) {\n";
-      o << "    // exclusive scan of the " << kNpt * W << " (kk, warp) counts in neuron order\n";
       o << "    u32 c = lane < " << kNpt * W << "u ? __popc(s_ballot[lane]) : 0u;\n";
       o << "    u32 x = c;\n";
       o << "#pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { u32 y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= (u32)d) x += y; }\n";
       o << "    if (lane < " << kNpt * W << "u) s_off[lane] = x - c;\n";
       o << "    const u32 total = __shfl_sync(0xffffffffu, x, 31);\n";
-      o << "    const u64 prefix = b2_lookback(tick, tile, " << P(es->status, "u64") << ", (u64)total, err);\n";
+      o << "    const u64 prefix = b2_tile_prefix(tick, tile, " << tiles << "u, " << P(es->status, "u64") << ", "
+        << P(es->gstatus, "u64") << ", (u64)total, err);\n";
       o << "    if (lane == 0) {\n";
       o << "      const u64 base = " << P(es->tick_start, "u64") << "[rel] + prefix;\n";
       o << "      s_base = base;\n";
@@ -1056,6 +1093,65 @@ struct Engine::Impl {
 
   // Spike-list traversal shared by pathway kernels: warp per fired endpoint,
   // lanes over its CSR row.
+  // Constant-addend delivery for one or more pathways that read the same spike
+  // stream at the same delay and write disjoint target variables.  Work item
+  // = (fired source, row chunk of kRowChunk entries); blocks stride over the
+  // items, threads over the chunk, so a tick's events spread over the whole
+  // GPU.  f64 updates are fire-and-forget reductions (red.global.add.f64); a
+  // non-finite result is caught by the next program that reads the variable
+  // (every operation of every neuron program is checked).
+  std::string gen_atomic_kernel(const std::string& name, const std::vector<PathwayDev*>& pws) {
+    const PathwayDev& p0 = *pws.front();
+    const EventStreamDev& es = streams[size_t(p0.stream)];
+    const size_t endpoint_count = m.populations[p0.endpoint_pop].count;
+    uint64_t chunks = 1;
+    for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + kRowChunk - 1) / kRowChunk);
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  if ((i64)rel - " << p0.delay << "ll < 0) return;\n  const u64 te = rel - " << p0.delay << "ull;\n";
+    o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
+    o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
+    for (size_t k = 0; k < pws.size(); ++k) o << "  u64 events" << k << " = 0;\n";
+    o << "  const u64 items = (b - a) * " << chunks << "ull;\n";
+    o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
+    o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
+    o << "    const u32 s = __ldg(ring + (j & " << u64lit(es.mask) << "));\n";
+    for (size_t k = 0; k < pws.size(); ++k) {
+      const PathwayDev& pw = *pws[k];
+      const auto& def = m.synapses[pw.synapse];
+      const auto& tgt = m.populations[def.target_population];
+      const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
+      const bool full = lo == 0 && hi == endpoint_count;
+      o << "    " << (full ? "{" : "if (s >= " + std::to_string(lo) + "u && s < " + std::to_string(hi) + "u) {") << "\n";
+      o << "      const u64* off = " << P(pw.offsets, "const u64") << ";\n";
+      o << "      const u32* other = " << P(pw.row_other, "const u32") << ";\n";
+      o << "      const u32 ep = s - " << lo << "u;\n";
+      o << "      const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
+      o << "      if (c == 0 && threadIdx.x == 0) events" << k << " += r1 - r0;\n";
+      o << "      const u64 q0 = r0 + c * " << kRowChunk << "ull;\n";
+      o << "      const u64 q1 = q0 + " << kRowChunk << "ull < r1 ? q0 + " << kRowChunk << "ull : r1;\n";
+      o << "#pragma unroll 4\n      for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
+      o << "        const u64 tgt_state = (u64)__ldg(other + q) + " << def.target_start << "ull;\n";
+      for (const auto& ad : pw.atomic_adds) {
+        DType d = tgt.states[ad.state].dtype;
+        int ptr = pops[def.target_population].states[ad.state].ptr;
+        std::string gate = ad.gated ? "if (" + P(pops[def.target_population].not_refractory, "const u8") + "[tgt_state]) " : "";
+        if (d == DType::F64)
+          o << "        " << gate << "atomicAdd(" << P(ptr, "double") << " + tgt_state, " << double_literal(ad.addend) << ");\n";
+        else
+          o << "        " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tgt_state, "
+            << double_literal(ad.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
+      }
+      o << "      }\n    }\n";
+    }
+    o << "  }\n";
+    for (size_t k = 0; k < pws.size(); ++k)
+      o << "  if (threadIdx.x == 0 && events" << k << ") atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64")
+        << " + " << pws[k]->delivered_slot << ", events" << k << ");\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
   std::string gen_pathway_kernel(const std::string& name, const std::string& body_fn, const PathwayDev& pw) {
     const auto& def = m.synapses[pw.synapse];
     const EventStreamDev& es = streams[size_t(pw.stream)];
@@ -1180,6 +1276,33 @@ struct Engine::Impl {
 
   std::vector<Program> programs;  // owned programs (stable addresses via reserve)
 
+  // A kernel in the tick, generated once the whole schedule is analysed.
+  struct StepSpec {
+    size_t pop = 0;
+    const Program* U = nullptr;
+    const Program* X = nullptr;
+    size_t x_event = 0;
+    bool x_spike = false;
+    const Program* R = nullptr;
+    std::vector<const Program*> deferred;  // previous tick's trailing neuron maps
+    size_t node_pos = 0;
+  };
+  struct PathSpec {
+    std::vector<PathwayDev*> pathways;
+    std::vector<const Program*> programs;
+    std::vector<std::string> codes;
+  };
+  struct OpSpec {
+    enum class Kind { Text, Step, Path } kind = Kind::Text;
+    std::string base, text;
+    size_t index = 0;
+    unsigned grid = 1, block = kThreads;
+  };
+  std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
+  std::vector<Op> flush_ops;
+  int deferred_flags = -1;                                  // per-population u64 tick of the last flush
+  bool deferred_pending = false;
+
   void build_plan() {
     const auto& nodes = m.schedule;
     check(!nodes.empty(), "model has no schedule");
@@ -1187,13 +1310,10 @@ struct Engine::Impl {
     for (const auto& n : nodes) eff.push_back(effects_of(n));
     programs.reserve(nodes.size() * 2 + 8);
     std::vector<bool> done(nodes.size(), false);
-    std::ostringstream src;
-    src << "// generated by brian2-atlas_b200 for one AtlasIR model\n";
-    src << kDeviceLibSource << "\n";
-    src << "__constant__ u64 g_ptr[PTR_COUNT_PLACEHOLDER];\n\n";
-    std::ostringstream bodies, kernels;
-    int kid = 0;
-    auto name_for = [&](const std::string& base) { return "b2_" + std::to_string(kid++) + "_" + sanitize(base); };
+    std::vector<OpSpec> specs;
+    std::vector<StepSpec> steps_;
+    std::vector<PathSpec> paths;
+    std::map<size_t, size_t> step_of_pop;  // population -> StepSpec index (state-update step)
     auto code_of = [&](const b2ir::ScheduleNode& n) -> const b2ir::CodeObject& {
       return n.owner_kind == b2ir::OwnerKind::Population ? m.populations[n.owner_index].code_objects[n.item_index]
                                                          : m.synapses[n.owner_index].code_objects[n.item_index];
@@ -1204,8 +1324,8 @@ struct Engine::Impl {
       programs.push_back(Program::compile(c, inputs, writable, m.functions));
       return &programs.back();
     };
-    // Can node `mover` move from position `from` to just after position `to`
-    // (to < from) past every not-yet-consumed node in between?
+    // Can the node at `from` move up to just after `to`, past every node in
+    // between that is not already folded into an earlier kernel?
     auto can_hoist = [&](size_t to, size_t from) {
       for (size_t y = to + 1; y < from; ++y)
         if (!done[y] && conflicts(eff[from], eff[y])) return false;
@@ -1222,11 +1342,13 @@ struct Engine::Impl {
         switch (node.operation) {
           case b2ir::ScheduleOp::StateMonitor: {
             if (pops[p].mon_records < 0) break;
-            std::string nm = name_for(def.name + "_statemon");
-            kernels << gen_state_monitor(nm, p);
+            OpSpec o;
+            o.base = def.name + "_statemon";
             size_t n = def.monitor.record.size() * def.monitor.variables.size();
-            ops.push_back({nm, nullptr, unsigned((n + kThreads - 1) / kThreads), kThreads});
-            // several monitor nodes of one population record once per tick
+            o.grid = unsigned((n + kThreads - 1) / kThreads);
+            o.index = p;
+            o.text = "statemon";
+            specs.push_back(o);
             for (size_t y = idx + 1; y < nodes.size(); ++y)
               if (nodes[y].operation == b2ir::ScheduleOp::StateMonitor && nodes[y].owner_kind == b2ir::OwnerKind::Population &&
                   nodes[y].owner_index == p && can_hoist(idx, y))
@@ -1237,24 +1359,23 @@ struct Engine::Impl {
           case b2ir::ScheduleOp::EventMonitor: throw Error("event monitors are not supported by the GPU engine yet");
           case b2ir::ScheduleOp::EventSource: {
             check(pops[p].gen_offsets >= 0, "event source without spike generator");
-            std::string nm = name_for(def.name + "_generator");
-            kernels << gen_event_source(nm, p, pops[p].stream_of_event[0]);
+            OpSpec o;
+            o.base = def.name + "_generator";
+            o.text = "generator";
+            o.index = p;
             stream_produced[size_t(pops[p].stream_of_event[0])] = true;
-            ops.push_back({nm, nullptr, 1, kThreads});
+            specs.push_back(o);
             break;
           }
           case b2ir::ScheduleOp::CodeObject: {
             const auto& code = def.code_objects[node.item_index];
             if (code.kind == "state_update" || code.kind == "threshold") {
-              const Program* U = nullptr;
-              const Program* X = nullptr;
-              const Program* R = nullptr;
-              size_t x_event = 0;
-              bool x_spike = false;
+              StepSpec st;
+              st.pop = p;
+              st.node_pos = idx;
               size_t x_pos = idx;
               if (code.kind == "state_update") {
-                U = compile_pop(p, code);
-                // fuse the population's next threshold
+                st.U = compile_pop(p, code);
                 for (size_t y = idx + 1; y < nodes.size(); ++y) {
                   const auto& n2 = nodes[y];
                   if (done[y] || n2.owner_kind != b2ir::OwnerKind::Population || n2.owner_index != p ||
@@ -1262,56 +1383,86 @@ struct Engine::Impl {
                     continue;
                   const auto& c2 = code_of(n2);
                   if (c2.kind == "threshold" && can_hoist(idx, y)) {
-                    X = compile_pop(p, c2);
+                    st.X = compile_pop(p, c2);
                     done[y] = true;
                     x_pos = y;
-                    x_event = size_t(std::find(def.events.begin(), def.events.end(), *c2.event_name) - def.events.begin());
-                    x_spike = *c2.event_name == "spike";
+                    st.x_event = size_t(std::find(def.events.begin(), def.events.end(), *c2.event_name) - def.events.begin());
+                    st.x_spike = *c2.event_name == "spike";
                   }
                   break;
                 }
               } else {
-                X = compile_pop(p, code);
-                x_event = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
-                x_spike = *code.event_name == "spike";
+                st.X = compile_pop(p, code);
+                st.x_event = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
+                st.x_spike = *code.event_name == "spike";
               }
-              if (X) {
-                check(x_event < def.events.size(), "threshold event is unknown");
-                stream_produced[size_t(pops[p].stream_of_event[x_event])] = true;
-                // fuse the matching reset when it can move up to the threshold
+              if (st.X) {
+                check(st.x_event < def.events.size(), "threshold event is unknown");
+                stream_produced[size_t(pops[p].stream_of_event[st.x_event])] = true;
                 for (size_t y = x_pos + 1; y < nodes.size(); ++y) {
                   const auto& n2 = nodes[y];
                   if (done[y] || n2.owner_kind != b2ir::OwnerKind::Population || n2.owner_index != p ||
                       n2.operation != b2ir::ScheduleOp::CodeObject)
                     continue;
                   const auto& c2 = code_of(n2);
-                  if (c2.kind == "reset" && c2.event_name && *c2.event_name == def.events[x_event]) {
+                  if (c2.kind == "reset" && c2.event_name && *c2.event_name == def.events[st.x_event]) {
                     bool movable = true;
                     for (size_t z = idx + 1; z < y; ++z)
                       if (!done[z] && conflicts(eff[y], eff[z])) movable = false;
                     if (movable) {
-                      R = compile_pop(p, c2);
+                      st.R = compile_pop(p, c2);
                       done[y] = true;
                     }
                     break;
                   }
                 }
               }
-              std::string nm = name_for(def.name + (X ? "_step" : "_update"));
-              kernels << gen_pop_step(nm, p, U, X, x_event, x_spike, R);
-              ops.push_back({nm, nullptr, unsigned(tiles_for(def.count)), kThreads});
+              OpSpec o;
+              o.kind = OpSpec::Kind::Step;
+              o.base = def.name + (st.X ? "_step" : "_update");
+              o.index = steps_.size();
+              o.grid = unsigned(tiles_for(def.count));
+              if (st.U) step_of_pop[p] = steps_.size();
+              steps_.push_back(st);
+              specs.push_back(o);
             } else if (code.kind == "reset") {
-              const Program* R = compile_pop(p, code);
+              OpSpec o;
+              o.base = def.name + "_reset";
               size_t e = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
               check(e < def.events.size(), "reset event is unknown");
-              std::string nm = name_for(def.name + "_reset");
-              kernels << gen_reset(nm, p, *R, pops[p].stream_of_event[e]);
-              ops.push_back({nm, nullptr, 148 * 4, kThreads});
+              const Program* R = compile_pop(p, code);
+              o.text = gen_reset("@NAME@", p, *R, pops[p].stream_of_event[e]);
+              o.grid = 148 * 4;
+              specs.push_back(o);
             } else if (code.kind == "poisson_input" || code.kind == "run_regularly" || code.kind == "subexpression_update") {
               const Program* pr = compile_pop(p, code);
-              std::string nm = name_for(def.name + "_" + code.kind);
-              kernels << gen_pop_step(nm, p, pr, nullptr, 0, false, nullptr);
-              ops.push_back({nm, nullptr, unsigned(tiles_for(def.count)), kThreads});
+              // Defer to the prologue of the population's next state-update
+              // step when this node commutes with everything between here and
+              // that step in the next tick (the schedule is cyclic).
+              auto it = step_of_pop.find(p);
+              bool defer = it != step_of_pop.end();
+              if (defer) {
+                for (size_t y = idx + 1; y < nodes.size() && defer; ++y)
+                  if (!done[y] && conflicts(eff[idx], eff[y])) defer = false;
+                for (size_t y = 0; y < steps_[it->second].node_pos && defer; ++y)
+                  if (conflicts(eff[idx], eff[y])) defer = false;
+              }
+              if (defer) {
+                steps_[it->second].deferred.push_back(pr);
+                flushes.push_back({p, pr});
+              } else {
+                StepSpec st;
+                st.pop = p;
+                st.U = pr;
+                st.node_pos = idx;
+                OpSpec o;
+                o.kind = OpSpec::Kind::Step;
+                o.base = def.name + "_" + code.kind;
+                o.index = steps_.size();
+                o.grid = unsigned(tiles_for(def.count));
+                steps_.push_back(st);
+                specs.push_back(o);
+              }
             } else {
               throw Error("population code object kind '" + code.kind + "' is not supported by the GPU engine");
             }
@@ -1334,24 +1485,101 @@ struct Engine::Impl {
         programs.push_back(Program::compile(code, inputs, writable, m.functions));
         const Program& pr = programs.back();
         classify_pathway(pw, pr);
-        std::string base = sanitize(code.name);
-        std::string body = "b2_body_" + std::to_string(kid) + "_" + base;
-        if (pw.mode != PathwayDev::Mode::Atomic) bodies << gen_pathway_body(body, s, pw, pr);
-        const char* mode = pw.mode == PathwayDev::Mode::Atomic ? "_atomic"
-                           : pw.mode == PathwayDev::Mode::EdgeParallel ? "_edges" : "_serial";
-        std::string nm = name_for(code.name + mode);
-        kernels << gen_pathway_kernel(nm, body, pw);
-        ops.push_back({nm, nullptr, pw.mode == PathwayDev::Mode::Serial ? 1u : 148u * 8u,
-                       pw.mode == PathwayDev::Mode::Serial ? 32u : kThreads});
+        // Constant-addend pathways reading one spike stream at one delay and
+        // writing disjoint target variables share a scatter launch.
+        bool merged = false;
+        if (pw.mode == PathwayDev::Mode::Atomic && !specs.empty() && specs.back().kind == OpSpec::Kind::Path) {
+          PathSpec& ps = paths[specs.back().index];
+          PathwayDev* first = ps.pathways.front();
+          bool ok = first->mode == PathwayDev::Mode::Atomic && first->stream == pw.stream && first->delay == pw.delay &&
+                    m.synapses[first->synapse].target_population == m.synapses[s].target_population;
+          for (PathwayDev* other : ps.pathways)
+            for (const auto& a : other->atomic_adds)
+              for (const auto& b : pw.atomic_adds) ok &= a.state != b.state;
+          if (ok) {
+            ps.pathways.push_back(&pw);
+            ps.programs.push_back(&pr);
+            ps.codes.push_back(code.name);
+            specs.back().base += "_" + code.name;
+            merged = true;
+          }
+        }
+        if (!merged) {
+          PathSpec ps;
+          ps.pathways.push_back(&pw);
+          ps.programs.push_back(&pr);
+          ps.codes.push_back(code.name);
+          OpSpec o;
+          o.kind = OpSpec::Kind::Path;
+          o.index = paths.size();
+          o.base = code.name;
+          bool serial = pw.mode == PathwayDev::Mode::Serial;
+          o.grid = serial ? 1u : 148u * 8u;
+          o.block = serial ? 32u : kThreads;
+          paths.push_back(ps);
+          specs.push_back(o);
+        }
       }
     }
     for (size_t sidx = 0; sidx < streams.size(); ++sidx) {
       streams[sidx].produced = stream_produced[sidx];
       if (!stream_produced[sidx]) {
-        std::string nm = name_for("empty_stream");
-        kernels << gen_empty_stream(nm, int(sidx));
-        ops.push_back({nm, nullptr, 1, 32});
+        OpSpec o;
+        o.base = "empty_stream";
+        o.text = gen_empty_stream("@NAME@", int(sidx));
+        o.block = 32;
+        specs.push_back(o);
       }
+    }
+    if (!flushes.empty()) {
+      std::vector<uint64_t> init(m.populations.size(), UINT64_MAX);
+      deferred_flags = upload(init.data(), init.size() * 8);
+    }
+    // ---- emit
+    std::ostringstream src, bodies, kernels;
+    src << "// generated by brian2-atlas_b200 for one AtlasIR model\n";
+    src << kDeviceLibSource << "\n";
+    src << "__constant__ u64 g_ptr[PTR_COUNT_PLACEHOLDER];\n\n";
+    int kid = 0;
+    for (auto& o : specs) {
+      std::string nm = "b2_" + std::to_string(kid++) + "_" + sanitize(o.base);
+      switch (o.kind) {
+        case OpSpec::Kind::Text:
+          if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
+          else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
+          else {
+            std::string t = o.text;
+            t.replace(t.find("@NAME@"), 6, nm);
+            kernels << t;
+          }
+          break;
+        case OpSpec::Kind::Step: {
+          const StepSpec& st = steps_[o.index];
+          kernels << gen_pop_step(nm, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred);
+          break;
+        }
+        case OpSpec::Kind::Path: {
+          PathSpec& ps = paths[o.index];
+          if (ps.pathways.size() == 1 && ps.pathways[0]->mode != PathwayDev::Mode::Atomic) {
+            std::string body = "b2_body_" + std::to_string(kid) + "_" + sanitize(ps.codes[0]);
+            bodies << gen_pathway_body(body, ps.pathways[0]->synapse, *ps.pathways[0], *ps.programs[0]);
+            const char* mode = ps.pathways[0]->mode == PathwayDev::Mode::EdgeParallel ? "_edges" : "_serial";
+            nm += mode;
+            kernels << gen_pathway_kernel(nm, body, *ps.pathways[0]);
+          } else {
+            nm += "_atomic";
+            kernels << gen_atomic_kernel(nm, ps.pathways);
+          }
+          break;
+        }
+      }
+      ops.push_back({nm, nullptr, o.grid, o.block});
+    }
+    for (size_t f = 0; f < flushes.size(); ++f) {
+      size_t p = flushes[f].first;
+      std::string nm = "b2_flush_" + std::to_string(f) + "_" + sanitize(m.populations[p].name);
+      kernels << gen_pop_step(nm, p, flushes[f].second, nullptr, 0, false, nullptr, {}, true);
+      flush_ops.push_back({nm, nullptr, unsigned(tiles_for(m.populations[p].count)), kThreads});
     }
     src << bodies.str() << "\n" << kernels.str();
     source = src.str();
@@ -1397,6 +1625,7 @@ struct Engine::Impl {
     B2_CUDA(cudaStreamSynchronize(stream));
     if (!ptrs.empty()) B2_CUDA(cudaMemcpy(table, ptrs.data(), ptrs.size() * 8, cudaMemcpyHostToDevice));
     for (auto& op : ops) B2_CUDA(cudaLibraryGetKernel(&op.fn, module, op.name.c_str()));
+    for (auto& op : flush_ops) B2_CUDA(cudaLibraryGetKernel(&op.fn, module, op.name.c_str()));
   }
   size_t cubin_bytes = 0;
 
@@ -1497,8 +1726,10 @@ struct Engine::Impl {
       cur_rel += n;
       remaining -= n;
       update_floor(cur_rel);
+      deferred_pending = !flushes.empty();
     }
     for (auto& e : evs) cudaEventDestroy(e);
+    if (cur_rel >= steps) flush_deferred();
     st.ticks = cur_rel;
     return out;
   }
@@ -1542,7 +1773,9 @@ struct Engine::Impl {
         cur_rel += n;
         remaining -= n;
         update_floor(cur_rel);
+        deferred_pending = !flushes.empty();
       }
+      if (cur_rel >= steps) flush_deferred();
     } catch (...) {
       failed = true;
       st.simulation_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
@@ -1551,6 +1784,25 @@ struct Engine::Impl {
     st.simulation_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     st.ticks = cur_rel;
     return cur_rel >= steps;
+  }
+
+  // Apply the deferred trailing neuron maps of the last simulated tick (they
+  // normally run in the next tick's step prologue) so that state reads and
+  // results see exactly the reference's state after that tick.
+  void flush_deferred() {
+    if (!deferred_pending || cur_rel == 0) return;
+    tick_host_ = start_tick + cur_rel - 1;
+    B2_CUDA(cudaMemcpy(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice));
+    void* ctl_ptr = ctl.ptr;
+    uint32_t k = 0;
+    for (auto& op : flush_ops) {
+      void* args[] = {&ctl_ptr, &k};
+      B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(op.fn), dim3(op.grid), dim3(op.block), args, 0, stream));
+      st.kernel_launches += 1;
+    }
+    B2_CUDA(cudaStreamSynchronize(stream));
+    check_error();
+    deferred_pending = false;
   }
 
   // ================================================================ results
@@ -1562,6 +1814,7 @@ struct Engine::Impl {
 
   b2dump::ResultSet results() {
     check(!failed && cur_rel >= steps, "results require a completed execution");
+    flush_deferred();
     B2_CUDA(cudaStreamSynchronize(stream));
     b2dump::ResultSet r;
     r.neuron_count = m.neuron_count;
@@ -1687,6 +1940,7 @@ const std::string& Engine::generated_source() const { return impl_->source; }
 
 void Engine::read_state(size_t population, const std::string& name, std::vector<uint8_t>& out) {
   check(population < impl_->m.populations.size(), "population index out of range");
+  if (!impl_->opt.dry_run && !impl_->failed) impl_->flush_deferred();
   const auto& def = impl_->m.populations[population];
   for (size_t s = 0; s < def.states.size(); ++s)
     if (def.states[s].name == name) {

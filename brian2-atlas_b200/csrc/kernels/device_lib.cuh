@@ -405,6 +405,45 @@ __device__ u64 b2_lookback(u64 tick, u32 tile, u64* status, u64 aggregate, u32& 
   return running;
 }
 
+// Spin until a tick-tagged status word is published; returns its 38-bit
+// value (0 and an error bit after the bounded wait).
+__device__ __forceinline__ u64 b2_wait_word(const u64* p, u64 tag, u32& err) {
+  u32 spins = 0;
+  while (true) {
+    const u64 s = b2_ld_acquire(p);
+    if ((s >> 40) == tag) return s & ((1ull << 38) - 1);
+    if (++spins > (1u << 22)) {
+      err |= B2_ERR_LOOKBACK;
+      return 0;
+    }
+    if (spins > 8) __nanosleep(32);
+  }
+}
+
+// Exclusive prefix of this tile's count among all tiles of the tick, run by
+// one full warp, in one pass and without prefix chains (a two-level
+// reduce-then-scan): every tile publishes its count; the last tile of each
+// group of 32 waits for its 31 group predecessors and publishes the group
+// sum; a tile then adds the group sums of earlier groups and the counts of its
+// own group's earlier tiles.  Each wait targets a tile with an earlier ticket
+// (already running), so it ends; waits are bounded anyway.
+__device__ u64 b2_tile_prefix(u64 tick, u32 tile, u32 tiles, u64* tile_status, u64* group_status, u64 count,
+                              u32& err) {
+  const u32 lane = threadIdx.x & 31;
+  const u64 tag = B2_TAG(tick);
+  if (lane == 0) b2_st_release(&tile_status[tile], b2_status(tick, 1, count));
+  const u32 group = tile >> 5, first = group << 5;
+  u64 own = 0;
+  if (first + lane < tile) own = b2_wait_word(&tile_status[first + lane], tag, err);
+  own = b2_warp_sum_u64(own);
+  if ((tile & 31u) == 31u || tile == tiles - 1) {
+    if (lane == 0) b2_st_release(&group_status[group], b2_status(tick, 1, own + count));
+  }
+  u64 prev = 0;
+  for (u32 g = lane; g < group; g += 32) prev += b2_wait_word(&group_status[g], tag, err);
+  return b2_warp_sum_u64(prev) + own;
+}
+
 // Block-level exclusive offsets of `fired` lanes and the block's global base
 // in the tick's ascending spike list.  `tile` is this block's position in
 // neuron order (taken from a ticket, so every predecessor tile has already

@@ -49,11 +49,16 @@ def load(name):
 
 
 @pytest.mark.parametrize("name,expected", [
-    ("cuba_small", ["statemon", "step", "exc_pre_atomic", "inh_pre_atomic"]),
-    ("cuba_poisson_small", ["step", "exc_pre_atomic", "inh_pre_atomic", "poisson_input"]),
+    # E and I pathways write different variables: one merged scatter launch
+    ("cuba_small", ["statemon", "step", "exc_pre_inh_pre_atomic"]),
+    # PoissonInput commutes with everything up to the next tick's update: it
+    # runs in the next step's prologue (plus a flush kernel for the last tick)
+    ("cuba_poisson_small", ["step", "exc_pre_inh_pre_atomic", "flush_0_neurons"]),
+    # both pathways write v (order matters) and PoissonInput writes v before
+    # the reset: nothing may be merged or deferred
     ("brunel_small", ["step", "excitatory_synapses_pre_atomic", "inhibitory_synapses_pre_atomic",
                       "poisson_input", "reset"]),
-    ("cobahh_small", ["step", "exc_pre_atomic", "inh_pre_atomic"]),
+    ("cobahh_small", ["step", "exc_pre_inh_pre_atomic"]),
     ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_serial", "stdp_post_edges"]),
 ])
 def test_codegen_plan(pkg, name, expected):
@@ -77,7 +82,7 @@ def test_exact_linear_update_is_pure_arithmetic(pkg):
     the per-neuron update issues no device transcendental."""
     src = pkg.codegen(load("cuba_small"))
     step = src[src.index("neurons_step"):]
-    step = step[:step.index("b2_lookback")]
+    step = step[:step.index("b2_tile_prefix")]
     assert "exp(" not in step and "log(" not in step
 
 

@@ -48,13 +48,42 @@ DeviceBuffer& DeviceBuffer::operator=(DeviceBuffer&& o) noexcept {
 namespace {
 
 constexpr unsigned kThreads = 256;
-constexpr unsigned kNpt = 4;                    // neurons per thread in neuron kernels
-constexpr unsigned kTile = kThreads * kNpt;     // neurons per block (one compaction tile)
+constexpr unsigned kMaxNpt = 4;                 // neurons per thread in neuron kernels (1, 2 or 4)
 
 constexpr uint64_t kRowChunk = 256;            // CSR row entries per scatter work item
-static_assert(kNpt * (kThreads / 32) <= 32, "one warp scans the per-(kk, warp) spike counts");
+static_assert(kMaxNpt * (kThreads / 32) <= 32, "one warp scans the per-(kk, warp) spike counts");
 
-size_t tiles_for(size_t count) { return std::max<size_t>(1, (count + kTile - 1) / kTile); }
+// Smallest double d >= 0 with (d + 1e-3*dt) / dt >= target, evaluated in
+// IEEE f64 exactly as Brian2 timestep() does (model.rs:981-992).  The map is
+// monotone in d, so a bisection over the ordered bit patterns of
+// non-negative doubles finds the threshold.
+double timestep_threshold(double dt, double target) {
+  auto steps = [dt](double d) {
+    volatile double x = d + 1e-3 * dt;
+    return x / dt;
+  };
+  auto bits = [](double v) {
+    uint64_t r;
+    std::memcpy(&r, &v, 8);
+    return r;
+  };
+  auto value = [](uint64_t r) {
+    double v;
+    std::memcpy(&v, &r, 8);
+    return v;
+  };
+  if (steps(0.0) >= target) return 0.0;
+  uint64_t lo = bits(0.0), hi = bits(1.7976931348623157e308);
+  if (!(steps(value(hi)) >= target)) return INFINITY;
+  while (hi - lo > 1) {
+    uint64_t mid = lo + (hi - lo) / 2;
+    if (steps(value(mid)) >= target) hi = mid;
+    else lo = mid;
+  }
+  return value(hi);
+}
+
+
 constexpr uint32_t kErrNonfinite = 0x1, kErrTimestep = 0x2, kErrBinomial = 0x4, kErrPoisson = 0x8,
                    kErrRing = 0x10, kErrLookback = 0x20, kErrIntDiv = 0x40, kErrTimedArray = 0x80,
                    kErrCast = 0x100, kErrExchange = 0x200;
@@ -203,7 +232,19 @@ struct Engine::Impl {
   double dt = 0.0;
   bool failed = false;
 
-  Impl(const b2ir::Model& model, const Options& o) : m(model), opt(o) {}
+  Impl(const b2ir::Model& model, const Options& o) : m(model), opt(o) {
+    if (const char* e = std::getenv("B2GPU_NPT")) npt_ = unsigned(std::atoi(e));
+    if (o.neurons_per_thread) npt_ = o.neurons_per_thread;
+    check(npt_ == 1 || npt_ == 2 || npt_ == 4, "neurons per thread must be 1, 2 or 4");
+    if (const char* e = std::getenv("B2GPU_MINBLOCKS")) min_blocks_ = unsigned(std::atoi(e));
+  }
+
+  unsigned npt_ = 4;         // neurons per thread in neuron kernels
+  unsigned min_blocks_ = 0;  // __launch_bounds__ occupancy hint for neuron kernels (0: none)
+  size_t tiles_for(size_t count) const {
+    const size_t tile = size_t(kThreads) * npt_;
+    return std::max<size_t>(1, (count + tile - 1) / tile);
+  }
 
   ~Impl() {
     if (ev_start) cudaEventDestroy(ev_start);
@@ -689,8 +730,9 @@ struct Engine::Impl {
     return o.str();
   }
 
-  std::string kernel_head(const std::string& name) {
-    return "extern \"C\" __global__ void __launch_bounds__(" + std::to_string(kThreads) + ") " + name +
+  std::string kernel_head(const std::string& name, unsigned min_blocks = 0) {
+    std::string bounds = std::to_string(kThreads) + (min_blocks ? ", " + std::to_string(min_blocks) : "");
+    return "extern \"C\" __global__ void __launch_bounds__(" + bounds + ") " + name +
            "(RunCtl* __restrict__ ctl, u32 k) {\n  u32 err = 0;\n  const u64 tick = ctl->tick_base + k;\n"
            "  const u64 rel = tick - " + u64lit(start_tick) + ";\n  const double t = (double)tick * " +
            double_literal(dt) + ";\n  (void)rel; (void)t;\n";
@@ -703,9 +745,9 @@ struct Engine::Impl {
   std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
                            bool x_is_spike, const Program* R, const std::vector<const Program*>& deferred = {},
                            bool flush = false) {
-    // One block owns a tile of kTile consecutive neurons; thread t handles
-    // neurons tile*kTile + kk*kThreads + t for kk < kNpt: all loads of the
-    // kNpt neurons are issued before any arithmetic (memory-level
+    // One block owns a tile of tile_n consecutive neurons; thread t handles
+    // neurons tile*tile_n + kk*kThreads + t for kk < npt: all loads of the
+    // npt neurons are issued before any arithmetic (memory-level
     // parallelism), every access is coalesced, and the fired lanes are
     // counted per (kk, warp) with ballots.  The tile's base in the tick's
     // ascending spike list comes from a chain-free two-level prefix over the
@@ -718,6 +760,7 @@ struct Engine::Impl {
     // state read, and marks it done so the next prologue skips it.
     const auto& def = m.populations[p];
     const PopDev& pd = pops[p];
+    const unsigned npt = npt_, tile_n = kThreads * npt_;
     std::vector<const Program*> progs(deferred.begin(), deferred.end());
     for (const Program* pr : {U, X, R})
       if (pr) progs.push_back(pr);
@@ -726,12 +769,12 @@ struct Engine::Impl {
     bool touch_refr = refr && (X || (U && pd.fixed_refractory && !flush) || writes_available(progs));
     bool read_refr = refr;
     std::ostringstream o;
-    o << kernel_head(name);
+    o << kernel_head(name, min_blocks_);
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
     size_t tiles = tiles_for(pd.count);
     constexpr unsigned W = kThreads / 32;
     if (X) {
-      o << "  __shared__ u32 s_ballot[" << kNpt * W << "];\n  __shared__ u32 s_off[" << kNpt * W + 1 << "];\n";
+      o << "  __shared__ u32 s_ballot[" << npt * W << "];\n  __shared__ u32 s_off[" << npt * W + 1 << "];\n";
       o << "  __shared__ u64 s_base;\n  __shared__ u32 s_tile;\n";
       o << "  if (threadIdx.x == 0) s_tile = (u32)(atomicAdd((unsigned long long*)" << P(es->ticket, "u64") << ", 1ull) % "
         << tiles << "ull);\n  __syncthreads();\n  const u32 tile = s_tile;\n";
@@ -749,11 +792,11 @@ struct Engine::Impl {
     auto ld = [&](int ptr, const char* ct) { return "__ldg(" + P(ptr, ct) + " + i)"; };
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
-      o << "  " << ct << " sva" << s << "[" << kNpt << "];\n";
+      o << "  " << ct << " sva" << s << "[" << npt << "];\n";
     }
-    if (read_refr) o << "  double lsa[" << kNpt << "];\n  u8 nra[" << kNpt << "];\n";
-    o << "#pragma unroll\n  for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
-    o << "    const u32 i = tile * " << kTile << "u + kk * " << kThreads << "u + threadIdx.x;\n";
+    if (read_refr) o << "  double lsa[" << npt << "];\n  u8 nra[" << npt << "];\n";
+    o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
+    o << "    const u32 i = tile * " << tile_n << "u + kk * " << kThreads << "u + threadIdx.x;\n";
     o << "    if (i < " << pd.count << "u) {\n";
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
@@ -767,8 +810,8 @@ struct Engine::Impl {
     EmitContext prev_ctx = ctx;
     prev_ctx.tick = "tick_prev";
     prev_ctx.time = "t_prev";
-    o << "#pragma unroll\n  for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
-    o << "  const u32 i = tile * " << kTile << "u + kk * " << kThreads << "u + threadIdx.x;\n";
+    o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
+    o << "  const u32 i = tile * " << tile_n << "u + kk * " << kThreads << "u + threadIdx.x;\n";
     o << "  const bool active = i < " << pd.count << "u;\n";
     o << "  bool fired = false;\n  (void)fired;\n";
     o << "  if (active) {\n";
@@ -779,8 +822,17 @@ struct Engine::Impl {
       o << "  if (run_deferred) {\n" << emit_program(*deferred[d], prev_ctx, pre) << commits(*deferred[d], p, pre) << "  }\n";
     }
     if (U) {
-      if (refr && pd.fixed_refractory && !flush)
-        o << "  nr = (u8)(b2_timestep(t - ls, " << double_literal(pd.dt) << ", err) >= " << u64lit(pd.period_ticks) << ");\n";
+      if (refr && pd.fixed_refractory && !flush) {
+        // timestep(t - lastspike, dt) >= period (model.rs:981-992) is monotone
+        // in the f64 difference, so it equals d >= d_star for the host-computed
+        // smallest such double; the reference's range errors become d outside
+        // [0, d_max).  Same decision for every d, no per-neuron division.
+        const double d_star = timestep_threshold(pd.dt, double(pd.period_ticks));
+        const double d_max = timestep_threshold(pd.dt, 9223372036854775808.0);
+        o << "  { const double d_ls = t - ls;\n";
+        o << "    if (!(d_ls >= 0.0 && d_ls < " << double_literal(d_max) << ")) err |= " << kErrTimestep << "u;\n";
+        o << "    nr = (u8)(d_ls >= " << double_literal(d_star) << "); }\n";
+      }
       o << "  {\n" << emit_program(*U, ctx, "u_") << commits(*U, p, "u_") << "  }\n";
     }
     if (X) {
@@ -811,10 +863,10 @@ struct Engine::Impl {
     if (X) {
       o << "  __syncthreads();\n";
       o << "  if (warp == 0) {\n";
-      o << "    u32 c = lane < " << kNpt * W << "u ? __popc(s_ballot[lane]) : 0u;\n";
+      o << "    u32 c = lane < " << npt * W << "u ? __popc(s_ballot[lane]) : 0u;\n";
       o << "    u32 x = c;\n";
       o << "#pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { u32 y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= (u32)d) x += y; }\n";
-      o << "    if (lane < " << kNpt * W << "u) s_off[lane] = x - c;\n";
+      o << "    if (lane < " << npt * W << "u) s_off[lane] = x - c;\n";
       o << "    const u32 total = __shfl_sync(0xffffffffu, x, 31);\n";
       o << "    const u64 prefix = b2_tile_prefix(tick, tile, " << tiles << "u, " << P(es->status, "u64") << ", "
         << P(es->gstatus, "u64") << ", (u64)total, err);\n";
@@ -827,11 +879,11 @@ struct Engine::Impl {
       o << "      }\n    }\n  }\n";
       o << "  __syncthreads();\n";
       o << "  if (fired_bits) {\n    u32* ring = " << P(es->ring, "u32") << ";\n";
-      o << "#pragma unroll\n    for (u32 kk = 0; kk < " << kNpt << "u; ++kk) {\n";
+      o << "#pragma unroll\n    for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
       o << "      if ((fired_bits >> kk) & 1u) {\n";
       o << "        const u32 slot = kk * " << W << "u + warp;\n";
       o << "        const u64 pos = s_base + s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u));\n";
-      o << "        ring[pos & " << u64lit(es->mask) << "] = tile * " << kTile << "u + kk * " << kThreads
+      o << "        ring[pos & " << u64lit(es->mask) << "] = tile * " << tile_n << "u + kk * " << kThreads
         << "u + threadIdx.x;\n";
       o << "      }\n    }\n  }\n";
     }

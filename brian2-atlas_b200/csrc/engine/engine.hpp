@@ -36,6 +36,7 @@ struct Options {
   void* nccl_comm = nullptr;    // ncclComm_t when world_size > 1
   bool use_graphs = true;
   bool verbose = false;
+  unsigned neurons_per_thread = 0;  // 1, 2 or 4 (0: default 4)
   // Build the plan and compile the generated kernels for sm_100a without
   // touching a GPU (device pointers are placeholders).  step() is disabled.
   bool dry_run = false;

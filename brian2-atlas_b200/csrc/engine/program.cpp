@@ -736,9 +736,79 @@ const char* intop_code(IntOp o) {
 }
 }  // namespace
 
+namespace {
+
+// Ops whose result the reference checks with is_finite (binary/ternary,
+// executor.rs:5725-5778) and that can produce a non-finite value.
+// Comparisons, logic and sign yield 0/1/-1 and need no check.
+bool finite_checked(IOp op) {
+  switch (op) {
+    case IOp::Not: case IOp::Sign: case IOp::Eq: case IOp::Ne: case IOp::Gt: case IOp::Ge: case IOp::Lt:
+    case IOp::Le: case IOp::And: case IOp::Or: case IOp::Cast: case IOp::IntNeg: case IOp::IntAbs:
+    case IOp::IntBinary: case IOp::Timestep: case IOp::Select: case IOp::Binomial: case IOp::TimedArray:
+      return false;
+    default:
+      return true;
+  }
+}
+
+// Does operand `pos` of `in` carry a non-finite input into the output?
+// (inf/NaN through +,-,*, the dividend, sign changes, roundings and sqrt stays
+// non-finite; a divisor, comparisons, exp(-inf), clip and pow can mask it.)
+bool propagates(const Instr& in, int pos) {
+  switch (in.op) {
+    case IOp::Add: case IOp::Sub: case IOp::Mul: return pos <= 1;
+    case IOp::Div: case IOp::Neg: case IOp::Abs: case IOp::Floor: case IOp::Ceil: case IOp::Trunc:
+    case IOp::Sqrt: case IOp::RoundF32: return pos == 0;
+    case IOp::Select: return pos == 0;  // the value taken where the guard holds
+    default: return false;
+  }
+}
+
+}  // namespace
+
 std::string emit_program(const Program& p, const EmitContext& ctx, const std::string& prefix) {
   std::ostringstream o;
   auto name = [&](size_t r) { return prefix + "r" + std::to_string(r); };
+  // ---- finiteness coverage.  The reference rejects a non-finite result at
+  // the op that produces it.  A value whose every use carries the non-finite
+  // value on (under the same guard) into a value that is itself checked
+  // raises the same error in the same tick without its own check; values that
+  // are committed are checked once at the end.  Dropping the redundant checks
+  // roughly halves the instruction count of an exact-linear update.
+  const size_t R = p.register_count;
+  std::vector<const Instr*> producer(R, nullptr);
+  std::vector<std::vector<std::pair<const Instr*, int>>> uses(R);
+  for (const auto* list : {&p.scalar, &p.vector})
+    for (const auto& in : *list) {
+      producer[in.output] = &in;
+      uses[in.left].push_back({&in, 0});
+      if (in.right != in.left) uses[in.right].push_back({&in, 1});
+      if (in.third >= 0) uses[size_t(in.third)].push_back({&in, 2});
+      if (in.guard >= 0) uses[size_t(in.guard)].push_back({&in, 3});
+    }
+  std::vector<bool> committed(R, false), floating(R, false), checked_here(R, false), safe(R, false);
+  for (const auto& w : p.writes) committed[w.second] = true;
+  for (const auto* list : {&p.scalar, &p.vector})
+    for (const auto& in : *list)
+      floating[in.output] = finite_checked(in.op) || (in.op == IOp::Select && floating[in.left]);
+  std::vector<const Instr*> order;
+  for (const auto* list : {&p.scalar, &p.vector})
+    for (const auto& in : *list) order.push_back(&in);
+  for (auto it = order.rbegin(); it != order.rend(); ++it) {
+    const Instr& in = **it;
+    size_t r = in.output;
+    if (p.regs[r].kind == RegKind::Const) continue;
+    bool covered = !uses[r].empty();
+    for (const auto& [user, pos] : uses[r]) {
+      if (!propagates(*user, pos) || user->guard != in.guard || !safe[user->output]) {
+        covered = false;
+        break;
+      }
+    }
+    checked_here[r] = finite_checked(in.op) && !covered && !committed[r];
+    safe[r] = covered || checked_here[r] || committed[r];
+  }
   // Bindings: loaded at program start, like Program::run copies its inputs.
   for (const auto& [slot, in] : p.bindings) {
     const RegInfo& ri = p.regs[slot];
@@ -761,6 +831,14 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
   auto emit_list = [&](const std::vector<Instr>& list) {
     for (const auto& in : list) {
       const RegInfo& out = p.regs[in.output];
+      // Operand r is exactly the constant v (bit for bit) where `in` runs.
+      auto is_const = [&](size_t r, double v) {
+        if (in.guard >= 0 && size_t(in.guard) == r && in.op != IOp::Select) {
+          const Input* b = p.binding_of(r);
+          if (b && b->type() == DType::Bool) return bits_of(v) == bits_of(1.0);
+        }
+        return p.regs[r].kind == RegKind::Const && bits_of(p.regs[r].value) == bits_of(v);
+      };
       auto opnd = [&](size_t r) -> std::string {
         if (in.guard >= 0 && size_t(in.guard) == r && in.op != IOp::Select) {
           const Input* b = p.binding_of(r);
@@ -812,9 +890,13 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
         case IOp::Tan: expr = "tan(" + a + ")"; break;
         case IOp::Tanh: expr = "tanh(" + a + ")"; break;
         case IOp::Add: expr = "(" + a + " + " + b + ")"; break;
-        case IOp::Sub: expr = "(" + a + " - " + b + ")"; break;
-        case IOp::Mul: expr = "(" + a + " * " + b + ")"; break;
-        case IOp::Div: expr = "(" + a + " / " + b + ")"; break;
+        // IEEE identities that hold for every x including -0, inf and NaN:
+        // x - (+0) == x, x * 1 == 1 * x == x, x / 1 == x.
+        case IOp::Sub: expr = is_const(in.right, 0.0) ? a : "(" + a + " - " + b + ")"; break;
+        case IOp::Mul:
+          expr = is_const(in.right, 1.0) ? a : is_const(in.left, 1.0) ? b : "(" + a + " * " + b + ")";
+          break;
+        case IOp::Div: expr = is_const(in.right, 1.0) ? a : "(" + a + " / " + b + ")"; break;
         case IOp::Pow: expr = "pow(" + a + ", " + b + ")"; break;
         case IOp::Mod: expr = "b2_fmod_floor(" + a + ", " + b + ")"; break;
         case IOp::FloorDiv: expr = "floor(" + a + " / " + b + ")"; break;
@@ -933,7 +1015,8 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
         body = expr;
       } else {
         body = out_name + " = " + expr + ";";
-        if (check_finite) body += " if (!b2_finite(" + out_name + ")) err |= " + std::to_string(check_bit) + "u;";
+        bool need = check_finite && (checked_here[in.output] || check_bit != ERR_NONFINITE);
+        if (need) body += " if (!b2_finite(" + out_name + ")) err |= " + std::to_string(check_bit) + "u;";
       }
       if (in.op == IOp::Select || guard_const) {
         if (!guard_const && in.op != IOp::Select) o << "  if (" << guard << " != 0.0) { " << body << " }\n";
@@ -947,6 +1030,14 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
   };
   emit_list(p.scalar);
   emit_list(p.vector);
+  // Committed floating values: one check each, where the commit happens.
+  std::set<size_t> done;
+  for (const auto& w : p.writes) {
+    size_t r = w.second;
+    if (p.regs[r].kind == RegKind::Const || !floating[r] || done.count(r)) continue;
+    done.insert(r);
+    o << "  if (!b2_finite(" << name(r) << ")) err |= " << ERR_NONFINITE << "u;\n";
+  }
   return o.str();
 }
 

@@ -237,7 +237,11 @@ struct Engine::Impl {
     if (o.neurons_per_thread) npt_ = o.neurons_per_thread;
     check(npt_ == 1 || npt_ == 2 || npt_ == 4, "neurons per thread must be 1, 2 or 4");
     if (const char* e = std::getenv("B2GPU_MINBLOCKS")) min_blocks_ = unsigned(std::atoi(e));
+    // Diagnostic: plan every schedule node as its own kernel (same work,
+    // same results) to attribute time per node.
+    if (const char* e = std::getenv("B2GPU_NO_FUSE")) no_fuse_ = std::atoi(e) != 0;
   }
+  bool no_fuse_ = false;
 
   unsigned npt_ = 4;         // neurons per thread in neuron kernels
   unsigned min_blocks_ = 0;  // __launch_bounds__ occupancy hint for neuron kernels (0: none)
@@ -1434,7 +1438,7 @@ struct Engine::Impl {
                       n2.operation != b2ir::ScheduleOp::CodeObject)
                     continue;
                   const auto& c2 = code_of(n2);
-                  if (c2.kind == "threshold" && can_hoist(idx, y)) {
+                  if (c2.kind == "threshold" && !no_fuse_ && can_hoist(idx, y)) {
                     st.X = compile_pop(p, c2);
                     done[y] = true;
                     x_pos = y;
@@ -1461,7 +1465,7 @@ struct Engine::Impl {
                     bool movable = true;
                     for (size_t z = idx + 1; z < y; ++z)
                       if (!done[z] && conflicts(eff[y], eff[z])) movable = false;
-                    if (movable) {
+                    if (movable && !no_fuse_) {
                       st.R = compile_pop(p, c2);
                       done[y] = true;
                     }
@@ -1492,7 +1496,7 @@ struct Engine::Impl {
               // step when this node commutes with everything between here and
               // that step in the next tick (the schedule is cyclic).
               auto it = step_of_pop.find(p);
-              bool defer = it != step_of_pop.end();
+              bool defer = it != step_of_pop.end() && !no_fuse_;
               if (defer) {
                 for (size_t y = idx + 1; y < nodes.size() && defer; ++y)
                   if (!done[y] && conflicts(eff[idx], eff[y])) defer = false;
@@ -1540,7 +1544,7 @@ struct Engine::Impl {
         // Constant-addend pathways reading one spike stream at one delay and
         // writing disjoint target variables share a scatter launch.
         bool merged = false;
-        if (pw.mode == PathwayDev::Mode::Atomic && !specs.empty() && specs.back().kind == OpSpec::Kind::Path) {
+        if (pw.mode == PathwayDev::Mode::Atomic && !no_fuse_ && !specs.empty() && specs.back().kind == OpSpec::Kind::Path) {
           PathSpec& ps = paths[specs.back().index];
           PathwayDev* first = ps.pathways.front();
           bool ok = first->mode == PathwayDev::Mode::Atomic && first->stream == pw.stream && first->delay == pw.delay &&

@@ -151,7 +151,7 @@ struct Engine::Impl {
   struct EventStreamDev {
     size_t pop = 0, event = 0;
     uint64_t cap = 0, mask = 0;
-    int ring = -1, tick_start = -1, status = -1, gstatus = -1, ticket = -1;
+    int ring = -1, tick_start = -1, tile_count = -1, stage = -1, done = -1;
     bool produced = false, ascending = true;
     size_t max_delay = 0;  // deepest consumer delay
     // host copy of drained spikes
@@ -578,13 +578,10 @@ struct Engine::Impl {
       es.tick_start = alloc((steps + 1) * 8);
       memset_dev(es.tick_start, 8);
       size_t tiles = tiles_for(pd.count);
-      es.status = alloc(tiles * 8);
-      memset_dev(es.status, tiles * 8);
-      size_t groups = (tiles + 31) / 32;
-      es.gstatus = alloc(groups * 8);
-      memset_dev(es.gstatus, groups * 8);
-      es.ticket = alloc(8);
-      memset_dev(es.ticket, 8);
+      es.tile_count = alloc(tiles * 4);
+      es.stage = alloc(tiles * size_t(kThreads) * npt_ * 4);
+      es.done = alloc(8);
+      memset_dev(es.done, 8);
       es.starts.assign(1, 0);
     }
   }
@@ -777,14 +774,11 @@ struct Engine::Impl {
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
     size_t tiles = tiles_for(pd.count);
     constexpr unsigned W = kThreads / 32;
+    o << "  const u32 tile = blockIdx.x;\n";
     if (X) {
       o << "  __shared__ u32 s_ballot[" << npt * W << "];\n  __shared__ u32 s_off[" << npt * W + 1 << "];\n";
-      o << "  __shared__ u64 s_base;\n  __shared__ u32 s_tile;\n";
-      o << "  if (threadIdx.x == 0) s_tile = (u32)(atomicAdd((unsigned long long*)" << P(es->ticket, "u64") << ", 1ull) % "
-        << tiles << "ull);\n  __syncthreads();\n  const u32 tile = s_tile;\n";
+      o << "  __shared__ u32 s_last;\n";
       o << "  u32 fired_bits = 0;\n";
-    } else {
-      o << "  const u32 tile = blockIdx.x;\n";
     }
     o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
     if (!deferred.empty()) {
@@ -865,31 +859,32 @@ struct Engine::Impl {
     o << "  }\n";  // kk loop
     if (flush) o << "  if (blockIdx.x == 0 && threadIdx.x == 0) " << P(deferred_flags, "u64") << "[" << p << "] = tick;\n";
     if (X) {
+      // Tile-local ascending compaction into the staging area, then the
+      // last block to finish lays all tiles out (b2_finalize_spikes).
       o << "  __syncthreads();\n";
       o << "  if (warp == 0) {\n";
       o << "    u32 c = lane < " << npt * W << "u ? __popc(s_ballot[lane]) : 0u;\n";
       o << "    u32 x = c;\n";
       o << "#pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { u32 y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= (u32)d) x += y; }\n";
       o << "    if (lane < " << npt * W << "u) s_off[lane] = x - c;\n";
-      o << "    const u32 total = __shfl_sync(0xffffffffu, x, 31);\n";
-      o << "    const u64 prefix = b2_tile_prefix(tick, tile, " << tiles << "u, " << P(es->status, "u64") << ", "
-        << P(es->gstatus, "u64") << ", (u64)total, err);\n";
-      o << "    if (lane == 0) {\n";
-      o << "      const u64 base = " << P(es->tick_start, "u64") << "[rel] + prefix;\n";
-      o << "      s_base = base;\n";
-      o << "      if (tile == " << tiles - 1 << "u) {\n";
-      o << "        " << P(es->tick_start, "u64") << "[rel + 1] = base + total;\n";
-      o << "        if (base + total - ctl->ring_floor > " << u64lit(es->cap) << ") err |= " << kErrRing << "u;\n";
-      o << "      }\n    }\n  }\n";
+      o << "    if (lane == 31) " << P(es->tile_count, "u32") << "[tile] = x;\n";
+      o << "  }\n";
       o << "  __syncthreads();\n";
-      o << "  if (fired_bits) {\n    u32* ring = " << P(es->ring, "u32") << ";\n";
+      o << "  if (fired_bits) {\n    u32* stage = " << P(es->stage, "u32") << " + (u64)tile * " << tile_n << "u;\n";
       o << "#pragma unroll\n    for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
       o << "      if ((fired_bits >> kk) & 1u) {\n";
       o << "        const u32 slot = kk * " << W << "u + warp;\n";
-      o << "        const u64 pos = s_base + s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u));\n";
-      o << "        ring[pos & " << u64lit(es->mask) << "] = tile * " << tile_n << "u + kk * " << kThreads
-        << "u + threadIdx.x;\n";
+      o << "        stage[s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u))] = tile * " << tile_n
+        << "u + kk * " << kThreads << "u + threadIdx.x;\n";
       o << "      }\n    }\n  }\n";
+      o << "  __threadfence();\n  __syncthreads();\n";
+      o << "  if (threadIdx.x == 0) s_last = (atomicAdd((unsigned long long*)" << P(es->done, "u64") << ", 1ull) % "
+        << tiles << "ull) == " << tiles - 1 << "ull;\n";
+      o << "  __syncthreads();\n";
+      o << "  if (s_last) {\n    __threadfence();\n";
+      o << "    b2_finalize_spikes<" << kThreads << ">(" << tiles << "u, " << tile_n << "u, " << P(es->tile_count, "const u32")
+        << ", " << P(es->stage, "const u32") << ", " << P(es->ring, "u32") << ", " << u64lit(es->mask) << ", "
+        << P(es->tick_start, "u64") << ", rel, " << u64lit(es->cap) << ", ctl->ring_floor, err);\n  }\n";
     }
     o << kernel_tail();
     return o.str();

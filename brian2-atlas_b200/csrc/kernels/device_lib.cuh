@@ -444,6 +444,55 @@ __device__ u64 b2_tile_prefix(u64 tick, u32 tile, u32 tiles, u64* tile_status, u
   return b2_warp_sum_u64(prev) + own;
 }
 
+// Last-block finalisation of a tick's spike list.  Every block has written
+// its tile's ascending spikes to stage[tile * tile_n ...] and their number to
+// tile_count[tile]; the block that finishes last (observed through a
+// monotonically increasing completion counter after a __threadfence) lays the
+// tiles out in tile order: an exclusive scan of the tile counts gives each
+// tile's offset in the tick's list, which is therefore globally ascending.
+// No block ever waits for another.  Called by all threads of the last block.
+template <int THREADS>
+__device__ void b2_finalize_spikes(u32 tiles, u32 tile_n, const u32* tile_count, const u32* stage, u32* ring,
+                                   u64 mask, u64* tick_start, u64 rel, u64 cap, u64 floor, u32& err) {
+  __shared__ u32 s_warp_sum[THREADS / 32];
+  __shared__ u32 s_total;
+  const u32 per = (tiles + THREADS - 1) / THREADS;
+  const u32 t0 = threadIdx.x * per, t1 = min(tiles, t0 + per);
+  u32 mine = 0;
+  for (u32 t = t0; t < t1; ++t) mine += __ldcg(tile_count + t);
+  const u32 lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  u32 x = mine;
+#pragma unroll
+  for (int d = 1; d < 32; d <<= 1) {
+    u32 y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= (u32)d) x += y;
+  }
+  if (lane == 31) s_warp_sum[warp] = x;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    u32 acc = 0;
+    for (int w = 0; w < THREADS / 32; ++w) {
+      u32 c = s_warp_sum[w];
+      s_warp_sum[w] = acc;
+      acc += c;
+    }
+    s_total = acc;
+  }
+  __syncthreads();
+  const u64 base = tick_start[rel];
+  u64 pos = base + s_warp_sum[warp] + (x - mine);
+  for (u32 t = t0; t < t1; ++t) {
+    const u32 n = __ldcg(tile_count + t);
+    for (u32 k = 0; k < n; ++k) ring[(pos + k) & mask] = __ldcg(stage + (u64)t * tile_n + k);
+    pos += n;
+  }
+  if (threadIdx.x == 0) {
+    const u64 end = base + s_total;
+    tick_start[rel + 1] = end;
+    if (end - floor > cap) err |= B2_ERR_RING;
+  }
+}
+
 // Block-level exclusive offsets of `fired` lanes and the block's global base
 // in the tick's ascending spike list.  `tile` is this block's position in
 // neuron order (taken from a ticket, so every predecessor tile has already

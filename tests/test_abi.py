@@ -82,7 +82,7 @@ def test_exact_linear_update_is_pure_arithmetic(pkg):
     the per-neuron update issues no device transcendental."""
     src = pkg.codegen(load("cuba_small"))
     step = src[src.index("neurons_step"):]
-    step = step[:step.index("b2_tile_prefix")]
+    step = step[:step.index("b2_finalize_spikes")]
     assert "exp(" not in step and "log(" not in step
 
 

@@ -10,8 +10,8 @@
 namespace b2gpu {
 
 // Source-major CSR of a fixed in-degree projection restricted to the targets
-// [t_lo, t_hi): offsets[S+1] (u64) and row_targets[] (u32, target indices
-// local to the target range), rows in ascending target order.
+// [t_lo, t_hi): offsets[S+1] (u64) and row_targets[] (u32, global target
+// indices in [t_lo, t_hi)), rows in ascending target order.
 void build_fixed_indegree_csr(uint64_t S, uint64_t T, uint64_t K, uint64_t seed, uint64_t t_lo, uint64_t t_hi,
                               DeviceBuffer& offsets, DeviceBuffer& row_targets, uint64_t& local_edges,
                               cudaStream_t stream);

@@ -37,7 +37,7 @@ def test_version(pkg):
 
 
 def kernels(src):
-    return re.findall(r"__global__ void __launch_bounds__\(\d+\) (\w+)", src)
+    return re.findall(r"__global__ void __launch_bounds__\(\d+(?:, \d+)?\) (\w+)", src)
 
 
 def load(name):

@@ -14,6 +14,14 @@ engine's stream) over the timed steps; `e2e` is the same count over the wall
 time of the public C-ABI b2g_step calls, which include the per-chunk
 host->device tick cursor and device->host spike-list drain.
 
+With N > 1 GPUs (torchrun, one process per GPU) the same network is split by
+target ownership: rank r owns neurons [floor(N r/G), floor(N (r+1)/G)) and
+their incoming edges, and the tick kernels exchange spikes by storing into the
+peers' memory over NVLink (strong scaling: the total work is fixed).  Every
+timed step is bracketed by a barrier and a device synchronisation on every
+rank; the step's time is the maximum over ranks; `value` counts every rank's
+deliveries.
+
 --impl reference times the CPU restatement of the reference executor
 (oracle/b2ref, single-threaded like b2-runner) on a bounded sample of the
 same network (50,000 neurons, in-degree 1000).
@@ -68,7 +76,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.device}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except OSError:
@@ -158,7 +166,7 @@ def run_reference(args, world, rank):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--neurons", type=int, default=N_NEURONS)
@@ -171,21 +179,43 @@ def main():
     if args.impl == "reference":
         run_reference(args, world, rank)
         return
-    if world != 1:
-        raise SystemExit("multi-GPU runs are launched through the distributed runner (not available yet)")
     assert args.warmup >= 3, "at least 3 warm-up steps"
     pkg = importlib.import_module("brian2-atlas_b200")
+    import torch  # plumbing: process group, barriers, an L2 flush buffer
+    torch.cuda.set_device(local_rank)
+    dist = None
+    if world > 1:
+        from datetime import timedelta
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local_rank))
+        distributed = importlib.import_module("brian2-atlas_b200.distributed")
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier()
+
+    def reduce(values, op):
+        if dist is None:
+            return values
+        t = torch.tensor(values, dtype=torch.float64, device=f"cuda:{local_rank}")
+        dist.all_reduce(t, op=op)
+        return t.tolist()
+
     total_ticks = (args.warmup + args.steps) * TICKS_PER_STEP
     t0 = time.time()
     model = build_model(args.neurons, args.indegree, total_ticks + 400)
     t_json = time.time() - t0
-    eng = pkg.Engine(model, device=local_rank)
+    if world > 1:
+        eng = pkg.Engine(model, device=local_rank, rank=rank, world_size=world)
+        distributed.connect(eng)
+    else:
+        eng = pkg.Engine(model, device=local_rank)
     del model
     st0 = eng.stats()
     for _ in range(args.warmup):
+        barrier()
         eng.step(TICKS_PER_STEP)
-    import torch  # plumbing only: an L2 flush buffer on the same device
-    torch.cuda.set_device(local_rank)
     flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=f"cuda:{local_rank}")
     before = eng.stats()
     wall = 0.0
@@ -193,26 +223,47 @@ def main():
     with ClockSampler(local_rank) as clocks:
         for _ in range(args.steps):
             flush.fill_(1)
-            torch.cuda.synchronize()
+            barrier()
             s0 = eng.stats()
             w0 = time.perf_counter()
             eng.step(TICKS_PER_STEP)
-            wall += time.perf_counter() - w0
+            w1 = time.perf_counter() - w0
             s1 = eng.stats()
-            dev += s1["device_seconds"] - s0["device_seconds"]
+            barrier()
+            # the step's time is the slowest rank's
+            d, w = reduce([s1["device_seconds"] - s0["device_seconds"], w1],
+                          dist.ReduceOp.MAX if dist else None)
+            dev += d
+            wall += w
     after = eng.stats()
-    events = after["synaptic_events"] - before["synaptic_events"]
+    # deliveries and launches of every rank; spikes are global on every rank
+    events, launches = reduce([after["synaptic_events"] - before["synaptic_events"],
+                               after["kernel_launches"] - before["kernel_launches"]],
+                              dist.ReduceOp.SUM if dist else None)
+    events, launches = int(events), int(launches)
     spikes = after["spikes"] - before["spikes"]
-    launches = after["kernel_launches"] - before["kernel_launches"]
     h2d = (after["h2d_bytes"] - before["h2d_bytes"]) / args.steps
     d2h = (after["d2h_bytes"] - before["d2h_bytes"]) / args.steps
     sim_seconds = args.steps * TICKS_PER_STEP * DT
     # Per-kernel timing (events around each launch) over 400 further ticks.
+    barrier()
     prof = eng.profile(400)
     prof_after = eng.stats()
     prof_spikes = prof_after["spikes"] - after["spikes"]
     prof_events = prof_after["synaptic_events"] - after["synaptic_events"]
+    clock_summary = clocks.summary()
+    barrier()
     eng.close()
+    if dist is not None:
+        clock_all = [None] * world
+        dist.all_gather_object(clock_all, clock_summary)
+        dist.destroy_process_group()
+        if rank != 0:
+            return
+        clock_summary = dict(clock_all[0], reasons=sorted({r for c in clock_all for r in c["reasons"]}),
+                             sm_mhz_min_over_ranks=min((c["sm_mhz"] or 0) for c in clock_all))
+    local_neurons = pkg.partition(args.neurons, rank, world)
+    local_neurons = local_neurons[1] - local_neurons[0]
     hbm, peak_kind = peaks()
     ticks_prof = 400
     kernels = []
@@ -221,13 +272,13 @@ def main():
         if "_step" in k["name"]:
             # neuron update + threshold + compaction + reset: read and write
             # v, ge, gi (f64) and read lastspike (f64) per neuron, 4 B per spike
-            per_launch = args.neurons * (2 * 24 + 8) + 4 * prof_spikes / ticks_prof
+            per_launch = local_neurons * (2 * 24 + 8) + 4 * prof_spikes / ticks_prof
         elif k["name"].endswith("_atomic"):
             # scatter: 4 B row entry per event, read+write of the f64 target per
             # event (upper bound of 2*8*U_t), 4 B per fired source
             per_launch = (4 + 16) * (prof_events / ticks_prof) / 2 + 4 * prof_spikes / ticks_prof
         elif "poisson_input" in k["name"]:
-            per_launch = args.neurons * 16
+            per_launch = local_neurons * 16
         else:
             per_launch = 0
         kernels.append({"name": k["name"], "avg_us": 1e3 * avg_ms, "launches": k["launches"],
@@ -238,7 +289,7 @@ def main():
         k["share"] = k["avg_us"] * k["launches"] / total
     dominant = max(kernels, key=lambda k: k["share"]) if kernels else None
     cpu = None
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and world == 1:
         with tempfile.TemporaryDirectory() as tmp:
             s = cpu_sample(Path(tmp), CPU_SAMPLE_WARMUP, CPU_SAMPLE_TICKS)
         cpu = {"value": s["synaptic_events"] / s["seconds"], "unit": UNIT, "cores": 1, "kind": "port",
@@ -246,13 +297,15 @@ def main():
                          f"{INDEGREE}) after {CPU_SAMPLE_WARMUP} warm-up ticks; oracle/b2ref single thread; "
                          f"{s['synaptic_events']} events in {s['seconds']:.3f} s"}
     line = {
-        "metric": METRIC, "value": events / dev if dev > 0 else 0.0, "unit": UNIT, "n_gpus": 1,
+        "metric": METRIC, "value": events / dev if dev > 0 else 0.0, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dev / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded; definition layer lowered by the reference frontend)",
         "config": {"workload": "config 2: CUBA 1M neurons, fixed in-degree 1000 (1e9 synapses), Poisson 100x10 Hz",
                    "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
-                   "ticks_per_step": TICKS_PER_STEP, "dt_s": DT, "parallelism": "single GPU",
+                   "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+                   "parallelism": "single GPU" if world == 1 else
+                   f"{world} GPUs: target-owned partition, spikes exchanged by peer stores over NVLink",
                    "l2": "256 MiB buffer written between timed steps; per-tick neuron state (56 MB) stays "
                          "L2-resident within a step"},
         "realtime_factor": sim_seconds / dev if dev > 0 else None,
@@ -265,7 +318,7 @@ def main():
             "bound": "hbm", "kernel": dominant["name"], "achieved": dominant["achieved_gbs"], "peak": hbm,
             "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["achieved_gbs"] / hbm, "traffic": None},
         "kernels": kernels,
-        "clocks": clocks.summary(),
+        "clocks": clock_summary,
         "build": {"json_seconds": t_json, "engine_build_seconds": st0["build_seconds"],
                   "nvrtc_seconds": st0["compile_seconds"]},
         "cpu_baseline": cpu,

@@ -31,7 +31,8 @@ class B2GpuError(RuntimeError):
 
 class Options(ctypes.Structure):
     _fields_ = [("struct_size", ctypes.c_uint32), ("device", ctypes.c_int32), ("chunk_ticks", ctypes.c_uint32),
-                ("use_graphs", ctypes.c_uint32), ("ring_capacity", ctypes.c_uint64)]
+                ("use_graphs", ctypes.c_uint32), ("ring_capacity", ctypes.c_uint64), ("rank", ctypes.c_int32),
+                ("world_size", ctypes.c_int32), ("exchange_timeout_ms", ctypes.c_uint32), ("reserved0", ctypes.c_uint32)]
 
 
 class Stats(ctypes.Structure):
@@ -66,8 +67,13 @@ def library() -> ctypes.CDLL:
         "b2g_spikes": (c.c_int, [c.c_void_p, c.c_uint32, c.c_uint64, c.c_void_p, c.c_size_t,
                                  c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
         "b2g_generated_source": (c.c_int, [c.c_void_p, c.c_char_p, c.c_size_t, c.POINTER(c.c_size_t)]),
-        "b2g_codegen": (c.c_int, [c.c_char_p, c.c_size_t, c.c_char_p, c.c_size_t, c.POINTER(c.c_size_t),
-                                  c.c_char_p, c.c_size_t]),
+        "b2g_codegen": (c.c_int, [c.c_char_p, c.c_size_t, c.POINTER(Options), c.c_char_p, c.c_size_t,
+                                  c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
+        "b2g_partition": (None, [c.c_uint64, c.c_int32, c.c_int32, c.POINTER(c.c_uint64), c.POINTER(c.c_uint64)]),
+        "b2g_ipc_handle": (c.c_int, [c.c_void_p, c.c_void_p, c.c_size_t, c.POINTER(c.c_size_t), c.c_char_p,
+                                     c.c_size_t]),
+        "b2g_connect": (c.c_int, [c.c_void_p, c.c_void_p, c.c_size_t, c.c_size_t, c.c_char_p, c.c_size_t]),
+        "b2g_publish_results": (c.c_int, [c.c_void_p, c.c_char_p, c.c_size_t]),
         "b2g_profile": (c.c_int, [c.c_void_p, c.c_uint64, c.POINTER(KernelTime), c.c_size_t,
                                   c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
         "b2g_destroy": (None, [c.c_void_p]),
@@ -89,31 +95,51 @@ def version() -> str:
     return library().b2g_version().decode()
 
 
-def codegen(model_json: bytes) -> str:
-    """Compile a model's plan for sm_100a without a GPU and return the source."""
+def _options(device=-1, chunk_ticks=0, use_graphs=True, ring_capacity=0, rank=0, world_size=1,
+             exchange_timeout_ms=0) -> Options:
+    opt = Options()
+    library().b2g_default_options(ctypes.byref(opt))
+    opt.device = device
+    if chunk_ticks:
+        opt.chunk_ticks = chunk_ticks
+    opt.use_graphs = 1 if use_graphs else 0
+    opt.ring_capacity = ring_capacity
+    opt.rank = rank
+    opt.world_size = world_size
+    opt.exchange_timeout_ms = exchange_timeout_ms
+    return opt
+
+
+def codegen(model_json: bytes, rank: int = 0, world_size: int = 1) -> str:
+    """Compile a model's plan (of one rank of `world_size`) for sm_100a without
+    a GPU and return the generated source."""
     lib = library()
+    opt = _options(rank=rank, world_size=world_size)
     err, need = _err(), ctypes.c_size_t(0)
-    if lib.b2g_codegen(model_json, len(model_json), None, 0, ctypes.byref(need), err, len(err)):
+    if lib.b2g_codegen(model_json, len(model_json), ctypes.byref(opt), None, 0, ctypes.byref(need), err, len(err)):
         raise B2GpuError(err.value.decode())
     buf = ctypes.create_string_buffer(need.value)
-    if lib.b2g_codegen(model_json, len(model_json), buf, need, ctypes.byref(need), err, len(err)):
+    if lib.b2g_codegen(model_json, len(model_json), ctypes.byref(opt), buf, need, ctypes.byref(need), err, len(err)):
         raise B2GpuError(err.value.decode())
     return buf.value.decode()
+
+
+def partition(count: int, rank: int, world_size: int) -> tuple:
+    """Global index range [lo, hi) that `rank` of `world_size` owns (the
+    reference's owner rule, brian2_rust/distributed.py:80-81)."""
+    lo, hi = ctypes.c_uint64(0), ctypes.c_uint64(0)
+    library().b2g_partition(count, rank, world_size, ctypes.byref(lo), ctypes.byref(hi))
+    return lo.value, hi.value
 
 
 class Engine:
     """One AtlasIR run on one GPU (mirrors the reference `Runtime`)."""
 
     def __init__(self, model_json: bytes, device: int = -1, chunk_ticks: int = 0, use_graphs: bool = True,
-                 ring_capacity: int = 0):
+                 ring_capacity: int = 0, rank: int = 0, world_size: int = 1, exchange_timeout_ms: int = 0):
         lib = library()
-        opt = Options()
-        lib.b2g_default_options(ctypes.byref(opt))
-        opt.device = device
-        if chunk_ticks:
-            opt.chunk_ticks = chunk_ticks
-        opt.use_graphs = 1 if use_graphs else 0
-        opt.ring_capacity = ring_capacity
+        opt = _options(device, chunk_ticks, use_graphs, ring_capacity, rank, world_size, exchange_timeout_ms)
+        self.rank, self.world_size = rank, world_size
         err = _err()
         self._h = lib.b2g_create(model_json, len(model_json), ctypes.byref(opt), err, len(err))
         if not self._h:
@@ -164,6 +190,25 @@ class Engine:
         return [{"name": out[i].name.decode(), "launches": out[i].launches, "total_ms": out[i].total_ms}
                 for i in range(min(count.value, 64))]
 
+    # ---- multi-GPU (see brian2-atlas_b200/distributed.py for the driver)
+    def ipc_handle(self) -> bytes:
+        """CUDA IPC handle of this rank's shared exchange/staging allocation."""
+        buf = ctypes.create_string_buffer(256)
+        n = ctypes.c_size_t(0)
+        self._call("b2g_ipc_handle", buf, 256, ctypes.byref(n))
+        return buf.raw[:n.value]
+
+    def connect(self, handles: list) -> None:
+        """Map every rank's allocation; `handles` = all ranks' ipc_handle() in rank order."""
+        if len({len(h) for h in handles}) != 1:
+            raise B2GpuError("IPC handles differ in length")
+        blob = b"".join(handles)
+        self._call("b2g_connect", blob, len(handles[0]), len(handles))
+
+    def publish_results(self) -> None:
+        """Stage this rank's final results for rank 0's write_results()."""
+        self._call("b2g_publish_results")
+
     def generated_source(self) -> str:
         need = ctypes.c_size_t(0)
         self._lib.b2g_generated_source(self._h, None, 0, ctypes.byref(need))
@@ -211,5 +256,5 @@ def package_dir() -> Path:
     return _PKG
 
 
-__all__ = ["Engine", "B2GpuError", "run_model", "codegen", "version", "library", "runner_path", "LIBRARY",
-           "RUNNER"]
+__all__ = ["Engine", "B2GpuError", "run_model", "codegen", "partition", "version", "library", "runner_path",
+           "LIBRARY", "RUNNER"]

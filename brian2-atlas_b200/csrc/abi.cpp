@@ -5,6 +5,7 @@
 #include <sys/stat.h>
 
 #include <chrono>
+#include <cstddef>
 #include <cstdio>
 #include <cstring>
 #include <fstream>
@@ -50,13 +51,22 @@ int guarded(b2g_engine* e, char* error, size_t cap, F f) {
   }
 }
 
+// Fields past struct_size keep their defaults (older callers).
+constexpr size_t kOptionsV1 = offsetof(b2g_options, rank);
+
 b2gpu::Options to_options(const b2g_options* o) {
   b2gpu::Options opt;
   if (!o) return opt;
+  if (o->struct_size < kOptionsV1) throw b2ir::Error("b2g_options.struct_size too small");
   opt.device = o->device;
   if (o->chunk_ticks) opt.chunk_ticks = o->chunk_ticks;
   opt.use_graphs = o->use_graphs != 0;
   opt.ring_capacity = o->ring_capacity;
+  if (o->struct_size >= offsetof(b2g_options, reserved0)) {
+    opt.rank = o->rank;
+    opt.world_size = o->world_size;
+    if (o->exchange_timeout_ms) opt.exchange_timeout_ms = o->exchange_timeout_ms;
+  }
   return opt;
 }
 
@@ -76,10 +86,10 @@ void b2g_default_options(b2g_options* o) {
 b2g_engine* b2g_create(const char* json, size_t len, const b2g_options* options, char* error, size_t cap) {
   try {
     if (!json) throw b2ir::Error("null model document");
-    if (options && options->struct_size < sizeof(b2g_options)) throw b2ir::Error("b2g_options.struct_size too small");
+    b2gpu::Options opt = to_options(options);
     b2ir::Model m = b2ir::load_model(json, len);
     auto e = std::make_unique<b2g_engine>();
-    e->engine = std::make_unique<b2gpu::Engine>(m, to_options(options));
+    e->engine = std::make_unique<b2gpu::Engine>(m, opt);
     set_error(error, cap, "");
     return e.release();
   } catch (const std::exception& ex) {
@@ -178,11 +188,12 @@ int b2g_generated_source(const b2g_engine* e, char* dst, size_t capacity, size_t
   return 0;
 }
 
-int b2g_codegen(const char* json, size_t len, char* dst, size_t capacity, size_t* needed, char* error, size_t cap) {
+int b2g_codegen(const char* json, size_t len, const b2g_options* options, char* dst, size_t capacity, size_t* needed,
+                char* error, size_t cap) {
   try {
     if (!json) throw b2ir::Error("null model document");
+    b2gpu::Options opt = to_options(options);
     b2ir::Model m = b2ir::load_model(json, len);
-    b2gpu::Options opt;
     opt.dry_run = true;
     b2gpu::Engine engine(m, opt);
     const std::string& s = engine.generated_source();
@@ -197,6 +208,46 @@ int b2g_codegen(const char* json, size_t len, char* dst, size_t capacity, size_t
     set_error(error, cap, ex.what());
     return 1;
   }
+}
+
+void b2g_partition(uint64_t count, int32_t rank, int32_t world_size, uint64_t* lo, uint64_t* hi) {
+  uint64_t l = 0, h = 0;
+  if (world_size > 0 && rank >= 0 && rank < world_size) {
+    // floor(count * r / G) without overflow for any u64 count
+    auto at = [&](uint64_t r) {
+      const unsigned __int128 x = static_cast<unsigned __int128>(count) * r;
+      return static_cast<uint64_t>(x / static_cast<uint64_t>(world_size));
+    };
+    l = at(uint64_t(rank));
+    h = at(uint64_t(rank) + 1);
+  }
+  if (lo) *lo = l;
+  if (hi) *hi = h;
+}
+
+int b2g_ipc_handle(b2g_engine* e, void* handle, size_t capacity, size_t* length, char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    std::vector<uint8_t> h = e->engine->ipc_handle();
+    if (length) *length = h.size();
+    if (handle) {
+      if (capacity < h.size()) throw b2ir::Error("handle buffer too small");
+      std::memcpy(handle, h.data(), h.size());
+    }
+  });
+}
+
+int b2g_connect(b2g_engine* e, const void* handles, size_t handle_length, size_t count, char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    if (!handles) throw b2ir::Error("null handles");
+    std::vector<std::vector<uint8_t>> hs(count);
+    const uint8_t* b = static_cast<const uint8_t*>(handles);
+    for (size_t q = 0; q < count; ++q) hs[q].assign(b + q * handle_length, b + (q + 1) * handle_length);
+    e->engine->connect(hs);
+  });
+}
+
+int b2g_publish_results(b2g_engine* e, char* error, size_t cap) {
+  return guarded(e, error, cap, [&] { e->engine->publish(); });
 }
 
 void b2g_destroy(b2g_engine* e) { delete e; }

@@ -85,7 +85,7 @@ double timestep_threshold(double dt, double target) {
 
 
 constexpr uint32_t kErrNonfinite = 0x1, kErrTimestep = 0x2, kErrBinomial = 0x4, kErrPoisson = 0x8,
-                   kErrRing = 0x10, kErrLookback = 0x20, kErrIntDiv = 0x40, kErrTimedArray = 0x80,
+                   kErrRing = 0x10, kErrIntDiv = 0x40, kErrTimedArray = 0x80,
                    kErrCast = 0x100, kErrExchange = 0x200;
 
 std::string error_message(uint32_t e) {
@@ -97,8 +97,7 @@ std::string error_message(uint32_t e) {
   if (e & kErrTimedArray) return "TimedArray index/value outside supported range";
   if (e & kErrCast) return "unsupported cast source";
   if (e & kErrRing) return "spike ring overflow (raise the ring capacity)";
-  if (e & kErrLookback) return "spike compaction look-back timed out";
-  if (e & kErrExchange) return "spike exchange failed";
+  if (e & kErrExchange) return "spike exchange with a peer GPU timed out (a rank stopped or fell behind)";
   return "device error";
 }
 
@@ -154,13 +153,22 @@ struct Engine::Impl {
     int ring = -1, tick_start = -1, tile_count = -1, stage = -1, done = -1;
     bool produced = false, ascending = true;
     size_t max_delay = 0;  // deepest consumer delay
+    // multi-GPU: every rank's fired words arrive in the exchange buffer
+    // (offset x_off of each rank's shared allocation; g_ptr slot xptr[q] is
+    // rank q's copy) and an expand kernel of x_tiles blocks turns them into
+    // the tick's ascending global list.
+    bool exchanged = false;
+    size_t x_off = 0;
+    std::vector<int> xptr;
+    uint64_t x_words = 0, x_tiles = 0;
     // host copy of drained spikes
     std::vector<uint32_t> ids;
     std::vector<uint64_t> starts;  // host positions per tick: starts[rel] .. starts[rel+1]
     uint64_t drained_pos = 0;
   };
   struct PopDev {
-    size_t count = 0, start_tick = 0, end_tick = 0, steps = 0;
+    size_t count = 0, start_tick = 0, end_tick = 0, steps = 0;  // count: neurons owned by this rank
+    uint64_t lo = 0, global_count = 0;                            // owned block [lo, lo + count)
     double dt = 0.0;
     std::vector<Slot> states;
     int lastspike = -1, not_refractory = -1;
@@ -172,6 +180,7 @@ struct Engine::Impl {
     bool has_spike_monitor = false;
     // state monitor
     int mon_records = -1;
+    size_t mon_nrec = 0;            // records owned by this rank
     std::vector<int> mon_samples;  // per monitor variable
     std::vector<DType> mon_dtypes;
     uint64_t mon_ticks = 0, mon_first_tick = 0;
@@ -204,7 +213,9 @@ struct Engine::Impl {
     bool has_pending = false;
   };
   struct SynDev {
-    uint64_t edges = 0;
+    uint64_t edges = 0;        // global edge count (the `N` of synaptic code)
+    uint64_t local_edges = 0;  // edges whose target this rank owns (== edges on one GPU)
+    bool procedural = false;
     std::vector<Slot> states;
     std::map<std::string, int> param_ptr;
     std::map<std::string, double> param_const;
@@ -232,7 +243,16 @@ struct Engine::Impl {
   double dt = 0.0;
   bool failed = false;
 
-  Impl(const b2ir::Model& model, const Options& o) : m(model), opt(o) {
+  // ---- multi-GPU partition
+  int world = 1, rank = 0;
+  DeviceBuffer arena;                 // exchange buffers + result staging (CUDA IPC exported)
+  size_t arena_stage_off = 0;
+  std::vector<void*> peer_base;       // other ranks' arenas, mapped by connect()
+  bool connected = false, published = false;
+  void* gptr_table = nullptr;         // device address of the module's g_ptr table
+  uint64_t part_lo(uint64_t n, int r) const { return n * uint64_t(r) / uint64_t(world); }
+
+  Impl(const b2ir::Model& model, const Options& o) : m(model), opt(o), world(o.world_size), rank(o.rank) {
     if (const char* e = std::getenv("B2GPU_NPT")) npt_ = unsigned(std::atoi(e));
     if (o.neurons_per_thread) npt_ = o.neurons_per_thread;
     check(npt_ == 1 || npt_ == 2 || npt_ == 4, "neurons per thread must be 1, 2 or 4");
@@ -254,6 +274,8 @@ struct Engine::Impl {
   }
 
   ~Impl() {
+    for (void* pb : peer_base)
+      if (pb) cudaIpcCloseMemHandle(pb);
     if (ev_start) cudaEventDestroy(ev_start);
     if (ev_stop) cudaEventDestroy(ev_stop);
     if (graph_exec) cudaGraphExecDestroy(graph_exec);
@@ -311,7 +333,24 @@ struct Engine::Impl {
     }
     for (const auto& si : m.synapse_instances)
       check(si.topology.kind != b2ir::Topology::Kind::BinaryCsr, "binary_csr topology is not supported by the GPU engine yet");
-    check(opt.world_size == 1, "multi-GPU partitioning is configured through the distributed runner");
+    // one warp lane per destination rank stores a fired word: at most 32 ranks
+    check(world >= 1 && world <= 32 && rank >= 0 && rank < world, "invalid rank / world size (1 to 32 GPUs)");
+    if (world > 1) {
+      // Target-owned partition (brian2_rust/distributed.py: rank-local neuron
+      // and synapse state, incoming CSR per rank).  What a rank cannot
+      // evaluate from its own block is rejected before any device work.
+      for (const auto& s : m.synapses) {
+        for (const auto& c : s.code_objects)
+          check(c.kind == "synapses", "multi-GPU runs support on_pre pathways only");
+      }
+      for (size_t k = 0; k < m.synapses.size(); ++k) {
+        const auto& inst = m.synapse_instances[k];
+        if (inst.topology.kind != b2ir::Topology::Kind::Explicit) {
+          check(m.synapses[k].states.empty(), "multi-GPU runs need explicit topologies for plastic synapses");
+          check(inst.topology.initializers.empty(), "multi-GPU runs do not support procedural per-edge initializers");
+        }
+      }
+    }
   }
 
   // ================================================================ populations
@@ -320,20 +359,25 @@ struct Engine::Impl {
       const auto& def = m.populations[p];
       const auto& inst = m.population_instances[p];
       PopDev pd;
-      pd.count = def.count;
+      pd.global_count = def.count;
+      pd.lo = part_lo(def.count, rank);
+      pd.count = part_lo(def.count, rank + 1) - pd.lo;
+      const size_t lo = pd.lo, n = pd.count;
       pd.start_tick = start_tick;
       pd.steps = def.steps;
       pd.end_tick = start_tick + def.steps;
       pd.dt = def.dt;
       for (const auto& s : def.states) {
         const auto& arr = inst.initial_state.at(s.name);
-        std::vector<uint8_t> bytes(arr.size() * b2ir::dtype_bytes(s.dtype));
-        for (size_t i = 0; i < arr.size(); ++i) std::memcpy(&bytes[i * b2ir::dtype_bytes(s.dtype)], &arr.raw[i], b2ir::dtype_bytes(s.dtype));
+        check(arr.size() == def.count, "initial state '" + s.name + "' has the wrong length");
+        const size_t w = b2ir::dtype_bytes(s.dtype);
+        std::vector<uint8_t> bytes(n * w);
+        for (size_t i = 0; i < n; ++i) std::memcpy(&bytes[i * w], &arr.raw[lo + i], w);
         pd.states.push_back({s.dtype, upload(bytes.data(), bytes.size())});
       }
       if (inst.refractory) {
-        pd.lastspike = upload(inst.refractory->initial_lastspike.data(), def.count * 8);
-        pd.not_refractory = upload(inst.refractory->initial_not_refractory.data(), def.count);
+        pd.lastspike = upload(inst.refractory->initial_lastspike.data() + lo, n * 8);
+        pd.not_refractory = upload(inst.refractory->initial_not_refractory.data() + lo, n);
         pd.period_ticks = inst.refractory->period_ticks;
         pd.fixed_refractory = def.refractory && def.refractory->mode == "fixed";
       }
@@ -344,9 +388,10 @@ struct Engine::Impl {
         if (s.index_domain == b2ir::IndexDomain::Scalar || uniform) {
           pd.param_const[s.name] = arr.as_f64(0);
         } else {
-          std::vector<double> v(arr.size());
-          for (size_t i = 0; i < arr.size(); ++i) v[i] = arr.as_f64(i);
-          pd.param_ptr[s.name] = upload(v.data(), v.size() * 8);
+          check(arr.size() == def.count, "parameter '" + s.name + "' has the wrong length");
+          std::vector<double> v(n);
+          for (size_t i = 0; i < n; ++i) v[i] = arr.as_f64(lo + i);
+          pd.param_ptr[s.name] = upload(v.data(), std::max<size_t>(n, 1) * 8);
         }
       }
       pd.stream_of_event.assign(def.events.size(), -1);
@@ -363,9 +408,14 @@ struct Engine::Impl {
           pd.has_spike_monitor = true;
       // state monitor buffers
       if (!def.state_monitors.empty() && !def.monitor.record.empty() && !def.monitor.variables.empty()) {
-        std::vector<uint32_t> rec(def.monitor.record.begin(), def.monitor.record.end());
-        for (auto r : rec) check(r < def.count, "state monitor record index out of range");
-        pd.mon_records = upload(rec.data(), rec.size() * 4);
+        // Records this rank owns, as local indices, in record order.
+        std::vector<uint32_t> rec;
+        for (auto r : def.monitor.record) {
+          check(r < def.count, "state monitor record index out of range");
+          if (r >= lo && r < lo + n) rec.push_back(uint32_t(r - lo));
+        }
+        pd.mon_nrec = rec.size();
+        if (!rec.empty()) pd.mon_records = upload(rec.data(), rec.size() * 4);
         uint64_t window = std::min<uint64_t>(def.monitor.window_steps, def.steps);
         pd.mon_ticks = window;
         pd.mon_first_tick = pd.end_tick - window;
@@ -376,7 +426,7 @@ struct Engine::Impl {
           for (const auto& s : def.parameters) if (s.name == name) { d = s.dtype; found = true; }
           check(found, "monitor symbol missing from population");
           pd.mon_dtypes.push_back(d);
-          pd.mon_samples.push_back(alloc(window * rec.size() * b2ir::dtype_bytes(d)));
+          pd.mon_samples.push_back(alloc(window * pd.mon_nrec * b2ir::dtype_bytes(d)));
         }
       }
       if (inst.spike_generator) {
@@ -414,11 +464,24 @@ struct Engine::Impl {
       std::map<std::string, std::vector<double>> generated_params;
       std::vector<std::vector<size_t>> delays;
       bool procedural = topo.kind != b2ir::Topology::Kind::Explicit;
+      sd.procedural = procedural;
+      // Edges this rank stores: every edge on one GPU; otherwise the edges
+      // whose target it owns, in creation order (local edge k is global edge
+      // edge_ids[k]).  Per-edge arrays are indexed by local edge.
+      std::vector<uint32_t> edge_ids;
+      const PopDev& tpop = pops[def.target_population];
       if (!procedural) {
         src_h = inst.source;
         tgt_h = inst.target;
         sd.edges = src_h.size();
+        check(tgt_h.size() == sd.edges, "explicit source and target arrays differ in length");
         for (const auto& pw : inst.pathways) delays.push_back(pw.delay_ticks);
+        if (world > 1) {
+          for (size_t e = 0; e < tgt_h.size(); ++e) {
+            const uint64_t tp = def.target_start + uint64_t(tgt_h[e]);
+            if (tp >= tpop.lo && tp < tpop.lo + tpop.count) edge_ids.push_back(uint32_t(e));
+          }
+        }
       } else {
         sd.edges = topo.edge_count;
         for (const auto& pw : inst.pathways) {
@@ -426,15 +489,18 @@ struct Engine::Impl {
           delays.push_back(pw.delay_ticks);
         }
       }
+      const bool all_edges = world == 1 || procedural;
+      sd.local_edges = all_edges ? sd.edges : edge_ids.size();
+      auto gid = [&](size_t k) -> size_t { return all_edges ? k : edge_ids[k]; };
       // synapse states
       for (const auto& sym : def.states) {
         auto it = inst.initial_state.find(sym.name);
         check(it != inst.initial_state.end() && it->second.size() == sd.edges,
               "synapse state '" + sym.name + "' has the wrong length");
         size_t w = b2ir::dtype_bytes(sym.dtype);
-        std::vector<uint8_t> bytes(sd.edges * w);
-        for (size_t i = 0; i < sd.edges; ++i) std::memcpy(&bytes[i * w], &it->second.raw[i], w);
-        sd.states.push_back({sym.dtype, upload(bytes.data(), bytes.size())});
+        std::vector<uint8_t> bytes(sd.local_edges * w);
+        for (size_t k = 0; k < sd.local_edges; ++k) std::memcpy(&bytes[k * w], &it->second.raw[gid(k)], w);
+        sd.states.push_back({sym.dtype, upload(bytes.data(), std::max<size_t>(bytes.size(), 1))});
       }
       // parameters (per-edge arrays indexed by edge id)
       for (const auto& sym : def.parameters) {
@@ -457,9 +523,10 @@ struct Engine::Impl {
           sd.param_const[sym.name] = arr.as_f64(0);
         } else {
           check(arr.size() == sd.edges, "synapse parameter '" + sym.name + "' has the wrong length");
-          std::vector<double> v(arr.size());
-          for (size_t i = 0; i < arr.size(); ++i) v[i] = arr.as_f64(i);
-          sd.param_ptr[sym.name] = upload(v.data(), v.size() * 8);
+          check(world == 1 || !procedural, "multi-GPU runs need explicit topologies for per-edge parameters");
+          std::vector<double> v(sd.local_edges);
+          for (size_t k = 0; k < sd.local_edges; ++k) v[k] = arr.as_f64(gid(k));
+          sd.param_ptr[sym.name] = upload(v.data(), std::max<size_t>(v.size(), 1) * 8);
         }
       }
       // pathways
@@ -488,19 +555,21 @@ struct Engine::Impl {
         if (!procedural) {
           const auto& idx = pd.is_pre ? src_h : tgt_h;
           const auto& other = pd.is_pre ? tgt_h : src_h;
+          const size_t L = sd.local_edges;
           std::vector<uint64_t> offs(pd.endpoint_count + 1, 0);
-          for (uint32_t i : idx) offs[i + 1]++;
+          for (size_t k = 0; k < L; ++k) offs[idx[gid(k)] + 1]++;
           for (size_t i = 0; i < pd.endpoint_count; ++i) offs[i + 1] += offs[i];
           std::vector<uint64_t> next(offs.begin(), offs.end() - 1);
-          std::vector<uint32_t> row_other(idx.size()), row_edge(idx.size());
+          std::vector<uint32_t> row_other(L), row_edge(L);
           std::vector<uint16_t> row_delay;
-          if (!pd.uniform) row_delay.resize(idx.size());
+          if (!pd.uniform) row_delay.resize(L);
           bool identity = true;
-          for (size_t e = 0; e < idx.size(); ++e) {
+          for (size_t k = 0; k < L; ++k) {
+            const size_t e = gid(k);
             uint64_t pos = next[idx[e]]++;
             row_other[pos] = other[e];
-            row_edge[pos] = uint32_t(e);
-            identity &= pos == e;
+            row_edge[pos] = uint32_t(k);
+            identity &= pos == k;
             if (!pd.uniform) {
               check(d[e] < 65535, "per-edge delay exceeds 65534 ticks");
               row_delay[pos] = uint16_t(d[e]);
@@ -521,13 +590,20 @@ struct Engine::Impl {
           } else {
             DeviceBuffer offs, rows;
             uint64_t local_edges = 0;
+            // synapse-level targets j whose population index target_start + j
+            // this rank owns
+            auto clampj = [&](uint64_t x) {
+              return x <= def.target_start ? uint64_t(0) : std::min<uint64_t>(x - def.target_start, def.target_count);
+            };
+            const uint64_t j0 = clampj(tpop.lo), j1 = clampj(tpop.lo + tpop.count);
             if (topo.kind == b2ir::Topology::Kind::FixedIndegree)
-              build_fixed_indegree_csr(def.source_count, def.target_count, topo.indegree, topo.seed, 0,
-                                       def.target_count, offs, rows, local_edges, stream);
+              build_fixed_indegree_csr(def.source_count, def.target_count, topo.indegree, topo.seed, j0, j1, offs,
+                                       rows, local_edges, stream);
             else
-              build_fixed_total_csr(def.source_count, def.target_count, topo.edge_count, topo.seed, 0,
-                                    def.target_count, offs, rows, local_edges, stream);
-            check(local_edges == sd.edges, "procedural edge count mismatch");
+              build_fixed_total_csr(def.source_count, def.target_count, topo.edge_count, topo.seed, j0, j1, offs,
+                                    rows, local_edges, stream);
+            check(world > 1 || local_edges == sd.edges, "procedural edge count mismatch");
+            if (world > 1) sd.local_edges = local_edges;
             std::vector<uint64_t> host_offs(def.source_count + 1);
             B2_CUDA(cudaMemcpy(host_offs.data(), offs.ptr, host_offs.size() * 8, cudaMemcpyDeviceToHost));
             for (size_t i = 0; i < def.source_count; ++i)
@@ -570,23 +646,141 @@ struct Engine::Impl {
 
   void StreamUse(int s, size_t delay) { streams[size_t(s)].max_delay = std::max(streams[size_t(s)].max_delay, delay); }
 
+  // Words of the exchange bitmap of a population: every rank's block padded
+  // to whole 32-neuron words, blocks in rank order.
+  uint64_t exchange_words(uint64_t count, int upto) const {
+    uint64_t w = 0;
+    for (int q = 0; q < upto; ++q) w += (part_lo(count, q + 1) - part_lo(count, q) + 31) / 32;
+    return w;
+  }
+
+  // Header at the start of every rank's shared allocation, checked by each
+  // peer in connect(): the GPU's UUID (ranks must sit on distinct GPUs: the
+  // exchange waits of one GPU are satisfied by kernels of the others only),
+  // and the rank, world size and allocation size (equal models and layouts).
+  struct ArenaHeader {
+    unsigned char uuid[16];
+    int32_t rank, world;
+    uint64_t bytes;
+    uint64_t magic;
+  };
+  static constexpr uint64_t kArenaMagic = 0x42324750555845ull;  // "B2GPUXE"
+  static constexpr size_t kArenaHeaderBytes = 256;
+  size_t arena_bytes_of(int q) const { return arena_stage_off + stage_layout(q).bytes; }
+
   void build_streams() {
+    size_t x_bytes = kArenaHeaderBytes;
     for (auto& es : streams) {
       const PopDev& pd = pops[es.pop];
+      // the ring holds the population's global spike list (every rank's)
       uint64_t want = opt.ring_capacity ? opt.ring_capacity
-                                        : uint64_t(std::max<size_t>(pd.count, 1)) * (opt.chunk_ticks + es.max_delay + 2);
+                                        : uint64_t(std::max<size_t>(pd.global_count, 1)) * (opt.chunk_ticks + es.max_delay + 2);
       es.cap = next_pow2(std::max<uint64_t>(want, 1024));
       es.mask = es.cap - 1;
       es.ring = alloc(es.cap * 4);
       es.tick_start = alloc((steps + 1) * 8);
       memset_dev(es.tick_start, 8);
-      size_t tiles = tiles_for(pd.count);
+      size_t tiles = tiles_for(pd.count), tile_n = size_t(kThreads) * npt_;
+      if (world > 1 && pd.gen_offsets < 0) {
+        // spike generators emit their (global, precomputed) list on every rank
+        es.exchanged = true;
+        es.x_words = exchange_words(pd.global_count, world);
+        es.x_tiles = std::max<uint64_t>(1, (es.x_words + kThreads - 1) / kThreads);
+        es.x_off = x_bytes;
+        x_bytes += (2 * es.x_words * 8 + 255) / 256 * 256;
+        tiles = es.x_tiles;
+        tile_n = size_t(kThreads) * 32;
+      }
       es.tile_count = alloc(tiles * 4);
-      es.stage = alloc(tiles * size_t(kThreads) * npt_ * 4);
+      es.stage = alloc(tiles * tile_n * 4);
       es.done = alloc(8);
       memset_dev(es.done, 8);
       es.starts.assign(1, 0);
     }
+    if (world > 1) {
+      arena_stage_off = x_bytes;
+      const size_t total = arena_bytes_of(rank);
+      if (!opt.dry_run) {
+        arena = DeviceBuffer(total);
+        B2_CUDA(cudaMemsetAsync(arena.ptr, 0, total, stream));  // tag 0 never matches a tick
+        cudaDeviceProp prop;
+        B2_CUDA(cudaGetDeviceProperties(&prop, device));
+        ArenaHeader h{};
+        std::memcpy(h.uuid, prop.uuid.bytes, 16);
+        h.rank = rank;
+        h.world = world;
+        h.bytes = total;
+        h.magic = kArenaMagic;
+        B2_CUDA(cudaMemcpyAsync(arena.ptr, &h, sizeof(h), cudaMemcpyHostToDevice, stream));
+        B2_CUDA(cudaStreamSynchronize(stream));
+      }
+      for (auto& es : streams) {
+        if (!es.exchanged) continue;
+        for (int q = 0; q < world; ++q) {
+          void* own = opt.dry_run ? reinterpret_cast<void*>(uintptr_t(0x100000) * (ptrs.size() + 1))
+                                  : static_cast<void*>(static_cast<char*>(arena.ptr) + es.x_off);
+          es.xptr.push_back(add_ptr(q == rank ? own : nullptr));  // peers: filled by connect()
+        }
+      }
+    }
+  }
+
+  // Result staging of rank q inside its shared allocation, relative to the
+  // staging base: per population the owned state columns, refractory arrays
+  // and owned monitor records' samples; per synapse the local edges' states;
+  // then the per-pathway event counters.  A pure function of (model, q,
+  // world), so rank 0 can read any rank's staging area.
+  struct StageLayout {
+    size_t bytes = 0, delivered = 0;
+    std::vector<uint64_t> lo, count;
+    std::vector<std::vector<size_t>> state, monitor, syn_state;
+    std::vector<size_t> lastspike, not_refractory;
+    std::vector<std::vector<size_t>> mon_positions;  // owned record positions, in record order
+    std::vector<std::vector<uint32_t>> syn_edges;    // global ids of the local edges
+  };
+  StageLayout stage_layout(int q) const {
+    StageLayout L;
+    auto take = [&L](size_t b) {
+      size_t o = L.bytes;
+      L.bytes += (b + 255) / 256 * 256;
+      return o;
+    };
+    for (size_t p = 0; p < m.populations.size(); ++p) {
+      const auto& def = m.populations[p];
+      const PopDev& pd = pops[p];
+      const uint64_t lo = part_lo(def.count, q), n = part_lo(def.count, q + 1) - lo;
+      L.lo.push_back(lo);
+      L.count.push_back(n);
+      L.state.emplace_back();
+      for (const auto& st : def.states) L.state.back().push_back(take(n * b2ir::dtype_bytes(st.dtype)));
+      L.lastspike.push_back(pd.lastspike >= 0 ? take(n * 8) : 0);
+      L.not_refractory.push_back(pd.lastspike >= 0 ? take(n) : 0);
+      L.mon_positions.emplace_back();
+      L.monitor.emplace_back();
+      if (!pd.mon_dtypes.empty()) {
+        for (size_t k = 0; k < def.monitor.record.size(); ++k)
+          if (def.monitor.record[k] >= lo && def.monitor.record[k] < lo + n) L.mon_positions.back().push_back(k);
+        for (DType d : pd.mon_dtypes)
+          L.monitor.back().push_back(take(pd.mon_ticks * L.mon_positions.back().size() * b2ir::dtype_bytes(d)));
+      }
+    }
+    for (size_t s = 0; s < m.synapses.size(); ++s) {
+      const auto& def = m.synapses[s];
+      const auto& inst = m.synapse_instances[s];
+      L.syn_edges.emplace_back();
+      L.syn_state.emplace_back();
+      if (def.states.empty()) continue;
+      const uint64_t lo = part_lo(m.populations[def.target_population].count, q);
+      const uint64_t hi = part_lo(m.populations[def.target_population].count, q + 1);
+      for (size_t e = 0; e < inst.target.size(); ++e) {
+        const uint64_t tp = def.target_start + uint64_t(inst.target[e]);
+        if (tp >= lo && tp < hi) L.syn_edges.back().push_back(uint32_t(e));
+      }
+      for (const auto& st : def.states)
+        L.syn_state.back().push_back(take(L.syn_edges.back().size() * b2ir::dtype_bytes(st.dtype)));
+    }
+    L.delivered = take(std::max<size_t>(delivered_count, 1) * 8);
+    return L;
   }
 
   // ================================================================ inputs
@@ -671,16 +865,23 @@ struct Engine::Impl {
   std::string P(int k, const char* type) const { return "((" + std::string(type) + "*)g_ptr[" + std::to_string(k) + "])"; }
 
   // Neuron-domain context: state slots sv<k>, refractory slots ls/nr.
+  // Global neuron index of local lane index `i` (the neuron's identity for
+  // the `i` variable and the RNG counter, unchanged by the partition).
+  std::string global_index(size_t p) const {
+    return pops[p].lo ? "((u64)i + " + u64lit(pops[p].lo) + ")" : "(u64)i";
+  }
+
   EmitContext neuron_ctx(size_t p) {
     EmitContext c;
     const PopDev& pd = pops[p];
     const auto& def = m.populations[p];
-    c.load = [this, p, &def](const Input& in) -> std::string {
+    const std::string gi = global_index(p);
+    c.load = [this, p, &def, gi](const Input& in) -> std::string {
       const PopDev& pd2 = pops[p];
       switch (in.kind) {
         case Input::Kind::State: return widen(def.states[in.index].dtype, "sv" + std::to_string(in.index));
         case Input::Kind::Parameter: return P(pd2.param_ptr.at(def.parameters[in.index].name), "const double") + "[i]";
-        case Input::Kind::Index: return "((double)i)";
+        case Input::Kind::Index: return pd2.lo ? "((double)" + gi + ")" : "((double)i)";
         case Input::Kind::LastSpike: return "ls";
         case Input::Kind::Available: return "(nr ? 1.0 : 0.0)";
         default: throw Error("input kind not available in a neuron program");
@@ -690,10 +891,7 @@ struct Engine::Impl {
     c.seed = u64lit(m.rng_seed);
     c.tick = "tick";
     c.time = "t";
-    c.index_for_domain[int(Domain::Neuron)] = "(u64)i";
-    c.index_for_domain[int(Domain::Pre)] = "(u64)i";
-    c.index_for_domain[int(Domain::Post)] = "(u64)i";
-    c.index_for_domain[int(Domain::Edge)] = "(u64)i";
+    for (auto& ix : c.index_for_domain) ix = gi;
     return c;
   }
 
@@ -775,10 +973,11 @@ struct Engine::Impl {
     std::ostringstream o;
     o << kernel_head(name, min_blocks_);
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
+    const bool exchange = es && es->exchanged;
     size_t tiles = tiles_for(pd.count);
     constexpr unsigned W = kThreads / 32;
     o << "  const u32 tile = blockIdx.x;\n";
-    if (X) {
+    if (X && !exchange) {
       o << "  __shared__ u32 s_ballot[" << npt * W << "];\n  __shared__ u32 s_off[" << npt * W + 1 << "];\n";
       o << "  __shared__ u32 s_last;\n";
       o << "  u32 fired_bits = 0;\n";
@@ -854,14 +1053,24 @@ struct Engine::Impl {
       o << "  " << P(pd.not_refractory, "u8") << "[i] = nr;\n";
     }
     o << "  }\n";  // active
-    if (X) {
+    if (X && exchange) {
+      // The warp's ballot is word tile*tile_n/32 + kk*W + warp of this rank's
+      // block; lanes 0..world-1 store it, tagged with the tick, into every
+      // rank's exchange buffer (this rank's included).
+      const uint64_t local_words = (pd.count + 31) / 32;
+      o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
+      o << "  const u32 xw = tile * " << tile_n / 32 << "u + kk * " << W << "u + warp;\n";
+      o << "  if (lane < " << world << "u && xw < " << local_words << "u)\n";
+      o << "    b2_ll_store(((u64*)g_ptr[" << es->xptr[0] << " + lane]) + (rel & 1ull) * " << es->x_words << "ull + "
+        << exchange_words(pd.global_count, rank) << "ull + xw, b, (u32)(rel + 1ull));\n";
+    } else if (X) {
       o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
       o << "  if (lane == 0) s_ballot[kk * " << W << "u + warp] = b;\n";
       o << "  fired_bits |= (fired ? 1u : 0u) << kk;\n";
     }
     o << "  }\n";  // kk loop
     if (flush) o << "  if (blockIdx.x == 0 && threadIdx.x == 0) " << P(deferred_flags, "u64") << "[" << p << "] = tick;\n";
-    if (X) {
+    if (X && !exchange) {
       // Tile-local ascending compaction into the staging area, then the
       // last block to finish lays all tiles out (b2_finalize_spikes).
       o << "  __syncthreads();\n";
@@ -893,6 +1102,49 @@ struct Engine::Impl {
     return o.str();
   }
 
+  // Multi-GPU expand: wait (bounded) for every rank's tagged words of this
+  // tick, then compact the global bitmap into the tick's ascending global
+  // spike list with the same tile staging + last-block layout as the step
+  // kernel.  Word w belongs to rank q's block when
+  // exchange_words(N, q) <= w < exchange_words(N, q + 1).
+  std::string gen_exchange(const std::string& name, int stream_id) {
+    const EventStreamDev& es = streams[size_t(stream_id)];
+    const PopDev& pd = pops[es.pop];
+    const uint64_t timeout_ns = uint64_t(opt.exchange_timeout_ms) * 1000000ull;
+    const unsigned tile_n = kThreads * 32;
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  __shared__ u32 s_last;\n";
+    o << "  const u32 tile = blockIdx.x;\n  const u32 w = tile * " << kThreads << "u + threadIdx.x;\n";
+    o << "  u32 bits = 0, id0 = 0;\n";
+    // once the run has failed (e.g. an earlier wait expired) later ticks
+    // must not wait again: their results are discarded anyway
+    o << "  const bool poisoned = *(volatile const u32*)&ctl->error != 0u;\n";
+    o << "  if (w < " << es.x_words << "u && !poisoned) {\n";
+    o << "    bits = b2_ll_wait(((const u64*)g_ptr[" << es.xptr[size_t(rank)] << "]) + (rel & 1ull) * " << es.x_words
+      << "ull + w, (u32)(rel + 1ull), " << timeout_ns << "ull, err);\n";
+    for (int q = 0; q < world; ++q) {
+      const uint64_t w0 = exchange_words(pd.global_count, q), w1 = exchange_words(pd.global_count, q + 1);
+      o << "    " << (q ? "else if" : "if") << " (w < " << w1 << "u) id0 = " << part_lo(pd.global_count, q) << "u + (w - "
+        << w0 << "u) * 32u;\n";
+    }
+    o << "  }\n";
+    o << "  u32 total;\n  u32 pos = b2_block_exclusive_scan<" << kThreads << ">(__popc(bits), &total);\n";
+    o << "  u32* stage = " << P(es.stage, "u32") << " + (u64)tile * " << tile_n << "u;\n";
+    o << "  for (u32 x = bits; x; x &= x - 1u) stage[pos++] = id0 + (u32)(__ffs(x) - 1);\n";
+    o << "  if (threadIdx.x == 0) " << P(es.tile_count, "u32") << "[tile] = total;\n";
+    o << "  __threadfence();\n  __syncthreads();\n";
+    o << "  if (threadIdx.x == 0) s_last = (atomicAdd((unsigned long long*)" << P(es.done, "u64") << ", 1ull) % "
+      << es.x_tiles << "ull) == " << es.x_tiles - 1 << "ull;\n";
+    o << "  __syncthreads();\n";
+    o << "  if (s_last) {\n    __threadfence();\n";
+    o << "    b2_finalize_spikes<" << kThreads << ">(" << es.x_tiles << "u, " << tile_n << "u, " << P(es.tile_count, "const u32")
+      << ", " << P(es.stage, "const u32") << ", " << P(es.ring, "u32") << ", " << u64lit(es.mask) << ", "
+      << P(es.tick_start, "u64") << ", rel, " << u64lit(es.cap) << ", ctl->ring_floor, err);\n  }\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
   // Reset over the tick's fired list (one thread per spike).
   std::string gen_reset(const std::string& name, size_t p, const Program& R, int stream_id) {
     const auto& def = m.populations[p];
@@ -904,7 +1156,13 @@ struct Engine::Impl {
     o << kernel_head(name);
     o << "  const u64* ts = " << P(es.tick_start, "u64") << ";\n  const u64 a = ts[rel], b = ts[rel + 1];\n";
     o << "  for (u64 j = a + blockIdx.x * (u64)blockDim.x + threadIdx.x; j < b; j += (u64)gridDim.x * blockDim.x) {\n";
-    o << "    const u32 i = " << P(es.ring, "const u32") << "[j & " << u64lit(es.mask) << "];\n";
+    if (world > 1) {
+      o << "    const u32 sid = " << P(es.ring, "const u32") << "[j & " << u64lit(es.mask) << "];\n";
+      o << "    if (sid < " << pops[p].lo << "u || sid >= " << pops[p].lo + pops[p].count << "u) continue;\n";
+      o << "    const u32 i = sid - " << pops[p].lo << "u;\n";
+    } else {
+      o << "    const u32 i = " << P(es.ring, "const u32") << "[j & " << u64lit(es.mask) << "];\n";
+    }
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "    " << ct << " sv" << s << " = " << P(pops[p].states[s].ptr, ct) << "[i];\n";
@@ -924,7 +1182,7 @@ struct Engine::Impl {
   std::string gen_state_monitor(const std::string& name, size_t p) {
     const auto& def = m.populations[p];
     const PopDev& pd = pops[p];
-    size_t nrec = def.monitor.record.size(), nvar = def.monitor.variables.size();
+    size_t nrec = pd.mon_nrec, nvar = def.monitor.variables.size();
     std::ostringstream o;
     o << kernel_head(name);
     o << "  if (tick < " << u64lit(pd.mon_first_tick) << ") return;\n";
@@ -980,6 +1238,13 @@ struct Engine::Impl {
   }
 
   // ---------------------------------------------------------------- pathways
+  // Offset from a synapse-level target index j to the target's local state
+  // index: target_start + j - (first neuron this rank owns), modulo 2^64 (the
+  // true value is never negative for a stored edge).
+  uint64_t target_bias(const b2ir::SynapseDef& def) const {
+    return uint64_t(def.target_start) - pops[def.target_population].lo;
+  }
+
   EmitContext event_ctx(size_t s, const PathwayDev& pw) {
     EmitContext c;
     const auto& def = m.synapses[s];
@@ -1030,7 +1295,7 @@ struct Engine::Impl {
     o << "__device__ __forceinline__ void " << fname
       << "(u32 src, u32 tgt, u64 edge, u64 tick, double t, u32& err) {\n";
     o << "  const u64 src_state = (u64)src + " << def.source_start << "ull;\n";
-    o << "  const u64 tgt_state = (u64)tgt + " << def.target_start << "ull;\n";
+    o << "  const u64 tgt_state = (u64)tgt + " << target_bias(def) << "ull;\n";
     o << "  (void)src_state; (void)tgt_state; (void)t; (void)tick;\n";
     o << emit_program(pr, event_ctx(s, pw), "e_");
     const auto& src = m.populations[def.source_population];
@@ -1185,7 +1450,7 @@ struct Engine::Impl {
       o << "      const u64 q0 = r0 + c * " << kRowChunk << "ull;\n";
       o << "      const u64 q1 = q0 + " << kRowChunk << "ull < r1 ? q0 + " << kRowChunk << "ull : r1;\n";
       o << "#pragma unroll 4\n      for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
-      o << "        const u64 tgt_state = (u64)__ldg(other + q) + " << def.target_start << "ull;\n";
+      o << "        const u64 tgt_state = (u64)__ldg(other + q) + " << target_bias(def) << "ull;\n";
       for (const auto& ad : pw.atomic_adds) {
         DType d = tgt.states[ad.state].dtype;
         int ptr = pops[def.target_population].states[ad.state].ptr;
@@ -1280,7 +1545,7 @@ struct Engine::Impl {
     o << "#pragma unroll 4\n    for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
     if (pw.mode == PathwayDev::Mode::Atomic) {
       const auto& tgt = m.populations[def.target_population];
-      o << "      const u64 tgt_state = (u64)__ldg(other + q) + " << def.target_start << "ull;\n";
+      o << "      const u64 tgt_state = (u64)__ldg(other + q) + " << target_bias(def) << "ull;\n";
       for (const auto& a : pw.atomic_adds) {
         DType d = tgt.states[a.state].dtype;
         int ptr = pops[def.target_population].states[a.state].ptr;
@@ -1398,7 +1663,7 @@ struct Engine::Impl {
             if (pops[p].mon_records < 0) break;
             OpSpec o;
             o.base = def.name + "_statemon";
-            size_t n = def.monitor.record.size() * def.monitor.variables.size();
+            size_t n = pops[p].mon_nrec * def.monitor.variables.size();
             o.grid = unsigned((n + kThreads - 1) / kThreads);
             o.index = p;
             o.text = "statemon";
@@ -1475,10 +1740,18 @@ struct Engine::Impl {
               o.kind = OpSpec::Kind::Step;
               o.base = def.name + (st.X ? "_step" : "_update");
               o.index = steps_.size();
-              o.grid = unsigned(tiles_for(def.count));
+              o.grid = unsigned(tiles_for(pops[p].count));
               if (st.U) step_of_pop[p] = steps_.size();
               steps_.push_back(st);
               specs.push_back(o);
+              if (st.X && streams[size_t(pops[p].stream_of_event[st.x_event])].exchanged) {
+                OpSpec x;
+                x.base = def.name + "_exchange";
+                x.text = "exchange";
+                x.index = size_t(pops[p].stream_of_event[st.x_event]);
+                x.grid = unsigned(streams[x.index].x_tiles);
+                specs.push_back(x);
+              }
             } else if (code.kind == "reset") {
               OpSpec o;
               o.base = def.name + "_reset";
@@ -1513,7 +1786,7 @@ struct Engine::Impl {
                 o.kind = OpSpec::Kind::Step;
                 o.base = def.name + "_" + code.kind;
                 o.index = steps_.size();
-                o.grid = unsigned(tiles_for(def.count));
+                o.grid = unsigned(tiles_for(pops[p].count));
                 steps_.push_back(st);
                 specs.push_back(o);
               }
@@ -1538,6 +1811,16 @@ struct Engine::Impl {
         auto inputs = synapse_inputs(s, pw.is_pre, writable);
         programs.push_back(Program::compile(code, inputs, writable, m.functions));
         const Program& pr = programs.back();
+        if (world > 1) {
+          for (const auto& b : pr.bindings)
+            check(b.second.kind != Input::Kind::PreState &&
+                      !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre),
+                  "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
+          for (const auto& w : pr.writes)
+            check(w.first.kind != WriteTarget::Kind::PreNeuron,
+                  "multi-GPU runs cannot write presynaptic state across GPUs ('" + code.name + "')");
+          check(!pr.uses_rng(), "multi-GPU runs do not support random draws in synaptic code ('" + code.name + "')");
+        }
         classify_pathway(pw, pr);
         // Constant-addend pathways reading one spike stream at one delay and
         // writing disjoint target variables share a scatter launch.
@@ -1601,6 +1884,7 @@ struct Engine::Impl {
         case OpSpec::Kind::Text:
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
+          else if (o.text == "exchange") kernels << gen_exchange(nm, int(o.index));
           else {
             std::string t = o.text;
             t.replace(t.find("@NAME@"), 6, nm);
@@ -1633,7 +1917,7 @@ struct Engine::Impl {
       size_t p = flushes[f].first;
       std::string nm = "b2_flush_" + std::to_string(f) + "_" + sanitize(m.populations[p].name);
       kernels << gen_pop_step(nm, p, flushes[f].second, nullptr, 0, false, nullptr, {}, true);
-      flush_ops.push_back({nm, nullptr, unsigned(tiles_for(m.populations[p].count)), kThreads});
+      flush_ops.push_back({nm, nullptr, unsigned(tiles_for(pops[p].count)), kThreads});
     }
     src << bodies.str() << "\n" << kernels.str();
     source = src.str();
@@ -1676,6 +1960,7 @@ struct Engine::Impl {
     size_t table_bytes = 0;
     B2_CUDA(cudaLibraryGetGlobal(&table, &table_bytes, module, "g_ptr"));
     check(table_bytes >= ptrs.size() * 8, "pointer table size mismatch");
+    gptr_table = table;
     B2_CUDA(cudaStreamSynchronize(stream));
     if (!ptrs.empty()) B2_CUDA(cudaMemcpy(table, ptrs.data(), ptrs.size() * 8, cudaMemcpyHostToDevice));
     for (auto& op : ops) B2_CUDA(cudaLibraryGetKernel(&op.fn, module, op.name.c_str()));
@@ -1748,6 +2033,7 @@ struct Engine::Impl {
   // Per-kernel timing: direct launches bracketed by events (no graph).
   std::vector<KernelTime> profile(uint64_t ticks) {
     check(!opt.dry_run && !failed, "profiling needs a live engine");
+    check(world == 1 || connected, "a multi-GPU engine must connect() to its peers before stepping");
     std::vector<KernelTime> out(ops.size());
     for (size_t i = 0; i < ops.size(); ++i) out[i].name = ops[i].name;
     std::vector<cudaEvent_t> evs(ops.size() + 1);
@@ -1801,6 +2087,7 @@ struct Engine::Impl {
     check(!opt.dry_run, "a dry-run engine cannot step");
     check(!failed, "execution failed; create a new executor");
     check(max_ticks > 0, "step requires a positive tick budget");
+    check(world == 1 || connected, "a multi-GPU engine must connect() to its peers before stepping");
     auto t0 = std::chrono::steady_clock::now();
     try {
       uint64_t remaining = std::min<uint64_t>(max_ticks, steps - cur_rel);
@@ -1866,10 +2153,114 @@ struct Engine::Impl {
     return out;
   }
 
+  // ---------------------------------------------------------------- multi-GPU
+  std::vector<uint8_t> ipc_handle() const {
+    check(world > 1 && !opt.dry_run, "IPC handles exist for live multi-GPU engines only");
+    cudaIpcMemHandle_t h;
+    B2_CUDA(cudaIpcGetMemHandle(&h, arena.ptr));
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&h);
+    return std::vector<uint8_t>(b, b + sizeof(h));
+  }
+
+  void connect(const std::vector<std::vector<uint8_t>>& handles) {
+    check(world > 1, "connect() is for multi-GPU engines");
+    check(!opt.dry_run && !failed, "connect() needs a live engine");
+    check(!connected, "engine is already connected");
+    check(handles.size() == size_t(world), "connect() needs one handle per rank");
+    peer_base.assign(size_t(world), nullptr);
+    for (int q = 0; q < world; ++q) {
+      if (q == rank) continue;
+      check(handles[size_t(q)].size() == sizeof(cudaIpcMemHandle_t), "malformed IPC handle");
+      cudaIpcMemHandle_t h;
+      std::memcpy(&h, handles[size_t(q)].data(), sizeof(h));
+      B2_CUDA(cudaIpcOpenMemHandle(&peer_base[size_t(q)], h, cudaIpcMemLazyEnablePeerAccess));
+    }
+    std::vector<ArenaHeader> heads(static_cast<size_t>(world));
+    for (int q = 0; q < world; ++q) {
+      const void* src = q == rank ? arena.ptr : peer_base[size_t(q)];
+      B2_CUDA(cudaMemcpy(&heads[size_t(q)], src, sizeof(ArenaHeader), cudaMemcpyDeviceToHost));
+      const ArenaHeader& h = heads[size_t(q)];
+      check(h.magic == kArenaMagic && h.rank == q && h.world == world,
+            "IPC handle " + std::to_string(q) + " is not rank " + std::to_string(q) + " of this run");
+      check(h.bytes == arena_bytes_of(q), "rank " + std::to_string(q) + " built a different model or partition");
+      for (int r = 0; r < q; ++r)
+        check(std::memcmp(heads[size_t(r)].uuid, h.uuid, 16) != 0,
+              "ranks " + std::to_string(r) + " and " + std::to_string(q) + " share one GPU; use one GPU per rank");
+    }
+    for (auto& es : streams) {
+      if (!es.exchanged) continue;
+      for (int q = 0; q < world; ++q)
+        if (q != rank)
+          ptrs[size_t(es.xptr[size_t(q)])] = reinterpret_cast<uint64_t>(static_cast<char*>(peer_base[size_t(q)]) + es.x_off);
+    }
+    B2_CUDA(cudaMemcpy(gptr_table, ptrs.data(), ptrs.size() * 8, cudaMemcpyHostToDevice));
+    connected = true;
+  }
+
+  void publish() {
+    check(world > 1, "publish() is for multi-GPU engines");
+    check(!failed && cur_rel >= steps, "publish requires a completed execution");
+    flush_deferred();
+    const StageLayout L = stage_layout(rank);
+    char* base = static_cast<char*>(arena.ptr) + arena_stage_off;
+    auto put = [&](size_t off, int k, size_t bytes) {
+      if (bytes) B2_CUDA(cudaMemcpyAsync(base + off, dptr(k), bytes, cudaMemcpyDeviceToDevice, stream));
+    };
+    for (size_t p = 0; p < m.populations.size(); ++p) {
+      const auto& def = m.populations[p];
+      const PopDev& pd = pops[p];
+      for (size_t s = 0; s < def.states.size(); ++s)
+        put(L.state[p][s], pd.states[s].ptr, pd.count * b2ir::dtype_bytes(def.states[s].dtype));
+      if (pd.lastspike >= 0) {
+        put(L.lastspike[p], pd.lastspike, pd.count * 8);
+        put(L.not_refractory[p], pd.not_refractory, pd.count);
+      }
+      if (pd.mon_records >= 0)
+        for (size_t v = 0; v < pd.mon_samples.size(); ++v)
+          put(L.monitor[p][v], pd.mon_samples[v], pd.mon_ticks * pd.mon_nrec * b2ir::dtype_bytes(pd.mon_dtypes[v]));
+    }
+    for (size_t s = 0; s < m.synapses.size(); ++s)
+      for (size_t k = 0; k < syns[s].states.size(); ++k)
+        put(L.syn_state[s][k], syns[s].states[k].ptr, syns[s].local_edges * b2ir::dtype_bytes(m.synapses[s].states[k].dtype));
+    put(L.delivered, delivered_ptr, delivered_count * 8);
+    B2_CUDA(cudaStreamSynchronize(stream));
+    published = true;
+  }
+
+  // Every rank's staging area as host bytes (rank 0, after all ranks published).
+  std::vector<std::vector<uint8_t>> gather_stages(std::vector<StageLayout>& layouts) {
+    check(rank == 0, "rank 0 assembles the results of a multi-GPU run");
+    check(published, "every rank must publish() before rank 0 reads results");
+    std::vector<std::vector<uint8_t>> out(static_cast<size_t>(world));
+    for (int q = 0; q < world; ++q) {
+      layouts.push_back(stage_layout(q));
+      const char* src = static_cast<const char*>(q == rank ? arena.ptr : peer_base[size_t(q)]) + arena_stage_off;
+      out[size_t(q)].resize(layouts.back().bytes);
+      if (layouts.back().bytes)
+        B2_CUDA(cudaMemcpy(out[size_t(q)].data(), src, layouts.back().bytes, cudaMemcpyDeviceToHost));
+    }
+    return out;
+  }
+
   b2dump::ResultSet results() {
     check(!failed && cur_rel >= steps, "results require a completed execution");
     flush_deferred();
     B2_CUDA(cudaStreamSynchronize(stream));
+    std::vector<StageLayout> lay;
+    std::vector<std::vector<uint8_t>> stg;
+    if (world > 1) stg = gather_stages(lay);
+    // population column: local device array on one GPU, else every rank's
+    // block in rank order
+    auto pop_column = [&](size_t p, int k, size_t elem, const std::function<size_t(const StageLayout&)>& off) {
+      if (world == 1) return read_bytes(k, m.populations[p].count * elem);
+      std::vector<uint8_t> out;
+      for (int q = 0; q < world; ++q) {
+        const StageLayout& L = lay[size_t(q)];
+        const uint8_t* b = stg[size_t(q)].data() + off(L);
+        out.insert(out.end(), b, b + L.count[p] * elem);
+      }
+      return out;
+    };
     b2dump::ResultSet r;
     r.neuron_count = m.neuron_count;
     r.final_time = m.run_start + m.run_duration;
@@ -1885,8 +2276,21 @@ struct Engine::Impl {
       for (size_t v = 0; v < def.monitor.variables.size(); ++v) {
         b2dump::Column c;
         c.dtype = pd.mon_dtypes.empty() ? DType::F64 : pd.mon_dtypes[v];
-        if (pd.mon_records >= 0)
-          c.bytes = read_bytes(pd.mon_samples[v], pd.mon_ticks * def.monitor.record.size() * b2ir::dtype_bytes(c.dtype));
+        const size_t w = b2ir::dtype_bytes(c.dtype), nrec = def.monitor.record.size();
+        if (world == 1) {
+          if (pd.mon_records >= 0) c.bytes = read_bytes(pd.mon_samples[v], pd.mon_ticks * nrec * w);
+        } else if (!pd.mon_dtypes.empty()) {
+          // samples are [tick][record]; each rank holds its owned records
+          c.bytes.assign(pd.mon_ticks * nrec * w, 0);
+          for (int q = 0; q < world; ++q) {
+            const StageLayout& L = lay[size_t(q)];
+            const auto& pos = L.mon_positions[p];
+            const uint8_t* b = stg[size_t(q)].data() + L.monitor[p][v];
+            for (uint64_t row = 0; row < pd.mon_ticks; ++row)
+              for (size_t j = 0; j < pos.size(); ++j)
+                std::memcpy(&c.bytes[(row * nrec + pos[j]) * w], b + (row * pos.size() + j) * w, w);
+          }
+        }
         pr.samples.push_back(std::move(c));
       }
       uint64_t window_first = pd.end_tick - std::min<uint64_t>(def.monitor.window_steps, pd.end_tick);
@@ -1915,20 +2319,29 @@ struct Engine::Impl {
       for (size_t s = 0; s < def.states.size(); ++s) {
         b2dump::Column c;
         c.dtype = def.states[s].dtype;
-        c.bytes = read_bytes(pd.states[s].ptr, def.count * b2ir::dtype_bytes(c.dtype));
+        c.bytes = pop_column(p, pd.states[s].ptr, b2ir::dtype_bytes(c.dtype), [p, s](const StageLayout& L) { return L.state[p][s]; });
         pr.states.push_back(std::move(c));
       }
       if (pd.lastspike >= 0) {
         pr.has_refractory = true;
-        auto ls = read_bytes(pd.lastspike, def.count * 8);
+        auto ls = pop_column(p, pd.lastspike, 8, [p](const StageLayout& L) { return L.lastspike[p]; });
         pr.lastspike.resize(def.count);
         std::memcpy(pr.lastspike.data(), ls.data(), ls.size());
-        pr.not_refractory = read_bytes(pd.not_refractory, def.count);
+        pr.not_refractory = pop_column(p, pd.not_refractory, 1, [p](const StageLayout& L) { return L.not_refractory[p]; });
       }
       r.populations.push_back(std::move(pr));
     }
-    std::vector<uint64_t> delivered(std::max<size_t>(delivered_count, 1));
-    B2_CUDA(cudaMemcpy(delivered.data(), dptr(delivered_ptr), delivered.size() * 8, cudaMemcpyDeviceToHost));
+    std::vector<uint64_t> delivered(std::max<size_t>(delivered_count, 1), 0);
+    if (world == 1) {
+      B2_CUDA(cudaMemcpy(delivered.data(), dptr(delivered_ptr), delivered.size() * 8, cudaMemcpyDeviceToHost));
+    } else {
+      for (int q = 0; q < world; ++q)
+        for (size_t k = 0; k < delivered_count; ++k) {
+          uint64_t x;
+          std::memcpy(&x, stg[size_t(q)].data() + lay[size_t(q)].delivered + k * 8, 8);
+          delivered[k] += x;
+        }
+    }
     for (size_t s = 0; s < m.synapses.size(); ++s) {
       const auto& def = m.synapses[s];
       const SynDev& sd = syns[s];
@@ -1937,7 +2350,18 @@ struct Engine::Impl {
       for (size_t k = 0; k < def.states.size(); ++k) {
         b2dump::Column c;
         c.dtype = def.states[k].dtype;
-        c.bytes = read_bytes(sd.states[k].ptr, sd.edges * b2ir::dtype_bytes(c.dtype));
+        const size_t w = b2ir::dtype_bytes(c.dtype);
+        if (world == 1) {
+          c.bytes = read_bytes(sd.states[k].ptr, sd.edges * w);
+        } else {
+          // local edges back to global edge order
+          c.bytes.assign(sd.edges * w, 0);
+          for (int q = 0; q < world; ++q) {
+            const StageLayout& L = lay[size_t(q)];
+            const uint8_t* b = stg[size_t(q)].data() + L.syn_state[s][k];
+            for (size_t j = 0; j < L.syn_edges[s].size(); ++j) std::memcpy(&c.bytes[size_t(L.syn_edges[s][j]) * w], b + j * w, w);
+          }
+        }
         sr.states.push_back(std::move(c));
       }
       for (const auto& pw : sd.pathways) sr.delivered += delivered[size_t(pw.delivered_slot)];
@@ -1998,13 +2422,22 @@ void Engine::read_state(size_t population, const std::string& name, std::vector<
   const auto& def = impl_->m.populations[population];
   for (size_t s = 0; s < def.states.size(); ++s)
     if (def.states[s].name == name) {
-      out = impl_->read_bytes(impl_->pops[population].states[s].ptr, def.count * b2ir::dtype_bytes(def.states[s].dtype));
+      out = impl_->read_bytes(impl_->pops[population].states[s].ptr,
+                              impl_->pops[population].count * b2ir::dtype_bytes(def.states[s].dtype));
       return;
     }
   throw Error("unknown state '" + name + "'");
 }
 
 std::vector<KernelTime> Engine::profile(uint64_t ticks) { return impl_->profile(ticks); }
+std::vector<uint8_t> Engine::ipc_handle() const { return impl_->ipc_handle(); }
+void Engine::connect(const std::vector<std::vector<uint8_t>>& handles) { impl_->connect(handles); }
+void Engine::publish() { impl_->publish(); }
+std::pair<uint64_t, uint64_t> Engine::owned_range(size_t population) const {
+  check(population < impl_->m.populations.size(), "population index out of range");
+  const auto& pd = impl_->pops[population];
+  return {pd.lo, pd.lo + pd.count};
+}
 
 std::vector<uint32_t> Engine::spikes_at(size_t population, uint64_t tick) const {
   check(population < impl_->m.populations.size(), "population index out of range");

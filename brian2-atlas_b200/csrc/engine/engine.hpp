@@ -32,8 +32,13 @@ struct Options {
   int device = -1;              // -1: current device
   uint32_t chunk_ticks = 128;   // ticks per CUDA-graph replay
   uint64_t ring_capacity = 0;   // spike ring entries per event stream (0: automatic)
-  int rank = 0, world_size = 1; // target-owned partition across GPUs
-  void* nccl_comm = nullptr;    // ncclComm_t when world_size > 1
+  // Multi-GPU: this engine is rank `rank` of `world_size` processes, one per
+  // GPU, each owning a contiguous block of every population (the reference's
+  // owner rule, brian2_rust/distributed.py:80-81).  Spikes travel between
+  // GPUs inside the tick kernels; exchange waits give up after
+  // exchange_timeout_ms and poison the engine.
+  int rank = 0, world_size = 1;
+  uint32_t exchange_timeout_ms = 10000;
   bool use_graphs = true;
   bool verbose = false;
   unsigned neurons_per_thread = 0;  // 1, 2 or 4 (0: default 4)
@@ -95,6 +100,21 @@ class Engine {
   // Advance `ticks` ticks launching each kernel directly with CUDA events
   // around it on the engine stream; returns per-kernel launch counts and time.
   std::vector<KernelTime> profile(uint64_t ticks);
+
+  // ---- multi-GPU (world_size > 1)
+  // CUDA IPC handle (opaque bytes) of this rank's shared allocation: the
+  // spike-exchange buffers every peer writes into and the staging area rank 0
+  // reads results from.
+  std::vector<uint8_t> ipc_handle() const;
+  // Map every other rank's shared allocation; `handles` holds every rank's
+  // ipc_handle() in rank order.  Must precede the first step().
+  void connect(const std::vector<std::vector<uint8_t>>& handles);
+  // Copy this rank's final local results (state, monitors, event counters)
+  // into its staging area.  Every rank publishes, the ranks synchronise on
+  // the host, and then rank 0's results() merges all ranks' staging areas.
+  void publish();
+  // Global index range [lo, hi) of `population` owned by this rank.
+  std::pair<uint64_t, uint64_t> owned_range(size_t population) const;
 
   struct Impl;
 

@@ -8,11 +8,11 @@
 //   * counter RNG (splitmix64 counters), restated from the reference
 //     brian2-rust/src/executor.rs:190-336.
 //   * Brian2 timestep() (brian2-rust/src/model.rs:981-992).
-//   * block-ascending spike compaction with decoupled look-back (Merrill &
-//     Garland, "Single-pass Parallel Prefix Scan with Decoupled Look-back",
-//     NVIDIA tech report NVR-2016-002): warp ballot + popc, a shared-memory
-//     block scan, and a bounded look-back over tile status words so the spike
-//     list of a tick comes out globally ascending in one pass.
+//   * ascending spike compaction: each tile stages its fired ids (warp ballot
+//     + popc + block scan) and the last block of the launch lays the tiles
+//     out in order, so a tick's spike list is globally ascending without any
+//     block waiting on another;
+//   * the GPU-to-GPU spike exchange (tagged 8-byte peer stores, bounded waits).
 #pragma once
 
 typedef unsigned long long u64;
@@ -39,7 +39,7 @@ struct RunCtl {
   u32 error;          // OR of B2_ERR_* bits
   u32 pad0;
   u64 ring_floor;     // oldest ring position the host still needs
-  u64 tile_ticket;    // monotonically increasing compaction tile ticket
+  u64 reserved;
 };
 
 __device__ __forceinline__ double b2_bits(u64 r) { return __longlong_as_double((i64)r); }
@@ -333,124 +333,84 @@ __device__ __forceinline__ bool b2_atomic_add_f32_via_f64(float* addr, double ad
   return isfinite(next);
 }
 
-// ---------------------------------------------------------------- look-back
-__device__ __forceinline__ u64 b2_ld_acquire(const u64* p) {
-  u64 v;
-  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ void b2_st_release(u64* p, u64 v) {
-  asm volatile("st.release.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-// Tile status word: [63:40] tick tag, [39:38] flag (1 aggregate, 2 inclusive
-// prefix), [37:0] count.  The tick tag makes stale words of earlier ticks
-// invisible, so the status array never needs clearing.
-#define B2_TAG(tick) (((tick) + 1ull) & 0xffffffull)
-__device__ __forceinline__ u64 b2_status(u64 tick, u64 flag, u64 value) {
-  return (B2_TAG(tick) << 40) | (flag << 38) | (value & ((1ull << 38) - 1));
-}
-
-__device__ __forceinline__ u64 b2_warp_sum_u64(u64 v) {
+// ---------------------------------------------------------------- block scan
+// Exclusive prefix of one u32 per thread over a block of THREADS threads;
+// *total receives the block sum (every thread).
+template <int THREADS>
+__device__ __forceinline__ u32 b2_block_exclusive_scan(u32 v, u32* total) {
+  __shared__ u32 s_part[THREADS / 32 + 1];
+  const u32 lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  u32 x = v;
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  for (int d = 1; d < 32; d <<= 1) {
+    u32 y = __shfl_up_sync(0xffffffffu, x, d);
+    if (lane >= (u32)d) x += y;
+  }
+  if (lane == 31) s_part[warp] = x;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    u32 acc = 0;
+    for (int w = 0; w < THREADS / 32; ++w) {
+      u32 c = s_part[w];
+      s_part[w] = acc;
+      acc += c;
+    }
+    s_part[THREADS / 32] = acc;
+  }
+  __syncthreads();
+  *total = s_part[THREADS / 32];
+  const u32 r = s_part[warp] + x - v;
+  __syncthreads();  // s_part may be reused by the next call
+  return r;
+}
+
+// ---------------------------------------------------------------- GPU-to-GPU spike exchange
+// Every rank owns a contiguous block of each population.  A 32-neuron ballot
+// word of the threshold travels to every rank (itself included) as ONE
+// aligned 8-byte store {word, tag} into the receiver's exchange buffer, made
+// through a CUDA IPC mapping over NVLink.  An aligned 8-byte store is
+// single-copy atomic, so a receiver that reads the tag of the current tick
+// also reads that tick's word: no fence and no separate ready flag are needed
+// (the "low-latency" protocol of NVIDIA's collective library).  The buffer has
+// two halves used on alternate ticks; a rank cannot run two ticks ahead of a
+// peer, because its own tick t+1 needs the peer's words of tick t+1, which the
+// peer only writes after it has consumed tick t.
+__device__ __forceinline__ void b2_ll_store(u64* p, u32 word, u32 tag) {
+  const u64 v = ((u64)tag << 32) | (u64)word;
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ u64 b2_ll_load(const u64* p) {
+  u64 v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
 }
-
-// Decoupled look-back run by one full warp: publishes this tile's aggregate,
-// then inspects 32 predecessors per step (nearest first) until it meets an
-// inclusive prefix, and publishes its own.  Returns the exclusive prefix in
-// every lane.  Every predecessor took its ticket earlier, so it is running and
-// publishes its aggregate before it looks back itself; waits are bounded and
-// raise B2_ERR_LOOKBACK instead of hanging.
-__device__ u64 b2_lookback(u64 tick, u32 tile, u64* status, u64 aggregate, u32& err) {
-  const u32 lane = threadIdx.x & 31;
-  if (tile == 0) {
-    if (lane == 0) b2_st_release(&status[0], b2_status(tick, 2, aggregate));
-    return 0;
+__device__ __forceinline__ u64 b2_globaltimer() {
+  u64 t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Word of the current tick at p.  The wait is bounded twice: by the global
+// timer (timeout_ns) and by an iteration count; on expiry it records
+// B2_ERR_EXCHANGE and returns 0, so the kernel ends and the host sees the error.
+__device__ __forceinline__ u32 b2_ll_wait(const u64* p, u32 tag, u64 timeout_ns, u32& err) {
+  u64 v = b2_ll_load(p);
+  if ((u32)(v >> 32) == tag) return (u32)v;
+  const u64 t0 = b2_globaltimer();
+  for (u64 it = 0; it < (1ull << 28); ++it) {
+    __nanosleep(64);
+    v = b2_ll_load(p);
+    if ((u32)(v >> 32) == tag) return (u32)v;
+    if ((it & 15) == 0 && b2_globaltimer() - t0 > timeout_ns) break;
   }
-  if (lane == 0) b2_st_release(&status[tile], b2_status(tick, 1, aggregate));
-  const u64 tag = B2_TAG(tick);
-  u64 running = 0;
-  i64 end = (i64)tile - 1;
-  u32 spins = 0;
-  while (true) {
-    const i64 idx = end - (i64)lane;
-    u32 flag = 2;
-    u64 val = 0;
-    if (idx >= 0) {
-      const u64 s = b2_ld_acquire(&status[idx]);
-      flag = ((s >> 40) == tag) ? (u32)((s >> 38) & 3ull) : 0u;
-      val = s & ((1ull << 38) - 1);
-    }
-    if (__ballot_sync(0xffffffffu, flag == 0)) {
-      if (++spins > (1u << 22)) {
-        err |= B2_ERR_LOOKBACK;
-        running = 0;
-        break;
-      }
-      if (spins > 16) __nanosleep(32);
-      continue;
-    }
-    const u32 prefix_lanes = __ballot_sync(0xffffffffu, flag == 2);
-    if (prefix_lanes) {
-      const u32 first = __ffs(prefix_lanes) - 1;
-      running += b2_warp_sum_u64(lane <= first ? val : 0ull);
-      break;
-    }
-    running += b2_warp_sum_u64(val);
-    end -= 32;
-  }
-  if (lane == 0) b2_st_release(&status[tile], b2_status(tick, 2, running + aggregate));
-  return running;
+  err |= B2_ERR_EXCHANGE;
+  return 0u;
 }
 
-// Spin until a tick-tagged status word is published; returns its 38-bit
-// value (0 and an error bit after the bounded wait).
-__device__ __forceinline__ u64 b2_wait_word(const u64* p, u64 tag, u32& err) {
-  u32 spins = 0;
-  while (true) {
-    const u64 s = b2_ld_acquire(p);
-    if ((s >> 40) == tag) return s & ((1ull << 38) - 1);
-    if (++spins > (1u << 22)) {
-      err |= B2_ERR_LOOKBACK;
-      return 0;
-    }
-    if (spins > 8) __nanosleep(32);
-  }
-}
-
-// Exclusive prefix of this tile's count among all tiles of the tick, run by
-// one full warp, in one pass and without prefix chains (a two-level
-// reduce-then-scan): every tile publishes its count; the last tile of each
-// group of 32 waits for its 31 group predecessors and publishes the group
-// sum; a tile then adds the group sums of earlier groups and the counts of its
-// own group's earlier tiles.  Each wait targets a tile with an earlier ticket
-// (already running), so it ends; waits are bounded anyway.
-__device__ u64 b2_tile_prefix(u64 tick, u32 tile, u32 tiles, u64* tile_status, u64* group_status, u64 count,
-                              u32& err) {
-  const u32 lane = threadIdx.x & 31;
-  const u64 tag = B2_TAG(tick);
-  if (lane == 0) b2_st_release(&tile_status[tile], b2_status(tick, 1, count));
-  const u32 group = tile >> 5, first = group << 5;
-  u64 own = 0;
-  if (first + lane < tile) own = b2_wait_word(&tile_status[first + lane], tag, err);
-  own = b2_warp_sum_u64(own);
-  if ((tile & 31u) == 31u || tile == tiles - 1) {
-    if (lane == 0) b2_st_release(&group_status[group], b2_status(tick, 1, own + count));
-  }
-  u64 prev = 0;
-  for (u32 g = lane; g < group; g += 32) prev += b2_wait_word(&group_status[g], tag, err);
-  return b2_warp_sum_u64(prev) + own;
-}
-
-// Last-block finalisation of a tick's spike list.  Every block has written
-// its tile's ascending spikes to stage[tile * tile_n ...] and their number to
-// tile_count[tile]; the block that finishes last (observed through a
-// monotonically increasing completion counter after a __threadfence) lays the
-// tiles out in tile order: an exclusive scan of the tile counts gives each
-// tile's offset in the tick's list, which is therefore globally ascending.
-// No block ever waits for another.  Called by all threads of the last block.
+// Lay out a tick's staged spike ids: every tile staged its ascending ids at
+// stage[tile * tile_n ...] and its count at tile_count[tile]; the last block
+// of the launch (after all tiles' stores are visible) computes the tiles'
+// exclusive offsets and copies the ids into the ring in tile order, which is
+// ascending neuron order.  Writes tick_start[rel + 1].
 template <int THREADS>
 __device__ void b2_finalize_spikes(u32 tiles, u32 tile_n, const u32* tile_count, const u32* stage, u32* ring,
                                    u64 mask, u64* tick_start, u64 rel, u64 cap, u64 floor, u32& err) {
@@ -491,61 +451,4 @@ __device__ void b2_finalize_spikes(u32 tiles, u32 tile_n, const u32* tile_count,
     tick_start[rel + 1] = end;
     if (end - floor > cap) err |= B2_ERR_RING;
   }
-}
-
-// Block-level exclusive offsets of `fired` lanes and the block's global base
-// in the tick's ascending spike list.  `tile` is this block's position in
-// neuron order (taken from a ticket, so every predecessor tile has already
-// started and will publish).  Returns the block-global exclusive offset of this
-// lane; *block_total/*base are broadcast.  Waits are bounded: on timeout the
-// error bit is raised and the block continues with base 0.
-template <int THREADS>
-__device__ __forceinline__ u32 b2_compact_offsets(bool fired, u64 tick, u32 tile, u64* status,
-                                                  u32* s_warp, u64* s_base, u32& err,
-                                                  u32* block_total_out) {
-  const u32 lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  u32 ballot = __ballot_sync(0xffffffffu, fired);
-  u32 within = __popc(ballot & ((1u << lane) - 1u));
-  if (lane == 0) s_warp[warp] = __popc(ballot);
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    u32 acc = 0;
-    for (int w = 0; w < THREADS / 32; ++w) {
-      u32 c = s_warp[w];
-      s_warp[w] = acc;
-      acc += c;
-    }
-    s_warp[THREADS / 32] = acc;
-    u64 base = 0;
-    if (tile == 0) {
-      b2_st_release(&status[0], b2_status(tick, 2, acc));
-    } else {
-      b2_st_release(&status[tile], b2_status(tick, 1, acc));
-      u64 running = 0;
-      int j = (int)tile - 1;
-      u32 spins = 0;
-      const u64 tag = B2_TAG(tick);
-      while (j >= 0) {
-        u64 s = b2_ld_acquire(&status[j]);
-        if ((s >> 40) != tag || ((s >> 38) & 3ull) == 0) {
-          if (++spins > (1u << 24)) {
-            err |= B2_ERR_LOOKBACK;
-            running = 0;
-            break;
-          }
-          if (spins > 64) __nanosleep(64);
-          continue;
-        }
-        running += s & ((1ull << 38) - 1);
-        if (((s >> 38) & 3ull) == 2) break;
-        --j;
-      }
-      base = running;
-      b2_st_release(&status[tile], b2_status(tick, 2, running + acc));
-    }
-    *s_base = base;
-  }
-  __syncthreads();
-  *block_total_out = s_warp[THREADS / 32];
-  return s_warp[warp] + within;
 }

@@ -36,6 +36,16 @@ typedef struct b2g_options {
   uint32_t chunk_ticks;   /* ticks per CUDA-graph replay, 0 for the default (128) */
   uint32_t use_graphs;    /* 1: replay captured graphs (default), 0: direct launches */
   uint64_t ring_capacity; /* spike-ring entries per event stream, 0 for automatic */
+  /* Multi-GPU (one process per GPU).  Rank r of world_size owns the global
+   * indices [floor(N*r/world_size), floor(N*(r+1)/world_size)) of every
+   * population, the reference's owner rule ((i+1)*world_size-1)/N
+   * (brian2_rust/distributed.py:80-81, mpi_codegen.py:40-44), and the
+   * incoming edges of its neurons.  Callers built against an older header
+   * pass a smaller struct_size and get world_size 1. */
+  int32_t rank;                 /* 0 .. world_size-1 */
+  int32_t world_size;           /* number of GPUs/processes, 1 for a single GPU */
+  uint32_t exchange_timeout_ms; /* bound on every wait for a peer's spikes, 0 for 10000 */
+  uint32_t reserved0;
 } b2g_options;
 
 typedef struct b2g_stats {
@@ -102,8 +112,40 @@ int b2g_generated_source(const b2g_engine* engine, char* dst, size_t capacity, s
 /* Build the plan of a model and compile its generated kernels for sm_100a
  * without a GPU; copies the generated source to dst (NULL queries *needed).
  * Same validation and capability errors as b2g_create. */
-int b2g_codegen(const char* json, size_t json_len, char* dst, size_t capacity, size_t* needed, char* error,
+int b2g_codegen(const char* json, size_t json_len, const b2g_options* options, char* dst, size_t capacity,
+                size_t* needed, char* error, size_t error_capacity);
+
+/* ---- multi-GPU ------------------------------------------------------------
+ * Replaces the reference's MPI exchange (brian2_rust/mpi_runtime/bridge.c:
+ * 74-101: MPI_Allgather of counts + MPI_Allgatherv of global spike ids every
+ * tick, rank 0 writing the results).  Here each engine's tick kernels store
+ * their spike words straight into every peer GPU's memory over NVLink, so the
+ * host only takes part once, to trade IPC handles:
+ *   1. every rank: b2g_create with rank/world_size, then b2g_ipc_handle;
+ *   2. the caller all-gathers the handles (any host transport: MPI, a
+ *      torch.distributed store, ...) and every rank calls b2g_connect;
+ *   3. b2g_step as usual (all ranks the same tick budgets);
+ *   4. every rank: b2g_publish_results; the caller synchronises the ranks;
+ *      rank 0: b2g_write_results (merged, identical to a one-GPU run).
+ * b2g_read_state returns the rank's own block; b2g_spikes returns the global
+ * list (every rank holds it); b2g_get_stats counts this rank's deliveries. */
+
+/* Global index range [*lo, *hi) that `rank` of `world_size` owns in a
+ * population of `count` neurons (pure function, no engine needed). */
+void b2g_partition(uint64_t count, int32_t rank, int32_t world_size, uint64_t* lo, uint64_t* hi);
+
+/* Opaque CUDA IPC handle of this engine's shared allocation (*length bytes,
+ * at most 64). */
+int b2g_ipc_handle(b2g_engine* engine, void* handle, size_t capacity, size_t* length, char* error,
+                   size_t error_capacity);
+
+/* Map the peers' allocations: `handles` is every rank's handle in rank order,
+ * `count` = world_size handles of `handle_length` bytes each. */
+int b2g_connect(b2g_engine* engine, const void* handles, size_t handle_length, size_t count, char* error,
                 size_t error_capacity);
+
+/* Stage this rank's final local results for rank 0 (after the last step). */
+int b2g_publish_results(b2g_engine* engine, char* error, size_t error_capacity);
 
 void b2g_destroy(b2g_engine* engine);
 

@@ -1,0 +1,177 @@
+"""Multi-GPU partition and spike exchange.
+
+CPU (no GPU): the owner rule against the reference's formula
+(brian2_rust/distributed.py:80-81), the per-rank plans, capability errors,
+and the host-side handshake over two gloo ranks.
+GPU (>= 2 GPUs): torchrun ranks against the oracle, byte for byte, as the
+reference's MPI equivalence tests demand of 1/2/3/4 ranks
+(brian2-rust/tests/test_mpi.py:265-734); and a rank that stops stepping makes
+its peer's bounded exchange wait expire with an error instead of a hang.
+"""
+from __future__ import annotations
+
+import json
+import os
+import re
+import socket
+import subprocess
+import sys
+
+import pytest
+
+from conftest import GOLDEN, MODELS, ROOT, model_file, run_oracle
+
+
+def owner(i, n, g):
+    return ((i + 1) * g - 1) // n
+
+
+@pytest.mark.parametrize("n,g", [(1, 1), (10, 3), (4000, 3), (100, 8), (1000003, 8), (7, 8)])
+def test_partition_is_the_reference_owner_rule(pkg, n, g):
+    covered = 0
+    for r in range(g):
+        lo, hi = pkg.partition(n, r, g)
+        assert lo == covered
+        for i in {lo, hi - 1} if hi > lo else set():
+            assert owner(i, n, g) == r
+        covered = hi
+    assert covered == n
+
+
+def kernels(src):
+    return re.findall(r"__global__ void __launch_bounds__\(\d+(?:, \d+)?\) (\w+)", src)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_rank_plans(pkg, world):
+    data = (MODELS / "cuba_small.json").read_bytes()
+    n = json.loads(data)["definition"]["populations"][0]["count"]
+    for r in range(world):
+        src = pkg.codegen(data, rank=r, world_size=world)
+        names = kernels(src)
+        # the step publishes fired words; the exchange kernel expands them
+        assert [k.split("_", 2)[2] for k in names] == ["neurons_statemon", "neurons_step", "neurons_exchange",
+                                                      "exc_pre_inh_pre_atomic"] or r > 0
+        assert any(k.endswith("_exchange") for k in names)
+        lo, hi = pkg.partition(n, r, world)
+        step = src[src.index("neurons_step("):src.index("neurons_exchange(")]
+        assert f"i < {hi - lo}u" in step and "b2_ll_store" in step
+        assert "b2_ll_wait" in src[src.index("neurons_exchange("):]
+
+
+def test_multi_gpu_capability_errors(pkg, tmp_path):
+    with pytest.raises(pkg.B2GpuError, match="on_pre pathways only"):
+        pkg.codegen(model_file("stdp_small", tmp_path).read_bytes(), rank=0, world_size=2)
+
+
+def _gloo_rank(rank, world, port, q):
+    import importlib
+    from datetime import timedelta
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=60))
+    sys.path.insert(0, str(ROOT))
+    distributed = importlib.import_module("brian2-atlas_b200.distributed")
+
+    class FakeEngine:  # stands in for a live engine: records what connect() receives
+        world_size = world
+        got = None
+
+        def ipc_handle(self):
+            return bytes([rank]) * 64
+
+        def connect(self, handles):
+            FakeEngine.got = handles
+
+    eng = FakeEngine()
+    distributed.connect(eng)
+    q.put((rank, [h[0] for h in FakeEngine.got], [len(h) for h in FakeEngine.got]))
+    dist.destroy_process_group()
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def test_handle_exchange_over_gloo():
+    """Two gloo ranks trade handles; each receives every rank's, in rank order."""
+    import multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_gloo_rank, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(60)
+        assert p.exitcode == 0
+    assert got == [(0, [0, 1], [64, 64]), (1, [0, 1], [64, 64])]
+
+
+# ---------------------------------------------------------------- GPU
+def gpu_count():
+    try:
+        import torch
+        return torch.cuda.device_count()
+    except Exception:
+        return 0
+
+
+def torchrun(world, args, timeout=600):
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes", "1", "--nproc-per-node", str(world),
+           "--master-addr", "127.0.0.1", "--master-port", str(free_port()), str(ROOT / "tests" / "mgpu_worker.py"),
+           *map(str, args)]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    proc = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
+    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    return [json.loads(line) for line in proc.stdout.splitlines() if line.startswith("{")]
+
+
+def assert_same_files(a, b):
+    assert (a / "results.bin").read_bytes() == (b / "results.bin").read_bytes()
+    ea, eb = a / "events.bin", b / "events.bin"
+    assert ea.exists() == eb.exists()
+    if ea.exists():
+        assert ea.read_bytes() == eb.read_bytes()
+    sa = json.loads((a / "summary.json").read_text())
+    sb = json.loads((b / "summary.json").read_text())
+    assert sa["synaptic_events"] == sb["synaptic_events"] and sa["spike_count"] == sb["spike_count"]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [2, 3, 4])
+def test_ranks_match_oracle(pkg, oracle, tmp_path, world):
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import importlib
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    template = json.loads((MODELS / "cuba_poisson_small.json").read_text())
+    c2 = tmp_path / "c2_20k.json"
+    c2.write_bytes(synthetic.encode(synthetic.cuba_fixed_indegree(template, n=20000, indegree=1000, ticks=300,
+                                                                  seed=9)))
+    models = [model_file(n, tmp_path) for n in ["cuba_small", "cuba_poisson_small", "brunel_small"]]
+    models += [GOLDEN / "reference-v1" / "model.json", c2]
+    args = []
+    for k, m in enumerate(models):
+        args += [m, tmp_path / f"gpu{k}"]
+    lines = torchrun(world, ["run", *args])
+    assert len(lines) == len(models)
+    for k, m in enumerate(models):
+        run_oracle(oracle, m, tmp_path / f"ref{k}")
+        assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}")
+        # every rank delivered to its own targets only
+        total = json.loads((tmp_path / f"ref{k}" / "summary.json").read_text())["synaptic_events"]
+        assert sum(lines[k]["events_per_rank"]) == total
+
+
+@pytest.mark.gpu
+def test_stalled_rank_expires_the_exchange_wait(tmp_path):
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    lines = torchrun(2, ["stall", MODELS / "cuba_small.json", 50], timeout=300)
+    outcome = lines[-1]["outcome"]
+    assert "spike exchange with a peer GPU timed out" in outcome
+    assert "then: execution failed" in outcome

@@ -74,6 +74,9 @@ def library() -> ctypes.CDLL:
                                      c.c_size_t]),
         "b2g_connect": (c.c_int, [c.c_void_p, c.c_void_p, c.c_size_t, c.c_size_t, c.c_char_p, c.c_size_t]),
         "b2g_publish_results": (c.c_int, [c.c_void_p, c.c_char_p, c.c_size_t]),
+        "b2g_spikes_scratch_bytes": (c.c_size_t, [c.c_uint64]),
+        "b2g_spikes_from_bitmap": (c.c_int, [c.c_void_p, c.c_uint64, c.c_void_p, c.c_void_p, c.c_void_p, c.c_size_t,
+                                             c.c_void_p, c.c_char_p, c.c_size_t]),
         "b2g_profile": (c.c_int, [c.c_void_p, c.c_uint64, c.POINTER(KernelTime), c.c_size_t,
                                   c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
         "b2g_destroy": (None, [c.c_void_p]),
@@ -130,6 +133,23 @@ def partition(count: int, rank: int, world_size: int) -> tuple:
     lo, hi = ctypes.c_uint64(0), ctypes.c_uint64(0)
     library().b2g_partition(count, rank, world_size, ctypes.byref(lo), ctypes.byref(hi))
     return lo.value, hi.value
+
+
+def spikes_from_bitmap(d_words: int, nbits: int, d_ids: int, d_count: int, d_scratch: int, scratch_bytes: int,
+                       stream: int = 0) -> None:
+    """Device primitive (pointers are device addresses, e.g. tensor.data_ptr()):
+    ascending indices of the set bits among the first `nbits` bits of the u32
+    words at d_words into d_ids, their number into the u32 at d_count;
+    asynchronous on `stream` (a cudaStream_t handle)."""
+    lib = library()
+    err = _err()
+    if lib.b2g_spikes_from_bitmap(d_words, nbits, d_ids, d_count, d_scratch, scratch_bytes, stream or None, err,
+                                  len(err)):
+        raise B2GpuError(err.value.decode())
+
+
+def spikes_scratch_bytes(nbits: int) -> int:
+    return library().b2g_spikes_scratch_bytes(nbits)
 
 
 class Engine:
@@ -256,5 +276,5 @@ def package_dir() -> Path:
     return _PKG
 
 
-__all__ = ["Engine", "B2GpuError", "run_model", "codegen", "partition", "version", "library", "runner_path",
-           "LIBRARY", "RUNNER"]
+__all__ = ["Engine", "B2GpuError", "run_model", "codegen", "partition", "spikes_from_bitmap", "spikes_scratch_bytes",
+           "version", "library", "runner_path", "LIBRARY", "RUNNER"]

@@ -36,7 +36,7 @@ HOST_SOURCES = [
     CSRC / "engine" / "engine.cpp",
     CSRC / "abi.cpp",
 ]
-CUDA_SOURCES = [CSRC / "engine" / "topology.cu"]
+CUDA_SOURCES = [CSRC / "engine" / "topology.cu", CSRC / "engine" / "spikes.cu"]
 HEADERS = sorted(CSRC.rglob("*.hpp")) + sorted(CSRC.rglob("*.cuh")) + [INCLUDE / "b2gpu.h"]
 
 

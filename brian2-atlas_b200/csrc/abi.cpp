@@ -4,6 +4,7 @@
 
 #include <sys/stat.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstddef>
 #include <cstdio>
@@ -15,6 +16,7 @@
 #include "common/dump.hpp"
 #include "common/ir.hpp"
 #include "engine/engine.hpp"
+#include "engine/spikes.hpp"
 
 struct b2g_engine {
   std::unique_ptr<b2gpu::Engine> engine;
@@ -248,6 +250,23 @@ int b2g_connect(b2g_engine* e, const void* handles, size_t handle_length, size_t
 
 int b2g_publish_results(b2g_engine* e, char* error, size_t cap) {
   return guarded(e, error, cap, [&] { e->engine->publish(); });
+}
+
+size_t b2g_spikes_scratch_bytes(uint64_t nbits) { return std::max<size_t>(16, b2gpu::bitmap_tiles(nbits) * 4); }
+
+int b2g_spikes_from_bitmap(const uint32_t* d_words, uint64_t nbits, uint32_t* d_ids, uint32_t* d_count,
+                           void* d_scratch, size_t scratch_bytes, void* stream, char* error, size_t cap) {
+  try {
+    if (!d_count || (nbits && (!d_words || !d_ids || !d_scratch))) throw b2ir::Error("null device pointer");
+    if (scratch_bytes < b2g_spikes_scratch_bytes(nbits)) throw b2ir::Error("scratch buffer too small");
+    b2gpu::bitmap_to_spikes(d_words, nbits, d_ids, d_count, static_cast<uint32_t*>(d_scratch),
+                            static_cast<cudaStream_t>(stream));
+    set_error(error, cap, "");
+    return 0;
+  } catch (const std::exception& ex) {
+    set_error(error, cap, ex.what());
+    return 1;
+  }
 }
 
 void b2g_destroy(b2g_engine* e) { delete e; }

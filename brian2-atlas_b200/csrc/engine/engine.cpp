@@ -50,7 +50,7 @@ namespace {
 constexpr unsigned kThreads = 256;
 constexpr unsigned kMaxNpt = 4;                 // neurons per thread in neuron kernels (1, 2 or 4)
 
-constexpr uint64_t kRowChunk = 256;            // CSR row entries per scatter work item
+constexpr unsigned kScatterUnroll = 4;          // default row entries per thread per scatter work item
 static_assert(kMaxNpt * (kThreads / 32) <= 32, "one warp scans the per-(kk, warp) spike counts");
 
 // Smallest double d >= 0 with (d + 1e-3*dt) / dt >= target, evaluated in
@@ -260,16 +260,43 @@ struct Engine::Impl {
     // Diagnostic: plan every schedule node as its own kernel (same work,
     // same results) to attribute time per node.
     if (const char* e = std::getenv("B2GPU_NO_FUSE")) no_fuse_ = std::atoi(e) != 0;
+    // Diagnostic: plain stream-ordered launches instead of programmatic
+    // dependent launches (same results) for A/B timing.
+    if (const char* e = std::getenv("B2GPU_PDL")) use_pdl_ = std::atoi(e) != 0;
+    // Tuning knobs (same results): wave-balanced neuron tiles, and row
+    // entries per thread in constant-addend scatters (1..8).
+    if (const char* e = std::getenv("B2GPU_BALANCE")) balance_tiles_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_SCATTER_UNROLL")) scatter_unroll_ = unsigned(std::atoi(e));
+    check(scatter_unroll_ >= 1 && scatter_unroll_ <= 8, "scatter unroll must be 1 to 8");
   }
   bool no_fuse_ = false;
+  bool use_pdl_ = true;
+  bool balance_tiles_ = true;                // tile_n_for: spread neurons over whole waves
+  unsigned scatter_unroll_ = kScatterUnroll;  // row entries per thread per scatter work item
+  uint64_t row_chunk() const { return uint64_t(kThreads) * scatter_unroll_; }
 
   unsigned npt_ = 4;         // neurons per thread in neuron kernels
   // __launch_bounds__ occupancy hint for neuron kernels (0: none).  Four
   // resident 256-thread blocks per SM (<= 64 registers) measured fastest for
   // the fused CUBA step: 25.3 us vs 28.6 us per 1M-neuron tick without it.
   unsigned min_blocks_ = 4;
+  unsigned sm_count_ = 148;   // multiprocessors of the device (dry runs: a B200's 148)
+  // Neurons per block tile of a neuron kernel: the population split as evenly
+  // as possible over whole waves of resident blocks (SMs x occupancy hint), in
+  // whole 32-neuron words, between one block of threads and kThreads * npt_.
+  // E.g. 1M neurons: 2 waves of 592 blocks of 864 neurons instead of 1.65
+  // waves of 1024; 125k neurons (one of 8 GPUs): one wave of 489 blocks of 256.
+  size_t tile_n_for(size_t count) const {
+    const size_t max_tile = size_t(kThreads) * npt_;
+    if (!balance_tiles_) return max_tile;
+    const size_t slots = size_t(sm_count_) * std::max(1u, min_blocks_);
+    const size_t waves = std::max<size_t>(1, (count + max_tile * slots - 1) / (max_tile * slots));
+    size_t t = (count + waves * slots - 1) / (waves * slots);
+    t = (t + 31) / 32 * 32;
+    return std::min(max_tile, std::max<size_t>(t, std::min<size_t>(kThreads, max_tile)));
+  }
   size_t tiles_for(size_t count) const {
-    const size_t tile = size_t(kThreads) * npt_;
+    const size_t tile = tile_n_for(count);
     return std::max<size_t>(1, (count + tile - 1) / tile);
   }
 
@@ -294,10 +321,17 @@ struct Engine::Impl {
     owned.emplace_back(std::max<size_t>(bytes, 16));
     return add_ptr(owned.back().ptr);
   }
+  // Device copy of host bytes.  Callers pad empty arrays to one element so
+  // every pointer is valid; the data of an empty std::vector may be null, in
+  // which case the padding is zero-filled instead of copied.
   int upload(const void* host, size_t bytes) {
     int k = alloc(bytes);
-    if (bytes && !opt.dry_run)
-      B2_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(ptrs[size_t(k)]), host, bytes, cudaMemcpyHostToDevice, stream));
+    if (bytes && !opt.dry_run) {
+      if (host)
+        B2_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(ptrs[size_t(k)]), host, bytes, cudaMemcpyHostToDevice, stream));
+      else
+        B2_CUDA(cudaMemsetAsync(reinterpret_cast<void*>(ptrs[size_t(k)]), 0, bytes, stream));
+    }
     return k;
   }
   void memset_dev(int k, size_t bytes) {
@@ -680,7 +714,7 @@ struct Engine::Impl {
       es.ring = alloc(es.cap * 4);
       es.tick_start = alloc((steps + 1) * 8);
       memset_dev(es.tick_start, 8);
-      size_t tiles = tiles_for(pd.count), tile_n = size_t(kThreads) * npt_;
+      size_t tiles = tiles_for(pd.count), tile_n = tile_n_for(pd.count);
       if (world > 1 && pd.gen_offsets < 0) {
         // spike generators emit their (global, precomputed) list on every rank
         es.exchanged = true;
@@ -932,10 +966,20 @@ struct Engine::Impl {
     return o.str();
   }
 
+  // Every tick kernel is launched as a programmatic dependent of the previous
+  // one: it lets its own dependent launch as soon as all its blocks are
+  // running (launch_dependents), reads the host-written tick cursor, and only
+  // then waits for its predecessor grid to complete and flush
+  // (griddepcontrol.wait) before touching any other memory.  Launch latency
+  // and block rasterisation overlap the predecessor's tail; without the
+  // launch attribute the wait returns at once.
   std::string kernel_head(const std::string& name, unsigned min_blocks = 0) {
     std::string bounds = std::to_string(kThreads) + (min_blocks ? ", " + std::to_string(min_blocks) : "");
     return "extern \"C\" __global__ void __launch_bounds__(" + bounds + ") " + name +
-           "(RunCtl* __restrict__ ctl, u32 k) {\n  u32 err = 0;\n  const u64 tick = ctl->tick_base + k;\n"
+           "(RunCtl* __restrict__ ctl, u32 k) {\n  u32 err = 0;\n"
+           "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n"
+           "  const u64 tick = ctl->tick_base + k;\n"
+           "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
            "  const u64 rel = tick - " + u64lit(start_tick) + ";\n  const double t = (double)tick * " +
            double_literal(dt) + ";\n  (void)rel; (void)t;\n";
   }
@@ -962,7 +1006,12 @@ struct Engine::Impl {
     // state read, and marks it done so the next prologue skips it.
     const auto& def = m.populations[p];
     const PopDev& pd = pops[p];
-    const unsigned npt = npt_, tile_n = kThreads * npt_;
+    const unsigned tile_n = unsigned(tile_n_for(pd.count));
+    const unsigned npt = (tile_n + kThreads - 1) / kThreads;  // neuron slots per thread
+    // condition that slot kk of this thread lies inside the tile (only needed
+    // when the tile is not a whole number of blocks of threads)
+    const std::string in_tile = tile_n % kThreads ? "kk * " + std::to_string(kThreads) + "u + threadIdx.x < " +
+                                                        std::to_string(tile_n) + "u && " : "";
     std::vector<const Program*> progs(deferred.begin(), deferred.end());
     for (const Program* pr : {U, X, R})
       if (pr) progs.push_back(pr);
@@ -997,7 +1046,7 @@ struct Engine::Impl {
     if (read_refr) o << "  double lsa[" << npt << "];\n  u8 nra[" << npt << "];\n";
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
     o << "    const u32 i = tile * " << tile_n << "u + kk * " << kThreads << "u + threadIdx.x;\n";
-    o << "    if (i < " << pd.count << "u) {\n";
+    o << "    if (" << in_tile << "i < " << pd.count << "u) {\n";
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "      sva" << s << "[kk] = " << ld(pops[p].states[s].ptr, ct) << ";\n";
@@ -1012,7 +1061,7 @@ struct Engine::Impl {
     prev_ctx.time = "t_prev";
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
     o << "  const u32 i = tile * " << tile_n << "u + kk * " << kThreads << "u + threadIdx.x;\n";
-    o << "  const bool active = i < " << pd.count << "u;\n";
+    o << "  const bool active = " << in_tile << "i < " << pd.count << "u;\n";
     o << "  bool fired = false;\n  (void)fired;\n";
     o << "  if (active) {\n";
     for (size_t s : used) o << "  " << storage_ctype(def.states[s].dtype) << " sv" << s << " = sva" << s << "[kk];\n";
@@ -1060,7 +1109,9 @@ struct Engine::Impl {
       const uint64_t local_words = (pd.count + 31) / 32;
       o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
       o << "  const u32 xw = tile * " << tile_n / 32 << "u + kk * " << W << "u + warp;\n";
-      o << "  if (lane < " << world << "u && xw < " << local_words << "u)\n";
+      std::string warp_in_tile = tile_n % kThreads ? "kk * " + std::to_string(kThreads) + "u + warp * 32u < " +
+                                                         std::to_string(tile_n) + "u && " : "";
+      o << "  if (" << warp_in_tile << "lane < " << world << "u && xw < " << local_words << "u)\n";
       o << "    b2_ll_store(((u64*)g_ptr[" << es->xptr[0] << " + lane]) + (rel & 1ull) * " << es->x_words << "ull + "
         << exchange_words(pd.global_count, rank) << "ull + xw, b, (u32)(rel + 1ull));\n";
     } else if (X) {
@@ -1414,17 +1465,56 @@ struct Engine::Impl {
   // lanes over its CSR row.
   // Constant-addend delivery for one or more pathways that read the same spike
   // stream at the same delay and write disjoint target variables.  Work item
-  // = (fired source, row chunk of kRowChunk entries); blocks stride over the
+  // = (fired source, row chunk of row_chunk() entries); blocks stride over the
   // items, threads over the chunk, so a tick's events spread over the whole
   // GPU.  f64 updates are fire-and-forget reductions (red.global.add.f64); a
   // non-finite result is caught by the next program that reads the variable
   // (every operation of every neuron program is checked).
+  // Constant-addend delivery of one row chunk [q0, q1): every thread first
+  // loads its kScatterUnroll row entries (and, for gated adds, the targets'
+  // not_refractory flags), then issues the reductions, so each thread keeps
+  // several independent loads in flight instead of one dependent chain per
+  // entry.
+  std::string emit_atomic_chunk(const PathwayDev& pw, const std::string& ind) {
+    const auto& def = m.synapses[pw.synapse];
+    const auto& tgt = m.populations[def.target_population];
+    const PopDev& tp = pops[def.target_population];
+    bool gated = false;
+    for (const auto& ad : pw.atomic_adds) gated |= ad.gated;
+    const unsigned U = scatter_unroll_;
+    std::ostringstream o;
+    o << ind << "u64 tq[" << U << "];\n" << ind << "bool tv[" << U << "];\n";
+    o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) {\n";
+    o << ind << "  const u64 q = q0 + threadIdx.x + u * " << kThreads << "ull;\n";
+    o << ind << "  tv[u] = q < q1;\n";
+    o << ind << "  tq[u] = tv[u] ? (u64)__ldg(other + q) + " << target_bias(def) << "ull : 0ull;\n" << ind << "}\n";
+    if (gated) {
+      o << ind << "u8 tg[" << U << "];\n";
+      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) tg[u] = tv[u] ? __ldg("
+        << P(tp.not_refractory, "const u8") << " + tq[u]) : (u8)0;\n";
+    }
+    o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) {\n";
+    o << ind << "  if (!tv[u]) continue;\n";
+    for (const auto& ad : pw.atomic_adds) {
+      DType d = tgt.states[ad.state].dtype;
+      int ptr = tp.states[ad.state].ptr;
+      std::string gate = ad.gated ? "if (tg[u]) " : "";
+      if (d == DType::F64)
+        o << ind << "  " << gate << "atomicAdd(" << P(ptr, "double") << " + tq[u], " << double_literal(ad.addend) << ");\n";
+      else
+        o << ind << "  " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tq[u], "
+          << double_literal(ad.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
+    }
+    o << ind << "}\n";
+    return o.str();
+  }
+
   std::string gen_atomic_kernel(const std::string& name, const std::vector<PathwayDev*>& pws) {
     const PathwayDev& p0 = *pws.front();
     const EventStreamDev& es = streams[size_t(p0.stream)];
     const size_t endpoint_count = m.populations[p0.endpoint_pop].count;
     uint64_t chunks = 1;
-    for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + kRowChunk - 1) / kRowChunk);
+    for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + row_chunk() - 1) / row_chunk());
     std::ostringstream o;
     o << kernel_head(name);
     o << "  if ((i64)rel - " << p0.delay << "ll < 0) return;\n  const u64 te = rel - " << p0.delay << "ull;\n";
@@ -1447,21 +1537,10 @@ struct Engine::Impl {
       o << "      const u32 ep = s - " << lo << "u;\n";
       o << "      const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
       o << "      if (c == 0 && threadIdx.x == 0) events" << k << " += r1 - r0;\n";
-      o << "      const u64 q0 = r0 + c * " << kRowChunk << "ull;\n";
-      o << "      const u64 q1 = q0 + " << kRowChunk << "ull < r1 ? q0 + " << kRowChunk << "ull : r1;\n";
-      o << "#pragma unroll 4\n      for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
-      o << "        const u64 tgt_state = (u64)__ldg(other + q) + " << target_bias(def) << "ull;\n";
-      for (const auto& ad : pw.atomic_adds) {
-        DType d = tgt.states[ad.state].dtype;
-        int ptr = pops[def.target_population].states[ad.state].ptr;
-        std::string gate = ad.gated ? "if (" + P(pops[def.target_population].not_refractory, "const u8") + "[tgt_state]) " : "";
-        if (d == DType::F64)
-          o << "        " << gate << "atomicAdd(" << P(ptr, "double") << " + tgt_state, " << double_literal(ad.addend) << ");\n";
-        else
-          o << "        " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tgt_state, "
-            << double_literal(ad.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
-      }
-      o << "      }\n    }\n";
+      o << "      const u64 q0 = r0 + c * " << row_chunk() << "ull;\n";
+      o << "      const u64 q1 = q0 + " << row_chunk() << "ull < r1 ? q0 + " << row_chunk() << "ull : r1;\n";
+      o << emit_atomic_chunk(pw, "      ");
+      o << "    }\n";
     }
     o << "  }\n";
     for (size_t k = 0; k < pws.size(); ++k)
@@ -1521,13 +1600,13 @@ struct Engine::Impl {
       o << kernel_tail();
       return o.str();
     }
-    // Parallel traversal.  Work item = (fired endpoint, row chunk of
-    // kRowChunk entries); blocks stride over items, threads over the chunk, so
-    // a tick's events spread across the whole GPU instead of one warp per
-    // spike.  Constant-addend updates are fire-and-forget reductions
-    // (red.global.add): their result is re-checked for finiteness by the next
-    // reader of the state (every neuron program checks every operation).
-    const uint64_t chunks = std::max<uint64_t>(1, (pw.max_row + kRowChunk - 1) / kRowChunk);
+    // Edge-parallel traversal (bodies that write only synapse state, so
+    // events commute).  Work item = (fired endpoint, row chunk of row_chunk()
+    // entries); blocks stride over items, threads over the chunk, so a tick's
+    // events spread across the whole GPU instead of one warp per spike.
+    // (Constant-addend pathways use gen_atomic_kernel.)
+    check(pw.mode == PathwayDev::Mode::EdgeParallel, "pathway kernel mode mismatch");
+    const uint64_t chunks = std::max<uint64_t>(1, (pw.max_row + row_chunk() - 1) / row_chunk());
     o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n  const u64 te = rel - " << pw.delay << "ull;\n";
     o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
     o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
@@ -1540,28 +1619,12 @@ struct Engine::Impl {
     if (!full) o << "    if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
     o << "    const u32 ep = s - " << lo << "u;\n    const u64 r0 = off[ep], r1 = off[ep + 1];\n";
     o << "    if (c == 0 && threadIdx.x == 0) events += r1 - r0;\n";
-    o << "    const u64 q0 = r0 + c * " << kRowChunk << "ull;\n    if (q0 >= r1) continue;\n";
-    o << "    const u64 q1 = q0 + " << kRowChunk << "ull < r1 ? q0 + " << kRowChunk << "ull : r1;\n";
+    o << "    const u64 q0 = r0 + c * " << row_chunk() << "ull;\n    if (q0 >= r1) continue;\n";
+    o << "    const u64 q1 = q0 + " << row_chunk() << "ull < r1 ? q0 + " << row_chunk() << "ull : r1;\n";
     o << "#pragma unroll 4\n    for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
-    if (pw.mode == PathwayDev::Mode::Atomic) {
-      const auto& tgt = m.populations[def.target_population];
-      o << "      const u64 tgt_state = (u64)__ldg(other + q) + " << target_bias(def) << "ull;\n";
-      for (const auto& a : pw.atomic_adds) {
-        DType d = tgt.states[a.state].dtype;
-        int ptr = pops[def.target_population].states[a.state].ptr;
-        std::string gate = a.gated ? "if (" + P(pops[def.target_population].not_refractory, "const u8") + "[tgt_state]) " : "";
-        if (d == DType::F64) {
-          o << "      " << gate << "atomicAdd(" << P(ptr, "double") << " + tgt_state, " << double_literal(a.addend) << ");\n";
-        } else {
-          o << "      " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tgt_state, "
-            << double_literal(a.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
-        }
-      }
-    } else {
-      o << "      const u64 e = " << edge_of_q << ";\n";
-      if (pw.is_pre) o << "      " << body_fn << "(ep, other[q], e, tick, t, err);\n";
-      else o << "      " << body_fn << "(other[q], ep, e, tick, t, err);\n";
-    }
+    o << "      const u64 e = " << edge_of_q << ";\n";
+    if (pw.is_pre) o << "      " << body_fn << "(ep, other[q], e, tick, t, err);\n";
+    else o << "      " << body_fn << "(other[q], ep, e, tick, t, err);\n";
     o << "    }\n  }\n";
     o << "  if (threadIdx.x == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
       << pw.delivered_slot << ", events);\n";
@@ -1971,9 +2034,18 @@ struct Engine::Impl {
   // ================================================================ run loop
   void launch_tick(uint32_t k) {
     void* ctl_ptr = ctl.ptr;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
     for (auto& op : ops) {
       void* args[] = {&ctl_ptr, &k};
-      B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(op.fn), dim3(op.grid), dim3(op.block), args, 0, stream));
+      cudaLaunchConfig_t cfg{};
+      cfg.gridDim = dim3(op.grid);
+      cfg.blockDim = dim3(op.block);
+      cfg.stream = stream;
+      cfg.attrs = attr;
+      cfg.numAttrs = use_pdl_ ? 1 : 0;
+      B2_CUDA(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(op.fn), args));
     }
   }
 
@@ -2377,6 +2449,9 @@ struct Engine::Impl {
       if (opt.device >= 0) B2_CUDA(cudaSetDevice(opt.device));
       B2_CUDA(cudaGetDevice(&device));
       B2_CUDA(cudaFree(nullptr));  // establish the primary context
+      int sms = 0;
+      B2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+      if (sms > 0) sm_count_ = unsigned(sms);
       B2_CUDA(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
       B2_CUDA(cudaEventCreate(&ev_start));
       B2_CUDA(cudaEventCreate(&ev_stop));

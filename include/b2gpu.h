@@ -147,6 +147,20 @@ int b2g_connect(b2g_engine* engine, const void* handles, size_t handle_length, s
 /* Stage this rank's final local results for rank 0 (after the last step). */
 int b2g_publish_results(b2g_engine* engine, char* error, size_t error_capacity);
 
+/* ---- device primitive ----------------------------------------------------
+ * The reference's ascending `fired` list (emit_threshold, executor.rs:
+ * 2949-3006) from a device bitmap with one bit per neuron (bit b of word w is
+ * neuron 32*w + b; bits at or past nbits are ignored) -- the fired-word layout
+ * of the engine's exchange between GPUs, for callers that evaluate thresholds
+ * in their own kernels.  All pointers are device pointers; d_ids needs room
+ * for the number of set bits; *d_count receives that number.  Asynchronous on
+ * `stream` (a cudaStream_t; NULL is the legacy default stream).  d_scratch:
+ * b2g_spikes_scratch_bytes(nbits) bytes of device memory, overwritten (it
+ * needs no initialisation).  No engine involved. */
+size_t b2g_spikes_scratch_bytes(uint64_t nbits);
+int b2g_spikes_from_bitmap(const uint32_t* d_words, uint64_t nbits, uint32_t* d_ids, uint32_t* d_count,
+                           void* d_scratch, size_t scratch_bytes, void* stream, char* error, size_t error_capacity);
+
 void b2g_destroy(b2g_engine* engine);
 
 const char* b2g_version(void);

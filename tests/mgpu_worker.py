@@ -28,37 +28,44 @@ def main(argv):
     distributed = importlib.import_module("brian2-atlas_b200.distributed")
     rank = dist.get_rank()
     try:
-        if argv[0] == "run":
-            for model, outdir in zip(argv[1::2], argv[2::2]):
-                stats = distributed.run_model_distributed(Path(model).read_bytes(), outdir)
-                events = [None] * dist.get_world_size()
-                dist.all_gather_object(events, stats["synaptic_events"])
-                if rank == 0:
-                    print(json.dumps({"model": model, "events_per_rank": events}), flush=True)
-        elif argv[0] == "stall":
-            model, ticks = Path(argv[1]).read_bytes(), int(argv[2])
-            outcome = "no error"
-            with distributed.create_engine(model, exchange_timeout_ms=1000) as eng:
-                eng.step(ticks)
-                if rank == 0:
-                    try:
-                        eng.step(ticks)
-                    except pkg.B2GpuError as exc:
-                        outcome = str(exc)
-                dist.barrier()  # rank 1 waits here with nothing in flight
-                # rank 0's engine is poisoned; its peers must also refuse
-                if rank == 0:
-                    try:
-                        eng.step(1)
-                    except pkg.B2GpuError as exc:
-                        outcome += " | then: " + str(exc)
-            if rank == 0:
-                print(json.dumps({"outcome": outcome}), flush=True)
-            dist.barrier()
-        else:
-            raise SystemExit(f"unknown mode {argv[0]}")
+        _run(argv, dist, pkg, distributed, rank)
+    except Exception as exc:  # surface the failing rank's message to the test
+        print(json.dumps({"error": f"rank {rank}: {type(exc).__name__}: {exc}"}), flush=True)
+        raise
     finally:
         dist.destroy_process_group()
+
+
+def _run(argv, dist, pkg, distributed, rank):
+    if argv[0] == "run":
+        for model, outdir in zip(argv[1::2], argv[2::2]):
+            stats = distributed.run_model_distributed(Path(model).read_bytes(), outdir)
+            events = [None] * dist.get_world_size()
+            dist.all_gather_object(events, stats["synaptic_events"])
+            if rank == 0:
+                print(json.dumps({"model": model, "events_per_rank": events}), flush=True)
+    elif argv[0] == "stall":
+        model, ticks = Path(argv[1]).read_bytes(), int(argv[2])
+        outcome = "no error"
+        with distributed.create_engine(model, exchange_timeout_ms=1000) as eng:
+            eng.step(ticks)
+            if rank == 0:
+                try:
+                    eng.step(ticks)
+                except pkg.B2GpuError as exc:
+                    outcome = str(exc)
+            dist.barrier()  # rank 1 waits here with nothing in flight
+            # rank 0's engine is poisoned; its peers must also refuse
+            if rank == 0:
+                try:
+                    eng.step(1)
+                except pkg.B2GpuError as exc:
+                    outcome += " | then: " + str(exc)
+        if rank == 0:
+            print(json.dumps({"outcome": outcome}), flush=True)
+        dist.barrier()
+    else:
+        raise SystemExit(f"unknown mode {argv[0]}")
 
 
 if __name__ == "__main__":

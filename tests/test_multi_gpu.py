@@ -126,7 +126,8 @@ def torchrun(world, args, timeout=600):
            *map(str, args)]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     proc = subprocess.run(cmd, capture_output=True, text=True, timeout=timeout, env=env)
-    assert proc.returncode == 0, proc.stdout[-3000:] + proc.stderr[-3000:]
+    errors = [line for line in proc.stdout.splitlines() if line.startswith('{"error"')]
+    assert proc.returncode == 0, "\n".join(errors) + "\n" + proc.stdout[-2000:] + proc.stderr[-2000:]
     return [json.loads(line) for line in proc.stdout.splitlines() if line.startswith("{")]
 
 
@@ -142,7 +143,7 @@ def assert_same_files(a, b):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("world", [2, 3, 4, 8])
 def test_ranks_match_oracle(pkg, oracle, tmp_path, world):
     if gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")

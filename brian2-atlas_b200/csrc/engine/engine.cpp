@@ -50,7 +50,7 @@ namespace {
 constexpr unsigned kThreads = 256;
 constexpr unsigned kMaxNpt = 4;                 // neurons per thread in neuron kernels (1, 2 or 4)
 
-constexpr unsigned kScatterUnroll = 4;          // default row entries per thread per scatter work item
+constexpr unsigned kScatterUnroll = 1;          // default row entries per thread per scatter work item
 static_assert(kMaxNpt * (kThreads / 32) <= 32, "one warp scans the per-(kk, warp) spike counts");
 
 // Smallest double d >= 0 with (d + 1e-3*dt) / dt >= target, evaluated in
@@ -281,17 +281,19 @@ struct Engine::Impl {
   // the fused CUBA step: 25.3 us vs 28.6 us per 1M-neuron tick without it.
   unsigned min_blocks_ = 4;
   unsigned sm_count_ = 148;   // multiprocessors of the device (dry runs: a B200's 148)
-  // Neurons per block tile of a neuron kernel: the population split as evenly
-  // as possible over whole waves of resident blocks (SMs x occupancy hint), in
-  // whole 32-neuron words, between one block of threads and kThreads * npt_.
-  // E.g. 1M neurons: 2 waves of 592 blocks of 864 neurons instead of 1.65
-  // waves of 1024; 125k neurons (one of 8 GPUs): one wave of 489 blocks of 256.
+  // Neurons per block tile of a neuron kernel.  A population that fills at
+  // least one wave of resident blocks (SMs x occupancy hint) at kThreads *
+  // npt_ neurons per block keeps that tile (measured: spreading 1M neurons
+  // over two even waves is slower than 1.65 waves of full tiles, because a
+  // block's time is set by its threads' neuron count).  A smaller one (one
+  // GPU's share of a partitioned network) is spread over all resident slots
+  // in whole 32-neuron words, at least one block of threads per tile: e.g.
+  // 125k neurons run as 489 blocks of 256 instead of 123 blocks of 1024.
   size_t tile_n_for(size_t count) const {
     const size_t max_tile = size_t(kThreads) * npt_;
-    if (!balance_tiles_) return max_tile;
     const size_t slots = size_t(sm_count_) * std::max(1u, min_blocks_);
-    const size_t waves = std::max<size_t>(1, (count + max_tile * slots - 1) / (max_tile * slots));
-    size_t t = (count + waves * slots - 1) / (waves * slots);
+    if (!balance_tiles_ || count >= max_tile * slots) return max_tile;
+    size_t t = (count + slots - 1) / slots;
     t = (t + 31) / 32 * 32;
     return std::min(max_tile, std::max<size_t>(t, std::min<size_t>(kThreads, max_tile)));
   }
@@ -2103,48 +2105,60 @@ struct Engine::Impl {
   }
 
   // Per-kernel timing: direct launches bracketed by events (no graph).
+  // Per-kernel timing: every kernel of a chunk launched directly (plain
+  // stream order, no programmatic overlap) with an event recorded after each
+  // one; the whole chunk is queued before the host waits, so the GPU runs
+  // the kernels back to back and each interval is the kernel's own time.
   std::vector<KernelTime> profile(uint64_t ticks) {
     check(!opt.dry_run && !failed, "profiling needs a live engine");
     check(world == 1 || connected, "a multi-GPU engine must connect() to its peers before stepping");
     std::vector<KernelTime> out(ops.size());
     for (size_t i = 0; i < ops.size(); ++i) out[i].name = ops[i].name;
-    std::vector<cudaEvent_t> evs(ops.size() + 1);
+    const size_t per_tick = ops.size();
+    std::vector<cudaEvent_t> evs(size_t(opt.chunk_ticks) * per_tick + 1);
     for (auto& e : evs) B2_CUDA(cudaEventCreate(&e));
     uint64_t remaining = std::min<uint64_t>(ticks, steps - cur_rel);
-    while (remaining > 0) {
-      uint32_t n = uint32_t(std::min<uint64_t>(remaining, opt.chunk_ticks));
-      tick_host_ = start_tick + cur_rel;
-      B2_CUDA(cudaMemcpyAsync(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice, stream));
-      for (uint32_t k = 0; k < n; ++k) {
-        void* ctl_ptr = ctl.ptr;
+    try {
+      while (remaining > 0) {
+        uint32_t n = uint32_t(std::min<uint64_t>(remaining, opt.chunk_ticks));
+        tick_host_ = start_tick + cur_rel;
+        B2_CUDA(cudaMemcpyAsync(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice, stream));
         B2_CUDA(cudaEventRecord(evs[0], stream));
-        for (size_t i = 0; i < ops.size(); ++i) {
-          void* args[] = {&ctl_ptr, &k};
-          B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(ops[i].fn), dim3(ops[i].grid), dim3(ops[i].block),
-                                   args, 0, stream));
-          B2_CUDA(cudaEventRecord(evs[i + 1], stream));
-        }
-        B2_CUDA(cudaEventSynchronize(evs.back()));
-        for (size_t i = 0; i < ops.size(); ++i) {
-          float ms = 0.f;
-          B2_CUDA(cudaEventElapsedTime(&ms, evs[i], evs[i + 1]));
-          out[i].total_ms += ms;
-          out[i].launches += 1;
-        }
+        void* ctl_ptr = ctl.ptr;
+        for (uint32_t k = 0; k < n; ++k)
+          for (size_t i = 0; i < per_tick; ++i) {
+            void* args[] = {&ctl_ptr, &k};
+            B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(ops[i].fn), dim3(ops[i].grid), dim3(ops[i].block),
+                                     args, 0, stream));
+            B2_CUDA(cudaEventRecord(evs[size_t(k) * per_tick + i + 1], stream));
+          }
+        B2_CUDA(cudaStreamSynchronize(stream));
+        for (uint32_t k = 0; k < n; ++k)
+          for (size_t i = 0; i < per_tick; ++i) {
+            float ms = 0.f;
+            const size_t at = size_t(k) * per_tick + i;
+            B2_CUDA(cudaEventElapsedTime(&ms, evs[at], evs[at + 1]));
+            out[i].total_ms += ms;
+            out[i].launches += 1;
+          }
+        st.kernel_launches += uint64_t(n) * per_tick;
+        check_error();
+        drain(cur_rel, cur_rel + n);
+        cur_rel += n;
+        remaining -= n;
+        update_floor(cur_rel);
+        deferred_pending = !flushes.empty();
       }
-      st.kernel_launches += uint64_t(n) * ops.size();
-      check_error();
-      drain(cur_rel, cur_rel + n);
-      cur_rel += n;
-      remaining -= n;
-      update_floor(cur_rel);
-      deferred_pending = !flushes.empty();
+    } catch (...) {
+      for (auto& e : evs) cudaEventDestroy(e);
+      throw;
     }
     for (auto& e : evs) cudaEventDestroy(e);
     if (cur_rel >= steps) flush_deferred();
     st.ticks = cur_rel;
     return out;
   }
+
 
   void check_error() {
     uint32_t err = 0;

@@ -75,6 +75,8 @@ def library() -> ctypes.CDLL:
         "b2g_connect": (c.c_int, [c.c_void_p, c.c_void_p, c.c_size_t, c.c_size_t, c.c_char_p, c.c_size_t]),
         "b2g_publish_results": (c.c_int, [c.c_void_p, c.c_char_p, c.c_size_t]),
         "b2g_spikes_scratch_bytes": (c.c_size_t, [c.c_uint64]),
+        "b2g_spikes_from_bitmap_noalloc": (c.c_int, [c.c_void_p, c.c_uint64, c.c_void_p, c.c_void_p, c.c_void_p,
+                                                     c.c_char_p, c.c_size_t]),
         "b2g_spikes_from_bitmap": (c.c_int, [c.c_void_p, c.c_uint64, c.c_void_p, c.c_void_p, c.c_void_p, c.c_size_t,
                                              c.c_void_p, c.c_char_p, c.c_size_t]),
         "b2g_profile": (c.c_int, [c.c_void_p, c.c_uint64, c.POINTER(KernelTime), c.c_size_t,
@@ -145,6 +147,19 @@ def spikes_from_bitmap(d_words: int, nbits: int, d_ids: int, d_count: int, d_scr
     err = _err()
     if lib.b2g_spikes_from_bitmap(d_words, nbits, d_ids, d_count, d_scratch, scratch_bytes, stream or None, err,
                                   len(err)):
+        raise B2GpuError(err.value.decode())
+
+
+SPIKES_NOALLOC_MAX_BITS = 1 << 27
+
+
+def spikes_from_bitmap_noalloc(d_words: int, nbits: int, d_ids: int, d_count: int, stream: int = 0) -> None:
+    """spikes_from_bitmap without device allocation (the library's fixed
+    scratch; nbits <= SPIKES_NOALLOC_MAX_BITS; overlapping calls on one GPU
+    race; the first call on a device does a one-time set-up)."""
+    lib = library()
+    err = _err()
+    if lib.b2g_spikes_from_bitmap_noalloc(d_words, nbits, d_ids, d_count, stream or None, err, len(err)):
         raise B2GpuError(err.value.decode())
 
 

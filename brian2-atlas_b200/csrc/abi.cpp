@@ -269,6 +269,20 @@ int b2g_spikes_from_bitmap(const uint32_t* d_words, uint64_t nbits, uint32_t* d_
   }
 }
 
+int b2g_spikes_from_bitmap_noalloc(const uint32_t* d_words, uint64_t nbits, uint32_t* d_ids, uint32_t* d_count,
+                                   void* stream, char* error, size_t cap) {
+  static_assert(B2G_SPIKES_NOALLOC_MAX_BITS == b2gpu::kNoAllocMaxBits, "no-alloc limit mismatch");
+  try {
+    if (!d_count || (nbits && (!d_words || !d_ids))) throw b2ir::Error("null device pointer");
+    b2gpu::bitmap_to_spikes_noalloc(d_words, nbits, d_ids, d_count, static_cast<cudaStream_t>(stream));
+    set_error(error, cap, "");
+    return 0;
+  } catch (const std::exception& ex) {
+    set_error(error, cap, ex.what());
+    return 1;
+  }
+}
+
 void b2g_destroy(b2g_engine* e) { delete e; }
 
 const char* b2g_version(void) { return "brian2-atlas-b200 0.1 (abi 1, sm_100a)"; }

@@ -16,6 +16,8 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <mutex>
+#include <string>
 
 #include "cuda_util.hpp"
 #include "spikes.hpp"
@@ -120,6 +122,49 @@ void bitmap_to_spikes(const uint32_t* d_bits, uint64_t nbits, uint32_t* d_out, u
   tile_write<<<unsigned(tiles), kThreads, 0, stream>>>(d_bits, words, last_mask, d_tile_counts, uint32_t(tiles),
                                                        d_out, d_count);
   B2_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- no-alloc variant
+// Callers that must not allocate device memory around the call -- a tick
+// loop that may not stall on an allocator, a host framework whose own caching
+// allocator holds the device's memory budget, a process that has already
+// reserved all free device memory -- get the same two launches with the
+// scratch in this file-scope array instead of a caller buffer.  Its size caps
+// the bitmap at kNoAllocMaxBits (2^27 neurons -> 4096 tile counts, 16 KiB).
+// The tile counts are fully overwritten by the first launch, so nothing has
+// to start at zero.  The array exists once per device: two calls whose
+// launches overlap on one GPU (different streams, or host threads) race on it.
+static __device__ __align__(256) uint32_t
+    g_noalloc_tile_counts[(kNoAllocMaxBits / 32 + kWordsPerTile - 1) / kWordsPerTile];
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mutex;
+uint32_t* g_noalloc_scratch[kNoAllocMaxDevices];  // device address per device ordinal, looked up once
+}  // namespace
+
+void bitmap_to_spikes_noalloc(const uint32_t* d_bits, uint64_t nbits, uint32_t* d_out, uint32_t* d_count,
+                              cudaStream_t stream) {
+  b2ir::check(nbits <= kNoAllocMaxBits,
+              "bitmap of " + std::to_string(nbits) + " bits exceeds the no-alloc limit of " +
+                  std::to_string(kNoAllocMaxBits) + " bits; use b2g_spikes_from_bitmap with a scratch buffer");
+  int device = -1;
+  B2_CUDA(cudaGetDevice(&device));
+  b2ir::check(device >= 0 && device < kNoAllocMaxDevices, "device ordinal out of range for the no-alloc scratch");
+  uint32_t* scratch = nullptr;
+  {
+    // Set-up, once per device, with that device current: the address of this
+    // device's copy of the array (the first call may load the module, so it
+    // belongs before any stream capture).
+    std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+    if (!g_noalloc_scratch[device]) {
+      void* p = nullptr;
+      const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_tile_counts);
+      b2ir::check(e == cudaSuccess && p, std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e));
+      g_noalloc_scratch[device] = static_cast<uint32_t*>(p);
+    }
+    scratch = g_noalloc_scratch[device];
+  }
+  bitmap_to_spikes(d_bits, nbits, d_out, d_count, scratch, stream);
 }
 
 }  // namespace b2gpu

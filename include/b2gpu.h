@@ -161,6 +161,21 @@ size_t b2g_spikes_scratch_bytes(uint64_t nbits);
 int b2g_spikes_from_bitmap(const uint32_t* d_words, uint64_t nbits, uint32_t* d_ids, uint32_t* d_count,
                            void* d_scratch, size_t scratch_bytes, void* stream, char* error, size_t error_capacity);
 
+/* No counterpart in the reference.  b2g_spikes_from_bitmap for callers that
+ * cannot allocate device memory around the call (a tick loop that must not
+ * stall on an allocator, a framework whose caching allocator holds the
+ * device's memory budget, a process that has reserved all free memory): the
+ * scratch is a fixed array inside the library, one per device, so
+ *   - nbits must not exceed B2G_SPIKES_NOALLOC_MAX_BITS (else error 1);
+ *   - calls whose launches overlap on one GPU race on that array;
+ *   - the first call on a device does a one-time set-up (it looks the array
+ *     up, which may load the library's device code), so make it before any
+ *     stream capture.
+ * Nothing needs to be zeroed beforehand. */
+#define B2G_SPIKES_NOALLOC_MAX_BITS (1ull << 27)
+int b2g_spikes_from_bitmap_noalloc(const uint32_t* d_words, uint64_t nbits, uint32_t* d_ids, uint32_t* d_count,
+                                   void* stream, char* error, size_t error_capacity);
+
 void b2g_destroy(b2g_engine* engine);
 
 const char* b2g_version(void);

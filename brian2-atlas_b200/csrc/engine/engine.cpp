@@ -11,6 +11,7 @@
 #include <functional>
 #include <set>
 #include <sstream>
+#include <unordered_map>
 #include <unordered_set>
 
 #include "cuda_util.hpp"
@@ -209,7 +210,7 @@ struct Engine::Impl {
     int delivered_slot = 0;
     enum class Mode { Atomic, EdgeParallel, Serial } mode = Mode::Serial;
     std::vector<AtomicAdd> atomic_adds;
-    int pend_offsets = -1, pend_items = -1;
+    int pend_offsets = -1, pend_items = -1, pend_src = -1, pend_tgt = -1;
     bool has_pending = false;
   };
   struct SynDev {
@@ -648,26 +649,64 @@ struct Engine::Impl {
             pd.row_other = adopt(std::move(rows));
           }
         }
-        // pending (continuation) events: CSR by consumption tick
+        // Pending (continuation) events, validated like model.rs:4315-4337,
+        // then laid out as a CSR by the tick that consumes them: the reference
+        // queues an event in ring slot delivery_tick % slots before the run and
+        // drains that slot at the first tick with that residue
+        // (PathwayQueue::new, executor.rs:6185-6212).  With a uniform delay an
+        // item is an endpoint index (its whole row is delivered); otherwise it
+        // is one edge, delivered with its source and target.
         if (!pw.pending.empty()) {
-          check(pd.uniform, "pending events on per-edge-delay pathways are not supported by the GPU engine yet");
+          check(pd.uniform || !procedural, "pending events on per-edge-delay procedural pathways are not supported");
+          const size_t end_tick = start_tick + endpoint.steps;
+          bool valid = pw.pending.size() <= 10'000'000;
+          for (size_t x = 0; valid && x < pw.pending.size(); ++x) {
+            const auto& ev2 = pw.pending[x];
+            valid = ev2.delivery_tick >= start_tick && ev2.delivery_tick < end_tick &&
+                    ev2.item < (pd.uniform ? pd.endpoint_count : sd.edges) &&
+                    (x == 0 || pw.pending[x - 1].delivery_tick <= ev2.delivery_tick);
+          }
+          check(valid, "invalid pending synaptic pathway event");
+          // multi-GPU: an edge item belongs to the rank that stores the edge
+          std::unordered_map<uint32_t, uint32_t> local_of;
+          if (!pd.uniform && !all_edges)
+            for (size_t k = 0; k < edge_ids.size(); ++k) local_of.emplace(edge_ids[k], uint32_t(k));
           size_t slots = std::min(pd.max_delay + 1, endpoint.steps);
-          std::vector<std::vector<uint32_t>> per(steps);
+          struct Item { uint32_t item, src, tgt; };
+          std::vector<std::vector<Item>> per(steps);
           for (const auto& ev2 : pw.pending) {
             size_t slot = ev2.delivery_tick % slots;
             size_t first = start_tick + ((slot + slots - start_tick % slots) % slots);
             if (first >= start_tick + steps) continue;
-            check(ev2.item <= UINT32_MAX, "pending item out of range");
-            per[first - start_tick].push_back(uint32_t(ev2.item));
+            if (pd.uniform) {
+              per[first - start_tick].push_back({uint32_t(ev2.item), 0, 0});
+            } else {
+              const uint32_t e = uint32_t(ev2.item);
+              uint32_t local = e;
+              if (!all_edges) {
+                auto it = local_of.find(e);
+                if (it == local_of.end()) continue;
+                local = it->second;
+              }
+              per[first - start_tick].push_back({local, src_h[e], tgt_h[e]});
+            }
           }
           std::vector<uint64_t> offs(steps + 1, 0);
-          std::vector<uint32_t> items;
+          std::vector<uint32_t> items, srcs, tgts;
           for (size_t t = 0; t < steps; ++t) {
-            items.insert(items.end(), per[t].begin(), per[t].end());
+            for (const Item& it : per[t]) {
+              items.push_back(it.item);
+              srcs.push_back(it.src);
+              tgts.push_back(it.tgt);
+            }
             offs[t + 1] = items.size();
           }
           pd.pend_offsets = upload(offs.data(), offs.size() * 8);
           pd.pend_items = upload(items.data(), std::max<size_t>(items.size(), 1) * 4);
+          if (!pd.uniform) {
+            pd.pend_src = upload(srcs.data(), std::max<size_t>(srcs.size(), 1) * 4);
+            pd.pend_tgt = upload(tgts.data(), std::max<size_t>(tgts.size(), 1) * 4);
+          }
           pd.has_pending = !items.empty();
         }
         pd.delivered_slot = int(delivered_count++);
@@ -927,6 +966,7 @@ struct Engine::Impl {
     c.seed = u64lit(m.rng_seed);
     c.tick = "tick";
     c.time = "t";
+    c.tables = &const_tables;
     for (auto& ix : c.index_for_domain) ix = gi;
     return c;
   }
@@ -1577,10 +1617,16 @@ struct Engine::Impl {
       };
       if (pw.has_pending) {
         // Pending items were queued before any runtime push, so they come first
-        // in their slot; with a uniform delay an item is an endpoint index.
+        // in their slot; with a uniform delay an item is an endpoint index,
+        // otherwise one edge (local index, with its source and target).
         o << "  { const u64* po = " << P(pw.pend_offsets, "const u64") << "; const u32* pi = " << P(pw.pend_items, "const u32") << ";\n";
         o << "    for (u64 x = po[rel]; x < po[rel + 1]; ++x) {\n";
-        o << "      const u32 ep = pi[x];\n" << deliver_row("");
+        if (pw.uniform) {
+          o << "      const u32 ep = pi[x];\n" << deliver_row("");
+        } else {
+          o << "      " << body_fn << "(" << P(pw.pend_src, "const u32") << "[x], " << P(pw.pend_tgt, "const u32")
+            << "[x], (u64)pi[x], tick, t, err);\n      ++events;\n";
+        }
         o << "    }\n  }\n";
       }
       o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n";
@@ -1659,6 +1705,7 @@ struct Engine::Impl {
   }
 
   std::vector<Program> programs;  // owned programs (stable addresses via reserve)
+  std::map<std::string, std::string> const_tables;  // file-scope tables referenced by emitted code
 
   // A kernel in the tick, generated once the whole schedule is analysed.
   struct StepSpec {
@@ -1984,6 +2031,7 @@ struct Engine::Impl {
       kernels << gen_pop_step(nm, p, flushes[f].second, nullptr, 0, false, nullptr, {}, true);
       flush_ops.push_back({nm, nullptr, unsigned(tiles_for(pops[p].count)), kThreads});
     }
+    for (const auto& [name, def] : const_tables) src << def << "\n";
     src << bodies.str() << "\n" << kernels.str();
     source = src.str();
     std::string placeholder = "PTR_COUNT_PLACEHOLDER";
@@ -2105,10 +2153,10 @@ struct Engine::Impl {
   }
 
   // Per-kernel timing: direct launches bracketed by events (no graph).
-  // Per-kernel timing: every kernel of a chunk launched directly (plain
-  // stream order, no programmatic overlap) with an event recorded after each
-  // one; the whole chunk is queued before the host waits, so the GPU runs
-  // the kernels back to back and each interval is the kernel's own time.
+  // Per-kernel timing: the chunk is captured as a CUDA graph like step()'s,
+  // with an event record node after every kernel (so kernels run back to
+  // back without host launch gaps, in plain stream order: the event nodes
+  // replace the programmatic overlap); each event interval is one kernel.
   std::vector<KernelTime> profile(uint64_t ticks) {
     check(!opt.dry_run && !failed, "profiling needs a live engine");
     check(world == 1 || connected, "a multi-GPU engine must connect() to its peers before stepping");
@@ -2117,21 +2165,40 @@ struct Engine::Impl {
     const size_t per_tick = ops.size();
     std::vector<cudaEvent_t> evs(size_t(opt.chunk_ticks) * per_tick + 1);
     for (auto& e : evs) B2_CUDA(cudaEventCreate(&e));
+    cudaGraphExec_t exec = nullptr;
+    uint32_t exec_ticks = 0;
+    auto release = [&] {
+      if (exec) cudaGraphExecDestroy(exec);
+      for (auto& e : evs) cudaEventDestroy(e);
+    };
     uint64_t remaining = std::min<uint64_t>(ticks, steps - cur_rel);
     try {
       while (remaining > 0) {
         uint32_t n = uint32_t(std::min<uint64_t>(remaining, opt.chunk_ticks));
+        if (!exec || exec_ticks != n) {
+          if (exec) cudaGraphExecDestroy(exec);
+          exec = nullptr;
+          cudaGraph_t graph;
+          B2_CUDA(cudaStreamBeginCapture(stream, cudaStreamCaptureModeThreadLocal));
+          // external record nodes: the events are timed after the replay
+          B2_CUDA(cudaEventRecordWithFlags(evs[0], stream, cudaEventRecordExternal));
+          void* ctl_ptr = ctl.ptr;
+          for (uint32_t k = 0; k < n; ++k)
+            for (size_t i = 0; i < per_tick; ++i) {
+              uint32_t kk = k;
+              void* args[] = {&ctl_ptr, &kk};
+              B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(ops[i].fn), dim3(ops[i].grid),
+                                       dim3(ops[i].block), args, 0, stream));
+              B2_CUDA(cudaEventRecordWithFlags(evs[size_t(k) * per_tick + i + 1], stream, cudaEventRecordExternal));
+            }
+          B2_CUDA(cudaStreamEndCapture(stream, &graph));
+          B2_CUDA(cudaGraphInstantiate(&exec, graph, 0));
+          cudaGraphDestroy(graph);
+          exec_ticks = n;
+        }
         tick_host_ = start_tick + cur_rel;
         B2_CUDA(cudaMemcpyAsync(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice, stream));
-        B2_CUDA(cudaEventRecord(evs[0], stream));
-        void* ctl_ptr = ctl.ptr;
-        for (uint32_t k = 0; k < n; ++k)
-          for (size_t i = 0; i < per_tick; ++i) {
-            void* args[] = {&ctl_ptr, &k};
-            B2_CUDA(cudaLaunchKernel(reinterpret_cast<const void*>(ops[i].fn), dim3(ops[i].grid), dim3(ops[i].block),
-                                     args, 0, stream));
-            B2_CUDA(cudaEventRecord(evs[size_t(k) * per_tick + i + 1], stream));
-          }
+        B2_CUDA(cudaGraphLaunch(exec, stream));
         B2_CUDA(cudaStreamSynchronize(stream));
         for (uint32_t k = 0; k < n; ++k)
           for (size_t i = 0; i < per_tick; ++i) {
@@ -2150,14 +2217,15 @@ struct Engine::Impl {
         deferred_pending = !flushes.empty();
       }
     } catch (...) {
-      for (auto& e : evs) cudaEventDestroy(e);
+      release();
       throw;
     }
-    for (auto& e : evs) cudaEventDestroy(e);
+    release();
     if (cur_rel >= steps) flush_deferred();
     st.ticks = cur_rel;
     return out;
   }
+
 
 
   void check_error() {

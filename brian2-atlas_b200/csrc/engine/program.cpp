@@ -989,9 +989,32 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
                 double q = 1.0 - prob;
                 double qn = std::exp(nf * std::log(q));
                 double bound = std::fmin(nf, nf * prob + 10.0 * std::sqrt(nf * prob * q + 1.0));
-                expr = "b2_binomial_inv(" + head + ", " + std::to_string(in.n) + "ull, " + double_literal(prob) +
-                       ", " + double_literal(q) + ", " + double_literal(qn) + ", " + double_literal(bound) + ", " +
-                       (reverse ? "true" : "false") + ")";
+                const double kf = std::floor(bound) + 1.0;  // probabilities P(X = x) the loop can reach
+                if (ctx.tables && kf <= 64.0) {
+                  // The inversion's probabilities depend only on (n, p): build
+                  // them here with the loop's own products and division, in
+                  // the same order (-ffp-contract=off), so the device only
+                  // compares and subtracts.
+                  const size_t K = size_t(kf);
+                  std::vector<double> tab(K);
+                  tab[0] = qn;
+                  for (size_t x = 1; x < K; ++x) {
+                    const uint64_t xu = x;
+                    tab[x] = ((double)(in.n - xu + 1) * prob * tab[x - 1]) / ((double)xu * q);
+                  }
+                  std::string body;
+                  for (size_t x = 0; x < K; ++x) body += (x ? ", " : "") + double_literal(tab[x]);
+                  std::string name = "b2_btab_" + std::to_string(ctx.tables->size());
+                  for (const auto& [nm, def] : *ctx.tables)
+                    if (def.find("{" + body + "}") != std::string::npos) name = nm;
+                  (*ctx.tables)[name] = "__constant__ double " + name + "[" + std::to_string(K) + "] = {" + body + "};";
+                  expr = "b2_binomial_tab(" + head + ", " + std::to_string(in.n) + "ull, " + name + ", " +
+                         std::to_string(K) + "u, " + (reverse ? "true" : "false") + ")";
+                } else {
+                  expr = "b2_binomial_inv(" + head + ", " + std::to_string(in.n) + "ull, " + double_literal(prob) +
+                         ", " + double_literal(q) + ", " + double_literal(qn) + ", " + double_literal(bound) + ", " +
+                         (reverse ? "true" : "false") + ")";
+                }
               }
             }
           } else {

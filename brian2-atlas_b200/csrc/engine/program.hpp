@@ -134,6 +134,9 @@ struct EmitContext {
   std::string tick;     // expression for the current tick (u64)
   std::string index_for_domain[4];  // RNG counter index per Domain (u64)
   std::string time;     // expression for t (double)
+  // Optional sink for file-scope constant tables (name -> definition) that
+  // emitted code may reference; null disables table-based emission.
+  std::map<std::string, std::string>* tables = nullptr;
 };
 
 // Emit the body of a program: declarations of every non-Const register used,

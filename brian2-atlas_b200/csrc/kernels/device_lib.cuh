@@ -105,6 +105,25 @@ __device__ double b2_binomial_inv(u64 seed, u64 stream, u64 tick, u64 index, u64
   return 0.0;
 }
 
+// The same inversion over a host-built table tab[x] = P(X = x), x < K =
+// floor(bound) + 1, whose entries are the loop's own px values (built with
+// the loop's products and division in the same order), so each step is one
+// compare and one subtraction: identical draws, comparisons and results.
+__device__ double b2_binomial_tab(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
+                                  const double* __restrict__ tab, u32 K, bool reverse) {
+  u64 draw = 0;
+  for (int restarts = 0; restarts < 1 << 16; ++restarts) {
+    double u = b2_uniform_draw(seed, stream, tick, index, draw);
+    for (u32 x = 0; x < K; ++x) {
+      const double px = tab[x];
+      if (u <= px) return (double)(reverse ? n - x : x);
+      u -= px;
+    }
+    draw += 1;
+  }
+  return 0.0;
+}
+
 // General binomial with a per-lane probability (device libm for q^n).
 __device__ double b2_binomial(u64 seed, u64 stream, u64 tick, u64 index, u64 n, double p,
                               bool approximate) {
@@ -197,6 +216,7 @@ __device__ __forceinline__ double b2_binomial_checked(u64 seed, u64 stream, u64 
 }
 
 // ---------------------------------------------------------------- scalar ops
+
 // Per-op rules of the reference evaluate() (executor.rs:5932-6158).
 __device__ __forceinline__ double b2_exprel(double a) {
   if (fabs(a) < 1e-16) return 1.0;

@@ -32,6 +32,7 @@ CXXFLAGS = ["-O2", "-std=c++17", "-fPIC", "-ffp-contract=off", "-fno-fast-math",
 HOST_SOURCES = [
     CSRC / "common" / "ir.cpp",
     CSRC / "common" / "dump.cpp",
+    CSRC / "common" / "canonical.cpp",
     CSRC / "engine" / "program.cpp",
     CSRC / "engine" / "engine.cpp",
     CSRC / "abi.cpp",

@@ -14,6 +14,7 @@
 #include <string>
 
 #include "common/dump.hpp"
+#include "common/canonical.hpp"
 #include "common/ir.hpp"
 #include "engine/engine.hpp"
 #include "engine/spikes.hpp"
@@ -289,12 +290,26 @@ const char* b2g_version(void) { return "brian2-atlas-b200 0.1 (abi 1, sm_100a)";
 
 int b2g_run_cli(int argc, const char* const* argv) {
   try {
-    b2ir::check(argc == 3, "usage: b2-runner MODEL.json OUTPUT_DIRECTORY | b2-runner --validate MODEL.json");
+    b2ir::check(argc == 3,
+                "usage: b2-runner MODEL.json OUTPUT_DIRECTORY | b2-runner --validate MODEL.json | "
+                "b2-runner --canonical-hashes MODEL.json");
     std::string first = argv[1];
     if (first == "--validate") {
       b2ir::Model m = b2ir::load_model_file(argv[2]);
       (void)m;
       std::printf("validated AtlasIR\n");
+      return 0;
+    }
+    if (first == "--canonical-hashes") {
+      // validated (hashes included) first, then the layers object as
+      // run_cli prints it (model.rs:4668-4670): keys in order, compact
+      b2ir::Model m = b2ir::load_model_file(argv[2]);
+      (void)m;
+      std::ifstream f(argv[2], std::ios::binary);
+      std::string data((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+      const b2canon::Layers h = b2canon::layer_hashes(b2json::parse(data.data(), data.size()));
+      std::printf("{\"definition\":\"%s\",\"instance\":\"%s\",\"run\":\"%s\"}\n", h.definition.c_str(),
+                  h.instance.c_str(), h.run.c_str());
       return 0;
     }
     b2ir::check(first.rfind("--", 0) != 0, "unknown b2-runner option");

@@ -12,6 +12,7 @@
 #include <fstream>
 #include <sstream>
 
+#include "canonical.hpp"
 #include "json.hpp"
 
 namespace b2ir {
@@ -463,6 +464,9 @@ Model load_model(const char* json, size_t size) {
     m.schema = str(doc, "schema");
     check(m.schema == "atlasir-v1" || m.schema == "b2ir-v1",
           "unsupported AtlasIR schema '" + m.schema + "'");
+    // prepare_protocol (model.rs:4719-4730) verifies a legacy envelope's
+    // hashes before migrating it
+    if (m.schema == "b2ir-v1") b2canon::verify_protocol(doc);
     const Value& d = doc.at("definition");
     check(str(d, "numeric_profile") == "reference-f64", "unsupported numeric profile");
     check(str(d, "rng_algorithm") == "splitmix64-counter-v1", "unsupported RNG algorithm");
@@ -640,6 +644,9 @@ Model load_model(const char* json, size_t size) {
     for (const auto& c : run.at("clocks").arr()) m.run_clocks.push_back({usz(c, "start_tick"), usz(c, "steps")});
     check(m.run_clocks.size() == m.clocks.size(), "run clock count mismatch");
     for (const auto& p : m.populations) check(p.clock < m.clocks.size(), "population clock out of range");
+    // A current-schema document is checked after its content, as run_cli
+    // does (model.rs:4651-4661); a legacy envelope was checked on entry.
+    if (m.schema == "atlasir-v1") b2canon::verify_protocol(doc);
     return m;
   } catch (const b2json::Error& e) {
     throw Error(e.what());

@@ -48,6 +48,13 @@ def model_file(name: str, tmp: Path) -> Path:
     return out
 
 
+def encode_model(doc: dict) -> bytes:
+    """JSON bytes of an edited model document with its protocol layer hashes
+    recomputed (the engine, like the reference runner, refuses stale hashes)."""
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    return synthetic.encode(synthetic.attach_protocol(doc))
+
+
 def run_oracle(oracle: Path, model: Path, outdir: Path) -> Path:
     proc = subprocess.run([str(oracle), str(model), str(outdir)], capture_output=True, text=True)
     assert proc.returncode == 0, proc.stderr

@@ -16,7 +16,7 @@ import re
 
 import pytest
 
-from conftest import GOLDEN, MODELS, ROOT
+from conftest import GOLDEN, MODELS, ROOT, encode_model
 
 
 def declared_symbols():
@@ -91,7 +91,7 @@ def test_unsupported_model_fails_before_results(pkg, tmp_path):
     doc["definition"]["clocks"].append(dict(doc["definition"]["clocks"][0], name="second"))
     doc["run"]["clocks"].append(dict(doc["run"]["clocks"][0]))
     with pytest.raises(pkg.B2GpuError, match="single clock"):
-        pkg.codegen(json.dumps(doc).encode())
+        pkg.codegen(encode_model(doc))
 
 
 def test_malformed_document_is_rejected(pkg):

@@ -1,0 +1,84 @@
+"""Canonical JSON layer hashes and the runner's non-run modes (CPU).
+
+Pins: the reference's own golden hash corpus
+(brian2-rust/tests/golden/{atlasir-v1,b2ir-v1}/{minimal-v1.json,hashes.json},
+copied to tests/golden/canonical/), Python's json.dumps(sort_keys=True,
+separators=(",", ":"), ensure_ascii=False) for reals, escapes and non-ASCII
+text, and the runner contract of `--canonical-hashes` / `--validate` /
+"AtlasIR canonical layer hash mismatch" (brian2-rust/src/model.rs:4596-4677).
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import subprocess
+
+import pytest
+
+from conftest import GOLDEN, MODELS, ROOT
+
+CANON = GOLDEN / "canonical"
+
+
+def runner(*args):
+    exe = ROOT / "brian2-atlas_b200" / "bin" / "b2gpu-runner"
+    return subprocess.run([str(exe), *map(str, args)], capture_output=True, text=True)
+
+
+@pytest.mark.parametrize("name", ["atlasir", "b2ir"])
+def test_golden_corpus_hashes(name):
+    proc = runner("--canonical-hashes", CANON / f"{name}-minimal-v1.json")
+    assert proc.returncode == 0, proc.stderr
+    want = json.loads((CANON / f"{name}-hashes.json").read_text())["layers"]
+    assert json.loads(proc.stdout) == want
+    assert proc.stdout.strip() == json.dumps(want, separators=(",", ":"))
+
+
+def python_hash(value) -> str:
+    text = json.dumps(value, sort_keys=True, separators=(",", ":"), ensure_ascii=False)
+    return hashlib.sha256(text.encode()).hexdigest()
+
+
+def test_reals_escapes_and_unicode_match_python(tmp_path):
+    doc = json.loads((MODELS / "cuba_small.json").read_text())
+    doc["run"]["x_canonical_probe"] = {
+        "reals": [0.1, 1e16, 1e15, 1e-5, 1.5e-4, 0.0001, 123456789012345678.0, 2.5, -0.0, 1e300, 5e-324,
+                  0.30000000000000004, 12345.678, -7.25e-12, 1.7976931348623157e308, 100.0],
+        "text": ["été", "☃", "tab\tnew\nline", "\x01\x1f", 'quote"back\\slash', "\x7f"],
+        "nested": {"b": [1, -2, 18446744073709551615, -9223372036854775808], "a": None, "c": True},
+    }
+    want = python_hash(doc["run"])
+    path = tmp_path / "probe.json"
+    path.write_text(json.dumps(doc, ensure_ascii=False))
+    proc = runner("--canonical-hashes", path)  # stale protocol: rejected, but only after hashing
+    assert proc.returncode == 1 and "canonical layer hash mismatch" in proc.stderr
+    import importlib
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    doc = synthetic.attach_protocol(doc)
+    assert doc["protocol"]["layers"]["run"] == want
+    path.write_text(json.dumps(doc, ensure_ascii=False))
+    proc = runner("--canonical-hashes", path)
+    assert proc.returncode == 0, proc.stderr
+    assert json.loads(proc.stdout)["run"] == want
+
+
+def test_tampered_document_is_refused(pkg, tmp_path):
+    doc = json.loads((MODELS / "cuba_small.json").read_text())
+    doc["instance"]["rng_seed"] = doc["instance"]["rng_seed"] + 1
+    path = tmp_path / "tampered.json"
+    path.write_text(json.dumps(doc))
+    for mode in ("--validate", "--canonical-hashes"):
+        proc = runner(mode, path)
+        assert proc.returncode == 1
+        assert proc.stderr.strip() == "b2-runner: AtlasIR canonical layer hash mismatch"
+    proc = runner(path, tmp_path / "out")
+    assert proc.returncode == 1 and not (tmp_path / "out").exists()
+    with pytest.raises(pkg.B2GpuError, match="canonical layer hash mismatch"):
+        pkg.codegen(path.read_bytes())
+
+
+def test_validate_accepts_fixtures():
+    for path in [GOLDEN / "reference-v1" / "model.json", MODELS / "cuba_small.json", MODELS / "brunel_small.json",
+                 CANON / "atlasir-minimal-v1.json", CANON / "b2ir-minimal-v1.json"]:
+        proc = runner("--validate", path)
+        assert proc.returncode == 0 and proc.stdout.strip() == "validated AtlasIR", (path, proc.stderr)

@@ -15,7 +15,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, MODELS, model_file, run_oracle
+from conftest import GOLDEN, MODELS, encode_model, model_file, run_oracle
 from b2results import load_model, read_results
 
 pytestmark = pytest.mark.gpu
@@ -133,7 +133,7 @@ def test_nonfinite_state_raises_instead_of_faulting(pkg):
         if st["target"] == "ge":
             st["value"] = {"op": "mul", "left": {"op": "load", "name": "ge"}, "right": {"op": "load", "name": "ge"}}
     doc["instance"]["populations"][0]["initial_state"]["ge"][5] = "6974e718d7d7625a"  # 1e200
-    with pkg.Engine(json.dumps(doc).encode(), device=0) as eng:
+    with pkg.Engine(encode_model(doc), device=0) as eng:
         with pytest.raises(pkg.B2GpuError, match="non-finite"):
             eng.run()
         with pytest.raises(pkg.B2GpuError, match="create a new executor"):

@@ -15,7 +15,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, MODELS, run_oracle
+from conftest import GOLDEN, MODELS, encode_model, run_oracle
 
 
 def with_pending(doc: dict, seed: int, per_pathway: int = 40) -> dict:
@@ -40,7 +40,7 @@ def with_pending(doc: dict, seed: int, per_pathway: int = 40) -> dict:
 def golden_with_pending(tmp_path, seed=1):
     doc = with_pending(json.loads((GOLDEN / "reference-v1" / "model.json").read_text()), seed)
     path = tmp_path / "golden_pending.json"
-    path.write_text(json.dumps(doc))
+    path.write_bytes(encode_model(doc))
     return path
 
 
@@ -52,7 +52,7 @@ def cuba_with_pending(tmp_path, seed=2):
             pw["delay_ticks"] = [3] * len(pw["delay_ticks"])
     doc = with_pending(doc, seed)
     path = tmp_path / "cuba_pending.json"
-    path.write_text(json.dumps(doc))
+    path.write_bytes(encode_model(doc))
     return path
 
 
@@ -70,10 +70,10 @@ def test_invalid_pending_is_rejected(pkg, tmp_path):
     pw = doc["instance"]["synapses"][0]["pathways"][0]
     pw["pending"] = [{"delivery_tick": 5, "item": 0}, {"delivery_tick": 2, "item": 0}]  # not sorted
     with pytest.raises(pkg.B2GpuError, match="invalid pending synaptic pathway event"):
-        pkg.codegen(json.dumps(doc).encode())
+        pkg.codegen(encode_model(doc))
     pw["pending"] = [{"delivery_tick": 1, "item": len(doc["instance"]["synapses"][0]["source"])}]  # no such edge
     with pytest.raises(pkg.B2GpuError, match="invalid pending synaptic pathway event"):
-        pkg.codegen(json.dumps(doc).encode())
+        pkg.codegen(encode_model(doc))
 
 
 def assert_same_files(a, b):

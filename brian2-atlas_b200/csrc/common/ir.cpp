@@ -7,9 +7,12 @@
 // (model.rs:4719-4730 `prepare_protocol`).
 #include "ir.hpp"
 
+#include <algorithm>
+#include <cctype>
 #include <cmath>
 #include <cstring>
 #include <fstream>
+#include <set>
 #include <sstream>
 
 #include "canonical.hpp"
@@ -337,6 +340,10 @@ Topology parse_topology(const Value& v) {
   if (kind == "binary_csr") {
     t.kind = Topology::Kind::BinaryCsr;
     t.edge_count = v.at("edge_count").u64();
+    t.path = str(v, "path");
+    t.sha256 = str(v, "sha256");
+    t.column_count = v.at("column_count").u64();
+    for (const auto& kv : v.at("initializers").obj()) t.columns[kv.first] = kv.second.u64();
     return t;
   }
   t.kind = kind == "fixed_total" ? Topology::Kind::FixedTotal
@@ -644,6 +651,31 @@ Model load_model(const char* json, size_t size) {
     for (const auto& c : run.at("clocks").arr()) m.run_clocks.push_back({usz(c, "start_tick"), usz(c, "steps")});
     check(m.run_clocks.size() == m.clocks.size(), "run clock count mismatch");
     for (const auto& p : m.populations) check(p.clock < m.clocks.size(), "population clock out of range");
+    // binary_csr mapping rules and file contents (model.rs:2163-2205)
+    for (size_t s = 0; s < m.synapses.size() && s < m.synapse_instances.size(); ++s) {
+      const SynapseDef& def = m.synapses[s];
+      const SynapseInstance& inst = m.synapse_instances[s];
+      const Topology& t = inst.topology;
+      if (t.kind != Topology::Kind::BinaryCsr) continue;
+      std::set<std::string> names, mapped;
+      bool ok = inst.source.empty() && inst.target.empty() && def.states.empty();
+      for (const auto& p : def.parameters)
+        if (p.index_domain == IndexDomain::Synapse) {
+          names.insert(p.name);
+          ok &= p.dtype == DType::F64;
+        }
+      std::set<uint64_t> cols;
+      for (const auto& [name, col] : t.columns) {
+        mapped.insert(name);
+        cols.insert(col);
+        ok &= col < t.column_count;
+      }
+      ok &= names == mapped && cols.size() == t.column_count;
+      ok &= t.sha256.size() == 64 && std::all_of(t.sha256.begin(), t.sha256.end(), [](char c) { return std::isxdigit(uint8_t(c)); });
+      for (const auto& p : inst.pathways) ok &= p.kind == "pre" && !p.delay_initializer && p.delay.size() == 1;
+      check(ok, "invalid binary CSR mapping/pathway");
+      read_binary_csr(t.path, def.source_count, def.target_count, t.edge_count, t.column_count, t.sha256, false);
+    }
     // A current-schema document is checked after its content, as run_cli
     // does (model.rs:4651-4661); a legacy envelope was checked on entry.
     if (m.schema == "atlasir-v1") b2canon::verify_protocol(doc);
@@ -655,6 +687,80 @@ Model load_model(const char* json, size_t size) {
   } catch (const std::out_of_range&) {
     throw Error("integer literal out of range");
   }
+}
+
+BinaryCsr read_binary_csr(const std::string& path, uint64_t sources, uint64_t targets, uint64_t edges,
+                          uint64_t columns, const std::string& sha256, bool materialize) {
+  check(sources > 0 && targets > 0 && sources <= 1'000'000 && targets <= 1'000'000 && edges > 0 &&
+            edges <= 100'000'000 && columns <= 128,
+        "invalid binary CSR shape");
+  std::ifstream f(path, std::ios::binary);
+  check(bool(f), "cannot open binary CSR file '" + path + "'");
+  const uint64_t expected = 40 + (sources + 1) * 8 + edges * (4 + 8 * columns);
+  f.seekg(0, std::ios::end);
+  check(uint64_t(f.tellg()) == expected, "binary CSR file length mismatch");
+  f.seekg(0);
+  {
+    b2canon::Sha256 digest;
+    std::vector<char> chunk(1 << 16);
+    while (f) {
+      f.read(chunk.data(), std::streamsize(chunk.size()));
+      digest.update(chunk.data(), size_t(f.gcount()));
+    }
+    std::string want = sha256;
+    for (char& c : want) c = char(std::tolower(uint8_t(c)));
+    check(digest.hex() == want, "binary CSR checksum mismatch");
+  }
+  f.clear();
+  f.seekg(0);
+  std::vector<char> bytes(expected);
+  f.read(bytes.data(), std::streamsize(expected));
+  check(uint64_t(f.gcount()) == expected, "binary CSR file length mismatch");
+  const char* p = bytes.data();
+  auto u64 = [&p]() {
+    uint64_t v;
+    std::memcpy(&v, p, 8);  // little-endian host
+    p += 8;
+    return v;
+  };
+  check(std::memcmp(p, "B2CSR001", 8) == 0, "binary CSR header mismatch");
+  p += 8;
+  const uint64_t hs = u64(), ht = u64(), he = u64(), hc = u64();
+  check(hs == sources && ht == targets && he == edges && hc == columns, "binary CSR header mismatch");
+  BinaryCsr out;
+  if (materialize) {
+    out.source.reserve(edges);
+    out.target.reserve(edges);
+  }
+  uint64_t previous = u64();
+  check(previous == 0, "binary CSR offsets must start at zero");
+  for (uint64_t neuron = 0; neuron < sources; ++neuron) {
+    const uint64_t next = u64();
+    check(next >= previous && next <= edges, "invalid binary CSR offsets");
+    if (materialize) out.source.resize(next, uint32_t(neuron));
+    previous = next;
+  }
+  check(previous == edges, "binary CSR final offset mismatch");
+  for (uint64_t e = 0; e < edges; ++e) {
+    uint32_t v;
+    std::memcpy(&v, p, 4);
+    p += 4;
+    check(v < targets, "binary CSR target outside population");
+    if (materialize) out.target.push_back(v);
+  }
+  for (uint64_t c = 0; c < columns; ++c) {
+    std::vector<double> column;
+    if (materialize) column.reserve(edges);
+    for (uint64_t e = 0; e < edges; ++e) {
+      double v;
+      std::memcpy(&v, p, 8);
+      p += 8;
+      check(std::isfinite(v), "nonfinite binary CSR parameter");
+      if (materialize) column.push_back(v);
+    }
+    if (materialize) out.columns.push_back(std::move(column));
+  }
+  return out;
 }
 
 Model load_model_file(const std::string& path) {

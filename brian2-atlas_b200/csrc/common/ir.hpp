@@ -229,7 +229,25 @@ struct Topology {
   enum class Kind : uint8_t { Explicit, FixedTotal, FixedIndegree, BinaryCsr } kind = Kind::Explicit;
   uint64_t edge_count = 0, indegree = 0, seed = 0;
   std::map<std::string, Initializer> initializers;
+  // binary_csr: external B2CSR001 file, its SHA-256 and the per-edge
+  // parameter -> value column mapping
+  std::string path, sha256;
+  uint64_t column_count = 0;
+  std::map<std::string, uint64_t> columns;
 };
+
+// A B2CSR001 source-major graph (brian2-rust/src/binary_topology.rs): the
+// header (magic, sources, targets, edges, columns as u64 LE), sources + 1 u64
+// row offsets, edges u32 targets in creation order, then `columns` f64
+// columns of per-edge values.  Shape, length, checksum and contents are
+// validated with the reference's messages; arrays are filled only when
+// `materialize` is set.
+struct BinaryCsr {
+  std::vector<uint32_t> source, target;
+  std::vector<std::vector<double>> columns;
+};
+BinaryCsr read_binary_csr(const std::string& path, uint64_t sources, uint64_t targets, uint64_t edges,
+                          uint64_t columns, const std::string& sha256, bool materialize);
 
 struct PendingEvent {
   size_t delivery_tick = 0, item = 0;

@@ -368,8 +368,6 @@ struct Engine::Impl {
         check(c.kind == "synapses" || c.kind == "synapses_post",
               "synapse code object kind '" + c.kind + "' is not supported by the GPU engine");
     }
-    for (const auto& si : m.synapse_instances)
-      check(si.topology.kind != b2ir::Topology::Kind::BinaryCsr, "binary_csr topology is not supported by the GPU engine yet");
     // one warp lane per destination rank stores a fired word: at most 32 ranks
     check(world >= 1 && world <= 32 && rank >= 0 && rank < world, "invalid rank / world size (1 to 32 GPUs)");
     if (world > 1) {
@@ -500,16 +498,22 @@ struct Engine::Impl {
       std::vector<uint32_t> src_h, tgt_h;  // explicit only
       std::map<std::string, std::vector<double>> generated_params;
       std::vector<std::vector<size_t>> delays;
-      bool procedural = topo.kind != b2ir::Topology::Kind::Explicit;
+      // a binary_csr graph is an explicit edge list stored in a file
+      const bool binary = topo.kind == b2ir::Topology::Kind::BinaryCsr;
+      bool procedural = topo.kind != b2ir::Topology::Kind::Explicit && !binary;
       sd.procedural = procedural;
+      b2ir::BinaryCsr csr;
+      if (binary)
+        csr = b2ir::read_binary_csr(topo.path, def.source_count, def.target_count, topo.edge_count, topo.column_count,
+                                    topo.sha256, true);
       // Edges this rank stores: every edge on one GPU; otherwise the edges
       // whose target it owns, in creation order (local edge k is global edge
       // edge_ids[k]).  Per-edge arrays are indexed by local edge.
       std::vector<uint32_t> edge_ids;
       const PopDev& tpop = pops[def.target_population];
       if (!procedural) {
-        src_h = inst.source;
-        tgt_h = inst.target;
+        src_h = binary ? std::move(csr.source) : inst.source;
+        tgt_h = binary ? std::move(csr.target) : inst.target;
         sd.edges = src_h.size();
         check(tgt_h.size() == sd.edges, "explicit source and target arrays differ in length");
         for (const auto& pw : inst.pathways) delays.push_back(pw.delay_ticks);
@@ -550,6 +554,14 @@ struct Engine::Impl {
             uniform_initializer_device(static_cast<double*>(dptr(k)), sd.edges, topo.seed, in.stream, *in.minimum,
                                        *in.maximum, 0, stream);
           sd.param_ptr[sym.name] = k;
+          continue;
+        }
+        auto col = binary ? topo.columns.find(sym.name) : topo.columns.end();
+        if (col != topo.columns.end()) {
+          const std::vector<double>& values = csr.columns[size_t(col->second)];
+          std::vector<double> v(sd.local_edges);
+          for (size_t k = 0; k < sd.local_edges; ++k) v[k] = values[gid(k)];
+          sd.param_ptr[sym.name] = upload(v.data(), std::max<size_t>(v.size(), 1) * 8);
           continue;
         }
         const auto& arr = inst.parameters.at(sym.name);

@@ -1144,8 +1144,17 @@ void materialize_projection(const Model& m, const SynapseDef& def, const Synapse
       target.assign(inst.target.begin(), inst.target.end());
       for (const auto& p : inst.pathways) delays.push_back(p.delay_ticks);
       return;
-    case Topology::Kind::BinaryCsr:
-      throw Error("binary_csr topology is outside the oracle's subset");
+    case Topology::Kind::BinaryCsr: {
+      // executor.rs:35-57: source-major edges in file order, mapped columns
+      // as per-edge parameters, the pathways' scalar delays
+      BinaryCsr csr = read_binary_csr(t.path, def.source_count, def.target_count, t.edge_count, t.column_count,
+                                      t.sha256, true);
+      source.assign(csr.source.begin(), csr.source.end());
+      target.assign(csr.target.begin(), csr.target.end());
+      for (const auto& [name, col] : t.columns) params[name] = csr.columns[size_t(col)];
+      for (const auto& p : inst.pathways) delays.push_back(p.delay_ticks);
+      return;
+    }
     case Topology::Kind::FixedTotal: {
       uint64_t S = def.source_count, T = def.target_count, E = t.edge_count;
       check(S && T && E && E <= UINT32_MAX, "invalid fixed-total topology specification");

@@ -161,7 +161,7 @@ struct Engine::Impl {
     bool exchanged = false;
     size_t x_off = 0;
     std::vector<int> xptr;
-    uint64_t x_words = 0, x_tiles = 0;
+    uint64_t x_words = 0, x_tiles = 0, x_wpb = 0;  // exchange words, blocks, words per block
     // host copy of drained spikes
     std::vector<uint32_t> ids;
     std::vector<uint64_t> starts;  // host positions per tick: starts[rel] .. starts[rel+1]
@@ -179,6 +179,10 @@ struct Engine::Impl {
     std::map<std::string, double> param_const; // scalar or uniform parameters
     std::vector<int> stream_of_event;          // event index -> event stream id
     bool has_spike_monitor = false;
+    // per EventMonitor: its event stream, and 1 when its schedule node runs
+    // before the node that produces the event in a tick (it then records the
+    // previous tick's list, as the reference's `fired` still holds it)
+    std::vector<int> evmon_stream, evmon_lag;
     // state monitor
     int mon_records = -1;
     size_t mon_nrec = 0;            // records owned by this rank
@@ -356,7 +360,8 @@ struct Engine::Impl {
       check(p.linked_variable_count == 0, "linked variables are not supported by the GPU engine");
       check(!p.spatial, "spatial neurons are not supported by the GPU engine");
       check(p.rate_monitor_count == 0, "rate monitors are not supported by the GPU engine");
-      check(p.event_monitors.empty(), "event monitors are not supported by the GPU engine yet");
+      for (const auto& em : p.event_monitors)
+        check(em.variables.empty(), "EventMonitor variables are not supported by the GPU engine yet");
       check(p.steps == steps, "population steps must match the run clock");
       for (const auto& c : p.code_objects) check(!c.adaptive, "adaptive integrators are not supported by the GPU engine");
     }
@@ -772,11 +777,13 @@ struct Engine::Impl {
         // spike generators emit their (global, precomputed) list on every rank
         es.exchanged = true;
         es.x_words = exchange_words(pd.global_count, world);
-        es.x_tiles = std::max<uint64_t>(1, (es.x_words + kThreads - 1) / kThreads);
+        // about eight blocks per SM, at most one word per thread
+        es.x_wpb = std::clamp<uint64_t>((es.x_words + sm_count_ * 8 - 1) / (sm_count_ * 8), 1, kThreads);
+        es.x_tiles = std::max<uint64_t>(1, (es.x_words + es.x_wpb - 1) / es.x_wpb);
         es.x_off = x_bytes;
         x_bytes += (2 * es.x_words * 8 + 255) / 256 * 256;
         tiles = es.x_tiles;
-        tile_n = size_t(kThreads) * 32;
+        tile_n = size_t(es.x_wpb) * 32;
       }
       es.tile_count = alloc(tiles * 4);
       es.stage = alloc(tiles * tile_n * 4);
@@ -1212,20 +1219,21 @@ struct Engine::Impl {
   // spike list with the same tile staging + last-block layout as the step
   // kernel.  Word w belongs to rank q's block when
   // exchange_words(N, q) <= w < exchange_words(N, q + 1).
-  std::string gen_exchange(const std::string& name, int stream_id) {
+  std::string gen_exchange(const std::string& name, int stream_id, const std::vector<PathwayDev*>& fused = {}) {
     const EventStreamDev& es = streams[size_t(stream_id)];
     const PopDev& pd = pops[es.pop];
     const uint64_t timeout_ns = uint64_t(opt.exchange_timeout_ms) * 1000000ull;
-    const unsigned tile_n = kThreads * 32;
+    const unsigned wpb = unsigned(es.x_wpb), tile_n = wpb * 32;
     std::ostringstream o;
     o << kernel_head(name);
     o << "  __shared__ u32 s_last;\n";
-    o << "  const u32 tile = blockIdx.x;\n  const u32 w = tile * " << kThreads << "u + threadIdx.x;\n";
+    if (!fused.empty()) o << "  __shared__ u32 s_ids[" << tile_n << "];\n";
+    o << "  const u32 tile = blockIdx.x;\n  const u32 w = tile * " << wpb << "u + threadIdx.x;\n";
     o << "  u32 bits = 0, id0 = 0;\n";
     // once the run has failed (e.g. an earlier wait expired) later ticks
     // must not wait again: their results are discarded anyway
     o << "  const bool poisoned = *(volatile const u32*)&ctl->error != 0u;\n";
-    o << "  if (w < " << es.x_words << "u && !poisoned) {\n";
+    o << "  if (threadIdx.x < " << wpb << "u && w < " << es.x_words << "u && !poisoned) {\n";
     o << "    bits = b2_ll_wait(((const u64*)g_ptr[" << es.xptr[size_t(rank)] << "]) + (rel & 1ull) * " << es.x_words
       << "ull + w, (u32)(rel + 1ull), " << timeout_ns << "ull, err);\n";
     for (int q = 0; q < world; ++q) {
@@ -1236,12 +1244,43 @@ struct Engine::Impl {
     o << "  }\n";
     o << "  u32 total;\n  u32 pos = b2_block_exclusive_scan<" << kThreads << ">(__popc(bits), &total);\n";
     o << "  u32* stage = " << P(es.stage, "u32") << " + (u64)tile * " << tile_n << "u;\n";
-    o << "  for (u32 x = bits; x; x &= x - 1u) stage[pos++] = id0 + (u32)(__ffs(x) - 1);\n";
+    o << "  for (u32 x = bits; x; x &= x - 1u) {\n    const u32 id = id0 + (u32)(__ffs(x) - 1);\n";
+    if (!fused.empty()) o << "    s_ids[pos] = id;\n";
+    o << "    stage[pos++] = id;\n  }\n";
     o << "  if (threadIdx.x == 0) " << P(es.tile_count, "u32") << "[tile] = total;\n";
     o << "  __threadfence();\n  __syncthreads();\n";
     o << "  if (threadIdx.x == 0) s_last = (atomicAdd((unsigned long long*)" << P(es.done, "u64") << ", 1ull) % "
       << es.x_tiles << "ull) == " << es.x_tiles - 1 << "ull;\n";
     o << "  __syncthreads();\n";
+    if (!fused.empty()) {
+      // Delay-0 constant-addend pathways of this stream, fused: every block
+      // delivers the rows of the spikes it has just unpacked (delivery order
+      // is free for these pathways), so the scatter needs no ring read and
+      // no kernel boundary of its own.
+      const PathwayDev& p0 = *fused.front();
+      const size_t endpoint_count = m.populations[p0.endpoint_pop].count;
+      for (size_t k = 0; k < fused.size(); ++k) o << "  u64 events" << k << " = 0;\n";
+      o << "  for (u32 k2 = 0; k2 < total; ++k2) {\n    const u32 s = s_ids[k2];\n";
+      for (size_t k = 0; k < fused.size(); ++k) {
+        const PathwayDev& pw = *fused[k];
+        const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
+        const bool full = lo == 0 && hi == endpoint_count;
+        o << "    " << (full ? "{" : "if (s >= " + std::to_string(lo) + "u && s < " + std::to_string(hi) + "u) {") << "\n";
+        o << "      const u64* off = " << P(pw.offsets, "const u64") << ";\n";
+        o << "      const u32* other = " << P(pw.row_other, "const u32") << ";\n";
+        o << "      const u32 ep = s - " << lo << "u;\n";
+        o << "      const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
+        o << "      if (threadIdx.x == 0) events" << k << " += r1 - r0;\n";
+        o << "      for (u64 q0 = r0; q0 < r1; q0 += " << row_chunk() << "ull) {\n";
+        o << "        const u64 q1 = q0 + " << row_chunk() << "ull < r1 ? q0 + " << row_chunk() << "ull : r1;\n";
+        o << emit_atomic_chunk(pw, "        ");
+        o << "      }\n    }\n";
+      }
+      o << "  }\n";
+      for (size_t k = 0; k < fused.size(); ++k)
+        o << "  if (threadIdx.x == 0 && events" << k << ") atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64")
+          << " + " << fused[k]->delivered_slot << ", events" << k << ");\n";
+    }
     o << "  if (s_last) {\n    __threadfence();\n";
     o << "    b2_finalize_spikes<" << kThreads << ">(" << es.x_tiles << "u, " << tile_n << "u, " << P(es.tile_count, "const u32")
       << ", " << P(es.stage, "const u32") << ", " << P(es.ring, "u32") << ", " << u64lit(es.mask) << ", "
@@ -1249,6 +1288,7 @@ struct Engine::Impl {
     o << kernel_tail();
     return o.str();
   }
+
 
   // Reset over the tick's fired list (one thread per spike).
   std::string gen_reset(const std::string& name, size_t p, const Program& R, int stream_id) {
@@ -1740,6 +1780,7 @@ struct Engine::Impl {
     std::string base, text;
     size_t index = 0;
     unsigned grid = 1, block = kThreads;
+    int fuse_path = -1;  // exchange: PathSpec delivered inside the same kernel
   };
   std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
   std::vector<Op> flush_ops;
@@ -1799,7 +1840,30 @@ struct Engine::Impl {
             break;
           }
           case b2ir::ScheduleOp::SpikeMonitor: break;  // read from the drained spike ring
-          case b2ir::ScheduleOp::EventMonitor: throw Error("event monitors are not supported by the GPU engine yet");
+          case b2ir::ScheduleOp::EventMonitor: {
+            // read from the drained ring at results time; no kernel
+            check(node.item_index < def.event_monitors.size(), "scheduled EventMonitor has no definition");
+            const auto& em = def.event_monitors[node.item_index];
+            auto ev = std::find(def.events.begin(), def.events.end(), em.event);
+            check(ev != def.events.end(), "EventMonitor event missing from population");
+            const size_t e = size_t(ev - def.events.begin());
+            size_t producer = nodes.size();
+            for (size_t y = 0; y < nodes.size(); ++y) {
+              const auto& n2 = nodes[y];
+              if (n2.owner_kind != b2ir::OwnerKind::Population || n2.owner_index != p) continue;
+              if (n2.operation == b2ir::ScheduleOp::EventSource && e == 0) producer = y;
+              if (n2.operation == b2ir::ScheduleOp::CodeObject) {
+                const auto& c2 = def.code_objects[n2.item_index];
+                if (c2.kind == "threshold" && c2.event_name && *c2.event_name == em.event) producer = y;
+              }
+            }
+            PopDev& pdv = pops[p];
+            pdv.evmon_stream.resize(def.event_monitors.size(), -1);
+            pdv.evmon_lag.resize(def.event_monitors.size(), 0);
+            pdv.evmon_stream[node.item_index] = pdv.stream_of_event[e];
+            pdv.evmon_lag[node.item_index] = producer < idx ? 0 : 1;
+            break;
+          }
           case b2ir::ScheduleOp::EventSource: {
             check(pops[p].gen_offsets >= 0, "event source without spike generator");
             OpSpec o;
@@ -1996,6 +2060,22 @@ struct Engine::Impl {
       std::vector<uint64_t> init(m.populations.size(), UINT64_MAX);
       deferred_flags = upload(init.data(), init.size() * 8);
     }
+    // Multi-GPU: an exchange directly followed by the delay-0
+    // constant-addend scatter of the same stream delivers the spikes it
+    // unpacks itself (gen_exchange), saving a kernel boundary per tick.
+    if (world > 1 && !no_fuse_) {
+      for (size_t i = 0; i + 1 < specs.size(); ++i) {
+        if (specs[i].text != "exchange" || specs[i + 1].kind != OpSpec::Kind::Path) continue;
+        const PathSpec& ps = paths[specs[i + 1].index];
+        bool ok = true;
+        for (const PathwayDev* pw : ps.pathways)
+          ok &= pw->mode == PathwayDev::Mode::Atomic && pw->stream == int(specs[i].index) && pw->delay == 0;
+        if (!ok) continue;
+        specs[i].fuse_path = int(specs[i + 1].index);
+        specs[i].base += "_" + specs[i + 1].base + "_atomic";
+        specs.erase(specs.begin() + long(i) + 1);
+      }
+    }
     // ---- emit
     std::ostringstream src, bodies, kernels;
     src << "// generated by brian2-atlas_b200 for one AtlasIR model\n";
@@ -2008,7 +2088,9 @@ struct Engine::Impl {
         case OpSpec::Kind::Text:
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
-          else if (o.text == "exchange") kernels << gen_exchange(nm, int(o.index));
+          else if (o.text == "exchange")
+            kernels << gen_exchange(nm, int(o.index),
+                                    o.fuse_path >= 0 ? paths[size_t(o.fuse_path)].pathways : std::vector<PathwayDev*>{});
           else {
             std::string t = o.text;
             t.replace(t.find("@NAME@"), 6, nm);
@@ -2469,6 +2551,21 @@ struct Engine::Impl {
           for (uint64_t x = es.starts[rel]; x < es.starts[rel + 1]; ++x)
             pr.event_history[e].push_back({tick, es.ids[x]});
         }
+      }
+      // EventMonitors: every tick's list of their event (no window), or the
+      // previous tick's for a monitor scheduled before the event's producer
+      for (size_t k = 0; k < def.event_monitors.size(); ++k) {
+        b2dump::EventMonitorResult er;
+        const int sid = k < pd.evmon_stream.size() ? pd.evmon_stream[k] : -1;
+        if (sid >= 0) {
+          const EventStreamDev& es = streams[size_t(sid)];
+          const size_t lag = size_t(pd.evmon_lag[k]);
+          for (size_t rel = lag; rel < steps; ++rel)
+            for (uint64_t x = es.starts[rel - lag]; x < es.starts[rel - lag + 1]; ++x)
+              er.events.push_back({start_tick + rel, es.ids[x]});
+          check(er.events.size() <= 10'000'000, "EventMonitor recording budget exceeded");
+        }
+        pr.event_monitors.push_back(std::move(er));
       }
       pr.counts.assign(def.count, 0);
       auto spike_it = std::find(def.events.begin(), def.events.end(), "spike");

@@ -72,10 +72,54 @@ def write_model(model: dict, name: str) -> Path:
     return path
 
 
+def cuba_events(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 1000, seed: int = 6) -> dict:
+    """CUBA with a custom event `near` (v > -55 mV) and two EventMonitors: one
+    on `near` in the thresholds slot, one on `spike` in the start slot (which,
+    in the reference's schedule, records the previous tick's spikes)."""
+    import numpy as np
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    b.start_scope()
+    taum, taue, taui = 20 * b.ms, 5 * b.ms, 10 * b.ms
+    Vt, Vr, El = -50 * b.mV, -60 * b.mV, -49 * b.mV
+    eqs = """
+    dv/dt  = (ge+gi-(v-El))/taum : volt (unless refractory)
+    dge/dt = -ge/taue : volt
+    dgi/dt = -gi/taui : volt
+    """
+    clock = b.Clock(dt=0.1 * b.ms, name="clock")
+    P = b.NeuronGroup(n, eqs, threshold="v>Vt", reset="v = Vr", refractory=5 * b.ms, method="exact",
+                      events={"near": "v > -55*mV"}, name="neurons", clock=clock)
+    rng = np.random.default_rng(seed)
+    P.v = Vr + rng.random(n) * (Vt - Vr)
+    we, wi = (60 * 0.27 / 10) * b.mV, (-20 * 4.5 / 10) * b.mV
+    Ce = b.Synapses(P, P, on_pre="ge += we", name="exc", clock=clock)
+    Ci = b.Synapses(P, P, on_pre="gi += wi", name="inh", clock=clock)
+    ne = int(n * 0.8)
+    mask = rng.random((n, n)) < p
+    src, tgt = np.nonzero(mask)
+    e = src < ne
+    Ce.connect(i=src[e], j=tgt[e])
+    Ci.connect(i=src[~e], j=tgt[~e])
+    spikes = b.SpikeMonitor(P, name="spikes")
+    near = b.EventMonitor(P, "near", name="near_events")
+    late = b.EventMonitor(P, "spike", name="spike_events_at_start", when="start")
+    net = b.Network(P, Ce, Ci, spikes, near, late)
+    ns = dict(taum=taum, taue=taue, taui=taui, Vt=Vt, Vr=Vr, El=El, we=we, wi=wi)
+    return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", default=None, help="write just this model (cuba_events_small)")
     args = ap.parse_args()
+    if args.only:
+        prepare_frontend(Path(args.reference))
+        write_model(cuba_events(Path(args.reference)), args.only)
+        print("wrote", args.only)
+        return
     reference = Path(args.reference)
     golden = reference / "brian2-rust" / "tests" / "fixtures" / "reference-v1"
     dst = HERE / "reference-v1"

@@ -49,14 +49,15 @@ def test_rank_plans(pkg, world):
     for r in range(world):
         src = pkg.codegen(data, rank=r, world_size=world)
         names = kernels(src)
-        # the step publishes fired words; the exchange kernel expands them
-        assert [k.split("_", 2)[2] for k in names] == ["neurons_statemon", "neurons_step", "neurons_exchange",
-                                                      "exc_pre_inh_pre_atomic"] or r > 0
-        assert any(k.endswith("_exchange") for k in names)
+        # the step publishes fired words; the exchange kernel expands them and
+        # delivers the delay-0 constant-addend pathways in the same launch
+        assert [k.split("_", 2)[2] for k in names][-2:] == ["neurons_step",
+                                                           "neurons_exchange_exc_pre_inh_pre_atomic"]
         lo, hi = pkg.partition(n, r, world)
-        step = src[src.index("neurons_step("):src.index("neurons_exchange(")]
+        step = src[src.index("neurons_step("):src.index("neurons_exchange_")]
         assert f"i < {hi - lo}u" in step and "b2_ll_store" in step
-        assert "b2_ll_wait" in src[src.index("neurons_exchange("):]
+        exchange = src[src.index("neurons_exchange_"):]
+        assert "b2_ll_wait" in exchange and "atomicAdd(" in exchange
 
 
 def test_multi_gpu_capability_errors(pkg, tmp_path):

@@ -230,6 +230,12 @@ struct Engine::Impl {
   std::vector<SynDev> syns;
   int delivered_ptr = -1;
   size_t delivered_count = 0;
+  // per event stream: oldest ring position the host or a delayed consumer
+  // still needs (ring positions count per stream), read by the appending
+  // kernels' overflow checks
+  int floors_ptr = -1;
+  std::vector<uint64_t> floors_host_;
+  std::string floor_of(size_t sid) const { return P(floors_ptr, "const u64") + "[" + std::to_string(sid) + "]"; }
 
   // ---- kernels
   struct Op {
@@ -272,11 +278,20 @@ struct Engine::Impl {
     // entries per thread in constant-addend scatters (1..8).
     if (const char* e = std::getenv("B2GPU_BALANCE")) balance_tiles_ = std::atoi(e) != 0;
     if (const char* e = std::getenv("B2GPU_SCATTER_UNROLL")) scatter_unroll_ = unsigned(std::atoi(e));
+    if (const char* e = std::getenv("B2GPU_EXCHANGE_WPB")) exchange_wpb_ = unsigned(std::atoi(e));
+    if (const char* e = std::getenv("B2GPU_FUSE_EXCHANGE")) fuse_exchange_ = std::atoi(e) != 0;
     check(scatter_unroll_ >= 1 && scatter_unroll_ <= 8, "scatter unroll must be 1 to 8");
   }
   bool no_fuse_ = false;
   bool use_pdl_ = true;
   bool balance_tiles_ = true;                // tile_n_for: spread neurons over whole waves
+  // Multi-GPU exchange: words per block (0: about eight blocks per SM), and
+  // whether the exchange also delivers the delay-0 scatter of its stream.
+  // Measured on 2/4/8 B200s (C2): 256 words per block with a separate
+  // scatter kernel, 17.6/14.6/14.5 ms per 1000 ticks, against 20.3/17.7/17.6
+  // ms for eight blocks per SM with the scatter fused in.
+  unsigned exchange_wpb_ = kThreads;
+  bool fuse_exchange_ = false;
   unsigned scatter_unroll_ = kScatterUnroll;  // row entries per thread per scatter work item
   uint64_t row_chunk() const { return uint64_t(kThreads) * scatter_unroll_; }
 
@@ -761,6 +776,8 @@ struct Engine::Impl {
   size_t arena_bytes_of(int q) const { return arena_stage_off + stage_layout(q).bytes; }
 
   void build_streams() {
+    floors_host_.assign(std::max<size_t>(streams.size(), 1), 0);
+    floors_ptr = upload(floors_host_.data(), floors_host_.size() * 8);
     size_t x_bytes = kArenaHeaderBytes;
     for (auto& es : streams) {
       const PopDev& pd = pops[es.pop];
@@ -777,8 +794,8 @@ struct Engine::Impl {
         // spike generators emit their (global, precomputed) list on every rank
         es.exchanged = true;
         es.x_words = exchange_words(pd.global_count, world);
-        // about eight blocks per SM, at most one word per thread
-        es.x_wpb = std::clamp<uint64_t>((es.x_words + sm_count_ * 8 - 1) / (sm_count_ * 8), 1, kThreads);
+        es.x_wpb = exchange_wpb_ ? std::min<uint64_t>(exchange_wpb_, kThreads)
+                                 : std::clamp<uint64_t>((es.x_words + sm_count_ * 8 - 1) / (sm_count_ * 8), 1, kThreads);
         es.x_tiles = std::max<uint64_t>(1, (es.x_words + es.x_wpb - 1) / es.x_wpb);
         es.x_off = x_bytes;
         x_bytes += (2 * es.x_words * 8 + 255) / 256 * 256;
@@ -1208,7 +1225,8 @@ struct Engine::Impl {
       o << "  if (s_last) {\n    __threadfence();\n";
       o << "    b2_finalize_spikes<" << kThreads << ">(" << tiles << "u, " << tile_n << "u, " << P(es->tile_count, "const u32")
         << ", " << P(es->stage, "const u32") << ", " << P(es->ring, "u32") << ", " << u64lit(es->mask) << ", "
-        << P(es->tick_start, "u64") << ", rel, " << u64lit(es->cap) << ", ctl->ring_floor, err);\n  }\n";
+        << P(es->tick_start, "u64") << ", rel, " << u64lit(es->cap) << ", " << floor_of(size_t(pd.stream_of_event[x_event]))
+        << ", err);\n  }\n";
     }
     o << kernel_tail();
     return o.str();
@@ -1284,7 +1302,7 @@ struct Engine::Impl {
     o << "  if (s_last) {\n    __threadfence();\n";
     o << "    b2_finalize_spikes<" << kThreads << ">(" << es.x_tiles << "u, " << tile_n << "u, " << P(es.tile_count, "const u32")
       << ", " << P(es.stage, "const u32") << ", " << P(es.ring, "u32") << ", " << u64lit(es.mask) << ", "
-      << P(es.tick_start, "u64") << ", rel, " << u64lit(es.cap) << ", ctl->ring_floor, err);\n  }\n";
+      << P(es.tick_start, "u64") << ", rel, " << u64lit(es.cap) << ", " << floor_of(size_t(stream_id)) << ", err);\n  }\n";
     o << kernel_tail();
     return o.str();
   }
@@ -1368,7 +1386,7 @@ struct Engine::Impl {
     o << "  for (u64 j = a + threadIdx.x; j < b; j += blockDim.x) " << P(es.ring, "u32") << "[(base + j - a) & "
       << u64lit(es.mask) << "] = " << P(pd.gen_ids, "const u32") << "[j];\n";
     o << "  if (threadIdx.x == 0) {\n    " << P(es.tick_start, "u64") << "[rel + 1] = base + (b - a);\n";
-    o << "    if (base + (b - a) - ctl->ring_floor > " << u64lit(es.cap) << ") err |= " << kErrRing << "u;\n  }\n";
+    o << "    if (base + (b - a) - " << floor_of(size_t(stream_id)) << " > " << u64lit(es.cap) << ") err |= " << kErrRing << "u;\n  }\n";
     o << kernel_tail();
     return o.str();
   }
@@ -2063,7 +2081,7 @@ struct Engine::Impl {
     // Multi-GPU: an exchange directly followed by the delay-0
     // constant-addend scatter of the same stream delivers the spikes it
     // unpacks itself (gen_exchange), saving a kernel boundary per tick.
-    if (world > 1 && !no_fuse_) {
+    if (world > 1 && !no_fuse_ && fuse_exchange_) {
       for (size_t i = 0; i + 1 < specs.size(); ++i) {
         if (specs[i].text != "exchange" || specs[i + 1].kind != OpSpec::Kind::Path) continue;
         const PathSpec& ps = paths[specs[i + 1].index];
@@ -2209,7 +2227,6 @@ struct Engine::Impl {
   }
 
   uint64_t tick_host_ = 0;  // pageable staging: the copy is complete when the call returns
-  uint64_t floor_host_ = 0;
 
   void drain(size_t rel0, size_t rel1) {
     for (auto& es : streams) {
@@ -2234,16 +2251,15 @@ struct Engine::Impl {
   }
 
   void update_floor(size_t rel_now) {
-    // Oldest ring position any consumer may still read next chunk.
-    uint64_t floor = UINT64_MAX;
-    for (auto& es : streams) {
+    // Per stream, the oldest ring position a consumer may still read in the
+    // next chunk (everything older has been drained to the host).
+    for (size_t k = 0; k < streams.size(); ++k) {
+      const auto& es = streams[k];
       size_t back = rel_now > es.max_delay ? rel_now - es.max_delay : 0;
-      floor = std::min<uint64_t>(floor, es.starts.size() > back ? es.starts[back] : 0);
+      floors_host_[k] = es.starts.size() > back ? es.starts[back] : 0;
     }
-    if (floor == UINT64_MAX) floor = 0;
-    floor_host_ = floor;
-    B2_CUDA(cudaMemcpy(static_cast<char*>(ctl.ptr) + 16, &floor_host_, 8, cudaMemcpyHostToDevice));
-    st.h2d_bytes += 8;
+    B2_CUDA(cudaMemcpy(dptr(floors_ptr), floors_host_.data(), floors_host_.size() * 8, cudaMemcpyHostToDevice));
+    st.h2d_bytes += floors_host_.size() * 8;
   }
 
   // Per-kernel timing: direct launches bracketed by events (no graph).

@@ -38,7 +38,7 @@ struct RunCtl {
   u64 tick_base;      // absolute tick of graph step k == 0
   u32 error;          // OR of B2_ERR_* bits
   u32 pad0;
-  u64 ring_floor;     // oldest ring position the host still needs
+  u64 reserved1;
   u64 reserved;
 };
 

@@ -49,15 +49,14 @@ def test_rank_plans(pkg, world):
     for r in range(world):
         src = pkg.codegen(data, rank=r, world_size=world)
         names = kernels(src)
-        # the step publishes fired words; the exchange kernel expands them and
-        # delivers the delay-0 constant-addend pathways in the same launch
-        assert [k.split("_", 2)[2] for k in names][-2:] == ["neurons_step",
-                                                           "neurons_exchange_exc_pre_inh_pre_atomic"]
+        # the step publishes fired words; the exchange kernel expands them
+        # into the global list the scatter reads
+        assert [k.split("_", 2)[2] for k in names][-3:] == ["neurons_step", "neurons_exchange",
+                                                           "exc_pre_inh_pre_atomic"]
         lo, hi = pkg.partition(n, r, world)
-        step = src[src.index("neurons_step("):src.index("neurons_exchange_")]
+        step = src[src.index("neurons_step("):src.index("neurons_exchange(")]
         assert f"i < {hi - lo}u" in step and "b2_ll_store" in step
-        exchange = src[src.index("neurons_exchange_"):]
-        assert "b2_ll_wait" in exchange and "atomicAdd(" in exchange
+        assert "b2_ll_wait" in src[src.index("neurons_exchange("):]
 
 
 def test_multi_gpu_capability_errors(pkg, tmp_path):

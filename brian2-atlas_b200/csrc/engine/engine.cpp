@@ -226,8 +226,22 @@ struct Engine::Impl {
     std::map<std::string, double> param_const;
     std::vector<PathwayDev> pathways;
     bool identity_edges = true;  // row position == edge id for pre CSR
+    // `(summed)` variables in code-object order: the destination endpoint's
+    // CSR (rows = destination neurons, entries in edge creation order)
+    struct Summed {
+      size_t code = 0;            // code-object index
+      bool to_pre = false;
+      size_t dest_pop = 0, dest_state = 0, dest_start = 0, dest_count = 0;
+      int offsets = -1, row_other = -1, row_edge = -1;
+    };
+    std::vector<Summed> summed;
   };
   std::vector<SynDev> syns;
+  struct SummedSpec {
+    size_t synapse = 0, k = 0;
+    const Program* program = nullptr;
+    size_t result = 0;  // register of `_synaptic_var`
+  };
   int delivered_ptr = -1;
   size_t delivered_count = 0;
   // per event stream: oldest ring position the host or a delayed consumer
@@ -385,7 +399,7 @@ struct Engine::Impl {
       check(s.linked_variable_count == 0, "synaptic linked variables are not supported by the GPU engine");
       check(s.state_monitor_count == 0, "synapse state monitors are not supported by the GPU engine");
       for (const auto& c : s.code_objects)
-        check(c.kind == "synapses" || c.kind == "synapses_post",
+        check(c.kind == "synapses" || c.kind == "synapses_post" || c.kind == "summed_variable",
               "synapse code object kind '" + c.kind + "' is not supported by the GPU engine");
     }
     // one warp lane per destination rank stores a fired word: at most 32 ranks
@@ -744,6 +758,47 @@ struct Engine::Impl {
         pd.delivered_slot = int(delivered_count++);
         StreamUse(pd.stream, pd.max_delay);
         sd.pathways.push_back(std::move(pd));
+      }
+      // summed variables (executor.rs:3657-3731): each destination neuron
+      // adds its edges' values in edge creation order, so the device walks a
+      // CSR by destination with ascending edge ids per row
+      for (size_t c = 0; c < def.code_objects.size(); ++c) {
+        const auto& code = def.code_objects[c];
+        if (code.kind != "summed_variable") continue;
+        check(!procedural, "summed variables on procedural topologies are not supported by the GPU engine yet");
+        SynDev::Summed sv;
+        sv.code = c;
+        sv.to_pre = code.summed_target && *code.summed_target == "pre";
+        check(world == 1 || !sv.to_pre, "multi-GPU runs cannot sum into presynaptic neurons");
+        sv.dest_pop = sv.to_pre ? def.source_population : def.target_population;
+        sv.dest_start = sv.to_pre ? def.source_start : def.target_start;
+        sv.dest_count = sv.to_pre ? def.source_count : def.target_count;
+        const auto& dpop = m.populations[sv.dest_pop];
+        check(bool(code.summed_state), "missing summed target state");
+        sv.dest_state = dpop.states.size();
+        for (size_t k = 0; k < dpop.states.size(); ++k)
+          if (dpop.states[k].name == *code.summed_state) sv.dest_state = k;
+        check(sv.dest_state < dpop.states.size(), "missing summed target state");
+        const DType dt = dpop.states[sv.dest_state].dtype;
+        check(dt == DType::F64 || dt == DType::F32, "summed variables require floating-point state");
+        const auto& idx = sv.to_pre ? src_h : tgt_h;
+        const auto& other = sv.to_pre ? tgt_h : src_h;
+        const size_t L = sd.local_edges;
+        std::vector<uint64_t> offs(sv.dest_count + 1, 0);
+        for (size_t k = 0; k < L; ++k) offs[idx[gid(k)] + 1]++;
+        for (size_t i = 0; i < sv.dest_count; ++i) offs[i + 1] += offs[i];
+        std::vector<uint64_t> next(offs.begin(), offs.end() - 1);
+        std::vector<uint32_t> row_other(L), row_edge(L);
+        for (size_t k = 0; k < L; ++k) {  // ascending local edge == creation order
+          const size_t e = gid(k);
+          const uint64_t pos = next[idx[e]]++;
+          row_other[pos] = other[e];
+          row_edge[pos] = uint32_t(k);
+        }
+        sv.offsets = upload(offs.data(), offs.size() * 8);
+        sv.row_other = upload(row_other.data(), std::max<size_t>(L, 1) * 4);
+        sv.row_edge = upload(row_edge.data(), std::max<size_t>(L, 1) * 4);
+        sd.summed.push_back(sv);
       }
       syns.push_back(std::move(sd));
     }
@@ -1308,6 +1363,55 @@ struct Engine::Impl {
   }
 
 
+  // `(summed)` variable (run_summed_program, executor.rs:2548-2597): one
+  // thread per destination neuron this rank owns clears it and adds its
+  // edges' values in creation order, rounding each addition to the storage
+  // type (StateArray::add_f64, executor.rs:517-523).  Destinations are
+  // independent (a summed expression never reads its own summed variable),
+  // so the per-neuron order is the reference's whole order.
+  std::string gen_summed_body(const std::string& fname, const SummedSpec& ss) {
+    const auto& def = m.synapses[ss.synapse];
+    std::ostringstream o;
+    o << "__device__ __forceinline__ double " << fname << "(u32 src, u32 tgt, u64 edge, u64 tick, double t, u32& err) {\n";
+    o << "  const u64 src_state = (u64)src + " << def.source_start << "ull;\n";
+    o << "  const u64 tgt_state = (u64)tgt + " << target_bias(def) << "ull;\n";
+    o << "  (void)src_state; (void)tgt_state; (void)t; (void)tick; (void)edge;\n";
+    PathwayDev none;
+    o << emit_program(*ss.program, event_ctx(ss.synapse, none), "e_");
+    o << "  return " << reg_expr(*ss.program, ss.result, "e_") << ";\n}\n";
+    return o.str();
+  }
+
+  std::string gen_summed(const std::string& name, const std::string& body, const SummedSpec& ss) {
+    const SynDev::Summed& sv = syns[ss.synapse].summed[ss.k];
+    const PopDev& dp = pops[sv.dest_pop];
+    const DType dt = m.populations[sv.dest_pop].states[sv.dest_state].dtype;
+    const char* ct = storage_ctype(dt);
+    // destinations (synapse-level indices) whose neuron this rank owns
+    auto clampd = [&](uint64_t x) {
+      return x <= sv.dest_start ? uint64_t(0) : std::min<uint64_t>(x - sv.dest_start, sv.dest_count);
+    };
+    const uint64_t d0 = clampd(dp.lo), d1 = clampd(dp.lo + dp.count);
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  const u64 d = " << d0 << "ull + blockIdx.x * (u64)blockDim.x + threadIdx.x;\n";
+    o << "  if (d < " << d1 << "ull) {\n";
+    o << "    const u64* off = " << P(sv.offsets, "const u64") << ";\n";
+    o << "    const u32* other = " << P(sv.row_other, "const u32") << ";\n";
+    o << "    const u32* ed = " << P(sv.row_edge, "const u32") << ";\n";
+    o << "    " << ct << " acc = " << narrow(dt, "0.0") << ";\n";
+    o << "    for (u64 q = off[d]; q < off[d + 1]; ++q) {\n";
+    if (sv.to_pre)
+      o << "      const double v = " << body << "((u32)d, other[q], (u64)ed[q], tick, t, err);\n";
+    else
+      o << "      const double v = " << body << "(other[q], (u32)d, (u64)ed[q], tick, t, err);\n";
+    o << "      acc = " << narrow(dt, widen(dt, "acc") + " + v") << ";\n    }\n";
+    o << "    " << P(dp.states[sv.dest_state].ptr, ct) << "[d + " << uint64_t(sv.dest_start) - dp.lo << "ull] = acc;\n";
+    o << "  }\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
   // Reset over the tick's fired list (one thread per spike).
   std::string gen_reset(const std::string& name, size_t p, const Program& R, int stream_id) {
     const auto& def = m.populations[p];
@@ -1801,6 +1905,7 @@ struct Engine::Impl {
     int fuse_path = -1;  // exchange: PathSpec delivered inside the same kernel
   };
   std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
+  std::vector<SummedSpec> summed_specs;
   std::vector<Op> flush_ops;
   int deferred_flags = -1;                                  // per-population u64 tick of the last flush
   bool deferred_pending = false;
@@ -2006,6 +2111,37 @@ struct Engine::Impl {
         check(node.operation == b2ir::ScheduleOp::CodeObject, "synapse monitors are not supported by the GPU engine");
         size_t s = node.owner_index;
         const auto& code = code_of(node);
+        if (code.kind == "summed_variable") {
+          size_t k = 0;
+          while (k < syns[s].summed.size() && syns[s].summed[k].code != node.item_index) ++k;
+          check(k < syns[s].summed.size(), "missing summed-variable runtime program");
+          const SynDev::Summed& sv = syns[s].summed[k];
+          std::map<std::string, WriteTarget> writable;
+          auto inputs = synapse_inputs(s, true, writable);
+          inputs["dt"] = Input::constant(m.populations[sv.dest_pop].dt, DType::F64);
+          programs.push_back(Program::compile(code, inputs, {}, m.functions));
+          const Program& pr = programs.back();
+          auto res = pr.symbols.find("_synaptic_var");
+          check(res != pr.symbols.end(), "missing summed expression result");
+          for (const auto& b : pr.bindings) {
+            const bool own = b.second.index == sv.dest_state &&
+                             (sv.to_pre ? b.second.kind == Input::Kind::PreState : b.second.kind == Input::Kind::PostState);
+            check(!own, "a summed expression that reads its own summed variable is not supported by the GPU engine");
+            check(world == 1 || (b.second.kind != Input::Kind::PreState &&
+                                 !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre)),
+                  "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
+          }
+          check(world == 1 || !pr.uses_rng(), "multi-GPU runs do not support random draws in synaptic code ('" + code.name + "')");
+          OpSpec o;
+          o.base = code.name;
+          o.text = "summed";
+          o.index = summed_specs.size();
+          const PopDev& dp = pops[sv.dest_pop];
+          o.grid = unsigned(std::max<size_t>(1, (dp.count + kThreads - 1) / kThreads));
+          summed_specs.push_back({s, k, &pr, res->second});
+          specs.push_back(o);
+          continue;
+        }
         check(bool(code.pathway_name), "scheduled pathway has no name");
         const auto& pws = m.synapse_instances[s].pathways;
         size_t pos = pws.size();
@@ -2106,7 +2242,12 @@ struct Engine::Impl {
         case OpSpec::Kind::Text:
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
-          else if (o.text == "exchange")
+          else if (o.text == "summed") {
+            const SummedSpec& ss = summed_specs[o.index];
+            std::string body = "b2_summed_" + std::to_string(kid);
+            bodies << gen_summed_body(body, ss);
+            kernels << gen_summed(nm, body, ss);
+          } else if (o.text == "exchange")
             kernels << gen_exchange(nm, int(o.index),
                                     o.fuse_path >= 0 ? paths[size_t(o.fuse_path)].pathways : std::vector<PathwayDev*>{});
           else {

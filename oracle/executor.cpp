@@ -953,10 +953,20 @@ struct PathwayRuntime {
   std::vector<size_t> active_sources;
 };
 
+// SummedRuntime (executor.rs:1417-1426): the program of one `(summed)`
+// variable, the register of its `_synaptic_var` result and the endpoint
+// state it accumulates into.
+struct SummedRuntime {
+  Program program;
+  size_t result = 0, target_population = 0, target_start = 0, target_count = 0, target_state = 0;
+  bool target_is_pre = false;
+};
+
 struct SynapseRuntime {
   std::vector<size_t> source, target;
   std::vector<StateArray> states;
   std::vector<PathwayRuntime> pathways;
+  std::vector<SummedRuntime> summed;  // in code-object order
 };
 
 std::shared_ptr<const std::vector<double>> decode_values(const EncodedArray& a) {
@@ -1295,8 +1305,32 @@ struct Runtime {
     for (const auto& [alias, state] : def.post_state_aliases)
       post_writable[alias] = WriteTarget{WriteTarget::Kind::Neuron, tgt_idx.at(state)};
     for (const auto& c : def.code_objects)
-      check(c.kind == "synapses" || c.kind == "synapses_post",
+      check(c.kind == "synapses" || c.kind == "synapses_post" || c.kind == "summed_variable",
             "synapse code object kind '" + c.kind + "' is outside the oracle's subset");
+    // summed variables (executor.rs:3657-3731): compiled with no writable
+    // symbol; `_synaptic_var` is the per-edge value
+    for (const auto& c : def.code_objects) {
+      if (c.kind != "summed_variable") continue;
+      const bool to_pre = c.summed_target && *c.summed_target == "pre";
+      const size_t tp = to_pre ? def.source_population : def.target_population;
+      const PopulationDef& tdef = m.populations[tp];
+      check(bool(c.summed_state), "missing summed target state");
+      size_t ts = tdef.states.size();
+      for (size_t i = 0; i < tdef.states.size(); ++i)
+        if (tdef.states[i].name == *c.summed_state) ts = i;
+      check(ts < tdef.states.size(), "missing summed target state");
+      check(tdef.states[ts].dtype == DType::F64 || tdef.states[ts].dtype == DType::F32,
+            "summed variables require floating-point state");
+      auto sin = inputs;
+      sin["dt"] = Input::constant(tdef.dt, DType::F64);
+      SummedRuntime sr{Program::compile(c, sin, {}, m.rng_seed, m.functions), 0, tp,
+                       to_pre ? def.source_start : def.target_start, to_pre ? def.source_count : def.target_count, ts,
+                       to_pre};
+      auto r = sr.program.symbols.find("_synaptic_var");
+      check(r != sr.program.symbols.end(), "missing summed expression result");
+      sr.result = r->second;
+      rt.summed.push_back(std::move(sr));
+    }
     for (size_t k = 0; k < inst.pathways.size(); ++k) {
       const PathwayInstance& pw = inst.pathways[k];
       bool is_pre = pw.kind == "pre";
@@ -1344,6 +1378,31 @@ struct Runtime {
     prog.run(tp.states, sp.states, tp.states, syn.states, refr, b);
     // Same-population pathways write pre and post aliases into one table.
     prog.commit_event(&sp.states, tp.states, syn.states, b.source_state, b.target_state, edge);
+  }
+
+  // run_summed_program (executor.rs:2548-2597): clear the endpoint range,
+  // then add each edge's value in creation order (f32 targets round each
+  // addition, StateArray::add_f64 executor.rs:517-523)
+  void run_summed(SummedRuntime& s, const SynapseDef& def, SynapseRuntime& syn, double time) {
+    PopulationRuntime& dest_pop = populations[s.target_population];
+    StateArray& dest = dest_pop.states[s.target_state];
+    for (size_t i = s.target_start; i < s.target_start + s.target_count; ++i) dest.set(i, 0.0);
+    s.program.prepare(time, dest_pop.tick);
+    PopulationRuntime& sp = populations[def.source_population];
+    PopulationRuntime& tp = populations[def.target_population];
+    const RefractoryRuntime* refr = tp.refractory ? &*tp.refractory : nullptr;
+    for (size_t edge = 0; edge < syn.source.size(); ++edge) {
+      Batch b;
+      b.len = 1;
+      b.source = syn.source[edge];
+      b.target = syn.target[edge];
+      b.source_state = b.source + def.source_start;
+      b.target_state = b.target + def.target_start;
+      b.edge = edge;
+      s.program.run(tp.states, sp.states, tp.states, syn.states, refr, b);
+      const size_t at = s.target_is_pre ? b.source_state : b.target_state;
+      dest.set(at, dest.get(at) + s.program.registers[s.result][0]);
+    }
   }
 
   // run_pathway (executor.rs:2292-2382)
@@ -1563,6 +1622,14 @@ struct Runtime {
           check(node.operation == ScheduleOp::CodeObject, "synapse monitors are outside the oracle's subset");
           const SynapseDef& def = m.synapses[node.owner_index];
           const CodeObject& code = def.code_objects[node.item_index];
+          if (code.kind == "summed_variable") {
+            size_t position = 0;
+            for (size_t k = 0; k < node.item_index; ++k) position += def.code_objects[k].kind == "summed_variable";
+            SynapseRuntime& syn = synapses[node.owner_index];
+            check(position < syn.summed.size(), "missing summed-variable runtime program");
+            run_summed(syn.summed[position], def, syn, time);
+            continue;
+          }
           check(code.kind == "synapses" || code.kind == "synapses_post", "unsupported scheduled synapse operation");
           check(bool(code.pathway_name), "scheduled pathway has no name");
           const auto& pws = m.synapse_instances[node.owner_index].pathways;

@@ -110,14 +110,56 @@ def cuba_events(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 1000
     return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
 
 
+def gap_junctions(reference: Path, n: int = 300, p: float = 0.05, ticks: int = 1000, seed: int = 7) -> dict:
+    """Brian's gap-junction network: a `(summed)` synaptic current into the
+    target, recomputed from pre/post voltages every tick, plus per-edge
+    weights, threshold and reset."""
+    import numpy as np
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    b.start_scope()
+    clock = b.Clock(dt=0.1 * b.ms, name="clock")
+    eqs = """
+    dv/dt = (v0 - v + Igap) / tau : 1
+    Igap : 1
+    v0 : 1
+    """
+    P = b.NeuronGroup(n, eqs, threshold="v > 1", reset="v = 0", method="euler", name="neurons", clock=clock)
+    rng = np.random.default_rng(seed)
+    P.v0 = np.linspace(0.0, 1.5, n)
+    P.v = rng.random(n)
+    S = b.Synapses(P, P, """
+                   w : 1
+                   Igap_post = w * (v_pre - v_post) : 1 (summed)
+                   """, name="gaps", clock=clock)
+    mask = rng.random((n, n)) < p
+    np.fill_diagonal(mask, False)
+    src, tgt = np.nonzero(mask)
+    S.connect(i=src, j=tgt)
+    S.w = 0.02 + 0.02 * rng.random(len(src))
+    spikes = b.SpikeMonitor(P, name="spikes")
+    trace = b.StateMonitor(P, ["v", "Igap"], record=[0, n // 2, n - 1], name="trace", clock=clock)
+    net = b.Network(P, S, spikes, trace)
+    ns = dict(tau=10 * b.ms)
+    model = lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+    # Brian2's numpy runtime on the same network: the oracle's independent pin
+    b.prefs.codegen.target = "numpy"
+    net.run(ticks * 0.1 * b.ms, namespace=ns)
+    np.savez_compressed(HERE / "brian_numpy" / "gap_junctions_small.npz", spike_i=np.array(spikes.i[:]),
+                        spike_t=np.array(spikes.t / b.second), v=np.array(P.v[:]), Igap=np.array(P.Igap[:]))
+    return model
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
-    ap.add_argument("--only", default=None, help="write just this model (cuba_events_small)")
+    ap.add_argument("--only", default=None, help="write just this model (cuba_events_small, gap_junctions_small)")
     args = ap.parse_args()
     if args.only:
         prepare_frontend(Path(args.reference))
-        write_model(cuba_events(Path(args.reference)), args.only)
+        make = {"cuba_events_small": cuba_events, "gap_junctions_small": gap_junctions}[args.only]
+        write_model(make(Path(args.reference)), args.only)
         print("wrote", args.only)
         return
     reference = Path(args.reference)

@@ -20,7 +20,8 @@ from b2results import load_model, read_results
 
 pytestmark = pytest.mark.gpu
 
-EXACT = ["cuba_small", "cuba_poisson_small", "brunel_small"]
+# gap_junctions_small: a `(summed)` synaptic current recomputed every tick
+EXACT = ["cuba_small", "cuba_poisson_small", "brunel_small", "gap_junctions_small"]
 
 
 def gpu_run(pkg, model_path, outdir, **kw):

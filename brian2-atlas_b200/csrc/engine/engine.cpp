@@ -235,6 +235,9 @@ struct Engine::Impl {
       int offsets = -1, row_other = -1, row_edge = -1;
     };
     std::vector<Summed> summed;
+    // per-edge endpoints (synapse-level source and target of each local
+    // edge) for programs that run over every edge
+    int edge_src = -1, edge_tgt = -1;
   };
   std::vector<SynDev> syns;
   struct SummedSpec {
@@ -399,7 +402,9 @@ struct Engine::Impl {
       check(s.linked_variable_count == 0, "synaptic linked variables are not supported by the GPU engine");
       check(s.state_monitor_count == 0, "synapse state monitors are not supported by the GPU engine");
       for (const auto& c : s.code_objects)
-        check(c.kind == "synapses" || c.kind == "synapses_post" || c.kind == "summed_variable",
+        check(c.kind == "synapses" || c.kind == "synapses_post" || c.kind == "summed_variable" ||
+                  c.kind == "synapse_state_update" || c.kind == "synapse_subexpression_update" ||
+                  c.kind == "synapse_run_regularly",
               "synapse code object kind '" + c.kind + "' is not supported by the GPU engine");
     }
     // one warp lane per destination rank stores a fired word: at most 32 ranks
@@ -758,6 +763,22 @@ struct Engine::Impl {
         pd.delivered_slot = int(delivered_count++);
         StreamUse(pd.stream, pd.max_delay);
         sd.pathways.push_back(std::move(pd));
+      }
+      // per-edge programs (synapse_state_update / _subexpression_update /
+      // _run_regularly) visit every edge with its endpoints
+      bool edge_programs = false;
+      for (const auto& code : def.code_objects)
+        edge_programs |= code.kind == "synapse_state_update" || code.kind == "synapse_subexpression_update" ||
+                         code.kind == "synapse_run_regularly";
+      if (edge_programs) {
+        check(!procedural, "synapse state updates on procedural topologies are not supported by the GPU engine yet");
+        std::vector<uint32_t> es(sd.local_edges), et(sd.local_edges);
+        for (size_t k = 0; k < sd.local_edges; ++k) {
+          es[k] = src_h[gid(k)];
+          et[k] = tgt_h[gid(k)];
+        }
+        sd.edge_src = upload(es.data(), std::max<size_t>(es.size(), 1) * 4);
+        sd.edge_tgt = upload(et.data(), std::max<size_t>(et.size(), 1) * 4);
       }
       // summed variables (executor.rs:3657-3731): each destination neuron
       // adds its edges' values in edge creation order, so the device walks a
@@ -1555,7 +1576,10 @@ struct Engine::Impl {
     return c;
   }
 
-  std::string gen_pathway_body(const std::string& fname, size_t s, const PathwayDev& pw, const Program& pr) {
+  // synapse_only: commit only synapse-state writes (commit_synapses,
+  // executor.rs:5615-5623), as per-edge update programs do
+  std::string gen_pathway_body(const std::string& fname, size_t s, const PathwayDev& pw, const Program& pr,
+                               bool synapse_only = false) {
     const auto& def = m.synapses[s];
     const SynDev& sd = syns[s];
     std::ostringstream o;
@@ -1569,6 +1593,7 @@ struct Engine::Impl {
     const auto& tgt = m.populations[def.target_population];
     for (const auto& [w, r] : pr.writes) {
       std::string v = reg_expr(pr, r, "e_");
+      if (synapse_only && w.kind != WriteTarget::Kind::Synapse) continue;
       switch (w.kind) {
         case WriteTarget::Kind::Neuron: {
           DType d = tgt.states[w.index].dtype;
@@ -1906,6 +1931,11 @@ struct Engine::Impl {
   };
   std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
   std::vector<SummedSpec> summed_specs;
+  struct SynProgSpec {
+    size_t synapse = 0;
+    const Program* program = nullptr;
+  };
+  std::vector<SynProgSpec> synprog_specs;
   std::vector<Op> flush_ops;
   int deferred_flags = -1;                                  // per-population u64 tick of the last flush
   bool deferred_pending = false;
@@ -2111,6 +2141,40 @@ struct Engine::Impl {
         check(node.operation == b2ir::ScheduleOp::CodeObject, "synapse monitors are not supported by the GPU engine");
         size_t s = node.owner_index;
         const auto& code = code_of(node);
+        if (code.kind == "synapse_state_update" || code.kind == "synapse_subexpression_update" ||
+            code.kind == "synapse_run_regularly") {
+          // run_synapse_program (executor.rs:2513-2546): every edge, only
+          // synapse-state writes committed; edges are independent (a program
+          // reads neuron state, which it cannot write, and its own edge's
+          // synapse state), so one thread per edge reproduces the edge loop
+          const auto& def = m.synapses[s];
+          std::map<std::string, WriteTarget> writable;
+          auto inputs = synapse_inputs(s, true, writable);
+          if (code.kind == "synapse_state_update") {
+            std::map<std::string, WriteTarget> clock_driven;
+            for (const auto& name : def.clock_driven_states)
+              for (size_t k = 0; k < def.states.size(); ++k)
+                if (def.states[k].name == name) clock_driven[name] = WriteTarget{WriteTarget::Kind::Synapse, k};
+            writable = clock_driven;
+          }
+          programs.push_back(Program::compile(code, inputs, writable, m.functions));
+          const Program& pr = programs.back();
+          if (world > 1) {
+            for (const auto& b : pr.bindings)
+              check(b.second.kind != Input::Kind::PreState &&
+                        !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre),
+                    "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
+            check(!pr.uses_rng(), "multi-GPU runs do not support random draws in synaptic code ('" + code.name + "')");
+          }
+          OpSpec o;
+          o.base = code.name;
+          o.text = "synprog";
+          o.index = synprog_specs.size();
+          o.grid = unsigned(std::max<uint64_t>(1, (syns[s].local_edges + kThreads - 1) / kThreads));
+          synprog_specs.push_back({s, &pr});
+          specs.push_back(o);
+          continue;
+        }
         if (code.kind == "summed_variable") {
           size_t k = 0;
           while (k < syns[s].summed.size() && syns[s].summed[k].code != node.item_index) ++k;
@@ -2242,7 +2306,20 @@ struct Engine::Impl {
         case OpSpec::Kind::Text:
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
-          else if (o.text == "summed") {
+          else if (o.text == "synprog") {
+            const SynProgSpec& sp = synprog_specs[o.index];
+            std::string body = "b2_synprog_" + std::to_string(kid);
+            PathwayDev none;
+            bodies << gen_pathway_body(body, sp.synapse, none, *sp.program, true);
+            const SynDev& sd = syns[sp.synapse];
+            std::ostringstream k;
+            k << kernel_head(nm);
+            k << "  const u64 e = blockIdx.x * (u64)blockDim.x + threadIdx.x;\n";
+            k << "  if (e < " << sd.local_edges << "ull) " << body << "(" << P(sd.edge_src, "const u32") << "[e], "
+              << P(sd.edge_tgt, "const u32") << "[e], e, tick, t, err);\n";
+            k << kernel_tail();
+            kernels << k.str();
+          } else if (o.text == "summed") {
             const SummedSpec& ss = summed_specs[o.index];
             std::string body = "b2_summed_" + std::to_string(kid);
             bodies << gen_summed_body(body, ss);

@@ -889,6 +889,11 @@ struct Program {
       if (t.kind == WriteTarget::Kind::Available)
         for (size_t l = 0; l < len; ++l) refr.not_refractory[start + l] = registers[r][l] != 0.0;
   }
+  // commit_synapses (executor.rs:5615-5623): only synapse-state writes
+  void commit_synapses(std::vector<StateArray>& syn, size_t edge) const {
+    for (const auto& [t, r] : writes)
+      if (t.kind == WriteTarget::Kind::Synapse) syn[t.index].set(edge, registers[r][0]);
+  }
   void commit_event(std::vector<StateArray>* pre, std::vector<StateArray>& post,
                     std::vector<StateArray>& syn, size_t source_neuron, size_t target_neuron,
                     size_t edge) const {
@@ -967,6 +972,12 @@ struct SynapseRuntime {
   std::vector<StateArray> states;
   std::vector<PathwayRuntime> pathways;
   std::vector<SummedRuntime> summed;  // in code-object order
+  // per-edge programs run over every edge (executor.rs:3612-3653):
+  // synapse_state_update (clock-driven states writable),
+  // synapse_subexpression_update and synapse_run_regularly (all writable,
+  // but only synapse states are committed)
+  std::optional<Program> update, subexpression;
+  std::vector<Program> regular;  // in code-object order
 };
 
 std::shared_ptr<const std::vector<double>> decode_values(const EncodedArray& a) {
@@ -1305,8 +1316,25 @@ struct Runtime {
     for (const auto& [alias, state] : def.post_state_aliases)
       post_writable[alias] = WriteTarget{WriteTarget::Kind::Neuron, tgt_idx.at(state)};
     for (const auto& c : def.code_objects)
-      check(c.kind == "synapses" || c.kind == "synapses_post" || c.kind == "summed_variable",
+      check(c.kind == "synapses" || c.kind == "synapses_post" || c.kind == "summed_variable" ||
+                c.kind == "synapse_state_update" || c.kind == "synapse_subexpression_update" ||
+                c.kind == "synapse_run_regularly",
             "synapse code object kind '" + c.kind + "' is outside the oracle's subset");
+    {
+      std::map<std::string, WriteTarget> clock_driven;
+      for (const auto& name : def.clock_driven_states) {
+        check(syn_idx.count(name) > 0, "clock-driven state is not a synapse state");
+        clock_driven[name] = WriteTarget{WriteTarget::Kind::Synapse, syn_idx.at(name)};
+      }
+      for (const auto& c : def.code_objects) {
+        if (c.kind == "synapse_state_update" && !rt.update)
+          rt.update = Program::compile(c, inputs, clock_driven, m.rng_seed, m.functions);
+        else if (c.kind == "synapse_subexpression_update" && !rt.subexpression)
+          rt.subexpression = Program::compile(c, inputs, writable, m.rng_seed, m.functions);
+        else if (c.kind == "synapse_run_regularly")
+          rt.regular.push_back(Program::compile(c, inputs, writable, m.rng_seed, m.functions));
+      }
+    }
     // summed variables (executor.rs:3657-3731): compiled with no writable
     // symbol; `_synaptic_var` is the per-edge value
     for (const auto& c : def.code_objects) {
@@ -1378,6 +1406,26 @@ struct Runtime {
     prog.run(tp.states, sp.states, tp.states, syn.states, refr, b);
     // Same-population pathways write pre and post aliases into one table.
     prog.commit_event(&sp.states, tp.states, syn.states, b.source_state, b.target_state, edge);
+  }
+
+  // run_synapse_program (executor.rs:2513-2546): every edge in creation
+  // order, committing only synapse-state writes
+  void run_synapse_program(Program& prog, const SynapseDef& def, SynapseRuntime& syn, double time, size_t tick) {
+    prog.prepare(time, tick);
+    PopulationRuntime& sp = populations[def.source_population];
+    PopulationRuntime& tp = populations[def.target_population];
+    const RefractoryRuntime* refr = tp.refractory ? &*tp.refractory : nullptr;
+    for (size_t edge = 0; edge < syn.source.size(); ++edge) {
+      Batch b;
+      b.len = 1;
+      b.source = syn.source[edge];
+      b.target = syn.target[edge];
+      b.source_state = b.source + def.source_start;
+      b.target_state = b.target + def.target_start;
+      b.edge = edge;
+      prog.run(tp.states, sp.states, tp.states, syn.states, refr, b);
+      prog.commit_synapses(syn.states, edge);
+    }
   }
 
   // run_summed_program (executor.rs:2548-2597): clear the endpoint range,
@@ -1622,6 +1670,21 @@ struct Runtime {
           check(node.operation == ScheduleOp::CodeObject, "synapse monitors are outside the oracle's subset");
           const SynapseDef& def = m.synapses[node.owner_index];
           const CodeObject& code = def.code_objects[node.item_index];
+          if (code.kind == "synapse_state_update" || code.kind == "synapse_subexpression_update" ||
+              code.kind == "synapse_run_regularly") {
+            SynapseRuntime& syn = synapses[node.owner_index];
+            Program* prog = nullptr;
+            if (code.kind == "synapse_state_update") prog = syn.update ? &*syn.update : nullptr;
+            else if (code.kind == "synapse_subexpression_update") prog = syn.subexpression ? &*syn.subexpression : nullptr;
+            else {
+              size_t position = 0;
+              for (size_t k = 0; k < node.item_index; ++k) position += def.code_objects[k].kind == "synapse_run_regularly";
+              if (position < syn.regular.size()) prog = &syn.regular[position];
+            }
+            check(prog != nullptr, "missing synapse program");
+            run_synapse_program(*prog, def, syn, time, clock_ticks[node.clock]);
+            continue;
+          }
           if (code.kind == "summed_variable") {
             size_t position = 0;
             for (size_t k = 0; k < node.item_index; ++k) position += def.code_objects[k].kind == "summed_variable";

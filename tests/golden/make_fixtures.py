@@ -151,6 +151,55 @@ def gap_junctions(reference: Path, n: int = 300, p: float = 0.05, ticks: int = 1
     return model
 
 
+def synapse_updates(reference: Path, n_in: int = 200, n_out: int = 50, p: float = 0.2, ticks: int = 1000,
+                    seed: int = 8) -> dict:
+    """STDP with clock-driven synaptic traces (a synapse state updater every
+    tick) and a synaptic run_regularly, driven by a PoissonGroup."""
+    import numpy as np
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    b.start_scope()
+    b.defaultclock.dt = 0.1 * b.ms  # one clock for every object (the generator keeps its default schedule)
+    rng = np.random.default_rng(seed)
+    # deterministic periodic inputs (integrators with seeded rates and
+    # phases), so Brian2's numpy runtime sees exactly the same input
+    inputs = b.NeuronGroup(n_in, "dv/dt = r : 1\nr : Hz", threshold="v > 1", reset="v = 0", method="euler",
+                           name="inputs")
+    inputs.r = (20 + 40 * rng.random(n_in)) * b.Hz
+    inputs.v = rng.random(n_in)
+    G = b.NeuronGroup(n_out, """
+                      dv/dt = (ge - v) / (10*ms) : 1
+                      dge/dt = -ge / (5*ms) : 1
+                      """, threshold="v > 0.3", reset="v = 0", method="exact", name="neurons")
+    S = b.Synapses(inputs, G, """
+                   w : 1
+                   dApre/dt = -Apre / (20*ms) : 1 (clock-driven)
+                   dApost/dt = -Apost / (20*ms) : 1 (clock-driven)
+                   """, on_pre="""
+                   ge += w
+                   Apre += 0.01
+                   w = clip(w + Apost, 0, 0.2)
+                   """, on_post="""
+                   Apost -= 0.0105
+                   w = clip(w + Apre, 0, 0.2)
+                   """, method="exact", name="stdp")
+    mask = rng.random((n_in, n_out)) < p
+    src, tgt = np.nonzero(mask)
+    S.connect(i=src, j=tgt)
+    S.w = 0.1 * rng.random(len(src))
+    S.run_regularly("w = w * 0.9999", name="decay")
+    spikes = b.SpikeMonitor(G, name="spikes")
+    net = b.Network(inputs, G, S, spikes)
+    model = lower_network(net, ticks * 0.1 * b.ms, rng_seed=seed)
+    b.prefs.codegen.target = "numpy"
+    net.run(ticks * 0.1 * b.ms)
+    np.savez_compressed(HERE / "brian_numpy" / "synapse_updates_small.npz", spike_i=np.array(spikes.i[:]),
+                        spike_t=np.array(spikes.t / b.second), v=np.array(G.v[:]), w=np.array(S.w[:]),
+                        Apre=np.array(S.Apre[:]), Apost=np.array(S.Apost[:]))
+    return model
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -158,7 +207,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.only:
         prepare_frontend(Path(args.reference))
-        make = {"cuba_events_small": cuba_events, "gap_junctions_small": gap_junctions}[args.only]
+        make = {"cuba_events_small": cuba_events, "gap_junctions_small": gap_junctions,
+                "synapse_updates_small": synapse_updates}[args.only]
         write_model(make(Path(args.reference)), args.only)
         print("wrote", args.only)
         return

@@ -76,3 +76,23 @@ def test_oracle_synaptic_events_equal_outdegree_of_spikes(oracle, tmp_path):
         outdeg = np.bincount(np.asarray(syn["source"]), minlength=model["definition"]["populations"][0]["count"])
         total += int(outdeg[spikes[:, 1]].sum())
     assert sum(res.delivered) == total
+
+
+def test_oracle_synapse_updates_match_brian_numpy(oracle, tmp_path):
+    """Clock-driven synaptic traces (synapse_state_update every tick), a
+    synaptic run_regularly and STDP pathways, against Brian2's numpy runtime
+    on the same network (deterministic inputs): output spikes exact, weights
+    and traces within 1e-12."""
+    model_path = MODELS / "synapse_updates_small.json"
+    out = run_oracle(oracle, model_path, tmp_path / "out")
+    res = read_results(out, load_model(model_path))
+    ref = np.load(GOLDEN / "brian_numpy" / "synapse_updates_small.npz")
+    spikes = res.populations[1].spikes
+    ticks = np.rint(ref["spike_t"] / 1e-4).astype(np.int64)
+    order = np.lexsort((ref["spike_i"], ticks))
+    assert len(spikes) == len(ticks) > 0
+    np.testing.assert_array_equal(spikes[:, 0], ticks[order])
+    np.testing.assert_array_equal(spikes[:, 1], ref["spike_i"][order])
+    np.testing.assert_allclose(res.populations[1].states["v"], ref["v"], rtol=1e-12, atol=1e-18)
+    for name in ("w", "Apre", "Apost"):
+        np.testing.assert_allclose(res.synapse_states[0][name], ref[name], rtol=1e-12, atol=1e-18)

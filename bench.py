@@ -54,6 +54,16 @@ METRIC = "synaptic events/s"
 UNIT = "events/s"
 
 
+# DRAM bytes (read + write) per launch of the neuron step kernel on the
+# default 1M-neuron network, from one ncu capture (dram__bytes_read.sum +
+# dram__bytes_write.sum, warm cache as in the timed run; the step kernel's
+# traffic does not depend on the in-degree, so the 1M-neuron in-degree-300
+# capture stands for the full network): 74,624 + 507,904 bytes.  The 56 MB of
+# per-tick neuron state stays L2-resident within a step, so DRAM carries ~1 %
+# of the algorithmic bytes.  None for other workloads.
+STEP_DRAM_BYTES = {1_000_000: 74_624 + 507_904}
+
+
 def peaks():
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
@@ -316,7 +326,8 @@ def main():
         "gpu_launches": launches,
         "roofline": None if dominant is None else {
             "bound": "hbm", "kernel": dominant["name"], "achieved": dominant["achieved_gbs"], "peak": hbm,
-            "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["achieved_gbs"] / hbm, "traffic": None},
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["achieved_gbs"] / hbm,
+            "traffic": STEP_DRAM_BYTES.get(local_neurons) if "_step" in dominant["name"] and world == 1 else None},
         "kernels": kernels,
         "clocks": clock_summary,
         "build": {"json_seconds": t_json, "engine_build_seconds": st0["build_seconds"],

@@ -1079,6 +1079,7 @@ struct Engine::Impl {
     c.tick = "tick";
     c.time = "t";
     c.tables = &const_tables;
+    c.device_array = [this](const std::vector<double>& v) { return device_table(v); };
     for (auto& ix : c.index_for_domain) ix = gi;
     return c;
   }
@@ -1905,6 +1906,13 @@ struct Engine::Impl {
 
   std::vector<Program> programs;  // owned programs (stable addresses via reserve)
   std::map<std::string, std::string> const_tables;  // file-scope tables referenced by emitted code
+  std::map<const double*, int> device_tables;       // uploaded TimedArray tables by source array
+  std::string device_table(const std::vector<double>& v) {
+    auto it = device_tables.find(v.data());
+    if (it == device_tables.end())
+      it = device_tables.emplace(v.data(), upload(v.data(), std::max<size_t>(v.size(), 1) * 8)).first;
+    return P(it->second, "const double");
+  }
 
   // A kernel in the tick, generated once the whole schedule is analysed.
   struct StepSpec {

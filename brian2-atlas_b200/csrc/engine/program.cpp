@@ -28,7 +28,7 @@ inline double from_bits(uint64_t r) {
 }
 // Error bits; keep in sync with device_lib.cuh.
 constexpr uint32_t ERR_NONFINITE = 0x1, ERR_TIMESTEP = 0x2, ERR_BINOMIAL = 0x4, ERR_POISSON = 0x8,
-                   ERR_INTDIV = 0x40, ERR_CAST = 0x100;
+                   ERR_INTDIV = 0x40, ERR_TIMEDARRAY = 0x80, ERR_CAST = 0x100;
 }  // namespace
 
 DType Input::type() const {
@@ -210,8 +210,14 @@ size_t Program::expression(const Expr& e, long guard, std::vector<Instr>& ops) {
       ins.domain = rng_domain;
       ins.left = ins.right = expression(*e.args[0], guard, ops);
       break;
-    case Op::TimedArray:
-      throw Error("TimedArray is not supported by the GPU engine yet");
+    case Op::TimedArray: {
+      ins.op = IOp::TimedArray;
+      ins.ta = &e;
+      const size_t t = expression(*e.args[0], guard, ops);
+      ins.left = t;
+      ins.right = e.args.size() > 1 ? expression(*e.args[1], guard, ops) : t;
+      break;
+    }
     case Op::F64ToF32:
       ins.op = IOp::RoundF32;
       ins.left = ins.right = expression(*e.args[0], guard, ops);
@@ -634,7 +640,7 @@ void Program::classify() {
       // result depends on the guard.
       RegKind k = std::max({L.kind, R.kind, T.kind});
       if (in.op == IOp::Select) k = std::max(k, G.kind);
-      if (in.op == IOp::Binomial || in.op == IOp::Poisson) k = RegKind::Lane;
+      if (in.op == IOp::Binomial || in.op == IOp::Poisson || in.op == IOp::TimedArray) k = RegKind::Lane;
       RegInfo& out = regs[in.output];
       assigned[in.output] = true;
       if (k == RegKind::Const) {
@@ -1030,7 +1036,21 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
                  ", " + a + ")";
           break;
         }
-        case IOp::TimedArray: throw Error("TimedArray is not supported by the GPU engine yet");
+        case IOp::TimedArray: {
+          // Op::TimedArray (executor.rs:6121-6154): row from the time, column
+          // from the index, both range-checked; a non-finite value is an error
+          check(bool(ctx.device_array), "TimedArray needs device tables");
+          const b2ir::Expr& ta = *in.ta;
+          const uint64_t width = ta.ta_columns >= 0 ? uint64_t(ta.ta_columns) : 1;
+          check(ta.ta_rows > 0 && ta.ta_values.size() == ta.ta_rows * width, "TimedArray table has the wrong size");
+          check_bit = ERR_TIMEDARRAY;
+          check_finite = true;
+          expr = "b2_timed_array(" + ctx.device_array(ta.ta_values) + ", " + std::to_string(ta.ta_rows) + "ull, " +
+                 std::to_string(width) + "ull, " + (ta.ta_columns >= 0 ? "true" : "false") + ", " +
+                 double_literal(ta.ta_epsilon) + ", " + double_literal(double(ta.ta_upsampling)) + ", " + a + ", " +
+                 b + ", err)";
+          break;
+        }
       }
       o << "  double " << out_name << " = 0.0;\n";
       std::string body;

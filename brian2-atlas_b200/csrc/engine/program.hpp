@@ -137,6 +137,9 @@ struct EmitContext {
   // Optional sink for file-scope constant tables (name -> definition) that
   // emitted code may reference; null disables table-based emission.
   std::map<std::string, std::string>* tables = nullptr;
+  // Expression for a device pointer to a copy of `values` (TimedArray
+  // tables); empty disables TimedArray emission.
+  std::function<std::string(const std::vector<double>& values)> device_array;
 };
 
 // Emit the body of a program: declarations of every non-Const register used,

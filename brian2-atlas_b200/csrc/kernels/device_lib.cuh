@@ -215,6 +215,27 @@ __device__ __forceinline__ double b2_binomial_checked(u64 seed, u64 stream, u64 
   return b2_binomial(seed, stream, tick, index, n, p, approximate);
 }
 
+// ---------------------------------------------------------------- TimedArray
+// Op::TimedArray (executor.rs:6121-6154): row = trunc((t / epsilon + 0.5) /
+// upsampling) clamped to [0, rows - 1] (a NaN row is row 0, like Rust's
+// saturating cast); with columns, the index must be finite and in
+// [0, width); a bad index or a non-finite value sets B2_ERR_TIMEDARRAY.
+__device__ __forceinline__ double b2_timed_array(const double* __restrict__ values, u64 rows, u64 width,
+                                                 bool has_columns, double epsilon, double upsampling, double time,
+                                                 double column, u32& err) {
+  const double raw_row = trunc((time / epsilon + 0.5) / upsampling);
+  const u64 row = !(raw_row > 0.0) ? 0ull : (raw_row >= (double)(rows - 1) ? rows - 1 : (u64)raw_row);
+  u64 col = 0;
+  if (has_columns) {
+    if (!(isfinite(column) && column >= 0.0 && column < (double)width)) {
+      err |= B2_ERR_TIMEDARRAY;
+      return 0.0;
+    }
+    col = (u64)column;
+  }
+  return values[row * width + col];
+}
+
 // ---------------------------------------------------------------- scalar ops
 
 // Per-op rules of the reference evaluate() (executor.rs:5932-6158).

@@ -154,7 +154,8 @@ def gap_junctions(reference: Path, n: int = 300, p: float = 0.05, ticks: int = 1
 def synapse_updates(reference: Path, n_in: int = 200, n_out: int = 50, p: float = 0.2, ticks: int = 1000,
                     seed: int = 8) -> dict:
     """STDP with clock-driven synaptic traces (a synapse state updater every
-    tick) and a synaptic run_regularly, driven by a PoissonGroup."""
+    tick) and a synaptic run_regularly, driven by deterministic periodic
+    inputs."""
     import numpy as np
     import brian2 as b
     import brian2_rust  # noqa: F401
@@ -200,6 +201,32 @@ def synapse_updates(reference: Path, n_in: int = 200, n_out: int = 50, p: float 
     return model
 
 
+def timed_input(reference: Path, n: int = 100, ticks: int = 1000, seed: int = 9) -> dict:
+    """Neurons driven by a two-dimensional TimedArray input (time x neuron,
+    1 ms rows over a 0.1 ms clock) plus a one-dimensional TimedArray gain."""
+    import numpy as np
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    b.start_scope()
+    b.defaultclock.dt = 0.1 * b.ms
+    rng = np.random.default_rng(seed)
+    stimulus = b.TimedArray(1.5 * rng.random((ticks // 10, n)), dt=1 * b.ms, name="stimulus")
+    gain = b.TimedArray(0.5 + rng.random(ticks // 50), dt=5 * b.ms, name="gain")
+    G = b.NeuronGroup(n, "dv/dt = (gain(t) * stimulus(t, i) - v) / (10*ms) : 1", threshold="v > 0.8",
+                      reset="v = 0", method="euler", name="neurons")
+    G.v = rng.random(n) * 0.5
+    spikes = b.SpikeMonitor(G, name="spikes")
+    net = b.Network(G, spikes)
+    ns = dict(stimulus=stimulus, gain=gain)
+    model = lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+    b.prefs.codegen.target = "numpy"
+    net.run(ticks * 0.1 * b.ms, namespace=ns)
+    np.savez_compressed(HERE / "brian_numpy" / "timed_input_small.npz", spike_i=np.array(spikes.i[:]),
+                        spike_t=np.array(spikes.t / b.second), v=np.array(G.v[:]))
+    return model
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -208,7 +235,7 @@ def main() -> None:
     if args.only:
         prepare_frontend(Path(args.reference))
         make = {"cuba_events_small": cuba_events, "gap_junctions_small": gap_junctions,
-                "synapse_updates_small": synapse_updates}[args.only]
+                "synapse_updates_small": synapse_updates, "timed_input_small": timed_input}[args.only]
         write_model(make(Path(args.reference)), args.only)
         print("wrote", args.only)
         return

@@ -23,7 +23,9 @@ pytestmark = pytest.mark.gpu
 # gap_junctions_small: a `(summed)` synaptic current recomputed every tick;
 # synapse_updates_small: clock-driven synaptic traces, a synaptic
 # run_regularly and STDP pathways
-EXACT = ["cuba_small", "cuba_poisson_small", "brunel_small", "gap_junctions_small", "synapse_updates_small"]
+# timed_input_small: two- and one-dimensional TimedArray inputs
+EXACT = ["cuba_small", "cuba_poisson_small", "brunel_small", "gap_junctions_small", "synapse_updates_small",
+         "timed_input_small"]
 
 
 def gpu_run(pkg, model_path, outdir, **kw):

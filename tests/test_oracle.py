@@ -39,7 +39,8 @@ def test_golden_comparison_detects_corruption(oracle, tmp_path):
     assert bytes(data) != (GOLDEN / "reference-v1" / "results.bin").read_bytes()
 
 
-@pytest.mark.parametrize("name,rtol", [("cuba_small", 1e-12), ("cobahh_small", 1e-9), ("gap_junctions_small", 1e-9)])
+@pytest.mark.parametrize("name,rtol", [("cuba_small", 1e-12), ("cobahh_small", 1e-9), ("gap_junctions_small", 1e-9),
+                                      ("timed_input_small", 1e-12)])
 def test_oracle_matches_brian_numpy(oracle, tmp_path, name, rtol):
     model_path = model_file(name, tmp_path)
     out = run_oracle(oracle, model_path, tmp_path / "out")

@@ -162,6 +162,12 @@ struct Engine::Impl {
     size_t x_off = 0;
     std::vector<int> xptr;
     uint64_t x_words = 0, x_tiles = 0, x_wpb = 0;  // exchange words, blocks, words per block
+    // fired bitmap ring for target-ordered pathways: slot rel % bm_slots holds
+    // the tick's ballot words (bit i = neuron i fired), written by the step
+    // kernel that produces the stream
+    bool needs_bitmap = false;
+    int bitmap = -1;
+    uint64_t bm_words = 0, bm_slots = 0;
     // host copy of drained spikes
     std::vector<uint32_t> ids;
     std::vector<uint64_t> starts;  // host positions per tick: starts[rel] .. starts[rel+1]
@@ -212,8 +218,12 @@ struct Engine::Impl {
     size_t delay = 0, max_delay = 0;
     uint64_t max_row = 0;  // longest CSR row (sizes the scatter work split)
     int delivered_slot = 0;
-    enum class Mode { Atomic, EdgeParallel, Serial } mode = Mode::Serial;
+    enum class Mode { Atomic, EdgeParallel, Targets, Serial } mode = Mode::Serial;
     std::vector<AtomicAdd> atomic_adds;
+    // Targets mode: target-major view (per target: entries by delay
+    // descending, then source ascending, then creation order)
+    int tm_off = -1, tm_src = -1, tm_edge = -1, tm_delay = -1;
+    uint64_t tm_targets = 0;
     int pend_offsets = -1, pend_items = -1, pend_src = -1, pend_tgt = -1;
     bool has_pending = false;
   };
@@ -297,9 +307,13 @@ struct Engine::Impl {
     if (const char* e = std::getenv("B2GPU_SCATTER_UNROLL")) scatter_unroll_ = unsigned(std::atoi(e));
     if (const char* e = std::getenv("B2GPU_EXCHANGE_WPB")) exchange_wpb_ = unsigned(std::atoi(e));
     if (const char* e = std::getenv("B2GPU_FUSE_EXCHANGE")) fuse_exchange_ = std::atoi(e) != 0;
+    // Diagnostic: deliver ordered pathways with one serial thread instead of
+    // the target-ordered kernel (same results) for A/B timing.
+    if (const char* e = std::getenv("B2GPU_TARGETS")) use_targets_ = std::atoi(e) != 0;
     check(scatter_unroll_ >= 1 && scatter_unroll_ <= 8, "scatter unroll must be 1 to 8");
   }
   bool no_fuse_ = false;
+  bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
   bool use_pdl_ = true;
   bool balance_tiles_ = true;                // tile_n_for: spread neurons over whole waves
   // Multi-GPU exchange: words per block (0: about eight blocks per SM), and
@@ -1272,6 +1286,15 @@ struct Engine::Impl {
     } else if (X) {
       o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
       o << "  if (lane == 0) s_ballot[kk * " << W << "u + warp] = b;\n";
+      if (es->bitmap >= 0) {
+        // fired bitmap for target-ordered pathways: word w covers neurons
+        // 32w .. 32w + 31 (tile_n is a multiple of 32)
+        std::string warp_in_tile = tile_n % kThreads ? "kk * " + std::to_string(kThreads) + "u + warp * 32u < " +
+                                                           std::to_string(tile_n) + "u && " : "";
+        o << "  { const u32 bw = tile * " << tile_n / 32 << "u + kk * " << W << "u + warp;\n";
+        o << "    if (lane == 0 && " << warp_in_tile << "bw < " << es->bm_words << "u) " << P(es->bitmap, "u32")
+          << "[(rel % " << es->bm_slots << "ull) * " << es->bm_words << "ull + bw] = b; }\n";
+      }
       o << "  fired_bits |= (fired ? 1u : 0u) << kk;\n";
     }
     o << "  }\n";  // kk loop
@@ -1627,7 +1650,7 @@ struct Engine::Impl {
       only_syn &= w.kind == WriteTarget::Kind::Synapse;
     }
     if (pw.has_pending || !pw.uniform) {
-      pw.mode = PathwayDev::Mode::Serial;
+      pw.mode = targets_ok(pw, pr) ? PathwayDev::Mode::Targets : PathwayDev::Mode::Serial;
       return;
     }
     if (only_post && !pr.writes.empty() && pw.is_pre) {
@@ -1700,7 +1723,72 @@ struct Engine::Impl {
       pw.mode = PathwayDev::Mode::EdgeParallel;
       return;
     }
-    pw.mode = PathwayDev::Mode::Serial;
+    pw.mode = targets_ok(pw, pr) ? PathwayDev::Mode::Targets : PathwayDev::Mode::Serial;
+  }
+
+  // Target-ordered delivery (Mode::Targets) reproduces the sequential event
+  // order per target: events reaching one target keep their canonical order
+  // (emission tick, source, creation order), and events of different targets
+  // touch disjoint state when the body writes only its target's neuron state
+  // and its own edge's synapse state, reads presynaptic state that no event
+  // writes, and draws from counter-based streams keyed by index.  The source
+  // stream must come from a step kernel (which writes the fired bitmap).
+  bool targets_ok(const PathwayDev& pw, const Program& pr) const {
+    if (world != 1 || !pw.is_pre || pw.has_pending || !use_targets_) return false;
+    const auto& def = m.synapses[pw.synapse];
+    for (const auto& [w, r] : pr.writes)
+      if (w.kind == WriteTarget::Kind::PreNeuron) return false;
+    if (def.source_population == def.target_population)
+      for (const auto& b : pr.bindings)
+        if (b.second.kind == Input::Kind::PreState)
+          for (const auto& [w, r] : pr.writes)
+            if (w.kind == WriteTarget::Kind::Neuron && w.index == b.second.index) return false;
+    if (syns[pw.synapse].local_edges > UINT32_MAX || def.target_count >= UINT32_MAX) return false;
+    const EventStreamDev& es = streams[size_t(pw.stream)];
+    const uint64_t words = (m.populations[es.pop].count + 31) / 32;
+    if (words * (es.max_delay + 1) * 4 > (uint64_t(1) << 30)) return false;
+    return stream_from_threshold(size_t(pw.stream));
+  }
+
+  // True when a threshold code object (compiled into a step kernel) produces
+  // the event stream and no spike generator does.
+  bool stream_from_threshold(size_t sid) const {
+    const EventStreamDev& es = streams[sid];
+    const auto& def = m.populations[es.pop];
+    size_t producers = 0;
+    for (const auto& n : m.schedule) {
+      if (n.owner_kind != b2ir::OwnerKind::Population || n.owner_index != es.pop) continue;
+      if (n.operation == b2ir::ScheduleOp::EventSource) return false;
+      if (n.operation != b2ir::ScheduleOp::CodeObject) continue;
+      const auto& c = def.code_objects[n.item_index];
+      if (c.kind == "threshold" && c.event_name && *c.event_name == def.events[es.event]) ++producers;
+    }
+    return producers == 1 && !es.exchanged;
+  }
+
+  // Device target-major view of a Targets-mode pathway's CSR.
+  void build_targets_view(PathwayDev& pw) {
+    const auto& def = m.synapses[pw.synapse];
+    const SynDev& sd = syns[pw.synapse];
+    pw.tm_targets = def.target_count;
+    EventStreamDev& es = streams[size_t(pw.stream)];
+    es.needs_bitmap = true;
+    if (opt.dry_run) {
+      pw.tm_off = alloc(0);
+      pw.tm_src = alloc(0);
+      pw.tm_edge = alloc(0);
+      if (!pw.uniform) pw.tm_delay = alloc(0);
+      return;
+    }
+    DeviceBuffer off, src, edge, delay;
+    build_target_major(static_cast<const uint64_t*>(dptr(pw.offsets)), static_cast<const uint32_t*>(dptr(pw.row_other)),
+                       pw.row_edge >= 0 ? static_cast<const uint32_t*>(dptr(pw.row_edge)) : nullptr,
+                       pw.uniform ? nullptr : static_cast<const uint16_t*>(dptr(pw.row_delay)), pw.max_delay,
+                       pw.endpoint_count, sd.local_edges, 0, pw.tm_targets, off, src, edge, delay, stream);
+    pw.tm_off = adopt(std::move(off));
+    pw.tm_src = adopt(std::move(src));
+    pw.tm_edge = adopt(std::move(edge));
+    if (!pw.uniform) pw.tm_delay = adopt(std::move(delay));
   }
 
   // Spike-list traversal shared by pathway kernels: warp per fired endpoint,
@@ -1845,6 +1933,55 @@ struct Engine::Impl {
         o << "      const u32 ep = s - " << lo << "u;\n" << deliver_row("dl[q] == lag") << "    }\n  }\n";
       }
       o << "  if (events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + " << pw.delivered_slot << ", events);\n";
+      o << kernel_tail();
+      return o.str();
+    }
+    if (pw.mode == PathwayDev::Mode::Targets) {
+      // Warp per target over its in-edges (delay descending, source
+      // ascending, creation order, i.e. the canonical delivery order): lanes
+      // test 32 entries at a time against the emission tick's fired bitmap,
+      // and the hits run one lane at a time in lane order, separated by
+      // __syncwarp (which orders the lanes' memory accesses).
+      constexpr unsigned U = 4;  // independent 32-entry groups in flight per warp
+      const std::string bm = P(es.bitmap, "const u32");
+      o << "  const u32 lane = threadIdx.x & 31u;\n";
+      o << "  const u64 warps = (u64)gridDim.x * (blockDim.x >> 5);\n";
+      o << "  const u64* toff = " << P(pw.tm_off, "const u64") << ";\n";
+      o << "  const u32* tsrc = " << P(pw.tm_src, "const u32") << ";\n";
+      o << "  const u32* tedge = " << P(pw.tm_edge, "const u32") << ";\n";
+      if (pw.uniform) {
+        o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n";
+        o << "  const u32* bmw = " << bm << " + ((rel - " << pw.delay << "ull) % " << es.bm_slots << "ull) * "
+          << es.bm_words << "ull;\n";
+      } else {
+        o << "  const u16* tdel = " << P(pw.tm_delay, "const u16") << ";\n";
+      }
+      o << "  u64 events = 0;\n";
+      o << "  for (u64 j = (blockIdx.x * (u64)blockDim.x + threadIdx.x) >> 5; j < " << pw.tm_targets << "ull; j += warps) {\n";
+      o << "    const u64 o0 = __ldg(toff + j), o1 = __ldg(toff + j + 1);\n";
+      o << "    for (u64 base = o0; base < o1; base += " << 32 * U << "ull) {\n";
+      o << "      u32 sv[" << U << "], mk[" << U << "];\n      bool in[" << U << "];\n";
+      o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
+      o << "        const u64 q = base + u * 32u + lane;\n        in[u] = q < o1;\n";
+      o << "        sv[u] = in[u] ? __ldg(tsrc + q) : 0u;\n      }\n";
+      o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
+      o << "        bool h = false;\n";
+      o << "        if (in[u]) {\n          const u32 s = sv[u] + " << pw.endpoint_start << "u;\n";
+      if (pw.uniform) {
+        o << "          h = (__ldg(bmw + (s >> 5)) >> (s & 31u)) & 1u;\n";
+      } else {
+        o << "          const u64 lag = __ldg(tdel + base + u * 32u + lane);\n";
+        o << "          if (lag <= rel) h = (__ldg(" << bm << " + ((rel - lag) % " << es.bm_slots << "ull) * " << es.bm_words
+          << "ull + (s >> 5)) >> (s & 31u)) & 1u;\n";
+      }
+      o << "        }\n        mk[u] = __ballot_sync(0xffffffffu, h);\n      }\n";
+      o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
+      o << "        u32 mm = mk[u];\n        events += lane == 0 ? __popc(mm) : 0u;\n";
+      o << "        while (mm) {\n          const u32 b = __ffs(mm) - 1u;\n          mm &= mm - 1u;\n";
+      o << "          if (lane == b) " << body_fn << "(sv[u], (u32)j, (u64)__ldg(tedge + base + u * 32u + lane), tick, t, err);\n";
+      o << "          __syncwarp();\n        }\n      }\n    }\n  }\n";
+      o << "  if (lane == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
+        << pw.delivered_slot << ", events);\n";
       o << kernel_tail();
       return o.str();
     }
@@ -2236,6 +2373,7 @@ struct Engine::Impl {
           check(!pr.uses_rng(), "multi-GPU runs do not support random draws in synaptic code ('" + code.name + "')");
         }
         classify_pathway(pw, pr);
+        if (pw.mode == PathwayDev::Mode::Targets) build_targets_view(pw);
         // Constant-addend pathways reading one spike stream at one delay and
         // writing disjoint target variables share a scatter launch.
         bool merged = false;
@@ -2267,6 +2405,9 @@ struct Engine::Impl {
           bool serial = pw.mode == PathwayDev::Mode::Serial;
           o.grid = serial ? 1u : 148u * 8u;
           o.block = serial ? 32u : kThreads;
+          if (pw.mode == PathwayDev::Mode::Targets)  // one warp per target
+            o.grid = unsigned(std::max<uint64_t>(1, std::min<uint64_t>((pw.tm_targets + kThreads / 32 - 1) / (kThreads / 32),
+                                                                        148u * 8u)));
           paths.push_back(ps);
           specs.push_back(o);
         }
@@ -2274,6 +2415,15 @@ struct Engine::Impl {
     }
     for (size_t sidx = 0; sidx < streams.size(); ++sidx) {
       streams[sidx].produced = stream_produced[sidx];
+      EventStreamDev& es = streams[sidx];
+      if (es.needs_bitmap) {
+        check(stream_produced[sidx], "target-ordered pathway without a threshold producer");
+        es.bm_words = (m.populations[es.pop].count + 31) / 32;
+        es.bm_slots = es.max_delay + 1;
+        const size_t bytes = size_t(es.bm_words * es.bm_slots * 4);
+        es.bitmap = alloc(bytes);
+        memset_dev(es.bitmap, bytes);
+      }
       if (!stream_produced[sidx]) {
         OpSpec o;
         o.base = "empty_stream";
@@ -2351,7 +2501,10 @@ struct Engine::Impl {
           if (ps.pathways.size() == 1 && ps.pathways[0]->mode != PathwayDev::Mode::Atomic) {
             std::string body = "b2_body_" + std::to_string(kid) + "_" + sanitize(ps.codes[0]);
             bodies << gen_pathway_body(body, ps.pathways[0]->synapse, *ps.pathways[0], *ps.programs[0]);
-            const char* mode = ps.pathways[0]->mode == PathwayDev::Mode::EdgeParallel ? "_edges" : "_serial";
+            const auto md = ps.pathways[0]->mode;
+            const char* mode = md == PathwayDev::Mode::EdgeParallel ? "_edges"
+                               : md == PathwayDev::Mode::Targets    ? "_targets"
+                                                                    : "_serial";
             nm += mode;
             kernels << gen_pathway_kernel(nm, body, *ps.pathways[0]);
           } else {

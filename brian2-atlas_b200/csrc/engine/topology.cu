@@ -243,6 +243,93 @@ void build_fixed_total_csr(uint64_t S, uint64_t T, uint64_t E, uint64_t seed, ui
   build_csr(S, per_chunk, chunks, gen, offsets, row_targets, local_edges, stream);
 }
 
+namespace {
+
+// source of every source-major position (one warp per source row)
+__global__ void row_sources(const uint64_t* __restrict__ offsets, uint64_t S, uint32_t* __restrict__ src) {
+  const uint64_t warps = (uint64_t)gridDim.x * (blockDim.x / 32);
+  for (uint64_t s = (blockIdx.x * (uint64_t)blockDim.x + threadIdx.x) / 32; s < S; s += warps)
+    for (uint64_t q = offsets[s] + (threadIdx.x & 31); q < offsets[s + 1]; q += 32) src[q] = (uint32_t)s;
+}
+
+// keys = (target - t_lo) * (D + 1) + (D - delay), values = position (edges
+// of non-owned targets never occur)
+__global__ void target_keys(const uint32_t* __restrict__ row_other, const uint16_t* __restrict__ row_delay,
+                            uint64_t E, uint32_t t_lo, uint64_t D, uint64_t* __restrict__ keys,
+                            uint32_t* __restrict__ pos) {
+  for (uint64_t q = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; q < E; q += (uint64_t)gridDim.x * blockDim.x) {
+    keys[q] = (uint64_t)(row_other[q] - t_lo) * (D + 1) + (row_delay ? D - row_delay[q] : 0);
+    pos[q] = (uint32_t)q;
+  }
+}
+
+// tm_off[j] = first sorted position whose key belongs to target >= j
+__global__ void target_offsets(const uint64_t* __restrict__ keys, uint64_t E, uint64_t T, uint64_t D,
+                               uint64_t* __restrict__ off) {
+  for (uint64_t j = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; j <= T; j += (uint64_t)gridDim.x * blockDim.x) {
+    const uint64_t first = j * (D + 1);
+    uint64_t lo = 0, hi = E;
+    while (lo < hi) {
+      const uint64_t mid = (lo + hi) / 2;
+      if (keys[mid] < first) lo = mid + 1;
+      else hi = mid;
+    }
+    off[j] = lo;
+  }
+}
+
+__global__ void gather_target_major(const uint32_t* __restrict__ pos, uint64_t E, const uint32_t* __restrict__ src_of,
+                                    const uint32_t* __restrict__ row_edge, const uint16_t* __restrict__ row_delay,
+                                    uint32_t* __restrict__ tm_src, uint32_t* __restrict__ tm_edge,
+                                    uint16_t* __restrict__ tm_delay) {
+  for (uint64_t k = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; k < E; k += (uint64_t)gridDim.x * blockDim.x) {
+    const uint32_t q = pos[k];
+    tm_src[k] = src_of[q];
+    tm_edge[k] = row_edge ? row_edge[q] : q;
+    if (tm_delay) tm_delay[k] = row_delay[q];
+  }
+}
+
+}  // namespace
+
+void build_target_major(const uint64_t* d_offsets, const uint32_t* d_row_other, const uint32_t* d_row_edge,
+                        const uint16_t* d_row_delay, uint64_t max_delay, uint64_t S, uint64_t E, uint64_t t_lo,
+                        uint64_t T, DeviceBuffer& tm_offsets, DeviceBuffer& tm_src, DeviceBuffer& tm_edge,
+                        DeviceBuffer& tm_delay, cudaStream_t stream) {
+  b2ir::check(E <= UINT32_MAX && T < UINT32_MAX, "target-major view needs u32 edge and target indices");
+  const uint64_t D = d_row_delay ? max_delay : 0;
+  tm_offsets = DeviceBuffer((T + 1) * sizeof(uint64_t));
+  tm_src = DeviceBuffer(std::max<uint64_t>(E, 1) * 4);
+  tm_edge = DeviceBuffer(std::max<uint64_t>(E, 1) * 4);
+  if (d_row_delay) tm_delay = DeviceBuffer(std::max<uint64_t>(E, 1) * 2);
+  if (E == 0) {
+    B2_CUDA(cudaMemsetAsync(tm_offsets.ptr, 0, tm_offsets.bytes, stream));
+    return;
+  }
+  DeviceBuffer src_of(E * 4), keys(E * 8), pos(E * 4), keys2(E * 8), pos2(E * 4);
+  row_sources<<<grid_for(S * 32, 256), 256, 0, stream>>>(d_offsets, S, src_of.as<uint32_t>());
+  target_keys<<<grid_for(E, 256), 256, 0, stream>>>(d_row_other, d_row_delay, E, (uint32_t)t_lo, D,
+                                                     keys.as<uint64_t>(), pos.as<uint32_t>());
+  B2_CUDA(cudaGetLastError());
+  // LSD radix sort is stable: within a target and delay, edges keep the
+  // source-major order, i.e. source ascending, then creation order
+  size_t temp_bytes = 0;
+  const int end_bit = bits_for(T * (D + 1) + 1);
+  cub::DeviceRadixSort::SortPairs(nullptr, temp_bytes, keys.as<uint64_t>(), keys2.as<uint64_t>(), pos.as<uint32_t>(),
+                                  pos2.as<uint32_t>(), (int64_t)E, 0, end_bit, stream);
+  {
+    DeviceBuffer temp(std::max<size_t>(temp_bytes, 16));
+    B2_CUDA(cub::DeviceRadixSort::SortPairs(temp.ptr, temp_bytes, keys.as<uint64_t>(), keys2.as<uint64_t>(),
+                                            pos.as<uint32_t>(), pos2.as<uint32_t>(), (int64_t)E, 0, end_bit, stream));
+  }
+  target_offsets<<<grid_for(T + 1, 256), 256, 0, stream>>>(keys2.as<uint64_t>(), E, T, D, tm_offsets.as<uint64_t>());
+  gather_target_major<<<grid_for(E, 256), 256, 0, stream>>>(pos2.as<uint32_t>(), E, src_of.as<uint32_t>(), d_row_edge,
+                                                            d_row_delay, tm_src.as<uint32_t>(), tm_edge.as<uint32_t>(),
+                                                            d_row_delay ? tm_delay.as<uint16_t>() : nullptr);
+  B2_CUDA(cudaGetLastError());
+  B2_CUDA(cudaStreamSynchronize(stream));
+}
+
 void uniform_initializer_device(double* out, uint64_t n, uint64_t seed, uint64_t stream_id, double lo, double hi,
                                 uint64_t edge_base, cudaStream_t stream) {
   if (n == 0) return;

@@ -137,3 +137,40 @@ def brunel_fixed_indegree(template: dict, n: int = 4_000_000, indegree: int = 10
                 vals[0] = f"{np.float64(p).view(np.uint64):016x}"
     doc["instance"]["rng_seed"] = seed
     return attach_protocol(doc)
+
+
+def stdp_feedforward(template: dict, n_inputs: int = 100_000, n_neurons: int = 10_000, indegree: int = 1000,
+                     ticks: int = 10_000, seed: int = 5) -> dict:
+    """The STDP-plastic feedforward network (the Song-Abbott example scaled
+    up): n_inputs Poisson inputs at the template's rate drive n_neurons
+    conductance-based LIF neurons, each receiving `indegree` inputs drawn
+    uniformly (with replacement), edges in target-major creation order;
+    w0 ~ U[0, gmax], traces and lastupdate zero, membrane at its template
+    value.  The template is stdp_small (one input group, one target group,
+    one explicit plastic projection with on_pre and on_post pathways)."""
+    doc = copy.deepcopy(template)
+    d, inst = doc["definition"], doc["instance"]
+    src_pop, tgt_pop = d["populations"]
+    src_pop["count"], tgt_pop["count"] = n_inputs, n_neurons
+    inst["neuron_count"] = n_inputs + n_neurons
+    syn = d["synapses"][0]
+    syn.update(source_start=0, source_count=n_inputs, target_start=0, target_count=n_neurons)
+    _set_run(doc, ticks)
+    pin_src, pin_tgt = inst["populations"]
+    pin_src["parameters"]["rates"] = [pin_src["parameters"]["rates"][0]] * n_inputs
+    for name, values in pin_tgt["initial_state"].items():
+        pin_tgt["initial_state"][name] = [values[0]] * n_neurons
+    rng = np.random.default_rng(seed)
+    E = n_neurons * indegree
+    source = rng.integers(0, n_inputs, size=E, dtype=np.int64)
+    target = np.repeat(np.arange(n_neurons, dtype=np.int64), indegree)
+    si = inst["synapses"][0]
+    si["source"], si["target"] = source.tolist(), target.tolist()
+    gmax = _f64(si["parameters"]["gmax"][0])
+    zero = ["0000000000000000"] * E
+    si["initial_state"] = {"w": _hex64(rng.random(E) * gmax), "Apre": zero, "Apost": zero, "lastupdate": zero}
+    for name, values in si["parameters"].items():
+        if len(values) > 1:
+            si["parameters"][name] = [values[0]] * E
+    inst["rng_seed"] = seed
+    return attach_protocol(doc)

@@ -59,7 +59,9 @@ def load(name):
     ("brunel_small", ["step", "excitatory_synapses_pre_atomic", "inhibitory_synapses_pre_atomic",
                       "poisson_input", "reset"]),
     ("cobahh_small", ["step", "exc_pre_inh_pre_atomic"]),
-    ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_serial", "stdp_post_edges"]),
+    # on_pre writes the target's conductance and the edge's weight and
+    # traces: target-ordered delivery; on_post writes only synapse state
+    ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_targets", "stdp_post_edges"]),
 ])
 def test_codegen_plan(pkg, name, expected):
     src = pkg.codegen(load(name))
@@ -72,9 +74,36 @@ def test_codegen_plan(pkg, name, expected):
 def test_codegen_golden_fixture(pkg):
     src = pkg.codegen((GOLDEN / "reference-v1" / "model.json").read_bytes())
     names = kernels(src)
-    # per-edge delays 1-4 ticks and per-edge weights: ordered (serial) delivery
-    assert sum(n.endswith("_serial") for n in names) == 4
+    # per-edge delays 1-4 ticks and per-edge weights: ordered delivery, one
+    # warp per target
+    assert sum(n.endswith("_targets") for n in names) == 4
     assert sum(n.endswith("_step") for n in names) == 2
+
+
+def golden_variant(expr):
+    """The golden fixture with projection_0_0 (population 0 onto itself)
+    delivering current_post + w * <expr>."""
+    doc = json.loads((GOLDEN / "reference-v1" / "model.json").read_text())
+    code = doc["definition"]["synapses"][0]["code_objects"][0]
+    value = code["vector"][0]["value"]
+    value["right"] = {"op": "mul", "left": value["right"], "right": {"op": "load", "name": expr}}
+    code["effects"]["reads"] = sorted(set(code["effects"]["reads"]) | {expr})
+    return encode_model(doc)
+
+
+def test_codegen_ordered_pathway_fallbacks(pkg, monkeypatch):
+    # reading presynaptic `current` while writing postsynaptic `current` of
+    # the same population makes the order across targets observable: serial
+    names = kernels(pkg.codegen(golden_variant("current_pre")))
+    assert names[4].endswith("projection_0_0_pre_serial")
+    assert sum(n.endswith("_targets") for n in names) == 3
+    # presynaptic `v` is never written by the pathway: target-ordered
+    names = kernels(pkg.codegen(golden_variant("v_pre")))
+    assert sum(n.endswith("_targets") for n in names) == 4
+    # diagnostic switch back to the single-thread fold
+    monkeypatch.setenv("B2GPU_TARGETS", "0")
+    names = kernels(pkg.codegen((GOLDEN / "reference-v1" / "model.json").read_bytes()))
+    assert sum(n.endswith("_serial") for n in names) == 4
 
 
 def test_exact_linear_update_is_pure_arithmetic(pkg):

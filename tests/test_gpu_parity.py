@@ -45,8 +45,12 @@ def assert_same_files(a, b):
         assert ea.read_bytes() == eb.read_bytes()
 
 
-def test_golden_fixture_bytes(pkg, tmp_path):
-    """The reference's golden b2-runner run, reproduced on the GPU byte for byte."""
+@pytest.mark.parametrize("targets", ["1", "0"])
+def test_golden_fixture_bytes(pkg, tmp_path, monkeypatch, targets):
+    """The reference's golden b2-runner run, reproduced on the GPU byte for
+    byte, with the per-edge-delay pathways delivered target-ordered (one warp
+    per target) and by the single-thread fold."""
+    monkeypatch.setenv("B2GPU_TARGETS", targets)
     out = tmp_path / "gpu"
     gpu_run(pkg, GOLDEN / "reference-v1" / "model.json", out)
     assert (out / "results.bin").read_bytes() == (GOLDEN / "reference-v1" / "results.bin").read_bytes()
@@ -58,6 +62,19 @@ def test_golden_fixture_bytes(pkg, tmp_path):
 @pytest.mark.parametrize("name", EXACT)
 def test_exact_models_match_oracle(pkg, oracle, tmp_path, name):
     path = model_file(name, tmp_path)
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
+@pytest.mark.parametrize("expr", ["v_pre", "current_pre"])
+def test_golden_variants_match_oracle(pkg, oracle, tmp_path, expr):
+    """projection_0_0 delivering current_post + w * <expr>: target-ordered
+    for v_pre, the serial fold for current_pre (presynaptic state that the
+    pathway writes); both byte-identical to the oracle."""
+    from test_abi import golden_variant
+    path = tmp_path / "model.json"
+    path.write_bytes(golden_variant(expr))
     gpu_run(pkg, path, tmp_path / "gpu")
     run_oracle(oracle, path, tmp_path / "ref")
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")
@@ -170,3 +187,23 @@ def test_cli_runner_drop_in(pkg, oracle, tmp_path):
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")
     again = subprocess.run([str(pkg.runner_path()), str(path), str(tmp_path / "gpu")], capture_output=True, text=True)
     assert again.returncode == 1 and again.stderr.startswith("b2-runner: ")
+
+
+def test_stdp_targets_equal_serial_fold(pkg, tmp_path, monkeypatch):
+    """Scaled STDP feedforward network (2,000 Poisson inputs onto 200
+    neurons, in-degree 200, 40k plastic synapses): the target-ordered on_pre
+    delivery and the single-thread fold run the same arithmetic in the same
+    per-target order, so every output byte agrees."""
+    import gzip
+    import importlib
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    with gzip.open(MODELS / "stdp_small.json.gz", "rb") as f:
+        template = json.loads(f.read())
+    path = tmp_path / "stdp_40k.json"
+    path.write_bytes(synthetic.encode(synthetic.stdp_feedforward(template, 2000, 200, 200, ticks=1500, seed=11)))
+    stats = {}
+    for mode in ("1", "0"):
+        monkeypatch.setenv("B2GPU_TARGETS", mode)
+        stats[mode] = gpu_run(pkg, path, tmp_path / f"gpu{mode}")
+    assert stats["1"]["synaptic_events"] == stats["0"]["synaptic_events"] > 0
+    assert_same_files(tmp_path / "gpu1", tmp_path / "gpu0")

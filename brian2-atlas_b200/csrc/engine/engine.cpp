@@ -176,6 +176,11 @@ struct Engine::Impl {
   struct PopDev {
     size_t count = 0, start_tick = 0, end_tick = 0, steps = 0;  // count: neurons owned by this rank
     uint64_t lo = 0, global_count = 0;                            // owned block [lo, lo + count)
+    // multi-GPU: every rank evaluates the whole population (no synapse
+    // targets it, so its evolution depends on its own state and counter-based
+    // draws only); its event lists are complete on every rank without an
+    // exchange, and rank 0 stages its results
+    bool replicated = false;
     double dt = 0.0;
     std::vector<Slot> states;
     int lastspike = -1, not_refractory = -1;
@@ -223,7 +228,7 @@ struct Engine::Impl {
     // Targets mode: target-major view (per target: entries by delay
     // descending, then source ascending, then creation order)
     int tm_off = -1, tm_src = -1, tm_edge = -1, tm_delay = -1;
-    uint64_t tm_targets = 0;
+    uint64_t tm_targets = 0, tm_lo = 0;  // local targets [tm_lo, tm_lo + tm_targets) (synapse-level)
     int pend_offsets = -1, pend_items = -1, pend_src = -1, pend_tgt = -1;
     bool has_pending = false;
   };
@@ -289,6 +294,25 @@ struct Engine::Impl {
   bool connected = false, published = false;
   void* gptr_table = nullptr;         // device address of the module's g_ptr table
   uint64_t part_lo(uint64_t n, int r) const { return n * uint64_t(r) / uint64_t(world); }
+  // Block of population p whose results rank q stages (replicated
+  // populations: all of it on rank 0, nothing elsewhere).
+  uint64_t stage_lo(size_t p, int q) const {
+    const uint64_t n = m.populations[p].count;
+    return pops[p].replicated ? (q == 0 ? 0 : n) : part_lo(n, q);
+  }
+  uint64_t stage_count(size_t p, int q) const {
+    const uint64_t n = m.populations[p].count;
+    return pops[p].replicated ? (q == 0 ? n : 0) : part_lo(n, q + 1) - part_lo(n, q);
+  }
+  bool replicate_ = true;  // multi-GPU: replicate populations that no synapse targets
+  // A population that no synapse targets, and that is no spike generator
+  // (which already emits its global list on every rank).
+  bool replicable(size_t p) const {
+    if (world == 1 || !replicate_ || m.population_instances[p].spike_generator) return false;
+    for (const auto& s : m.synapses)
+      if (s.target_population == p) return false;
+    return true;
+  }
 
   Impl(const b2ir::Model& model, const Options& o) : m(model), opt(o), world(o.world_size), rank(o.rank) {
     if (const char* e = std::getenv("B2GPU_NPT")) npt_ = unsigned(std::atoi(e));
@@ -310,6 +334,9 @@ struct Engine::Impl {
     // Diagnostic: deliver ordered pathways with one serial thread instead of
     // the target-ordered kernel (same results) for A/B timing.
     if (const char* e = std::getenv("B2GPU_TARGETS")) use_targets_ = std::atoi(e) != 0;
+    // Diagnostic: partition and exchange every population on N > 1 GPUs
+    // (same results) instead of replicating the ones no synapse targets.
+    if (const char* e = std::getenv("B2GPU_REPLICATE")) replicate_ = std::atoi(e) != 0;
     check(scatter_unroll_ >= 1 && scatter_unroll_ <= 8, "scatter unroll must be 1 to 8");
   }
   bool no_fuse_ = false;
@@ -429,7 +456,8 @@ struct Engine::Impl {
       // evaluate from its own block is rejected before any device work.
       for (const auto& s : m.synapses) {
         for (const auto& c : s.code_objects)
-          check(c.kind == "synapses", "multi-GPU runs support on_pre pathways only");
+          check(c.kind == "synapses" || c.kind == "synapses_post",
+                "multi-GPU runs support on_pre and on_post pathways only");
       }
       for (size_t k = 0; k < m.synapses.size(); ++k) {
         const auto& inst = m.synapse_instances[k];
@@ -448,8 +476,9 @@ struct Engine::Impl {
       const auto& inst = m.population_instances[p];
       PopDev pd;
       pd.global_count = def.count;
-      pd.lo = part_lo(def.count, rank);
-      pd.count = part_lo(def.count, rank + 1) - pd.lo;
+      pd.replicated = replicable(p);
+      pd.lo = pd.replicated ? 0 : part_lo(def.count, rank);
+      pd.count = pd.replicated ? def.count : part_lo(def.count, rank + 1) - pd.lo;
       const size_t lo = pd.lo, n = pd.count;
       pd.start_tick = start_tick;
       pd.steps = def.steps;
@@ -880,8 +909,9 @@ struct Engine::Impl {
       es.tick_start = alloc((steps + 1) * 8);
       memset_dev(es.tick_start, 8);
       size_t tiles = tiles_for(pd.count), tile_n = tile_n_for(pd.count);
-      if (world > 1 && pd.gen_offsets < 0) {
-        // spike generators emit their (global, precomputed) list on every rank
+      if (world > 1 && pd.gen_offsets < 0 && !pd.replicated) {
+        // spike generators emit their (global, precomputed) list on every
+        // rank, and replicated populations compute it on every rank
         es.exchanged = true;
         es.x_words = exchange_words(pd.global_count, world);
         es.x_wpb = exchange_wpb_ ? std::min<uint64_t>(exchange_wpb_, kThreads)
@@ -949,7 +979,7 @@ struct Engine::Impl {
     for (size_t p = 0; p < m.populations.size(); ++p) {
       const auto& def = m.populations[p];
       const PopDev& pd = pops[p];
-      const uint64_t lo = part_lo(def.count, q), n = part_lo(def.count, q + 1) - lo;
+      const uint64_t lo = stage_lo(p, q), n = stage_count(p, q);
       L.lo.push_back(lo);
       L.count.push_back(n);
       L.state.emplace_back();
@@ -1734,7 +1764,7 @@ struct Engine::Impl {
   // writes, and draws from counter-based streams keyed by index.  The source
   // stream must come from a step kernel (which writes the fired bitmap).
   bool targets_ok(const PathwayDev& pw, const Program& pr) const {
-    if (world != 1 || !pw.is_pre || pw.has_pending || !use_targets_) return false;
+    if (!pw.is_pre || pw.has_pending || !use_targets_) return false;
     const auto& def = m.synapses[pw.synapse];
     for (const auto& [w, r] : pr.writes)
       if (w.kind == WriteTarget::Kind::PreNeuron) return false;
@@ -1770,7 +1800,13 @@ struct Engine::Impl {
   void build_targets_view(PathwayDev& pw) {
     const auto& def = m.synapses[pw.synapse];
     const SynDev& sd = syns[pw.synapse];
-    pw.tm_targets = def.target_count;
+    // synapse-level targets j whose population index target_start + j this rank owns
+    const PopDev& tp = pops[def.target_population];
+    auto clampj = [&](uint64_t x) {
+      return x <= def.target_start ? uint64_t(0) : std::min<uint64_t>(x - def.target_start, def.target_count);
+    };
+    pw.tm_lo = clampj(tp.lo);
+    pw.tm_targets = clampj(tp.lo + tp.count) - pw.tm_lo;
     EventStreamDev& es = streams[size_t(pw.stream)];
     es.needs_bitmap = true;
     if (opt.dry_run) {
@@ -1784,7 +1820,7 @@ struct Engine::Impl {
     build_target_major(static_cast<const uint64_t*>(dptr(pw.offsets)), static_cast<const uint32_t*>(dptr(pw.row_other)),
                        pw.row_edge >= 0 ? static_cast<const uint32_t*>(dptr(pw.row_edge)) : nullptr,
                        pw.uniform ? nullptr : static_cast<const uint16_t*>(dptr(pw.row_delay)), pw.max_delay,
-                       pw.endpoint_count, sd.local_edges, 0, pw.tm_targets, off, src, edge, delay, stream);
+                       pw.endpoint_count, sd.local_edges, pw.tm_lo, pw.tm_targets, off, src, edge, delay, stream);
     pw.tm_off = adopt(std::move(off));
     pw.tm_src = adopt(std::move(src));
     pw.tm_edge = adopt(std::move(edge));
@@ -1978,7 +2014,8 @@ struct Engine::Impl {
       o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
       o << "        u32 mm = mk[u];\n        events += lane == 0 ? __popc(mm) : 0u;\n";
       o << "        while (mm) {\n          const u32 b = __ffs(mm) - 1u;\n          mm &= mm - 1u;\n";
-      o << "          if (lane == b) " << body_fn << "(sv[u], (u32)j, (u64)__ldg(tedge + base + u * 32u + lane), tick, t, err);\n";
+      o << "          if (lane == b) " << body_fn << "(sv[u], (u32)(j + " << pw.tm_lo
+        << "ull), (u64)__ldg(tedge + base + u * 32u + lane), tick, t, err);\n";
       o << "          __syncwarp();\n        }\n      }\n    }\n  }\n";
       o << "  if (lane == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
         << pw.delivered_slot << ", events);\n";
@@ -2363,9 +2400,11 @@ struct Engine::Impl {
         programs.push_back(Program::compile(code, inputs, writable, m.functions));
         const Program& pr = programs.back();
         if (world > 1) {
+          // presynaptic state is complete on every rank only for a replicated source
           for (const auto& b : pr.bindings)
-            check(b.second.kind != Input::Kind::PreState &&
-                      !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre),
+            check(pops[m.synapses[s].source_population].replicated ||
+                      (b.second.kind != Input::Kind::PreState &&
+                       !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre)),
                   "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
           for (const auto& w : pr.writes)
             check(w.first.kind != WriteTarget::Kind::PreNeuron,
@@ -2852,13 +2891,15 @@ struct Engine::Impl {
     for (size_t p = 0; p < m.populations.size(); ++p) {
       const auto& def = m.populations[p];
       const PopDev& pd = pops[p];
+      // a replicated population is staged by rank 0 only (count 0 elsewhere)
+      const uint64_t n = L.count[p];
       for (size_t s = 0; s < def.states.size(); ++s)
-        put(L.state[p][s], pd.states[s].ptr, pd.count * b2ir::dtype_bytes(def.states[s].dtype));
+        put(L.state[p][s], pd.states[s].ptr, n * b2ir::dtype_bytes(def.states[s].dtype));
       if (pd.lastspike >= 0) {
-        put(L.lastspike[p], pd.lastspike, pd.count * 8);
-        put(L.not_refractory[p], pd.not_refractory, pd.count);
+        put(L.lastspike[p], pd.lastspike, n * 8);
+        put(L.not_refractory[p], pd.not_refractory, n);
       }
-      if (pd.mon_records >= 0)
+      if (pd.mon_records >= 0 && !L.mon_positions[p].empty())
         for (size_t v = 0; v < pd.mon_samples.size(); ++v)
           put(L.monitor[p][v], pd.mon_samples[v], pd.mon_ticks * pd.mon_nrec * b2ir::dtype_bytes(pd.mon_dtypes[v]));
     }

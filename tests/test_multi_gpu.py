@@ -60,8 +60,33 @@ def test_rank_plans(pkg, world):
 
 
 def test_multi_gpu_capability_errors(pkg, tmp_path):
-    with pytest.raises(pkg.B2GpuError, match="on_pre pathways only"):
-        pkg.codegen(model_file("stdp_small", tmp_path).read_bytes(), rank=0, world_size=2)
+    with pytest.raises(pkg.B2GpuError, match="on_pre and on_post pathways only"):
+        pkg.codegen(model_file("synapse_updates_small", tmp_path).read_bytes(), rank=0, world_size=2)
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_stdp_rank_plans_replicate_the_inputs(pkg, tmp_path, world):
+    """The Poisson inputs, which no synapse targets, run whole on every rank
+    (draws keyed by global index), so their spikes need no exchange and feed
+    the target-ordered on_pre kernel over the rank's own targets; the target
+    neurons are partitioned and exchanged for on_post."""
+    data = model_file("stdp_small", tmp_path).read_bytes()
+    targets = json.loads(data)["definition"]["populations"][1]["count"]
+    for r in range(world):
+        src = pkg.codegen(data, rank=r, world_size=world)
+        names = [k.split("_", 2)[2] for k in kernels(src)]
+        assert names == ["neurons_step", "neurons_exchange", "inputs_step", "stdp_pre_targets", "stdp_post_edges"]
+        lo, hi = pkg.partition(targets, r, world)
+        body = src[src.index("stdp_pre_targets("):]
+        assert f"j < {hi - lo}ull" in body and f"(u32)(j + {lo}ull)" in body
+    # diagnostic: partition and exchange the inputs as well (ordered serial fold)
+    os.environ["B2GPU_REPLICATE"] = "0"
+    try:
+        names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=0, world_size=world))]
+    finally:
+        del os.environ["B2GPU_REPLICATE"]
+    assert names == ["neurons_step", "neurons_exchange", "inputs_step", "inputs_exchange", "stdp_pre_serial",
+                     "stdp_post_edges"]
 
 
 def _gloo_rank(rank, world, port, q):
@@ -166,6 +191,26 @@ def test_ranks_match_oracle(pkg, oracle, tmp_path, world):
         # every rank delivered to its own targets only
         total = json.loads((tmp_path / f"ref{k}" / "summary.json").read_text())["synaptic_events"]
         assert sum(lines[k]["events_per_rank"]) == total
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world,replicate", [(2, "1"), (3, "1"), (2, "0")])
+def test_stdp_ranks_match_one_gpu(pkg, tmp_path, monkeypatch, world, replicate):
+    """STDP with on_pre and on_post on 2-3 ranks against the same network on
+    one GPU, byte for byte (the device arithmetic is the same; the trace
+    decay's exp rules out the oracle as a byte-exact reference)."""
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    model = model_file("stdp_small", tmp_path)
+    with pkg.Engine(model.read_bytes(), device=0) as eng:
+        eng.run()
+        (tmp_path / "one").mkdir()
+        eng.write_results(tmp_path / "one")
+    monkeypatch.setenv("B2GPU_REPLICATE", replicate)
+    lines = torchrun(world, ["run", model, tmp_path / "many"])
+    assert_same_files(tmp_path / "many", tmp_path / "one")
+    total = json.loads((tmp_path / "one" / "summary.json").read_text())["synaptic_events"]
+    assert sum(lines[0]["events_per_rank"]) == total
 
 
 @pytest.mark.gpu

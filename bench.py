@@ -25,6 +25,14 @@ deliveries.
 --impl reference times the CPU restatement of the reference executor
 (oracle/b2ref, single-threaded like b2-runner) on a bounded sample of the
 same network (50,000 neurons, in-degree 1000).
+
+--workload stdp measures config 4 instead: 100,000 Poisson inputs at 15 Hz
+onto 10,000 conductance-based LIF neurons, in-degree 1000 (1e7 plastic
+synapses, f64 weights U[0, gmax], additive pre/post traces; definition layer
+from the reference frontend's lowering of the Song-Abbott STDP example,
+tests/golden/models/stdp_small.json.gz).  On N > 1 GPUs the inputs run whole
+on every rank and the targets are partitioned.  Its CPU sample is the same
+network at 10,000 inputs onto 1,000 neurons (1e6 synapses).
 """
 from __future__ import annotations
 
@@ -132,11 +140,27 @@ def build_model(n, indegree, ticks, seed=3):
     return synthetic.encode(synthetic.cuba_fixed_indegree(template, n=n, indegree=indegree, ticks=ticks, seed=seed))
 
 
-def cpu_sample(workdir: Path, warmup_ticks: int, timed_ticks: int):
+STDP_INPUTS, STDP_NEURONS, STDP_INDEGREE = 100_000, 10_000, 1000
+STDP_SAMPLE_INPUTS, STDP_SAMPLE_NEURONS = 10_000, 1000
+
+
+def build_stdp(n_inputs, n_neurons, indegree, ticks, seed=5):
+    import gzip
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    with gzip.open(ROOT / "tests" / "golden" / "models" / "stdp_small.json.gz", "rb") as f:
+        template = json.loads(f.read())
+    return synthetic.stdp_feedforward(template, n_inputs, n_neurons, indegree, ticks=ticks, seed=seed, spliced=True)
+
+
+def cpu_sample(workdir: Path, warmup_ticks: int, timed_ticks: int, workload: str = "c2"):
     """Oracle (CPU restatement of b2-runner) on the bounded sample network."""
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
     path = workdir / "cpu_sample.json"
-    path.write_bytes(build_model(CPU_SAMPLE_NEURONS, INDEGREE, warmup_ticks + timed_ticks + 1))
+    ticks = warmup_ticks + timed_ticks + 1
+    if workload == "stdp":
+        path.write_bytes(build_stdp(STDP_SAMPLE_INPUTS, STDP_SAMPLE_NEURONS, STDP_INDEGREE, ticks))
+    else:
+        path.write_bytes(build_model(CPU_SAMPLE_NEURONS, INDEGREE, ticks))
     out = subprocess.run([str(ROOT / "oracle" / "b2ref"), "--timed", str(warmup_ticks), str(timed_ticks), str(path)],
                          check=True, capture_output=True, text=True)
     return json.loads(out.stdout)
@@ -152,7 +176,7 @@ def run_reference(args, world, rank):
         return
     steps, warmup = args.steps, args.warmup
     with tempfile.TemporaryDirectory() as tmp:
-        s = cpu_sample(Path(tmp), REFERENCE_TICKS_PER_STEP * warmup, REFERENCE_TICKS_PER_STEP * steps)
+        s = cpu_sample(Path(tmp), REFERENCE_TICKS_PER_STEP * warmup, REFERENCE_TICKS_PER_STEP * steps, args.workload)
     total_events, total_seconds = s["synaptic_events"], s["seconds"]
     value = total_events / total_seconds if total_seconds > 0 else 0.0
     sim_seconds = s["ticks"] * DT
@@ -161,12 +185,16 @@ def run_reference(args, world, rank):
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
         "warmup": warmup, "ms_per_step": 1e3 * total_seconds / max(steps, 1), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"CUBA fixed in-degree sample: {CPU_SAMPLE_NEURONS} neurons x {INDEGREE} in-degree "
+        "config": {"workload": f"STDP feedforward sample: {STDP_SAMPLE_INPUTS} inputs onto {STDP_SAMPLE_NEURONS} "
+                               f"neurons x {STDP_INDEGREE} in-degree (config 4 scaled for one CPU core)",
+                   "inputs": STDP_SAMPLE_INPUTS, "neurons": STDP_SAMPLE_NEURONS, "indegree": STDP_INDEGREE,
+                   "dt_s": DT} if args.workload == "stdp" else
+                  {"workload": f"CUBA fixed in-degree sample: {CPU_SAMPLE_NEURONS} neurons x {INDEGREE} in-degree "
                                f"+ Poisson drive (config 2 scaled for one CPU core)",
                    "neurons": CPU_SAMPLE_NEURONS, "indegree": INDEGREE, "dt_s": DT},
         "realtime_factor": sim_seconds / total_seconds if total_seconds else None,
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
-                         "sample": f"{per_step[0]['ticks']} ticks of the {CPU_SAMPLE_NEURONS}-neuron sample after "
+                         "sample": f"{per_step[0]['ticks']} ticks of the sample network after "
                                    f"{REFERENCE_TICKS_PER_STEP * warmup} warm-up ticks"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -182,6 +210,7 @@ def main():
     ap.add_argument("--neurons", type=int, default=N_NEURONS)
     ap.add_argument("--indegree", type=int, default=INDEGREE)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="c2", choices=["c2", "stdp"])
     args = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -214,7 +243,11 @@ def main():
 
     total_ticks = (args.warmup + args.steps) * TICKS_PER_STEP
     t0 = time.time()
-    model = build_model(args.neurons, args.indegree, total_ticks + 400)
+    stdp = args.workload == "stdp"
+    if stdp:
+        model = build_stdp(STDP_INPUTS, STDP_NEURONS, STDP_INDEGREE, total_ticks + 400)
+    else:
+        model = build_model(args.neurons, args.indegree, total_ticks + 400)
     t_json = time.time() - t0
     if world > 1:
         eng = pkg.Engine(model, device=local_rank, rank=rank, world_size=world)
@@ -272,14 +305,20 @@ def main():
             return
         clock_summary = dict(clock_all[0], reasons=sorted({r for c in clock_all for r in c["reasons"]}),
                              sm_mhz_min_over_ranks=min((c["sm_mhz"] or 0) for c in clock_all))
-    local_neurons = pkg.partition(args.neurons, rank, world)
+    local_neurons = pkg.partition(STDP_NEURONS if stdp else args.neurons, rank, world)
     local_neurons = local_neurons[1] - local_neurons[0]
     hbm, peak_kind = peaks()
     ticks_prof = 400
     kernels = []
     for k in prof:
         avg_ms = k["total_ms"] / max(k["launches"], 1)
-        if "_step" in k["name"]:
+        if stdp:
+            # target-ordered on_pre scan: the 4 B source id of every local
+            # in-edge and the 8 B row offset of every local target (the
+            # delivered events' state traffic comes on top)
+            per_launch = 4 * local_neurons * STDP_INDEGREE + 8 * (local_neurons + 1) if k["name"].endswith(
+                "_targets") else 0
+        elif "_step" in k["name"]:
             # neuron update + threshold + compaction + reset: read and write
             # v, ge, gi (f64) and read lastspike (f64) per neuron, 4 B per spike
             per_launch = local_neurons * (2 * 24 + 8) + 4 * prof_spikes / ticks_prof
@@ -301,23 +340,36 @@ def main():
     cpu = None
     if not args.no_cpu_baseline and world == 1:
         with tempfile.TemporaryDirectory() as tmp:
-            s = cpu_sample(Path(tmp), CPU_SAMPLE_WARMUP, CPU_SAMPLE_TICKS)
+            s = cpu_sample(Path(tmp), CPU_SAMPLE_WARMUP, CPU_SAMPLE_TICKS, args.workload)
+        sample = (f"config 4 scaled to {STDP_SAMPLE_INPUTS} inputs onto {STDP_SAMPLE_NEURONS} neurons (in-degree "
+                  f"{STDP_INDEGREE})" if stdp else
+                  f"config 2 scaled to {CPU_SAMPLE_NEURONS} neurons (in-degree {INDEGREE})")
         cpu = {"value": s["synaptic_events"] / s["seconds"], "unit": UNIT, "cores": 1, "kind": "port",
-               "sample": f"{s['ticks']} ticks of config 2 scaled to {CPU_SAMPLE_NEURONS} neurons (in-degree "
-                         f"{INDEGREE}) after {CPU_SAMPLE_WARMUP} warm-up ticks; oracle/b2ref single thread; "
-                         f"{s['synaptic_events']} events in {s['seconds']:.3f} s"}
+               "sample": f"{s['ticks']} ticks of {sample} after {CPU_SAMPLE_WARMUP} warm-up ticks; oracle/b2ref "
+                         f"single thread; {s['synaptic_events']} events in {s['seconds']:.3f} s"}
+    if stdp:
+        config = {"workload": "config 4: STDP feedforward, 100k Poisson inputs at 15 Hz onto 10k COBA LIF neurons, "
+                              "in-degree 1000 (1e7 plastic synapses, on_pre + on_post)",
+                  "inputs": STDP_INPUTS, "neurons": STDP_NEURONS, "indegree": STDP_INDEGREE,
+                  "synapses": STDP_NEURONS * STDP_INDEGREE, "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+                  "parallelism": "single GPU" if world == 1 else
+                  f"{world} GPUs: inputs replicated on every rank, targets partitioned, target spikes exchanged "
+                  f"by peer stores over NVLink",
+                  "l2": "256 MiB buffer written between timed steps; the 1e7-edge synapse state (320 MB) exceeds L2"}
+    else:
+        config = {"workload": "config 2: CUBA 1M neurons, fixed in-degree 1000 (1e9 synapses), Poisson 100x10 Hz",
+                  "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
+                  "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+                  "parallelism": "single GPU" if world == 1 else
+                  f"{world} GPUs: target-owned partition, spikes exchanged by peer stores over NVLink",
+                  "l2": "256 MiB buffer written between timed steps; per-tick neuron state (56 MB) stays "
+                        "L2-resident within a step"}
     line = {
         "metric": METRIC, "value": events / dev if dev > 0 else 0.0, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dev / args.steps,
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
         "data": "synthetic (seeded; definition layer lowered by the reference frontend)",
-        "config": {"workload": "config 2: CUBA 1M neurons, fixed in-degree 1000 (1e9 synapses), Poisson 100x10 Hz",
-                   "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
-                   "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
-                   "parallelism": "single GPU" if world == 1 else
-                   f"{world} GPUs: target-owned partition, spikes exchanged by peer stores over NVLink",
-                   "l2": "256 MiB buffer written between timed steps; per-tick neuron state (56 MB) stays "
-                         "L2-resident within a step"},
+        "config": config,
         "realtime_factor": sim_seconds / dev if dev > 0 else None,
         "realtime_factor_e2e": sim_seconds / wall if wall > 0 else None,
         "synaptic_events": events, "spikes": spikes,
@@ -327,7 +379,8 @@ def main():
         "roofline": None if dominant is None else {
             "bound": "hbm", "kernel": dominant["name"], "achieved": dominant["achieved_gbs"], "peak": hbm,
             "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["achieved_gbs"] / hbm,
-            "traffic": STEP_DRAM_BYTES.get(local_neurons) if "_step" in dominant["name"] and world == 1 else None},
+            "traffic": STEP_DRAM_BYTES.get(local_neurons) if "_step" in dominant["name"] and world == 1 and not stdp
+            else None},
         "kernels": kernels,
         "clocks": clock_summary,
         "build": {"json_seconds": t_json, "engine_build_seconds": st0["build_seconds"],

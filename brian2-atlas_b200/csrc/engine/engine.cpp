@@ -229,6 +229,8 @@ struct Engine::Impl {
     // descending, then source ascending, then creation order)
     int tm_off = -1, tm_src = -1, tm_edge = -1, tm_delay = -1;
     uint64_t tm_targets = 0, tm_lo = 0;  // local targets [tm_lo, tm_lo + tm_targets) (synapse-level)
+    uint64_t tm_max_deg = 0;             // longest in-edge list
+    unsigned tm_warps = 1;               // warps per target (targets_group)
     int pend_offsets = -1, pend_items = -1, pend_src = -1, pend_tgt = -1;
     bool has_pending = false;
   };
@@ -334,6 +336,12 @@ struct Engine::Impl {
     // Diagnostic: deliver ordered pathways with one serial thread instead of
     // the target-ordered kernel (same results) for A/B timing.
     if (const char* e = std::getenv("B2GPU_TARGETS")) use_targets_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_TARGETS_UNROLL")) targets_unroll_ = unsigned(std::atoi(e));
+    check(targets_unroll_ >= 1 && targets_unroll_ <= 16, "target-ordered unroll must be 1 to 16");
+    if (const char* e = std::getenv("B2GPU_TARGETS_WARPS")) targets_warps_ = unsigned(std::atoi(e));
+    check(targets_warps_ == 0 || targets_warps_ == 1 || targets_warps_ == 2 || targets_warps_ == 4 ||
+              targets_warps_ == 8,
+          "warps per target must be 1, 2, 4 or 8");
     // Diagnostic: partition and exchange every population on N > 1 GPUs
     // (same results) instead of replicating the ones no synapse targets.
     if (const char* e = std::getenv("B2GPU_REPLICATE")) replicate_ = std::atoi(e) != 0;
@@ -341,6 +349,8 @@ struct Engine::Impl {
   }
   bool no_fuse_ = false;
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
+  unsigned targets_unroll_ = 4;  // 32-entry groups each warp of a target-ordered kernel keeps in flight
+  unsigned targets_warps_ = 0;   // warps per target (0: targets_group chooses)
   bool use_pdl_ = true;
   bool balance_tiles_ = true;                // tile_n_for: spread neurons over whole waves
   // Multi-GPU exchange: words per block (0: about eight blocks per SM), and
@@ -1809,6 +1819,7 @@ struct Engine::Impl {
     pw.tm_targets = clampj(tp.lo + tp.count) - pw.tm_lo;
     EventStreamDev& es = streams[size_t(pw.stream)];
     es.needs_bitmap = true;
+    pw.tm_max_deg = sd.local_edges;  // dry runs: upper bound
     if (opt.dry_run) {
       pw.tm_off = alloc(0);
       pw.tm_src = alloc(0);
@@ -1821,10 +1832,34 @@ struct Engine::Impl {
                        pw.row_edge >= 0 ? static_cast<const uint32_t*>(dptr(pw.row_edge)) : nullptr,
                        pw.uniform ? nullptr : static_cast<const uint16_t*>(dptr(pw.row_delay)), pw.max_delay,
                        pw.endpoint_count, sd.local_edges, pw.tm_lo, pw.tm_targets, off, src, edge, delay, stream);
+    std::vector<uint64_t> toff(pw.tm_targets + 1);
+    B2_CUDA(cudaMemcpy(toff.data(), off.ptr, toff.size() * 8, cudaMemcpyDeviceToHost));
+    pw.tm_max_deg = 0;
+    for (uint64_t j = 0; j < pw.tm_targets; ++j) pw.tm_max_deg = std::max(pw.tm_max_deg, toff[j + 1] - toff[j]);
     pw.tm_off = adopt(std::move(off));
     pw.tm_src = adopt(std::move(src));
     pw.tm_edge = adopt(std::move(edge));
     if (!pw.uniform) pw.tm_delay = adopt(std::move(delay));
+  }
+
+  // Warps per target of a target-ordered kernel: 1, or (when targets are too
+  // few to fill the GPU with one warp each) up to 8 warps that test disjoint
+  // 32*U-entry tiles of the target's list into shared-memory hit masks, after
+  // which the group's first warp delivers in order.  The masks of a block
+  // (8/G targets) must fit 48 KB.
+  unsigned targets_group(const PathwayDev& pw) const {
+    const uint64_t tile = 32ull * targets_unroll_;
+    const uint64_t tiles = (pw.tm_max_deg + tile - 1) / tile;
+    unsigned g = 1;
+    if (targets_warps_) g = targets_warps_;
+    else
+      while (g < 8 && 2ull * g <= tiles && pw.tm_targets * 2ull * g <= uint64_t(sm_count_) * 64) g *= 2;
+    const uint64_t nw = targets_mask_words(pw);
+    return nw * (kThreads / 32 / g) * 4 <= 48 * 1024 ? g : 1u;
+  }
+  uint64_t targets_mask_words(const PathwayDev& pw) const {
+    const uint64_t u = targets_unroll_;
+    return ((pw.tm_max_deg + 31) / 32 + u - 1) / u * u;
   }
 
   // Spike-list traversal shared by pathway kernels: warp per fired endpoint,
@@ -1978,7 +2013,7 @@ struct Engine::Impl {
       // test 32 entries at a time against the emission tick's fired bitmap,
       // and the hits run one lane at a time in lane order, separated by
       // __syncwarp (which orders the lanes' memory accesses).
-      constexpr unsigned U = 4;  // independent 32-entry groups in flight per warp
+      const unsigned U = targets_unroll_;  // independent 32-entry groups in flight per warp
       const std::string bm = P(es.bitmap, "const u32");
       o << "  const u32 lane = threadIdx.x & 31u;\n";
       o << "  const u64 warps = (u64)gridDim.x * (blockDim.x >> 5);\n";
@@ -1993,24 +2028,67 @@ struct Engine::Impl {
         o << "  const u16* tdel = " << P(pw.tm_delay, "const u16") << ";\n";
       }
       o << "  u64 events = 0;\n";
+      // hit test of the U 32-entry groups at `tb` (u64, local names q/s/h)
+      auto hit_test = [&](const std::string& tb, const std::string& end) {
+        std::ostringstream h;
+        h << "      u32 sv[" << U << "], mk[" << U << "];\n      bool in[" << U << "];\n";
+        h << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
+        h << "        const u64 q = " << tb << " + u * 32u + lane;\n        in[u] = q < " << end << ";\n";
+        h << "        sv[u] = in[u] ? __ldg(tsrc + q) : 0u;\n      }\n";
+        h << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
+        h << "        bool h = false;\n";
+        h << "        if (in[u]) {\n          const u32 s = sv[u] + " << pw.endpoint_start << "u;\n";
+        if (pw.uniform) {
+          h << "          h = (__ldg(bmw + (s >> 5)) >> (s & 31u)) & 1u;\n";
+        } else {
+          h << "          const u64 lag = __ldg(tdel + " << tb << " + u * 32u + lane);\n";
+          h << "          if (lag <= rel) h = (__ldg(" << bm << " + ((rel - lag) % " << es.bm_slots << "ull) * "
+            << es.bm_words << "ull + (s >> 5)) >> (s & 31u)) & 1u;\n";
+        }
+        h << "        }\n        mk[u] = __ballot_sync(0xffffffffu, h);\n      }\n";
+        return h.str();
+      };
+      if (pw.tm_warps > 1) {
+        // G warps per target: warp g of the group tests tiles g, g+G, ... of
+        // 32*U entries into the target's shared hit masks; after the block
+        // barrier the group's first warp walks the masks in entry order.
+        const unsigned G = pw.tm_warps, TPB = kThreads / 32 / G;
+        const uint64_t NW = targets_mask_words(pw);
+        o << "  __shared__ u32 s_mask[" << TPB * NW << "];\n";
+        o << "  const u32 warp = threadIdx.x >> 5, slot = warp / " << G << "u, gw = warp % " << G << "u;\n";
+        o << "  u32* msk = s_mask + slot * " << NW << "u;\n";
+        o << "  for (u64 t0 = (u64)blockIdx.x * " << TPB << "u; t0 < " << pw.tm_targets << "ull; t0 += (u64)gridDim.x * "
+          << TPB << "u) {\n";
+        o << "    const u64 j = t0 + slot;\n    const bool live = j < " << pw.tm_targets << "ull;\n";
+        o << "    const u64 o0 = live ? __ldg(toff + j) : 0ull, o1 = live ? __ldg(toff + j + 1) : 0ull;\n";
+        o << "    for (u64 tb = o0 + (u64)gw * " << 32 * U << "u; tb < o1; tb += " << uint64_t(G) * 32 * U << "ull) {\n";
+        o << hit_test("tb", "o1");
+        o << "      const u32 w0 = (u32)((tb - o0) >> 5);\n";
+        o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) if (lane == u) msk[w0 + u] = mk[u];\n";
+        o << "    }\n    __syncthreads();\n";
+        o << "    if (gw == 0 && live) {\n";
+        o << "      const u32 nw = (u32)((o1 - o0 + 31u) >> 5);\n";
+        o << "      for (u32 w0 = 0; w0 < nw; w0 += 32u) {\n";
+        o << "        const u32 m = w0 + lane < nw ? msk[w0 + lane] : 0u;\n";
+        o << "        events += __popc(m);\n";
+        o << "        u32 any = __ballot_sync(0xffffffffu, m != 0u);\n";
+        o << "        while (any) {\n          const u32 L = __ffs(any) - 1u;\n          any &= any - 1u;\n";
+        o << "          u32 mm = __shfl_sync(0xffffffffu, m, L);\n";
+        o << "          while (mm) {\n            const u32 b = __ffs(mm) - 1u;\n            mm &= mm - 1u;\n";
+        o << "            if (lane == b) {\n              const u64 q = o0 + (u64)(w0 + L) * 32u + b;\n";
+        o << "              " << body_fn << "(__ldg(tsrc + q), (u32)(j + " << pw.tm_lo
+          << "ull), (u64)__ldg(tedge + q), tick, t, err);\n            }\n";
+        o << "            __syncwarp();\n          }\n        }\n      }\n    }\n";
+        o << "    __syncthreads();\n  }\n";
+        o << "  if (events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + " << pw.delivered_slot
+          << ", events);\n";
+        o << kernel_tail();
+        return o.str();
+      }
       o << "  for (u64 j = (blockIdx.x * (u64)blockDim.x + threadIdx.x) >> 5; j < " << pw.tm_targets << "ull; j += warps) {\n";
       o << "    const u64 o0 = __ldg(toff + j), o1 = __ldg(toff + j + 1);\n";
       o << "    for (u64 base = o0; base < o1; base += " << 32 * U << "ull) {\n";
-      o << "      u32 sv[" << U << "], mk[" << U << "];\n      bool in[" << U << "];\n";
-      o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
-      o << "        const u64 q = base + u * 32u + lane;\n        in[u] = q < o1;\n";
-      o << "        sv[u] = in[u] ? __ldg(tsrc + q) : 0u;\n      }\n";
-      o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
-      o << "        bool h = false;\n";
-      o << "        if (in[u]) {\n          const u32 s = sv[u] + " << pw.endpoint_start << "u;\n";
-      if (pw.uniform) {
-        o << "          h = (__ldg(bmw + (s >> 5)) >> (s & 31u)) & 1u;\n";
-      } else {
-        o << "          const u64 lag = __ldg(tdel + base + u * 32u + lane);\n";
-        o << "          if (lag <= rel) h = (__ldg(" << bm << " + ((rel - lag) % " << es.bm_slots << "ull) * " << es.bm_words
-          << "ull + (s >> 5)) >> (s & 31u)) & 1u;\n";
-      }
-      o << "        }\n        mk[u] = __ballot_sync(0xffffffffu, h);\n      }\n";
+      o << hit_test("base", "o1");
       o << "#pragma unroll\n      for (u32 u = 0; u < " << U << "u; ++u) {\n";
       o << "        u32 mm = mk[u];\n        events += lane == 0 ? __popc(mm) : 0u;\n";
       o << "        while (mm) {\n          const u32 b = __ffs(mm) - 1u;\n          mm &= mm - 1u;\n";
@@ -2444,9 +2522,12 @@ struct Engine::Impl {
           bool serial = pw.mode == PathwayDev::Mode::Serial;
           o.grid = serial ? 1u : 148u * 8u;
           o.block = serial ? 32u : kThreads;
-          if (pw.mode == PathwayDev::Mode::Targets)  // one warp per target
-            o.grid = unsigned(std::max<uint64_t>(1, std::min<uint64_t>((pw.tm_targets + kThreads / 32 - 1) / (kThreads / 32),
-                                                                        148u * 8u)));
+          if (pw.mode == PathwayDev::Mode::Targets) {  // tm_warps warps per target
+            pw.tm_warps = targets_group(pw);
+            const uint64_t per_block = kThreads / 32 / pw.tm_warps;
+            o.grid = unsigned(std::max<uint64_t>(1, std::min<uint64_t>((pw.tm_targets + per_block - 1) / per_block,
+                                                                        148u * 16u)));
+          }
           paths.push_back(ps);
           specs.push_back(o);
         }

@@ -139,8 +139,65 @@ def brunel_fixed_indegree(template: dict, n: int = 4_000_000, indegree: int = 10
     return attach_protocol(doc)
 
 
+_HEX = np.frombuffer(b"0123456789abcdef", dtype=np.uint8)
+
+
+def _json_hex64(values: np.ndarray) -> bytes:
+    """JSON list of the f64 bit patterns as 16-digit hex strings (the same
+    text as json.dumps(_hex64(values))), rendered with array operations."""
+    raw = np.ascontiguousarray(values, dtype=np.float64).view(np.uint64)
+    if raw.size == 0:
+        return b"[]"
+    out = np.empty((raw.size, 19), dtype=np.uint8)
+    out[:, 0] = out[:, 17] = ord('"')
+    out[:, 18] = ord(",")
+    for k in range(16):
+        out[:, 1 + k] = _HEX[((raw >> np.uint64(60 - 4 * k)) & np.uint64(15)).astype(np.intp)]
+    return b"[" + out.tobytes()[:-1] + b"]"
+
+
+def _json_ints(values: np.ndarray) -> bytes:
+    return ("[" + ",".join(map(str, np.asarray(values).tolist())) + "]").encode()
+
+
+def _json_repeat(item: str, n: int) -> bytes:
+    return b"[" + (f'"{item}",'.encode() * n)[:-1] + b"]" if n else b"[]"
+
+
+def _splice(text: bytes, arrays: dict) -> bytes:
+    cuts = []
+    for name in arrays:
+        key = f'"@@splice:{name}@@"'.encode()
+        at = text.find(key)
+        assert at >= 0 and text.find(key, at + 1) < 0, name
+        cuts.append((at, len(key), name))
+    parts, pos = [], 0
+    for at, n, name in sorted(cuts):
+        parts += [text[pos:at], arrays[name]]
+        pos = at + n
+    parts.append(text[pos:])
+    return b"".join(parts)
+
+
+def encode_spliced(doc: dict, arrays: dict) -> bytes:
+    """encode(attach_protocol(doc)) for a document whose large arrays are
+    given pre-rendered: doc holds the string "@@splice:NAME@@" where array
+    NAME goes, and arrays[NAME] is that array's compact JSON text.  The
+    arrays sit in the instance layer, whose hash is taken over the spliced
+    canonical text, as the reference writer hashes the whole layer."""
+    layers = {}
+    for layer in ("definition", "instance", "run"):
+        text = json.dumps(doc[layer], sort_keys=True, separators=(",", ":"), ensure_ascii=False, allow_nan=False)
+        data = text.encode()
+        if layer == "instance":
+            data = _splice(data, arrays)
+        layers[layer] = hashlib.sha256(data).hexdigest()
+    doc["protocol"]["layers"] = layers
+    return _splice(encode(doc), arrays)
+
+
 def stdp_feedforward(template: dict, n_inputs: int = 100_000, n_neurons: int = 10_000, indegree: int = 1000,
-                     ticks: int = 10_000, seed: int = 5) -> dict:
+                     ticks: int = 10_000, seed: int = 5, spliced: bool = False):
     """The STDP-plastic feedforward network (the Song-Abbott example scaled
     up): n_inputs Poisson inputs at the template's rate drive n_neurons
     conductance-based LIF neurons, each receiving `indegree` inputs drawn
@@ -165,12 +222,28 @@ def stdp_feedforward(template: dict, n_inputs: int = 100_000, n_neurons: int = 1
     source = rng.integers(0, n_inputs, size=E, dtype=np.int64)
     target = np.repeat(np.arange(n_neurons, dtype=np.int64), indegree)
     si = inst["synapses"][0]
-    si["source"], si["target"] = source.tolist(), target.tolist()
     gmax = _f64(si["parameters"]["gmax"][0])
-    zero = ["0000000000000000"] * E
-    si["initial_state"] = {"w": _hex64(rng.random(E) * gmax), "Apre": zero, "Apost": zero, "lastupdate": zero}
-    for name, values in si["parameters"].items():
-        if len(values) > 1:
-            si["parameters"][name] = [values[0]] * E
+    w = rng.random(E) * gmax
     inst["rng_seed"] = seed
+    zero = "0000000000000000"
+    per_edge = [name for name, values in si["parameters"].items() if len(values) > 1]
+    if spliced:
+        # the same document, encoded without materialising per-edge Python lists
+        arrays = {"source": _json_ints(source), "target": _json_ints(target), "w": _json_hex64(w),
+                  "zero": None}
+        si["source"], si["target"] = "@@splice:source@@", "@@splice:target@@"
+        si["initial_state"] = {"w": "@@splice:w@@"}
+        for name in ("Apre", "Apost", "lastupdate"):
+            si["initial_state"][name] = f"@@splice:{name}@@"
+            arrays[name] = _json_repeat(zero, E)
+        for name in per_edge:
+            arrays[f"param_{name}"] = _json_repeat(si["parameters"][name][0], E)
+            si["parameters"][name] = f"@@splice:param_{name}@@"
+        del arrays["zero"]
+        return encode_spliced(doc, arrays)
+    si["source"], si["target"] = source.tolist(), target.tolist()
+    zeros = [zero] * E
+    si["initial_state"] = {"w": _hex64(w), "Apre": zeros, "Apost": zeros, "lastupdate": zeros}
+    for name in per_edge:
+        si["parameters"][name] = [si["parameters"][name][0]] * E
     return attach_protocol(doc)

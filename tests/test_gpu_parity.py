@@ -45,12 +45,14 @@ def assert_same_files(a, b):
         assert ea.read_bytes() == eb.read_bytes()
 
 
-@pytest.mark.parametrize("targets", ["1", "0"])
-def test_golden_fixture_bytes(pkg, tmp_path, monkeypatch, targets):
+@pytest.mark.parametrize("targets,warps", [("1", "0"), ("1", "1"), ("1", "2"), ("1", "8"), ("0", "0")])
+def test_golden_fixture_bytes(pkg, tmp_path, monkeypatch, targets, warps):
     """The reference's golden b2-runner run, reproduced on the GPU byte for
-    byte, with the per-edge-delay pathways delivered target-ordered (one warp
-    per target) and by the single-thread fold."""
+    byte, with the per-edge-delay pathways delivered target-ordered (1, 2 or
+    8 warps per target, or the planner's choice) and by the single-thread
+    fold."""
     monkeypatch.setenv("B2GPU_TARGETS", targets)
+    monkeypatch.setenv("B2GPU_TARGETS_WARPS", warps)
     out = tmp_path / "gpu"
     gpu_run(pkg, GOLDEN / "reference-v1" / "model.json", out)
     assert (out / "results.bin").read_bytes() == (GOLDEN / "reference-v1" / "results.bin").read_bytes()
@@ -202,8 +204,10 @@ def test_stdp_targets_equal_serial_fold(pkg, tmp_path, monkeypatch):
     path = tmp_path / "stdp_40k.json"
     path.write_bytes(synthetic.encode(synthetic.stdp_feedforward(template, 2000, 200, 200, ticks=1500, seed=11)))
     stats = {}
-    for mode in ("1", "0"):
+    for mode, warps in (("0", "0"), ("1", "1"), ("1", "4")):
         monkeypatch.setenv("B2GPU_TARGETS", mode)
-        stats[mode] = gpu_run(pkg, path, tmp_path / f"gpu{mode}")
-    assert stats["1"]["synaptic_events"] == stats["0"]["synaptic_events"] > 0
-    assert_same_files(tmp_path / "gpu1", tmp_path / "gpu0")
+        monkeypatch.setenv("B2GPU_TARGETS_WARPS", warps)
+        stats[mode + warps] = gpu_run(pkg, path, tmp_path / f"gpu{mode}{warps}")
+    assert stats["11"]["synaptic_events"] == stats["14"]["synaptic_events"] == stats["00"]["synaptic_events"] > 0
+    assert_same_files(tmp_path / "gpu11", tmp_path / "gpu00")
+    assert_same_files(tmp_path / "gpu14", tmp_path / "gpu00")

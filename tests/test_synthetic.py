@@ -34,3 +34,20 @@ def test_brunel_scaler_keeps_f32_state_and_drive():
     doc = synthetic.brunel_fixed_indegree(template, n=10000, indegree=1000, ticks=20, seed=4)
     v = doc["instance"]["populations"][0]["initial_state"]["v"]
     assert len(v) == 10000 and all(len(x) == 8 for x in v[:10])
+
+
+def test_stdp_spliced_encoding_is_the_plain_encoding(pkg):
+    """The scaled STDP network's array-rendered encoding (used at 1e7 edges)
+    is byte-identical to encode(attach_protocol(doc)), canonical hashes
+    included, and the engine's validator accepts it."""
+    import gzip
+    with gzip.open(MODELS / "stdp_small.json.gz", "rb") as f:
+        template = json.loads(f.read())
+    plain = synthetic.encode(synthetic.stdp_feedforward(template, 3000, 50, 40, ticks=100, seed=2))
+    spliced = synthetic.stdp_feedforward(template, 3000, 50, 40, ticks=100, seed=2, spliced=True)
+    assert plain == spliced
+    doc = json.loads(spliced)
+    inst = doc["instance"]["synapses"][0]
+    assert len(inst["source"]) == len(inst["initial_state"]["w"]) == 50 * 40
+    assert max(inst["source"]) < 3000 and inst["target"][:41] == [0] * 40 + [1]
+    assert "stdp_pre_targets" in pkg.codegen(spliced)  # layer hashes verified on load

@@ -194,6 +194,16 @@ struct Engine::Impl {
     // before the node that produces the event in a tick (it then records the
     // previous tick's list, as the reference's `fired` still holds it)
     std::vector<int> evmon_stream, evmon_lag;
+    // per EventMonitor with recorded variables: one sample ring per variable,
+    // indexed like the event stream's ring (record j of the stream's list at
+    // ring position j), drained to host bytes alongside the spikes
+    struct EvMonVars {
+      std::vector<int> ring;
+      std::vector<size_t> width;
+      std::vector<std::vector<uint8_t>> host;
+      uint64_t drained = 0;
+    };
+    std::vector<EvMonVars> evmon_vars;
     // state monitor
     int mon_records = -1;
     size_t mon_nrec = 0;            // records owned by this rank
@@ -444,7 +454,13 @@ struct Engine::Impl {
       check(!p.spatial, "spatial neurons are not supported by the GPU engine");
       check(p.rate_monitor_count == 0, "rate monitors are not supported by the GPU engine");
       for (const auto& em : p.event_monitors)
-        check(em.variables.empty(), "EventMonitor variables are not supported by the GPU engine yet");
+        for (const auto& v : em.variables) {
+          check(world == 1, "multi-GPU runs do not support EventMonitor variables");
+          bool known = false;
+          for (const auto& st : p.states) known |= st.name == v;
+          for (const auto& pa : p.parameters) known |= pa.name == v && pa.dtype == DType::F64;
+          check(known, "EventMonitor variable '" + v + "' must be a state or an f64 parameter of its population");
+        }
       check(p.steps == steps, "population steps must match the run clock");
       for (const auto& c : p.code_objects) check(!c.adaptive, "adaptive integrators are not supported by the GPU engine");
     }
@@ -603,6 +619,42 @@ struct Engine::Impl {
       // edge_ids[k]).  Per-edge arrays are indexed by local edge.
       std::vector<uint32_t> edge_ids;
       const PopDev& tpop = pops[def.target_population];
+      // Procedural topologies: the source-major device CSR (rows hold the
+      // global synapse-level target j; the edge id is the row position, the
+      // reference's creation order), built once per synapse and shared by its
+      // pathways, per-edge programs and summed variables.
+      int proc_off = -1, proc_rows = -1;
+      uint64_t proc_max_row = 0;
+      auto procedural_csr = [&]() {
+        if (proc_off >= 0) return;
+        if (opt.dry_run) {
+          proc_off = alloc(0);
+          proc_rows = alloc(0);
+          return;
+        }
+        DeviceBuffer offs, rows;
+        uint64_t local_edges = 0;
+        // synapse-level targets j whose population index target_start + j
+        // this rank owns
+        auto clampj = [&](uint64_t x) {
+          return x <= def.target_start ? uint64_t(0) : std::min<uint64_t>(x - def.target_start, def.target_count);
+        };
+        const uint64_t j0 = clampj(tpop.lo), j1 = clampj(tpop.lo + tpop.count);
+        if (topo.kind == b2ir::Topology::Kind::FixedIndegree)
+          build_fixed_indegree_csr(def.source_count, def.target_count, topo.indegree, topo.seed, j0, j1, offs, rows,
+                                   local_edges, stream);
+        else
+          build_fixed_total_csr(def.source_count, def.target_count, topo.edge_count, topo.seed, j0, j1, offs, rows,
+                                local_edges, stream);
+        check(world > 1 || local_edges == sd.edges, "procedural edge count mismatch");
+        if (world > 1) sd.local_edges = local_edges;
+        std::vector<uint64_t> host_offs(def.source_count + 1);
+        B2_CUDA(cudaMemcpy(host_offs.data(), offs.ptr, host_offs.size() * 8, cudaMemcpyDeviceToHost));
+        for (size_t i = 0; i < def.source_count; ++i)
+          proc_max_row = std::max<uint64_t>(proc_max_row, host_offs[i + 1] - host_offs[i]);
+        proc_off = adopt(std::move(offs));
+        proc_rows = adopt(std::move(rows));
+      };
       if (!procedural) {
         src_h = binary ? std::move(csr.source) : inst.source;
         tgt_h = binary ? std::move(csr.target) : inst.target;
@@ -723,34 +775,30 @@ struct Engine::Impl {
           if (!identity) pd.row_edge = upload(row_edge.data(), std::max<size_t>(row_edge.size(), 1) * 4);
           if (!pd.uniform) pd.row_delay = upload(row_delay.data(), std::max<size_t>(row_delay.size(), 1) * 2);
         } else {
-          check(pd.is_pre, "procedural topologies support on_pre pathways only");
           check(pd.uniform, "procedural topologies with per-edge delays are not supported by the GPU engine yet");
-          if (opt.dry_run) {
+          check(pd.is_pre || world == 1, "multi-GPU runs support on_pre pathways on procedural topologies only");
+          procedural_csr();
+          if (pd.is_pre) {
+            pd.offsets = proc_off;
+            pd.row_other = proc_rows;
+            pd.max_row = proc_max_row;
+          } else if (opt.dry_run) {
             pd.offsets = alloc(0);
             pd.row_other = alloc(0);
+            pd.row_edge = alloc(0);
           } else {
-            DeviceBuffer offs, rows;
-            uint64_t local_edges = 0;
-            // synapse-level targets j whose population index target_start + j
-            // this rank owns
-            auto clampj = [&](uint64_t x) {
-              return x <= def.target_start ? uint64_t(0) : std::min<uint64_t>(x - def.target_start, def.target_count);
-            };
-            const uint64_t j0 = clampj(tpop.lo), j1 = clampj(tpop.lo + tpop.count);
-            if (topo.kind == b2ir::Topology::Kind::FixedIndegree)
-              build_fixed_indegree_csr(def.source_count, def.target_count, topo.indegree, topo.seed, j0, j1, offs,
-                                       rows, local_edges, stream);
-            else
-              build_fixed_total_csr(def.source_count, def.target_count, topo.edge_count, topo.seed, j0, j1, offs,
-                                    rows, local_edges, stream);
-            check(world > 1 || local_edges == sd.edges, "procedural edge count mismatch");
-            if (world > 1) sd.local_edges = local_edges;
-            std::vector<uint64_t> host_offs(def.source_count + 1);
-            B2_CUDA(cudaMemcpy(host_offs.data(), offs.ptr, host_offs.size() * 8, cudaMemcpyDeviceToHost));
-            for (size_t i = 0; i < def.source_count; ++i)
+            // rows over targets: the target-major view (sources, edge ids)
+            DeviceBuffer off, src, edge, unused;
+            build_target_major(static_cast<const uint64_t*>(dptr(proc_off)),
+                               static_cast<const uint32_t*>(dptr(proc_rows)), nullptr, nullptr, 0, def.source_count,
+                               sd.local_edges, 0, def.target_count, off, src, edge, unused, stream);
+            std::vector<uint64_t> host_offs(def.target_count + 1);
+            B2_CUDA(cudaMemcpy(host_offs.data(), off.ptr, host_offs.size() * 8, cudaMemcpyDeviceToHost));
+            for (size_t i = 0; i < def.target_count; ++i)
               pd.max_row = std::max<uint64_t>(pd.max_row, host_offs[i + 1] - host_offs[i]);
-            pd.offsets = adopt(std::move(offs));
-            pd.row_other = adopt(std::move(rows));
+            pd.offsets = adopt(std::move(off));
+            pd.row_other = adopt(std::move(src));
+            pd.row_edge = adopt(std::move(edge));
           }
         }
         // Pending (continuation) events, validated like model.rs:4315-4337,
@@ -823,8 +871,19 @@ struct Engine::Impl {
       for (const auto& code : def.code_objects)
         edge_programs |= code.kind == "synapse_state_update" || code.kind == "synapse_subexpression_update" ||
                          code.kind == "synapse_run_regularly";
-      if (edge_programs) {
-        check(!procedural, "synapse state updates on procedural topologies are not supported by the GPU engine yet");
+      if (edge_programs && procedural) {
+        // edge id = source-major position: its target is the row entry, its
+        // source the row that holds it
+        procedural_csr();
+        sd.edge_tgt = proc_rows;
+        if (opt.dry_run) {
+          sd.edge_src = alloc(0);
+        } else {
+          DeviceBuffer src;
+          csr_row_sources(static_cast<const uint64_t*>(dptr(proc_off)), def.source_count, sd.local_edges, src, stream);
+          sd.edge_src = adopt(std::move(src));
+        }
+      } else if (edge_programs) {
         std::vector<uint32_t> es(sd.local_edges), et(sd.local_edges);
         for (size_t k = 0; k < sd.local_edges; ++k) {
           es[k] = src_h[gid(k)];
@@ -839,7 +898,6 @@ struct Engine::Impl {
       for (size_t c = 0; c < def.code_objects.size(); ++c) {
         const auto& code = def.code_objects[c];
         if (code.kind != "summed_variable") continue;
-        check(!procedural, "summed variables on procedural topologies are not supported by the GPU engine yet");
         SynDev::Summed sv;
         sv.code = c;
         sv.to_pre = code.summed_target && *code.summed_target == "pre";
@@ -855,6 +913,29 @@ struct Engine::Impl {
         check(sv.dest_state < dpop.states.size(), "missing summed target state");
         const DType dt = dpop.states[sv.dest_state].dtype;
         check(dt == DType::F64 || dt == DType::F32, "summed variables require floating-point state");
+        if (procedural) {
+          // to_pre: the source-major CSR itself (edge id = position); to_post:
+          // its target-major view (positions ascending per target)
+          procedural_csr();
+          if (sv.to_pre) {
+            sv.offsets = proc_off;
+            sv.row_other = proc_rows;
+          } else if (opt.dry_run) {
+            sv.offsets = alloc(0);
+            sv.row_other = alloc(0);
+            sv.row_edge = alloc(0);
+          } else {
+            DeviceBuffer off, src, edge, unused;
+            build_target_major(static_cast<const uint64_t*>(dptr(proc_off)),
+                               static_cast<const uint32_t*>(dptr(proc_rows)), nullptr, nullptr, 0, def.source_count,
+                               sd.local_edges, 0, def.target_count, off, src, edge, unused, stream);
+            sv.offsets = adopt(std::move(off));
+            sv.row_other = adopt(std::move(src));
+            sv.row_edge = adopt(std::move(edge));
+          }
+          sd.summed.push_back(sv);
+          continue;
+        }
         const auto& idx = sv.to_pre ? src_h : tgt_h;
         const auto& other = sv.to_pre ? tgt_h : src_h;
         const size_t L = sd.local_edges;
@@ -1483,13 +1564,14 @@ struct Engine::Impl {
     o << "  if (d < " << d1 << "ull) {\n";
     o << "    const u64* off = " << P(sv.offsets, "const u64") << ";\n";
     o << "    const u32* other = " << P(sv.row_other, "const u32") << ";\n";
-    o << "    const u32* ed = " << P(sv.row_edge, "const u32") << ";\n";
+    if (sv.row_edge >= 0) o << "    const u32* ed = " << P(sv.row_edge, "const u32") << ";\n";
+    const std::string edge = sv.row_edge >= 0 ? "(u64)ed[q]" : "q";
     o << "    " << ct << " acc = " << narrow(dt, "0.0") << ";\n";
     o << "    for (u64 q = off[d]; q < off[d + 1]; ++q) {\n";
     if (sv.to_pre)
-      o << "      const double v = " << body << "((u32)d, other[q], (u64)ed[q], tick, t, err);\n";
+      o << "      const double v = " << body << "((u32)d, other[q], " << edge << ", tick, t, err);\n";
     else
-      o << "      const double v = " << body << "(other[q], (u32)d, (u64)ed[q], tick, t, err);\n";
+      o << "      const double v = " << body << "(other[q], (u32)d, " << edge << ", tick, t, err);\n";
     o << "      acc = " << narrow(dt, widen(dt, "acc") + " + v") << ";\n    }\n";
     o << "    " << P(dp.states[sv.dest_state].ptr, ct) << "[d + " << uint64_t(sv.dest_start) - dp.lo << "ull] = acc;\n";
     o << "  }\n";
@@ -1576,6 +1658,45 @@ struct Engine::Impl {
       << u64lit(es.mask) << "] = " << P(pd.gen_ids, "const u32") << "[j];\n";
     o << "  if (threadIdx.x == 0) {\n    " << P(es.tick_start, "u64") << "[rel + 1] = base + (b - a);\n";
     o << "    if (base + (b - a) - " << floor_of(size_t(stream_id)) << " > " << u64lit(es.cap) << ") err |= " << kErrRing << "u;\n  }\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
+  // EventMonitor variables (record_events, executor.rs:3053-3080): for every
+  // event of the monitored list (this tick's, or the previous tick's when the
+  // monitor runs before the event's producer), the variables' current values,
+  // stored at the event's ring position.
+  std::string gen_evmon(const std::string& name, size_t p, size_t k) {
+    const auto& def = m.populations[p];
+    const PopDev& pd = pops[p];
+    const auto& em = def.event_monitors[k];
+    const EventStreamDev& es = streams[size_t(pd.evmon_stream[k])];
+    const size_t lag = size_t(pd.evmon_lag[k]);
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  if (rel < " << lag << "ull) return;\n  const u64 te = rel - " << lag << "ull;\n";
+    o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n";
+    o << "  for (u64 j = ts[te] + blockIdx.x * (u64)blockDim.x + threadIdx.x; j < ts[te + 1]; j += (u64)gridDim.x * blockDim.x) {\n";
+    o << "    const u64 r = j & " << u64lit(es.mask) << ";\n";
+    o << "    const u32 n = " << P(es.ring, "const u32") << "[r];\n";
+    for (size_t v = 0; v < em.variables.size(); ++v) {
+      const std::string& name_v = em.variables[v];
+      const int out = pd.evmon_vars[k].ring[v];
+      bool done_v = false;
+      for (size_t s = 0; s < def.states.size() && !done_v; ++s)
+        if (def.states[s].name == name_v) {
+          const char* ct = storage_ctype(def.states[s].dtype);
+          o << "    ((" << ct << "*)g_ptr[" << out << "])[r] = " << P(pd.states[s].ptr, ct) << "[n];\n";
+          done_v = true;
+        }
+      if (done_v) continue;
+      auto ptr = pd.param_ptr.find(name_v);
+      if (ptr != pd.param_ptr.end())
+        o << "    ((double*)g_ptr[" << out << "])[r] = " << P(ptr->second, "const double") << "[n];\n";
+      else
+        o << "    ((double*)g_ptr[" << out << "])[r] = " << double_literal(pd.param_const.at(name_v)) << ";\n";
+    }
+    o << "  }\n";
     o << kernel_tail();
     return o.str();
   }
@@ -2275,6 +2396,29 @@ struct Engine::Impl {
             pdv.evmon_lag.resize(def.event_monitors.size(), 0);
             pdv.evmon_stream[node.item_index] = pdv.stream_of_event[e];
             pdv.evmon_lag[node.item_index] = producer < idx ? 0 : 1;
+            if (!em.variables.empty()) {
+              // sample kernel at the monitor's place in the tick; with lag 1
+              // the previous tick's list must still be in the ring
+              EventStreamDev& es = streams[size_t(pdv.stream_of_event[e])];
+              es.max_delay = std::max<size_t>(es.max_delay, size_t(pdv.evmon_lag[node.item_index]));
+              pdv.evmon_vars.resize(def.event_monitors.size());
+              auto& ev = pdv.evmon_vars[node.item_index];
+              for (const auto& v : em.variables) {
+                size_t w = 8;
+                for (const auto& st : def.states)
+                  if (st.name == v) w = b2ir::dtype_bytes(st.dtype);
+                ev.width.push_back(w);
+                ev.ring.push_back(alloc(es.cap * w));
+                ev.host.emplace_back();
+              }
+              OpSpec o;
+              o.base = def.name + "_" + em.name;
+              o.text = "evmon";
+              o.index = p;
+              o.grid = 148;
+              o.fuse_path = int(node.item_index);  // monitor index
+              specs.push_back(o);
+            }
             break;
           }
           case b2ir::ScheduleOp::EventSource: {
@@ -2584,6 +2728,7 @@ struct Engine::Impl {
         case OpSpec::Kind::Text:
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
+          else if (o.text == "evmon") kernels << gen_evmon(nm, o.index, size_t(o.fuse_path));
           else if (o.text == "synprog") {
             const SynProgSpec& sp = synprog_specs[o.index];
             std::string body = "b2_synprog_" + std::to_string(kid);
@@ -2747,6 +2892,34 @@ struct Engine::Impl {
       for (size_t k = 1; k < ts.size(); ++k) es.starts.push_back(ts[k]);
       es.drained_pos = b;
     }
+    // EventMonitor samples of the ticks whose sample kernel has run: all of
+    // [rel0, rel1) for lag 0, one tick less for a monitor that samples the
+    // previous tick's list
+    for (auto& pd : pops)
+      for (size_t k = 0; k < pd.evmon_vars.size(); ++k) {
+        auto& ev = pd.evmon_vars[k];
+        if (ev.ring.empty()) continue;
+        const EventStreamDev& es = streams[size_t(pd.evmon_stream[k])];
+        const size_t lag = size_t(pd.evmon_lag[k]);
+        if (rel1 < lag) continue;
+        const uint64_t b = es.starts[rel1 - lag];
+        for (size_t v = 0; v < ev.ring.size(); ++v) {
+          const size_t w = ev.width[v];
+          auto& host = ev.host[v];
+          const size_t old = host.size();
+          host.resize(old + (b - ev.drained) * w);
+          uint64_t pos = ev.drained;
+          while (pos < b) {
+            uint64_t idx = pos & es.mask;
+            uint64_t n = std::min<uint64_t>(b - pos, es.cap - idx);
+            B2_CUDA(cudaMemcpy(host.data() + old + (pos - ev.drained) * w, static_cast<uint8_t*>(dptr(ev.ring[v])) + idx * w,
+                               n * w, cudaMemcpyDeviceToHost));
+            pos += n;
+          }
+          st.d2h_bytes += (b - ev.drained) * w;
+        }
+        ev.drained = b;
+      }
   }
 
   void update_floor(size_t rel_now) {
@@ -3081,6 +3254,17 @@ struct Engine::Impl {
             for (uint64_t x = es.starts[rel - lag]; x < es.starts[rel - lag + 1]; ++x)
               er.events.push_back({start_tick + rel, es.ids[x]});
           check(er.events.size() <= 10'000'000, "EventMonitor recording budget exceeded");
+          if (k < pd.evmon_vars.size())
+            for (size_t v = 0; v < pd.evmon_vars[k].ring.size(); ++v) {
+              b2dump::Column c;
+              const std::string& vn = def.event_monitors[k].variables[v];
+              c.dtype = DType::F64;
+              for (const auto& st2 : def.states)
+                if (st2.name == vn) c.dtype = st2.dtype;
+              c.bytes = pd.evmon_vars[k].host[v];
+              check(c.bytes.size() == er.events.size() * b2ir::dtype_bytes(c.dtype), "EventMonitor sample count mismatch");
+              er.samples.push_back(std::move(c));
+            }
         }
         pr.event_monitors.push_back(std::move(er));
       }

@@ -292,6 +292,15 @@ __global__ void gather_target_major(const uint32_t* __restrict__ pos, uint64_t E
 
 }  // namespace
 
+void csr_row_sources(const uint64_t* d_offsets, uint64_t S, uint64_t E, DeviceBuffer& src, cudaStream_t stream) {
+  b2ir::check(E <= UINT32_MAX && S <= UINT32_MAX, "row sources need u32 indices");
+  src = DeviceBuffer(std::max<uint64_t>(E, 1) * 4);
+  if (E == 0) return;
+  row_sources<<<grid_for(S * 32, 256), 256, 0, stream>>>(d_offsets, S, src.as<uint32_t>());
+  B2_CUDA(cudaGetLastError());
+  B2_CUDA(cudaStreamSynchronize(stream));
+}
+
 void build_target_major(const uint64_t* d_offsets, const uint32_t* d_row_other, const uint32_t* d_row_edge,
                         const uint16_t* d_row_delay, uint64_t max_delay, uint64_t S, uint64_t E, uint64_t t_lo,
                         uint64_t T, DeviceBuffer& tm_offsets, DeviceBuffer& tm_src, DeviceBuffer& tm_edge,

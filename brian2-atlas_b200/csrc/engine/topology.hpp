@@ -21,6 +21,10 @@ void build_fixed_total_csr(uint64_t S, uint64_t T, uint64_t E, uint64_t seed, ui
                            DeviceBuffer& offsets, DeviceBuffer& row_targets, uint64_t& local_edges,
                            cudaStream_t stream);
 
+// Row (source) index of every position of a source-major CSR with S rows and
+// E entries (u32 per entry).
+void csr_row_sources(const uint64_t* d_offsets, uint64_t S, uint64_t E, DeviceBuffer& src, cudaStream_t stream);
+
 // Target-major view of a source-major CSR restricted to the targets
 // [t_lo, t_lo + T): tm_offsets[T+1] (u64), and per entry the source index
 // (u32), the edge index (row_edge[q], or the position q when row_edge is null)

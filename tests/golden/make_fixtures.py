@@ -72,7 +72,17 @@ def write_model(model: dict, name: str) -> Path:
     return path
 
 
-def cuba_events(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 1000, seed: int = 6) -> dict:
+def event_variables(reference: Path) -> dict:
+    """cuba_events with recorded variables: `near` events record v and ge
+    (after the thresholds, before the reset), start-slot spike events record
+    v (after the previous tick's reset) and the per-neuron parameter vt0;
+    also runs Brian2's numpy runtime on the same network and saves the
+    monitors' records."""
+    return cuba_events(reference, seed=8, variables=True)
+
+
+def cuba_events(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 1000, seed: int = 6,
+                variables: bool = False) -> dict:
     """CUBA with a custom event `near` (v > -55 mV) and two EventMonitors: one
     on `near` in the thresholds slot, one on `spike` in the start slot (which,
     in the reference's schedule, records the previous tick's spikes)."""
@@ -89,10 +99,14 @@ def cuba_events(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 1000
     dgi/dt = -gi/taui : volt
     """
     clock = b.Clock(dt=0.1 * b.ms, name="clock")
+    if variables:
+        eqs += "vt0 : volt (constant)\n"
     P = b.NeuronGroup(n, eqs, threshold="v>Vt", reset="v = Vr", refractory=5 * b.ms, method="exact",
                       events={"near": "v > -55*mV"}, name="neurons", clock=clock)
     rng = np.random.default_rng(seed)
     P.v = Vr + rng.random(n) * (Vt - Vr)
+    if variables:
+        P.vt0 = Vt + rng.random(n) * b.mV
     we, wi = (60 * 0.27 / 10) * b.mV, (-20 * 4.5 / 10) * b.mV
     Ce = b.Synapses(P, P, on_pre="ge += we", name="exc", clock=clock)
     Ci = b.Synapses(P, P, on_pre="gi += wi", name="inh", clock=clock)
@@ -103,11 +117,23 @@ def cuba_events(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 1000
     Ce.connect(i=src[e], j=tgt[e])
     Ci.connect(i=src[~e], j=tgt[~e])
     spikes = b.SpikeMonitor(P, name="spikes")
-    near = b.EventMonitor(P, "near", name="near_events")
-    late = b.EventMonitor(P, "spike", name="spike_events_at_start", when="start")
+    near = b.EventMonitor(P, "near", name="near_events", variables=["v", "ge"] if variables else None)
+    late = b.EventMonitor(P, "spike", name="spike_events_at_start", when="start",
+                          variables=["v", "vt0"] if variables else None)
     net = b.Network(P, Ce, Ci, spikes, near, late)
     ns = dict(taum=taum, taue=taue, taui=taui, Vt=Vt, Vr=Vr, El=El, we=we, wi=wi)
-    return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+    model = lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+    if variables:
+        b.prefs.codegen.target = "numpy"
+        net.run(ticks * 0.1 * b.ms, namespace=ns)
+        # the first 20,000 `near` records (and their total) keep the fixture small
+        k = 20000
+        np.savez_compressed(HERE / "brian_numpy" / "event_variables_small.npz", near_count=len(near.i),
+                            near_i=np.array(near.i[:k]), near_t=np.array(near.t[:k] / b.second),
+                            near_v=np.array(near.v[:k] / b.volt), near_ge=np.array(near.ge[:k] / b.volt),
+                            late_i=np.array(late.i[:]), late_t=np.array(late.t / b.second),
+                            late_v=np.array(late.v / b.volt), late_vt0=np.array(late.vt0 / b.volt))
+    return model
 
 
 def gap_junctions(reference: Path, n: int = 300, p: float = 0.05, ticks: int = 1000, seed: int = 7) -> dict:
@@ -234,7 +260,8 @@ def main() -> None:
     args = ap.parse_args()
     if args.only:
         prepare_frontend(Path(args.reference))
-        make = {"cuba_events_small": cuba_events, "gap_junctions_small": gap_junctions,
+        make = {"cuba_events_small": cuba_events, "event_variables_small": event_variables,
+                "gap_junctions_small": gap_junctions,
                 "synapse_updates_small": synapse_updates, "timed_input_small": timed_input}[args.only]
         write_model(make(Path(args.reference)), args.only)
         print("wrote", args.only)

@@ -16,7 +16,7 @@ import re
 
 import pytest
 
-from conftest import GOLDEN, MODELS, ROOT, encode_model
+from conftest import GOLDEN, MODELS, ROOT, encode_model, procedural_variant
 
 
 def declared_symbols():
@@ -128,3 +128,14 @@ def test_malformed_document_is_rejected(pkg):
         pkg.codegen(b"{not json")
     with pytest.raises(pkg.B2GpuError, match="schema"):
         pkg.codegen(json.dumps({"schema": "other"}).encode())
+
+
+def test_codegen_procedural_synapse_programs(pkg):
+    """Summed variables, synaptic state updates, run_regularly and on_post on
+    fixed in-degree topologies: the engine derives their edge endpoints and
+    destination-major rows from the device-built source-major CSR."""
+    names = kernels(pkg.codegen(procedural_variant("gap_junctions_small", 15)))
+    assert names[1].endswith("gaps_summed_variable_Igap_post")
+    names = kernels(pkg.codegen(procedural_variant("synapse_updates_small", 40)))
+    assert [n.split("_", 2)[2] for n in names] == ["decay", "inputs_step", "neurons_step", "stdp_stateupdater",
+                                                   "stdp_pre_targets", "stdp_post_edges"]

@@ -15,7 +15,7 @@ import json
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, MODELS, encode_model, model_file, run_oracle
+from conftest import GOLDEN, MODELS, encode_model, model_file, procedural_variant, run_oracle
 from b2results import load_model, read_results
 
 pytestmark = pytest.mark.gpu
@@ -77,6 +77,18 @@ def test_golden_variants_match_oracle(pkg, oracle, tmp_path, expr):
     from test_abi import golden_variant
     path = tmp_path / "model.json"
     path.write_bytes(golden_variant(expr))
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
+@pytest.mark.parametrize("name,indegree", [("gap_junctions_small", 15), ("synapse_updates_small", 40)])
+def test_procedural_synapse_programs_match_oracle(pkg, oracle, tmp_path, name, indegree):
+    """Summed variables, synaptic state updates, run_regularly, target-ordered
+    on_pre and on_post over fixed in-degree topologies generated on the
+    device, against the oracle's host-side generation, byte for byte."""
+    path = tmp_path / f"{name}_fixed_indegree.json"
+    path.write_bytes(procedural_variant(name, indegree))
     gpu_run(pkg, path, tmp_path / "gpu")
     run_oracle(oracle, path, tmp_path / "ref")
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")

@@ -241,6 +241,12 @@ struct Engine::Impl {
     uint64_t tm_targets = 0, tm_lo = 0;  // local targets [tm_lo, tm_lo + tm_targets) (synapse-level)
     uint64_t tm_max_deg = 0;             // longest in-edge list
     unsigned tm_warps = 1;               // warps per target (targets_group)
+    // event-driven variant (one delay): a scatter kernel appends each event
+    // (source << 32 | row position) to its target's bucket (capacity = the
+    // target's in-degree, at tm_off) and lists the targets it touched; a
+    // delivery kernel sorts each listed bucket and runs the bodies in order
+    bool tm_events = false;
+    int tm_cnt = -1, tm_bucket = -1, tm_active = -1, tm_nactive = -1;
     int pend_offsets = -1, pend_items = -1, pend_src = -1, pend_tgt = -1;
     bool has_pending = false;
   };
@@ -349,6 +355,10 @@ struct Engine::Impl {
     if (const char* e = std::getenv("B2GPU_TARGETS_UNROLL")) targets_unroll_ = unsigned(std::atoi(e));
     check(targets_unroll_ >= 1 && targets_unroll_ <= 16, "target-ordered unroll must be 1 to 16");
     if (const char* e = std::getenv("B2GPU_TARGETS_WARPS")) targets_warps_ = unsigned(std::atoi(e));
+    if (const char* e = std::getenv("B2GPU_TARGETS_SMEM")) targets_smem_bitmap_ = std::atoi(e) != 0;
+    // Diagnostic: deliver single-delay target-ordered pathways with the
+    // bitmap scan instead of the event buckets (same results).
+    if (const char* e = std::getenv("B2GPU_TARGETS_SCAN")) targets_scan_ = std::atoi(e) != 0;
     check(targets_warps_ == 0 || targets_warps_ == 1 || targets_warps_ == 2 || targets_warps_ == 4 ||
               targets_warps_ == 8,
           "warps per target must be 1, 2, 4 or 8");
@@ -361,6 +371,8 @@ struct Engine::Impl {
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
   unsigned targets_unroll_ = 4;  // 32-entry groups each warp of a target-ordered kernel keeps in flight
   unsigned targets_warps_ = 0;   // warps per target (0: targets_group chooses)
+  bool targets_smem_bitmap_ = true;  // stage the fired bitmap slot in shared memory
+  bool targets_scan_ = false;        // scan variant also for single-delay pathways
   bool use_pdl_ = true;
   bool balance_tiles_ = true;                // tile_n_for: spread neurons over whole waves
   // Multi-GPU exchange: words per block (0: about eight blocks per SM), and
@@ -1905,6 +1917,7 @@ struct Engine::Impl {
           for (const auto& [w, r] : pr.writes)
             if (w.kind == WriteTarget::Kind::Neuron && w.index == b.second.index) return false;
     if (syns[pw.synapse].local_edges > UINT32_MAX || def.target_count >= UINT32_MAX) return false;
+    if (pw.uniform && !targets_scan_) return true;  // event buckets: any source stream
     const EventStreamDev& es = streams[size_t(pw.stream)];
     const uint64_t words = (m.populations[es.pop].count + 31) / 32;
     if (words * (es.max_delay + 1) * 4 > (uint64_t(1) << 30)) return false;
@@ -1939,7 +1952,16 @@ struct Engine::Impl {
     pw.tm_lo = clampj(tp.lo);
     pw.tm_targets = clampj(tp.lo + tp.count) - pw.tm_lo;
     EventStreamDev& es = streams[size_t(pw.stream)];
-    es.needs_bitmap = true;
+    pw.tm_events = pw.uniform && !targets_scan_;
+    es.needs_bitmap |= !pw.tm_events;
+    if (pw.tm_events) {
+      pw.tm_cnt = alloc(std::max<uint64_t>(pw.tm_targets, 1) * 4);
+      memset_dev(pw.tm_cnt, std::max<uint64_t>(pw.tm_targets, 1) * 4);
+      pw.tm_bucket = alloc(std::max<uint64_t>(sd.local_edges, 1) * 8);
+      pw.tm_active = alloc(std::max<uint64_t>(pw.tm_targets, 1) * 4);
+      pw.tm_nactive = alloc(16);
+      memset_dev(pw.tm_nactive, 16);
+    }
     pw.tm_max_deg = sd.local_edges;  // dry runs: upper bound
     if (opt.dry_run) {
       pw.tm_off = alloc(0);
@@ -1958,6 +1980,7 @@ struct Engine::Impl {
     pw.tm_max_deg = 0;
     for (uint64_t j = 0; j < pw.tm_targets; ++j) pw.tm_max_deg = std::max(pw.tm_max_deg, toff[j + 1] - toff[j]);
     pw.tm_off = adopt(std::move(off));
+    if (pw.tm_events) return;  // the buckets carry sources and positions
     pw.tm_src = adopt(std::move(src));
     pw.tm_edge = adopt(std::move(edge));
     if (!pw.uniform) pw.tm_delay = adopt(std::move(delay));
@@ -2128,6 +2151,42 @@ struct Engine::Impl {
       o << kernel_tail();
       return o.str();
     }
+    if (pw.mode == PathwayDev::Mode::Targets && pw.tm_events) {
+      // Bucket scatter: work items (fired source, row chunk) as in the
+      // edge-parallel kernel; each event takes the next slot of its target's
+      // bucket, and the first event of a target lists the target.  The
+      // delivery kernel of the same tick consumes list rel & 1; this kernel
+      // clears the other list's count, which the previous tick consumed.
+      const uint64_t chunks = std::max<uint64_t>(1, (pw.max_row + row_chunk() - 1) / row_chunk());
+      o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n  const u64 te = rel - " << pw.delay << "ull;\n";
+      o << "  u32* nact = " << P(pw.tm_nactive, "u32") << ";\n";
+      o << "  if (blockIdx.x == 0 && threadIdx.x == 0) nact[(rel + 1ull) & 1ull] = 0u;\n";
+      o << "  u32* cnt = " << P(pw.tm_cnt, "u32") << ";\n  u64* bucket = " << P(pw.tm_bucket, "u64") << ";\n";
+      o << "  u32* active = " << P(pw.tm_active, "u32") << ";\n  const u64* toff = " << P(pw.tm_off, "const u64") << ";\n";
+      o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
+      o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
+      o << "  const u64* off = " << P(pw.offsets, "const u64") << ";\n  const u32* other = " << P(pw.row_other, "const u32") << ";\n";
+      o << "  u64 events = 0;\n";
+      o << "  const u64 items = (b - a) * " << chunks << "ull;\n";
+      o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
+      o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
+      o << "    const u32 s = __ldg(ring + (j & " << u64lit(es.mask) << "));\n";
+      if (!full) o << "    if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
+      o << "    const u32 ep = s - " << lo << "u;\n    const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
+      o << "    if (c == 0 && threadIdx.x == 0) events += r1 - r0;\n";
+      o << "    const u64 q0 = r0 + c * " << row_chunk() << "ull;\n    if (q0 >= r1) continue;\n";
+      o << "    const u64 q1 = q0 + " << row_chunk() << "ull < r1 ? q0 + " << row_chunk() << "ull : r1;\n";
+      o << "    for (u64 q = q0 + threadIdx.x; q < q1; q += " << kThreads << "ull) {\n";
+      o << "      const u32 tj = __ldg(other + q) - " << pw.tm_lo << "u;\n";
+      o << "      const u32 slot = atomicAdd(cnt + tj, 1u);\n";
+      o << "      bucket[__ldg(toff + tj) + slot] = ((u64)ep << 32) | q;\n";
+      o << "      if (slot == 0u) active[atomicAdd(nact + (rel & 1ull), 1u)] = tj;\n";
+      o << "    }\n  }\n";
+      o << "  if (threadIdx.x == 0 && events) atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
+        << pw.delivered_slot << ", events);\n";
+      o << kernel_tail();
+      return o.str();
+    }
     if (pw.mode == PathwayDev::Mode::Targets) {
       // Warp per target over its in-edges (delay descending, source
       // ascending, creation order, i.e. the canonical delivery order): lanes
@@ -2141,10 +2200,20 @@ struct Engine::Impl {
       o << "  const u64* toff = " << P(pw.tm_off, "const u64") << ";\n";
       o << "  const u32* tsrc = " << P(pw.tm_src, "const u32") << ";\n";
       o << "  const u32* tedge = " << P(pw.tm_edge, "const u32") << ";\n";
+      // With one delay the emission tick's bitmap slot is staged in shared
+      // memory once per block, so each entry's test is one global load (its
+      // source id) and one shared-memory lookup.
+      const uint64_t mask_bytes = pw.tm_warps > 1 ? targets_mask_words(pw) * (kThreads / 32 / pw.tm_warps) * 4 : 0;
+      const bool smem_bm = pw.uniform && es.bm_words * 4 + mask_bytes <= 48 * 1024 && targets_smem_bitmap_;
       if (pw.uniform) {
         o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n";
         o << "  const u32* bmw = " << bm << " + ((rel - " << pw.delay << "ull) % " << es.bm_slots << "ull) * "
           << es.bm_words << "ull;\n";
+        if (smem_bm) {
+          o << "  __shared__ u32 s_bm[" << es.bm_words << "];\n";
+          o << "  for (u32 w = threadIdx.x; w < " << es.bm_words << "u; w += blockDim.x) s_bm[w] = __ldg(bmw + w);\n";
+          o << "  __syncthreads();\n";
+        }
       } else {
         o << "  const u16* tdel = " << P(pw.tm_delay, "const u16") << ";\n";
       }
@@ -2160,7 +2229,7 @@ struct Engine::Impl {
         h << "        bool h = false;\n";
         h << "        if (in[u]) {\n          const u32 s = sv[u] + " << pw.endpoint_start << "u;\n";
         if (pw.uniform) {
-          h << "          h = (__ldg(bmw + (s >> 5)) >> (s & 31u)) & 1u;\n";
+          h << "          h = (" << (smem_bm ? "s_bm[s >> 5]" : "__ldg(bmw + (s >> 5))") << " >> (s & 31u)) & 1u;\n";
         } else {
           h << "          const u64 lag = __ldg(tdel + " << tb << " + u * 32u + lane);\n";
           h << "          if (lag <= rel) h = (__ldg(" << bm << " + ((rel - lag) % " << es.bm_slots << "ull) * "
@@ -2253,6 +2322,30 @@ struct Engine::Impl {
     return o.str();
   }
 
+  // Bucket delivery of a single-delay target-ordered pathway: one thread per
+  // listed target sorts its bucket (keys source << 32 | row position, i.e.
+  // the canonical order: source ascending, then creation order) and runs the
+  // bodies in that order, then clears the target's count.
+  std::string gen_targets_deliver(const std::string& name, const std::string& body_fn, const PathwayDev& pw) {
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n";
+    o << "  const u32 n = " << P(pw.tm_nactive, "const u32") << "[rel & 1ull];\n";
+    o << "  u32* cnt = " << P(pw.tm_cnt, "u32") << ";\n  u64* bucket = " << P(pw.tm_bucket, "u64") << ";\n";
+    o << "  const u32* active = " << P(pw.tm_active, "const u32") << ";\n  const u64* toff = " << P(pw.tm_off, "const u64")
+      << ";\n";
+    if (pw.row_edge >= 0) o << "  const u32* red = " << P(pw.row_edge, "const u32") << ";\n";
+    o << "  for (u32 x = blockIdx.x * blockDim.x + threadIdx.x; x < n; x += gridDim.x * blockDim.x) {\n";
+    o << "    const u32 tj = active[x];\n    const u32 c = cnt[tj];\n    u64* bk = bucket + toff[tj];\n";
+    o << "    b2_sort_u64(bk, c);\n";
+    o << "    for (u32 k = 0; k < c; ++k) {\n      const u64 key = bk[k];\n      const u32 q = (u32)key;\n";
+    o << "      " << body_fn << "((u32)(key >> 32), tj + " << pw.tm_lo << "u, "
+      << (pw.row_edge >= 0 ? "(u64)red[q]" : "(u64)q") << ", tick, t, err);\n    }\n";
+    o << "    cnt[tj] = 0u;\n  }\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
   // ================================================================ plan
   NodeEffects effects_of(const b2ir::ScheduleNode& node) {
     NodeEffects e;
@@ -2302,6 +2395,7 @@ struct Engine::Impl {
     std::vector<PathwayDev*> pathways;
     std::vector<const Program*> programs;
     std::vector<std::string> codes;
+    std::string body;  // device function of a single non-atomic pathway
   };
   struct OpSpec {
     enum class Kind { Text, Step, Path } kind = Kind::Text;
@@ -2666,7 +2760,7 @@ struct Engine::Impl {
           bool serial = pw.mode == PathwayDev::Mode::Serial;
           o.grid = serial ? 1u : 148u * 8u;
           o.block = serial ? 32u : kThreads;
-          if (pw.mode == PathwayDev::Mode::Targets) {  // tm_warps warps per target
+          if (pw.mode == PathwayDev::Mode::Targets && !pw.tm_events) {  // tm_warps warps per target
             pw.tm_warps = targets_group(pw);
             const uint64_t per_block = kThreads / 32 / pw.tm_warps;
             o.grid = unsigned(std::max<uint64_t>(1, std::min<uint64_t>((pw.tm_targets + per_block - 1) / per_block,
@@ -2674,6 +2768,14 @@ struct Engine::Impl {
           }
           paths.push_back(ps);
           specs.push_back(o);
+          if (pw.mode == PathwayDev::Mode::Targets && pw.tm_events) {
+            OpSpec d;  // bucket delivery after the scatter
+            d.base = code.name + "_deliver";
+            d.text = "tdeliver";
+            d.index = paths.size() - 1;
+            d.grid = 148u * 8u;
+            specs.push_back(d);
+          }
         }
       }
     }
@@ -2729,6 +2831,7 @@ struct Engine::Impl {
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
           else if (o.text == "evmon") kernels << gen_evmon(nm, o.index, size_t(o.fuse_path));
+          else if (o.text == "tdeliver") kernels << gen_targets_deliver(nm, paths[o.index].body, *paths[o.index].pathways[0]);
           else if (o.text == "synprog") {
             const SynProgSpec& sp = synprog_specs[o.index];
             std::string body = "b2_synprog_" + std::to_string(kid);
@@ -2766,6 +2869,7 @@ struct Engine::Impl {
           if (ps.pathways.size() == 1 && ps.pathways[0]->mode != PathwayDev::Mode::Atomic) {
             std::string body = "b2_body_" + std::to_string(kid) + "_" + sanitize(ps.codes[0]);
             bodies << gen_pathway_body(body, ps.pathways[0]->synapse, *ps.pathways[0], *ps.programs[0]);
+            ps.body = body;
             const auto md = ps.pathways[0]->mode;
             const char* mode = md == PathwayDev::Mode::EdgeParallel ? "_edges"
                                : md == PathwayDev::Mode::Targets    ? "_targets"

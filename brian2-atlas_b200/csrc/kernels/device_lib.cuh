@@ -80,6 +80,44 @@ __device__ double b2_normal(u64 seed, u64 stream, u64 tick, u64 index) {
   return 0.0;
 }
 
+// ---------------------------------------------------------------- sorting
+// In-place ascending sort of n keys by one thread: insertion sort for short
+// runs (a target's events of one tick are usually a handful), heapsort
+// (O(n log n), no recursion) beyond.
+__device__ __forceinline__ void b2_sift_u64(u64* a, u32 root, u32 end) {
+  while (2u * root + 1u < end) {
+    u32 child = 2u * root + 1u;
+    if (child + 1u < end && a[child] < a[child + 1u]) ++child;
+    if (!(a[root] < a[child])) return;
+    const u64 t = a[root];
+    a[root] = a[child];
+    a[child] = t;
+    root = child;
+  }
+}
+
+__device__ inline void b2_sort_u64(u64* a, u32 n) {
+  if (n <= 16u) {
+    for (u32 i = 1; i < n; ++i) {
+      const u64 v = a[i];
+      u32 j = i;
+      while (j > 0u && a[j - 1u] > v) {
+        a[j] = a[j - 1u];
+        --j;
+      }
+      a[j] = v;
+    }
+    return;
+  }
+  for (u32 start = n / 2u; start-- > 0u;) b2_sift_u64(a, start, n);
+  for (u32 end = n - 1u; end > 0u; --end) {
+    const u64 t = a[0];
+    a[0] = a[end];
+    a[end] = t;
+    b2_sift_u64(a, 0u, end);
+  }
+}
+
 // Binomial inversion with the per-pathway constants precomputed on the host in
 // glibc f64 (probability, q, q^n, restart bound), so the device loop is pure
 // IEEE arithmetic and bit-identical to executor.rs:224-268.

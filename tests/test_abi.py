@@ -60,8 +60,9 @@ def load(name):
                       "poisson_input", "reset"]),
     ("cobahh_small", ["step", "exc_pre_inh_pre_atomic"]),
     # on_pre writes the target's conductance and the edge's weight and
-    # traces: target-ordered delivery; on_post writes only synapse state
-    ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_targets", "stdp_post_edges"]),
+    # traces: target-ordered delivery (bucket scatter, then per-target
+    # delivery); on_post writes only synapse state
+    ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]),
 ])
 def test_codegen_plan(pkg, name, expected):
     src = pkg.codegen(load(name))
@@ -138,4 +139,4 @@ def test_codegen_procedural_synapse_programs(pkg):
     assert names[1].endswith("gaps_summed_variable_Igap_post")
     names = kernels(pkg.codegen(procedural_variant("synapse_updates_small", 40)))
     assert [n.split("_", 2)[2] for n in names] == ["decay", "inputs_step", "neurons_step", "stdp_stateupdater",
-                                                   "stdp_pre_targets", "stdp_post_edges"]
+                                                   "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]

@@ -215,11 +215,16 @@ def test_stdp_targets_equal_serial_fold(pkg, tmp_path, monkeypatch):
         template = json.loads(f.read())
     path = tmp_path / "stdp_40k.json"
     path.write_bytes(synthetic.encode(synthetic.stdp_feedforward(template, 2000, 200, 200, ticks=1500, seed=11)))
+    # serial fold; event buckets; bitmap scan with 1 and 4 warps per target
+    variants = {"fold": dict(B2GPU_TARGETS="0"), "buckets": dict(B2GPU_TARGETS="1"),
+                "scan1": dict(B2GPU_TARGETS="1", B2GPU_TARGETS_SCAN="1", B2GPU_TARGETS_WARPS="1"),
+                "scan4": dict(B2GPU_TARGETS="1", B2GPU_TARGETS_SCAN="1", B2GPU_TARGETS_WARPS="4")}
     stats = {}
-    for mode, warps in (("0", "0"), ("1", "1"), ("1", "4")):
-        monkeypatch.setenv("B2GPU_TARGETS", mode)
-        monkeypatch.setenv("B2GPU_TARGETS_WARPS", warps)
-        stats[mode + warps] = gpu_run(pkg, path, tmp_path / f"gpu{mode}{warps}")
-    assert stats["11"]["synaptic_events"] == stats["14"]["synaptic_events"] == stats["00"]["synaptic_events"] > 0
-    assert_same_files(tmp_path / "gpu11", tmp_path / "gpu00")
-    assert_same_files(tmp_path / "gpu14", tmp_path / "gpu00")
+    for name, env in variants.items():
+        for key in ("B2GPU_TARGETS", "B2GPU_TARGETS_SCAN", "B2GPU_TARGETS_WARPS"):
+            monkeypatch.setenv(key, env.get(key, "0"))
+        stats[name] = gpu_run(pkg, path, tmp_path / name)
+    assert stats["fold"]["synaptic_events"] > 0
+    for name in variants:
+        assert stats[name]["synaptic_events"] == stats["fold"]["synaptic_events"]
+        assert_same_files(tmp_path / name, tmp_path / "fold")

@@ -75,18 +75,20 @@ def test_stdp_rank_plans_replicate_the_inputs(pkg, tmp_path, world):
     for r in range(world):
         src = pkg.codegen(data, rank=r, world_size=world)
         names = [k.split("_", 2)[2] for k in kernels(src)]
-        assert names == ["neurons_step", "neurons_exchange", "inputs_step", "stdp_pre_targets", "stdp_post_edges"]
+        assert names == ["neurons_step", "neurons_exchange", "inputs_step", "stdp_pre_targets", "stdp_pre_deliver",
+                         "stdp_post_edges"]
         lo, hi = pkg.partition(targets, r, world)
-        body = src[src.index("stdp_pre_targets("):]
-        assert f"j < {hi - lo}ull" in body and f"(u32)(j + {lo}ull)" in body
-    # diagnostic: partition and exchange the inputs as well (ordered serial fold)
+        assert f"__ldg(other + q) - {lo}u" in src[src.index("stdp_pre_targets("):]
+        assert f"tj + {lo}u" in src[src.index("stdp_pre_deliver("):]
+    # diagnostic: partition and exchange the inputs as well (the bucket
+    # scatter reads the exchanged global list)
     os.environ["B2GPU_REPLICATE"] = "0"
     try:
         names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=0, world_size=world))]
     finally:
         del os.environ["B2GPU_REPLICATE"]
-    assert names == ["neurons_step", "neurons_exchange", "inputs_step", "inputs_exchange", "stdp_pre_serial",
-                     "stdp_post_edges"]
+    assert names == ["neurons_step", "neurons_exchange", "inputs_step", "inputs_exchange", "stdp_pre_targets",
+                     "stdp_pre_deliver", "stdp_post_edges"]
 
 
 def _gloo_rank(rank, world, port, q):

@@ -140,7 +140,7 @@ def build_model(n, indegree, ticks, seed=3):
     return synthetic.encode(synthetic.cuba_fixed_indegree(template, n=n, indegree=indegree, ticks=ticks, seed=seed))
 
 
-STDP_INPUTS, STDP_NEURONS, STDP_INDEGREE = 100_000, 10_000, 1000
+STDP_INPUTS, STDP_NEURONS, STDP_INDEGREE, STDP_RATE_HZ = 100_000, 10_000, 1000, 15.0
 STDP_SAMPLE_INPUTS, STDP_SAMPLE_NEURONS = 10_000, 1000
 
 
@@ -313,11 +313,25 @@ def main():
     for k in prof:
         avg_ms = k["total_ms"] / max(k["launches"], 1)
         if stdp:
-            # target-ordered on_pre scan: the 4 B source id of every local
-            # in-edge and the 8 B row offset of every local target (the
-            # delivered events' state traffic comes on top)
-            per_launch = 4 * local_neurons * STDP_INDEGREE + 8 * (local_neurons + 1) if k["name"].endswith(
-                "_targets") else 0
+            # on_pre events per tick on this rank: inputs x 15 Hz x dt x
+            # out-degree, i.e. 15 Hz x dt x local edges (the expectation of
+            # the Poisson drive; the run's own count is within a percent)
+            pre = STDP_RATE_HZ * DT * local_neurons * STDP_INDEGREE
+            if k["name"].endswith("_targets") and os.environ.get("B2GPU_TARGETS_SCAN", "0") != "0":
+                # bitmap scan: the 4 B source id of every local in-edge and
+                # the 8 B row offset of every local target
+                per_launch = 4 * local_neurons * STDP_INDEGREE + 8 * (local_neurons + 1)
+            elif k["name"].endswith("_targets"):
+                # bucket scatter per event: 4 B row entry, 4+4 B count
+                # atomic, 8 B bucket offset, 8 B bucket entry
+                per_launch = 28 * pre
+            elif k["name"].endswith("_deliver"):
+                # per event: 8 B bucket entry, 4 B edge id, the edge's f64
+                # w, Apre, Apost, lastupdate read and w, Apre, lastupdate
+                # written, the target's f64 ge read and written
+                per_launch = (8 + 4 + 32 + 24 + 16) * pre
+            else:
+                per_launch = 0
         elif "_step" in k["name"]:
             # neuron update + threshold + compaction + reset: read and write
             # v, ge, gi (f64) and read lastspike (f64) per neuron, 4 B per spike

@@ -2326,7 +2326,16 @@ struct Engine::Impl {
   // listed target sorts its bucket (keys source << 32 | row position, i.e.
   // the canonical order: source ascending, then creation order) and runs the
   // bodies in that order, then clears the target's count.
-  std::string gen_targets_deliver(const std::string& name, const std::string& body_fn, const PathwayDev& pw) {
+  //
+  // One warp per listed target (interleaved across blocks so a tick's few
+  // thousand targets spread over every SM).  Up to 32 events: lane k holds
+  // key k, its rank among the keys comes from 32 shuffles, every lane
+  // prefetches its event's state into L1 at once, and the bodies then run one
+  // lane at a time in rank order (separated by __syncwarp), so the chain of
+  // dependent accesses per target is paid once rather than per event.  More
+  // events: lane 0 sorts the bucket in place and runs them in order.
+  std::string gen_targets_deliver(const std::string& name, const std::string& body_fn, const std::string& prefetch_fn,
+                                  const PathwayDev& pw) {
     std::ostringstream o;
     o << kernel_head(name);
     o << "  if ((i64)rel - " << pw.delay << "ll < 0) return;\n";
@@ -2335,14 +2344,58 @@ struct Engine::Impl {
     o << "  const u32* active = " << P(pw.tm_active, "const u32") << ";\n  const u64* toff = " << P(pw.tm_off, "const u64")
       << ";\n";
     if (pw.row_edge >= 0) o << "  const u32* red = " << P(pw.row_edge, "const u32") << ";\n";
-    o << "  for (u32 x = blockIdx.x * blockDim.x + threadIdx.x; x < n; x += gridDim.x * blockDim.x) {\n";
+    const std::string edge = pw.row_edge >= 0 ? "(u64)red[(u32)key]" : "(u64)(u32)key";
+    o << "  const u32 lane = threadIdx.x & 31u;\n";
+    o << "  for (u32 x = (threadIdx.x >> 5) * gridDim.x + blockIdx.x; x < n; x += gridDim.x * (blockDim.x >> 5)) {\n";
     o << "    const u32 tj = active[x];\n    const u32 c = cnt[tj];\n    u64* bk = bucket + toff[tj];\n";
-    o << "    b2_sort_u64(bk, c);\n";
-    o << "    for (u32 k = 0; k < c; ++k) {\n      const u64 key = bk[k];\n      const u32 q = (u32)key;\n";
-    o << "      " << body_fn << "((u32)(key >> 32), tj + " << pw.tm_lo << "u, "
-      << (pw.row_edge >= 0 ? "(u64)red[q]" : "(u64)q") << ", tick, t, err);\n    }\n";
-    o << "    cnt[tj] = 0u;\n  }\n";
+    o << "    const u32 tgt = tj + " << pw.tm_lo << "u;\n";
+    o << "    if (c <= 32u) {\n";
+    o << "      const u64 key = lane < c ? bk[lane] : ~0ull;\n";
+    o << "      u32 rank = 0;\n";
+    o << "      for (u32 L = 0; L < c; ++L) rank += __shfl_sync(0xffffffffu, key, L) < key ? 1u : 0u;\n";
+    o << "      u64 e = 0;\n";
+    o << "      if (lane < c) {\n        e = " << edge << ";\n        " << prefetch_fn << "((u32)(key >> 32), tgt, e);\n      }\n";
+    o << "      for (u32 r = 0; r < c; ++r) {\n";
+    o << "        if (lane < c && rank == r) " << body_fn << "((u32)(key >> 32), tgt, e, tick, t, err);\n";
+    o << "        __syncwarp();\n      }\n";
+    o << "    } else if (lane == 0u) {\n";
+    o << "      b2_sort_u64(bk, c);\n";
+    o << "      for (u32 k = 0; k < c; ++k) {\n        const u64 key = bk[k];\n";
+    o << "        " << body_fn << "((u32)(key >> 32), tgt, " << edge << ", tick, t, err);\n      }\n";
+    o << "    }\n";
+    o << "    __syncwarp();\n    if (lane == 0u) cnt[tj] = 0u;\n  }\n";
     o << kernel_tail();
+    return o.str();
+  }
+
+  // L1 prefetch of every state and per-edge parameter element a pathway body
+  // reads (same addresses as the body's loads).
+  std::string gen_pathway_prefetch(const std::string& fname, size_t s, const Program& pr) {
+    const auto& def = m.synapses[s];
+    const SynDev& sd = syns[s];
+    const auto& src = m.populations[def.source_population];
+    const auto& tgt = m.populations[def.target_population];
+    std::ostringstream o;
+    o << "__device__ __forceinline__ void " << fname << "(u32 src, u32 tgt, u64 edge) {\n";
+    o << "  const u64 src_state = (u64)src + " << def.source_start << "ull;\n";
+    o << "  const u64 tgt_state = (u64)tgt + " << target_bias(def) << "ull;\n";
+    o << "  (void)src_state; (void)tgt_state; (void)edge;\n";
+    std::set<std::string> seen;
+    for (const auto& [slot, in] : pr.bindings) {
+      std::string addr;
+      if (in.kind == Input::Kind::PreState)
+        addr = P(pops[def.source_population].states[in.index].ptr, storage_ctype(src.states[in.index].dtype)) + " + src_state";
+      else if (in.kind == Input::Kind::PostState)
+        addr = P(pops[def.target_population].states[in.index].ptr, storage_ctype(tgt.states[in.index].dtype)) + " + tgt_state";
+      else if (in.kind == Input::Kind::SynapseState)
+        addr = P(sd.states[in.index].ptr, storage_ctype(def.states[in.index].dtype)) + " + edge";
+      else if (in.kind == Input::Kind::Parameter && sd.param_ptr.count(def.parameters[in.index].name))
+        addr = P(sd.param_ptr.at(def.parameters[in.index].name), "const double") + " + edge";
+      else
+        continue;
+      if (seen.insert(addr).second) o << "  b2_prefetch(" << addr << ");\n";
+    }
+    o << "}\n";
     return o.str();
   }
 
@@ -2831,7 +2884,12 @@ struct Engine::Impl {
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
           else if (o.text == "evmon") kernels << gen_evmon(nm, o.index, size_t(o.fuse_path));
-          else if (o.text == "tdeliver") kernels << gen_targets_deliver(nm, paths[o.index].body, *paths[o.index].pathways[0]);
+          else if (o.text == "tdeliver") {
+            PathSpec& ps = paths[o.index];
+            const std::string pf = ps.body + "_prefetch";
+            bodies << gen_pathway_prefetch(pf, ps.pathways[0]->synapse, *ps.programs[0]);
+            kernels << gen_targets_deliver(nm, ps.body, pf, *ps.pathways[0]);
+          }
           else if (o.text == "synprog") {
             const SynProgSpec& sp = synprog_specs[o.index];
             std::string body = "b2_synprog_" + std::to_string(kid);

@@ -80,6 +80,10 @@ __device__ double b2_normal(u64 seed, u64 stream, u64 tick, u64 index) {
   return 0.0;
 }
 
+// Bring the line holding *p into this SM's L1 ahead of a dependent chain of
+// loads (callers pass addresses the following code loads anyway).
+__device__ __forceinline__ void b2_prefetch(const void* p) { asm volatile("prefetch.global.L1 [%0];" ::"l"(p)); }
+
 // ---------------------------------------------------------------- sorting
 // In-place ascending sort of n keys by one thread: insertion sort for short
 // runs (a target's events of one tick are usually a handful), heapsort

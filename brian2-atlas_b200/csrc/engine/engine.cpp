@@ -352,6 +352,8 @@ struct Engine::Impl {
     // Diagnostic: deliver ordered pathways with one serial thread instead of
     // the target-ordered kernel (same results) for A/B timing.
     if (const char* e = std::getenv("B2GPU_TARGETS")) use_targets_ = std::atoi(e) != 0;
+    // Diagnostic: one launch per population step (same results).
+    if (const char* e = std::getenv("B2GPU_FUSE_STEPS")) fuse_steps_ = std::atoi(e) != 0;
     if (const char* e = std::getenv("B2GPU_TARGETS_UNROLL")) targets_unroll_ = unsigned(std::atoi(e));
     check(targets_unroll_ >= 1 && targets_unroll_ <= 16, "target-ordered unroll must be 1 to 16");
     if (const char* e = std::getenv("B2GPU_TARGETS_WARPS")) targets_warps_ = unsigned(std::atoi(e));
@@ -369,6 +371,7 @@ struct Engine::Impl {
   }
   bool no_fuse_ = false;
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
+  bool fuse_steps_ = true;   // one launch for consecutive step kernels of different populations
   unsigned targets_unroll_ = 4;  // 32-entry groups each warp of a target-ordered kernel keeps in flight
   unsigned targets_warps_ = 0;   // warps per target (0: targets_group chooses)
   bool targets_smem_bitmap_ = true;  // stage the fired bitmap slot in shared memory
@@ -1292,7 +1295,7 @@ struct Engine::Impl {
   // compaction into the event ring), optional reset R on fired lanes.
   std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
                            bool x_is_spike, const Program* R, const std::vector<const Program*>& deferred = {},
-                           bool flush = false) {
+                           bool flush = false, bool as_fn = false) {
     // One block owns a tile of tile_n consecutive neurons; thread t handles
     // neurons tile*tile_n + kk*kThreads + t for kk < npt: all loads of the
     // npt neurons are issued before any arithmetic (memory-level
@@ -1322,12 +1325,19 @@ struct Engine::Impl {
     bool touch_refr = refr && (X || (U && pd.fixed_refractory && !flush) || writes_available(progs));
     bool read_refr = refr;
     std::ostringstream o;
-    o << kernel_head(name, min_blocks_);
+    // as_fn: the same code as a device function over one tile, for a launch
+    // that steps several populations (block ranges dispatch to the functions)
+    if (as_fn)
+      o << "__device__ __forceinline__ void " << name
+        << "(RunCtl* __restrict__ ctl, u64 tick, u64 rel, double t, u32 tile, u32& err) {\n"
+        << "  (void)ctl; (void)tick; (void)rel; (void)t;\n";
+    else
+      o << kernel_head(name, min_blocks_);
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
     const bool exchange = es && es->exchanged;
     size_t tiles = tiles_for(pd.count);
     constexpr unsigned W = kThreads / 32;
-    o << "  const u32 tile = blockIdx.x;\n";
+    if (!as_fn) o << "  const u32 tile = blockIdx.x;\n";
     if (X && !exchange) {
       o << "  __shared__ u32 s_ballot[" << npt * W << "];\n  __shared__ u32 s_off[" << npt * W + 1 << "];\n";
       o << "  __shared__ u32 s_last;\n";
@@ -1461,7 +1471,7 @@ struct Engine::Impl {
         << P(es->tick_start, "u64") << ", rel, " << u64lit(es->cap) << ", " << floor_of(size_t(pd.stream_of_event[x_event]))
         << ", err);\n  }\n";
     }
-    o << kernel_tail();
+    o << (as_fn ? std::string("}\n") : kernel_tail());
     return o.str();
   }
 
@@ -2456,6 +2466,7 @@ struct Engine::Impl {
     size_t index = 0;
     unsigned grid = 1, block = kThreads;
     int fuse_path = -1;  // exchange: PathSpec delivered inside the same kernel
+    std::vector<size_t> fused_steps;  // Step: further StepSpecs stepped by the same launch
   };
   std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
   std::vector<SummedSpec> summed_specs;
@@ -2871,6 +2882,30 @@ struct Engine::Impl {
         specs.erase(specs.begin() + long(i) + 1);
       }
     }
+    // Consecutive step kernels of different populations touch disjoint state
+    // (population code reads and writes only its own population), so one
+    // launch steps them all: block ranges dispatch to per-population tiles,
+    // saving a dependent launch per tick.
+    if (!no_fuse_ && fuse_steps_) {
+      for (size_t i = 0; i + 1 < specs.size();) {
+        OpSpec& a = specs[i];
+        const OpSpec& b = specs[i + 1];
+        bool ok = a.kind == OpSpec::Kind::Step && b.kind == OpSpec::Kind::Step;
+        if (ok) {
+          std::set<size_t> seen{steps_[a.index].pop};
+          for (size_t f : a.fused_steps) seen.insert(steps_[f].pop);
+          ok = !seen.count(steps_[b.index].pop);
+        }
+        if (!ok) {
+          ++i;
+          continue;
+        }
+        a.fused_steps.push_back(b.index);
+        a.base += "_" + b.base;
+        a.grid += b.grid;
+        specs.erase(specs.begin() + long(i) + 1);
+      }
+    }
     // ---- emit
     std::ostringstream src, bodies, kernels;
     src << "// generated by brian2-atlas_b200 for one AtlasIR model\n";
@@ -2918,8 +2953,26 @@ struct Engine::Impl {
           }
           break;
         case OpSpec::Kind::Step: {
-          const StepSpec& st = steps_[o.index];
-          kernels << gen_pop_step(nm, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred);
+          if (o.fused_steps.empty()) {
+            const StepSpec& st = steps_[o.index];
+            kernels << gen_pop_step(nm, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred);
+            break;
+          }
+          std::vector<size_t> group{o.index};
+          group.insert(group.end(), o.fused_steps.begin(), o.fused_steps.end());
+          std::ostringstream disp;
+          uint64_t first = 0;
+          for (size_t g = 0; g < group.size(); ++g) {
+            const StepSpec& st = steps_[group[g]];
+            const std::string fn = nm + "_part" + std::to_string(g);
+            kernels << gen_pop_step(fn, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred, false, true);
+            const uint64_t tiles = tiles_for(pops[st.pop].count);
+            disp << "  " << (g ? "else if" : "if") << " (blockIdx.x < " << first + tiles << "u) " << fn
+                 << "(ctl, tick, rel, t, blockIdx.x - " << first << "u, err);\n";
+            first += tiles;
+          }
+          check(first == o.grid, "fused step grid mismatch");
+          kernels << kernel_head(nm, min_blocks_) << disp.str() << kernel_tail();
           break;
         }
         case OpSpec::Kind::Path: {

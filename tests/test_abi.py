@@ -59,10 +59,11 @@ def load(name):
     ("brunel_small", ["step", "excitatory_synapses_pre_atomic", "inhibitory_synapses_pre_atomic",
                       "poisson_input", "reset"]),
     ("cobahh_small", ["step", "exc_pre_inh_pre_atomic"]),
-    # on_pre writes the target's conductance and the edge's weight and
-    # traces: target-ordered delivery (bucket scatter, then per-target
-    # delivery); on_post writes only synapse state
-    ("stdp_small", ["neurons_step", "inputs_step", "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]),
+    # the two populations step in one launch; on_pre writes the target's
+    # conductance and the edge's weight and traces: target-ordered delivery
+    # (bucket scatter, then per-target delivery); on_post writes only
+    # synapse state
+    ("stdp_small", ["neurons_step_inputs_step", "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]),
 ])
 def test_codegen_plan(pkg, name, expected):
     src = pkg.codegen(load(name))
@@ -78,7 +79,7 @@ def test_codegen_golden_fixture(pkg):
     # per-edge delays 1-4 ticks and per-edge weights: ordered delivery, one
     # warp per target
     assert sum(n.endswith("_targets") for n in names) == 4
-    assert sum(n.endswith("_step") for n in names) == 2
+    assert names[2].endswith("exc_step_inh_step")  # both populations in one launch
 
 
 def golden_variant(expr):
@@ -96,7 +97,7 @@ def test_codegen_ordered_pathway_fallbacks(pkg, monkeypatch):
     # reading presynaptic `current` while writing postsynaptic `current` of
     # the same population makes the order across targets observable: serial
     names = kernels(pkg.codegen(golden_variant("current_pre")))
-    assert names[4].endswith("projection_0_0_pre_serial")
+    assert names[3].endswith("projection_0_0_pre_serial")
     assert sum(n.endswith("_targets") for n in names) == 3
     # presynaptic `v` is never written by the pathway: target-ordered
     names = kernels(pkg.codegen(golden_variant("v_pre")))
@@ -138,5 +139,5 @@ def test_codegen_procedural_synapse_programs(pkg):
     names = kernels(pkg.codegen(procedural_variant("gap_junctions_small", 15)))
     assert names[1].endswith("gaps_summed_variable_Igap_post")
     names = kernels(pkg.codegen(procedural_variant("synapse_updates_small", 40)))
-    assert [n.split("_", 2)[2] for n in names] == ["decay", "inputs_step", "neurons_step", "stdp_stateupdater",
+    assert [n.split("_", 2)[2] for n in names] == ["decay", "inputs_step_neurons_step", "stdp_stateupdater",
                                                    "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]

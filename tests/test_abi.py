@@ -141,3 +141,24 @@ def test_codegen_procedural_synapse_programs(pkg):
     names = kernels(pkg.codegen(procedural_variant("synapse_updates_small", 40)))
     assert [n.split("_", 2)[2] for n in names] == ["decay", "inputs_step_neurons_step", "stdp_stateupdater",
                                                    "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]
+
+
+def golden_uniform_variant(ticks=3):
+    """golden_variant("v_pre") with every pathway's per-edge delays replaced
+    by one delay of `ticks` ticks (seconds taken from an edge that already
+    had it): projection_0_0 (per-edge w times the source's v) is delivered
+    through the event buckets, the constant-addend projections by atomics."""
+    doc = json.loads(golden_variant("v_pre"))
+    for inst in doc["instance"]["synapses"]:
+        for pw in inst["pathways"]:
+            k = pw["delay_ticks"].index(ticks)
+            pw["delay"] = [pw["delay"][k]] * len(pw["delay"])
+            pw["delay_ticks"] = [ticks] * len(pw["delay_ticks"])
+    return encode_model(doc)
+
+
+def test_codegen_single_delay_golden_uses_buckets(pkg):
+    names = kernels(pkg.codegen(golden_uniform_variant()))
+    assert [n.split("_", 2)[2] for n in names[3:]] == [
+        "projection_0_0_pre_targets", "projection_0_0_pre_deliver", "projection_0_1_pre_atomic",
+        "projection_1_0_pre_atomic", "projection_1_1_pre_atomic"]

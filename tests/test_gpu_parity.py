@@ -94,6 +94,18 @@ def test_procedural_synapse_programs_match_oracle(pkg, oracle, tmp_path, name, i
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")
 
 
+def test_single_delay_golden_variant_matches_oracle(pkg, oracle, tmp_path):
+    """The golden network (projection_0_0 scaled by the source's v) with one
+    3-tick delay per pathway: event buckets and atomics, nothing delivered
+    before tick 3."""
+    from test_abi import golden_uniform_variant
+    path = tmp_path / "model.json"
+    path.write_bytes(golden_uniform_variant())
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
 def test_cuba_4k_full_second(pkg, oracle, tmp_path):
     """Config 0 (CUBA 4000 neurons, ~320k synapses, 10,000 ticks)."""
     path = model_file("cuba_4k", tmp_path)

@@ -2467,6 +2467,7 @@ struct Engine::Impl {
     unsigned grid = 1, block = kThreads;
     int fuse_path = -1;  // exchange: PathSpec delivered inside the same kernel
     std::vector<size_t> fused_steps;  // Step: further StepSpecs stepped by the same launch
+    size_t item = 0;                  // evmon: EventMonitor index within its population
   };
   std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
   std::vector<SummedSpec> summed_specs;
@@ -2574,7 +2575,7 @@ struct Engine::Impl {
               o.text = "evmon";
               o.index = p;
               o.grid = 148;
-              o.fuse_path = int(node.item_index);  // monitor index
+              o.item = node.item_index;
               specs.push_back(o);
             }
             break;
@@ -2918,7 +2919,7 @@ struct Engine::Impl {
         case OpSpec::Kind::Text:
           if (o.text == "statemon") kernels << gen_state_monitor(nm, o.index);
           else if (o.text == "generator") kernels << gen_event_source(nm, o.index, pops[o.index].stream_of_event[0]);
-          else if (o.text == "evmon") kernels << gen_evmon(nm, o.index, size_t(o.fuse_path));
+          else if (o.text == "evmon") kernels << gen_evmon(nm, o.index, o.item);
           else if (o.text == "tdeliver") {
             PathSpec& ps = paths[o.index];
             const std::string pf = ps.body + "_prefetch";

@@ -685,7 +685,13 @@ struct Engine::Impl {
       } else {
         sd.edges = topo.edge_count;
         for (const auto& pw : inst.pathways) {
-          check(!pw.delay_initializer, "procedural delay initializers are not supported by the GPU engine yet");
+          if (pw.delay_initializer) {
+            // drawn per edge on the device below (edge id = source-major position)
+            check(pw.delay_initializer->kind == b2ir::Initializer::Kind::Uniform,
+                  "clipped-normal delay initializers are not supported by the GPU engine yet");
+            check(pw.kind == "pre" && world == 1,
+                  "procedural delay initializers are supported on on_pre pathways of one GPU");
+          }
           delays.push_back(pw.delay_ticks);
         }
       }
@@ -753,11 +759,29 @@ struct Engine::Impl {
         check(ev != endpoint.events.end(), "pathway event missing from endpoint");
         pd.stream = pops[pd.endpoint_pop].stream_of_event[size_t(ev - endpoint.events.begin())];
         const auto& d = delays[k];
-        check(!d.empty(), "pathway has no delay");
-        pd.uniform = std::all_of(d.begin(), d.end(), [&](size_t x) { return x == d[0]; });
-        pd.delay = d[0];
-        pd.max_delay = *std::max_element(d.begin(), d.end());
-        if (!pd.uniform) check(d.size() == sd.edges, "per-edge delay array has the wrong length");
+        int init_delay = -1;  // device per-edge delays of a procedural delay initializer
+        if (procedural && pw.delay_initializer) {
+          const auto& in = *pw.delay_initializer;
+          uint64_t dmin = 0, dmax = 0;
+          if (opt.dry_run) {
+            init_delay = alloc(0);
+            dmax = 1;  // plan as per-edge delays
+          } else {
+            DeviceBuffer ticks;
+            delay_ticks_uniform_device(sd.edges, topo.seed, in.stream, *in.minimum, *in.maximum,
+                                       m.populations[def.source_population].dt, ticks, dmin, dmax, stream);
+            init_delay = adopt(std::move(ticks));
+          }
+          pd.uniform = dmin == dmax;
+          pd.delay = dmin;
+          pd.max_delay = dmax;
+        } else {
+          check(!d.empty(), "pathway has no delay");
+          pd.uniform = std::all_of(d.begin(), d.end(), [&](size_t x) { return x == d[0]; });
+          pd.delay = d[0];
+          pd.max_delay = *std::max_element(d.begin(), d.end());
+          if (!pd.uniform) check(d.size() == sd.edges, "per-edge delay array has the wrong length");
+        }
         // CSR over the endpoint (source for pre, target for post), rows in
         // edge creation order (stable counting sort).
         if (!procedural) {
@@ -790,13 +814,15 @@ struct Engine::Impl {
           if (!identity) pd.row_edge = upload(row_edge.data(), std::max<size_t>(row_edge.size(), 1) * 4);
           if (!pd.uniform) pd.row_delay = upload(row_delay.data(), std::max<size_t>(row_delay.size(), 1) * 2);
         } else {
-          check(pd.uniform, "procedural topologies with per-edge delays are not supported by the GPU engine yet");
+          check(pd.uniform || init_delay >= 0,
+                "procedural topologies with per-edge delays are not supported by the GPU engine yet");
           check(pd.is_pre || world == 1, "multi-GPU runs support on_pre pathways on procedural topologies only");
           procedural_csr();
           if (pd.is_pre) {
             pd.offsets = proc_off;
             pd.row_other = proc_rows;
             pd.max_row = proc_max_row;
+            if (!pd.uniform) pd.row_delay = init_delay;  // row position == edge id
           } else if (opt.dry_run) {
             pd.offsets = alloc(0);
             pd.row_other = alloc(0);

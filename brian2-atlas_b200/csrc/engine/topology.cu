@@ -143,6 +143,29 @@ __global__ void uniform_initializer(double* __restrict__ out, uint64_t n, uint64
     out[i] = lo + (hi - lo) * topo_uniform_open(seed, stream, edge_base + i, 0);
 }
 
+// Per-edge delay in ticks from a uniform delay initializer
+// (materialize_delay_initializer, brian2-rust/src/executor.rs:160-188, and the
+// tick rounding of its caller): d = lo + (hi - lo) * u, ticks = floor(d/dt +
+// 0.5); bounds[0] / bounds[1] collect the smallest / largest tick count,
+// bounds[2] is set when a delay is negative or does not fit 16 bits.
+__global__ void delay_ticks_uniform(uint16_t* __restrict__ out, uint64_t n, uint64_t seed, uint64_t stream,
+                                    double lo, double hi, double dt, unsigned int* __restrict__ bounds) {
+  unsigned int mn = 0xffffffffu, mx = 0, bad = 0;
+  for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x) {
+    const double d = lo + (hi - lo) * topo_uniform_open(seed, stream, i, 0);
+    const double t = floor(d / dt + 0.5);
+    unsigned int k = 0;
+    if (!(t >= 0.0 && t < 65535.0)) bad = 1;
+    else k = (unsigned int)t;
+    out[i] = (uint16_t)k;
+    mn = min(mn, k);
+    mx = max(mx, k);
+  }
+  atomicMin(bounds, mn);
+  atomicMax(bounds + 1, mx);
+  if (bad) atomicOr(bounds + 2, 1u);
+}
+
 int bits_for(uint64_t n) {
   int b = 1;
   while ((1ull << b) < n) ++b;
@@ -291,6 +314,23 @@ __global__ void gather_target_major(const uint32_t* __restrict__ pos, uint64_t E
 }
 
 }  // namespace
+
+void delay_ticks_uniform_device(uint64_t n, uint64_t seed, uint64_t stream, double lo, double hi, double dt,
+                                DeviceBuffer& ticks, uint64_t& min_ticks, uint64_t& max_ticks, cudaStream_t stream_) {
+  ticks = DeviceBuffer(std::max<uint64_t>(n, 1) * 2);
+  DeviceBuffer bounds(16);
+  const unsigned int init[4] = {0xffffffffu, 0u, 0u, 0u};
+  B2_CUDA(cudaMemcpyAsync(bounds.ptr, init, sizeof init, cudaMemcpyHostToDevice, stream_));
+  if (n) delay_ticks_uniform<<<grid_for(n, 256), 256, 0, stream_>>>(ticks.as<uint16_t>(), n, seed, stream, lo, hi, dt,
+                                                                   bounds.as<unsigned int>());
+  B2_CUDA(cudaGetLastError());
+  unsigned int host[4];
+  B2_CUDA(cudaMemcpyAsync(host, bounds.ptr, sizeof host, cudaMemcpyDeviceToHost, stream_));
+  B2_CUDA(cudaStreamSynchronize(stream_));
+  b2ir::check(host[2] == 0, "procedural delay outside 0 to 65534 ticks");
+  min_ticks = n ? host[0] : 0;
+  max_ticks = host[1];
+}
 
 void csr_row_sources(const uint64_t* d_offsets, uint64_t S, uint64_t E, DeviceBuffer& src, cudaStream_t stream) {
   b2ir::check(E <= UINT32_MAX && S <= UINT32_MAX, "row sources need u32 indices");

@@ -21,6 +21,11 @@ void build_fixed_total_csr(uint64_t S, uint64_t T, uint64_t E, uint64_t seed, ui
                            DeviceBuffer& offsets, DeviceBuffer& row_targets, uint64_t& local_edges,
                            cudaStream_t stream);
 
+// Delays in ticks (u16 per edge, edge order) of a uniform delay initializer,
+// and their smallest and largest value.
+void delay_ticks_uniform_device(uint64_t n, uint64_t seed, uint64_t stream, double lo, double hi, double dt,
+                                DeviceBuffer& ticks, uint64_t& min_ticks, uint64_t& max_ticks, cudaStream_t stream_);
+
 // Row (source) index of every position of a source-major CSR with S rows and
 // E entries (u32 per entry).
 void csr_row_sources(const uint64_t* d_offsets, uint64_t S, uint64_t E, DeviceBuffer& src, cudaStream_t stream);

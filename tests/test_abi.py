@@ -16,7 +16,7 @@ import re
 
 import pytest
 
-from conftest import GOLDEN, MODELS, ROOT, encode_model, procedural_variant
+from conftest import GOLDEN, MODELS, ROOT, encode_model, golden_procedural_initializers, procedural_variant
 
 
 def declared_symbols():
@@ -162,3 +162,16 @@ def test_codegen_single_delay_golden_uses_buckets(pkg):
     assert [n.split("_", 2)[2] for n in names[3:]] == [
         "projection_0_0_pre_targets", "projection_0_0_pre_deliver", "projection_0_1_pre_atomic",
         "projection_1_0_pre_atomic", "projection_1_1_pre_atomic"]
+
+
+def test_codegen_procedural_delay_initializers(pkg):
+    """Uniform delay initializers on fixed in-degree projections plan as
+    per-edge delays (target-ordered scan); clipped-normal ones are refused
+    before any device work."""
+    names = kernels(pkg.codegen(golden_procedural_initializers()))
+    assert sum(n.endswith("_pre_targets") for n in names) == 4
+    doc = json.loads(golden_procedural_initializers())
+    doc["instance"]["synapses"][0]["pathways"][0]["delay_initializer"] = {
+        "kind": "clipped_normal", "mean": "3f1a36e2eb1c432d", "std": "3f1a36e2eb1c432d", "stream": 1}
+    with pytest.raises(pkg.B2GpuError, match="clipped-normal delay initializers"):
+        pkg.codegen(encode_model(doc))

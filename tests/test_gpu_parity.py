@@ -15,7 +15,8 @@ import json
 import numpy as np
 import pytest
 
-from conftest import GOLDEN, MODELS, encode_model, model_file, procedural_variant, run_oracle
+from conftest import (GOLDEN, MODELS, encode_model, golden_procedural_initializers, model_file, procedural_variant,
+                      run_oracle)
 from b2results import load_model, read_results
 
 pytestmark = pytest.mark.gpu
@@ -101,6 +102,17 @@ def test_single_delay_golden_variant_matches_oracle(pkg, oracle, tmp_path):
     from test_abi import golden_uniform_variant
     path = tmp_path / "model.json"
     path.write_bytes(golden_uniform_variant())
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+
+
+def test_procedural_initializers_match_oracle(pkg, oracle, tmp_path):
+    """Fixed in-degree edges, uniform per-edge weights and uniform per-edge
+    delays all generated on the device (target-ordered scan over per-edge
+    delays), against the oracle's host-side materialisation, byte for byte."""
+    path = tmp_path / "model.json"
+    path.write_bytes(golden_procedural_initializers())
     gpu_run(pkg, path, tmp_path / "gpu")
     run_oracle(oracle, path, tmp_path / "ref")
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")

@@ -62,6 +62,11 @@ def test_rank_plans(pkg, world):
 def test_multi_gpu_capability_errors(pkg, tmp_path):
     with pytest.raises(pkg.B2GpuError, match="on_pre and on_post pathways only"):
         pkg.codegen(model_file("synapse_updates_small", tmp_path).read_bytes(), rank=0, world_size=2)
+    with pytest.raises(pkg.B2GpuError, match="EventMonitor variables"):
+        pkg.codegen(model_file("event_variables_small", tmp_path).read_bytes(), rank=0, world_size=2)
+    from conftest import golden_procedural_initializers
+    with pytest.raises(pkg.B2GpuError, match="procedural per-edge initializers"):
+        pkg.codegen(golden_procedural_initializers(), rank=1, world_size=2)
 
 
 @pytest.mark.parametrize("world", [2, 3])

@@ -159,6 +159,11 @@ struct Engine::Impl {
     // rank q's copy) and an expand kernel of x_tiles blocks turns them into
     // the tick's ascending global list.
     bool exchanged = false;
+    // multi-GPU: a partitioned population's list that only its own rank
+    // consumes (on_post rows over the rank's targets, resets, results) stays
+    // local: no exchange wait; rank 0 merges every rank's drained list for
+    // the results (global ids, rank order = ascending order)
+    bool local = false;
     size_t x_off = 0;
     std::vector<int> xptr;
     uint64_t x_words = 0, x_tiles = 0, x_wpb = 0;  // exchange words, blocks, words per block
@@ -310,6 +315,8 @@ struct Engine::Impl {
   size_t arena_stage_off = 0;
   std::vector<void*> peer_base;       // other ranks' arenas, mapped by connect()
   bool connected = false, published = false;
+  std::vector<DeviceBuffer> published_lists;  // local event lists exported by publish()
+  bool lists_merged = false;
   void* gptr_table = nullptr;         // device address of the module's g_ptr table
   uint64_t part_lo(uint64_t n, int r) const { return n * uint64_t(r) / uint64_t(world); }
   // Block of population p whose results rank q stages (replicated
@@ -323,6 +330,7 @@ struct Engine::Impl {
     return pops[p].replicated ? (q == 0 ? n : 0) : part_lo(n, q + 1) - part_lo(n, q);
   }
   bool replicate_ = true;  // multi-GPU: replicate populations that no synapse targets
+  bool local_streams_ = true;  // multi-GPU: keep lists that only their own rank reads local
   // A population that no synapse targets, and that is no spike generator
   // (which already emits its global list on every rank).
   bool replicable(size_t p) const {
@@ -367,6 +375,8 @@ struct Engine::Impl {
     // Diagnostic: partition and exchange every population on N > 1 GPUs
     // (same results) instead of replicating the ones no synapse targets.
     if (const char* e = std::getenv("B2GPU_REPLICATE")) replicate_ = std::atoi(e) != 0;
+    // Diagnostic: exchange every partitioned population's list (same results).
+    if (const char* e = std::getenv("B2GPU_LOCAL_STREAMS")) local_streams_ = std::atoi(e) != 0;
     check(scatter_unroll_ >= 1 && scatter_unroll_ <= 8, "scatter unroll must be 1 to 8");
   }
   bool no_fuse_ = false;
@@ -1041,7 +1051,14 @@ struct Engine::Impl {
       es.tick_start = alloc((steps + 1) * 8);
       memset_dev(es.tick_start, 8);
       size_t tiles = tiles_for(pd.count), tile_n = tile_n_for(pd.count);
-      if (world > 1 && pd.gen_offsets < 0 && !pd.replicated) {
+      if (world > 1 && pd.gen_offsets < 0 && !pd.replicated && local_streams_) {
+        // local unless an on_pre pathway reads it (it needs every rank's spikes)
+        es.local = true;
+        for (const auto& sd : syns)
+          for (const auto& pw : sd.pathways)
+            if (pw.stream == int(&es - streams.data()) && pw.is_pre) es.local = false;
+      }
+      if (world > 1 && pd.gen_offsets < 0 && !pd.replicated && !es.local) {
         // spike generators emit their (global, precomputed) list on every
         // rank, and replicated populations compute it on every rank
         es.exchanged = true;
@@ -1100,6 +1117,7 @@ struct Engine::Impl {
     std::vector<size_t> lastspike, not_refractory;
     std::vector<std::vector<size_t>> mon_positions;  // owned record positions, in record order
     std::vector<std::vector<uint32_t>> syn_edges;    // global ids of the local edges
+    std::vector<size_t> local_starts, local_handle;  // per event stream (local streams only)
   };
   StageLayout stage_layout(int q) const {
     StageLayout L;
@@ -1143,6 +1161,12 @@ struct Engine::Impl {
         L.syn_state.back().push_back(take(L.syn_edges.back().size() * b2ir::dtype_bytes(st.dtype)));
     }
     L.delivered = take(std::max<size_t>(delivered_count, 1) * 8);
+    // local event lists: per tick the rank's list start (steps + 1 positions),
+    // the list length and the CUDA IPC handle of a device copy of the list
+    for (const auto& es : streams) {
+      L.local_starts.push_back(es.local ? take((steps + 1) * 8) : 0);
+      L.local_handle.push_back(es.local ? take(64 + 8) : 0);
+    }
     return L;
   }
 
@@ -1484,7 +1508,9 @@ struct Engine::Impl {
       o << "#pragma unroll\n    for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
       o << "      if ((fired_bits >> kk) & 1u) {\n";
       o << "        const u32 slot = kk * " << W << "u + warp;\n";
-      o << "        stage[s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u))] = tile * " << tile_n
+      // global ids (a local multi-GPU list covers the block [lo, lo + count))
+      o << "        stage[s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u))] = "
+        << (es->local && pd.lo ? std::to_string(pd.lo) + "u + " : std::string()) << "tile * " << tile_n
         << "u + kk * " << kThreads << "u + threadIdx.x;\n";
       o << "      }\n    }\n  }\n";
       o << "  __threadfence();\n  __syncthreads();\n";
@@ -2108,8 +2134,6 @@ struct Engine::Impl {
     o << "    const u32 s = __ldg(ring + (j & " << u64lit(es.mask) << "));\n";
     for (size_t k = 0; k < pws.size(); ++k) {
       const PathwayDev& pw = *pws[k];
-      const auto& def = m.synapses[pw.synapse];
-      const auto& tgt = m.populations[def.target_population];
       const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
       const bool full = lo == 0 && hi == endpoint_count;
       o << "    " << (full ? "{" : "if (s >= " + std::to_string(lo) + "u && s < " + std::to_string(hi) + "u) {") << "\n";
@@ -2132,7 +2156,6 @@ struct Engine::Impl {
   }
 
   std::string gen_pathway_kernel(const std::string& name, const std::string& body_fn, const PathwayDev& pw) {
-    const auto& def = m.synapses[pw.synapse];
     const EventStreamDev& es = streams[size_t(pw.stream)];
     const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
     const bool full = lo == 0 && hi == m.populations[pw.endpoint_pop].count;
@@ -3403,6 +3426,25 @@ struct Engine::Impl {
       for (size_t k = 0; k < syns[s].states.size(); ++k)
         put(L.syn_state[s][k], syns[s].states[k].ptr, syns[s].local_edges * b2ir::dtype_bytes(m.synapses[s].states[k].dtype));
     put(L.delivered, delivered_ptr, delivered_count * 8);
+    // local event lists: a device copy of the drained list, exported by IPC
+    // handle, and the per-tick starts (kept until the engine is destroyed, so
+    // rank 0 can read them after the host barrier)
+    for (size_t k = 0; k < streams.size(); ++k) {
+      const EventStreamDev& es = streams[k];
+      if (!es.local) continue;
+      check(es.starts.size() == steps + 1, "local event list bookkeeping mismatch");
+      published_lists.emplace_back(std::max<size_t>(es.ids.size(), 4) * 4);
+      DeviceBuffer& buf = published_lists.back();
+      if (!es.ids.empty())
+        B2_CUDA(cudaMemcpyAsync(buf.ptr, es.ids.data(), es.ids.size() * 4, cudaMemcpyHostToDevice, stream));
+      cudaIpcMemHandle_t h;
+      B2_CUDA(cudaIpcGetMemHandle(&h, buf.ptr));
+      const uint64_t n = es.ids.size();
+      B2_CUDA(cudaMemcpyAsync(base + L.local_starts[k], es.starts.data(), (steps + 1) * 8, cudaMemcpyHostToDevice, stream));
+      B2_CUDA(cudaMemcpyAsync(base + L.local_handle[k], &h, 64, cudaMemcpyHostToDevice, stream));
+      B2_CUDA(cudaMemcpyAsync(base + L.local_handle[k] + 64, &n, 8, cudaMemcpyHostToDevice, stream));
+      B2_CUDA(cudaStreamSynchronize(stream));  // h and n are stack values
+    }
     B2_CUDA(cudaStreamSynchronize(stream));
     published = true;
   }
@@ -3429,6 +3471,45 @@ struct Engine::Impl {
     std::vector<StageLayout> lay;
     std::vector<std::vector<uint8_t>> stg;
     if (world > 1) stg = gather_stages(lay);
+    if (world > 1 && !lists_merged) {
+      // local lists: every rank's list per tick, in rank order (= ascending)
+      for (size_t k = 0; k < streams.size(); ++k) {
+        EventStreamDev& es = streams[k];
+        if (!es.local) continue;
+        std::vector<std::vector<uint32_t>> ids(static_cast<size_t>(world));
+        std::vector<std::vector<uint64_t>> starts(static_cast<size_t>(world), std::vector<uint64_t>(steps + 1));
+        for (int q = 0; q < world; ++q) {
+          const uint8_t* b = stg[size_t(q)].data();
+          std::memcpy(starts[size_t(q)].data(), b + lay[size_t(q)].local_starts[k], (steps + 1) * 8);
+          uint64_t n = 0;
+          std::memcpy(&n, b + lay[size_t(q)].local_handle[k] + 64, 8);
+          if (q == rank) {
+            ids[size_t(q)] = es.ids;
+          } else if (n) {
+            cudaIpcMemHandle_t h;
+            std::memcpy(&h, b + lay[size_t(q)].local_handle[k], 64);
+            void* peer = nullptr;
+            B2_CUDA(cudaIpcOpenMemHandle(&peer, h, cudaIpcMemLazyEnablePeerAccess));
+            ids[size_t(q)].resize(n);
+            cudaError_t e = cudaMemcpy(ids[size_t(q)].data(), peer, n * 4, cudaMemcpyDeviceToHost);
+            cudaIpcCloseMemHandle(peer);
+            B2_CUDA(e);
+          }
+          check(ids[size_t(q)].size() == n && starts[size_t(q)][steps] == n, "local event list size mismatch");
+        }
+        std::vector<uint32_t> merged;
+        std::vector<uint64_t> mstarts(1, 0);
+        for (size_t rel = 0; rel < steps; ++rel) {
+          for (int q = 0; q < world; ++q)
+            merged.insert(merged.end(), ids[size_t(q)].begin() + long(starts[size_t(q)][rel]),
+                          ids[size_t(q)].begin() + long(starts[size_t(q)][rel + 1]));
+          mstarts.push_back(merged.size());
+        }
+        es.ids = std::move(merged);
+        es.starts = std::move(mstarts);
+      }
+      lists_merged = true;
+    }
     // population column: local device array on one GPU, else every rank's
     // block in rank order
     auto pop_column = [&](size_t p, int k, size_t elem, const std::function<size_t(const StageLayout&)>& off) {

@@ -74,26 +74,30 @@ def test_stdp_rank_plans_replicate_the_inputs(pkg, tmp_path, world):
     """The Poisson inputs, which no synapse targets, run whole on every rank
     (draws keyed by global index), so their spikes need no exchange and feed
     the target-ordered on_pre kernel over the rank's own targets; the target
-    neurons are partitioned and exchanged for on_post."""
+    neurons are partitioned, and their spikes, which only on_post over the
+    rank's own in-edges reads, stay local: no kernel of the tick waits on
+    another GPU."""
     data = model_file("stdp_small", tmp_path).read_bytes()
     targets = json.loads(data)["definition"]["populations"][1]["count"]
     for r in range(world):
         src = pkg.codegen(data, rank=r, world_size=world)
         names = [k.split("_", 2)[2] for k in kernels(src)]
-        assert names == ["neurons_step", "neurons_exchange", "inputs_step", "stdp_pre_targets", "stdp_pre_deliver",
-                         "stdp_post_edges"]
+        assert names == ["neurons_step_inputs_step", "stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]
+        assert "b2_ll_store(((u64*)" not in src  # no peer stores either
         lo, hi = pkg.partition(targets, r, world)
         assert f"__ldg(other + q) - {lo}u" in src[src.index("stdp_pre_targets("):]
         assert f"tj + {lo}u" in src[src.index("stdp_pre_deliver("):]
-    # diagnostic: partition and exchange the inputs as well (the bucket
-    # scatter reads the exchanged global list)
-    os.environ["B2GPU_REPLICATE"] = "0"
-    try:
-        names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=0, world_size=world))]
-    finally:
-        del os.environ["B2GPU_REPLICATE"]
-    assert names == ["neurons_step", "neurons_exchange", "inputs_step", "inputs_exchange", "stdp_pre_targets",
-                     "stdp_pre_deliver", "stdp_post_edges"]
+    # diagnostics: partition and exchange the inputs as well (the bucket
+    # scatter reads the exchanged global list); exchange the targets too
+    for env, expect in ((dict(B2GPU_REPLICATE="0"), ["neurons_step_inputs_step", "inputs_exchange"]),
+                        (dict(B2GPU_LOCAL_STREAMS="0"), ["neurons_step", "neurons_exchange", "inputs_step"])):
+        os.environ.update(env)
+        try:
+            names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=0, world_size=world))]
+        finally:
+            for key in env:
+                del os.environ[key]
+        assert names == expect + ["stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]
 
 
 def _gloo_rank(rank, world, port, q):
@@ -201,8 +205,8 @@ def test_ranks_match_oracle(pkg, oracle, tmp_path, world):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world,replicate", [(2, "1"), (3, "1"), (2, "0")])
-def test_stdp_ranks_match_one_gpu(pkg, tmp_path, monkeypatch, world, replicate):
+@pytest.mark.parametrize("world,replicate,local", [(2, "1", "1"), (3, "1", "1"), (2, "0", "1"), (2, "1", "0")])
+def test_stdp_ranks_match_one_gpu(pkg, tmp_path, monkeypatch, world, replicate, local):
     """STDP with on_pre and on_post on 2-3 ranks against the same network on
     one GPU, byte for byte (the device arithmetic is the same; the trace
     decay's exp rules out the oracle as a byte-exact reference)."""
@@ -214,6 +218,7 @@ def test_stdp_ranks_match_one_gpu(pkg, tmp_path, monkeypatch, world, replicate):
         (tmp_path / "one").mkdir()
         eng.write_results(tmp_path / "one")
     monkeypatch.setenv("B2GPU_REPLICATE", replicate)
+    monkeypatch.setenv("B2GPU_LOCAL_STREAMS", local)
     lines = torchrun(world, ["run", model, tmp_path / "many"])
     assert_same_files(tmp_path / "many", tmp_path / "one")
     total = json.loads((tmp_path / "one" / "summary.json").read_text())["synaptic_events"]

@@ -129,8 +129,10 @@ int b2g_codegen(const char* json, size_t json_len, const b2g_options* options, c
  *      rank 0: b2g_write_results (merged, identical to a one-GPU run).
  * b2g_read_state returns the rank's own block (all of a replicated
  * population, i.e. one that no synapse targets: every rank evaluates it
- * whole); b2g_spikes returns the global list (every rank holds it);
- * b2g_get_stats counts this rank's deliveries. */
+ * whole); b2g_spikes returns the global list of a population whose spikes
+ * an on_pre pathway reads (every rank holds it), else the rank's own block's
+ * (rank 0's results merge every rank's); b2g_get_stats counts this rank's
+ * deliveries. */
 
 /* Global index range [*lo, *hi) that `rank` of `world_size` owns in a
  * population of `count` neurons (pure function, no engine needed). */

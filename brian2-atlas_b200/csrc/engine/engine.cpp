@@ -772,14 +772,19 @@ struct Engine::Impl {
         int init_delay = -1;  // device per-edge delays of a procedural delay initializer
         if (procedural && pw.delay_initializer) {
           const auto& in = *pw.delay_initializer;
+          const double ddt = m.populations[def.source_population].dt;
+          // materialize_uniform_ticks' own check
+          check(std::isfinite(*in.minimum) && std::isfinite(*in.maximum) && *in.minimum >= 0.0 &&
+                    *in.minimum <= *in.maximum && std::isfinite(ddt) && ddt > 0.0 && *in.maximum / ddt < 1000001.0,
+                "invalid uniform delay initializer");
           uint64_t dmin = 0, dmax = 0;
           if (opt.dry_run) {
             init_delay = alloc(0);
             dmax = 1;  // plan as per-edge delays
           } else {
             DeviceBuffer ticks;
-            delay_ticks_uniform_device(sd.edges, topo.seed, in.stream, *in.minimum, *in.maximum,
-                                       m.populations[def.source_population].dt, ticks, dmin, dmax, stream);
+            delay_ticks_uniform_device(sd.edges, topo.seed, in.stream, *in.minimum, *in.maximum, ddt, ticks, dmin, dmax,
+                                       stream);
             init_delay = adopt(std::move(ticks));
           }
           pd.uniform = dmin == dmax;

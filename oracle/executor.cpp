@@ -1219,6 +1219,12 @@ void materialize_projection(const Model& m, const SynapseDef& def, const Synapse
   for (const auto& p : inst.pathways) {
     if (p.delay_initializer) {
       double dt = p.kind == "pre" ? m.populations[def.source_population].dt : m.populations[def.target_population].dt;
+      const Initializer& di = *p.delay_initializer;
+      // materialize_uniform_ticks validates before drawing
+      if (di.kind == Initializer::Kind::Uniform)
+        check(std::isfinite(*di.minimum) && std::isfinite(*di.maximum) && *di.minimum >= 0.0 &&
+                  *di.minimum <= *di.maximum && std::isfinite(dt) && dt > 0.0 && *di.maximum / dt < 1000001.0,
+              "invalid uniform delay initializer");
       auto d = materialize_initializer(t.edge_count, t.seed, *p.delay_initializer, dt);
       std::vector<size_t> ticks(d.size());
       for (size_t e = 0; e < d.size(); ++e) ticks[e] = size_t(std::floor(d[e] / dt + 0.5));

@@ -175,3 +175,18 @@ def test_codegen_procedural_delay_initializers(pkg):
         "kind": "clipped_normal", "mean": "3f1a36e2eb1c432d", "std": "3f1a36e2eb1c432d", "stream": 1}
     with pytest.raises(pkg.B2GpuError, match="clipped-normal delay initializers"):
         pkg.codegen(encode_model(doc))
+
+
+def test_invalid_uniform_delay_initializer_is_refused(pkg, oracle, tmp_path):
+    """A negative minimum fails materialize_uniform_ticks' check, in the
+    engine and in the oracle, with the reference's message."""
+    import subprocess
+    doc = json.loads(golden_procedural_initializers())
+    doc["instance"]["synapses"][1]["pathways"][0]["delay_initializer"]["minimum"] = "bf1a36e2eb1c432d"  # -1e-4
+    data = encode_model(doc)
+    with pytest.raises(pkg.B2GpuError, match="invalid uniform delay initializer"):
+        pkg.codegen(data)
+    path = tmp_path / "model.json"
+    path.write_bytes(data)
+    proc = subprocess.run([str(oracle), str(path), str(tmp_path / "out")], capture_output=True, text=True)
+    assert proc.returncode == 1 and "invalid uniform delay initializer" in proc.stderr

@@ -6,6 +6,7 @@
 #include <algorithm>
 #include <chrono>
 #include <cmath>
+#include <optional>
 #include <cstdio>
 #include <cstring>
 #include <functional>
@@ -23,6 +24,57 @@ extern const char* const kDeviceLibSource;  // device_lib.cuh, embedded at build
 
 using b2ir::check;
 using b2ir::Error;
+
+// ------------------------------------------------------- host initializers
+namespace {
+
+// Topology counter draws (brian2-rust/src/large_topology.rs; the device
+// generators in topology.cu use the same constants and steps).
+uint64_t host_topo_draw(uint64_t seed, uint64_t stream, uint64_t edge, uint64_t attempt) {
+  uint64_t v = seed ^ (stream * 0xd2b74407b1ce6e93ull) ^ (edge * 0x9e3779b97f4a7c15ull) ^
+               (attempt * 0xca5a826395121157ull);
+  v += 0x9e3779b97f4a7c15ull;
+  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+  v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+  return v ^ (v >> 31);
+}
+
+double host_topo_unit(uint64_t seed, uint64_t stream, uint64_t edge, uint64_t attempt) {
+  return (double(host_topo_draw(seed, stream, edge, attempt) >> 11) + 0.5) * (1.0 / 9007199254740992.0);
+}
+
+// Clipped-normal per-edge values (materialize_initializer and
+// materialize_delay_initializer, brian2-rust/src/executor.rs:120-188): per
+// edge the first of up to 1000 Box-Muller draws (u1 on `stream`, u2 on
+// `stream + 1`; sqrt, log and cos are the host's, as the reference's f64
+// calls) that lies in [minimum, maximum].  Delays clip the bounds to
+// [max(minimum, 0), maximum or dt * 1e6].  Host arithmetic keeps the values
+// bit-identical to the reference's; the edge count is that of one projection.
+std::vector<double> clipped_normal_host(uint64_t n, uint64_t seed, const b2ir::Initializer& in,
+                                        std::optional<double> delay_dt) {
+  std::optional<double> lo = in.minimum, hi = in.maximum;
+  if (delay_dt) {
+    lo = std::fmax(lo.value_or(0.0), 0.0);
+    hi = hi.value_or(*delay_dt * 1000000.0);
+  }
+  std::vector<double> out(n);
+  for (uint64_t e = 0; e < n; ++e) {
+    bool found = false;
+    for (uint64_t attempt = 0; attempt < 1000 && !found; ++attempt) {
+      const double u1 = host_topo_unit(seed, in.stream, e, attempt * 2);
+      const double u2 = host_topo_unit(seed, in.stream + 1, e, attempt * 2 + 1);
+      const double v = in.mean + in.std * (std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2));
+      if ((!lo || v >= *lo) && (!hi || v <= *hi)) {
+        out[e] = v;
+        found = true;
+      }
+    }
+    check(found, "clipped-normal rejection limit exceeded");
+  }
+  return out;
+}
+
+}  // namespace
 
 // ------------------------------------------------------------------ buffers
 DeviceBuffer::DeviceBuffer(size_t n) : bytes(n) {
@@ -697,8 +749,6 @@ struct Engine::Impl {
         for (const auto& pw : inst.pathways) {
           if (pw.delay_initializer) {
             // drawn per edge on the device below (edge id = source-major position)
-            check(pw.delay_initializer->kind == b2ir::Initializer::Kind::Uniform,
-                  "clipped-normal delay initializers are not supported by the GPU engine yet");
             check(pw.kind == "pre" && world == 1,
                   "procedural delay initializers are supported on on_pre pathways of one GPU");
           }
@@ -723,7 +773,12 @@ struct Engine::Impl {
         auto init = topo.initializers.find(sym.name);
         if (procedural && init != topo.initializers.end()) {
           const auto& in = init->second;
-          check(in.kind == b2ir::Initializer::Kind::Uniform, "clipped-normal initializers are not supported by the GPU engine yet");
+          if (in.kind == b2ir::Initializer::Kind::ClippedNormal) {
+            // rejection sampling with transcendentals: drawn on the host
+            const std::vector<double> v = clipped_normal_host(opt.dry_run ? 0 : sd.edges, topo.seed, in, std::nullopt);
+            sd.param_ptr[sym.name] = upload(v.data(), std::max<size_t>(sd.edges, 1) * 8);
+            continue;
+          }
           int k = alloc(sd.edges * 8);
           if (!opt.dry_run)
             uniform_initializer_device(static_cast<double*>(dptr(k)), sd.edges, topo.seed, in.stream, *in.minimum,
@@ -770,7 +825,25 @@ struct Engine::Impl {
         pd.stream = pops[pd.endpoint_pop].stream_of_event[size_t(ev - endpoint.events.begin())];
         const auto& d = delays[k];
         int init_delay = -1;  // device per-edge delays of a procedural delay initializer
-        if (procedural && pw.delay_initializer) {
+        if (procedural && pw.delay_initializer && pw.delay_initializer->kind == b2ir::Initializer::Kind::ClippedNormal) {
+          // drawn on the host (rejection sampling with transcendentals)
+          const double ddt = m.populations[def.source_population].dt;
+          const std::vector<double> v = clipped_normal_host(opt.dry_run ? 0 : sd.edges, topo.seed, *pw.delay_initializer, ddt);
+          std::vector<uint16_t> ticks(v.size());
+          uint64_t dmin = UINT64_MAX, dmax = 0;
+          for (size_t e = 0; e < v.size(); ++e) {
+            const double t = std::floor(v[e] / ddt + 0.5);
+            check(t >= 0.0 && t < 65535.0, "procedural delay outside 0 to 65534 ticks");
+            ticks[e] = uint16_t(t);
+            dmin = std::min<uint64_t>(dmin, ticks[e]);
+            dmax = std::max<uint64_t>(dmax, ticks[e]);
+          }
+          if (opt.dry_run) dmin = 0, dmax = 1;  // plan as per-edge delays
+          init_delay = upload(ticks.data(), std::max<size_t>(ticks.size(), 1) * 2);
+          pd.uniform = dmin == dmax;
+          pd.delay = dmin;
+          pd.max_delay = dmax;
+        } else if (procedural && pw.delay_initializer) {
           const auto& in = *pw.delay_initializer;
           const double ddt = m.populations[def.source_population].dt;
           // materialize_uniform_ticks' own check

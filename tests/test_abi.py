@@ -164,17 +164,20 @@ def test_codegen_single_delay_golden_uses_buckets(pkg):
         "projection_1_0_pre_atomic", "projection_1_1_pre_atomic"]
 
 
-def test_codegen_procedural_delay_initializers(pkg):
-    """Uniform delay initializers on fixed in-degree projections plan as
-    per-edge delays (target-ordered scan); clipped-normal ones are refused
-    before any device work."""
-    names = kernels(pkg.codegen(golden_procedural_initializers()))
-    assert sum(n.endswith("_pre_targets") for n in names) == 4
-    doc = json.loads(golden_procedural_initializers())
-    doc["instance"]["synapses"][0]["pathways"][0]["delay_initializer"] = {
-        "kind": "clipped_normal", "mean": "3f1a36e2eb1c432d", "std": "3f1a36e2eb1c432d", "stream": 1}
-    with pytest.raises(pkg.B2GpuError, match="clipped-normal delay initializers"):
-        pkg.codegen(encode_model(doc))
+def test_codegen_procedural_delay_initializers(pkg, oracle, tmp_path):
+    """Uniform and clipped-normal delay initializers on fixed in-degree
+    projections plan as per-edge delays (target-ordered scan); the oracle
+    runs both."""
+    import subprocess
+    for normal in (False, True):
+        data = golden_procedural_initializers(normal=normal)
+        names = kernels(pkg.codegen(data))
+        assert sum(n.endswith("_pre_targets") for n in names) == 4
+        path = tmp_path / f"model{int(normal)}.json"
+        path.write_bytes(data)
+        proc = subprocess.run([str(oracle), str(path), str(tmp_path / f"out{int(normal)}")], capture_output=True,
+                              text=True)
+        assert proc.returncode == 0, proc.stderr
 
 
 def test_invalid_uniform_delay_initializer_is_refused(pkg, oracle, tmp_path):

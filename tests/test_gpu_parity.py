@@ -107,12 +107,14 @@ def test_single_delay_golden_variant_matches_oracle(pkg, oracle, tmp_path):
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")
 
 
-def test_procedural_initializers_match_oracle(pkg, oracle, tmp_path):
-    """Fixed in-degree edges, uniform per-edge weights and uniform per-edge
-    delays all generated on the device (target-ordered scan over per-edge
-    delays), against the oracle's host-side materialisation, byte for byte."""
+@pytest.mark.parametrize("normal", [False, True])
+def test_procedural_initializers_match_oracle(pkg, oracle, tmp_path, normal):
+    """Fixed in-degree edges generated on the device with uniform per-edge
+    weights and delays (drawn on the device) or clipped-normal ones (drawn on
+    the host), delivered by the target-ordered scan over per-edge delays,
+    against the oracle's host-side materialisation, byte for byte."""
     path = tmp_path / "model.json"
-    path.write_bytes(golden_procedural_initializers())
+    path.write_bytes(golden_procedural_initializers(normal=normal))
     gpu_run(pkg, path, tmp_path / "gpu")
     run_oracle(oracle, path, tmp_path / "ref")
     assert_same_files(tmp_path / "gpu", tmp_path / "ref")

@@ -1,8 +1,8 @@
 """Generate the committed AtlasIR fixtures from the reference's own frontend.
 
-Run in a container that has the reference checkout (default /root/reference):
+Run where the reference checkout is available (--reference names its root):
 
-    python tests/golden/make_fixtures.py [--reference /root/reference]
+    python tests/golden/make_fixtures.py --reference PATH [--only NAME]
 
 What it writes (all under tests/golden/):
   reference-v1/        the reference's golden b2-runner run, copied verbatim

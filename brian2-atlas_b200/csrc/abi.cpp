@@ -307,7 +307,9 @@ int b2g_run_cli(int argc, const char* const* argv) {
       (void)m;
       std::ifstream f(argv[2], std::ios::binary);
       std::string data((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
-      const b2canon::Layers h = b2canon::layer_hashes(b2json::parse(data.data(), data.size()));
+      b2json::Value doc = b2json::parse(data.data(), data.size());
+      b2canon::migrate_probe(doc);  // hashes of the migrated layers, as the reference prints them
+      const b2canon::Layers h = b2canon::layer_hashes(doc);
       std::printf("{\"definition\":\"%s\",\"instance\":\"%s\",\"run\":\"%s\"}\n", h.definition.c_str(),
                   h.instance.c_str(), h.run.c_str());
       return 0;

@@ -289,4 +289,35 @@ void verify_protocol(const b2json::Value& root) {
     throw b2json::Error("AtlasIR canonical layer hash mismatch");
 }
 
+bool migrate_probe(b2json::Value& root) {
+  // prepare_protocol's predecessor branch (brian2-rust/src/model.rs:4733-4777)
+  const std::string schema = root.at("schema").str();
+  if (schema != "b2ir-gate0-probe-v34" && schema != "b2ir-gate0-probe-v35" && schema != "b2ir-gate0-probe-v36" &&
+      schema != "b2ir-gate0-probe-v37")
+    return false;
+  if (schema == "b2ir-gate0-probe-v34") {
+    if (root.find("protocol")) throw b2json::Error("legacy AtlasIR has a protocol envelope");
+  } else {
+    verify_protocol(root);
+  }
+  b2json::Value* definition = root.find_mut("definition");
+  b2json::Value* populations = definition ? definition->find_mut("populations") : nullptr;
+  if (!populations || !populations->is_array()) throw b2json::Error("legacy AtlasIR has no population table");
+  for (auto& population : populations->arr_mut()) {
+    if (!population.is_object()) throw b2json::Error("invalid legacy population definition");
+    if (!population.find("linked_variables")) population.set("linked_variables", b2json::Value::array());
+  }
+  b2json::Value* functions = definition->find_mut("functions");
+  if (!functions || !functions->is_array()) throw b2json::Error("legacy AtlasIR has no Function table");
+  for (auto& function : functions->arr_mut()) {
+    if (!function.is_object()) throw b2json::Error("invalid legacy Function definition");
+    function.set("abi", b2json::Value::string("b2ir-function-v1"));
+    if (!function.find("backend_implementations")) function.set("backend_implementations", b2json::Value::object());
+  }
+  root.set("schema", b2json::Value::string("atlasir-v1"));
+  const std::string protocol = expected_protocol(root, layer_hashes(root));
+  root.set("protocol", b2json::parse(protocol.data(), protocol.size()));
+  return true;
+}
+
 }  // namespace b2canon

@@ -57,4 +57,11 @@ std::string expected_protocol(const b2json::Value& root, const Layers& layers);
 // the expected envelope.
 void verify_protocol(const b2json::Value& root);
 
+// Migrates a b2ir-gate0-probe-v34..v37 document in place to atlasir-v1 as
+// the reference does before hashing (v34: no envelope allowed; v35..v37:
+// envelope verified first; populations gain `linked_variables: []`, functions
+// the `b2ir-function-v1` ABI and empty `backend_implementations`; the
+// envelope is recomputed).  Returns false for any other schema.
+bool migrate_probe(b2json::Value& root);
+
 }  // namespace b2canon

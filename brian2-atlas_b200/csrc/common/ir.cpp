@@ -468,6 +468,9 @@ Model load_model(const char* json, size_t size) {
   }
   try {
     Model m;
+    // the probe predecessors are migrated (and their envelopes checked) on
+    // entry, like the legacy b2ir-v1 envelope below
+    b2canon::migrate_probe(doc);
     m.schema = str(doc, "schema");
     check(m.schema == "atlasir-v1" || m.schema == "b2ir-v1",
           "unsupported AtlasIR schema '" + m.schema + "'");

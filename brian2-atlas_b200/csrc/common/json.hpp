@@ -96,6 +96,39 @@ class Value {
     return !v || v->is_null();
   }
 
+  // ---- editing (schema migrations rewrite a parsed document in place)
+  static Value string(std::string s) {
+    Value v;
+    v.type_ = Type::String;
+    v.text_ = std::move(s);
+    return v;
+  }
+  static Value array() {
+    Value v;
+    v.type_ = Type::Array;
+    return v;
+  }
+  static Value object() {
+    Value v;
+    v.type_ = Type::Object;
+    return v;
+  }
+  std::vector<Value>& arr_mut() {
+    if (type_ != Type::Array) throw Error("JSON value is not an array");
+    return items_;
+  }
+  Value* find_mut(const char* key) {
+    if (type_ != Type::Object) throw Error("JSON value is not an object");
+    for (auto& kv : members_)
+      if (kv.first == key) return &kv.second;
+    return nullptr;
+  }
+  // Replace the member's value, or append the member.
+  void set(const char* key, Value v) {
+    if (Value* old = find_mut(key)) *old = std::move(v);
+    else members_.emplace_back(key, std::move(v));
+  }
+
  private:
   friend class Parser;
   Type type_ = Type::Null;

@@ -1,8 +1,9 @@
 """Canonical JSON layer hashes and the runner's non-run modes (CPU).
 
 Pins: the reference's own golden hash corpus
-(brian2-rust/tests/golden/{atlasir-v1,b2ir-v1}/{minimal-v1.json,hashes.json},
-copied to tests/golden/canonical/), Python's json.dumps(sort_keys=True,
+(brian2-rust/tests/golden/{atlasir-v1,b2ir-v1}/{minimal-v1.json,hashes.json}
+and the probe predecessors b2ir-v1/minimal-v34..v37.json, copied to
+tests/golden/canonical/), Python's json.dumps(sort_keys=True,
 separators=(",", ":"), ensure_ascii=False) for reals, escapes and non-ASCII
 text, and the runner contract of `--canonical-hashes` / `--validate` /
 "AtlasIR canonical layer hash mismatch" (brian2-rust/src/model.rs:4596-4677).
@@ -82,3 +83,34 @@ def test_validate_accepts_fixtures():
                  CANON / "atlasir-minimal-v1.json", CANON / "b2ir-minimal-v1.json"]:
         proc = runner("--validate", path)
         assert proc.returncode == 0 and proc.stdout.strip() == "validated AtlasIR", (path, proc.stderr)
+
+
+@pytest.mark.parametrize("version", [34, 35, 36, 37])
+def test_probe_predecessors_migrate(oracle, tmp_path, version):
+    """b2ir-gate0-probe-v34..v37 documents are migrated as the reference's
+    prepare_protocol does: their migrated layers hash like the current
+    minimal document (the reference's Python migrate_model gives the same
+    hashes), they validate, and they run to the same result bytes."""
+    path = CANON / f"b2ir-minimal-v{version}.json"
+    proc = runner("--canonical-hashes", path)
+    assert proc.returncode == 0, proc.stderr
+    assert json.loads(proc.stdout) == json.loads((CANON / "atlasir-hashes.json").read_text())["layers"]
+    proc = runner("--validate", path)
+    assert proc.returncode == 0 and proc.stdout.strip() == "validated AtlasIR", proc.stderr
+    for name, model in (("probe", path), ("current", CANON / "atlasir-minimal-v1.json")):
+        done = subprocess.run([str(oracle), str(model), str(tmp_path / name)], capture_output=True, text=True)
+        assert done.returncode == 0, done.stderr
+    assert (tmp_path / "probe" / "results.bin").read_bytes() == (tmp_path / "current" / "results.bin").read_bytes()
+
+
+def test_probe_predecessor_envelopes_are_checked(tmp_path):
+    doc = json.loads((CANON / "b2ir-minimal-v35.json").read_text())
+    doc["instance"]["rng_seed"] += 1
+    (tmp_path / "v35.json").write_text(json.dumps(doc))
+    proc = runner("--validate", tmp_path / "v35.json")
+    assert proc.returncode == 1 and "canonical layer hash mismatch" in proc.stderr
+    doc = json.loads((CANON / "b2ir-minimal-v34.json").read_text())
+    doc["protocol"] = json.loads((CANON / "b2ir-minimal-v35.json").read_text())["protocol"]
+    (tmp_path / "v34.json").write_text(json.dumps(doc))
+    proc = runner("--validate", tmp_path / "v34.json")
+    assert proc.returncode == 1 and "legacy AtlasIR has a protocol envelope" in proc.stderr

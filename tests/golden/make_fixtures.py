@@ -8,6 +8,9 @@ What it writes (all under tests/golden/):
   reference-v1/        the reference's golden b2-runner run, copied verbatim
                        (brian2-rust/tests/fixtures/reference-v1/): model.json,
                        results.bin, events.bin, summary.json
+  canonical/           the reference's canonical-hash corpus
+                       (brian2-rust/tests/golden/{atlasir-v1,b2ir-v1}/) and its
+                       b2ir-gate0-probe-v34..v37 vectors, copied verbatim
   models/*.json[.gz]   AtlasIR documents lowered by the reference's
                        brian2_rust.export.lower_network (export.py:2540) from
                        small versions of the benchmark networks (CUBA, COBAHH,
@@ -272,6 +275,15 @@ def main() -> None:
     dst.mkdir(exist_ok=True)
     for name in ("model.json", "reference/results.bin", "reference/events.bin", "reference/summary.json"):
         shutil.copyfile(golden / name, dst / Path(name).name)
+    # canonical-hash corpus and the probe predecessors, renamed by schema
+    corpus = reference / "brian2-rust" / "tests" / "golden"
+    canon = HERE / "canonical"
+    canon.mkdir(exist_ok=True)
+    for schema in ("atlasir", "b2ir"):
+        for name in ("minimal-v1.json", "hashes.json"):
+            shutil.copyfile(corpus / f"{schema}-v1" / name, canon / f"{schema}-{name}")
+    for version in (34, 35, 36, 37):
+        shutil.copyfile(corpus / "b2ir-v1" / f"minimal-v{version}.json", canon / f"b2ir-minimal-v{version}.json")
 
     prepare_frontend(reference)
     import numpy as np

@@ -254,3 +254,27 @@ def test_stdp_targets_equal_serial_fold(pkg, tmp_path, monkeypatch):
     for name in variants:
         assert stats[name]["synaptic_events"] == stats["fold"]["synaptic_events"]
         assert_same_files(tmp_path / name, tmp_path / "fold")
+
+
+def test_bucket_delivery_of_crowded_targets(pkg, tmp_path, monkeypatch):
+    """150 inputs firing with probability 0.4 per tick onto 4 neurons with
+    in-degree 100: about 40 on_pre events reach each target every tick, past
+    the 32 a delivery warp ranks by shuffles, so the in-place bucket sort
+    runs; results equal the single-thread fold's byte for byte."""
+    import gzip
+    import importlib
+    import struct
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    with gzip.open(MODELS / "stdp_small.json.gz", "rb") as f:
+        template = json.loads(f.read())
+    doc = synthetic.stdp_feedforward(template, 150, 4, 100, ticks=300, seed=13)
+    rates = doc["instance"]["populations"][0]["parameters"]["rates"]
+    doc["instance"]["populations"][0]["parameters"]["rates"] = [struct.pack(">d", 4000.0).hex()] * len(rates)
+    path = tmp_path / "crowded.json"
+    path.write_bytes(encode_model(doc))
+    stats = {}
+    for mode in ("0", "1"):
+        monkeypatch.setenv("B2GPU_TARGETS", mode)
+        stats[mode] = gpu_run(pkg, path, tmp_path / f"gpu{mode}")
+    assert stats["1"]["synaptic_events"] == stats["0"]["synaptic_events"] > 300 * 4 * 33
+    assert_same_files(tmp_path / "gpu1", tmp_path / "gpu0")

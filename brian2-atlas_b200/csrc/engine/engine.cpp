@@ -1,6 +1,24 @@
 // B200 engine: plan construction, kernel generation, device state, tick loop.
 // Reference semantics: brian2-rust/src/executor.rs `Runtime::new` (:3473-3901)
 // and `Runtime::advance` (:3927-4360).
+//
+// Engine::Impl, in file order:
+//   checks        capability errors before any device work
+//   populations   SoA state, parameters, event streams, monitors, partition
+//                 (target-owned blocks, replicated populations)
+//   synapses      CSRs (explicit, binary, procedural on the device), per-edge
+//                 state and parameters, delays, pending events, summed rows
+//   streams       spike rings, exchange buffers, result staging layout
+//   codegen       per-model CUDA source: step kernels (update, threshold,
+//                 compaction, reset), pathway kernels (constant-addend
+//                 atomics, edge-parallel, target-ordered buckets and scan,
+//                 serial fold), summed variables, synapse programs,
+//                 monitors, the multi-GPU exchange
+//   plan          schedule analysis: fusion, deferral, merging, one launch
+//                 per tick node
+//   compile/run   NVRTC for sm_100a, CUDA graphs of chunk ticks with
+//                 programmatic dependent launch, drains, error words
+//   results       the reference's dump layout, multi-GPU merge on rank 0
 #include "engine.hpp"
 
 #include <algorithm>

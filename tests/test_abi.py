@@ -193,3 +193,26 @@ def test_invalid_uniform_delay_initializer_is_refused(pkg, oracle, tmp_path):
     path.write_bytes(data)
     proc = subprocess.run([str(oracle), str(path), str(tmp_path / "out")], capture_output=True, text=True)
     assert proc.returncode == 1 and "invalid uniform delay initializer" in proc.stderr
+
+
+def test_no_cpu_fallback(pkg, tmp_path):
+    """Without a usable GPU the engine raises instead of computing on the
+    host, and without the built library the package refuses to load."""
+    import os
+    import subprocess
+    import sys
+    try:
+        import torch
+        if torch.cuda.is_available():
+            pytest.skip("a GPU is present")
+    except ImportError:
+        pass
+    with pytest.raises(pkg.B2GpuError, match="cuda"):
+        pkg.Engine(load("cuba_small"), device=0)
+    code = ("import importlib, sys; sys.path.insert(0, sys.argv[1]); "
+            "pkg = importlib.import_module('brian2-atlas_b200'); pkg.LIBRARY = pkg.LIBRARY.with_name('absent.so'); "
+            "pkg._lib = None\n"
+            "try:\n    pkg.library()\nexcept pkg.B2GpuError as e:\n    print('refused:', e)\n")
+    out = subprocess.run([sys.executable, "-c", code, str(ROOT)], capture_output=True, text=True,
+                         env=dict(os.environ))
+    assert out.stdout.startswith("refused:") and "build.py" in out.stdout, out.stdout + out.stderr

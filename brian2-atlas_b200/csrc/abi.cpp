@@ -288,6 +288,43 @@ void b2g_destroy(b2g_engine* e) { delete e; }
 
 const char* b2g_version(void) { return "brian2-atlas-b200 0.1 (abi 1, sm_100a)"; }
 
+namespace {
+
+// The runner's opt-in process budgets (brian2-rust/src/resource_limits.rs):
+// an environment variable of decimal digits in 1..maximum, else the default.
+uint64_t runner_budget(const char* name, uint64_t fallback, uint64_t maximum) {
+  const char* text = std::getenv(name);
+  if (!text) return fallback;
+  const std::string t = text;
+  bool digits = !t.empty() && t.size() <= 20;
+  for (char c : t) digits &= c >= '0' && c <= '9';
+  const uint64_t v = digits ? std::strtoull(t.c_str(), nullptr, 10) : 0;
+  b2ir::check(digits && v >= 1 && v <= maximum,
+              std::string(name) + " requires decimal digits in 1.." + std::to_string(maximum));
+  return v;
+}
+
+// Budgets run_cli applies (model.rs:4605-4608 and the model checks they
+// feed): IR bytes, neuron count, population steps and neuron-steps.
+b2ir::Model load_for_runner(const char* path) {
+  const uint64_t max_ir = runner_budget("B2_MAX_IR_BYTES", 2048ull * 1048576ull, 64ull * 1073741824ull);
+  runner_budget("B2_MAX_INITIAL_VALUES", 100000000ull, 8000000000ull);
+  const uint64_t max_neurons = runner_budget("B2_MAX_NEURONS", 1000000ull, 16000000ull);
+  const uint64_t max_steps = runner_budget("B2_MAX_POPULATION_STEPS", 10000000ull, 10000000ull);
+  struct stat st;
+  b2ir::check(stat(path, &st) == 0, std::string("cannot open ") + path);
+  b2ir::check(uint64_t(st.st_size) <= max_ir, "IR exceeds the configured byte budget");
+  b2ir::Model m = b2ir::load_model_file(path);
+  b2ir::check(m.neuron_count >= 1 && m.neuron_count <= max_neurons, "invalid neuron count");
+  for (const auto& p : m.populations) {
+    b2ir::check(p.steps <= max_steps, "positive population dt and valid Clock interval required");
+    b2ir::check((unsigned __int128)p.count * p.steps <= 250000000000ull, "probe population duration budget exceeded");
+  }
+  return m;
+}
+
+}  // namespace
+
 int b2g_run_cli(int argc, const char* const* argv) {
   try {
     b2ir::check(argc == 3,
@@ -295,7 +332,7 @@ int b2g_run_cli(int argc, const char* const* argv) {
                 "b2-runner --canonical-hashes MODEL.json");
     std::string first = argv[1];
     if (first == "--validate") {
-      b2ir::Model m = b2ir::load_model_file(argv[2]);
+      b2ir::Model m = load_for_runner(argv[2]);
       (void)m;
       std::printf("validated AtlasIR\n");
       return 0;
@@ -303,7 +340,7 @@ int b2g_run_cli(int argc, const char* const* argv) {
     if (first == "--canonical-hashes") {
       // validated (hashes included) first, then the layers object as
       // run_cli prints it (model.rs:4668-4670): keys in order, compact
-      b2ir::Model m = b2ir::load_model_file(argv[2]);
+      b2ir::Model m = load_for_runner(argv[2]);
       (void)m;
       std::ifstream f(argv[2], std::ios::binary);
       std::string data((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
@@ -317,7 +354,7 @@ int b2g_run_cli(int argc, const char* const* argv) {
     b2ir::check(first.rfind("--", 0) != 0, "unknown b2-runner option");
     struct stat st;
     b2ir::check(stat(argv[2], &st) != 0, "output directory already exists; choose a new directory");
-    b2ir::Model m = b2ir::load_model_file(argv[1]);
+    b2ir::Model m = load_for_runner(argv[1]);
     b2gpu::Options opt;
     b2gpu::Engine engine(m, opt);
     engine.step(UINT64_MAX);

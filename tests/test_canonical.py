@@ -114,3 +114,24 @@ def test_probe_predecessor_envelopes_are_checked(tmp_path):
     (tmp_path / "v34.json").write_text(json.dumps(doc))
     proc = runner("--validate", tmp_path / "v34.json")
     assert proc.returncode == 1 and "legacy AtlasIR has a protocol envelope" in proc.stderr
+
+
+@pytest.mark.parametrize("env,message", [
+    ({"B2_MAX_IR_BYTES": "100"}, "IR exceeds the configured byte budget"),
+    ({"B2_MAX_NEURONS": "10"}, "invalid neuron count"),
+    ({"B2_MAX_NEURONS": "1e6"}, "B2_MAX_NEURONS requires decimal digits in 1..16000000"),
+    ({"B2_MAX_IR_BYTES": "0"}, "B2_MAX_IR_BYTES requires decimal digits in 1..68719476736"),
+    ({"B2_MAX_POPULATION_STEPS": "10"}, "positive population dt and valid Clock interval required"),
+])
+def test_runner_process_budgets(tmp_path, env, message):
+    """The runner's opt-in budgets (brian2-rust/src/resource_limits.rs) with
+    the reference's defaults, limits and messages; the library API has none."""
+    import os
+    exe = ROOT / "brian2-atlas_b200" / "bin" / "b2gpu-runner"
+    for args in (["--validate", MODELS / "cuba_small.json"], [MODELS / "cuba_small.json", tmp_path / "out"]):
+        proc = subprocess.run([str(exe), *map(str, args)], capture_output=True, text=True, env=dict(os.environ, **env))
+        assert proc.returncode == 1 and message in proc.stderr, proc.stderr
+        assert not (tmp_path / "out").exists()
+    proc = subprocess.run([str(exe), "--validate", str(MODELS / "cuba_small.json")], capture_output=True, text=True,
+                          env=dict(os.environ, B2_MAX_NEURONS="400"))
+    assert proc.returncode == 0, proc.stderr

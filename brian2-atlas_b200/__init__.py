@@ -16,6 +16,7 @@ fails with an error instead of degrading.
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 from pathlib import Path
 
@@ -61,6 +62,8 @@ def library() -> ctypes.CDLL:
         "b2g_create": (c.c_void_p, [c.c_char_p, c.c_size_t, c.POINTER(Options), c.c_char_p, c.c_size_t]),
         "b2g_step": (c.c_int, [c.c_void_p, c.c_uint64, c.POINTER(c.c_int), c.c_char_p, c.c_size_t]),
         "b2g_write_results": (c.c_int, [c.c_void_p, c.c_char_p, c.c_char_p, c.c_size_t]),
+        "b2g_summary_json": (c.c_int, [c.c_void_p, c.c_char_p, c.c_size_t, c.POINTER(c.c_size_t), c.c_char_p,
+                                       c.c_size_t]),
         "b2g_get_stats": (c.c_int, [c.c_void_p, c.POINTER(Stats), c.c_char_p, c.c_size_t]),
         "b2g_read_state": (c.c_int, [c.c_void_p, c.c_uint32, c.c_char_p, c.c_void_p, c.c_size_t,
                                      c.POINTER(c.c_size_t), c.c_char_p, c.c_size_t]),
@@ -197,6 +200,14 @@ class Engine:
 
     def write_results(self, outdir) -> None:
         self._call("b2g_write_results", str(outdir).encode())
+
+    def summary(self) -> dict:
+        """summary.json of the completed run, without writing files."""
+        need = ctypes.c_size_t(0)
+        self._call("b2g_summary_json", None, 0, ctypes.byref(need))
+        buf = ctypes.create_string_buffer(need.value + 1)
+        self._call("b2g_summary_json", buf, need.value + 1, ctypes.byref(need))
+        return json.loads(buf.value.decode())
 
     def stats(self) -> dict:
         s = Stats()

@@ -123,6 +123,23 @@ int b2g_write_results(b2g_engine* e, const char* outdir, char* error, size_t cap
   });
 }
 
+int b2g_summary_json(b2g_engine* e, char* buffer, size_t capacity, size_t* length, char* error, size_t cap) {
+  return guarded(e, error, cap, [&] {
+    if (!length) throw b2ir::Error("null length");
+    b2dump::ResultSet r = e->engine->results();
+    b2gpu::Stats s = e->engine->stats();
+    // the sizes write_results would produce; nothing is written, so no dump time
+    const std::string text =
+        b2dump::summary_json(r, b2dump::dump_size(r), b2dump::event_dump_size(r), s.simulation_seconds, 0.0);
+    *length = text.size();
+    if (buffer && capacity) {
+      const size_t n = std::min(text.size(), capacity - 1);
+      std::memcpy(buffer, text.data(), n);
+      buffer[n] = '\0';
+    }
+  });
+}
+
 int b2g_get_stats(const b2g_engine* e, b2g_stats* out, char* error, size_t cap) {
   return guarded(const_cast<b2g_engine*>(e), error, cap, [&] {
     if (!out) throw b2ir::Error("null stats");

@@ -88,6 +88,14 @@ int b2g_step(b2g_engine* engine, uint64_t max_ticks, int* finished, char* error,
  * (executor.rs:4749-4824). */
 int b2g_write_results(b2g_engine* engine, const char* outdir, char* error, size_t error_capacity);
 
+/* summary.json of a completed run as text, without writing files: *length
+ * receives the text's size; when `buffer` is given, up to capacity - 1 bytes
+ * and a NUL are copied.  dump_bytes / event_dump_bytes are the sizes
+ * b2g_write_results would write; the recording time is 0.  Replaces the
+ * summary of `execute` (executor.rs:4749-4824). */
+int b2g_summary_json(b2g_engine* engine, char* buffer, size_t capacity, size_t* length, char* error,
+                     size_t error_capacity);
+
 int b2g_get_stats(const b2g_engine* engine, b2g_stats* stats, char* error, size_t error_capacity);
 
 /* Advance `ticks` ticks launching every kernel directly, bracketed by CUDA

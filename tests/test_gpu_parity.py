@@ -185,6 +185,20 @@ def test_stepwise_api_and_state_readback(pkg, oracle, tmp_path):
         assert eng.spikes(0, tick) == [int(i) for t, i in last if t == tick]
 
 
+def test_summary_without_files(pkg, tmp_path):
+    """b2g_summary_json gives summary.json's content (timings aside) without
+    writing anything."""
+    with pkg.Engine((MODELS / "cuba_small.json").read_bytes(), device=0) as eng:
+        eng.run()
+        summary = eng.summary()
+        (tmp_path / "out").mkdir()
+        eng.write_results(tmp_path / "out")
+    written = json.loads((tmp_path / "out" / "summary.json").read_text())
+    for doc in (summary, written):
+        doc.pop("timings")
+    assert summary == written and summary["synaptic_events"] > 0
+
+
 def test_nonfinite_state_raises_instead_of_faulting(pkg):
     """A value the reference would reject (overflow to inf) sets the device
     error word; the host raises and poisons the engine."""

@@ -322,7 +322,9 @@ uint64_t runner_budget(const char* name, uint64_t fallback, uint64_t maximum) {
 }
 
 // Budgets run_cli applies (model.rs:4605-4608 and the model checks they
-// feed): IR bytes, neuron count, population steps and neuron-steps.
+// feed): IR bytes, neuron count, population steps and neuron-steps, states
+// and parameters per population, statements per code object, explicit edges
+// per projection.
 b2ir::Model load_for_runner(const char* path) {
   const uint64_t max_ir = runner_budget("B2_MAX_IR_BYTES", 2048ull * 1048576ull, 64ull * 1073741824ull);
   runner_budget("B2_MAX_INITIAL_VALUES", 100000000ull, 8000000000ull);
@@ -333,9 +335,25 @@ b2ir::Model load_for_runner(const char* path) {
   b2ir::check(uint64_t(st.st_size) <= max_ir, "IR exceeds the configured byte budget");
   b2ir::Model m = b2ir::load_model_file(path);
   b2ir::check(m.neuron_count >= 1 && m.neuron_count <= max_neurons, "invalid neuron count");
+  const uint64_t max_states = runner_budget("B2_MAX_POPULATION_STATES", 32, 1024);
+  const uint64_t max_parameters = runner_budget("B2_MAX_POPULATION_PARAMETERS", 128, 1024);
+  const uint64_t max_statements = runner_budget("B2_MAX_STATEMENTS", 128, 1024);
+  const uint64_t max_edges = runner_budget("B2_MAX_EXPLICIT_SYNAPSES", 50000000ull, 1000000000ull);
+  auto statements = [&](const std::vector<b2ir::CodeObject>& codes) {
+    for (const auto& c : codes) b2ir::check(c.scalar.size() + c.vector.size() <= max_statements, "too many statements");
+  };
   for (const auto& p : m.populations) {
     b2ir::check(p.steps <= max_steps, "positive population dt and valid Clock interval required");
     b2ir::check((unsigned __int128)p.count * p.steps <= 250000000000ull, "probe population duration budget exceeded");
+    b2ir::check(p.states.size() <= max_states, "population state arrays do not match definition");
+    b2ir::check(p.parameters.size() <= max_parameters, "population parameter arrays do not match definition");
+    statements(p.code_objects);
+  }
+  for (size_t s = 0; s < m.synapses.size(); ++s) {
+    const auto& inst = m.synapse_instances[s];
+    if (inst.topology.kind == b2ir::Topology::Kind::Explicit)
+      b2ir::check(inst.source.size() <= max_edges, "invalid synaptic topology");
+    statements(m.synapses[s].code_objects);
   }
   return m;
 }

@@ -122,6 +122,10 @@ def test_probe_predecessor_envelopes_are_checked(tmp_path):
     ({"B2_MAX_NEURONS": "1e6"}, "B2_MAX_NEURONS requires decimal digits in 1..16000000"),
     ({"B2_MAX_IR_BYTES": "0"}, "B2_MAX_IR_BYTES requires decimal digits in 1..68719476736"),
     ({"B2_MAX_POPULATION_STEPS": "10"}, "positive population dt and valid Clock interval required"),
+    ({"B2_MAX_POPULATION_STATES": "1"}, "population state arrays do not match definition"),
+    ({"B2_MAX_POPULATION_PARAMETERS": "1"}, "population parameter arrays do not match definition"),
+    ({"B2_MAX_STATEMENTS": "1"}, "too many statements"),
+    ({"B2_MAX_STATEMENTS": "2000"}, "B2_MAX_STATEMENTS requires decimal digits in 1..1024"),
 ])
 def test_runner_process_budgets(tmp_path, env, message):
     """The runner's opt-in budgets (brian2-rust/src/resource_limits.rs) with
@@ -135,3 +139,11 @@ def test_runner_process_budgets(tmp_path, env, message):
     proc = subprocess.run([str(exe), "--validate", str(MODELS / "cuba_small.json")], capture_output=True, text=True,
                           env=dict(os.environ, B2_MAX_NEURONS="400"))
     assert proc.returncode == 0, proc.stderr
+
+
+def test_runner_explicit_synapse_budget():
+    import os
+    exe = ROOT / "brian2-atlas_b200" / "bin" / "b2gpu-runner"
+    proc = subprocess.run([str(exe), "--validate", str(GOLDEN / "reference-v1" / "model.json")], capture_output=True,
+                          text=True, env=dict(os.environ, B2_MAX_EXPLICIT_SYNAPSES="100"))
+    assert proc.returncode == 1 and "invalid synaptic topology" in proc.stderr

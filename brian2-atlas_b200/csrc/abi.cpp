@@ -9,6 +9,7 @@
 #include <cstddef>
 #include <cstdio>
 #include <cstring>
+#include <functional>
 #include <fstream>
 #include <memory>
 #include <string>
@@ -323,8 +324,8 @@ uint64_t runner_budget(const char* name, uint64_t fallback, uint64_t maximum) {
 
 // Budgets run_cli applies (model.rs:4605-4608 and the model checks they
 // feed): IR bytes, neuron count, population steps and neuron-steps, states
-// and parameters per population, statements per code object, explicit edges
-// per projection.
+// and parameters per population, statements per code object, TimedArray
+// values, explicit edges per projection.
 b2ir::Model load_for_runner(const char* path) {
   const uint64_t max_ir = runner_budget("B2_MAX_IR_BYTES", 2048ull * 1048576ull, 64ull * 1073741824ull);
   runner_budget("B2_MAX_INITIAL_VALUES", 100000000ull, 8000000000ull);
@@ -339,9 +340,20 @@ b2ir::Model load_for_runner(const char* path) {
   const uint64_t max_parameters = runner_budget("B2_MAX_POPULATION_PARAMETERS", 128, 1024);
   const uint64_t max_statements = runner_budget("B2_MAX_STATEMENTS", 128, 1024);
   const uint64_t max_edges = runner_budget("B2_MAX_EXPLICIT_SYNAPSES", 50000000ull, 1000000000ull);
-  auto statements = [&](const std::vector<b2ir::CodeObject>& codes) {
-    for (const auto& c : codes) b2ir::check(c.scalar.size() + c.vector.size() <= max_statements, "too many statements");
+  const uint64_t max_table = runner_budget("B2_MAX_TIMED_ARRAY_VALUES", 10000000ull, 1000000000ull);
+  std::function<void(const b2ir::ExprPtr&)> tables = [&](const b2ir::ExprPtr& e) {
+    if (!e) return;
+    if (e->op == b2ir::Op::TimedArray) b2ir::check(e->ta_values.size() <= max_table, "invalid TimedArray layout");
+    for (const auto& a : e->args) tables(a);
   };
+  auto statements = [&](const std::vector<b2ir::CodeObject>& codes) {
+    for (const auto& c : codes) {
+      b2ir::check(c.scalar.size() + c.vector.size() <= max_statements, "too many statements");
+      for (const auto* list : {&c.scalar, &c.vector})
+        for (const auto& st : *list) tables(st.value);
+    }
+  };
+  for (const auto& f : m.functions) tables(f.body);
   for (const auto& p : m.populations) {
     b2ir::check(p.steps <= max_steps, "positive population dt and valid Clock interval required");
     b2ir::check((unsigned __int128)p.count * p.steps <= 250000000000ull, "probe population duration budget exceeded");

@@ -141,9 +141,15 @@ def test_runner_process_budgets(tmp_path, env, message):
     assert proc.returncode == 0, proc.stderr
 
 
-def test_runner_explicit_synapse_budget():
+@pytest.mark.parametrize("model,env,message", [
+    (GOLDEN / "reference-v1" / "model.json", {"B2_MAX_EXPLICIT_SYNAPSES": "100"}, "invalid synaptic topology"),
+    (MODELS / "timed_input_small.json", {"B2_MAX_TIMED_ARRAY_VALUES": "3"}, "invalid TimedArray layout"),
+])
+def test_runner_model_budgets(model, env, message):
     import os
     exe = ROOT / "brian2-atlas_b200" / "bin" / "b2gpu-runner"
-    proc = subprocess.run([str(exe), "--validate", str(GOLDEN / "reference-v1" / "model.json")], capture_output=True,
-                          text=True, env=dict(os.environ, B2_MAX_EXPLICIT_SYNAPSES="100"))
-    assert proc.returncode == 1 and "invalid synaptic topology" in proc.stderr
+    proc = subprocess.run([str(exe), "--validate", str(model)], capture_output=True, text=True,
+                          env=dict(os.environ, **env))
+    assert proc.returncode == 1 and message in proc.stderr, proc.stderr
+    proc = subprocess.run([str(exe), "--validate", str(model)], capture_output=True, text=True)
+    assert proc.returncode == 0, proc.stderr

@@ -325,10 +325,10 @@ uint64_t runner_budget(const char* name, uint64_t fallback, uint64_t maximum) {
 // Budgets run_cli applies (model.rs:4605-4608 and the model checks they
 // feed): IR bytes, neuron count, population steps and neuron-steps, states
 // and parameters per population, statements per code object, TimedArray
-// values, explicit edges per projection.
+// values, explicit edges per projection, instance values.
 b2ir::Model load_for_runner(const char* path) {
   const uint64_t max_ir = runner_budget("B2_MAX_IR_BYTES", 2048ull * 1048576ull, 64ull * 1073741824ull);
-  runner_budget("B2_MAX_INITIAL_VALUES", 100000000ull, 8000000000ull);
+  const uint64_t max_values = runner_budget("B2_MAX_INITIAL_VALUES", 100000000ull, 8000000000ull);
   const uint64_t max_neurons = runner_budget("B2_MAX_NEURONS", 1000000ull, 16000000ull);
   const uint64_t max_steps = runner_budget("B2_MAX_POPULATION_STEPS", 10000000ull, 10000000ull);
   struct stat st;
@@ -367,6 +367,24 @@ b2ir::Model load_for_runner(const char* path) {
       b2ir::check(inst.source.size() <= max_edges, "invalid synaptic topology");
     statements(m.synapses[s].code_objects);
   }
+  // Instance values counted as the reference's validation counts them:
+  // state and parameter arrays, refractory arrays (2 per neuron), generator
+  // schedules (2 per spike), explicit edge lists (2 per edge), delay arrays.
+  uint64_t values = 0;
+  for (size_t p = 0; p < m.populations.size(); ++p) {
+    const auto& inst = m.population_instances[p];
+    for (const auto* table : {&inst.initial_state, &inst.parameters})
+      for (const auto& kv : *table) values += kv.second.size();
+    if (inst.refractory) values += 2 * m.populations[p].count;
+    if (inst.spike_generator) values += 2 * inst.spike_generator->spike_ticks.size();
+  }
+  for (const auto& inst : m.synapse_instances) {
+    for (const auto* table : {&inst.initial_state, &inst.parameters})
+      for (const auto& kv : *table) values += kv.second.size();
+    if (inst.topology.kind == b2ir::Topology::Kind::Explicit) values += 2 * inst.source.size();
+    for (const auto& pw : inst.pathways) values += pw.delay.size() + pw.delay_ticks.size();
+  }
+  b2ir::check(values <= max_values, "probe array budget exceeded");
   return m;
 }
 

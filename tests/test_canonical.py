@@ -144,6 +144,7 @@ def test_runner_process_budgets(tmp_path, env, message):
 @pytest.mark.parametrize("model,env,message", [
     (GOLDEN / "reference-v1" / "model.json", {"B2_MAX_EXPLICIT_SYNAPSES": "100"}, "invalid synaptic topology"),
     (MODELS / "timed_input_small.json", {"B2_MAX_TIMED_ARRAY_VALUES": "3"}, "invalid TimedArray layout"),
+    (GOLDEN / "reference-v1" / "model.json", {"B2_MAX_INITIAL_VALUES": "1000"}, "probe array budget exceeded"),
 ])
 def test_runner_model_budgets(model, env, message):
     import os

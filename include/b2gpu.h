@@ -38,10 +38,12 @@ typedef struct b2g_options {
   uint64_t ring_capacity; /* spike-ring entries per event stream, 0 for automatic */
   /* Multi-GPU (one process per GPU).  Rank r of world_size owns the global
    * indices [floor(N*r/world_size), floor(N*(r+1)/world_size)) of every
-   * population, the reference's owner rule ((i+1)*world_size-1)/N
-   * (brian2_rust/distributed.py:80-81, mpi_codegen.py:40-44), and the
-   * incoming edges of its neurons.  Callers built against an older header
-   * pass a smaller struct_size and get world_size 1. */
+   * population that a synapse targets, the reference's owner rule
+   * ((i+1)*world_size-1)/N (brian2_rust/distributed.py:80-81,
+   * mpi_codegen.py:40-44), and the incoming edges of its neurons; a
+   * population that no synapse targets runs whole on every rank.  Callers
+   * built against an older header pass a smaller struct_size and get
+   * world_size 1. */
   int32_t rank;                 /* 0 .. world_size-1 */
   int32_t world_size;           /* number of GPUs/processes, 1 for a single GPU */
   uint32_t exchange_timeout_ms; /* bound on every wait for a peer's spikes, 0 for 10000 */

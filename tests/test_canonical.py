@@ -154,3 +154,14 @@ def test_runner_model_budgets(model, env, message):
     assert proc.returncode == 1 and message in proc.stderr, proc.stderr
     proc = subprocess.run([str(exe), "--validate", str(model)], capture_output=True, text=True)
     assert proc.returncode == 0, proc.stderr
+
+
+def test_probe_function_migration_matches_reference():
+    """The Function branch of the probe migration (abi set to
+    b2ir-function-v1, empty backend_implementations added): the migrated
+    layer hashes equal those of the reference's Python migrate_model
+    (tests/golden/make_probe_function.py wrote both files)."""
+    proc = runner("--canonical-hashes", CANON / "b2ir-probe-v37-function.json")
+    assert proc.returncode == 0, proc.stderr
+    want = json.loads((CANON / "b2ir-probe-v37-function-migrated-hashes.json").read_text())["layers"]
+    assert json.loads(proc.stdout) == want

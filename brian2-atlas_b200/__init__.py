@@ -303,4 +303,4 @@ def package_dir() -> Path:
 
 
 __all__ = ["Engine", "B2GpuError", "run_model", "codegen", "partition", "spikes_from_bitmap", "spikes_scratch_bytes",
-           "version", "library", "runner_path", "LIBRARY", "RUNNER"]
+           "spikes_from_bitmap_noalloc", "SPIKES_NOALLOC_MAX_BITS", "version", "library", "runner_path", "LIBRARY", "RUNNER"]

@@ -139,7 +139,43 @@ static __device__ __align__(256) uint32_t
 namespace {
 constexpr int kNoAllocMaxDevices = 64;
 std::mutex g_noalloc_mutex;
-uint32_t* g_noalloc_scratch[kNoAllocMaxDevices];  // device address per device ordinal, looked up once
+// Per device ordinal: the array's device address and the unique id of the
+// CUDA context it was looked up in.  A context that the host framework tore
+// down and re-created (cudaDeviceReset, primary-context release) gets a new
+// id, and the address is looked up again in the new context.
+struct NoAllocSlot {
+  unsigned long long context_id = 0;
+  uint32_t* scratch = nullptr;
+};
+NoAllocSlot g_noalloc_slots[kNoAllocMaxDevices];
+
+// Unique id of the calling thread's current CUDA context (cuCtxGetCurrent +
+// cuCtxGetId, reached through the runtime's driver entry points, so the
+// library still links no driver library); 0 when it cannot be read, which
+// makes every call look the address up again.
+unsigned long long current_context_id() {
+  using GetCurrent = int (*)(void**);
+  using GetId = int (*)(void*, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  static bool resolved = false;
+  if (!resolved) {
+    resolved = true;
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<GetCurrent>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &fn, 12000, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<GetId>(fn);
+  }
+  void* ctx = nullptr;
+  unsigned long long id = 0;
+  if (!get_current || !get_id || get_current(&ctx) != 0 || !ctx || get_id(ctx, &id) != 0) return 0;
+  return id;
+}
 }  // namespace
 
 void bitmap_to_spikes_noalloc(const uint32_t* d_bits, uint64_t nbits, uint32_t* d_out, uint32_t* d_count,
@@ -147,22 +183,37 @@ void bitmap_to_spikes_noalloc(const uint32_t* d_bits, uint64_t nbits, uint32_t* 
   b2ir::check(nbits <= kNoAllocMaxBits,
               "bitmap of " + std::to_string(nbits) + " bits exceeds the no-alloc limit of " +
                   std::to_string(kNoAllocMaxBits) + " bits; use b2g_spikes_from_bitmap with a scratch buffer");
-  int device = -1;
-  B2_CUDA(cudaGetDevice(&device));
+  // The launches go to the stream's device, with that device's copy of the
+  // array: make it current for the call when it is not already.
+  int current = -1, device = -1;
+  B2_CUDA(cudaGetDevice(&current));
+  B2_CUDA(cudaStreamGetDevice(stream, &device));
   b2ir::check(device >= 0 && device < kNoAllocMaxDevices, "device ordinal out of range for the no-alloc scratch");
+  struct Restore {
+    int device;
+    bool active;
+    ~Restore() {
+      if (active) cudaSetDevice(device);
+    }
+  } restore{current, device != current};
+  if (device != current) B2_CUDA(cudaSetDevice(device));
   uint32_t* scratch = nullptr;
   {
-    // Set-up, once per device, with that device current: the address of this
-    // device's copy of the array (the first call may load the module, so it
-    // belongs before any stream capture).
+    // Set-up, once per device and context, with that device current: the
+    // address of this device's copy of the array (the first call may load
+    // the module, so it belongs before any stream capture).
     std::lock_guard<std::mutex> lock(g_noalloc_mutex);
-    if (!g_noalloc_scratch[device]) {
+    NoAllocSlot& slot = g_noalloc_slots[device];
+    const unsigned long long ctx = current_context_id();
+    if (!slot.scratch || ctx == 0 || slot.context_id != ctx) {
       void* p = nullptr;
       const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_tile_counts);
       b2ir::check(e == cudaSuccess && p, std::string("cudaGetSymbolAddress(no-alloc scratch): ") + cudaGetErrorString(e));
-      g_noalloc_scratch[device] = static_cast<uint32_t*>(p);
+      slot.scratch = static_cast<uint32_t*>(p);
+      // the lookup initialises the device's context if nothing had yet
+      slot.context_id = ctx ? ctx : current_context_id();
     }
-    scratch = g_noalloc_scratch[device];
+    scratch = slot.scratch;
   }
   bitmap_to_spikes(d_bits, nbits, d_out, d_count, scratch, stream);
 }

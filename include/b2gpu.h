@@ -184,7 +184,11 @@ int b2g_spikes_from_bitmap(const uint32_t* d_words, uint64_t nbits, uint32_t* d_
  *   - calls whose launches overlap on one GPU race on that array;
  *   - the first call on a device does a one-time set-up (it looks the array
  *     up, which may load the library's device code), so make it before any
- *     stream capture.
+ *     stream capture; the set-up is repeated, in the same way, on the first
+ *     call after the device's context was destroyed and re-created (for
+ *     instance by cudaDeviceReset), because the array then has a new address;
+ *   - the launches go to `stream`'s device, which the call makes current for
+ *     its duration when another device is current.
  * Nothing needs to be zeroed beforehand. */
 #define B2G_SPIKES_NOALLOC_MAX_BITS (1ull << 27)
 int b2g_spikes_from_bitmap_noalloc(const uint32_t* d_words, uint64_t nbits, uint32_t* d_ids, uint32_t* d_count,

@@ -258,7 +258,7 @@ def timed_input(reference: Path, n: int = 100, ticks: int = 1000, seed: int = 9)
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout")
     ap.add_argument("--only", default=None, help="write just this model (cuba_events_small, gap_junctions_small)")
     args = ap.parse_args()
     if args.only:

@@ -14,17 +14,30 @@ engine's stream) over the timed steps; `e2e` is the same count over the wall
 time of the public C-ABI b2g_step calls, which include the per-chunk
 host->device tick cursor and device->host spike-list drain.
 
+`raster_sha256` is the SHA-256 of the timed window's spikes (little-endian
+int64 (tick, index) pairs in tick, then index order, per population, the
+layout of results.bin's spike records) and `final_state_sha256` that of the
+membrane state `v` read right after the window, merged over ranks: the same
+digests at every GPU count show that a partitioned run computes the one-GPU
+network.
+
 With N > 1 GPUs (torchrun, one process per GPU) the same network is split by
 target ownership: rank r owns neurons [floor(N r/G), floor(N (r+1)/G)) and
-their incoming edges, and the tick kernels exchange spikes by storing into the
-peers' memory over NVLink (strong scaling: the total work is fixed).  Every
-timed step is bracketed by a barrier and a device synchronisation on every
-rank; the step's time is the maximum over ranks; `value` counts every rank's
-deliveries.
+their incoming edges, and the tick kernels exchange spike lists by storing
+into the peers' memory over NVLink (strong scaling: the total work is fixed).
+Every timed step is bracketed by a barrier and a device synchronisation on
+every rank; the step's time is the maximum over ranks; `value` counts every
+rank's deliveries.
 
---impl reference times the CPU restatement of the reference executor
-(oracle/b2ref, single-threaded like b2-runner) on a bounded sample of the
-same network (50,000 neurons, in-degree 1000).
+CPU side (one figure, one window): the CPU restatement of the reference
+executor (oracle/b2ref, single-threaded like b2-runner; its one-time topology
+build uses every host thread) runs the SAME network (same size, seed and
+parameters) from tick 0 for W warm-up and K timed steps of
+REFERENCE_TICKS_PER_STEP ticks.  `--impl reference` prints that as the
+reference arm; the default run reports the same measurement as
+`cpu_baseline`.  Its window lies in the network's opening transient, where
+activity (events per tick) is ~3x the steady state the GPU window sees, which
+raises a per-event CPU rate: the comparison favours the CPU.
 
 --workload stdp measures config 4 instead: 100,000 Poisson inputs at 15 Hz
 onto 10,000 conductance-based LIF neurons, in-degree 1000 (1e7 plastic
@@ -32,11 +45,22 @@ synapses, f64 weights U[0, gmax], additive pre/post traces; definition layer
 from the reference frontend's lowering of the Song-Abbott STDP example,
 tests/golden/models/stdp_small.json.gz).  On N > 1 GPUs the inputs run whole
 on every rank and the targets are partitioned.  Its CPU sample is the same
-network at 10,000 inputs onto 1,000 neurons (1e6 synapses).
+network at 10,000 inputs onto 1,000 neurons (1e6 synapses), because the full
+network's 1 GB document and 1e7 interpreted synapses do not fit a bounded CPU
+run.
+
+--workload brunel measures config 3: the balanced Brunel network of
+4,000,000 f32 LIF neurons, fixed in-degree 800 + 200 (4e9 synapses), a
+homogeneous 1.5 ms (15-tick) delay, J = 0.1 mV, g = 5, PoissonInput of 800
+inputs at twice the threshold rate (definition layer from the reference
+frontend's lowering of brunel_device.py's network at 2000 neurons,
+tests/golden/models/brunel_small.json).
 """
 from __future__ import annotations
 
 import argparse
+import gzip
+import hashlib
 import importlib
 import json
 import os
@@ -53,23 +77,29 @@ sys.path.insert(0, str(ROOT))
 
 TICKS_PER_STEP = 1000
 DT = 1e-4
-N_NEURONS = 1_000_000
-INDEGREE = 1000
-CPU_SAMPLE_NEURONS = 50_000
-CPU_SAMPLE_WARMUP = 50
-CPU_SAMPLE_TICKS = 200
 METRIC = "synaptic events/s"
 UNIT = "events/s"
+# CPU window: ticks per step of the reference arm (and of cpu_baseline, which
+# times the same window): W warm-up + K timed steps of this many ticks.
+REFERENCE_TICKS_PER_STEP = 2
 
+WORKLOADS = {
+    "c2": {"neurons": 1_000_000, "indegree": 1000, "dtype": "f64", "state_bytes": 24, "target_bytes": 8,
+           "delay": 0},
+    "brunel": {"neurons": 4_000_000, "indegree": 1000, "dtype": "f32", "state_bytes": 4, "target_bytes": 4,
+               "delay": 15},
+    "stdp": {"inputs": 100_000, "neurons": 10_000, "indegree": 1000, "rate_hz": 15.0, "dtype": "f64",
+             "sample_inputs": 10_000, "sample_neurons": 1000},
+}
 
-# DRAM bytes (read + write) per launch of the neuron step kernel on the
-# default 1M-neuron network, from one ncu capture (dram__bytes_read.sum +
-# dram__bytes_write.sum, warm cache as in the timed run; the step kernel's
-# traffic does not depend on the in-degree, so the 1M-neuron in-degree-300
-# capture stands for the full network): 74,624 + 507,904 bytes.  The 56 MB of
-# per-tick neuron state stays L2-resident within a step, so DRAM carries ~1 %
-# of the algorithmic bytes.  None for other workloads.
-STEP_DRAM_BYTES = {1_000_000: 74_624 + 507_904}
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
+# dominant kernel, from one ncu capture of that kernel at the bench's network
+# size (profiles/*.md gives the command and the figures).  The C2 step
+# kernel's traffic does not depend on the in-degree, so a capture at in-degree
+# 300 (a smaller device footprint) stands for the full network.  The per-tick
+# neuron state (56 MB) stays L2-resident within a bench step, so DRAM carries
+# ~1 % of the algorithmic bytes.  None where no capture exists.
+TRAFFIC = {("c2", "_step", 1): 74_624 + 507_904}
 
 
 def peaks():
@@ -78,6 +108,28 @@ def peaks():
         p = json.loads(path.read_text())
         return float(p["hbm_gbs"]), "measured"
     return 6650.0, "fallback"
+
+
+def host_facts() -> dict:
+    model = None
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    model = line.split(":", 1)[1].strip()
+                    break
+    except OSError:
+        pass
+    mem = None
+    try:
+        with open("/proc/meminfo") as f:
+            for line in f:
+                if line.startswith("MemTotal:"):
+                    mem = round(int(line.split()[1]) / 2 ** 20, 1)
+    except OSError:
+        pass
+    return {"cpu_model": model, "nproc": os.cpu_count(), "cpus_usable": len(os.sched_getaffinity(0)),
+            "mem_gib": mem}
 
 
 class ClockSampler:
@@ -112,6 +164,7 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
+            self.thread.join(timeout=5)
 
     def summary(self):
         sm, mx, reasons = [], [], set()
@@ -134,71 +187,149 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _synthetic():
+    return importlib.import_module("brian2-atlas_b200.synthetic")
+
+
 def build_model(n, indegree, ticks, seed=3):
-    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
     template = json.loads((ROOT / "tests" / "golden" / "models" / "cuba_poisson_small.json").read_text())
-    return synthetic.encode(synthetic.cuba_fixed_indegree(template, n=n, indegree=indegree, ticks=ticks, seed=seed))
+    return _synthetic().encode(_synthetic().cuba_fixed_indegree(template, n=n, indegree=indegree, ticks=ticks,
+                                                                seed=seed))
 
 
-STDP_INPUTS, STDP_NEURONS, STDP_INDEGREE, STDP_RATE_HZ = 100_000, 10_000, 1000, 15.0
-STDP_SAMPLE_INPUTS, STDP_SAMPLE_NEURONS = 10_000, 1000
+def build_brunel(n, indegree, ticks, seed=4):
+    template = json.loads((ROOT / "tests" / "golden" / "models" / "brunel_small.json").read_text())
+    return _synthetic().encode(_synthetic().brunel_fixed_indegree(template, n=n, indegree=indegree, ticks=ticks,
+                                                                  seed=seed))
 
 
 def build_stdp(n_inputs, n_neurons, indegree, ticks, seed=5):
-    import gzip
-    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
     with gzip.open(ROOT / "tests" / "golden" / "models" / "stdp_small.json.gz", "rb") as f:
         template = json.loads(f.read())
-    return synthetic.stdp_feedforward(template, n_inputs, n_neurons, indegree, ticks=ticks, seed=seed, spliced=True)
+    return _synthetic().stdp_feedforward(template, n_inputs, n_neurons, indegree, ticks=ticks, seed=seed,
+                                         spliced=True)
 
 
-def cpu_sample(workdir: Path, warmup_ticks: int, timed_ticks: int, workload: str = "c2"):
-    """Oracle (CPU restatement of b2-runner) on the bounded sample network."""
+def build_workload(args, ticks, cpu_sample=False):
+    w = WORKLOADS[args.workload]
+    if args.workload == "stdp":
+        if cpu_sample:
+            return build_stdp(w["sample_inputs"], w["sample_neurons"], w["indegree"], ticks)
+        return build_stdp(w["inputs"], w["neurons"], w["indegree"], ticks)
+    if args.workload == "brunel":
+        return build_brunel(args.neurons, args.indegree, ticks)
+    return build_model(args.neurons, args.indegree, ticks)
+
+
+def describe(args, world):
+    """The `config` object of both arms (identical, so the lines compare)."""
+    w = WORKLOADS[args.workload]
+    if args.workload == "stdp":
+        return {"workload": "config 4: STDP feedforward, 100k Poisson inputs at 15 Hz onto 10k COBA LIF neurons, "
+                            "in-degree 1000 (1e7 plastic synapses, on_pre + on_post)",
+                "inputs": w["inputs"], "neurons": w["neurons"], "indegree": w["indegree"],
+                "synapses": w["neurons"] * w["indegree"], "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+                "parallelism": "single GPU" if world == 1 else
+                f"{world} GPUs: inputs replicated on every rank, targets partitioned",
+                "l2": "256 MiB buffer written between timed steps; the 1e7-edge synapse state (320 MB) exceeds L2"}
+    if args.workload == "brunel":
+        return {"workload": "config 3: Brunel balanced network, f32 LIF, fixed in-degree 800+200, 15-tick delay, "
+                            "PoissonInput 800 at 2x threshold rate",
+                "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
+                "delay_ticks": 15, "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+                "parallelism": "single GPU" if world == 1 else
+                f"{world} GPUs: target-owned partition, spike lists exchanged by peer stores over NVLink",
+                "l2": "256 MiB buffer written between timed steps; 16 GB of row targets exceed L2"}
+    return {"workload": "config 2: CUBA 1M neurons, fixed in-degree 1000 (1e9 synapses), Poisson 100x10 Hz",
+            "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
+            "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+            "parallelism": "single GPU" if world == 1 else
+            f"{world} GPUs: target-owned partition, spike lists exchanged by peer stores over NVLink",
+            "l2": "256 MiB buffer written between timed steps; per-tick neuron state (56 MB) stays "
+                  "L2-resident within a step"}
+
+
+def cpu_window(args):
+    """The oracle (CPU restatement of b2-runner) over W warm-up and K timed
+    steps of REFERENCE_TICKS_PER_STEP ticks of the workload's network, from
+    tick 0.  Returns the oracle's measurement plus a description."""
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
-    path = workdir / "cpu_sample.json"
-    ticks = warmup_ticks + timed_ticks + 1
-    if workload == "stdp":
-        path.write_bytes(build_stdp(STDP_SAMPLE_INPUTS, STDP_SAMPLE_NEURONS, STDP_INDEGREE, ticks))
-    else:
-        path.write_bytes(build_model(CPU_SAMPLE_NEURONS, INDEGREE, ticks))
-    out = subprocess.run([str(ROOT / "oracle" / "b2ref"), "--timed", str(warmup_ticks), str(timed_ticks), str(path)],
-                         check=True, capture_output=True, text=True)
-    return json.loads(out.stdout)
-
-
-REFERENCE_TICKS_PER_STEP = 20  # one reference step: 20 ticks of the CPU sample network
+    warm = REFERENCE_TICKS_PER_STEP * args.warmup
+    timed = REFERENCE_TICKS_PER_STEP * args.steps
+    t0 = time.time()
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "cpu_window.json"
+        path.write_bytes(build_workload(args, warm + timed + 1, cpu_sample=True))
+        t_json = time.time() - t0
+        out = subprocess.run([str(ROOT / "oracle" / "b2ref"), "--timed", str(warm), str(timed), str(path)],
+                             check=True, capture_output=True, text=True)
+    s = json.loads(out.stdout)
+    w = WORKLOADS[args.workload]
+    network = (f"config 4 scaled to {w['sample_inputs']} inputs onto {w['sample_neurons']} neurons (in-degree "
+               f"{w['indegree']})" if args.workload == "stdp" else "the bench's own network (same size and seed)")
+    s["sample"] = (f"ticks {warm}..{warm + timed} of {network}, from tick 0 (the opening transient); "
+                   f"oracle/b2ref tick loop on one thread; {s['synaptic_events']} events and {s['spikes']} spikes "
+                   f"in {s['seconds']:.3f} s; topology build {s['build_seconds']:.1f} s on every host thread, "
+                   f"document {t_json:.1f} s")
+    s["host"] = host_facts()
+    return s
 
 
 def run_reference(args, world, rank):
-    """CPU reference arm: rank 0 only; W warm-up steps then K timed steps of
-    REFERENCE_TICKS_PER_STEP ticks each, in one oracle process."""
+    """CPU reference arm: rank 0 only (the others exit without work)."""
     if rank != 0:
         return
-    steps, warmup = args.steps, args.warmup
-    with tempfile.TemporaryDirectory() as tmp:
-        s = cpu_sample(Path(tmp), REFERENCE_TICKS_PER_STEP * warmup, REFERENCE_TICKS_PER_STEP * steps, args.workload)
-    total_events, total_seconds = s["synaptic_events"], s["seconds"]
-    value = total_events / total_seconds if total_seconds > 0 else 0.0
-    sim_seconds = s["ticks"] * DT
-    per_step = [s]
+    s = cpu_window(args)
+    value = s["synaptic_events"] / s["seconds"] if s["seconds"] > 0 else 0.0
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": steps,
-        "warmup": warmup, "ms_per_step": 1e3 * total_seconds / max(steps, 1), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic",
-        "config": {"workload": f"STDP feedforward sample: {STDP_SAMPLE_INPUTS} inputs onto {STDP_SAMPLE_NEURONS} "
-                               f"neurons x {STDP_INDEGREE} in-degree (config 4 scaled for one CPU core)",
-                   "inputs": STDP_SAMPLE_INPUTS, "neurons": STDP_SAMPLE_NEURONS, "indegree": STDP_INDEGREE,
-                   "dt_s": DT} if args.workload == "stdp" else
-                  {"workload": f"CUBA fixed in-degree sample: {CPU_SAMPLE_NEURONS} neurons x {INDEGREE} in-degree "
-                               f"+ Poisson drive (config 2 scaled for one CPU core)",
-                   "neurons": CPU_SAMPLE_NEURONS, "indegree": INDEGREE, "dt_s": DT},
-        "realtime_factor": sim_seconds / total_seconds if total_seconds else None,
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port",
-                         "sample": f"{per_step[0]['ticks']} ticks of the sample network after "
-                                   f"{REFERENCE_TICKS_PER_STEP * warmup} warm-up ticks"},
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * s["seconds"] / max(args.steps, 1), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": WORKLOADS[args.workload]["dtype"], "data": "synthetic",
+        "config": describe(args, world),
+        "realtime_factor": s["ticks"] * DT / s["seconds"] if s["seconds"] else None,
+        "synaptic_events": s["synaptic_events"], "spikes": s["spikes"],
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": 1, "kind": "port", "sample": s["sample"],
+                         "host": s["host"]},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
+
+
+def raster_bytes(eng, populations, t0, t1):
+    """Per population: the window's spikes as little-endian int64 (tick,
+    index) pairs, tick then index order, and the per-tick counts."""
+    import numpy as np
+    out = []
+    for p in populations:
+        ticks, ids = [], []
+        for tick in range(t0, t1):
+            s = eng.spikes(p, tick)
+            if s:
+                ticks.append(np.full(len(s), tick, dtype=np.int64))
+                ids.append(np.asarray(s, dtype=np.int64))
+        if ticks:
+            pairs = np.stack([np.concatenate(ticks), np.concatenate(ids)], axis=1)
+        else:
+            pairs = np.zeros((0, 2), dtype=np.int64)
+        out.append(pairs.astype("<i8"))
+    return out
+
+
+def merge_rasters(per_rank):
+    """Rank 0's merge of every rank's rasters: a list that every rank holds
+    whole is taken once; rank-local blocks (disjoint, in rank order) are
+    merged by (tick, index)."""
+    import numpy as np
+    merged = []
+    for p in range(len(per_rank[0])):
+        lists = [r[p] for r in per_rank]
+        if all(a.shape == lists[0].shape and np.array_equal(a, lists[0]) for a in lists):
+            merged.append(lists[0])
+        else:
+            both = np.concatenate(lists)
+            order = np.lexsort((both[:, 1], both[:, 0]))
+            merged.append(both[order])
+    return merged
 
 
 def main():
@@ -207,11 +338,16 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--neurons", type=int, default=N_NEURONS)
-    ap.add_argument("--indegree", type=int, default=INDEGREE)
+    ap.add_argument("--workload", default="c2", choices=sorted(WORKLOADS))
+    ap.add_argument("--neurons", type=int, default=None)
+    ap.add_argument("--indegree", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--workload", default="c2", choices=["c2", "stdp"])
     args = ap.parse_args()
+    w = WORKLOADS[args.workload]
+    if args.neurons is None:
+        args.neurons = w["neurons"]
+    if args.indegree is None:
+        args.indegree = w["indegree"]
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -220,6 +356,7 @@ def main():
         return
     assert args.warmup >= 3, "at least 3 warm-up steps"
     pkg = importlib.import_module("brian2-atlas_b200")
+    import numpy as np
     import torch  # plumbing: process group, barriers, an L2 flush buffer
     torch.cuda.set_device(local_rank)
     dist = None
@@ -241,20 +378,26 @@ def main():
         dist.all_reduce(t, op=op)
         return t.tolist()
 
+    def gather(obj):
+        if dist is None:
+            return [obj]
+        out = [None] * world
+        dist.all_gather_object(out, obj)
+        return out
+
     total_ticks = (args.warmup + args.steps) * TICKS_PER_STEP
-    t0 = time.time()
     stdp = args.workload == "stdp"
-    if stdp:
-        model = build_stdp(STDP_INPUTS, STDP_NEURONS, STDP_INDEGREE, total_ticks + 400)
-    else:
-        model = build_model(args.neurons, args.indegree, total_ticks + 400)
+    t0 = time.time()
+    model = build_workload(args, total_ticks + 400)
     t_json = time.time() - t0
-    if world > 1:
+    if dist is not None:
         eng = pkg.Engine(model, device=local_rank, rank=rank, world_size=world)
         distributed.connect(eng)
     else:
         eng = pkg.Engine(model, device=local_rank)
     del model
+    n_pops = 2 if stdp else 1
+    state_pop = 1 if stdp else 0
     st0 = eng.stats()
     for _ in range(args.warmup):
         barrier()
@@ -274,10 +417,10 @@ def main():
             s1 = eng.stats()
             barrier()
             # the step's time is the slowest rank's
-            d, w = reduce([s1["device_seconds"] - s0["device_seconds"], w1],
-                          dist.ReduceOp.MAX if dist else None)
+            d, wt = reduce([s1["device_seconds"] - s0["device_seconds"], w1],
+                           dist.ReduceOp.MAX if dist else None)
             dev += d
-            wall += w
+            wall += wt
     after = eng.stats()
     # deliveries and launches of every rank; spikes are global on every rank
     events, launches = reduce([after["synaptic_events"] - before["synaptic_events"],
@@ -288,6 +431,11 @@ def main():
     h2d = (after["h2d_bytes"] - before["h2d_bytes"]) / args.steps
     d2h = (after["d2h_bytes"] - before["d2h_bytes"]) / args.steps
     sim_seconds = args.steps * TICKS_PER_STEP * DT
+    # digests of the timed window (host copies of the drained lists) and of
+    # the membrane state right after it, merged over ranks on rank 0
+    w_lo, w_hi = args.warmup * TICKS_PER_STEP, (args.warmup + args.steps) * TICKS_PER_STEP
+    rasters = gather(raster_bytes(eng, range(n_pops), w_lo, w_hi))
+    v_block = gather(eng.read_state(state_pop, "v"))
     # Per-kernel timing (events around each launch) over 400 further ticks.
     barrier()
     prof = eng.profile(400)
@@ -297,109 +445,112 @@ def main():
     clock_summary = clocks.summary()
     barrier()
     eng.close()
+    clock_all = gather(clock_summary)
     if dist is not None:
-        clock_all = [None] * world
-        dist.all_gather_object(clock_all, clock_summary)
         dist.destroy_process_group()
         if rank != 0:
             return
         clock_summary = dict(clock_all[0], reasons=sorted({r for c in clock_all for r in c["reasons"]}),
                              sm_mhz_min_over_ranks=min((c["sm_mhz"] or 0) for c in clock_all))
-    local_neurons = pkg.partition(STDP_NEURONS if stdp else args.neurons, rank, world)
+    merged = merge_rasters(rasters)
+    raster_sha = hashlib.sha256(b"".join(m.tobytes() for m in merged)).hexdigest()
+    # a replicated population (one that no synapse targets) is whole on
+    # every rank; a partitioned one is the concatenation of the rank blocks
+    full = w["neurons"] * (4 if w["dtype"] == "f32" else 8) if stdp else \
+        args.neurons * (4 if w["dtype"] == "f32" else 8)
+    v_all = v_block[0] if len(v_block[0]) == full else b"".join(v_block)
+    state_sha = hashlib.sha256(v_all).hexdigest()
+    local_neurons = pkg.partition(w["neurons"] if stdp else args.neurons, rank, world)
     local_neurons = local_neurons[1] - local_neurons[0]
     hbm, peak_kind = peaks()
     ticks_prof = 400
+    e_t = prof_events / ticks_prof  # this rank's deliveries per tick
+    f_t = prof_spikes / ticks_prof  # spikes per tick (global list)
     kernels = []
     for k in prof:
-        avg_ms = k["total_ms"] / max(k["launches"], 1)
+        name = k["name"]
         if stdp:
-            # on_pre events per tick on this rank: inputs x 15 Hz x dt x
-            # out-degree, i.e. 15 Hz x dt x local edges (the expectation of
-            # the Poisson drive; the run's own count is within a percent)
-            pre = STDP_RATE_HZ * DT * local_neurons * STDP_INDEGREE
-            if k["name"].endswith("_targets") and os.environ.get("B2GPU_TARGETS_SCAN", "0") != "0":
-                # bitmap scan: the 4 B source id of every local in-edge and
-                # the 8 B row offset of every local target
-                per_launch = 4 * local_neurons * STDP_INDEGREE + 8 * (local_neurons + 1)
-            elif k["name"].endswith("_targets"):
+            # on_pre events per tick on this rank: 15 Hz x dt x local edges
+            pre = w["rate_hz"] * DT * local_neurons * w["indegree"]
+            if name.endswith("_targets") and os.environ.get("B2GPU_TARGETS_SCAN", "0") != "0":
+                per_launch = 4 * local_neurons * w["indegree"] + 8 * (local_neurons + 1)
+            elif name.endswith("_targets"):
                 # bucket scatter per event: 4 B row entry, 4+4 B count
                 # atomic, 8 B bucket offset, 8 B bucket entry
                 per_launch = 28 * pre
-            elif k["name"].endswith("_deliver"):
+            elif name.endswith("_deliver"):
                 # per event: 8 B bucket entry, 4 B edge id, the edge's f64
                 # w, Apre, Apost, lastupdate read and w, Apre, lastupdate
                 # written, the target's f64 ge read and written
                 per_launch = (8 + 4 + 32 + 24 + 16) * pre
             else:
                 per_launch = 0
-        elif "_step" in k["name"]:
+        elif "_step" in name:
             # neuron update + threshold + compaction + reset: read and write
-            # v, ge, gi (f64) and read lastspike (f64) per neuron, 4 B per spike
-            per_launch = local_neurons * (2 * 24 + 8) + 4 * prof_spikes / ticks_prof
-        elif k["name"].endswith("_atomic"):
-            # scatter: 4 B row entry per event, read+write of the f64 target per
-            # event (upper bound of 2*8*U_t), 4 B per fired source
-            per_launch = (4 + 16) * (prof_events / ticks_prof) / 2 + 4 * prof_spikes / ticks_prof
-        elif "poisson_input" in k["name"]:
-            per_launch = local_neurons * 16
+            # the state (S bytes) and read lastspike (8 B) per neuron, 4 B
+            # per spike written to the list
+            per_launch = local_neurons * (2 * w["state_bytes"] + 8) + 4 * f_t
+        elif name.endswith("_atomic"):
+            # constant-addend scatter: 4 B row entry per event; read + write
+            # of each distinct (target, variable) touched, U = N (1 - (1 -
+            # 1/N)^E) per pathway for uniformly drawn targets, the in-degree
+            # split 80/20 between the two pathways; per fired source its
+            # ring entry (4 B) and row bounds (16 B)
+            n = max(local_neurons, 1)
+            u = sum(n * (1.0 - (1.0 - 1.0 / n) ** (share * e_t)) for share in (0.8, 0.2))
+            per_launch = 4 * e_t + 2 * w["target_bytes"] * u + 20 * f_t
         else:
             per_launch = 0
-        kernels.append({"name": k["name"], "avg_us": 1e3 * avg_ms, "launches": k["launches"],
-                        "share": 0.0, "algorithmic_bytes": per_launch,
-                        "achieved_gbs": per_launch / (avg_ms * 1e-3) / 1e9 if avg_ms > 0 else 0.0})
-    total = sum(k["avg_us"] * k["launches"] for k in kernels) or 1.0
+        kernels.append({"name": name, "event_us": 1e3 * k["total_ms"] / max(k["launches"], 1),
+                        "launches": k["launches"], "algorithmic_bytes": per_launch})
+    # A kernel's duration inside the graph-replayed tick: its share of the
+    # event-timed launch sum times the measured device time per tick (the
+    # event-timed launches also hold launch latency and lose the
+    # programmatic-dependent-launch overlap, so their sum exceeds the tick).
+    ms_tick = 1e3 * dev / (args.steps * TICKS_PER_STEP)
+    total = sum(k["event_us"] * k["launches"] for k in kernels) or 1.0
+    per_tick_launches = {k["name"]: k["launches"] / ticks_prof for k in kernels}
     for k in kernels:
-        k["share"] = k["avg_us"] * k["launches"] / total
+        k["share"] = k["event_us"] * k["launches"] / total
+        k["avg_us"] = k["share"] * ms_tick * 1e3 / max(per_tick_launches[k["name"]], 1e-9)
+        k["achieved_gbs"] = k["algorithmic_bytes"] / (k["avg_us"] * 1e-6) / 1e9 if k["avg_us"] > 0 else 0.0
     dominant = max(kernels, key=lambda k: k["share"]) if kernels else None
+    traffic = None
+    if dominant is not None:
+        for (wl, frag, n_gpu), b in TRAFFIC.items():
+            if wl == args.workload and frag in dominant["name"] and n_gpu == world and \
+                    args.neurons == w["neurons"]:
+                traffic = b
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        with tempfile.TemporaryDirectory() as tmp:
-            s = cpu_sample(Path(tmp), CPU_SAMPLE_WARMUP, CPU_SAMPLE_TICKS, args.workload)
-        sample = (f"config 4 scaled to {STDP_SAMPLE_INPUTS} inputs onto {STDP_SAMPLE_NEURONS} neurons (in-degree "
-                  f"{STDP_INDEGREE})" if stdp else
-                  f"config 2 scaled to {CPU_SAMPLE_NEURONS} neurons (in-degree {INDEGREE})")
+        s = cpu_window(args)
         cpu = {"value": s["synaptic_events"] / s["seconds"], "unit": UNIT, "cores": 1, "kind": "port",
-               "sample": f"{s['ticks']} ticks of {sample} after {CPU_SAMPLE_WARMUP} warm-up ticks; oracle/b2ref "
-                         f"single thread; {s['synaptic_events']} events in {s['seconds']:.3f} s"}
-    if stdp:
-        config = {"workload": "config 4: STDP feedforward, 100k Poisson inputs at 15 Hz onto 10k COBA LIF neurons, "
-                              "in-degree 1000 (1e7 plastic synapses, on_pre + on_post)",
-                  "inputs": STDP_INPUTS, "neurons": STDP_NEURONS, "indegree": STDP_INDEGREE,
-                  "synapses": STDP_NEURONS * STDP_INDEGREE, "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
-                  "parallelism": "single GPU" if world == 1 else
-                  f"{world} GPUs: inputs replicated on every rank, targets partitioned, target spikes exchanged "
-                  f"by peer stores over NVLink",
-                  "l2": "256 MiB buffer written between timed steps; the 1e7-edge synapse state (320 MB) exceeds L2"}
-    else:
-        config = {"workload": "config 2: CUBA 1M neurons, fixed in-degree 1000 (1e9 synapses), Poisson 100x10 Hz",
-                  "neurons": args.neurons, "indegree": args.indegree, "synapses": args.neurons * args.indegree,
-                  "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
-                  "parallelism": "single GPU" if world == 1 else
-                  f"{world} GPUs: target-owned partition, spikes exchanged by peer stores over NVLink",
-                  "l2": "256 MiB buffer written between timed steps; per-tick neuron state (56 MB) stays "
-                        "L2-resident within a step"}
+               "sample": s["sample"], "host": s["host"]}
     line = {
         "metric": METRIC, "value": events / dev if dev > 0 else 0.0, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * dev / args.steps,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": w["dtype"],
         "data": "synthetic (seeded; definition layer lowered by the reference frontend)",
-        "config": config,
+        "config": describe(args, world),
         "realtime_factor": sim_seconds / dev if dev > 0 else None,
         "realtime_factor_e2e": sim_seconds / wall if wall > 0 else None,
         "synaptic_events": events, "spikes": spikes,
+        "raster_sha256": raster_sha, "final_state_sha256": state_sha,
+        "digest_window_ticks": [w_lo, w_hi],
         "e2e": {"value": events / wall if wall > 0 else 0.0, "unit": UNIT, "h2d_bytes_per_step": int(h2d),
                 "d2h_bytes_per_step": int(d2h)},
         "gpu_launches": launches,
         "roofline": None if dominant is None else {
             "bound": "hbm", "kernel": dominant["name"], "achieved": dominant["achieved_gbs"], "peak": hbm,
-            "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["achieved_gbs"] / hbm,
-            "traffic": STEP_DRAM_BYTES.get(local_neurons) if "_step" in dominant["name"] and world == 1 and not stdp
-            else None},
+            "peak_kind": peak_kind, "unit": "GB/s", "frac": dominant["achieved_gbs"] / hbm, "traffic": traffic,
+            "kernel_us": dominant["avg_us"], "algorithmic_bytes": dominant["algorithmic_bytes"],
+            "timing": "kernel share of the event-timed launches x graph-replayed device time per tick"},
         "kernels": kernels,
         "clocks": clock_summary,
         "build": {"json_seconds": t_json, "engine_build_seconds": st0["build_seconds"],
                   "nvrtc_seconds": st0["compile_seconds"]},
         "cpu_baseline": cpu,
+        "host": host_facts(),
     }
     print(json.dumps(line), flush=True)
 

@@ -23,6 +23,7 @@
 #include <map>
 #include <optional>
 #include <set>
+#include <thread>
 #include <unordered_set>
 
 #include "rng.hpp"
@@ -943,7 +944,8 @@ struct PopulationRuntime {
 };
 
 struct PathwayQueue {
-  std::vector<size_t> offsets, edges;
+  std::vector<size_t> offsets;
+  std::vector<uint32_t> edges;  // edge ids (edge counts are checked to fit 32 bits)
   std::vector<std::vector<size_t>> queue;
   std::optional<size_t> uniform_delay;
   uint64_t delivered = 0;
@@ -968,7 +970,7 @@ struct SummedRuntime {
 };
 
 struct SynapseRuntime {
-  std::vector<size_t> source, target;
+  std::vector<uint32_t> source, target;  // endpoint indices per edge (counts checked to fit 32 bits)
   std::vector<StateArray> states;
   std::vector<PathwayRuntime> pathways;
   std::vector<SummedRuntime> summed;  // in code-object order
@@ -1115,14 +1117,33 @@ PopulationRuntime population_runtime(const Model& m, size_t index) {
 }
 
 // edge_csr (executor.rs:6168-6183): stable counting sort of edge ids by endpoint.
-void edge_csr(const std::vector<size_t>& indices, size_t count, std::vector<size_t>& offsets,
-              std::vector<size_t>& edges) {
+void edge_csr(const std::vector<uint32_t>& indices, size_t count, std::vector<size_t>& offsets,
+              std::vector<uint32_t>& edges) {
   offsets.assign(count + 1, 0);
-  for (size_t i : indices) offsets[i + 1] += 1;
+  for (uint32_t i : indices) offsets[i + 1] += 1;
   for (size_t i = 0; i < count; ++i) offsets[i + 1] += offsets[i];
   std::vector<size_t> next(offsets.begin(), offsets.end() - 1);
   edges.assign(indices.size(), 0);
-  for (size_t e = 0; e < indices.size(); ++e) edges[next[indices[e]]++] = e;
+  for (size_t e = 0; e < indices.size(); ++e) edges[next[indices[e]]++] = uint32_t(e);
+}
+
+// Worker threads for the one-time topology build (not the timed tick loop,
+// which stays single-threaded like b2-runner): at most the host's hardware
+// threads, one per 4096 targets.
+unsigned build_threads(uint64_t targets) {
+  unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+  return unsigned(std::max<uint64_t>(1, std::min<uint64_t>({uint64_t(hw), 64, targets / 4096 + 1})));
+}
+
+template <class F>
+void parallel_chunks(unsigned n, F f) {
+  if (n == 1) {
+    f(0u);
+    return;
+  }
+  std::vector<std::thread> pool;
+  for (unsigned c = 0; c < n; ++c) pool.emplace_back(f, c);
+  for (auto& t : pool) t.join();
 }
 
 std::vector<double> materialize_initializer(uint64_t edge_count, uint64_t seed, const Initializer& init,
@@ -1155,10 +1176,15 @@ std::vector<double> materialize_initializer(uint64_t edge_count, uint64_t seed, 
 
 // materialize_projection (executor.rs:19-137)
 void materialize_projection(const Model& m, const SynapseDef& def, const SynapseInstance& inst,
-                            std::vector<size_t>& source, std::vector<size_t>& target,
+                            std::vector<uint32_t>& source, std::vector<uint32_t>& target,
                             std::map<std::string, std::vector<double>>& params,
                             std::vector<std::vector<size_t>>& delays) {
   const Topology& t = inst.topology;
+  // 32-bit edge and endpoint storage (the reference keeps usize; the
+  // values are the same while they fit)
+  check(def.source_count <= UINT32_MAX && def.target_count <= UINT32_MAX && t.edge_count <= UINT32_MAX &&
+            inst.source.size() <= UINT32_MAX,
+        "projections beyond 2^32 edges or neurons are outside the oracle's subset");
   switch (t.kind) {
     case Topology::Kind::Explicit:
       source.assign(inst.source.begin(), inst.source.end());
@@ -1197,21 +1223,37 @@ void materialize_projection(const Model& m, const SynapseDef& def, const Synapse
       uint64_t S = def.source_count, T = def.target_count, K = t.indegree;
       check(S && T && K && K <= S && T * K <= UINT32_MAX, "invalid fixed-indegree topology specification");
       check(T * K == t.edge_count, "fixed-indegree edge count mismatch");
-      std::vector<uint32_t> counts(S, 0);
-      std::unordered_set<uint64_t> selected;
-      selected.reserve(K * 2);
-      for (uint64_t tg = 0; tg < T; ++tg)
-        fixed_indegree_sources(S, K, tg, t.seed, selected, [&](uint64_t s) { counts[s]++; });
-      std::vector<uint64_t> cursor(S, 0);
-      for (uint64_t s = 1; s < S; ++s) cursor[s] = cursor[s - 1] + counts[s - 1];
+      // Stable counting sort of the target-major draws by source, as the
+      // serial two passes would do it, split over target ranges: chunk c's
+      // edges of source s start after the earlier chunks' edges of s.
+      const unsigned nth = build_threads(T);
+      std::vector<std::vector<uint32_t>> cursor(nth, std::vector<uint32_t>(S, 0));
+      auto targets_of = [&](unsigned c) { return std::make_pair(T * c / nth, T * (c + 1) / nth); };
+      parallel_chunks(nth, [&](unsigned c) {
+        FloydSet selected(K);
+        auto [a, b] = targets_of(c);
+        for (uint64_t tg = a; tg < b; ++tg)
+          fixed_indegree_sources(S, K, tg, t.seed, selected, [&](uint64_t s) { cursor[c][s]++; });
+      });
+      uint64_t acc = 0;
+      for (uint64_t s = 0; s < S; ++s)
+        for (unsigned c = 0; c < nth; ++c) {
+          const uint32_t n = cursor[c][s];
+          cursor[c][s] = uint32_t(acc);
+          acc += n;
+        }
       source.assign(T * K, 0);
       target.assign(T * K, 0);
-      for (uint64_t tg = 0; tg < T; ++tg)
-        fixed_indegree_sources(S, K, tg, t.seed, selected, [&](uint64_t s) {
-          uint64_t pos = cursor[s]++;
-          source[pos] = s;
-          target[pos] = tg;
-        });
+      parallel_chunks(nth, [&](unsigned c) {
+        FloydSet selected(K);
+        auto [a, b] = targets_of(c);
+        for (uint64_t tg = a; tg < b; ++tg)
+          fixed_indegree_sources(S, K, tg, t.seed, selected, [&](uint64_t s) {
+            uint64_t pos = cursor[c][s]++;
+            source[pos] = uint32_t(s);
+            target[pos] = uint32_t(tg);
+          });
+      });
       break;
     }
   }

@@ -6,6 +6,7 @@
 //   topology hashes ........ brian2-rust/src/large_topology.rs:55-142, 189-260
 #pragma once
 
+#include <algorithm>
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
@@ -165,11 +166,12 @@ inline double topo_normal(uint64_t seed, uint64_t stream, uint64_t edge, uint64_
   return std::sqrt(-2.0 * std::log(u1)) * std::cos(6.283185307179586 * u2);
 }
 
-// Floyd subset sampling for one target (large_topology.rs:189-208).
-template <class Visit>
+// Floyd subset sampling for one target (large_topology.rs:189-208).  `selected`
+// is any set of u64 with clear/count/insert (the reference uses a HashSet; the
+// set's kind changes nothing but speed).
+template <class Set, class Visit>
 inline void fixed_indegree_sources(uint64_t source_count, uint64_t indegree, uint64_t target,
-                                   uint64_t seed, std::unordered_set<uint64_t>& selected,
-                                   Visit visit) {
+                                   uint64_t seed, Set& selected, Visit visit) {
   selected.clear();
   for (uint64_t candidate = source_count - indegree; candidate < source_count; ++candidate) {
     uint64_t logical = target * source_count + candidate;
@@ -179,5 +181,48 @@ inline void fixed_indegree_sources(uint64_t source_count, uint64_t indegree, uin
     visit(source);
   }
 }
+
+// Open-addressing set of at most `capacity` u64 keys for the Floyd sampler:
+// cleared in O(1) by bumping a generation stamp (a target's selection never
+// outlives the target).
+class FloydSet {
+ public:
+  explicit FloydSet(uint64_t capacity) {
+    uint64_t n = 16;
+    while (n < 2 * capacity) n <<= 1;
+    keys_.assign(n, 0);
+    stamp_.assign(n, 0);
+    mask_ = n - 1;
+  }
+  void clear() {
+    if (++gen_ == 0) {
+      std::fill(stamp_.begin(), stamp_.end(), 0u);
+      gen_ = 1;
+    }
+  }
+  size_t count(uint64_t k) const {
+    for (uint64_t h = slot(k);; h = (h + 1) & mask_) {
+      if (stamp_[h] != gen_) return 0;
+      if (keys_[h] == k) return 1;
+    }
+  }
+  void insert(uint64_t k) {
+    for (uint64_t h = slot(k);; h = (h + 1) & mask_) {
+      if (stamp_[h] != gen_) {
+        stamp_[h] = gen_;
+        keys_[h] = k;
+        return;
+      }
+      if (keys_[h] == k) return;
+    }
+  }
+
+ private:
+  uint64_t slot(uint64_t k) const { return (k * 0x9e3779b97f4a7c15ull >> 17) & mask_; }
+  std::vector<uint64_t> keys_;
+  std::vector<uint32_t> stamp_;
+  uint64_t mask_ = 0;
+  uint32_t gen_ = 1;
+};
 
 }  // namespace oracle

@@ -256,15 +256,157 @@ def timed_input(reference: Path, n: int = 100, ticks: int = 1000, seed: int = 9)
     return model
 
 
+COBAHH_STATES = ["v", "m", "n", "h", "ge", "gi"]
+
+
+def cobahh_network(n: int, p: float, seed: int, trace: bool = False):
+    """The COBAHH network (examples/COBAHH.py at n neurons, connection
+    probability p): exponential Euler with exprel/exp rate functions,
+    threshold without reset, 3 ms refractory.  trace: a StateMonitor on every
+    state of every neuron.  Returns (network, group, spike monitor, state
+    monitor or None, namespace)."""
+    import numpy as np
+    import brian2 as b
+    b.start_scope()
+    area = 20000 * b.umetre ** 2
+    Cm = (1 * b.ufarad * b.cm ** -2) * area
+    gl = (5e-5 * b.siemens * b.cm ** -2) * area
+    El, EK, ENa = -60 * b.mV, -90 * b.mV, 50 * b.mV
+    g_na = (100 * b.msiemens * b.cm ** -2) * area
+    g_kd = (30 * b.msiemens * b.cm ** -2) * area
+    VT, taue, taui, Ee, Ei = -63 * b.mV, 5 * b.ms, 10 * b.ms, 0 * b.mV, -80 * b.mV
+    we, wi = 6 * b.nS, 67 * b.nS
+    eqs = b.Equations("""
+    dv/dt = (gl*(El-v)+ge*(Ee-v)+gi*(Ei-v)-g_na*(m*m*m)*h*(v-ENa)-g_kd*(n*n*n*n)*(v-EK))/Cm : volt
+    dm/dt = alpha_m*(1-m)-beta_m*m : 1
+    dn/dt = alpha_n*(1-n)-beta_n*n : 1
+    dh/dt = alpha_h*(1-h)-beta_h*h : 1
+    dge/dt = -ge*(1./taue) : siemens
+    dgi/dt = -gi*(1./taui) : siemens
+    alpha_m = 0.32*(mV**-1)*4*mV/exprel((13*mV-v+VT)/(4*mV))/ms : Hz
+    beta_m = 0.28*(mV**-1)*5*mV/exprel((v-VT-40*mV)/(5*mV))/ms : Hz
+    alpha_h = 0.128*exp((17*mV-v+VT)/(18*mV))/ms : Hz
+    beta_h = 4./(1+exp((40*mV-v+VT)/(5*mV)))/ms : Hz
+    alpha_n = 0.032*(mV**-1)*5*mV/exprel((15*mV-v+VT)/(5*mV))/ms : Hz
+    beta_n = .5*exp((10*mV-v+VT)/(40*mV))/ms : Hz
+    """)
+    clock = b.Clock(dt=0.1 * b.ms, name="clock")
+    P = b.NeuronGroup(n, model=eqs, threshold="v>-20*mV", refractory=3 * b.ms, method="exponential_euler",
+                      name="neurons", clock=clock)
+    ne = int(n * 0.8)
+    Ce = b.Synapses(P[:ne], P, on_pre="ge+=we", name="exc", clock=clock)
+    Ci = b.Synapses(P[ne:], P, on_pre="gi+=wi", name="inh", clock=clock)
+    rng = np.random.default_rng(seed)
+    mask = rng.random((n, n)) < p
+    src, tgt = np.nonzero(mask)
+    e = src < ne
+    Ce.connect(i=src[e], j=tgt[e])
+    Ci.connect(i=src[~e] - ne, j=tgt[~e])
+    P.v = El + rng.normal(0, 5, n) * b.mV
+    P.ge = (rng.normal(0, 1.5, n) + 4) * 10 * b.nS
+    P.gi = (rng.normal(0, 12, n) + 20) * 10 * b.nS
+    spikes = b.SpikeMonitor(P, name="spikes")
+    mon = b.StateMonitor(P, COBAHH_STATES, record=True, name="trace", clock=clock) if trace else None
+    net = b.Network(P, Ce, Ci, spikes, *([mon] if mon is not None else []))
+    ns = dict(area=area, Cm=Cm, gl=gl, El=El, EK=EK, ENa=ENa, g_na=g_na, g_kd=g_kd, VT=VT, taue=taue,
+              taui=taui, Ee=Ee, Ei=Ei, we=we, wi=wi)
+    return net, P, spikes, mon, ns
+
+
+def stdp_network(n_in: int, n_out: int, indegree: int, seed: int, trace: bool = False):
+    """The Song-Abbott STDP feedforward network (examples/synapses/STDP.py
+    scaled): Poisson inputs at 15 Hz, conductance LIF targets (Euler),
+    plastic weights with event-driven pre/post traces.  trace: a
+    StateMonitor on v and ge of every target.  Returns (network, namespace)."""
+    import numpy as np
+    import brian2 as b
+    b.start_scope()
+    taum, taupre, taupost = 10 * b.ms, 20 * b.ms, 20 * b.ms
+    Ee, vt, vr, El, taue = 0 * b.mV, -54 * b.mV, -60 * b.mV, -74 * b.mV, 5 * b.ms
+    gmax, dApre = 0.01, 0.01
+    dApost = -dApre * taupre / taupost * 1.05
+    dApost *= gmax
+    dApre *= gmax
+    clock = b.Clock(dt=0.1 * b.ms, name="clock")
+    inputs = b.PoissonGroup(n_in, rates=15 * b.Hz, name="inputs", clock=clock)
+    neurons = b.NeuronGroup(n_out, "dv/dt = (ge * (Ee-v) + El - v) / taum : volt\ndge/dt = -ge / taue : 1",
+                            threshold="v>vt", reset="v = vr", method="euler", name="neurons", clock=clock)
+    neurons.v = vr
+    S = b.Synapses(inputs, neurons,
+                   """w : 1
+                      dApre/dt = -Apre / taupre : 1 (event-driven)
+                      dApost/dt = -Apost / taupost : 1 (event-driven)""",
+                   on_pre="ge += w\nApre += dApre\nw = clip(w + Apost, 0, gmax)",
+                   on_post="Apost += dApost\nw = clip(w + Apre, 0, gmax)", name="stdp", clock=clock)
+    rng = np.random.default_rng(seed)
+    src = np.concatenate([rng.choice(n_in, indegree, replace=False) for _ in range(n_out)])
+    tgt = np.repeat(np.arange(n_out), indegree)
+    S.connect(i=src, j=tgt)
+    S.w = rng.random(len(src)) * gmax
+    spikes = b.SpikeMonitor(neurons, name="spikes")
+    extra = [b.StateMonitor(neurons, ["v", "ge"], record=True, name="trace", clock=clock)] if trace else []
+    net = b.Network(inputs, neurons, S, spikes, *extra)
+    ns = dict(taum=taum, taupre=taupre, taupost=taupost, Ee=Ee, vt=vt, vr=vr, El=El, taue=taue, gmax=gmax,
+              dApre=dApre, dApost=dApost)
+    return net, ns
+
+
+def cobahh_trace(reference: Path, n: int = 400, p: float = 0.1, ticks: int = 100, seed: int = 2) -> dict:
+    """cobahh_small's network (same seed) over its first 100 ticks with every
+    state of every neuron recorded every tick."""
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    net, _, _, _, ns = cobahh_network(n, p, seed, trace=True)
+    return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+
+
+def stdp_trace(reference: Path, n_in: int = 1000, n_out: int = 20, indegree: int = 1000, ticks: int = 100,
+               seed: int = 5) -> dict:
+    """stdp_small's network (same seed) over its first 100 ticks with v and ge
+    of every target recorded every tick."""
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    net, ns = stdp_network(n_in, n_out, indegree, seed, trace=True)
+    return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+
+
+def random_draws(reference: Path, n: int = 200, ticks: int = 300, seed: int = 12) -> dict:
+    """Per-tick random draws on the device: an Euler-Maruyama membrane with
+    white noise (Brian's xi, lowered to randn()) and a run_regularly Poisson
+    draw whose rates span both of the reference's branches (Knuth's product
+    below 10, PTRS at 10 and above); both recorded every tick."""
+    import numpy as np
+    import brian2 as b
+    import brian2_rust  # noqa: F401
+    from brian2_rust.export import lower_network
+    b.start_scope()
+    clock = b.Clock(dt=0.1 * b.ms, name="clock")
+    G = b.NeuronGroup(n, "dv/dt = (mu - v) / tau + sigma * xi * tau**-0.5 : 1", threshold="v > 1", reset="v = 0",
+                      method="euler", name="noisy", clock=clock)
+    G.v = np.linspace(0.0, 0.9, n)
+    D = b.NeuronGroup(n, "lam : 1\nk : 1", name="draws", clock=clock)
+    D.lam = np.linspace(0.5, 60.0, n)
+    D.run_regularly("k = poisson(lam)", dt=0.1 * b.ms, name="draw")
+    spikes = b.SpikeMonitor(G, name="spikes")
+    tv = b.StateMonitor(G, "v", record=True, name="trace_v", clock=clock)
+    tk = b.StateMonitor(D, "k", record=True, name="trace_k", clock=clock)
+    net = b.Network(G, D, spikes, tv, tk)
+    ns = dict(mu=0.8, sigma=0.5, tau=10 * b.ms)
+    return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
-    ap.add_argument("--only", default=None, help="write just this model (cuba_events_small, gap_junctions_small)")
+    ap.add_argument("--only", default=None, help="write just this model (e.g. cobahh_trace_small)")
     args = ap.parse_args()
     if args.only:
         prepare_frontend(Path(args.reference))
         make = {"cuba_events_small": cuba_events, "event_variables_small": event_variables,
-                "gap_junctions_small": gap_junctions,
+                "gap_junctions_small": gap_junctions, "cobahh_trace_small": cobahh_trace,
+                "stdp_trace_small": stdp_trace, "random_draws_small": random_draws,
                 "synapse_updates_small": synapse_updates, "timed_input_small": timed_input}[args.only]
         write_model(make(Path(args.reference)), args.only)
         print("wrote", args.only)
@@ -338,48 +480,7 @@ def main() -> None:
 
     # ---------------------------------------------------------------- COBAHH
     def cobahh(n, p, ticks, seed, numpy_run):
-        b.start_scope()
-        area = 20000 * b.umetre ** 2
-        Cm = (1 * b.ufarad * b.cm ** -2) * area
-        gl = (5e-5 * b.siemens * b.cm ** -2) * area
-        El, EK, ENa = -60 * b.mV, -90 * b.mV, 50 * b.mV
-        g_na = (100 * b.msiemens * b.cm ** -2) * area
-        g_kd = (30 * b.msiemens * b.cm ** -2) * area
-        VT, taue, taui, Ee, Ei = -63 * b.mV, 5 * b.ms, 10 * b.ms, 0 * b.mV, -80 * b.mV
-        we, wi = 6 * b.nS, 67 * b.nS
-        eqs = b.Equations("""
-        dv/dt = (gl*(El-v)+ge*(Ee-v)+gi*(Ei-v)-g_na*(m*m*m)*h*(v-ENa)-g_kd*(n*n*n*n)*(v-EK))/Cm : volt
-        dm/dt = alpha_m*(1-m)-beta_m*m : 1
-        dn/dt = alpha_n*(1-n)-beta_n*n : 1
-        dh/dt = alpha_h*(1-h)-beta_h*h : 1
-        dge/dt = -ge*(1./taue) : siemens
-        dgi/dt = -gi*(1./taui) : siemens
-        alpha_m = 0.32*(mV**-1)*4*mV/exprel((13*mV-v+VT)/(4*mV))/ms : Hz
-        beta_m = 0.28*(mV**-1)*5*mV/exprel((v-VT-40*mV)/(5*mV))/ms : Hz
-        alpha_h = 0.128*exp((17*mV-v+VT)/(18*mV))/ms : Hz
-        beta_h = 4./(1+exp((40*mV-v+VT)/(5*mV)))/ms : Hz
-        alpha_n = 0.032*(mV**-1)*5*mV/exprel((15*mV-v+VT)/(5*mV))/ms : Hz
-        beta_n = .5*exp((10*mV-v+VT)/(40*mV))/ms : Hz
-        """)
-        clock = b.Clock(dt=0.1 * b.ms, name="clock")
-        P = b.NeuronGroup(n, model=eqs, threshold="v>-20*mV", refractory=3 * b.ms, method="exponential_euler",
-                          name="neurons", clock=clock)
-        ne = int(n * 0.8)
-        Ce = b.Synapses(P[:ne], P, on_pre="ge+=we", name="exc", clock=clock)
-        Ci = b.Synapses(P[ne:], P, on_pre="gi+=wi", name="inh", clock=clock)
-        rng = np.random.default_rng(seed)
-        mask = rng.random((n, n)) < p
-        src, tgt = np.nonzero(mask)
-        e = src < ne
-        Ce.connect(i=src[e], j=tgt[e])
-        Ci.connect(i=src[~e] - ne, j=tgt[~e])
-        P.v = El + rng.normal(0, 5, n) * b.mV
-        P.ge = (rng.normal(0, 1.5, n) + 4) * 10 * b.nS
-        P.gi = (rng.normal(0, 12, n) + 20) * 10 * b.nS
-        spikes = b.SpikeMonitor(P, name="spikes")
-        net = b.Network(P, Ce, Ci, spikes)
-        ns = dict(area=area, Cm=Cm, gl=gl, El=El, EK=EK, ENa=ENa, g_na=g_na, g_kd=g_kd, VT=VT, taue=taue,
-                  taui=taui, Ee=Ee, Ei=Ei, we=we, wi=wi)
+        net, P, spikes, _, ns = cobahh_network(n, p, seed)
         model = lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
         if numpy_run:
             net.run(ticks * 0.1 * b.ms, namespace=ns)
@@ -395,33 +496,7 @@ def main() -> None:
 
     # ---------------------------------------------------------------- STDP
     def stdp(n_in, n_out, indegree, ticks, seed):
-        b.start_scope()
-        taum, taupre, taupost = 10 * b.ms, 20 * b.ms, 20 * b.ms
-        Ee, vt, vr, El, taue = 0 * b.mV, -54 * b.mV, -60 * b.mV, -74 * b.mV, 5 * b.ms
-        gmax, dApre = 0.01, 0.01
-        dApost = -dApre * taupre / taupost * 1.05
-        dApost *= gmax
-        dApre *= gmax
-        clock = b.Clock(dt=0.1 * b.ms, name="clock")
-        inputs = b.PoissonGroup(n_in, rates=15 * b.Hz, name="inputs", clock=clock)
-        neurons = b.NeuronGroup(n_out, "dv/dt = (ge * (Ee-v) + El - v) / taum : volt\ndge/dt = -ge / taue : 1",
-                                threshold="v>vt", reset="v = vr", method="euler", name="neurons", clock=clock)
-        neurons.v = vr
-        S = b.Synapses(inputs, neurons,
-                       """w : 1
-                          dApre/dt = -Apre / taupre : 1 (event-driven)
-                          dApost/dt = -Apost / taupost : 1 (event-driven)""",
-                       on_pre="ge += w\nApre += dApre\nw = clip(w + Apost, 0, gmax)",
-                       on_post="Apost += dApost\nw = clip(w + Apre, 0, gmax)", name="stdp", clock=clock)
-        rng = np.random.default_rng(seed)
-        src = np.concatenate([rng.choice(n_in, indegree, replace=False) for _ in range(n_out)])
-        tgt = np.repeat(np.arange(n_out), indegree)
-        S.connect(i=src, j=tgt)
-        S.w = rng.random(len(src)) * gmax
-        spikes = b.SpikeMonitor(neurons, name="spikes")
-        net = b.Network(inputs, neurons, S, spikes)
-        ns = dict(taum=taum, taupre=taupre, taupost=taupost, Ee=Ee, vt=vt, vr=vr, El=El, taue=taue, gmax=gmax,
-                  dApre=dApre, dApost=dApost)
+        net, ns = stdp_network(n_in, n_out, indegree, seed)
         return lower_network(net, ticks * 0.1 * b.ms, namespace=ns, rng_seed=seed)
 
     write_model(stdp(1000, 20, 1000, 2000, 5), "stdp_small")

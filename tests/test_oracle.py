@@ -97,3 +97,34 @@ def test_oracle_synapse_updates_match_brian_numpy(oracle, tmp_path):
     np.testing.assert_allclose(res.populations[1].states["v"], ref["v"], rtol=1e-12, atol=1e-18)
     for name in ("w", "Apre", "Apost"):
         np.testing.assert_allclose(res.synapse_states[0][name], ref[name], rtol=1e-12, atol=1e-18)
+
+
+def test_oracle_random_draws_have_their_distributions(oracle, tmp_path):
+    """The oracle's restated counter streams (executor.rs:209-222 polar
+    normal, :290-336 Knuth below 10 and PTRS from 10) drawn through a model
+    (random_draws_small, lowered by the reference frontend): every neuron's
+    300 Poisson counts have mean lam and variance lam within 5 standard
+    errors (both branches), and the membrane driven by white noise has the
+    Ornstein-Uhlenbeck spread it implies.  The GPU engine must then equal
+    these draws (tests/test_gpu_tolerance.py)."""
+    path = MODELS / "random_draws_small.json"
+    model = load_model(path)
+    r = read_results(run_oracle(oracle, path, tmp_path / "ref"), model)
+    names = [p["name"] for p in model["definition"]["populations"]]
+    k = r.populations[names.index("draws")].samples["k"]  # (ticks, neurons)
+    lam = np.linspace(0.5, 60.0, k.shape[1])
+    assert np.all(k == np.floor(k)) and np.all(k >= 0)
+    mean_err = (k.mean(axis=0) - lam) / np.sqrt(lam / k.shape[0])
+    assert np.max(np.abs(mean_err)) < 5, mean_err
+    var_ratio = k.var(axis=0, ddof=1) / lam
+    assert np.all(np.abs(var_ratio - 1.0) < 5 * np.sqrt(2.0 / (k.shape[0] - 1)) + 0.05)
+    # pooled: the z-scores of the means look standard normal
+    assert abs(mean_err.mean()) < 0.5 and 0.6 < mean_err.std() < 1.4
+    # white noise: v's increments over one tick below threshold have std
+    # sigma * sqrt(dt / tau) (Euler-Maruyama), sigma = 0.5, dt/tau = 0.01
+    v = r.populations[names.index("noisy")].samples["v"]
+    dv = np.diff(v, axis=0)
+    quiet = (v[:-1] > 0.05) & (v[1:] > 0.05) & (v[:-1] < 0.95)
+    drift = (0.8 - v[:-1]) * 0.01
+    noise = (dv - drift)[quiet]
+    assert abs(noise.std() / 0.05 - 1.0) < 0.05 and abs(noise.mean()) < 0.002

@@ -256,6 +256,11 @@ def cpu_window(args):
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
     warm = REFERENCE_TICKS_PER_STEP * args.warmup
     timed = REFERENCE_TICKS_PER_STEP * args.steps
+    if args.workload == "brunel":
+        # nothing is delivered before the 15-tick delay has passed, and a
+        # tick of the full network (17M events) takes seconds on one core:
+        # start after the delay, at most 10 timed ticks
+        warm, timed = WORKLOADS["brunel"]["delay"] + 1 + args.warmup, min(args.steps, 10)
     t0 = time.time()
     with tempfile.TemporaryDirectory() as tmp:
         path = Path(tmp) / "cpu_window.json"
@@ -267,6 +272,8 @@ def cpu_window(args):
     w = WORKLOADS[args.workload]
     network = (f"config 4 scaled to {w['sample_inputs']} inputs onto {w['sample_neurons']} neurons (in-degree "
                f"{w['indegree']})" if args.workload == "stdp" else "the bench's own network (same size and seed)")
+    if args.workload == "brunel":
+        network += ", after the 15-tick delay"
     s["sample"] = (f"ticks {warm}..{warm + timed} of {network}, from tick 0 (the opening transient); "
                    f"oracle/b2ref tick loop on one thread; {s['synaptic_events']} events and {s['spikes']} spikes "
                    f"in {s['seconds']:.3f} s; topology build {s['build_seconds']:.1f} s on every host thread, "
@@ -494,11 +501,13 @@ def main():
             # constant-addend scatter: 4 B row entry per event; read + write
             # of each distinct (target, variable) touched, U = N (1 - (1 -
             # 1/N)^E) per pathway for uniformly drawn targets, the in-degree
-            # split 80/20 between the two pathways; per fired source its
-            # ring entry (4 B) and row bounds (16 B)
+            # split 80/20 between the two pathways (a kernel of one pathway
+            # gets its share); per fired source its ring entry (4 B) and row
+            # bounds (16 B)
             n = max(local_neurons, 1)
-            u = sum(n * (1.0 - (1.0 - 1.0 / n) ** (share * e_t)) for share in (0.8, 0.2))
-            per_launch = 4 * e_t + 2 * w["target_bytes"] * u + 20 * f_t
+            shares = (0.8,) if "excitatory" in name else (0.2,) if "inhibitory" in name else (0.8, 0.2)
+            u = sum(n * (1.0 - (1.0 - 1.0 / n) ** (share * e_t)) for share in shares)
+            per_launch = 4 * sum(shares) * e_t + 2 * w["target_bytes"] * u + 20 * f_t
         else:
             per_launch = 0
         kernels.append({"name": name, "event_us": 1e3 * k["total_ms"] / max(k["launches"], 1),

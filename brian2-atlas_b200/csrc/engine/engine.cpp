@@ -201,6 +201,10 @@ bool conflicts(const NodeEffects& a, const NodeEffects& b) {
 }  // namespace
 
 // ------------------------------------------------------------------ impl
+// Blocks of a stand-alone list-layout kernel (gen_consumer): each reads every
+// tile count of the tick and copies its share of the list into the ring.
+constexpr unsigned kLayoutBlocks = 16;
+
 struct Engine::Impl {
   b2ir::Model m;
   Options opt;
@@ -224,10 +228,11 @@ struct Engine::Impl {
     int ring = -1, tick_start = -1, tile_count = -1, stage = -1, done = -1;
     bool produced = false, ascending = true;
     size_t max_delay = 0;  // deepest consumer delay
-    // multi-GPU: every rank's fired words arrive in the exchange buffer
-    // (offset x_off of each rank's shared allocation; g_ptr slot xptr[q] is
-    // rank q's copy) and an expand kernel of x_tiles blocks turns them into
-    // the tick's ascending global list.
+    // multi-GPU: every rank's ascending list of its block's spikes arrives
+    // in the inbox (offset x_off of each rank's shared allocation; g_ptr slot
+    // xptr[q] is rank q's inbox), two halves of x_half words used on
+    // alternate ticks; a receive kernel (alone or fused with the delay-0
+    // scatter) lays them out as the tick's ascending global list.
     bool exchanged = false;
     // multi-GPU: a partitioned population's list that only its own rank
     // consumes (on_post rows over the rank's targets, resets, results) stays
@@ -236,7 +241,18 @@ struct Engine::Impl {
     bool local = false;
     size_t x_off = 0;
     std::vector<int> xptr;
-    uint64_t x_words = 0, x_tiles = 0, x_wpb = 0;  // exchange words, blocks, words per block
+    // Inbox layout (words per parity half, x_half in all): rank q's tiles
+    // start at word x_base[q]; each of its x_tiles[q] tiles has a count word
+    // and room for x_tile_n[q] ids.  A producing block publishes its tile's
+    // count and ids as soon as it has compacted them.
+    uint64_t x_half = 0;
+    std::vector<uint64_t> x_tiles, x_tile_n, x_base;
+    // The producing step leaves the tick's list as per-tile counts and ids
+    // (tile_count and stage, or the inboxes) and the first kernel that reads
+    // the list lays it out in the ring (gen_consumer): single GPU when a
+    // delay-0 constant-addend scatter directly follows the step, and every
+    // exchanged list.
+    bool consumer_layout = false;
     // fired bitmap ring for target-ordered pathways: slot rel % bm_slots holds
     // the tick's ballot words (bit i = neuron i fired), written by the step
     // kernel that produces the stream
@@ -324,6 +340,12 @@ struct Engine::Impl {
     int tm_cnt = -1, tm_bucket = -1, tm_active = -1, tm_nactive = -1;
     int pend_offsets = -1, pend_items = -1, pend_src = -1, pend_tgt = -1;
     bool has_pending = false;
+    // counted delivery (constant-addend pathways into f32 state): the
+    // scatter adds 1 to the target's event counter (count_ptr, u32 per
+    // target) and the next dense kernel of the target population applies
+    // the pathway's map that many times (StepSpec::applies)
+    bool counted = false;
+    int count_ptr = -1;
   };
   struct SynDev {
     uint64_t edges = 0;        // global edge count (the `N` of synaptic code)
@@ -424,8 +446,12 @@ struct Engine::Impl {
     // Tuning knobs (same results): wave-balanced neuron tiles, and row
     // entries per thread in constant-addend scatters (1..8).
     if (const char* e = std::getenv("B2GPU_BALANCE")) balance_tiles_ = std::atoi(e) != 0;
+    // Diagnostic: deliver constant-addend pathways into f32 state with a
+    // compare-and-swap per event instead of counted delivery (same results).
+    if (const char* e = std::getenv("B2GPU_COUNTED")) counted_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_TILE")) tile_override_ = size_t(std::atoll(e));
+    check(tile_override_ % 32 == 0 && tile_override_ <= size_t(kThreads) * 32, "B2GPU_TILE must be a multiple of 32 up to 8192");
     if (const char* e = std::getenv("B2GPU_SCATTER_UNROLL")) scatter_unroll_ = unsigned(std::atoi(e));
-    if (const char* e = std::getenv("B2GPU_EXCHANGE_WPB")) exchange_wpb_ = unsigned(std::atoi(e));
     if (const char* e = std::getenv("B2GPU_FUSE_EXCHANGE")) fuse_exchange_ = std::atoi(e) != 0;
     // Diagnostic: deliver ordered pathways with one serial thread instead of
     // the target-ordered kernel (same results) for A/B timing.
@@ -450,6 +476,7 @@ struct Engine::Impl {
     check(scatter_unroll_ >= 1 && scatter_unroll_ <= 8, "scatter unroll must be 1 to 8");
   }
   bool no_fuse_ = false;
+  bool counted_ = true;  // counted delivery of constant-addend pathways into f32 state
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
   bool fuse_steps_ = true;   // one launch for consecutive step kernels of different populations
   unsigned targets_unroll_ = 4;  // 32-entry groups each warp of a target-ordered kernel keeps in flight
@@ -457,14 +484,12 @@ struct Engine::Impl {
   bool targets_smem_bitmap_ = true;  // stage the fired bitmap slot in shared memory
   bool targets_scan_ = false;        // scan variant also for single-delay pathways
   bool use_pdl_ = true;
-  bool balance_tiles_ = true;                // tile_n_for: spread neurons over whole waves
-  // Multi-GPU exchange: words per block (0: about eight blocks per SM), and
-  // whether the exchange also delivers the delay-0 scatter of its stream.
-  // Measured on 2/4/8 B200s (C2): 256 words per block with a separate
-  // scatter kernel, 17.6/14.6/14.5 ms per 1000 ticks, against 20.3/17.7/17.6
-  // ms for eight blocks per SM with the scatter fused in.
-  unsigned exchange_wpb_ = kThreads;
-  bool fuse_exchange_ = false;
+  bool balance_tiles_ = true;                // tile_n_for: spread small populations over a whole wave
+  size_t tile_override_ = 0;                 // B2GPU_TILE: neurons per tile (multiple of 32)
+  // Multi-GPU: the receiving kernel of an exchanged stream also delivers the
+  // delay-0 constant-addend scatter that follows it (0: a separate receive
+  // launch, then the scatter reads the ring; same results).
+  bool fuse_exchange_ = true;
   unsigned scatter_unroll_ = kScatterUnroll;  // row entries per thread per scatter work item
   uint64_t row_chunk() const { return uint64_t(kThreads) * scatter_unroll_; }
 
@@ -476,14 +501,18 @@ struct Engine::Impl {
   unsigned sm_count_ = 148;   // multiprocessors of the device (dry runs: a B200's 148)
   // Neurons per block tile of a neuron kernel.  A population that fills at
   // least one wave of resident blocks (SMs x occupancy hint) at kThreads *
-  // npt_ neurons per block keeps that tile (measured: spreading 1M neurons
-  // over two even waves is slower than 1.65 waves of full tiles, because a
-  // block's time is set by its threads' neuron count).  A smaller one (one
-  // GPU's share of a partitioned network) is spread over all resident slots
-  // in whole 32-neuron words, at least one block of threads per tile: e.g.
-  // 125k neurons run as 489 blocks of 256 instead of 123 blocks of 1024.
+  // npt_ neurons per block keeps that tile: measured on config 2 (1M
+  // neurons, ms per 1000 ticks), 977 tiles of 1024 over 592 resident blocks
+  // run in 19.98, against 21.12 for one wave of 590 tiles of 1696 that each
+  // walk 1.66 chunks and 20.48 for the same with 2 neurons per thread (4
+  // chunks).  A smaller population (one GPU's share of a partitioned
+  // network) is spread over all resident slots in whole 32-neuron words, at
+  // least one block of threads per tile: 125k neurons run as 489 blocks of
+  // 256 instead of 123 blocks of 1024.  The step kernel walks a tile in
+  // chunks of kThreads * npt_, so larger tiles (B2GPU_TILE) are valid too.
   size_t tile_n_for(size_t count) const {
     const size_t max_tile = size_t(kThreads) * npt_;
+    if (tile_override_) return tile_override_;
     const size_t slots = size_t(sm_count_) * std::max(1u, min_blocks_);
     if (!balance_tiles_ || count >= max_tile * slots) return max_tile;
     size_t t = (count + slots - 1) / slots;
@@ -1110,14 +1139,6 @@ struct Engine::Impl {
 
   void StreamUse(int s, size_t delay) { streams[size_t(s)].max_delay = std::max(streams[size_t(s)].max_delay, delay); }
 
-  // Words of the exchange bitmap of a population: every rank's block padded
-  // to whole 32-neuron words, blocks in rank order.
-  uint64_t exchange_words(uint64_t count, int upto) const {
-    uint64_t w = 0;
-    for (int q = 0; q < upto; ++q) w += (part_lo(count, q + 1) - part_lo(count, q) + 31) / 32;
-    return w;
-  }
-
   // Header at the start of every rank's shared allocation, checked by each
   // peer in connect(): the GPU's UUID (ranks must sit on distinct GPUs: the
   // exchange waits of one GPU are satisfied by kernels of the others only),
@@ -1158,14 +1179,17 @@ struct Engine::Impl {
         // spike generators emit their (global, precomputed) list on every
         // rank, and replicated populations compute it on every rank
         es.exchanged = true;
-        es.x_words = exchange_words(pd.global_count, world);
-        es.x_wpb = exchange_wpb_ ? std::min<uint64_t>(exchange_wpb_, kThreads)
-                                 : std::clamp<uint64_t>((es.x_words + sm_count_ * 8 - 1) / (sm_count_ * 8), 1, kThreads);
-        es.x_tiles = std::max<uint64_t>(1, (es.x_words + es.x_wpb - 1) / es.x_wpb);
+        es.consumer_layout = true;
+        for (int q = 0; q < world; ++q) {
+          const uint64_t cq = part_lo(pd.global_count, q + 1) - part_lo(pd.global_count, q);
+          es.x_base.push_back(es.x_half);
+          es.x_tiles.push_back(tiles_for(cq));
+          es.x_tile_n.push_back(tile_n_for(cq));
+          es.x_half += es.x_tiles.back() * (1 + es.x_tile_n.back());
+        }
+        check(es.x_tiles[size_t(rank)] == tiles && es.x_tile_n[size_t(rank)] == tile_n, "inbox layout mismatch");
         es.x_off = x_bytes;
-        x_bytes += (2 * es.x_words * 8 + 255) / 256 * 256;
-        tiles = es.x_tiles;
-        tile_n = size_t(es.x_wpb) * 32;
+        x_bytes += (2 * es.x_half * 8 + 255) / 256 * 256;
       }
       es.tile_count = alloc(tiles * 4);
       es.stage = alloc(tiles * tile_n * 4);
@@ -1441,14 +1465,16 @@ struct Engine::Impl {
   // compaction into the event ring), optional reset R on fired lanes.
   std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
                            bool x_is_spike, const Program* R, const std::vector<const Program*>& deferred = {},
-                           bool flush = false, bool as_fn = false) {
-    // One block owns a tile of tile_n consecutive neurons; thread t handles
-    // neurons tile*tile_n + kk*kThreads + t for kk < npt: all loads of the
-    // npt neurons are issued before any arithmetic (memory-level
-    // parallelism), every access is coalesced, and the fired lanes are
-    // counted per (kk, warp) with ballots.  The tile's base in the tick's
-    // ascending spike list comes from a chain-free two-level prefix over the
-    // tiles (ticket order == neuron order).
+                           bool flush = false, bool as_fn = false, const std::vector<PathwayDev*>& applies = {},
+                           const Program* post_R = nullptr) {
+    // One block owns a tile of tile_n consecutive neurons (whole 32-neuron
+    // words) and walks it in chunks of kThreads * npt neurons; in a chunk,
+    // thread t handles neurons chunk_base + kk*kThreads + t for kk < npt: all
+    // loads of the npt neurons are issued before any arithmetic
+    // (memory-level parallelism), every access is coalesced, and the fired
+    // lanes are counted per (chunk, kk, warp) with ballots.  Tiles are sized
+    // so that one wave of resident blocks covers the population with equal
+    // shares (tile_n_for), instead of a last partial wave of full tiles.
     //
     // `deferred` programs are trailing neuron maps of the previous tick (e.g.
     // PoissonInput) that the schedule analysis moved to the start of this
@@ -1458,15 +1484,27 @@ struct Engine::Impl {
     const auto& def = m.populations[p];
     const PopDev& pd = pops[p];
     const unsigned tile_n = unsigned(tile_n_for(pd.count));
-    const unsigned npt = (tile_n + kThreads - 1) / kThreads;  // neuron slots per thread
-    // condition that slot kk of this thread lies inside the tile (only needed
-    // when the tile is not a whole number of blocks of threads)
-    const std::string in_tile = tile_n % kThreads ? "kk * " + std::to_string(kThreads) + "u + threadIdx.x < " +
-                                                        std::to_string(tile_n) + "u && " : "";
+    const unsigned chunk_n = std::min<unsigned>(tile_n, kThreads * npt_);
+    const unsigned chunks = (tile_n + chunk_n - 1) / chunk_n;
+    const unsigned npt = (chunk_n + kThreads - 1) / kThreads;  // neuron slots per thread and chunk
+    constexpr unsigned W = kThreads / 32;
+    const unsigned words = tile_n / 32;  // ballot words per tile
+    check(tile_n % 32 == 0 && chunks * npt <= 32 && words <= kThreads, "neuron tile layout out of range");
+    // offset of slot kk of this thread inside the tile, and whether it lies
+    // inside the tile (only needed when the tile is not a whole number of
+    // chunks of kThreads)
+    const std::string slot_off = "ch * " + std::to_string(chunk_n) + "u + kk * " + std::to_string(kThreads) + "u";
+    const bool ragged = tile_n % kThreads != 0 || tile_n % chunk_n != 0;
+    const std::string in_tile = ragged ? slot_off + " + threadIdx.x < " + std::to_string(tile_n) + "u && " : "";
     std::vector<const Program*> progs(deferred.begin(), deferred.end());
-    for (const Program* pr : {U, X, R})
+    for (const Program* pr : {U, X, R, post_R})
       if (pr) progs.push_back(pr);
     std::set<size_t> used = slots_used(progs), written = slots_written(progs);
+    for (const PathwayDev* pw : applies)
+      for (const auto& ad : pw->atomic_adds) {
+        used.insert(ad.state);
+        written.insert(ad.state);
+      }
     bool refr = pd.lastspike >= 0;
     bool touch_refr = refr && (X || (U && pd.fixed_refractory && !flush) || writes_available(progs));
     bool read_refr = refr;
@@ -1482,12 +1520,11 @@ struct Engine::Impl {
     const EventStreamDev* es = X ? &streams[size_t(pd.stream_of_event[x_event])] : nullptr;
     const bool exchange = es && es->exchanged;
     size_t tiles = tiles_for(pd.count);
-    constexpr unsigned W = kThreads / 32;
     if (!as_fn) o << "  const u32 tile = blockIdx.x;\n";
-    if (X && !exchange) {
-      o << "  __shared__ u32 s_ballot[" << npt * W << "];\n  __shared__ u32 s_off[" << npt * W + 1 << "];\n";
-      o << "  __shared__ u32 s_last;\n";
-      o << "  u32 fired_bits = 0;\n";
+    if (X) {
+      o << "  __shared__ u32 s_ballot[" << words << "];\n  __shared__ u32 s_off[" << words << "];\n";
+      if (!es->consumer_layout) o << "  __shared__ u32 s_last;\n";
+      o << "  u32 fired_bits = 0;  // bit ch * " << npt << " + kk: this thread's slot fired\n";
     }
     o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
     if (!deferred.empty()) {
@@ -1495,6 +1532,7 @@ struct Engine::Impl {
       o << "  const u64 tick_prev = tick - 1;\n  const double t_prev = (double)tick_prev * " << double_literal(dt) << ";\n";
       o << "  (void)t_prev;\n";
     }
+    o << "#pragma unroll 1\n  for (u32 ch = 0; ch < " << chunks << "u; ++ch) {\n";
     // ---- load phase
     auto ld = [&](int ptr, const char* ct) { return "__ldg(" + P(ptr, ct) + " + i)"; };
     for (size_t s : used) {
@@ -1502,9 +1540,12 @@ struct Engine::Impl {
       o << "  " << ct << " sva" << s << "[" << npt << "];\n";
     }
     if (read_refr) o << "  double lsa[" << npt << "];\n  u8 nra[" << npt << "];\n";
+    for (size_t a = 0; a < applies.size(); ++a) o << "  u32 cna" << a << "[" << npt << "];\n";
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
-    o << "    const u32 i = tile * " << tile_n << "u + kk * " << kThreads << "u + threadIdx.x;\n";
+    o << "    const u32 i = tile * " << tile_n << "u + " << slot_off << " + threadIdx.x;\n";
     o << "    if (" << in_tile << "i < " << pd.count << "u) {\n";
+    for (size_t a = 0; a < applies.size(); ++a)
+      o << "      cna" << a << "[kk] = __ldcg(" << P(applies[a]->count_ptr, "const u32") << " + i);\n";
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "      sva" << s << "[kk] = " << ld(pops[p].states[s].ptr, ct) << ";\n";
@@ -1518,7 +1559,7 @@ struct Engine::Impl {
     prev_ctx.tick = "tick_prev";
     prev_ctx.time = "t_prev";
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
-    o << "  const u32 i = tile * " << tile_n << "u + kk * " << kThreads << "u + threadIdx.x;\n";
+    o << "  const u32 i = tile * " << tile_n << "u + " << slot_off << " + threadIdx.x;\n";
     o << "  const bool active = " << in_tile << "i < " << pd.count << "u;\n";
     o << "  bool fired = false;\n  (void)fired;\n";
     o << "  if (active) {\n";
@@ -1527,6 +1568,27 @@ struct Engine::Impl {
     for (size_t d = 0; d < deferred.size(); ++d) {
       std::string pre = "d" + std::to_string(d) + "_";
       o << "  if (run_deferred) {\n" << emit_program(*deferred[d], prev_ctx, pre) << commits(*deferred[d], p, pre) << "  }\n";
+    }
+    // counted deliveries of this tick (in schedule order): the pathway's map
+    // applied as often as events reached this neuron, each result rounded to
+    // the storage type and checked finite like one delivery of the
+    // reference's (executor.rs:2166-2251 per event); the gate is the target's
+    // not_refractory as stored by this tick's threshold
+    for (size_t a = 0; a < applies.size(); ++a) {
+      const PathwayDev* pw = applies[a];
+      o << "  { const u32 n_ev = cna" << a << "[kk];\n";
+      o << "    if (n_ev) {\n      " << P(pw->count_ptr, "u32") << "[i] = 0u;\n";
+      o << "      for (u32 r = 0; r < n_ev; ++r) {\n";
+      for (const auto& ad : pw->atomic_adds) {
+        const std::string v = "sv" + std::to_string(ad.state);
+        o << "        " << (ad.gated ? "if (nr) { " : "{ ");
+        if (def.states[ad.state].dtype == DType::F64)
+          o << v << " = " << v << " + " << double_literal(ad.addend) << ";";
+        else
+          o << v << " = (float)((double)" << v << " + " << double_literal(ad.addend) << ");";
+        o << " if (!b2_finite((double)" << v << ")) err |= " << kErrNonfinite << "u; }\n";
+      }
+      o << "      }\n    }\n  }\n";
     }
     if (U) {
       if (refr && pd.fixed_refractory && !flush) {
@@ -1551,6 +1613,10 @@ struct Engine::Impl {
       if (x_is_spike && refr) o << "  if (fired) { ls = t; nr = 0; }\n";
     }
     if (R) o << "  if (fired) {\n" << emit_program(*R, ctx, "r_") << commits(*R, p, "r_") << "  }\n";
+    if (post_R) {
+      check(read_refr, "trailing reset without lastspike");
+      o << "  if (ls == t) {\n" << emit_program(*post_R, ctx, "pr_") << commits(*post_R, p, "pr_") << "  }\n";
+    }
     for (size_t s : written) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "  " << P(pops[p].states[s].ptr, ct) << "[i] = sv" << s << ";\n";
@@ -1560,144 +1626,231 @@ struct Engine::Impl {
       o << "  " << P(pd.not_refractory, "u8") << "[i] = nr;\n";
     }
     o << "  }\n";  // active
-    if (X && exchange) {
-      // The warp's ballot is word tile*tile_n/32 + kk*W + warp of this rank's
-      // block; lanes 0..world-1 store it, tagged with the tick, into every
-      // rank's exchange buffer (this rank's included).
-      const uint64_t local_words = (pd.count + 31) / 32;
+    if (X) {
+      // ballot word ch * npt * W + kk * W + warp of the tile covers its
+      // neurons 32 * (that word) .. + 31 (chunks are whole words)
+      const std::string word = "ch * " + std::to_string(npt * W) + "u + kk * " + std::to_string(W) + "u + warp";
+      const std::string warp_in_tile =
+          ragged ? slot_off + " + warp * 32u < " + std::to_string(tile_n) + "u" : std::string("true");
       o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
-      o << "  const u32 xw = tile * " << tile_n / 32 << "u + kk * " << W << "u + warp;\n";
-      std::string warp_in_tile = tile_n % kThreads ? "kk * " + std::to_string(kThreads) + "u + warp * 32u < " +
-                                                         std::to_string(tile_n) + "u && " : "";
-      o << "  if (" << warp_in_tile << "lane < " << world << "u && xw < " << local_words << "u)\n";
-      o << "    b2_ll_store(((u64*)g_ptr[" << es->xptr[0] << " + lane]) + (rel & 1ull) * " << es->x_words << "ull + "
-        << exchange_words(pd.global_count, rank) << "ull + xw, b, (u32)(rel + 1ull));\n";
-    } else if (X) {
-      o << "  const u32 b = __ballot_sync(0xffffffffu, fired);\n";
-      o << "  if (lane == 0) s_ballot[kk * " << W << "u + warp] = b;\n";
+      o << "  if (lane == 0 && " << warp_in_tile << ") s_ballot[" << word << "] = b;\n";
       if (es->bitmap >= 0) {
         // fired bitmap for target-ordered pathways: word w covers neurons
         // 32w .. 32w + 31 (tile_n is a multiple of 32)
-        std::string warp_in_tile = tile_n % kThreads ? "kk * " + std::to_string(kThreads) + "u + warp * 32u < " +
-                                                           std::to_string(tile_n) + "u && " : "";
-        o << "  { const u32 bw = tile * " << tile_n / 32 << "u + kk * " << W << "u + warp;\n";
-        o << "    if (lane == 0 && " << warp_in_tile << "bw < " << es->bm_words << "u) " << P(es->bitmap, "u32")
+        o << "  { const u32 bw = tile * " << words << "u + " << word << ";\n";
+        o << "    if (lane == 0 && " << warp_in_tile << " && bw < " << es->bm_words << "u) " << P(es->bitmap, "u32")
           << "[(rel % " << es->bm_slots << "ull) * " << es->bm_words << "ull + bw] = b; }\n";
       }
-      o << "  fired_bits |= (fired ? 1u : 0u) << kk;\n";
+      o << "  fired_bits |= (fired ? 1u : 0u) << (ch * " << npt << "u + kk);\n";
     }
     o << "  }\n";  // kk loop
+    o << "  }\n";  // chunk loop
     if (flush) o << "  if (blockIdx.x == 0 && threadIdx.x == 0) " << P(deferred_flags, "u64") << "[" << p << "] = tick;\n";
-    if (X && !exchange) {
-      // Tile-local ascending compaction into the staging area, then the
-      // last block to finish lays all tiles out (b2_finalize_spikes).
+    if (X) {
+      // Tile-local ascending compaction (warp 0 scans the tile's ballot
+      // words, per lane a contiguous run of them).  Then one of:
+      //  * exchanged list: the tile's count and ids go straight to every
+      //    rank's inbox (tagged 8-byte peer stores), no wait on other blocks;
+      //  * list laid out by its consumer: the tile's count and ids stay in
+      //    tile_count / stage for the next kernel;
+      //  * otherwise the last block to finish lays all tiles out in the ring
+      //    (b2_finalize_spikes).
+      const unsigned per = (words + 31) / 32;
+      const std::string gid =
+          ((es->local || exchange) && pd.lo ? std::to_string(pd.lo) + "u + " : std::string()) + "tile * " +
+          std::to_string(tile_n) + "u + " + slot_off + " + threadIdx.x";
+      auto peer = [&](const std::string& q) {
+        return "(((u64*)g_ptr[" + std::to_string(es->xptr[0]) + " + " + q + "]) + (rel & 1ull) * " +
+               std::to_string(es->x_half) + "ull + " + std::to_string(exchange ? es->x_base[size_t(rank)] : 0) +
+               "ull + (u64)tile * " + std::to_string(tile_n + 1) + "ull)";
+      };
       o << "  __syncthreads();\n";
       o << "  if (warp == 0) {\n";
-      o << "    u32 c = lane < " << npt * W << "u ? __popc(s_ballot[lane]) : 0u;\n";
+      o << "    u32 c = 0;\n";
+      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 w = lane * " << per
+        << "u + j; if (w < " << words << "u) c += __popc(s_ballot[w]); }\n";
       o << "    u32 x = c;\n";
       o << "#pragma unroll\n    for (int d = 1; d < 32; d <<= 1) { u32 y = __shfl_up_sync(0xffffffffu, x, d); if (lane >= (u32)d) x += y; }\n";
-      o << "    if (lane < " << npt * W << "u) s_off[lane] = x - c;\n";
-      o << "    if (lane == 31) " << P(es->tile_count, "u32") << "[tile] = x;\n";
+      o << "    u32 acc = x - c;\n";
+      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 w = lane * " << per
+        << "u + j; if (w < " << words << "u) { s_off[w] = acc; acc += __popc(s_ballot[w]); } }\n";
+      if (exchange)
+        o << "    if (lane == 31) for (u32 q = 0; q < " << world << "u; ++q) b2_ll_store(" << peer("q")
+          << ", x, (u32)(rel + 1ull));\n";
+      else
+        o << "    if (lane == 31) " << P(es->tile_count, "u32") << "[tile] = x;\n";
       o << "  }\n";
       o << "  __syncthreads();\n";
-      o << "  if (fired_bits) {\n    u32* stage = " << P(es->stage, "u32") << " + (u64)tile * " << tile_n << "u;\n";
-      o << "#pragma unroll\n    for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
-      o << "      if ((fired_bits >> kk) & 1u) {\n";
-      o << "        const u32 slot = kk * " << W << "u + warp;\n";
-      // global ids (a local multi-GPU list covers the block [lo, lo + count))
-      o << "        stage[s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u))] = "
-        << (es->local && pd.lo ? std::to_string(pd.lo) + "u + " : std::string()) << "tile * " << tile_n
-        << "u + kk * " << kThreads << "u + threadIdx.x;\n";
-      o << "      }\n    }\n  }\n";
-      o << "  __threadfence();\n  __syncthreads();\n";
-      o << "  if (threadIdx.x == 0) s_last = (atomicAdd((unsigned long long*)" << P(es->done, "u64") << ", 1ull) % "
-        << tiles << "ull) == " << tiles - 1 << "ull;\n";
-      o << "  __syncthreads();\n";
-      o << "  if (s_last) {\n    __threadfence();\n";
-      o << "    b2_finalize_spikes<" << kThreads << ">(" << tiles << "u, " << tile_n << "u, " << P(es->tile_count, "const u32")
-        << ", " << P(es->stage, "const u32") << ", " << P(es->ring, "u32") << ", " << u64lit(es->mask) << ", "
-        << P(es->tick_start, "u64") << ", rel, " << u64lit(es->cap) << ", " << floor_of(size_t(pd.stream_of_event[x_event]))
-        << ", err);\n  }\n";
+      o << "  if (fired_bits) {\n";
+      if (!exchange) o << "    u32* stage = " << P(es->stage, "u32") << " + (u64)tile * " << tile_n << "u;\n";
+      o << "    for (u32 f = fired_bits; f; f &= f - 1u) {\n";
+      o << "      const u32 bit = (u32)(__ffs(f) - 1), ch = bit / " << npt << "u, kk = bit % " << npt << "u;\n";
+      o << "      const u32 slot = ch * " << npt * W << "u + kk * " << W << "u + warp;\n";
+      o << "      const u32 pos = s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u));\n";
+      // global ids (a multi-GPU list covers the block [lo, lo + count))
+      if (exchange)
+        o << "      for (u32 q = 0; q < " << world << "u; ++q) b2_ll_store(" << peer("q") << " + 1ull + pos, " << gid
+          << ", (u32)(rel + 1ull));\n";
+      else
+        o << "      stage[pos] = " << gid << ";\n";
+      o << "    }\n  }\n";
+      if (!es->consumer_layout) {
+        // Only the threads that staged ids, and the one that wrote the
+        // tile's count, need their writes visible to the last block: they
+        // fence, the barrier orders the fences before the ticket.
+        o << "  if (fired_bits || (warp == 0 && lane == 31)) __threadfence();\n  __syncthreads();\n";
+        o << "  if (threadIdx.x == 0) s_last = (atomicAdd((unsigned long long*)" << P(es->done, "u64") << ", 1ull) % "
+          << tiles << "ull) == " << tiles - 1 << "ull;\n";
+        o << "  __syncthreads();\n";
+        o << "  if (s_last) {\n    __threadfence();\n";
+        o << "    b2_finalize_spikes<" << kThreads << ">(" << tiles << "u, " << tile_n << "u, " << P(es->tile_count, "const u32")
+          << ", " << P(es->stage, "const u32") << ", " << P(es->ring, "u32") << ", " << u64lit(es->mask) << ", "
+          << P(es->tick_start, "u64") << ", rel, " << u64lit(es->cap) << ", " << floor_of(size_t(pd.stream_of_event[x_event]))
+          << ", err);\n  }\n";
+      }
     }
     o << (as_fn ? std::string("}\n") : kernel_tail());
     return o.str();
   }
 
-  // Multi-GPU expand: wait (bounded) for every rank's tagged words of this
-  // tick, then compact the global bitmap into the tick's ascending global
-  // spike list with the same tile staging + last-block layout as the step
-  // kernel.  Word w belongs to rank q's block when
-  // exchange_words(N, q) <= w < exchange_words(N, q + 1).
-  std::string gen_exchange(const std::string& name, int stream_id, const std::vector<PathwayDev*>& fused = {}) {
+  // Consumer layout of a tick's list (gen_pop_step leaves it as per-tile
+  // counts and ids): pair p = (rank, tile) in rank-then-tile order, which is
+  // ascending neuron order.  No block waits for another:
+  //  * layout blocks (the first `lb` of the grid) each read every pair's
+  //    count (waiting, bounded, for a peer's tagged word where the list is
+  //    exchanged), scan them into the pairs' offsets, so that position g of
+  //    the list lies in the last pair whose offset is <= g, and copy the list
+  //    into the ring (position g -> thread g of the layout blocks); block 0
+  //    writes tick_start[rel + 1].  Rank order is global order, so an
+  //    exchanged list is ascending without a sort (the reference's MPI path
+  //    sorts the gathered ids, mpi_codegen.py:79-82);
+  //  * `fused`: the delay-0 constant-addend pathways of the stream, whose
+  //    result does not depend on the order of events, are delivered by the
+  //    other blocks straight from the tile lists: block b takes pairs b,
+  //    b + blocks, ... (one count read per pair, all of a block's at once),
+  //    and its warps share the block's work items (id, 256-entry row chunk),
+  //    so the scatter needs no ring read, no prefix over all tiles and no
+  //    kernel boundary of its own.
+  std::string gen_consumer(const std::string& name, int stream_id, const std::vector<PathwayDev*>& fused,
+                           unsigned grid, unsigned lb) {
     const EventStreamDev& es = streams[size_t(stream_id)];
     const PopDev& pd = pops[es.pop];
+    const bool remote = es.exchanged;
     const uint64_t timeout_ns = uint64_t(opt.exchange_timeout_ms) * 1000000ull;
-    const unsigned wpb = unsigned(es.x_wpb), tile_n = wpb * 32;
+    uint64_t pairs = 0;
+    std::vector<uint64_t> pair_start;  // remote: first pair of each rank
+    if (remote) {
+      for (int q = 0; q < world; ++q) {
+        pair_start.push_back(pairs);
+        pairs += es.x_tiles[size_t(q)];
+      }
+    } else {
+      pairs = tiles_for(pd.count);
+    }
+    check(pairs <= 8192, "spike list layout: too many tiles");
+    check(lb >= 1 && lb <= grid && (fused.empty() ? lb == grid : grid > lb), "spike list layout: bad grid split");
+    const unsigned per = unsigned((pairs + kThreads - 1) / kThreads);
+    constexpr unsigned W = kThreads / 32;
     std::ostringstream o;
     o << kernel_head(name);
-    o << "  __shared__ u32 s_last;\n";
-    if (!fused.empty()) o << "  __shared__ u32 s_ids[" << tile_n << "];\n";
-    o << "  const u32 tile = blockIdx.x;\n  const u32 w = tile * " << wpb << "u + threadIdx.x;\n";
-    o << "  u32 bits = 0, id0 = 0;\n";
-    // once the run has failed (e.g. an earlier wait expired) later ticks
-    // must not wait again: their results are discarded anyway
-    o << "  const bool poisoned = *(volatile const u32*)&ctl->error != 0u;\n";
-    o << "  if (threadIdx.x < " << wpb << "u && w < " << es.x_words << "u && !poisoned) {\n";
-    o << "    bits = b2_ll_wait(((const u64*)g_ptr[" << es.xptr[size_t(rank)] << "]) + (rel & 1ull) * " << es.x_words
-      << "ull + w, (u32)(rel + 1ull), " << timeout_ns << "ull, err);\n";
-    for (int q = 0; q < world; ++q) {
-      const uint64_t w0 = exchange_words(pd.global_count, q), w1 = exchange_words(pd.global_count, q + 1);
-      o << "    " << (q ? "else if" : "if") << " (w < " << w1 << "u) id0 = " << part_lo(pd.global_count, q) << "u + (w - "
-        << w0 << "u) * 32u;\n";
+    o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
+    if (remote) {
+      // once the run has failed (e.g. an earlier wait expired) later ticks
+      // must not wait again: their results are discarded anyway
+      o << "  const bool poisoned = *(volatile const u32*)&ctl->error != 0u;\n";
+      o << "  const u64* inbox = ((const u64*)g_ptr[" << es.xptr[size_t(rank)] << "]) + (rel & 1ull) * " << es.x_half
+        << "ull;\n";
+      o << "  const u32 tag = (u32)(rel + 1ull);\n";
+      // word of pair p's count in this rank's inbox
+      o << "  auto slot = [](u32 p) -> u64 {\n";
+      for (int q = world - 1; q >= 0; --q)
+        o << "    " << (q ? "if (p >= " + std::to_string(pair_start[size_t(q)]) + "u) " : std::string()) << "return "
+          << es.x_base[size_t(q)] << "ull + (u64)(p - " << pair_start[size_t(q)] << "u) * " << es.x_tile_n[size_t(q)] + 1
+          << "ull;\n";
+      o << "  };\n";
+      o << "  auto count_of = [&](u32 p) -> u32 { return poisoned ? 0u : b2_ll_wait(inbox + slot(p), tag, " << timeout_ns
+        << "ull, err); };\n";
+      o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return poisoned ? 0u : b2_ll_wait(inbox + slot(p) + 1ull + k, tag, "
+        << timeout_ns << "ull, err); };\n";
+    } else {
+      o << "  auto count_of = [&](u32 p) -> u32 { return __ldcg(" << P(es.tile_count, "const u32") << " + p); };\n";
+      o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return __ldcg(" << P(es.stage, "const u32") << " + (u64)p * "
+        << tile_n_for(pd.count) << "u + k); };\n";
     }
+    // ---- layout blocks
+    o << "  if (blockIdx.x < " << lb << "u) {\n";
+    o << "    __shared__ u32 s_pre[" << pairs + 1 << "];\n";
+    o << "    u32 c = 0;\n";
+    o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
+      << "u + j; if (p < " << pairs << "u) c += count_of(p); }\n";
+    o << "    u32 total;\n    u32 off = b2_block_exclusive_scan<" << kThreads << ">(c, &total);\n";
+    o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
+      << "u + j; if (p < " << pairs << "u) { s_pre[p] = off; off += count_of(p); } }\n";
+    o << "    if (threadIdx.x == 0) s_pre[" << pairs << "] = total;\n";
+    o << "    __syncthreads();\n";
+    o << "    const u64 base = " << P(es.tick_start, "const u64") << "[rel];\n";
+    o << "    u32* ring = " << P(es.ring, "u32") << ";\n";
+    // last pair whose offset is <= g (pairs with no ids share the next
+    // pair's offset, so the last one is the pair that holds position g)
+    o << "    for (u32 g = blockIdx.x * " << kThreads << "u + threadIdx.x; g < total; g += " << lb * kThreads << "u) {\n";
+    o << "      u32 lo = 0, hi = " << pairs - 1 << "u;\n";
+    o << "      while (lo < hi) { const u32 mid = (lo + hi + 1u) >> 1; if (s_pre[mid] <= g) lo = mid; else hi = mid - 1u; }\n";
+    o << "      ring[(base + g) & " << u64lit(es.mask) << "] = id_of(lo, g - s_pre[lo]);\n    }\n";
+    o << "    if (blockIdx.x == 0 && threadIdx.x == 0) {\n";
+    o << "      const u64 end = base + total;\n      " << P(es.tick_start, "u64") << "[rel + 1] = end;\n";
+    o << "      if (end - " << floor_of(size_t(stream_id)) << " > " << u64lit(es.cap) << ") err |= " << kErrRing
+      << "u;\n    }\n";
     o << "  }\n";
-    o << "  u32 total;\n  u32 pos = b2_block_exclusive_scan<" << kThreads << ">(__popc(bits), &total);\n";
-    o << "  u32* stage = " << P(es.stage, "u32") << " + (u64)tile * " << tile_n << "u;\n";
-    o << "  for (u32 x = bits; x; x &= x - 1u) {\n    const u32 id = id0 + (u32)(__ffs(x) - 1);\n";
-    if (!fused.empty()) o << "    s_ids[pos] = id;\n";
-    o << "    stage[pos++] = id;\n  }\n";
-    o << "  if (threadIdx.x == 0) " << P(es.tile_count, "u32") << "[tile] = total;\n";
-    o << "  __threadfence();\n  __syncthreads();\n";
-    o << "  if (threadIdx.x == 0) s_last = (atomicAdd((unsigned long long*)" << P(es.done, "u64") << ", 1ull) % "
-      << es.x_tiles << "ull) == " << es.x_tiles - 1 << "ull;\n";
-    o << "  __syncthreads();\n";
     if (!fused.empty()) {
-      // Delay-0 constant-addend pathways of this stream, fused: every block
-      // delivers the rows of the spikes it has just unpacked (delivery order
-      // is free for these pathways), so the scatter needs no ring read and
-      // no kernel boundary of its own.
+      // ---- scatter blocks
+      const unsigned blocks = grid - lb;
+      const unsigned mine = unsigned((pairs + blocks - 1) / blocks);  // pairs per block, at most
+      check(mine <= kThreads, "spike list layout: too many tiles per scatter block");
       const PathwayDev& p0 = *fused.front();
       const size_t endpoint_count = m.populations[p0.endpoint_pop].count;
-      for (size_t k = 0; k < fused.size(); ++k) o << "  u64 events" << k << " = 0;\n";
-      o << "  for (u32 k2 = 0; k2 < total; ++k2) {\n    const u32 s = s_ids[k2];\n";
+      uint64_t chunks = 1;
+      for (const PathwayDev* pw : fused) chunks = std::max<uint64_t>(chunks, (pw->max_row + 255) / 256);
+      o << "  else {\n";
+      o << "    __shared__ u32 s_cnt[" << mine << "];\n";
+      o << "    const u32 b = blockIdx.x - " << lb << "u;\n";
+      o << "    if (threadIdx.x < " << mine << "u) { const u32 p = b + threadIdx.x * " << blocks << "u; s_cnt[threadIdx.x] = p < "
+        << pairs << "u ? count_of(p) : 0u; }\n";
+      o << "    __syncthreads();\n";
+      for (size_t k = 0; k < fused.size(); ++k) o << "    u64 events" << k << " = 0;\n";
+      // the block's items in (pair, id, chunk) order; warp w takes items
+      // w, w + W, ...
+      o << "    u32 item = 0;\n";
+      o << "    for (u32 j = 0; j < " << mine << "u; ++j) {\n";
+      o << "      const u32 n = s_cnt[j], p = b + j * " << blocks << "u;\n";
+      o << "      for (u32 kk = 0; kk < n; ++kk)\n";
+      o << "        for (u32 c = 0; c < " << chunks << "u; ++c, ++item) {\n";
+      o << "          if (item % " << W << "u != warp) continue;\n";
+      o << "          const u32 s = id_of(p, kk);\n";
       for (size_t k = 0; k < fused.size(); ++k) {
         const PathwayDev& pw = *fused[k];
         const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
         const bool full = lo == 0 && hi == endpoint_count;
-        o << "    " << (full ? "{" : "if (s >= " + std::to_string(lo) + "u && s < " + std::to_string(hi) + "u) {") << "\n";
-        o << "      const u64* off = " << P(pw.offsets, "const u64") << ";\n";
-        o << "      const u32* other = " << P(pw.row_other, "const u32") << ";\n";
-        o << "      const u32 ep = s - " << lo << "u;\n";
-        o << "      const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
-        o << "      if (threadIdx.x == 0) events" << k << " += r1 - r0;\n";
-        o << "      for (u64 q0 = r0; q0 < r1; q0 += " << row_chunk() << "ull) {\n";
-        o << "        const u64 q1 = q0 + " << row_chunk() << "ull < r1 ? q0 + " << row_chunk() << "ull : r1;\n";
-        o << emit_atomic_chunk(pw, "        ");
-        o << "      }\n    }\n";
+        o << "          " << (full ? "{" : "if (s >= " + std::to_string(lo) + "u && s < " + std::to_string(hi) + "u) {")
+          << "\n";
+        o << "            const u64* off = " << P(pw.offsets, "const u64") << ";\n";
+        o << "            const u32* other = " << P(pw.row_other, "const u32") << ";\n";
+        o << "            const u32 ep = s - " << lo << "u;\n";
+        o << "            const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
+        o << "            if (c == 0 && lane == 0) events" << k << " += r1 - r0;\n";
+        o << "            const u64 q0 = r0 + c * 256ull;\n";
+        o << "            const u64 q1 = q0 + 256ull < r1 ? q0 + 256ull : r1;\n";
+        o << emit_warp_chunk(pw, "            ");
+        o << "          }\n";
       }
-      o << "  }\n";
+      o << "        }\n    }\n";
       for (size_t k = 0; k < fused.size(); ++k)
-        o << "  if (threadIdx.x == 0 && events" << k << ") atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64")
-          << " + " << fused[k]->delivered_slot << ", events" << k << ");\n";
+        o << "    if (lane == 0 && events" << k << ") atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64") << " + "
+          << fused[k]->delivered_slot << ", events" << k << ");\n";
+      o << "  }\n";
     }
-    o << "  if (s_last) {\n    __threadfence();\n";
-    o << "    b2_finalize_spikes<" << kThreads << ">(" << es.x_tiles << "u, " << tile_n << "u, " << P(es.tile_count, "const u32")
-      << ", " << P(es.stage, "const u32") << ", " << P(es.ring, "u32") << ", " << u64lit(es.mask) << ", "
-      << P(es.tick_start, "u64") << ", rel, " << u64lit(es.cap) << ", " << floor_of(size_t(stream_id)) << ", err);\n  }\n";
     o << kernel_tail();
     return o.str();
   }
-
 
   // `(summed)` variable (run_summed_program, executor.rs:2548-2597): one
   // thread per destination neuron this rank owns clears it and adds its
@@ -1750,6 +1903,18 @@ struct Engine::Impl {
   }
 
   // Reset over the tick's fired list (one thread per spike).
+  // No initial lastspike of population p is at or after the run's first
+  // tick, so during the run lastspike == t holds exactly for the neurons the
+  // tick's threshold fired.
+  bool lastspike_before_start(size_t p) const {
+    const auto& inst = m.population_instances[p];
+    if (!inst.refractory) return false;
+    const double t0 = double(start_tick) * dt;
+    for (double v : inst.refractory->initial_lastspike)
+      if (v >= t0) return false;
+    return true;
+  }
+
   std::string gen_reset(const std::string& name, size_t p, const Program& R, int stream_id) {
     const auto& def = m.populations[p];
     const EventStreamDev& es = streams[size_t(stream_id)];
@@ -2191,12 +2356,59 @@ struct Engine::Impl {
     o << ind << "  const u64 q = q0 + threadIdx.x + u * " << kThreads << "ull;\n";
     o << ind << "  tv[u] = q < q1;\n";
     o << ind << "  tq[u] = tv[u] ? (u64)__ldg(other + q) + " << target_bias(def) << "ull : 0ull;\n" << ind << "}\n";
+    if (pw.counted) {
+      // counted delivery: one event more for the target (the gate and the
+      // map are applied by the target's next dense kernel)
+      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) if (tv[u]) atomicAdd("
+        << P(pw.count_ptr, "u32") << " + tq[u], 1u);\n";
+      return o.str();
+    }
     if (gated) {
       o << ind << "u8 tg[" << U << "];\n";
       o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) tg[u] = tv[u] ? __ldg("
         << P(tp.not_refractory, "const u8") << " + tq[u]) : (u8)0;\n";
     }
     o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) {\n";
+    o << ind << "  if (!tv[u]) continue;\n";
+    for (const auto& ad : pw.atomic_adds) {
+      DType d = tgt.states[ad.state].dtype;
+      int ptr = tp.states[ad.state].ptr;
+      std::string gate = ad.gated ? "if (tg[u]) " : "";
+      if (d == DType::F64)
+        o << ind << "  " << gate << "atomicAdd(" << P(ptr, "double") << " + tq[u], " << double_literal(ad.addend) << ");\n";
+      else
+        o << ind << "  " << gate << "{ if (!b2_atomic_add_f32_via_f64(" << P(ptr, "float") << " + tq[u], "
+          << double_literal(ad.addend) << ")) err |= " << kErrNonfinite << "u; }\n";
+    }
+    o << ind << "}\n";
+    return o.str();
+  }
+
+  // One warp delivers row entries [q0, q1) (at most 256) of a constant-addend
+  // pathway: every lane loads its eight entries first, then applies them.
+  std::string emit_warp_chunk(const PathwayDev& pw, const std::string& ind) {
+    const auto& def = m.synapses[pw.synapse];
+    const auto& tgt = m.populations[def.target_population];
+    const PopDev& tp = pops[def.target_population];
+    bool gated = false;
+    for (const auto& ad : pw.atomic_adds) gated |= ad.gated;
+    std::ostringstream o;
+    o << ind << "u64 tq[8];\n" << ind << "bool tv[8];\n";
+    o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) {\n";
+    o << ind << "  const u64 q = q0 + lane + u * 32ull;\n";
+    o << ind << "  tv[u] = q < q1;\n";
+    o << ind << "  tq[u] = tv[u] ? (u64)__ldg(other + q) + " << target_bias(def) << "ull : 0ull;\n" << ind << "}\n";
+    if (pw.counted) {
+      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) if (tv[u]) atomicAdd("
+        << P(pw.count_ptr, "u32") << " + tq[u], 1u);\n";
+      return o.str();
+    }
+    if (gated) {
+      o << ind << "u8 tg[8];\n";
+      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) tg[u] = tv[u] ? __ldg("
+        << P(tp.not_refractory, "const u8") << " + tq[u]) : (u8)0;\n";
+    }
+    o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) {\n";
     o << ind << "  if (!tv[u]) continue;\n";
     for (const auto& ad : pw.atomic_adds) {
       DType d = tgt.states[ad.state].dtype;
@@ -2597,6 +2809,8 @@ struct Engine::Impl {
     bool x_spike = false;
     const Program* R = nullptr;
     std::vector<const Program*> deferred;  // previous tick's trailing neuron maps
+    std::vector<PathwayDev*> applies;      // counted pathways of this tick, applied first, in order
+    const Program* post_R = nullptr;       // spike reset of this tick, on lanes whose lastspike is t
     size_t node_pos = 0;
   };
   struct PathSpec {
@@ -2613,6 +2827,8 @@ struct Engine::Impl {
     int fuse_path = -1;  // exchange: PathSpec delivered inside the same kernel
     std::vector<size_t> fused_steps;  // Step: further StepSpecs stepped by the same launch
     size_t item = 0;                  // evmon: EventMonitor index within its population
+    int reads = -1;                   // Text ops: the event stream whose lists they read
+    unsigned lb = 1;                  // list consumers: blocks that lay the list out in the ring
   };
   std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
   std::vector<SummedSpec> summed_specs;
@@ -2721,6 +2937,7 @@ struct Engine::Impl {
               o.index = p;
               o.grid = 148;
               o.item = node.item_index;
+              o.reads = pops[p].evmon_stream[node.item_index];
               specs.push_back(o);
             }
             break;
@@ -2795,10 +3012,10 @@ struct Engine::Impl {
               specs.push_back(o);
               if (st.X && streams[size_t(pops[p].stream_of_event[st.x_event])].exchanged) {
                 OpSpec x;
-                x.base = def.name + "_exchange";
+                x.base = def.name + "_receive";
                 x.text = "exchange";
                 x.index = size_t(pops[p].stream_of_event[st.x_event]);
-                x.grid = unsigned(streams[x.index].x_tiles);
+                x.grid = x.lb = kLayoutBlocks;
                 specs.push_back(x);
               }
             } else if (code.kind == "reset") {
@@ -2807,7 +3024,26 @@ struct Engine::Impl {
               size_t e = size_t(std::find(def.events.begin(), def.events.end(), *code.event_name) - def.events.begin());
               check(e < def.events.size(), "reset event is unknown");
               const Program* R = compile_pop(p, code);
+              // The spike reset of a population whose threshold sets
+              // lastspike, scheduled right after a dense kernel of the same
+              // population in this tick (Brunel: after the PoissonInput
+              // kernel, which follows the synaptic deliveries): that kernel
+              // applies it to the lanes whose lastspike is this tick's t --
+              // exactly the tick's fired neurons, since the threshold writes
+              // lastspike = t on firing and no initial lastspike is at or
+              // after the run's start -- instead of a kernel walking the list.
+              if (!no_fuse_ && *code.event_name == "spike" && pops[p].lastspike >= 0 && lastspike_before_start(p) &&
+                  stream_produced[size_t(pops[p].stream_of_event[e])] && !specs.empty() &&
+                  specs.back().kind == OpSpec::Kind::Step && specs.back().fused_steps.empty()) {
+                StepSpec& prev = steps_[specs.back().index];
+                std::vector<const Program*> rp{R};
+                if (prev.pop == p && !prev.R && !prev.post_R && !writes_available(rp)) {
+                  prev.post_R = R;
+                  break;
+                }
+              }
               o.text = gen_reset("@NAME@", p, *R, pops[p].stream_of_event[e]);
+              o.reads = pops[p].stream_of_event[e];
               o.grid = 148 * 4;
               specs.push_back(o);
             } else if (code.kind == "poisson_input" || code.kind == "run_regularly" || code.kind == "subexpression_update") {
@@ -3012,20 +3248,134 @@ struct Engine::Impl {
       std::vector<uint64_t> init(m.populations.size(), UINT64_MAX);
       deferred_flags = upload(init.data(), init.size() * 8);
     }
-    // Multi-GPU: an exchange directly followed by the delay-0
-    // constant-addend scatter of the same stream delivers the spikes it
-    // unpacks itself (gen_exchange), saving a kernel boundary per tick.
+    // Counted delivery: a run of constant-addend scatters into f32 state of
+    // one population, directly followed in the tick by a dense kernel of that
+    // population, only counts each target's events (an integer reduction
+    // instead of a compare-and-swap loop per event, and no gate load); the
+    // dense kernel applies each pathway's map as often, pathways in schedule
+    // order, before its own programs.  Every event of a pathway applies the
+    // same map, so the result is the reference's sequential one, and nothing
+    // between the scatters and that kernel touches the target population.
+    // The counts commute, so the scatters of one stream and delay then share
+    // a launch.
+    if (!no_fuse_ && counted_) {
+      auto target_of = [&](const OpSpec& o, size_t& T) -> bool {
+        if (o.kind != OpSpec::Kind::Path) return false;
+        const auto& pws = paths[o.index].pathways;
+        if (pws.empty()) return false;
+        for (const PathwayDev* pw : pws) {
+          if (pw->mode != PathwayDev::Mode::Atomic || pw->has_pending || !pw->uniform) return false;
+          const size_t tpop = m.synapses[pw->synapse].target_population;
+          if (pw != pws.front() && tpop != T) return false;
+          T = tpop;
+          for (const auto& ad : pw->atomic_adds)
+            if (m.populations[T].states[ad.state].dtype != DType::F32) return false;
+        }
+        return true;
+      };
+      for (size_t i = 0; i < specs.size(); ++i) {
+        size_t T = 0, T2 = 0;
+        if (!target_of(specs[i], T)) continue;
+        size_t j = i + 1;
+        while (j < specs.size() && target_of(specs[j], T2) && T2 == T) ++j;
+        if (j >= specs.size() || specs[j].kind != OpSpec::Kind::Step || steps_[specs[j].index].pop != T) continue;
+        StepSpec& st = steps_[specs[j].index];
+        for (size_t k = i; k < j; ++k)
+          for (PathwayDev* pw : paths[specs[k].index].pathways) {
+            pw->counted = true;
+            pw->count_ptr = alloc(std::max<size_t>(pops[T].count, 1) * 4);
+            memset_dev(pw->count_ptr, std::max<size_t>(pops[T].count, 1) * 4);
+            st.applies.push_back(pw);
+          }
+        for (size_t k = i + 1; k < j;) {
+          PathSpec& a = paths[specs[i].index];
+          const PathSpec& b = paths[specs[k].index];
+          if (a.pathways.front()->stream == b.pathways.front()->stream &&
+              a.pathways.front()->delay == b.pathways.front()->delay) {
+            a.pathways.insert(a.pathways.end(), b.pathways.begin(), b.pathways.end());
+            a.programs.insert(a.programs.end(), b.programs.begin(), b.programs.end());
+            a.codes.insert(a.codes.end(), b.codes.begin(), b.codes.end());
+            specs[i].base += "_" + specs[k].base;
+            specs.erase(specs.begin() + long(k));
+            --j;
+          } else {
+            ++k;
+          }
+        }
+        specs[i].base += "_count";
+        i = j;  // the dense kernel
+      }
+    }
+    // One GPU: a step directly followed by the delay-0 constant-addend
+    // scatter of the list it produces leaves the list as tile counts and
+    // ids, and the scatter lays it out in the ring while delivering it
+    // (gen_consumer): the step kernel then has no last-block pass.
+    auto fusable = [&](const OpSpec& o, int sid) {
+      if (o.kind != OpSpec::Kind::Path) return false;
+      for (const PathwayDev* pw : paths[o.index].pathways)
+        if (!(pw->mode == PathwayDev::Mode::Atomic && pw->stream == sid && pw->delay == 0 && pw->uniform &&
+              !pw->has_pending))
+          return false;
+      return true;
+    };
+    if (world == 1 && !no_fuse_ && fuse_exchange_) {
+      for (size_t i = 0; i + 1 < specs.size(); ++i) {
+        if (specs[i].kind != OpSpec::Kind::Step) continue;
+        const StepSpec& st = steps_[specs[i].index];
+        if (!st.X) continue;
+        const int sid = pops[st.pop].stream_of_event[st.x_event];
+        if (!fusable(specs[i + 1], sid) || streams[size_t(sid)].bitmap >= 0) continue;
+        streams[size_t(sid)].consumer_layout = true;
+        OpSpec& c = specs[i + 1];
+        c.fuse_path = int(c.index);
+        c.kind = OpSpec::Kind::Text;
+        c.text = "exchange";
+        c.index = size_t(sid);
+        c.base += "_atomic";
+        c.lb = 2;  // ~ a few hundred ids per tick at config 2
+        c.grid += c.lb;
+      }
+    }
+    // Multi-GPU: a receive directly followed by the delay-0 constant-addend
+    // scatter of the same stream delivers the spikes itself (gen_consumer),
+    // saving a kernel boundary and the ring read per tick.
     if (world > 1 && !no_fuse_ && fuse_exchange_) {
       for (size_t i = 0; i + 1 < specs.size(); ++i) {
-        if (specs[i].text != "exchange" || specs[i + 1].kind != OpSpec::Kind::Path) continue;
-        const PathSpec& ps = paths[specs[i + 1].index];
-        bool ok = true;
-        for (const PathwayDev* pw : ps.pathways)
-          ok &= pw->mode == PathwayDev::Mode::Atomic && pw->stream == int(specs[i].index) && pw->delay == 0;
-        if (!ok) continue;
+        if (specs[i].text != "exchange" || specs[i].fuse_path >= 0 || !fusable(specs[i + 1], int(specs[i].index)))
+          continue;
         specs[i].fuse_path = int(specs[i + 1].index);
         specs[i].base += "_" + specs[i + 1].base + "_atomic";
+        specs[i].lb = 4;
+        specs[i].grid = specs[i + 1].grid + specs[i].lb;
         specs.erase(specs.begin() + long(i) + 1);
+      }
+      // A receive whose list nothing reads later in the same tick (every
+      // consumer delivers it after a delay) moves to just before the first
+      // op that does, or to the end of the tick: the peers' lists then
+      // arrive while this rank delivers older ticks' spikes.
+      auto reads_now = [&](const OpSpec& o, int sid) {
+        if (o.kind == OpSpec::Kind::Path) {
+          for (const PathwayDev* pw : paths[o.index].pathways)
+            if (pw->stream == sid && (pw->delay == 0 || !pw->uniform || pw->has_pending)) return true;
+          return false;
+        }
+        if (o.kind == OpSpec::Kind::Step) return false;  // steps publish lists, they read none
+        if (o.text == "tdeliver") return paths[o.index].pathways.front()->stream == sid;
+        return o.reads == sid || o.text == "exchange";
+      };
+      std::set<int> placed;
+      for (size_t i = 0; i < specs.size();) {
+        if (specs[i].text != "exchange" || specs[i].fuse_path >= 0 || placed.count(int(specs[i].index))) {
+          ++i;
+          continue;
+        }
+        const int sid = int(specs[i].index);
+        placed.insert(sid);
+        size_t j = i + 1;
+        while (j < specs.size() && !reads_now(specs[j], sid)) ++j;
+        OpSpec moved = specs[i];
+        specs.erase(specs.begin() + long(i));
+        specs.insert(specs.begin() + long(j - 1), moved);  // i now holds the next unvisited op
       }
     }
     // Consecutive step kernels of different populations touch disjoint state
@@ -3090,8 +3440,9 @@ struct Engine::Impl {
             bodies << gen_summed_body(body, ss);
             kernels << gen_summed(nm, body, ss);
           } else if (o.text == "exchange")
-            kernels << gen_exchange(nm, int(o.index),
-                                    o.fuse_path >= 0 ? paths[size_t(o.fuse_path)].pathways : std::vector<PathwayDev*>{});
+            kernels << gen_consumer(nm, int(o.index),
+                                    o.fuse_path >= 0 ? paths[size_t(o.fuse_path)].pathways : std::vector<PathwayDev*>{},
+                                    o.grid, o.lb);
           else {
             std::string t = o.text;
             t.replace(t.find("@NAME@"), 6, nm);
@@ -3101,7 +3452,8 @@ struct Engine::Impl {
         case OpSpec::Kind::Step: {
           if (o.fused_steps.empty()) {
             const StepSpec& st = steps_[o.index];
-            kernels << gen_pop_step(nm, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred);
+            kernels << gen_pop_step(nm, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred, false, false,
+                                    st.applies, st.post_R);
             break;
           }
           std::vector<size_t> group{o.index};
@@ -3111,7 +3463,8 @@ struct Engine::Impl {
           for (size_t g = 0; g < group.size(); ++g) {
             const StepSpec& st = steps_[group[g]];
             const std::string fn = nm + "_part" + std::to_string(g);
-            kernels << gen_pop_step(fn, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred, false, true);
+            kernels << gen_pop_step(fn, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred, false, true,
+                                    st.applies, st.post_R);
             const uint64_t tiles = tiles_for(pops[st.pop].count);
             disp << "  " << (g ? "else if" : "if") << " (blockIdx.x < " << first + tiles << "u) " << fn
                  << "(ctl, tick, rel, t, blockIdx.x - " << first << "u, err);\n";

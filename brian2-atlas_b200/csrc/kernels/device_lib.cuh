@@ -44,7 +44,9 @@ struct RunCtl {
 
 __device__ __forceinline__ double b2_bits(u64 r) { return __longlong_as_double((i64)r); }
 __device__ __forceinline__ u64 b2_raw(double v) { return (u64)__double_as_longlong(v); }
-__device__ __forceinline__ bool b2_finite(double v) { return isfinite(v); }
+// Exponent field not all ones (an integer test on the high word, which keeps
+// the check off the FP64 pipe); the same answer as isfinite.
+__device__ __forceinline__ bool b2_finite(double v) { return (__double2hiint(v) & 0x7ff00000) != 0x7ff00000; }
 
 // ---------------------------------------------------------------- RNG
 __device__ __forceinline__ u64 b2_mix64(u64 v) {
@@ -151,7 +153,7 @@ __device__ double b2_binomial_inv(u64 seed, u64 stream, u64 tick, u64 index, u64
 // floor(bound) + 1, whose entries are the loop's own px values (built with
 // the loop's products and division in the same order), so each step is one
 // compare and one subtraction: identical draws, comparisons and results.
-__device__ double b2_binomial_tab(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
+__device__ __forceinline__ double b2_binomial_tab(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
                                   const double* __restrict__ tab, u32 K, bool reverse) {
   u64 draw = 0;
   for (int restarts = 0; restarts < 1 << 16; ++restarts) {
@@ -448,16 +450,19 @@ __device__ __forceinline__ u32 b2_block_exclusive_scan(u32 v, u32* total) {
 }
 
 // ---------------------------------------------------------------- GPU-to-GPU spike exchange
-// Every rank owns a contiguous block of each population.  A 32-neuron ballot
-// word of the threshold travels to every rank (itself included) as ONE
-// aligned 8-byte store {word, tag} into the receiver's exchange buffer, made
-// through a CUDA IPC mapping over NVLink.  An aligned 8-byte store is
-// single-copy atomic, so a receiver that reads the tag of the current tick
-// also reads that tick's word: no fence and no separate ready flag are needed
-// (the "low-latency" protocol of NVIDIA's collective library).  The buffer has
-// two halves used on alternate ticks; a rank cannot run two ticks ahead of a
-// peer, because its own tick t+1 needs the peer's words of tick t+1, which the
-// peer only writes after it has consumed tick t.
+// Every rank owns a contiguous block of each population and publishes the
+// tick's ascending list of its block's spikes (global ids) to every rank,
+// itself included: one aligned 8-byte store {value, tag} per id, plus one
+// {count, tag} word, into the receiver's inbox through a CUDA IPC mapping
+// over NVLink.  An aligned 8-byte store is single-copy atomic, so a receiver
+// that reads the tag of the current tick also reads that tick's value: no
+// fence and no separate ready flag are needed (the "low-latency" protocol of
+// NVIDIA's collective library).  Inbox layout per parity half: rank q's slot
+// starts at word q + lo_q (lo_q = first neuron of q's block): its count word,
+// then up to (block size) id words.  The two halves are used on alternate
+// ticks; a rank cannot run two ticks ahead of a peer, because its own tick t+1
+// needs the peer's list of tick t+1, which the peer only publishes after it
+// has consumed tick t.
 __device__ __forceinline__ void b2_ll_store(u64* p, u32 word, u32 tag) {
   const u64 v = ((u64)tag << 32) | (u64)word;
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -480,7 +485,7 @@ __device__ __forceinline__ u32 b2_ll_wait(const u64* p, u32 tag, u64 timeout_ns,
   if ((u32)(v >> 32) == tag) return (u32)v;
   const u64 t0 = b2_globaltimer();
   for (u64 it = 0; it < (1ull << 28); ++it) {
-    __nanosleep(64);
+    __nanosleep(32);
     v = b2_ll_load(p);
     if ((u32)(v >> 32) == tag) return (u32)v;
     if ((it & 15) == 0 && b2_globaltimer() - t0 > timeout_ns) break;
@@ -489,20 +494,19 @@ __device__ __forceinline__ u32 b2_ll_wait(const u64* p, u32 tag, u64 timeout_ns,
   return 0u;
 }
 
-// Lay out a tick's staged spike ids: every tile staged its ascending ids at
-// stage[tile * tile_n ...] and its count at tile_count[tile]; the last block
-// of the launch (after all tiles' stores are visible) computes the tiles'
-// exclusive offsets and copies the ids into the ring in tile order, which is
-// ascending neuron order.  Writes tick_start[rel + 1].
+// Exclusive offsets of the tiles' staged counts for the calling thread's
+// contiguous tile range [*t0, *t1) (the last block of a step launch; every
+// tile's count is visible): *pos = spikes before the range, *total = all.
 template <int THREADS>
-__device__ void b2_finalize_spikes(u32 tiles, u32 tile_n, const u32* tile_count, const u32* stage, u32* ring,
-                                   u64 mask, u64* tick_start, u64 rel, u64 cap, u64 floor, u32& err) {
+__device__ __forceinline__ void b2_tile_offsets(u32 tiles, const u32* tile_count, u32* t0, u32* t1, u32* pos,
+                                                u32* total) {
   __shared__ u32 s_warp_sum[THREADS / 32];
   __shared__ u32 s_total;
   const u32 per = (tiles + THREADS - 1) / THREADS;
-  const u32 t0 = threadIdx.x * per, t1 = min(tiles, t0 + per);
+  *t0 = threadIdx.x * per;
+  *t1 = min(tiles, *t0 + per);
   u32 mine = 0;
-  for (u32 t = t0; t < t1; ++t) mine += __ldcg(tile_count + t);
+  for (u32 t = *t0; t < *t1; ++t) mine += __ldcg(tile_count + t);
   const u32 lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   u32 x = mine;
 #pragma unroll
@@ -522,15 +526,49 @@ __device__ void b2_finalize_spikes(u32 tiles, u32 tile_n, const u32* tile_count,
     s_total = acc;
   }
   __syncthreads();
+  *pos = s_warp_sum[warp] + (x - mine);
+  *total = s_total;
+}
+
+// Publish a rank's staged spike list (last block of its step launch): the
+// tiles' ids in tile order (= ascending global ids) and the count go to the
+// inbox slot `slot` (in words) of every rank's inbox; inbox(q) returns rank
+// q's inbox half of this tick.
+template <int THREADS, class Inbox>
+__device__ void b2_publish_spikes(u32 tiles, u32 tile_n, const u32* tile_count, const u32* stage, Inbox inbox,
+                                  u32 world, u64 slot, u32 tag) {
+  u32 t0, t1, pos, total;
+  b2_tile_offsets<THREADS>(tiles, tile_count, &t0, &t1, &pos, &total);
+  for (u32 t = t0; t < t1; ++t) {
+    const u32 n = __ldcg(tile_count + t);
+    for (u32 k = 0; k < n; ++k) {
+      const u32 id = __ldcg(stage + (u64)t * tile_n + k);
+      for (u32 q = 0; q < world; ++q) b2_ll_store(inbox(q) + slot + 1 + pos + k, id, tag);
+    }
+    pos += n;
+  }
+  if (threadIdx.x < world) b2_ll_store(inbox(threadIdx.x) + slot, total, tag);
+}
+
+// Lay out a tick's staged spike ids: every tile staged its ascending ids at
+// stage[tile * tile_n ...] and its count at tile_count[tile]; the last block
+// of the launch (after all tiles' stores are visible) computes the tiles'
+// exclusive offsets and copies the ids into the ring in tile order, which is
+// ascending neuron order.  Writes tick_start[rel + 1].
+template <int THREADS>
+__device__ void b2_finalize_spikes(u32 tiles, u32 tile_n, const u32* tile_count, const u32* stage, u32* ring,
+                                   u64 mask, u64* tick_start, u64 rel, u64 cap, u64 floor, u32& err) {
+  u32 t0, t1, off, total;
+  b2_tile_offsets<THREADS>(tiles, tile_count, &t0, &t1, &off, &total);
   const u64 base = tick_start[rel];
-  u64 pos = base + s_warp_sum[warp] + (x - mine);
+  u64 pos = base + off;
   for (u32 t = t0; t < t1; ++t) {
     const u32 n = __ldcg(tile_count + t);
     for (u32 k = 0; k < n; ++k) ring[(pos + k) & mask] = __ldcg(stage + (u64)t * tile_n + k);
     pos += n;
   }
   if (threadIdx.x == 0) {
-    const u64 end = base + s_total;
+    const u64 end = base + total;
     tick_start[rel + 1] = end;
     if (end - floor > cap) err |= B2_ERR_RING;
   }

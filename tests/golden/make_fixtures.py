@@ -388,7 +388,7 @@ def random_draws(reference: Path, n: int = 200, ticks: int = 300, seed: int = 12
     G.v = np.linspace(0.0, 0.9, n)
     D = b.NeuronGroup(n, "lam : 1\nk : 1", name="draws", clock=clock)
     D.lam = np.linspace(0.5, 60.0, n)
-    D.run_regularly("k = poisson(lam)", dt=0.1 * b.ms, name="draw")
+    D.run_regularly("k = poisson(lam)", clock=clock, name="draw")
     spikes = b.SpikeMonitor(G, name="spikes")
     tv = b.StateMonitor(G, "v", record=True, name="trace_v", clock=clock)
     tk = b.StateMonitor(D, "k", record=True, name="trace_k", clock=clock)

@@ -54,10 +54,10 @@ def load(name):
     # PoissonInput commutes with everything up to the next tick's update: it
     # runs in the next step's prologue (plus a flush kernel for the last tick)
     ("cuba_poisson_small", ["step", "exc_pre_inh_pre_atomic", "flush_0_neurons"]),
-    # both pathways write v (order matters) and PoissonInput writes v before
-    # the reset: nothing may be merged or deferred
-    ("brunel_small", ["step", "excitatory_synapses_pre_atomic", "inhibitory_synapses_pre_atomic",
-                      "poisson_input", "reset"]),
+    # both pathways write f32 v (order matters): counted delivery, both
+    # counts in one launch, applied E then I by the PoissonInput kernel, which
+    # also resets the lanes the tick fired
+    ("brunel_small", ["step", "excitatory_synapses_pre_inhibitory_synap_atomic", "poisson_input"]),
     ("cobahh_small", ["step", "exc_pre_inh_pre_atomic"]),
     # the two populations step in one launch; on_pre writes the target's
     # conductance and the edge's weight and traces: target-ordered delivery
@@ -112,8 +112,8 @@ def test_exact_linear_update_is_pure_arithmetic(pkg):
     """CUBA's exp(-dt/tau) terms fold to host constants computed with glibc, so
     the per-neuron update issues no device transcendental."""
     src = pkg.codegen(load("cuba_small"))
-    step = src[src.index("neurons_step"):]
-    step = step[:step.index("b2_finalize_spikes")]
+    step = src[src.index("_neurons_step(RunCtl"):]
+    step = step[:step.index("\n}\n")]
     assert "exp(" not in step and "log(" not in step
 
 
@@ -216,3 +216,27 @@ def test_no_cpu_fallback(pkg, tmp_path):
     out = subprocess.run([sys.executable, "-c", code, str(ROOT)], capture_output=True, text=True,
                          env=dict(os.environ))
     assert out.stdout.startswith("refused:") and "build.py" in out.stdout, out.stdout + out.stderr
+
+
+def test_counted_delivery_plan(pkg, monkeypatch):
+    """Brunel (f32 membrane, E then I constant-addend pathways, then the
+    PoissonInput kernel): the two scatters only count events per target, in
+    one launch, and the PoissonInput kernel applies E's then I's map that
+    many times before its own program; B2GPU_COUNTED=0 keeps one
+    compare-and-swap scatter per pathway."""
+    import re
+    src = pkg.codegen(load("brunel_small"))
+    names = [n.split("_", 2)[2] for n in re.findall(r"__global__ void __launch_bounds__\([^)]*\) (\w+)", src)]
+    assert len([n for n in names if n.endswith("_atomic")]) == 1 and "b2_atomic_add_f32_via_f64(" not in src.split(
+        "__constant__ u64 g_ptr")[1]
+    poisson = src[src.index("_neurons_poisson_input(RunCtl"):]
+    poisson = poisson[:poisson.index("\n}\n")]
+    applies = [m.start() for m in re.finditer(r"const u32 n_ev = cna", poisson)]
+    assert len(applies) == 2 and applies[-1] < poisson.index("b2_binomial_tab")
+    # the spike reset runs in the same kernel, after the drive, on the lanes
+    # the tick's threshold fired
+    assert "neurons_reset" not in names and poisson.index("if (ls == t)") > poisson.index("b2_binomial_tab")
+    monkeypatch.setenv("B2GPU_COUNTED", "0")
+    src = pkg.codegen(load("brunel_small"))
+    names = [n.split("_", 2)[2] for n in re.findall(r"__global__ void __launch_bounds__\([^)]*\) (\w+)", src)]
+    assert len([n for n in names if n.endswith("_atomic")]) == 2 and "n_ev" not in src

@@ -43,20 +43,39 @@ def kernels(src):
 
 
 @pytest.mark.parametrize("world", [2, 3])
-def test_rank_plans(pkg, world):
+def test_rank_plans(pkg, world, monkeypatch):
     data = (MODELS / "cuba_small.json").read_bytes()
     n = json.loads(data)["definition"]["populations"][0]["count"]
     for r in range(world):
         src = pkg.codegen(data, rank=r, world_size=world)
         names = kernels(src)
-        # the step publishes fired words; the exchange kernel expands them
-        # into the global list the scatter reads
-        assert [k.split("_", 2)[2] for k in names][-3:] == ["neurons_step", "neurons_exchange",
-                                                           "exc_pre_inh_pre_atomic"]
+        # the step publishes its block's ascending list to every rank; the
+        # scatter waits for every rank's list, delivers it straight from the
+        # inbox and lays the global list out in the ring
+        assert [k.split("_", 2)[2] for k in names][-2:] == ["neurons_step", "neurons_receive_exc_pre_inh_pre_atomic"]
         lo, hi = pkg.partition(n, r, world)
-        step = src[src.index("neurons_step("):src.index("neurons_exchange(")]
-        assert f"i < {hi - lo}u" in step and "b2_ll_store" in step
-        assert "b2_ll_wait" in src[src.index("neurons_exchange("):]
+        step = src[src.index("neurons_step("):src.index("neurons_receive_exc_pre_inh_pre_atomic(")]
+        assert f"i < {hi - lo}u" in step and "b2_ll_store" in step and "atomicAdd" not in step
+        assert "b2_ll_wait" in src[src.index("neurons_receive_exc_pre_inh_pre_atomic("):]
+    # a separate receive launch, then the scatter reads the ring
+    monkeypatch.setenv("B2GPU_FUSE_EXCHANGE", "0")
+    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=0, world_size=world))]
+    assert names[-3:] == ["neurons_step", "neurons_receive", "exc_pre_inh_pre_atomic"]
+
+
+def test_delayed_receive_moves_after_the_delivery(pkg, tmp_path, monkeypatch):
+    """Brunel (one 15-tick delay): no kernel reads the tick's own list (the
+    reset runs inside the PoissonInput kernel, on the lanes the threshold
+    just fired), so the receive is the tick's last kernel and the peers'
+    lists travel while the delayed deliveries and the Poisson drive run;
+    with no fusion at all (one kernel per node) it stays right after the
+    step."""
+    data = (MODELS / "brunel_small.json").read_bytes()
+    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4))]
+    assert names[-1] == "neurons_receive" and "neurons_reset" not in names
+    monkeypatch.setenv("B2GPU_NO_FUSE", "1")
+    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4))]
+    assert names.index("neurons_receive") == names.index("neurons_step") + 1
 
 
 def test_multi_gpu_capability_errors(pkg, tmp_path):
@@ -89,15 +108,17 @@ def test_stdp_rank_plans_replicate_the_inputs(pkg, tmp_path, world):
         assert f"tj + {lo}u" in src[src.index("stdp_pre_deliver("):]
     # diagnostics: partition and exchange the inputs as well (the bucket
     # scatter reads the exchanged global list); exchange the targets too
-    for env, expect in ((dict(B2GPU_REPLICATE="0"), ["neurons_step_inputs_step", "inputs_exchange"]),
-                        (dict(B2GPU_LOCAL_STREAMS="0"), ["neurons_step", "neurons_exchange", "inputs_step"])):
+    for env, expect in ((dict(B2GPU_REPLICATE="0"), ["neurons_step_inputs_step", "inputs_receive", "stdp_pre_targets",
+                                                    "stdp_pre_deliver", "stdp_post_edges"]),
+                        (dict(B2GPU_LOCAL_STREAMS="0"), ["neurons_step_inputs_step", "stdp_pre_targets",
+                                                         "stdp_pre_deliver", "neurons_receive", "stdp_post_edges"])):
         os.environ.update(env)
         try:
             names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=0, world_size=world))]
         finally:
             for key in env:
                 del os.environ[key]
-        assert names == expect + ["stdp_pre_targets", "stdp_pre_deliver", "stdp_post_edges"]
+        assert names == expect
 
 
 def _gloo_rank(rank, world, port, q):
@@ -179,10 +200,13 @@ def assert_same_files(a, b):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("world", [2, 3, 4, 8])
-def test_ranks_match_oracle(pkg, oracle, tmp_path, world):
+@pytest.mark.parametrize("world,fuse", [(2, "1"), (2, "0"), (3, "1"), (4, "1"), (8, "1")])
+def test_ranks_match_oracle(pkg, oracle, tmp_path, monkeypatch, world, fuse):
+    """fuse=0: a separate receive launch before a scatter that reads the ring
+    (the default delivers delay-0 constant-addend pathways from the inbox)."""
     if gpu_count() < world:
         pytest.skip(f"needs {world} GPUs")
+    monkeypatch.setenv("B2GPU_FUSE_EXCHANGE", fuse)
     import importlib
     synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
     template = json.loads((MODELS / "cuba_poisson_small.json").read_text())

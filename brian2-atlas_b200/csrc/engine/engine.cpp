@@ -204,6 +204,10 @@ bool conflicts(const NodeEffects& a, const NodeEffects& b) {
 // Blocks of a stand-alone list-layout kernel (gen_consumer): each reads every
 // tile count of the tick and copies its share of the list into the ring.
 constexpr unsigned kLayoutBlocks = 16;
+// One GPU: populations of at least this many step tiles get a layout kernel.
+constexpr size_t kLayoutMinTiles = 1024;
+// Blocks of a presynaptic replicate kernel (each writes one flag per rank).
+constexpr unsigned kReplicaBlocks = 8;
 
 struct Engine::Impl {
   b2ir::Model m;
@@ -374,6 +378,7 @@ struct Engine::Impl {
     size_t synapse = 0, k = 0;
     const Program* program = nullptr;
     size_t result = 0;  // register of `_synaptic_var`
+    std::map<size_t, int> pre_replica;  // presynaptic state -> replica read (multi-GPU)
   };
   int delivered_ptr = -1;
   size_t delivered_count = 0;
@@ -493,7 +498,7 @@ struct Engine::Impl {
   unsigned scatter_unroll_ = kScatterUnroll;  // row entries per thread per scatter work item
   uint64_t row_chunk() const { return uint64_t(kThreads) * scatter_unroll_; }
 
-  unsigned npt_ = 4;         // neurons per thread in neuron kernels
+  unsigned npt_ = 2;         // neurons per thread in neuron kernels (config 2: 18.2 ms per 1000 ticks at 2, 19.9 at 4)
   // __launch_bounds__ occupancy hint for neuron kernels (0: none).  Four
   // resident 256-thread blocks per SM (<= 64 registers) measured fastest for
   // the fused CUBA step: 25.3 us vs 28.6 us per 1M-neuron tick without it.
@@ -604,10 +609,14 @@ struct Engine::Impl {
       // Target-owned partition (brian2_rust/distributed.py: rank-local neuron
       // and synapse state, incoming CSR per rank).  What a rank cannot
       // evaluate from its own block is rejected before any device work.
+      // Per-edge programs (synaptic state updates, subexpressions,
+      // run_regularly) run over the rank's own edges, and a summed variable
+      // into the target population sums the rank's own targets' in-edges;
+      // a sum into the source population would need every rank's edges.
       for (const auto& s : m.synapses) {
         for (const auto& c : s.code_objects)
-          check(c.kind == "synapses" || c.kind == "synapses_post",
-                "multi-GPU runs support on_pre and on_post pathways only");
+          check(c.kind != "summed_variable" || !(c.summed_target && *c.summed_target == "pre"),
+                "multi-GPU runs do not support summed variables into the presynaptic population");
       }
       for (size_t k = 0; k < m.synapses.size(); ++k) {
         const auto& inst = m.synapse_instances[k];
@@ -1198,31 +1207,72 @@ struct Engine::Impl {
       es.starts.assign(1, 0);
     }
     if (world > 1) {
-      arena_stage_off = x_bytes;
-      const size_t total = arena_bytes_of(rank);
-      if (!opt.dry_run) {
-        arena = DeviceBuffer(total);
-        B2_CUDA(cudaMemsetAsync(arena.ptr, 0, total, stream));  // tag 0 never matches a tick
-        cudaDeviceProp prop;
-        B2_CUDA(cudaGetDeviceProperties(&prop, device));
-        ArenaHeader h{};
-        std::memcpy(h.uuid, prop.uuid.bytes, 16);
-        h.rank = rank;
-        h.world = world;
-        h.bytes = total;
-        h.magic = kArenaMagic;
-        B2_CUDA(cudaMemcpyAsync(arena.ptr, &h, sizeof(h), cudaMemcpyHostToDevice, stream));
-        B2_CUDA(cudaStreamSynchronize(stream));
-      }
+      arena_x_end = x_bytes;
       for (auto& es : streams) {
         if (!es.exchanged) continue;
-        for (int q = 0; q < world; ++q) {
-          void* own = opt.dry_run ? reinterpret_cast<void*>(uintptr_t(0x100000) * (ptrs.size() + 1))
-                                  : static_cast<void*>(static_cast<char*>(arena.ptr) + es.x_off);
-          es.xptr.push_back(add_ptr(q == rank ? own : nullptr));  // peers: filled by connect()
-        }
+        for (int q = 0; q < world; ++q) es.xptr.push_back(add_ptr(nullptr));  // own: build_arena; peers: connect()
       }
     }
+  }
+
+  // Allocate this rank's shared allocation once the plan has reserved every
+  // region in it (inboxes, presynaptic replicas), and point this rank's own
+  // slots at it; the peers' slots are filled by connect().
+  void build_arena() {
+    if (world == 1) return;
+    arena_stage_off = (arena_x_end + 255) / 256 * 256;
+    const size_t total = arena_bytes_of(rank);
+    if (!opt.dry_run) {
+      arena = DeviceBuffer(total);
+      B2_CUDA(cudaMemsetAsync(arena.ptr, 0, total, stream));  // tag 0 never matches a tick
+      cudaDeviceProp prop;
+      B2_CUDA(cudaGetDeviceProperties(&prop, device));
+      ArenaHeader h{};
+      std::memcpy(h.uuid, prop.uuid.bytes, 16);
+      h.rank = rank;
+      h.world = world;
+      h.bytes = total;
+      h.magic = kArenaMagic;
+      B2_CUDA(cudaMemcpyAsync(arena.ptr, &h, sizeof(h), cudaMemcpyHostToDevice, stream));
+      B2_CUDA(cudaStreamSynchronize(stream));
+    }
+    auto own = [&](size_t off) {
+      return opt.dry_run ? uint64_t(0x100000) * (off / 256 + 1)
+                         : reinterpret_cast<uint64_t>(static_cast<char*>(arena.ptr) + off);
+    };
+    for (auto& es : streams)
+      if (es.exchanged) ptrs[size_t(es.xptr[size_t(rank)])] = own(es.x_off);
+    for (auto& r : replicas) {
+      ptrs[size_t(r.rptr[size_t(rank)])] = own(r.off);
+      ptrs[size_t(r.fptr[size_t(rank)])] = own(r.flags_off);
+    }
+  }
+
+  // Read-only replica of one presynaptic state for one reading kernel
+  // (multi-GPU; the reference's MPI path keeps the same, distributed.py:255,
+  // mpi_codegen.py:300): every rank's block of the variable, copied into
+  // every rank's region by a replicate kernel right before the reader, two
+  // halves used on alternate ticks, and per (rank, replicate block) a
+  // tagged flag.
+  struct Replica {
+    size_t pop = 0, state = 0, width = 8;
+    size_t off = 0, flags_off = 0;  // arena offsets of the data halves and the flag halves
+    std::vector<int> rptr, fptr;    // g_ptr slots of every rank's data and flags
+  };
+  std::vector<Replica> replicas;
+  size_t arena_x_end = 0;
+  int new_replica(size_t pop, size_t state) {
+    Replica r;
+    r.pop = pop;
+    r.state = state;
+    r.width = b2ir::dtype_bytes(m.populations[pop].states[state].dtype);
+    r.off = (arena_x_end + 255) / 256 * 256;
+    r.flags_off = r.off + (2 * pops[pop].global_count * r.width + 255) / 256 * 256;
+    arena_x_end = r.flags_off + 2 * size_t(world) * kReplicaBlocks * 8;
+    for (int q = 0; q < world; ++q) r.rptr.push_back(add_ptr(nullptr));
+    for (int q = 0; q < world; ++q) r.fptr.push_back(add_ptr(nullptr));
+    replicas.push_back(r);
+    return int(replicas.size() - 1);
   }
 
   // Result staging of rank q inside its shared allocation, relative to the
@@ -1866,7 +1916,7 @@ struct Engine::Impl {
     o << "  const u64 tgt_state = (u64)tgt + " << target_bias(def) << "ull;\n";
     o << "  (void)src_state; (void)tgt_state; (void)t; (void)tick; (void)edge;\n";
     PathwayDev none;
-    o << emit_program(*ss.program, event_ctx(ss.synapse, none), "e_");
+    o << emit_program(*ss.program, event_ctx(ss.synapse, none, &ss.pre_replica), "e_");
     o << "  return " << reg_expr(*ss.program, ss.result, "e_") << ";\n}\n";
     return o.str();
   }
@@ -2053,16 +2103,23 @@ struct Engine::Impl {
     return uint64_t(def.target_start) - pops[def.target_population].lo;
   }
 
-  EmitContext event_ctx(size_t s, const PathwayDev& pw) {
+  EmitContext event_ctx(size_t s, const PathwayDev& pw, const std::map<size_t, int>* pre_replica = nullptr) {
     EmitContext c;
     const auto& def = m.synapses[s];
-    c.load = [this, s, &def](const Input& in) -> std::string {
+    c.load = [this, s, &def, pre_replica](const Input& in) -> std::string {
       const SynDev& sd = syns[s];
       const auto& src = m.populations[def.source_population];
       const auto& tgt = m.populations[def.target_population];
       switch (in.kind) {
         case Input::Kind::PreState: {
           DType d = src.states[in.index].dtype;
+          if (pre_replica && pre_replica->count(in.index)) {
+            // every rank's block, copied this tick (half (tick - start) & 1)
+            const Replica& r = replicas[size_t(pre_replica->at(in.index))];
+            return widen(d, "__ldcg(" + P(r.rptr[size_t(rank)], (std::string("const ") + storage_ctype(d)).c_str()) +
+                                " + ((tick - " + u64lit(start_tick) + ") & 1ull) * " +
+                                std::to_string(pops[def.source_population].global_count) + "ull + src_state)");
+          }
           return widen(d, P(pops[def.source_population].states[in.index].ptr, storage_ctype(d)) + "[src_state]");
         }
         case Input::Kind::PostState: {
@@ -2099,7 +2156,7 @@ struct Engine::Impl {
   // synapse_only: commit only synapse-state writes (commit_synapses,
   // executor.rs:5615-5623), as per-edge update programs do
   std::string gen_pathway_body(const std::string& fname, size_t s, const PathwayDev& pw, const Program& pr,
-                               bool synapse_only = false) {
+                               bool synapse_only = false, const std::map<size_t, int>* pre_replica = nullptr) {
     const auto& def = m.synapses[s];
     const SynDev& sd = syns[s];
     std::ostringstream o;
@@ -2108,7 +2165,7 @@ struct Engine::Impl {
     o << "  const u64 src_state = (u64)src + " << def.source_start << "ull;\n";
     o << "  const u64 tgt_state = (u64)tgt + " << target_bias(def) << "ull;\n";
     o << "  (void)src_state; (void)tgt_state; (void)t; (void)tick;\n";
-    o << emit_program(pr, event_ctx(s, pw), "e_");
+    o << emit_program(pr, event_ctx(s, pw, pre_replica), "e_");
     const auto& src = m.populations[def.source_population];
     const auto& tgt = m.populations[def.target_population];
     for (const auto& [w, r] : pr.writes) {
@@ -2737,7 +2794,8 @@ struct Engine::Impl {
 
   // L1 prefetch of every state and per-edge parameter element a pathway body
   // reads (same addresses as the body's loads).
-  std::string gen_pathway_prefetch(const std::string& fname, size_t s, const Program& pr) {
+  std::string gen_pathway_prefetch(const std::string& fname, size_t s, const Program& pr,
+                                   const std::map<size_t, int>* pre_replica = nullptr) {
     const auto& def = m.synapses[s];
     const SynDev& sd = syns[s];
     const auto& src = m.populations[def.source_population];
@@ -2750,6 +2808,8 @@ struct Engine::Impl {
     std::set<std::string> seen;
     for (const auto& [slot, in] : pr.bindings) {
       std::string addr;
+      if (in.kind == Input::Kind::PreState && pre_replica && pre_replica->count(in.index))
+        continue;  // read from this tick's replica, not the rank's own block
       if (in.kind == Input::Kind::PreState)
         addr = P(pops[def.source_population].states[in.index].ptr, storage_ctype(src.states[in.index].dtype)) + " + src_state";
       else if (in.kind == Input::Kind::PostState)
@@ -2818,6 +2878,7 @@ struct Engine::Impl {
     std::vector<const Program*> programs;
     std::vector<std::string> codes;
     std::string body;  // device function of a single non-atomic pathway
+    std::map<size_t, int> pre_replica;  // presynaptic state -> replica read (multi-GPU)
   };
   struct OpSpec {
     enum class Kind { Text, Step, Path } kind = Kind::Text;
@@ -2835,10 +2896,81 @@ struct Engine::Impl {
   struct SynProgSpec {
     size_t synapse = 0;
     const Program* program = nullptr;
+    std::map<size_t, int> pre_replica;  // presynaptic state -> replica read (multi-GPU)
   };
   std::vector<SynProgSpec> synprog_specs;
   std::vector<Op> flush_ops;
   int deferred_flags = -1;                                  // per-population u64 tick of the last flush
+  // Multi-GPU: the presynaptic states a synaptic program reads from a
+  // partitioned source population get a replica each, refreshed by a
+  // replicate kernel and a wait kernel placed right before the reader (the
+  // value is the current one: every earlier writer of the tick is already in
+  // `specs`).  Presynaptic refractoriness is not replicated.
+  std::map<size_t, int> replicate_pre_state(const Program& pr, size_t s, std::vector<OpSpec>& specs_out,
+                                            const std::string& code_name) {
+    std::map<size_t, int> out;
+    if (world == 1) return out;
+    const size_t sp = m.synapses[s].source_population;
+    for (const auto& b : pr.bindings) {
+      check(pops[sp].replicated || !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre),
+            "multi-GPU runs cannot read presynaptic refractoriness across GPUs ('" + code_name + "')");
+      if (b.second.kind != Input::Kind::PreState || pops[sp].replicated || out.count(b.second.index)) continue;
+      const int r = new_replica(sp, b.second.index);
+      out[b.second.index] = r;
+      const std::string var = sanitize(m.populations[sp].name + "_" + m.populations[sp].states[b.second.index].name);
+      OpSpec rep;
+      rep.base = var + "_replicate";
+      rep.text = "replicate";
+      rep.index = size_t(r);
+      rep.grid = kReplicaBlocks;
+      specs_out.push_back(rep);
+      OpSpec w;
+      w.base = var + "_replica_wait";
+      w.text = "replica_wait";
+      w.index = size_t(r);
+      w.grid = 1;
+      specs_out.push_back(w);
+    }
+    return out;
+  }
+
+  // Copy this rank's block of the replicated state into every rank's replica
+  // half of this tick (plain peer stores over NVLink), then, per block, a
+  // system-scope fence and one tagged flag per rank.
+  std::string gen_replicate(const std::string& name, const Replica& r) {
+    const PopDev& pd = pops[r.pop];
+    const char* ct = storage_ctype(m.populations[r.pop].states[r.state].dtype);
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  const u64 half = (rel & 1ull) * " << pd.global_count << "ull;\n";
+    o << "  const " << ct << "* mine = " << P(pd.states[r.state].ptr, (std::string("const ") + ct).c_str()) << ";\n";
+    o << "  for (u64 i = blockIdx.x * (u64)blockDim.x + threadIdx.x; i < " << pd.count
+      << "ull; i += (u64)gridDim.x * blockDim.x) {\n";
+    o << "    const " << ct << " v = mine[i];\n";
+    o << "    for (u32 q = 0; q < " << world << "u; ++q) ((" << ct << "*)g_ptr[" << r.rptr[0] << " + q])[half + "
+      << pd.lo << "ull + i] = v;\n  }\n";
+    o << "  __threadfence_system();\n  __syncthreads();\n";
+    o << "  if (threadIdx.x < " << world << "u) b2_ll_store(((u64*)g_ptr[" << r.fptr[0] << " + threadIdx.x]) + (rel & 1ull) * "
+      << world * kReplicaBlocks << "ull + " << rank * int(kReplicaBlocks) << "ull + blockIdx.x, 1u, (u32)(rel + 1ull));\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
+  // Wait (bounded) for every rank's replicate flags of this tick; the fence
+  // after them orders the peers' stores before the readers that follow.
+  std::string gen_replica_wait(const std::string& name, const Replica& r) {
+    const uint64_t timeout_ns = uint64_t(opt.exchange_timeout_ms) * 1000000ull;
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  const bool poisoned = *(volatile const u32*)&ctl->error != 0u;\n";
+    o << "  if (threadIdx.x < " << world * kReplicaBlocks << "u && !poisoned) b2_ll_wait(((const u64*)g_ptr["
+      << r.fptr[size_t(rank)] << "]) + (rel & 1ull) * " << world * kReplicaBlocks << "ull + threadIdx.x, (u32)(rel + 1ull), "
+      << timeout_ns << "ull, err);\n";
+    o << "  __syncthreads();\n  __threadfence_system();\n";
+    o << kernel_tail();
+    return o.str();
+  }
+
   bool deferred_pending = false;
 
   void build_plan() {
@@ -3103,19 +3235,15 @@ struct Engine::Impl {
           }
           programs.push_back(Program::compile(code, inputs, writable, m.functions));
           const Program& pr = programs.back();
-          if (world > 1) {
-            for (const auto& b : pr.bindings)
-              check(b.second.kind != Input::Kind::PreState &&
-                        !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre),
-                    "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
+          if (world > 1)
             check(!pr.uses_rng(), "multi-GPU runs do not support random draws in synaptic code ('" + code.name + "')");
-          }
+          auto rep = replicate_pre_state(pr, s, specs, code.name);
           OpSpec o;
           o.base = code.name;
           o.text = "synprog";
           o.index = synprog_specs.size();
           o.grid = unsigned(std::max<uint64_t>(1, (syns[s].local_edges + kThreads - 1) / kThreads));
-          synprog_specs.push_back({s, &pr});
+          synprog_specs.push_back({s, &pr, rep});
           specs.push_back(o);
           continue;
         }
@@ -3135,18 +3263,16 @@ struct Engine::Impl {
             const bool own = b.second.index == sv.dest_state &&
                              (sv.to_pre ? b.second.kind == Input::Kind::PreState : b.second.kind == Input::Kind::PostState);
             check(!own, "a summed expression that reads its own summed variable is not supported by the GPU engine");
-            check(world == 1 || (b.second.kind != Input::Kind::PreState &&
-                                 !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre)),
-                  "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
           }
           check(world == 1 || !pr.uses_rng(), "multi-GPU runs do not support random draws in synaptic code ('" + code.name + "')");
+          auto rep = replicate_pre_state(pr, s, specs, code.name);
           OpSpec o;
           o.base = code.name;
           o.text = "summed";
           o.index = summed_specs.size();
           const PopDev& dp = pops[sv.dest_pop];
           o.grid = unsigned(std::max<size_t>(1, (dp.count + kThreads - 1) / kThreads));
-          summed_specs.push_back({s, k, &pr, res->second});
+          summed_specs.push_back({s, k, &pr, res->second, rep});
           specs.push_back(o);
           continue;
         }
@@ -3161,13 +3287,11 @@ struct Engine::Impl {
         auto inputs = synapse_inputs(s, pw.is_pre, writable);
         programs.push_back(Program::compile(code, inputs, writable, m.functions));
         const Program& pr = programs.back();
+        std::map<size_t, int> pre_rep;
         if (world > 1) {
-          // presynaptic state is complete on every rank only for a replicated source
-          for (const auto& b : pr.bindings)
-            check(pops[m.synapses[s].source_population].replicated ||
-                      (b.second.kind != Input::Kind::PreState &&
-                       !(b.second.kind == Input::Kind::Available && b.second.domain == Domain::Pre)),
-                  "multi-GPU runs cannot read presynaptic state across GPUs ('" + code.name + "')");
+          // presynaptic state is complete on every rank for a replicated
+          // source; a partitioned one's is copied to every rank first
+          pre_rep = replicate_pre_state(pr, s, specs, code.name);
           for (const auto& w : pr.writes)
             check(w.first.kind != WriteTarget::Kind::PreNeuron,
                   "multi-GPU runs cannot write presynaptic state across GPUs ('" + code.name + "')");
@@ -3199,6 +3323,7 @@ struct Engine::Impl {
           ps.pathways.push_back(&pw);
           ps.programs.push_back(&pr);
           ps.codes.push_back(code.name);
+          ps.pre_replica = pre_rep;
           OpSpec o;
           o.kind = OpSpec::Kind::Path;
           o.index = paths.size();
@@ -3336,6 +3461,28 @@ struct Engine::Impl {
         c.grid += c.lb;
       }
     }
+    // One GPU, large populations whose list no fused scatter lays out: a
+    // layout kernel of kLayoutBlocks blocks after the step (moved below to
+    // just before the list's first reader) instead of the step's last block,
+    // which would copy a big tick's ids alone (config 3: ~17k ids per tick,
+    // 88 us of a 4M-neuron step).
+    if (world == 1 && !no_fuse_ && fuse_exchange_) {
+      for (size_t i = 0; i < specs.size(); ++i) {
+        if (specs[i].kind != OpSpec::Kind::Step) continue;
+        const StepSpec& st = steps_[specs[i].index];
+        if (!st.X) continue;
+        const int sid = pops[st.pop].stream_of_event[st.x_event];
+        EventStreamDev& es = streams[size_t(sid)];
+        if (es.consumer_layout || tiles_for(pops[st.pop].count) < kLayoutMinTiles) continue;
+        es.consumer_layout = true;
+        OpSpec x;
+        x.base = m.populations[st.pop].name + "_layout";
+        x.text = "exchange";
+        x.index = size_t(sid);
+        x.grid = x.lb = kLayoutBlocks;
+        specs.insert(specs.begin() + long(i) + 1, x);
+      }
+    }
     // Multi-GPU: a receive directly followed by the delay-0 constant-addend
     // scatter of the same stream delivers the spikes itself (gen_consumer),
     // saving a kernel boundary and the ring read per tick.
@@ -3349,10 +3496,12 @@ struct Engine::Impl {
         specs[i].grid = specs[i + 1].grid + specs[i].lb;
         specs.erase(specs.begin() + long(i) + 1);
       }
-      // A receive whose list nothing reads later in the same tick (every
-      // consumer delivers it after a delay) moves to just before the first
-      // op that does, or to the end of the tick: the peers' lists then
-      // arrive while this rank delivers older ticks' spikes.
+    }
+    // A receive or layout kernel whose list nothing reads later in the same
+    // tick (every consumer delivers it after a delay) moves to just before
+    // the first op that does, or to the end of the tick: on several GPUs the
+    // peers' lists then arrive while this rank delivers older ticks' spikes.
+    if (!no_fuse_ && fuse_exchange_) {
       auto reads_now = [&](const OpSpec& o, int sid) {
         if (o.kind == OpSpec::Kind::Path) {
           for (const PathwayDev* pw : paths[o.index].pathways)
@@ -3418,14 +3567,14 @@ struct Engine::Impl {
           else if (o.text == "tdeliver") {
             PathSpec& ps = paths[o.index];
             const std::string pf = ps.body + "_prefetch";
-            bodies << gen_pathway_prefetch(pf, ps.pathways[0]->synapse, *ps.programs[0]);
+            bodies << gen_pathway_prefetch(pf, ps.pathways[0]->synapse, *ps.programs[0], &ps.pre_replica);
             kernels << gen_targets_deliver(nm, ps.body, pf, *ps.pathways[0]);
           }
           else if (o.text == "synprog") {
             const SynProgSpec& sp = synprog_specs[o.index];
             std::string body = "b2_synprog_" + std::to_string(kid);
             PathwayDev none;
-            bodies << gen_pathway_body(body, sp.synapse, none, *sp.program, true);
+            bodies << gen_pathway_body(body, sp.synapse, none, *sp.program, true, &sp.pre_replica);
             const SynDev& sd = syns[sp.synapse];
             std::ostringstream k;
             k << kernel_head(nm);
@@ -3439,7 +3588,11 @@ struct Engine::Impl {
             std::string body = "b2_summed_" + std::to_string(kid);
             bodies << gen_summed_body(body, ss);
             kernels << gen_summed(nm, body, ss);
-          } else if (o.text == "exchange")
+          } else if (o.text == "replicate")
+            kernels << gen_replicate(nm, replicas[o.index]);
+          else if (o.text == "replica_wait")
+            kernels << gen_replica_wait(nm, replicas[o.index]);
+          else if (o.text == "exchange")
             kernels << gen_consumer(nm, int(o.index),
                                     o.fuse_path >= 0 ? paths[size_t(o.fuse_path)].pathways : std::vector<PathwayDev*>{},
                                     o.grid, o.lb);
@@ -3478,7 +3631,8 @@ struct Engine::Impl {
           PathSpec& ps = paths[o.index];
           if (ps.pathways.size() == 1 && ps.pathways[0]->mode != PathwayDev::Mode::Atomic) {
             std::string body = "b2_body_" + std::to_string(kid) + "_" + sanitize(ps.codes[0]);
-            bodies << gen_pathway_body(body, ps.pathways[0]->synapse, *ps.pathways[0], *ps.programs[0]);
+            bodies << gen_pathway_body(body, ps.pathways[0]->synapse, *ps.pathways[0], *ps.programs[0], false,
+                                       &ps.pre_replica);
             ps.body = body;
             const auto md = ps.pathways[0]->mode;
             const char* mode = md == PathwayDev::Mode::EdgeParallel ? "_edges"
@@ -3843,6 +3997,13 @@ struct Engine::Impl {
         if (q != rank)
           ptrs[size_t(es.xptr[size_t(q)])] = reinterpret_cast<uint64_t>(static_cast<char*>(peer_base[size_t(q)]) + es.x_off);
     }
+    for (auto& r : replicas)
+      for (int q = 0; q < world; ++q)
+        if (q != rank) {
+          ptrs[size_t(r.rptr[size_t(q)])] = reinterpret_cast<uint64_t>(static_cast<char*>(peer_base[size_t(q)]) + r.off);
+          ptrs[size_t(r.fptr[size_t(q)])] =
+              reinterpret_cast<uint64_t>(static_cast<char*>(peer_base[size_t(q)]) + r.flags_off);
+        }
     B2_CUDA(cudaMemcpy(gptr_table, ptrs.data(), ptrs.size() * 8, cudaMemcpyHostToDevice));
     connected = true;
   }
@@ -4126,6 +4287,7 @@ struct Engine::Impl {
     build_synapses();
     build_streams();
     build_plan();
+    build_arena();
     compile_module();
     if (!opt.dry_run) B2_CUDA(cudaStreamSynchronize(stream));
     st.launches_per_tick = ops.size();

@@ -78,9 +78,22 @@ def test_delayed_receive_moves_after_the_delivery(pkg, tmp_path, monkeypatch):
     assert names.index("neurons_receive") == names.index("neurons_step") + 1
 
 
+def test_multi_gpu_synapse_programs_and_presynaptic_replicas(pkg, tmp_path):
+    """Synaptic state updates and run_regularly run over each rank's own
+    edges; a summed variable that reads the presynaptic v of a partitioned
+    population (gap junctions) reads a replica that a replicate kernel and a
+    bounded wait refresh right before it (the reference's MPI path keeps
+    read-only presynaptic replicas, distributed.py:255)."""
+    names = kernels(pkg.codegen(model_file("synapse_updates_small", tmp_path).read_bytes(), rank=1, world_size=2))
+    assert [n.split("_", 2)[2] for n in names][:3] == ["decay", "inputs_step_neurons_step", "stdp_stateupdater"]
+    src = pkg.codegen(model_file("gap_junctions_small", tmp_path).read_bytes(), rank=1, world_size=3)
+    names = [n.split("_", 2)[2] for n in kernels(src)]
+    assert names[1:4] == ["neurons_v_replicate", "neurons_v_replica_wait", "gaps_summed_variable_Igap_post"]
+    summed = src[src.index("gaps_summed_variable_Igap_post(RunCtl"):]
+    assert "__ldcg(" in summed[:summed.index("\n}\n")] or "__ldcg(" in src[:src.index("gaps_summed_variable_Igap_post(RunCtl")]
+
+
 def test_multi_gpu_capability_errors(pkg, tmp_path):
-    with pytest.raises(pkg.B2GpuError, match="on_pre and on_post pathways only"):
-        pkg.codegen(model_file("synapse_updates_small", tmp_path).read_bytes(), rank=0, world_size=2)
     with pytest.raises(pkg.B2GpuError, match="EventMonitor variables"):
         pkg.codegen(model_file("event_variables_small", tmp_path).read_bytes(), rank=0, world_size=2)
     from conftest import golden_procedural_initializers
@@ -213,7 +226,8 @@ def test_ranks_match_oracle(pkg, oracle, tmp_path, monkeypatch, world, fuse):
     c2 = tmp_path / "c2_20k.json"
     c2.write_bytes(synthetic.encode(synthetic.cuba_fixed_indegree(template, n=20000, indegree=1000, ticks=300,
                                                                   seed=9)))
-    models = [model_file(n, tmp_path) for n in ["cuba_small", "cuba_poisson_small", "brunel_small"]]
+    models = [model_file(n, tmp_path) for n in ["cuba_small", "cuba_poisson_small", "brunel_small",
+                                                "synapse_updates_small", "gap_junctions_small"]]
     models += [GOLDEN / "reference-v1" / "model.json", c2]
     args = []
     for k, m in enumerate(models):

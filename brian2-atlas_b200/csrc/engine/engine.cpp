@@ -1818,10 +1818,11 @@ struct Engine::Impl {
           << es.x_base[size_t(q)] << "ull + (u64)(p - " << pair_start[size_t(q)] << "u) * " << es.x_tile_n[size_t(q)] + 1
           << "ull;\n";
       o << "  };\n";
-      o << "  auto count_of = [&](u32 p) -> u32 { return poisoned ? 0u : b2_ll_wait(inbox + slot(p), tag, " << timeout_ns
-        << "ull, err); };\n";
-      o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return poisoned ? 0u : b2_ll_wait(inbox + slot(p) + 1ull + k, tag, "
-        << timeout_ns << "ull, err); };\n";
+      // a thread whose wait has expired waits no more (the run is failed)
+      o << "  auto count_of = [&](u32 p) -> u32 { return poisoned || (err & " << kErrExchange
+        << "u) ? 0u : b2_ll_wait(inbox + slot(p), tag, " << timeout_ns << "ull, err); };\n";
+      o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return poisoned || (err & " << kErrExchange
+        << "u) ? 0u : b2_ll_wait(inbox + slot(p) + 1ull + k, tag, " << timeout_ns << "ull, err); };\n";
     } else {
       o << "  auto count_of = [&](u32 p) -> u32 { return __ldcg(" << P(es.tile_count, "const u32") << " + p); };\n";
       o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return __ldcg(" << P(es.stage, "const u32") << " + (u64)p * "

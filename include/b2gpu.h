@@ -128,9 +128,11 @@ int b2g_codegen(const char* json, size_t json_len, const b2g_options* options, c
 /* ---- multi-GPU ------------------------------------------------------------
  * Replaces the reference's MPI exchange (brian2_rust/mpi_runtime/bridge.c:
  * 74-101: MPI_Allgather of counts + MPI_Allgatherv of global spike ids every
- * tick, rank 0 writing the results).  Here each engine's tick kernels store
- * their spike words straight into every peer GPU's memory over NVLink, so the
- * host only takes part once, to trade IPC handles:
+ * tick, rank 0 writing the results).  Here each engine's step kernel stores
+ * every tile's spike list straight into every peer GPU's memory over NVLink
+ * (and, where synaptic code reads a partitioned population's state, a
+ * replicate kernel copies it the same way), so the host only takes part
+ * once, to trade IPC handles:
  *   1. every rank: b2g_create with rank/world_size, then b2g_ipc_handle;
  *   2. the caller all-gathers the handles (any host transport: MPI, a
  *      torch.distributed store, ...) and every rank calls b2g_connect;

@@ -454,6 +454,9 @@ struct Engine::Impl {
     // Diagnostic: deliver constant-addend pathways into f32 state with a
     // compare-and-swap per event instead of counted delivery (same results).
     if (const char* e = std::getenv("B2GPU_COUNTED")) counted_ = std::atoi(e) != 0;
+    // Diagnostic: constant-addend scatter items per block, one row entry per
+    // thread, instead of per warp (same results).
+    if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
     if (const char* e = std::getenv("B2GPU_TILE")) tile_override_ = size_t(std::atoll(e));
     check(tile_override_ % 32 == 0 && tile_override_ <= size_t(kThreads) * 32, "B2GPU_TILE must be a multiple of 32 up to 8192");
     if (const char* e = std::getenv("B2GPU_SCATTER_UNROLL")) scatter_unroll_ = unsigned(std::atoi(e));
@@ -482,6 +485,7 @@ struct Engine::Impl {
   }
   bool no_fuse_ = false;
   bool counted_ = true;  // counted delivery of constant-addend pathways into f32 state
+  bool scatter_warp_ = true;  // constant-addend scatter items per warp (else per block)
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
   bool fuse_steps_ = true;   // one launch for consecutive step kernels of different populations
   unsigned targets_unroll_ = 4;  // 32-entry groups each warp of a target-ordered kernel keeps in flight
@@ -2482,20 +2486,32 @@ struct Engine::Impl {
     return o.str();
   }
 
+  // Constant-addend scatter of one or more pathways on one spike stream:
+  // work item = (fired source, 256-entry row chunk).  Items go to warps (a
+  // block holds eight independent ring -> row bounds -> row -> update chains,
+  // each lane loading its eight entries before applying them); with
+  // B2GPU_SCATTER_WARP=0 to whole blocks, one entry per thread.
   std::string gen_atomic_kernel(const std::string& name, const std::vector<PathwayDev*>& pws) {
     const PathwayDev& p0 = *pws.front();
     const EventStreamDev& es = streams[size_t(p0.stream)];
     const size_t endpoint_count = m.populations[p0.endpoint_pop].count;
+    const bool per_warp = scatter_warp_;
+    const uint64_t span = per_warp ? 256 : row_chunk();
     uint64_t chunks = 1;
-    for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + row_chunk() - 1) / row_chunk());
+    for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + span - 1) / span);
     std::ostringstream o;
     o << kernel_head(name);
     o << "  if ((i64)rel - " << p0.delay << "ll < 0) return;\n  const u64 te = rel - " << p0.delay << "ull;\n";
     o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
     o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
+    o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
     for (size_t k = 0; k < pws.size(); ++k) o << "  u64 events" << k << " = 0;\n";
     o << "  const u64 items = (b - a) * " << chunks << "ull;\n";
-    o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
+    if (per_warp)
+      o << "  for (u64 w = (u64)blockIdx.x * " << kThreads / 32 << "u + warp; w < items; w += (u64)gridDim.x * "
+        << kThreads / 32 << "u) {\n";
+    else
+      o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
     o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
     o << "    const u32 s = __ldg(ring + (j & " << u64lit(es.mask) << "));\n";
     for (size_t k = 0; k < pws.size(); ++k) {
@@ -2507,16 +2523,16 @@ struct Engine::Impl {
       o << "      const u32* other = " << P(pw.row_other, "const u32") << ";\n";
       o << "      const u32 ep = s - " << lo << "u;\n";
       o << "      const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
-      o << "      if (c == 0 && threadIdx.x == 0) events" << k << " += r1 - r0;\n";
-      o << "      const u64 q0 = r0 + c * " << row_chunk() << "ull;\n";
-      o << "      const u64 q1 = q0 + " << row_chunk() << "ull < r1 ? q0 + " << row_chunk() << "ull : r1;\n";
-      o << emit_atomic_chunk(pw, "      ");
+      o << "      if (c == 0 && " << (per_warp ? "lane" : "threadIdx.x") << " == 0) events" << k << " += r1 - r0;\n";
+      o << "      const u64 q0 = r0 + c * " << span << "ull;\n";
+      o << "      const u64 q1 = q0 + " << span << "ull < r1 ? q0 + " << span << "ull : r1;\n";
+      o << (per_warp ? emit_warp_chunk(pw, "      ") : emit_atomic_chunk(pw, "      "));
       o << "    }\n";
     }
     o << "  }\n";
     for (size_t k = 0; k < pws.size(); ++k)
-      o << "  if (threadIdx.x == 0 && events" << k << ") atomicAdd((unsigned long long*)" << P(delivered_ptr, "u64")
-        << " + " << pws[k]->delivered_slot << ", events" << k << ");\n";
+      o << "  if (" << (per_warp ? "lane" : "threadIdx.x") << " == 0 && events" << k << ") atomicAdd((unsigned long long*)"
+        << P(delivered_ptr, "u64") << " + " << pws[k]->delivered_slot << ", events" << k << ");\n";
     o << kernel_tail();
     return o.str();
   }

@@ -261,14 +261,16 @@ def test_bucket_delivery_of_crowded_targets(pkg, tmp_path, monkeypatch):
     assert_same_files(tmp_path / "gpu1", tmp_path / "gpu0")
 
 
-@pytest.mark.parametrize("counted", ["0", "1"])
-def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, monkeypatch, counted):
+@pytest.mark.parametrize("counted,warp", [("0", "1"), ("1", "1"), ("1", "0")])
+def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, monkeypatch, counted, warp):
     """Brunel's f32 constant-addend pathways delivered by per-event
-    compare-and-swap (0) or counted per target and applied by the
-    PoissonInput kernel (1, the default): both byte-identical to the oracle,
-    on the fixture and on a fixed in-degree variant at 20k neurons."""
+    compare-and-swap (counted=0) or counted per target and applied by the
+    PoissonInput kernel (counted=1, the default), with scatter items per warp
+    (the default) or per block: all byte-identical to the oracle, on the
+    fixture and on a fixed in-degree variant at 20k neurons."""
     import importlib
     monkeypatch.setenv("B2GPU_COUNTED", counted)
+    monkeypatch.setenv("B2GPU_SCATTER_WARP", warp)
     synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
     template = json.loads((MODELS / "brunel_small.json").read_text())
     big = tmp_path / "brunel_20k.json"
@@ -278,3 +280,20 @@ def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, 
         gpu_run(pkg, path, tmp_path / f"gpu{k}")
         run_oracle(oracle, path, tmp_path / f"ref{k}")
         assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}")
+
+
+@pytest.mark.parametrize("warp", ["0", "1"])
+def test_unfused_scatter_matches_oracle(pkg, oracle, tmp_path, monkeypatch, warp):
+    """Config 2's shape at 20k neurons with the step laying out its own list
+    (B2GPU_FUSE_EXCHANGE=0) and a separate f64 constant-addend scatter, items
+    per block (0) or per warp (1): byte-identical to the oracle."""
+    import importlib
+    monkeypatch.setenv("B2GPU_FUSE_EXCHANGE", "0")
+    monkeypatch.setenv("B2GPU_SCATTER_WARP", warp)
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    template = json.loads((MODELS / "cuba_poisson_small.json").read_text())
+    path = tmp_path / "c2_20k.json"
+    path.write_bytes(synthetic.encode(synthetic.cuba_fixed_indegree(template, n=20000, indegree=1000, ticks=300, seed=9)))
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref")

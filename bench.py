@@ -349,6 +349,8 @@ def main():
     ap.add_argument("--neurons", type=int, default=None)
     ap.add_argument("--indegree", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--chunk-ticks", type=int, default=0, help="ticks per CUDA-graph replay (0: the engine default)")
+    ap.add_argument("--no-graphs", action="store_true", help="launch every kernel directly (diagnostics)")
     args = ap.parse_args()
     w = WORKLOADS[args.workload]
     if args.neurons is None:
@@ -397,11 +399,12 @@ def main():
     t0 = time.time()
     model = build_workload(args, total_ticks + 400)
     t_json = time.time() - t0
+    eopt = dict(chunk_ticks=args.chunk_ticks, use_graphs=not args.no_graphs)
     if dist is not None:
-        eng = pkg.Engine(model, device=local_rank, rank=rank, world_size=world)
+        eng = pkg.Engine(model, device=local_rank, rank=rank, world_size=world, **eopt)
         distributed.connect(eng)
     else:
-        eng = pkg.Engine(model, device=local_rank)
+        eng = pkg.Engine(model, device=local_rank, **eopt)
     del model
     n_pops = 2 if stdp else 1
     state_pop = 1 if stdp else 0

@@ -99,7 +99,7 @@ WORKLOADS = {
 # 300 (a smaller device footprint) stands for the full network.  The per-tick
 # neuron state (56 MB) stays L2-resident within a bench step, so DRAM carries
 # ~1 % of the algorithmic bytes.  None where no capture exists.
-TRAFFIC = {("c2", "_step", 1): 74_624 + 507_904}
+TRAFFIC = {("c2", "_step", 1): 34_048 + 14_251}
 
 
 def peaks():

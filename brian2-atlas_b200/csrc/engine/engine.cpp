@@ -448,6 +448,8 @@ struct Engine::Impl {
     // Diagnostic: plain stream-ordered launches instead of programmatic
     // dependent launches (same results) for A/B timing.
     if (const char* e = std::getenv("B2GPU_PDL")) use_pdl_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_PDL_TRIGGER")) pdl_trigger_end_ = std::string(e) == "end";
+    if (const char* e = std::getenv("B2GPU_CONSUMER_BLOCKS")) consumer_blocks_ = unsigned(std::atoi(e));
     // Tuning knobs (same results): wave-balanced neuron tiles, and row
     // entries per thread in constant-addend scatters (1..8).
     if (const char* e = std::getenv("B2GPU_BALANCE")) balance_tiles_ = std::atoi(e) != 0;
@@ -486,6 +488,7 @@ struct Engine::Impl {
   bool no_fuse_ = false;
   bool counted_ = true;  // counted delivery of constant-addend pathways into f32 state
   bool scatter_warp_ = true;  // constant-addend scatter items per warp (else per block)
+  unsigned consumer_blocks_ = 0;  // B2GPU_CONSUMER_BLOCKS: scatter blocks of a fused list consumer (0: the scatter's grid)
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
   bool fuse_steps_ = true;   // one launch for consecutive step kernels of different populations
   unsigned targets_unroll_ = 4;  // 32-entry groups each warp of a target-ordered kernel keeps in flight
@@ -493,6 +496,7 @@ struct Engine::Impl {
   bool targets_smem_bitmap_ = true;  // stage the fired bitmap slot in shared memory
   bool targets_scan_ = false;        // scan variant also for single-delay pathways
   bool use_pdl_ = true;
+  bool pdl_trigger_end_ = false;  // B2GPU_PDL_TRIGGER=end: trigger dependents after a block's work
   bool balance_tiles_ = true;                // tile_n_for: spread small populations over a whole wave
   size_t tile_override_ = 0;                 // B2GPU_TILE: neurons per tile (multiple of 32)
   // Multi-GPU: the receiving kernel of an exchanged stream also delivers the
@@ -1505,14 +1509,21 @@ struct Engine::Impl {
   std::string kernel_head(const std::string& name, unsigned min_blocks = 0) {
     std::string bounds = std::to_string(kThreads) + (min_blocks ? ", " + std::to_string(min_blocks) : "");
     return "extern \"C\" __global__ void __launch_bounds__(" + bounds + ") " + name +
-           "(RunCtl* __restrict__ ctl, u32 k) {\n  u32 err = 0;\n"
-           "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n"
+           "(RunCtl* __restrict__ ctl, u32 k) {\n  u32 err = 0;\n" +
+           std::string(pdl_trigger_end_ ? "" : "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n") +
            "  const u64 tick = ctl->tick_base + k;\n"
            "  asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");\n"
            "  const u64 rel = tick - " + u64lit(start_tick) + ";\n  const double t = (double)tick * " +
            double_literal(dt) + ";\n  (void)rel; (void)t;\n";
   }
-  static std::string kernel_tail() { return "  if (err) atomicOr(&ctl->error, err);\n}\n"; }
+  // With pdl_trigger_end_ a block lets the dependent grid launch only when it
+  // has done its work (a block that returns early counts as triggered when it
+  // exits), so waiting blocks of the next kernel do not hold SM slots for the
+  // whole of a long kernel.
+  std::string kernel_tail() const {
+    return std::string(pdl_trigger_end_ ? "  asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");\n" : "") +
+           "  if (err) atomicOr(&ctl->error, err);\n}\n";
+  }
 
   // ================================================================ step kernels
   // Population step: optional update U, optional threshold X (with ascending
@@ -3475,6 +3486,7 @@ struct Engine::Impl {
         c.index = size_t(sid);
         c.base += "_atomic";
         c.lb = 2;  // ~ a few hundred ids per tick at config 2
+        if (consumer_blocks_) c.grid = consumer_blocks_;
         c.grid += c.lb;
       }
     }

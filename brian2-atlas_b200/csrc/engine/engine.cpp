@@ -448,7 +448,7 @@ struct Engine::Impl {
     // Diagnostic: plain stream-ordered launches instead of programmatic
     // dependent launches (same results) for A/B timing.
     if (const char* e = std::getenv("B2GPU_PDL")) use_pdl_ = std::atoi(e) != 0;
-    if (const char* e = std::getenv("B2GPU_PDL_TRIGGER")) pdl_trigger_end_ = std::string(e) == "end";
+    if (const char* e = std::getenv("B2GPU_PDL_TRIGGER")) pdl_trigger_end_ = std::string(e) != "start";
     if (const char* e = std::getenv("B2GPU_CONSUMER_BLOCKS")) consumer_blocks_ = unsigned(std::atoi(e));
     // Tuning knobs (same results): wave-balanced neuron tiles, and row
     // entries per thread in constant-addend scatters (1..8).
@@ -496,7 +496,7 @@ struct Engine::Impl {
   bool targets_smem_bitmap_ = true;  // stage the fired bitmap slot in shared memory
   bool targets_scan_ = false;        // scan variant also for single-delay pathways
   bool use_pdl_ = true;
-  bool pdl_trigger_end_ = false;  // B2GPU_PDL_TRIGGER=end: trigger dependents after a block's work
+  bool pdl_trigger_end_ = true;  // trigger dependents after a block's work (B2GPU_PDL_TRIGGER=start: before)
   bool balance_tiles_ = true;                // tile_n_for: spread small populations over a whole wave
   size_t tile_override_ = 0;                 // B2GPU_TILE: neurons per tile (multiple of 32)
   // Multi-GPU: the receiving kernel of an exchanged stream also delivers the
@@ -1500,12 +1500,16 @@ struct Engine::Impl {
   }
 
   // Every tick kernel is launched as a programmatic dependent of the previous
-  // one: it lets its own dependent launch as soon as all its blocks are
-  // running (launch_dependents), reads the host-written tick cursor, and only
-  // then waits for its predecessor grid to complete and flush
-  // (griddepcontrol.wait) before touching any other memory.  Launch latency
-  // and block rasterisation overlap the predecessor's tail; without the
-  // launch attribute the wait returns at once.
+  // one: it reads the host-written tick cursor, then waits for its
+  // predecessor grid to complete and flush (griddepcontrol.wait) before
+  // touching any other memory, and each of its blocks lets the next kernel
+  // launch once it has done its work (launch_dependents in kernel_tail).
+  // Launch latency and block rasterisation overlap the predecessor's tail;
+  // without the launch attribute the wait returns at once.  Triggering at
+  // the start instead (B2GPU_PDL_TRIGGER=start) let the next kernel's waiting
+  // blocks hold SM slots through long kernels: config 3 ran 430 ms per 1000
+  // ticks that way, 248 with the trigger at the end and 251 without PDL;
+  // config 2 18.20 / 18.23 / 19.20.
   std::string kernel_head(const std::string& name, unsigned min_blocks = 0) {
     std::string bounds = std::to_string(kThreads) + (min_blocks ? ", " + std::to_string(min_blocks) : "");
     return "extern \"C\" __global__ void __launch_bounds__(" + bounds + ") " + name +

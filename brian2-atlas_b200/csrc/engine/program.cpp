@@ -1013,7 +1013,9 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
                   std::string name = "b2_btab_" + std::to_string(ctx.tables->size());
                   for (const auto& [nm, def] : *ctx.tables)
                     if (def.find("{" + body + "}") != std::string::npos) name = nm;
-                  (*ctx.tables)[name] = "__constant__ double " + name + "[" + std::to_string(K) + "] = {" + body + "};";
+                  // global memory read through L1: lanes of a warp stop at
+                  // different x, which the constant cache would serialise
+                  (*ctx.tables)[name] = "__device__ const double " + name + "[" + std::to_string(K) + "] = {" + body + "};";
                   expr = "b2_binomial_tab(" + head + ", " + std::to_string(in.n) + "ull, " + name + ", " +
                          std::to_string(K) + "u, " + (reverse ? "true" : "false") + ")";
                 } else {

@@ -159,7 +159,7 @@ __device__ __forceinline__ double b2_binomial_tab(u64 seed, u64 stream, u64 tick
   for (int restarts = 0; restarts < 1 << 16; ++restarts) {
     double u = b2_uniform_draw(seed, stream, tick, index, draw);
     for (u32 x = 0; x < K; ++x) {
-      const double px = tab[x];
+      const double px = __ldg(tab + x);
       if (u <= px) return (double)(reverse ? n - x : x);
       u -= px;
     }

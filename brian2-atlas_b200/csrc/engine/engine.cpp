@@ -1535,7 +1535,8 @@ struct Engine::Impl {
   std::string gen_pop_step(const std::string& name, size_t p, const Program* U, const Program* X, size_t x_event,
                            bool x_is_spike, const Program* R, const std::vector<const Program*>& deferred = {},
                            bool flush = false, bool as_fn = false, const std::vector<PathwayDev*>& applies = {},
-                           const Program* post_R = nullptr) {
+                           const Program* post_R = nullptr, const std::vector<PathwayDev*>& deferred_applies = {},
+                           const Program* deferred_post_R = nullptr) {
     // One block owns a tile of tile_n consecutive neurons (whole 32-neuron
     // words) and walks it in chunks of kThreads * npt neurons; in a chunk,
     // thread t handles neurons chunk_base + kk*kThreads + t for kk < npt: all
@@ -1566,10 +1567,12 @@ struct Engine::Impl {
     const bool ragged = tile_n % kThreads != 0 || tile_n % chunk_n != 0;
     const std::string in_tile = ragged ? slot_off + " + threadIdx.x < " + std::to_string(tile_n) + "u && " : "";
     std::vector<const Program*> progs(deferred.begin(), deferred.end());
-    for (const Program* pr : {U, X, R, post_R})
+    for (const Program* pr : {U, X, R, post_R, deferred_post_R})
       if (pr) progs.push_back(pr);
     std::set<size_t> used = slots_used(progs), written = slots_written(progs);
-    for (const PathwayDev* pw : applies)
+    std::vector<PathwayDev*> all_applies(deferred_applies.begin(), deferred_applies.end());
+    all_applies.insert(all_applies.end(), applies.begin(), applies.end());
+    for (const PathwayDev* pw : all_applies)
       for (const auto& ad : pw->atomic_adds) {
         used.insert(ad.state);
         written.insert(ad.state);
@@ -1596,7 +1599,8 @@ struct Engine::Impl {
       o << "  u32 fired_bits = 0;  // bit ch * " << npt << " + kk: this thread's slot fired\n";
     }
     o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
-    if (!deferred.empty()) {
+    const bool any_deferred = !deferred.empty() || !deferred_applies.empty() || deferred_post_R;
+    if (any_deferred) {
       o << "  const bool run_deferred = rel > 0 && " << P(deferred_flags, "const u64") << "[" << p << "] != tick - 1;\n";
       o << "  const u64 tick_prev = tick - 1;\n  const double t_prev = (double)tick_prev * " << double_literal(dt) << ";\n";
       o << "  (void)t_prev;\n";
@@ -1609,12 +1613,14 @@ struct Engine::Impl {
       o << "  " << ct << " sva" << s << "[" << npt << "];\n";
     }
     if (read_refr) o << "  double lsa[" << npt << "];\n  u8 nra[" << npt << "];\n";
-    for (size_t a = 0; a < applies.size(); ++a) o << "  u32 cna" << a << "[" << npt << "];\n";
+    // event counters of the counted applies: the previous tick's (deferred)
+    // first, then this tick's
+    for (size_t a = 0; a < all_applies.size(); ++a) o << "  u32 cna" << a << "[" << npt << "];\n";
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
     o << "    const u32 i = tile * " << tile_n << "u + " << slot_off << " + threadIdx.x;\n";
     o << "    if (" << in_tile << "i < " << pd.count << "u) {\n";
-    for (size_t a = 0; a < applies.size(); ++a)
-      o << "      cna" << a << "[kk] = __ldcg(" << P(applies[a]->count_ptr, "const u32") << " + i);\n";
+    for (size_t a = 0; a < all_applies.size(); ++a)
+      o << "      cna" << a << "[kk] = __ldcg(" << P(all_applies[a]->count_ptr, "const u32") << " + i);\n";
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "      sva" << s << "[kk] = " << ld(pops[p].states[s].ptr, ct) << ";\n";
@@ -1634,31 +1640,40 @@ struct Engine::Impl {
     o << "  if (active) {\n";
     for (size_t s : used) o << "  " << storage_ctype(def.states[s].dtype) << " sv" << s << " = sva" << s << "[kk];\n";
     if (read_refr) o << "  double ls = lsa[kk];\n  u8 nr = nra[kk];\n  (void)ls;\n";
-    for (size_t d = 0; d < deferred.size(); ++d) {
-      std::string pre = "d" + std::to_string(d) + "_";
-      o << "  if (run_deferred) {\n" << emit_program(*deferred[d], prev_ctx, pre) << commits(*deferred[d], p, pre) << "  }\n";
-    }
-    // counted deliveries of this tick (in schedule order): the pathway's map
-    // applied as often as events reached this neuron, each result rounded to
-    // the storage type and checked finite like one delivery of the
-    // reference's (executor.rs:2166-2251 per event); the gate is the target's
-    // not_refractory as stored by this tick's threshold
-    for (size_t a = 0; a < applies.size(); ++a) {
-      const PathwayDev* pw = applies[a];
-      o << "  { const u32 n_ev = cna" << a << "[kk];\n";
-      o << "    if (n_ev) {\n      " << P(pw->count_ptr, "u32") << "[i] = 0u;\n";
-      o << "      for (u32 r = 0; r < n_ev; ++r) {\n";
+    // counted deliveries (in schedule order): the pathway's map applied as
+    // often as events reached this neuron, each result rounded to the
+    // storage type and checked finite like one delivery of the reference's
+    // (executor.rs:2166-2251 per event); the gate is the target's
+    // not_refractory as stored by the delivering tick's threshold
+    auto emit_apply = [&](size_t a, const std::string& cond) {
+      const PathwayDev* pw = all_applies[a];
+      o << "  if (" << cond << "cna" << a << "[kk]) {\n    const u32 n_ev = cna" << a << "[kk];\n";
+      o << "    " << P(pw->count_ptr, "u32") << "[i] = 0u;\n";
+      o << "    for (u32 r = 0; r < n_ev; ++r) {\n";
       for (const auto& ad : pw->atomic_adds) {
         const std::string v = "sv" + std::to_string(ad.state);
-        o << "        " << (ad.gated ? "if (nr) { " : "{ ");
+        o << "      " << (ad.gated ? "if (nr) { " : "{ ");
         if (def.states[ad.state].dtype == DType::F64)
           o << v << " = " << v << " + " << double_literal(ad.addend) << ";";
         else
           o << v << " = (float)((double)" << v << " + " << double_literal(ad.addend) << ");";
         o << " if (!b2_finite((double)" << v << ")) err |= " << kErrNonfinite << "u; }\n";
       }
-      o << "      }\n    }\n  }\n";
+      o << "    }\n  }\n";
+    };
+    // the previous tick's trailing dense kernel, in its order: its applies,
+    // its program, its reset of the lanes that tick fired
+    for (size_t a = 0; a < deferred_applies.size(); ++a) emit_apply(a, "run_deferred && ");
+    for (size_t d = 0; d < deferred.size(); ++d) {
+      std::string pre = "d" + std::to_string(d) + "_";
+      o << "  if (run_deferred) {\n" << emit_program(*deferred[d], prev_ctx, pre) << commits(*deferred[d], p, pre) << "  }\n";
     }
+    if (deferred_post_R) {
+      check(read_refr, "deferred reset without lastspike");
+      o << "  if (run_deferred && ls == t_prev) {\n" << emit_program(*deferred_post_R, prev_ctx, "dr_")
+        << commits(*deferred_post_R, p, "dr_") << "  }\n";
+    }
+    for (size_t a = deferred_applies.size(); a < all_applies.size(); ++a) emit_apply(a, "");
     if (U) {
       if (refr && pd.fixed_refractory && !flush) {
         // timestep(t - lastspike, dt) >= period (model.rs:981-992) is monotone
@@ -2903,6 +2918,11 @@ struct Engine::Impl {
     std::vector<const Program*> deferred;  // previous tick's trailing neuron maps
     std::vector<PathwayDev*> applies;      // counted pathways of this tick, applied first, in order
     const Program* post_R = nullptr;       // spike reset of this tick, on lanes whose lastspike is t
+    // the previous tick's trailing dense kernel, run in this kernel's
+    // prologue: its counted applies, then its program (in `deferred`), then
+    // its reset on lanes whose lastspike is the previous tick's t
+    std::vector<PathwayDev*> deferred_applies;
+    const Program* deferred_post_R = nullptr;
     size_t node_pos = 0;
   };
   struct PathSpec {
@@ -2923,7 +2943,15 @@ struct Engine::Impl {
     int reads = -1;                   // Text ops: the event stream whose lists they read
     unsigned lb = 1;                  // list consumers: blocks that lay the list out in the ring
   };
-  std::vector<std::pair<size_t, const Program*>> flushes;  // (population, deferred program)
+  // Deferred work of a population's last tick that a flush kernel applies at
+  // the end of a run or before a state read.
+  struct Flush {
+    size_t pop = 0;
+    const Program* program = nullptr;
+    std::vector<PathwayDev*> applies;
+    const Program* post_R = nullptr;
+  };
+  std::vector<Flush> flushes;
   std::vector<SummedSpec> summed_specs;
   struct SynProgSpec {
     size_t synapse = 0;
@@ -3225,7 +3253,7 @@ struct Engine::Impl {
               }
               if (defer) {
                 steps_[it->second].deferred.push_back(pr);
-                flushes.push_back({p, pr});
+                flushes.push_back({p, pr, {}, nullptr});
               } else {
                 StepSpec st;
                 st.pop = p;
@@ -3560,6 +3588,35 @@ struct Engine::Impl {
         specs.insert(specs.begin() + long(j - 1), moved);  // i now holds the next unvisited op
       }
     }
+    // The tick's last dense kernel of a population (after it only list
+    // layout or receive kernels, which touch no population state), when the
+    // tick's first kernel is that population's state-update step: nothing
+    // runs between the two, so the dense kernel's work -- its counted
+    // applies, its program, its reset of the lanes the tick fired -- moves
+    // into the step's prologue, with the previous tick's t and RNG counter
+    // (config 3: the PoissonInput kernel).  A flush kernel applies the last
+    // tick's copy at the end of a run or before a state read.
+    if (!no_fuse_ && specs.size() >= 2) {
+      size_t last = specs.size();
+      while (last > 0 && specs[last - 1].text == "exchange" && specs[last - 1].fuse_path < 0) --last;
+      if (last >= 2 && specs[last - 1].kind == OpSpec::Kind::Step && specs[0].kind == OpSpec::Kind::Step) {
+        const StepSpec T = steps_[specs[last - 1].index];
+        StepSpec& S = steps_[specs[0].index];
+        if (T.pop == S.pop && T.U && !T.X && !T.R && T.deferred.empty() && T.deferred_applies.empty() &&
+            !T.deferred_post_R && S.U && S.deferred.empty() && S.deferred_applies.empty() && !S.deferred_post_R &&
+            specs[last - 1].fused_steps.empty() && specs[0].fused_steps.empty()) {
+          S.deferred.push_back(T.U);
+          S.deferred_applies = T.applies;
+          S.deferred_post_R = T.post_R;
+          flushes.push_back({T.pop, T.U, T.applies, T.post_R});
+          if (deferred_flags < 0) {
+            std::vector<uint64_t> init(m.populations.size(), UINT64_MAX);
+            deferred_flags = upload(init.data(), init.size() * 8);
+          }
+          specs.erase(specs.begin() + long(last - 1));
+        }
+      }
+    }
     // Consecutive step kernels of different populations touch disjoint state
     // (population code reads and writes only its own population), so one
     // launch steps them all: block ranges dispatch to per-population tiles,
@@ -3639,7 +3696,7 @@ struct Engine::Impl {
           if (o.fused_steps.empty()) {
             const StepSpec& st = steps_[o.index];
             kernels << gen_pop_step(nm, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred, false, false,
-                                    st.applies, st.post_R);
+                                    st.applies, st.post_R, st.deferred_applies, st.deferred_post_R);
             break;
           }
           std::vector<size_t> group{o.index};
@@ -3650,7 +3707,7 @@ struct Engine::Impl {
             const StepSpec& st = steps_[group[g]];
             const std::string fn = nm + "_part" + std::to_string(g);
             kernels << gen_pop_step(fn, st.pop, st.U, st.X, st.x_event, st.x_spike, st.R, st.deferred, false, true,
-                                    st.applies, st.post_R);
+                                    st.applies, st.post_R, st.deferred_applies, st.deferred_post_R);
             const uint64_t tiles = tiles_for(pops[st.pop].count);
             disp << "  " << (g ? "else if" : "if") << " (blockIdx.x < " << first + tiles << "u) " << fn
                  << "(ctl, tick, rel, t, blockIdx.x - " << first << "u, err);\n";
@@ -3683,9 +3740,10 @@ struct Engine::Impl {
       ops.push_back({nm, nullptr, o.grid, o.block});
     }
     for (size_t f = 0; f < flushes.size(); ++f) {
-      size_t p = flushes[f].first;
+      size_t p = flushes[f].pop;
       std::string nm = "b2_flush_" + std::to_string(f) + "_" + sanitize(m.populations[p].name);
-      kernels << gen_pop_step(nm, p, flushes[f].second, nullptr, 0, false, nullptr, {}, true);
+      kernels << gen_pop_step(nm, p, flushes[f].program, nullptr, 0, false, nullptr, {}, true, false, flushes[f].applies,
+                              flushes[f].post_R);
       flush_ops.push_back({nm, nullptr, unsigned(tiles_for(pops[p].count)), kThreads});
     }
     for (const auto& [name, def] : const_tables) src << def << "\n";

@@ -55,9 +55,10 @@ def load(name):
     # runs in the next step's prologue (plus a flush kernel for the last tick)
     ("cuba_poisson_small", ["step", "exc_pre_inh_pre_atomic", "flush_0_neurons"]),
     # both pathways write f32 v (order matters): counted delivery, both
-    # counts in one launch, applied E then I by the PoissonInput kernel, which
-    # also resets the lanes the tick fired
-    ("brunel_small", ["step", "excitatory_synapses_pre_inhibitory_synap_atomic", "poisson_input"]),
+    # counts in one launch, applied E then I by the PoissonInput work, which
+    # also resets the lanes the tick fired; that work, the tick's last, runs
+    # in the next tick's step prologue (plus a flush kernel for the last tick)
+    ("brunel_small", ["step", "excitatory_synapses_pre_inhibitory_synap_atomic", "flush_0_neurons"]),
     ("cobahh_small", ["step", "exc_pre_inh_pre_atomic"]),
     # the two populations step in one launch; on_pre writes the target's
     # conductance and the edge's weight and traces: target-ordered delivery
@@ -220,22 +221,22 @@ def test_no_cpu_fallback(pkg, tmp_path):
 
 def test_counted_delivery_plan(pkg, monkeypatch):
     """Brunel (f32 membrane, E then I constant-addend pathways, then the
-    PoissonInput kernel): the two scatters only count events per target, in
-    one launch, and the PoissonInput kernel applies E's then I's map that
-    many times before its own program; B2GPU_COUNTED=0 keeps one
-    compare-and-swap scatter per pathway."""
+    PoissonInput): the two scatters only count events per target, in one
+    launch; the PoissonInput work applies E's then I's map that many times
+    before its own draw and resets the lanes the tick fired, and as the tick's
+    last dense work it runs in the next tick's step prologue;
+    B2GPU_COUNTED=0 keeps one compare-and-swap scatter per pathway."""
     import re
     src = pkg.codegen(load("brunel_small"))
     names = [n.split("_", 2)[2] for n in re.findall(r"__global__ void __launch_bounds__\([^)]*\) (\w+)", src)]
     assert len([n for n in names if n.endswith("_atomic")]) == 1 and "b2_atomic_add_f32_via_f64(" not in src.split(
         "__constant__ u64 g_ptr")[1]
-    poisson = src[src.index("_neurons_poisson_input(RunCtl"):]
-    poisson = poisson[:poisson.index("\n}\n")]
-    applies = [m.start() for m in re.finditer(r"const u32 n_ev = cna", poisson)]
-    assert len(applies) == 2 and applies[-1] < poisson.index("b2_binomial_tab")
-    # the spike reset runs in the same kernel, after the drive, on the lanes
-    # the tick's threshold fired
-    assert "neurons_reset" not in names and poisson.index("if (ls == t)") > poisson.index("b2_binomial_tab")
+    step = src[src.index("_neurons_step(RunCtl"):]
+    step = step[:step.index("\n}\n")]
+    applies = [m.start() for m in re.finditer(r"if \(run_deferred && cna", step)]
+    draw = step.index("b2_binomial_tab")
+    assert len(applies) == 2 and applies[-1] < draw < step.index("ls == t_prev") < step.index("d_ls = t - ls")
+    assert "neurons_reset" not in names and "neurons_poisson_input" not in names
     monkeypatch.setenv("B2GPU_COUNTED", "0")
     src = pkg.codegen(load("brunel_small"))
     names = [n.split("_", 2)[2] for n in re.findall(r"__global__ void __launch_bounds__\([^)]*\) (\w+)", src)]

@@ -71,10 +71,10 @@ def test_delayed_receive_moves_after_the_delivery(pkg, tmp_path, monkeypatch):
     with no fusion at all (one kernel per node) it stays right after the
     step."""
     data = (MODELS / "brunel_small.json").read_bytes()
-    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4))]
+    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4)) if not k.startswith("b2_flush_")]
     assert names[-1] == "neurons_receive" and "neurons_reset" not in names
     monkeypatch.setenv("B2GPU_NO_FUSE", "1")
-    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4))]
+    names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4)) if not k.startswith("b2_flush_")]
     assert names.index("neurons_receive") == names.index("neurons_step") + 1
 
 

@@ -1896,10 +1896,22 @@ struct Engine::Impl {
       uint64_t chunks = 1;
       for (const PathwayDev* pw : fused) chunks = std::max<uint64_t>(chunks, (pw->max_row + 255) / 256);
       o << "  else {\n";
-      o << "    __shared__ u32 s_cnt[" << mine << "];\n";
+      // per pair its count and, fetched in the same round trip, its first id
+      // (most tiles hold at most one spike): the first id's word is read
+      // before the count is known and used once the count says it is part of
+      // this tick's list (exchanged: once its tag is this tick's)
+      o << "    __shared__ u32 s_cnt[" << mine << "], s_id0[" << mine << "];\n";
       o << "    const u32 b = blockIdx.x - " << lb << "u;\n";
-      o << "    if (threadIdx.x < " << mine << "u) { const u32 p = b + threadIdx.x * " << blocks << "u; s_cnt[threadIdx.x] = p < "
-        << pairs << "u ? count_of(p) : 0u; }\n";
+      o << "    if (threadIdx.x < " << mine << "u) {\n      const u32 p = b + threadIdx.x * " << blocks
+        << "u;\n      u32 c = 0, i0 = 0;\n";
+      o << "      if (p < " << pairs << "u) {\n";
+      if (remote)
+        o << "        const u64 v0 = poisoned ? 0ull : b2_ll_load(inbox + slot(p) + 1ull);\n"
+          << "        c = count_of(p);\n"
+          << "        if (c) i0 = (u32)(v0 >> 32) == tag ? (u32)v0 : id_of(p, 0u);\n";
+      else
+        o << "        i0 = id_of(p, 0u);\n        c = count_of(p);\n";
+      o << "      }\n      s_cnt[threadIdx.x] = c;\n      s_id0[threadIdx.x] = i0;\n    }\n";
       o << "    __syncthreads();\n";
       for (size_t k = 0; k < fused.size(); ++k) o << "    u64 events" << k << " = 0;\n";
       // the block's items in (pair, id, chunk) order; warp w takes items
@@ -1910,7 +1922,7 @@ struct Engine::Impl {
       o << "      for (u32 kk = 0; kk < n; ++kk)\n";
       o << "        for (u32 c = 0; c < " << chunks << "u; ++c, ++item) {\n";
       o << "          if (item % " << W << "u != warp) continue;\n";
-      o << "          const u32 s = id_of(p, kk);\n";
+      o << "          const u32 s = kk == 0u ? s_id0[j] : id_of(p, kk);\n";
       for (size_t k = 0; k < fused.size(); ++k) {
         const PathwayDev& pw = *fused[k];
         const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;

@@ -49,6 +49,10 @@ network at 10,000 inputs onto 1,000 neurons (1e6 synapses), because the full
 network's 1 GB document and 1e7 interpreted synapses do not fit a bounded CPU
 run.
 
+--workload c0 / c1 measure configs 0 and 1 (CUBA and COBAHH, 4000 neurons
+each, the committed networks lowered by the reference frontend); their CPU
+arm runs the GPU arm's own window (same ticks), not a shortened one.
+
 --workload brunel measures config 3: the balanced Brunel network of
 4,000,000 f32 LIF neurons, fixed in-degree 800 + 200 (4e9 synapses), a
 homogeneous 1.5 ms (15-tick) delay, J = 0.1 mV, g = 5, PoissonInput of 800
@@ -84,6 +88,10 @@ UNIT = "events/s"
 REFERENCE_TICKS_PER_STEP = 2
 
 WORKLOADS = {
+    "c0": {"neurons": 4000, "indegree": 80, "dtype": "f64", "state_bytes": 24, "target_bytes": 8, "delay": 0,
+           "fixture": "cuba_4k"},
+    "c1": {"neurons": 4000, "indegree": 80, "dtype": "f64", "state_bytes": 48, "target_bytes": 8, "delay": 0,
+           "fixture": "cobahh_4k"},
     "c2": {"neurons": 1_000_000, "indegree": 1000, "dtype": "f64", "state_bytes": 24, "target_bytes": 8,
            "delay": 0},
     "brunel": {"neurons": 4_000_000, "indegree": 1000, "dtype": "f32", "state_bytes": 4, "target_bytes": 4,
@@ -210,8 +218,19 @@ def build_stdp(n_inputs, n_neurons, indegree, ticks, seed=5):
                                          spliced=True)
 
 
+def build_fixture(name, ticks):
+    """A committed network lowered by the reference frontend (configs 0 and
+    1 at their full size), its run extended to `ticks`."""
+    with gzip.open(ROOT / "tests" / "golden" / "models" / f"{name}.json.gz", "rb") as f:
+        doc = json.loads(f.read())
+    _synthetic()._set_run(doc, ticks)
+    return _synthetic().encode(_synthetic().attach_protocol(doc))
+
+
 def build_workload(args, ticks, cpu_sample=False):
     w = WORKLOADS[args.workload]
+    if "fixture" in w:
+        return build_fixture(w["fixture"], ticks)
     if args.workload == "stdp":
         if cpu_sample:
             return build_stdp(w["sample_inputs"], w["sample_neurons"], w["indegree"], ticks)
@@ -224,6 +243,13 @@ def build_workload(args, ticks, cpu_sample=False):
 def describe(args, world):
     """The `config` object of both arms (identical, so the lines compare)."""
     w = WORKLOADS[args.workload]
+    if "fixture" in w:
+        what = ("config 0: CUBA 4000 neurons (examples/CUBA.py), p = 0.02 (~320k synapses), exact-linear, f64"
+                if args.workload == "c0" else
+                "config 1: COBAHH 4000 neurons (examples/COBAHH.py), p = 0.02, exponential Euler, f64")
+        return {"workload": what, "neurons": w["neurons"], "ticks_per_step": TICKS_PER_STEP, "dt_s": DT,
+                "parallelism": "single GPU" if world == 1 else f"{world} GPUs: target-owned partition",
+                "l2": "256 MiB buffer written between timed steps; the network fits in L2"}
     if args.workload == "stdp":
         return {"workload": "config 4: STDP feedforward, 100k Poisson inputs at 15 Hz onto 10k COBA LIF neurons, "
                             "in-degree 1000 (1e7 plastic synapses, on_pre + on_post)",
@@ -256,6 +282,9 @@ def cpu_window(args):
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
     warm = REFERENCE_TICKS_PER_STEP * args.warmup
     timed = REFERENCE_TICKS_PER_STEP * args.steps
+    if "fixture" in WORKLOADS[args.workload]:
+        # a 4000-neuron network: the CPU runs the GPU arm's own window
+        warm, timed = TICKS_PER_STEP * args.warmup, TICKS_PER_STEP * args.steps
     if args.workload == "brunel":
         # nothing is delivered before the 15-tick delay has passed, and a
         # tick of the full network (17M events) takes seconds on one core:
@@ -272,6 +301,8 @@ def cpu_window(args):
     w = WORKLOADS[args.workload]
     network = (f"config 4 scaled to {w['sample_inputs']} inputs onto {w['sample_neurons']} neurons (in-degree "
                f"{w['indegree']})" if args.workload == "stdp" else "the bench's own network (same size and seed)")
+    if "fixture" in w:
+        network += ", the GPU arm's own window"
     if args.workload == "brunel":
         network += ", after the 15-tick delay"
     s["sample"] = (f"ticks {warm}..{warm + timed} of {network}, from tick 0 (the opening transient); "

@@ -1865,12 +1865,24 @@ struct Engine::Impl {
     // ---- layout blocks
     o << "  if (blockIdx.x < " << lb << "u) {\n";
     o << "    __shared__ u32 s_pre[" << pairs + 1 << "];\n";
-    o << "    u32 c = 0;\n";
-    o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
-      << "u + j; if (p < " << pairs << "u) c += count_of(p); }\n";
+    // this thread's counts, kept in registers; exchanged counts are read
+    // all at once first (independent loads in flight together), and only
+    // a word whose tag is not yet this tick's is waited for
+    o << "    u32 cnt[" << per << "];\n";
+    if (remote) {
+      o << "    u64 raw[" << per << "];\n";
+      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
+        << "u + j; raw[j] = p < " << pairs << "u && !poisoned ? b2_ll_load(inbox + slot(p)) : 0ull; }\n";
+      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
+        << "u + j; cnt[j] = p >= " << pairs << "u ? 0u : (u32)(raw[j] >> 32) == tag ? (u32)raw[j] : count_of(p); }\n";
+    } else {
+      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
+        << "u + j; cnt[j] = p < " << pairs << "u ? count_of(p) : 0u; }\n";
+    }
+    o << "    u32 c = 0;\n#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) c += cnt[j];\n";
     o << "    u32 total;\n    u32 off = b2_block_exclusive_scan<" << kThreads << ">(c, &total);\n";
     o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
-      << "u + j; if (p < " << pairs << "u) { s_pre[p] = off; off += count_of(p); } }\n";
+      << "u + j; if (p < " << pairs << "u) { s_pre[p] = off; off += cnt[j]; } }\n";
     o << "    if (threadIdx.x == 0) s_pre[" << pairs << "] = total;\n";
     o << "    __syncthreads();\n";
     o << "    const u64 base = " << P(es.tick_start, "const u64") << "[rel];\n";

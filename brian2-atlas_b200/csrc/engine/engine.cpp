@@ -514,15 +514,15 @@ struct Engine::Impl {
   unsigned sm_count_ = 148;   // multiprocessors of the device (dry runs: a B200's 148)
   // Neurons per block tile of a neuron kernel.  A population that fills at
   // least one wave of resident blocks (SMs x occupancy hint) at kThreads *
-  // npt_ neurons per block keeps that tile: measured on config 2 (1M
-  // neurons, ms per 1000 ticks), 977 tiles of 1024 over 592 resident blocks
-  // run in 19.98, against 21.12 for one wave of 590 tiles of 1696 that each
-  // walk 1.66 chunks and 20.48 for the same with 2 neurons per thread (4
-  // chunks).  A smaller population (one GPU's share of a partitioned
-  // network) is spread over all resident slots in whole 32-neuron words, at
-  // least one block of threads per tile: 125k neurons run as 489 blocks of
-  // 256 instead of 123 blocks of 1024.  The step kernel walks a tile in
-  // chunks of kThreads * npt_, so larger tiles (B2GPU_TILE) are valid too.
+  // npt_ neurons per block keeps that tile: config 2 (1M neurons) runs as
+  // 1954 tiles of 512.  Measured there (ms per 1000 ticks, 4 neurons per
+  // thread): 977 tiles of 1024 over 592 resident blocks ran in 19.98, one
+  // wave of 590 tiles of 1696 that each walk 1.66 chunks in 21.12.  A
+  // smaller population (one GPU's share of a partitioned network) is spread
+  // over all resident slots in whole 32-neuron words, at least one block of
+  // threads per tile: 125k neurons run as 489 blocks of 256 instead of 245
+  // blocks of 512.  The step kernel walks a tile in chunks of kThreads *
+  // npt_, so larger tiles (B2GPU_TILE) are valid too.
   size_t tile_n_for(size_t count) const {
     const size_t max_tile = size_t(kThreads) * npt_;
     if (tile_override_) return tile_override_;

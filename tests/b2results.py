@@ -137,3 +137,40 @@ def read_results(directory, model: dict) -> Results:
             n = e.u64()
             events.append(e.array(np.int64, 2 * n).reshape(n, 2))
     return Results(pops, syn_states, delivered, final_time, events)
+
+
+def describe_difference(a, b, model: dict) -> str:
+    """First differences between two result directories, per section (for
+    assertion messages when two runs that must be identical are not)."""
+    try:
+        ra, rb = read_results(a, model), read_results(b, model)
+    except Exception as exc:  # a layout the reader rejects is itself the finding
+        return f"unreadable results: {exc!r}"
+    out = []
+    names = [p["name"] for p in model["definition"]["populations"]]
+    for name, pa, pb in zip(names, ra.populations, rb.populations):
+        if pa.spikes.shape != pb.spikes.shape or not np.array_equal(pa.spikes, pb.spikes):
+            n = min(len(pa.spikes), len(pb.spikes))
+            bad = np.nonzero(np.any(pa.spikes[:n] != pb.spikes[:n], axis=1))[0]
+            first = int(bad[0]) if len(bad) else n
+            out.append(f"{name}: {len(pa.spikes)} vs {len(pb.spikes)} spikes, first difference at #{first}: "
+                       f"{pa.spikes[first].tolist() if first < len(pa.spikes) else None} vs "
+                       f"{pb.spikes[first].tolist() if first < len(pb.spikes) else None}")
+        for var in pb.samples:
+            sa, sb = pa.samples.get(var), pb.samples[var]
+            if sa is None or sa.shape != sb.shape:
+                out.append(f"{name}.{var} samples: shape {None if sa is None else sa.shape} vs {sb.shape}")
+            elif not np.array_equal(sa, sb):
+                t, r = (int(x[0]) for x in np.nonzero(sa != sb))
+                out.append(f"{name}.{var} samples: first difference at tick {t}, record {r}: {sa[t, r]!r} vs {sb[t, r]!r}")
+        for var in pb.states:
+            if not np.array_equal(pa.states[var], pb.states[var]):
+                i = int(np.nonzero(pa.states[var] != pb.states[var])[0][0])
+                out.append(f"{name}.{var} final: {int(np.sum(pa.states[var] != pb.states[var]))} differ, first at {i}")
+    for s, (sa, sb) in enumerate(zip(ra.synapse_states, rb.synapse_states)):
+        for var in sb:
+            if not np.array_equal(sa[var], sb[var]):
+                out.append(f"synapse {s}.{var}: {int(np.sum(sa[var] != sb[var]))} differ")
+    if ra.delivered != rb.delivered:
+        out.append(f"delivered {ra.delivered} vs {rb.delivered}")
+    return "; ".join(out) or "no difference in the decoded sections"

@@ -20,6 +20,7 @@ import sys
 import pytest
 
 from conftest import GOLDEN, MODELS, ROOT, model_file, run_oracle
+from b2results import describe_difference, load_model
 
 
 def owner(i, n, g):
@@ -201,8 +202,9 @@ def torchrun(world, args, timeout=600):
     return [json.loads(line) for line in proc.stdout.splitlines() if line.startswith("{")]
 
 
-def assert_same_files(a, b):
-    assert (a / "results.bin").read_bytes() == (b / "results.bin").read_bytes()
+def assert_same_files(a, b, model=None):
+    same = (a / "results.bin").read_bytes() == (b / "results.bin").read_bytes()
+    assert same, describe_difference(a, b, load_model(model)) if model else "results.bin differs"
     ea, eb = a / "events.bin", b / "events.bin"
     assert ea.exists() == eb.exists()
     if ea.exists():
@@ -236,7 +238,7 @@ def test_ranks_match_oracle(pkg, oracle, tmp_path, monkeypatch, world, fuse):
     assert len(lines) == len(models)
     for k, m in enumerate(models):
         run_oracle(oracle, m, tmp_path / f"ref{k}")
-        assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}")
+        assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}", m)
         # every rank delivered to its own targets only
         total = json.loads((tmp_path / f"ref{k}" / "summary.json").read_text())["synaptic_events"]
         assert sum(lines[k]["events_per_rank"]) == total
@@ -258,7 +260,7 @@ def test_stdp_ranks_match_one_gpu(pkg, tmp_path, monkeypatch, world, replicate, 
     monkeypatch.setenv("B2GPU_REPLICATE", replicate)
     monkeypatch.setenv("B2GPU_LOCAL_STREAMS", local)
     lines = torchrun(world, ["run", model, tmp_path / "many"])
-    assert_same_files(tmp_path / "many", tmp_path / "one")
+    assert_same_files(tmp_path / "many", tmp_path / "one", model)
     total = json.loads((tmp_path / "one" / "summary.json").read_text())["synaptic_events"]
     assert sum(lines[0]["events_per_rank"]) == total
 

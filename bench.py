@@ -97,7 +97,7 @@ WORKLOADS = {
     "brunel": {"neurons": 4_000_000, "indegree": 1000, "dtype": "f32", "state_bytes": 4, "target_bytes": 4,
                "delay": 15},
     "stdp": {"inputs": 100_000, "neurons": 10_000, "indegree": 1000, "rate_hz": 15.0, "dtype": "f64",
-             "sample_inputs": 10_000, "sample_neurons": 1000},
+             "cpu_warm": 100, "cpu_ticks": 300},
 }
 
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the
@@ -227,13 +227,11 @@ def build_fixture(name, ticks):
     return _synthetic().encode(_synthetic().attach_protocol(doc))
 
 
-def build_workload(args, ticks, cpu_sample=False):
+def build_workload(args, ticks):
     w = WORKLOADS[args.workload]
     if "fixture" in w:
         return build_fixture(w["fixture"], ticks)
     if args.workload == "stdp":
-        if cpu_sample:
-            return build_stdp(w["sample_inputs"], w["sample_neurons"], w["indegree"], ticks)
         return build_stdp(w["inputs"], w["neurons"], w["indegree"], ticks)
     if args.workload == "brunel":
         return build_brunel(args.neurons, args.indegree, ticks)
@@ -275,10 +273,12 @@ def describe(args, world):
                   "L2-resident within a step"}
 
 
-def cpu_window(args):
+def cpu_window(args, model=None):
     """The oracle (CPU restatement of b2-runner) over W warm-up and K timed
     steps of REFERENCE_TICKS_PER_STEP ticks of the workload's network, from
-    tick 0.  Returns the oracle's measurement plus a description."""
+    tick 0.  `model`: the GPU arm's own document (its run is longer than the
+    window; the oracle stops after the window), else one is built.  Returns
+    the oracle's measurement plus a description."""
     subprocess.run(["make", "-s", "-C", str(ROOT / "oracle")], check=True)
     warm = REFERENCE_TICKS_PER_STEP * args.warmup
     timed = REFERENCE_TICKS_PER_STEP * args.steps
@@ -290,17 +290,20 @@ def cpu_window(args):
         # tick of the full network (17M events) takes seconds on one core:
         # start after the delay, at most 10 timed ticks
         warm, timed = WORKLOADS["brunel"]["delay"] + 1 + args.warmup, min(args.steps, 10)
+    if args.workload == "stdp":
+        # the full network: its output neurons fire only after the inputs
+        # have driven them for some ticks; ~60k events per tick after that
+        warm, timed = WORKLOADS["stdp"]["cpu_warm"], WORKLOADS["stdp"]["cpu_ticks"]
     t0 = time.time()
     with tempfile.TemporaryDirectory() as tmp:
         path = Path(tmp) / "cpu_window.json"
-        path.write_bytes(build_workload(args, warm + timed + 1, cpu_sample=True))
+        path.write_bytes(model if model is not None else build_workload(args, warm + timed + 1))
         t_json = time.time() - t0
         out = subprocess.run([str(ROOT / "oracle" / "b2ref"), "--timed", str(warm), str(timed), str(path)],
                              check=True, capture_output=True, text=True)
     s = json.loads(out.stdout)
     w = WORKLOADS[args.workload]
-    network = (f"config 4 scaled to {w['sample_inputs']} inputs onto {w['sample_neurons']} neurons (in-degree "
-               f"{w['indegree']})" if args.workload == "stdp" else "the bench's own network (same size and seed)")
+    network = "the bench's own network (same size and seed)"
     if "fixture" in w:
         network += ", the GPU arm's own window"
     if args.workload == "brunel":
@@ -308,7 +311,7 @@ def cpu_window(args):
     s["sample"] = (f"ticks {warm}..{warm + timed} of {network}, from tick 0 (the opening transient); "
                    f"oracle/b2ref tick loop on one thread; {s['synaptic_events']} events and {s['spikes']} spikes "
                    f"in {s['seconds']:.3f} s; topology build {s['build_seconds']:.1f} s on every host thread, "
-                   f"document {t_json:.1f} s")
+                   + ("the GPU arm's document" if model is not None else f"document {t_json:.1f} s"))
     s["host"] = host_facts()
     return s
 
@@ -436,7 +439,8 @@ def main():
         distributed.connect(eng)
     else:
         eng = pkg.Engine(model, device=local_rank, **eopt)
-    del model
+    if args.no_cpu_baseline or world > 1:
+        del model  # else kept for the CPU leg, which runs the same document
     n_pops = 2 if stdp else 1
     state_pop = 1 if stdp else 0
     st0 = eng.stats()
@@ -566,7 +570,8 @@ def main():
                 traffic = b
     cpu = None
     if not args.no_cpu_baseline and world == 1:
-        s = cpu_window(args)
+        s = cpu_window(args, model)
+        del model
         cpu = {"value": s["synaptic_events"] / s["seconds"], "unit": UNIT, "cores": 1, "kind": "port",
                "sample": s["sample"], "host": s["host"]}
     line = {

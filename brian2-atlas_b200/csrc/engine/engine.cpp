@@ -245,10 +245,11 @@ struct Engine::Impl {
     bool local = false;
     size_t x_off = 0;
     std::vector<int> xptr;
-    // Inbox layout (words per parity half, x_half in all): rank q's tiles
-    // start at word x_base[q]; each of its x_tiles[q] tiles has a count word
-    // and room for x_tile_n[q] ids.  A producing block publishes its tile's
-    // count and ids as soon as it has compacted them.
+    // Inbox layout (words per parity half, x_half in all): rank q's region
+    // starts at word x_base[q] with the count words of its x_tiles[q] tiles
+    // (adjacent, so a reader loads them coalesced), followed by room for
+    // x_tile_n[q] ids per tile.  A producing block publishes its tile's count
+    // and ids as soon as it has compacted them.
     uint64_t x_half = 0;
     std::vector<uint64_t> x_tiles, x_tile_n, x_base;
     // The producing step leaves the tick's list as per-tile counts and ids
@@ -1743,10 +1744,12 @@ struct Engine::Impl {
       const std::string gid =
           ((es->local || exchange) && pd.lo ? std::to_string(pd.lo) + "u + " : std::string()) + "tile * " +
           std::to_string(tile_n) + "u + " + slot_off + " + threadIdx.x";
-      auto peer = [&](const std::string& q) {
+      // rank q's inbox words of this tile: its count, and its first id
+      auto peer = [&](const std::string& q, bool ids) {
         return "(((u64*)g_ptr[" + std::to_string(es->xptr[0]) + " + " + q + "]) + (rel & 1ull) * " +
                std::to_string(es->x_half) + "ull + " + std::to_string(exchange ? es->x_base[size_t(rank)] : 0) +
-               "ull + (u64)tile * " + std::to_string(tile_n + 1) + "ull)";
+               (ids ? "ull + " + std::to_string(tiles) + "ull + (u64)tile * " + std::to_string(tile_n) + "ull)"
+                    : "ull + (u64)tile)");
       };
       o << "  __syncthreads();\n";
       o << "  if (warp == 0) {\n";
@@ -1759,7 +1762,7 @@ struct Engine::Impl {
       o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 w = lane * " << per
         << "u + j; if (w < " << words << "u) { s_off[w] = acc; acc += __popc(s_ballot[w]); } }\n";
       if (exchange)
-        o << "    if (lane == 31) for (u32 q = 0; q < " << world << "u; ++q) b2_ll_store(" << peer("q")
+        o << "    if (lane == 31) for (u32 q = 0; q < " << world << "u; ++q) b2_ll_store(" << peer("q", false)
           << ", x, (u32)(rel + 1ull));\n";
       else
         o << "    if (lane == 31) " << P(es->tile_count, "u32") << "[tile] = x;\n";
@@ -1773,7 +1776,7 @@ struct Engine::Impl {
       o << "      const u32 pos = s_off[slot] + __popc(s_ballot[slot] & ((1u << lane) - 1u));\n";
       // global ids (a multi-GPU list covers the block [lo, lo + count))
       if (exchange)
-        o << "      for (u32 q = 0; q < " << world << "u; ++q) b2_ll_store(" << peer("q") << " + 1ull + pos, " << gid
+        o << "      for (u32 q = 0; q < " << world << "u; ++q) b2_ll_store(" << peer("q", true) << " + pos, " << gid
           << ", (u32)(rel + 1ull));\n";
       else
         o << "      stage[pos] = " << gid << ";\n";
@@ -1845,18 +1848,23 @@ struct Engine::Impl {
       o << "  const u64* inbox = ((const u64*)g_ptr[" << es.xptr[size_t(rank)] << "]) + (rel & 1ull) * " << es.x_half
         << "ull;\n";
       o << "  const u32 tag = (u32)(rel + 1ull);\n";
-      // word of pair p's count in this rank's inbox
+      // words of pair p's count and of its first id in this rank's inbox
       o << "  auto slot = [](u32 p) -> u64 {\n";
       for (int q = world - 1; q >= 0; --q)
         o << "    " << (q ? "if (p >= " + std::to_string(pair_start[size_t(q)]) + "u) " : std::string()) << "return "
-          << es.x_base[size_t(q)] << "ull + (u64)(p - " << pair_start[size_t(q)] << "u) * " << es.x_tile_n[size_t(q)] + 1
-          << "ull;\n";
+          << es.x_base[size_t(q)] << "ull + (u64)(p - " << pair_start[size_t(q)] << "u);\n";
+      o << "  };\n";
+      o << "  auto id_slot = [](u32 p) -> u64 {\n";
+      for (int q = world - 1; q >= 0; --q)
+        o << "    " << (q ? "if (p >= " + std::to_string(pair_start[size_t(q)]) + "u) " : std::string()) << "return "
+          << es.x_base[size_t(q)] + es.x_tiles[size_t(q)] << "ull + (u64)(p - " << pair_start[size_t(q)] << "u) * "
+          << es.x_tile_n[size_t(q)] << "ull;\n";
       o << "  };\n";
       // a thread whose wait has expired waits no more (the run is failed)
       o << "  auto count_of = [&](u32 p) -> u32 { return poisoned || (err & " << kErrExchange
         << "u) ? 0u : b2_ll_wait(inbox + slot(p), tag, " << timeout_ns << "ull, err); };\n";
       o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return poisoned || (err & " << kErrExchange
-        << "u) ? 0u : b2_ll_wait(inbox + slot(p) + 1ull + k, tag, " << timeout_ns << "ull, err); };\n";
+        << "u) ? 0u : b2_ll_wait(inbox + id_slot(p) + k, tag, " << timeout_ns << "ull, err); };\n";
     } else {
       o << "  auto count_of = [&](u32 p) -> u32 { return __ldcg(" << P(es.tile_count, "const u32") << " + p); };\n";
       o << "  auto id_of = [&](u32 p, u32 k) -> u32 { return __ldcg(" << P(es.stage, "const u32") << " + (u64)p * "
@@ -1865,20 +1873,28 @@ struct Engine::Impl {
     // ---- layout blocks
     o << "  if (blockIdx.x < " << lb << "u) {\n";
     o << "    __shared__ u32 s_pre[" << pairs + 1 << "];\n";
-    // this thread's counts, kept in registers; exchanged counts are read
-    // all at once first (independent loads in flight together), and only
-    // a word whose tag is not yet this tick's is waited for
-    o << "    u32 cnt[" << per << "];\n";
+    // every pair's count into s_pre, coalesced (thread x reads pairs x,
+    // x + threads, ...), all loads in flight together; an exchanged word
+    // whose tag is not yet this tick's is waited for (bounded)
+    o << "    {\n";
     if (remote) {
-      o << "    u64 raw[" << per << "];\n";
-      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
-        << "u + j; raw[j] = p < " << pairs << "u && !poisoned ? b2_ll_load(inbox + slot(p)) : 0ull; }\n";
-      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
-        << "u + j; cnt[j] = p >= " << pairs << "u ? 0u : (u32)(raw[j] >> 32) == tag ? (u32)raw[j] : count_of(p); }\n";
+      o << "      u64 raw[" << per << "];\n";
+      o << "#pragma unroll\n      for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = j * " << kThreads
+        << "u + threadIdx.x; raw[j] = p < " << pairs << "u && !poisoned ? b2_ll_load(inbox + slot(p)) : 0ull; }\n";
+      o << "#pragma unroll\n      for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = j * " << kThreads
+        << "u + threadIdx.x; if (p < " << pairs << "u) s_pre[p] = (u32)(raw[j] >> 32) == tag ? (u32)raw[j] : count_of(p); }\n";
     } else {
-      o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
-        << "u + j; cnt[j] = p < " << pairs << "u ? count_of(p) : 0u; }\n";
+      o << "      u32 cv[" << per << "];\n";
+      o << "#pragma unroll\n      for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = j * " << kThreads
+        << "u + threadIdx.x; cv[j] = p < " << pairs << "u ? count_of(p) : 0u; }\n";
+      o << "#pragma unroll\n      for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = j * " << kThreads
+        << "u + threadIdx.x; if (p < " << pairs << "u) s_pre[p] = cv[j]; }\n";
     }
+    o << "    }\n    __syncthreads();\n";
+    // then each thread scans a contiguous run of pairs
+    o << "    u32 cnt[" << per << "];\n";
+    o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
+      << "u + j; cnt[j] = p < " << pairs << "u ? s_pre[p] : 0u; }\n";
     o << "    u32 c = 0;\n#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) c += cnt[j];\n";
     o << "    u32 total;\n    u32 off = b2_block_exclusive_scan<" << kThreads << ">(c, &total);\n";
     o << "#pragma unroll\n    for (u32 j = 0; j < " << per << "u; ++j) { const u32 p = threadIdx.x * " << per
@@ -1918,7 +1934,7 @@ struct Engine::Impl {
         << "u;\n      u32 c = 0, i0 = 0;\n";
       o << "      if (p < " << pairs << "u) {\n";
       if (remote)
-        o << "        const u64 v0 = poisoned ? 0ull : b2_ll_load(inbox + slot(p) + 1ull);\n"
+        o << "        const u64 v0 = poisoned ? 0ull : b2_ll_load(inbox + id_slot(p));\n"
           << "        c = count_of(p);\n"
           << "        if (c) i0 = (u32)(v0 >> 32) == tag ? (u32)v0 : id_of(p, 0u);\n";
       else

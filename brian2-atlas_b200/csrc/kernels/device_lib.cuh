@@ -530,26 +530,6 @@ __device__ __forceinline__ void b2_tile_offsets(u32 tiles, const u32* tile_count
   *total = s_total;
 }
 
-// Publish a rank's staged spike list (last block of its step launch): the
-// tiles' ids in tile order (= ascending global ids) and the count go to the
-// inbox slot `slot` (in words) of every rank's inbox; inbox(q) returns rank
-// q's inbox half of this tick.
-template <int THREADS, class Inbox>
-__device__ void b2_publish_spikes(u32 tiles, u32 tile_n, const u32* tile_count, const u32* stage, Inbox inbox,
-                                  u32 world, u64 slot, u32 tag) {
-  u32 t0, t1, pos, total;
-  b2_tile_offsets<THREADS>(tiles, tile_count, &t0, &t1, &pos, &total);
-  for (u32 t = t0; t < t1; ++t) {
-    const u32 n = __ldcg(tile_count + t);
-    for (u32 k = 0; k < n; ++k) {
-      const u32 id = __ldcg(stage + (u64)t * tile_n + k);
-      for (u32 q = 0; q < world; ++q) b2_ll_store(inbox(q) + slot + 1 + pos + k, id, tag);
-    }
-    pos += n;
-  }
-  if (threadIdx.x < world) b2_ll_store(inbox(threadIdx.x) + slot, total, tag);
-}
-
 // Lay out a tick's staged spike ids: every tile staged its ascending ids at
 // stage[tile * tile_n ...] and its count at tile_count[tile]; the last block
 // of the launch (after all tiles' stores are visible) computes the tiles'

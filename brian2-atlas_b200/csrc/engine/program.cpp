@@ -740,6 +740,37 @@ const char* intop_code(IntOp o) {
   static const char* names[] = {"0", "1", "2", "3", "4", "5", "6", "7", "8"};
   return names[int(o)];
 }
+
+// Thresholds of the binomial inversion over the probabilities tab[x] =
+// P(X = x), x < K (executor.rs:224-268 walks them with u -= P(X = x)): for
+// each x the largest m in [0, 2^53) whose draw u = m * 2^-53 passes the
+// loop's test at x, u - tab[0] - ... - tab[x-1] <= tab[x] (subtractions
+// rounded in that order, as the loop does them), then the running maximum
+// over x.  Passing draws form a prefix because rounded subtraction is
+// non-decreasing in u; m = 0 always passes (its remainders are <= 0).
+std::vector<uint64_t> binomial_thresholds(const std::vector<double>& tab) {
+  std::vector<uint64_t> thr(tab.size());
+  uint64_t run = 0;
+  for (size_t x = 0; x < tab.size(); ++x) {
+    auto passes = [&](uint64_t m) {
+      double u = double(m) * 0x1p-53;
+      for (size_t j = 0; j < x; ++j) u -= tab[j];
+      return u <= tab[x];
+    };
+    uint64_t lo = 0, hi = (uint64_t(1) << 53) - 1;
+    if (passes(hi)) {
+      lo = hi;
+    } else {
+      while (hi - lo > 1) {  // passes(lo) and !passes(hi)
+        const uint64_t mid = lo + (hi - lo) / 2;
+        (passes(mid) ? lo : hi) = mid;
+      }
+    }
+    run = std::max(run, lo);
+    thr[x] = run;
+  }
+  return thr;
+}
 }  // namespace
 
 namespace {
@@ -1008,16 +1039,25 @@ std::string emit_program(const Program& p, const EmitContext& ctx, const std::st
                     const uint64_t xu = x;
                     tab[x] = ((double)(in.n - xu + 1) * prob * tab[x - 1]) / ((double)xu * q);
                   }
+                  // The loop returns the first x whose remainder u - tab[0]
+                  // - ... - tab[x-1] (each subtraction rounded) is <= tab[x].
+                  // IEEE subtraction is non-decreasing in u, so for each x
+                  // the draws passing that test form a prefix of [0, 2^53):
+                  // its last element, found by bisection on the loop's own
+                  // arithmetic, made non-decreasing over x (a draw stopped
+                  // by an earlier x is counted there), is the threshold
+                  // b2_binomial_thr compares the draw's bits against.
+                  const std::vector<uint64_t> thr = binomial_thresholds(tab);
                   std::string body;
-                  for (size_t x = 0; x < K; ++x) body += (x ? ", " : "") + double_literal(tab[x]);
-                  std::string name = "b2_btab_" + std::to_string(ctx.tables->size());
+                  for (size_t x = 0; x < K; ++x) body += (x ? ", " : "") + std::to_string(thr[x]) + "ull";
+                  std::string name = "b2_bthr_" + std::to_string(ctx.tables->size());
                   for (const auto& [nm, def] : *ctx.tables)
                     if (def.find("{" + body + "}") != std::string::npos) name = nm;
-                  // global memory read through L1: lanes of a warp stop at
-                  // different x, which the constant cache would serialise
-                  (*ctx.tables)[name] = "__device__ const double " + name + "[" + std::to_string(K) + "] = {" + body + "};";
-                  expr = "b2_binomial_tab(" + head + ", " + std::to_string(in.n) + "ull, " + name + ", " +
-                         std::to_string(K) + "u, " + (reverse ? "true" : "false") + ")";
+                  (*ctx.tables)[name] = "// inversion thresholds of binomial(n = " + std::to_string(in.n) + ", p = " +
+                                        double_literal(pv) + ")\n__constant__ u64 " + name + "[" + std::to_string(K) +
+                                        "] = {" + body + "};";
+                  expr = "b2_binomial_thr<" + std::to_string(K) + "u>(" + head + ", " + std::to_string(in.n) + "ull, " +
+                         name + ", " + (reverse ? "true" : "false") + ")";
                 } else {
                   expr = "b2_binomial_inv(" + head + ", " + std::to_string(in.n) + "ull, " + double_literal(prob) +
                          ", " + double_literal(q) + ", " + double_literal(qn) + ", " + double_literal(bound) + ", " +

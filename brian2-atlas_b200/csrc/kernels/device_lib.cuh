@@ -55,10 +55,15 @@ __device__ __forceinline__ u64 b2_mix64(u64 v) {
   return v ^ (v >> 31);
 }
 
-__device__ __forceinline__ double b2_uniform_draw(u64 seed, u64 stream, u64 tick, u64 index, u64 draw) {
+// The draw's 53 random bits m; the uniform is exactly m * 2^-53.
+__device__ __forceinline__ u64 b2_uniform_bits(u64 seed, u64 stream, u64 tick, u64 index, u64 draw) {
   u64 c = seed ^ (stream * 0x9e3779b97f4a7c15ull) ^ (tick * 0xd1b54a32d192ed03ull) ^
           (index * 0x94d049bb133111ebull) ^ (draw * 0x369dea0f31a53f85ull);
-  return (double)(b2_mix64(c) >> 11) * (1.0 / 9007199254740992.0);
+  return b2_mix64(c) >> 11;
+}
+
+__device__ __forceinline__ double b2_uniform_draw(u64 seed, u64 stream, u64 tick, u64 index, u64 draw) {
+  return (double)b2_uniform_bits(seed, stream, tick, index, draw) * (1.0 / 9007199254740992.0);
 }
 
 __device__ __forceinline__ double b2_uniform(u64 seed, u64 stream, u64 tick, u64 index) {
@@ -149,21 +154,21 @@ __device__ double b2_binomial_inv(u64 seed, u64 stream, u64 tick, u64 index, u64
   return 0.0;
 }
 
-// The same inversion over a host-built table tab[x] = P(X = x), x < K =
-// floor(bound) + 1, whose entries are the loop's own px values (built with
-// the loop's products and division in the same order), so each step is one
-// compare and one subtraction: identical draws, comparisons and results.
-__device__ __forceinline__ double b2_binomial_tab(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
-                                  const double* __restrict__ tab, u32 K, bool reverse) {
-  u64 draw = 0;
-  for (int restarts = 0; restarts < 1 << 16; ++restarts) {
-    double u = b2_uniform_draw(seed, stream, tick, index, draw);
-    for (u32 x = 0; x < K; ++x) {
-      const double px = __ldg(tab + x);
-      if (u <= px) return (double)(reverse ? n - x : x);
-      u -= px;
-    }
-    draw += 1;
+// The same inversion decided on the draw's integer bits: thr[x] is the
+// largest m whose inversion returns at most x (host-built from the loop's
+// own subtractions, non-decreasing), so the result is the number of
+// thresholds below m, and K of them (m above every threshold) is a restart
+// with the next draw.  Every lane reads thr[j] at the same j (a broadcast);
+// no floating-point operation remains.
+template <u32 K>
+__device__ __forceinline__ double b2_binomial_thr(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
+                                                  const u64* __restrict__ thr, bool reverse) {
+  for (u64 draw = 0; draw < (1ull << 16); ++draw) {
+    const u64 m = b2_uniform_bits(seed, stream, tick, index, draw);
+    u32 x = 0;
+#pragma unroll
+    for (u32 j = 0; j < K; ++j) x += m > thr[j] ? 1u : 0u;
+    if (x < K) return (double)(reverse ? n - x : x);
   }
   return 0.0;
 }

@@ -234,7 +234,7 @@ def test_counted_delivery_plan(pkg, monkeypatch):
     step = src[src.index("_neurons_step(RunCtl"):]
     step = step[:step.index("\n}\n")]
     applies = [m.start() for m in re.finditer(r"if \(run_deferred && cna", step)]
-    draw = step.index("b2_binomial_tab")
+    draw = step.index("b2_binomial_thr")
     assert len(applies) == 2 and applies[-1] < draw < step.index("ls == t_prev") < step.index("d_ls = t - ls")
     assert "neurons_reset" not in names and "neurons_poisson_input" not in names
     monkeypatch.setenv("B2GPU_COUNTED", "0")

@@ -457,6 +457,9 @@ struct Engine::Impl {
     // Diagnostic: deliver constant-addend pathways into f32 state with a
     // compare-and-swap per event instead of counted delivery (same results).
     if (const char* e = std::getenv("B2GPU_COUNTED")) counted_ = std::atoi(e) != 0;
+    // Counted delivery also into f64 state (the map x <- x + w is applied by
+    // the next dense kernel instead of a red.add.f64 per event; same results).
+    if (const char* e = std::getenv("B2GPU_COUNTED_F64")) counted_f64_ = std::atoi(e) != 0;
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -488,6 +491,7 @@ struct Engine::Impl {
   }
   bool no_fuse_ = false;
   bool counted_ = true;  // counted delivery of constant-addend pathways into f32 state
+  bool counted_f64_ = false;  // ... and into f64 state
   bool scatter_warp_ = true;  // constant-addend scatter items per warp (else per block)
   unsigned consumer_blocks_ = 0;  // B2GPU_CONSUMER_BLOCKS: scatter blocks of a fused list consumer (0: the scatter's grid)
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
@@ -3493,8 +3497,10 @@ struct Engine::Impl {
           const size_t tpop = m.synapses[pw->synapse].target_population;
           if (pw != pws.front() && tpop != T) return false;
           T = tpop;
-          for (const auto& ad : pw->atomic_adds)
-            if (m.populations[T].states[ad.state].dtype != DType::F32) return false;
+          for (const auto& ad : pw->atomic_adds) {
+            const DType d = m.populations[T].states[ad.state].dtype;
+            if (d != DType::F32 && !(d == DType::F64 && counted_f64_)) return false;
+          }
         }
         return true;
       };
@@ -3503,14 +3509,31 @@ struct Engine::Impl {
         if (!target_of(specs[i], T)) continue;
         size_t j = i + 1;
         while (j < specs.size() && target_of(specs[j], T2) && T2 == T) ++j;
-        if (j >= specs.size() || specs[j].kind != OpSpec::Kind::Step || steps_[specs[j].index].pop != T) continue;
-        StepSpec& st = steps_[specs[j].index];
+        // The scatters may also end the tick: then the tick's first kernel,
+        // T's state-update step, applies the counts in its prologue ahead of
+        // the programs deferred into it (they follow the scatters in the
+        // schedule, or commute with them), and so does T's flush kernel
+        // after the last tick.
+        const bool wrap = j >= specs.size() && i > 0 && specs[0].kind == OpSpec::Kind::Step &&
+                          steps_[specs[0].index].pop == T && !steps_[specs[0].index].deferred.empty() &&
+                          std::any_of(flushes.begin(), flushes.end(), [&](const Flush& f) { return f.pop == T; });
+        if (!wrap && (j >= specs.size() || specs[j].kind != OpSpec::Kind::Step || steps_[specs[j].index].pop != T))
+          continue;
+        Flush* fl = nullptr;
+        if (wrap)
+          for (Flush& f : flushes)
+            if (f.pop == T && !fl) fl = &f;
         for (size_t k = i; k < j; ++k)
           for (PathwayDev* pw : paths[specs[k].index].pathways) {
             pw->counted = true;
             pw->count_ptr = alloc(std::max<size_t>(pops[T].count, 1) * 4);
             memset_dev(pw->count_ptr, std::max<size_t>(pops[T].count, 1) * 4);
-            st.applies.push_back(pw);
+            if (wrap) {
+              steps_[specs[0].index].deferred_applies.push_back(pw);
+              fl->applies.push_back(pw);
+            } else {
+              steps_[specs[j].index].applies.push_back(pw);
+            }
           }
         for (size_t k = i + 1; k < j;) {
           PathSpec& a = paths[specs[i].index];

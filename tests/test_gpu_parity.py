@@ -282,6 +282,27 @@ def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, 
         assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}")
 
 
+def test_counted_f64_delivery_matches_oracle(pkg, oracle, tmp_path, monkeypatch):
+    """Config 2's f64 constant-addend pathways counted per target instead of
+    one red.add.f64 per event: the scatters end the tick, so the next tick's
+    step applies the counts ahead of the PoissonInput program deferred into
+    it (and the flush kernel after the last tick): byte-identical to the
+    oracle on the fixture and on a fixed in-degree variant at 20k neurons."""
+    import importlib
+    monkeypatch.setenv("B2GPU_COUNTED_F64", "1")
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    template = json.loads((MODELS / "cuba_poisson_small.json").read_text())
+    big = tmp_path / "c2_20k.json"
+    big.write_bytes(synthetic.encode(synthetic.cuba_fixed_indegree(template, n=20000, indegree=1000, ticks=300,
+                                                                   seed=9)))
+    for k, path in enumerate([MODELS / "cuba_poisson_small.json", big]):
+        src = pkg.codegen(path.read_bytes())
+        assert "_count_atomic" in src or "_count(" in src, "the counted plan was not taken"
+        gpu_run(pkg, path, tmp_path / f"gpu{k}")
+        run_oracle(oracle, path, tmp_path / f"ref{k}")
+        assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}")
+
+
 @pytest.mark.parametrize("warp", ["0", "1"])
 def test_unfused_scatter_matches_oracle(pkg, oracle, tmp_path, monkeypatch, warp):
     """Config 2's shape at 20k neurons with the step laying out its own list

@@ -157,7 +157,7 @@ double timestep_threshold(double dt, double target) {
 
 constexpr uint32_t kErrNonfinite = 0x1, kErrTimestep = 0x2, kErrBinomial = 0x4, kErrPoisson = 0x8,
                    kErrRing = 0x10, kErrIntDiv = 0x40, kErrTimedArray = 0x80,
-                   kErrCast = 0x100, kErrExchange = 0x200;
+                   kErrCast = 0x100, kErrExchange = 0x200, kErrBarrier = 0x400;
 
 std::string error_message(uint32_t e) {
   if (e & kErrNonfinite) return "non-finite numeric value";
@@ -169,6 +169,7 @@ std::string error_message(uint32_t e) {
   if (e & kErrCast) return "unsupported cast source";
   if (e & kErrRing) return "spike ring overflow (raise the ring capacity)";
   if (e & kErrExchange) return "spike exchange with a peer GPU timed out (a rank stopped or fell behind)";
+  if (e & kErrBarrier) return "grid barrier of the tick kernel timed out";
   return "device error";
 }
 
@@ -460,6 +461,9 @@ struct Engine::Impl {
     // Counted delivery also into f64 state (the map x <- x + w is applied by
     // the next dense kernel instead of a red.add.f64 per event; same results).
     if (const char* e = std::getenv("B2GPU_COUNTED_F64")) counted_f64_ = std::atoi(e) != 0;
+    // One cooperative launch per chunk runs every tick's kernels as phases
+    // separated by grid barriers (same results).
+    if (const char* e = std::getenv("B2GPU_MEGA")) mega_ = std::atoi(e) != 0;
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -492,6 +496,13 @@ struct Engine::Impl {
   bool no_fuse_ = false;
   bool counted_ = true;  // counted delivery of constant-addend pathways into f32 state
   bool counted_f64_ = false;  // ... and into f64 state
+  // Chunk kernel: the tick's kernels as device functions, called by a
+  // co-resident grid for their virtual blocks, with a grid barrier after each
+  // (B2GPU_MEGA); mega_grid is the launch's block count (0: not available).
+  bool mega_ = false;
+  unsigned mega_grid = 0;
+  cudaKernel_t mega_fn = nullptr;
+  DeviceBuffer mega_bar;
   bool scatter_warp_ = true;  // constant-addend scatter items per warp (else per block)
   unsigned consumer_blocks_ = 0;  // B2GPU_CONSUMER_BLOCKS: scatter blocks of a fused list consumer (0: the scatter's grid)
   bool use_targets_ = true;  // target-ordered delivery for ordered pathways (else one serial thread)
@@ -3075,6 +3086,78 @@ struct Engine::Impl {
     return o.str();
   }
 
+  // The chunk kernel (B2GPU_MEGA): every op of the tick becomes a device
+  // function of a virtual block index, its kernel text with the block index
+  // and grid size replaced, no programmatic-launch instructions, and loads
+  // through L2 (ld.global.cg) instead of the read-only path, since data that
+  // other blocks wrote earlier in the same launch is not read-only.  The
+  // kernel runs ticks k0 .. k0+n-1; per tick and op its blocks take the op's
+  // virtual blocks in turn, then meet at a grid barrier, which orders the ops
+  // as the launch boundaries of the per-op kernels do.  Ops that are not a
+  // single 256-thread kernel (fused multi-population steps) disable it.
+  static void replace_all(std::string& t, const std::string& a, const std::string& b) {
+    for (size_t at = t.find(a); at != std::string::npos; at = t.find(a, at + b.size())) t.replace(at, a.size(), b);
+  }
+  // A kernel's `return` ends the thread; in a device function it only ends
+  // the op for that virtual block, and the thread goes on to the next one.
+  // That is the same unless some threads of a block return while others go
+  // on to a block or warp barrier (bar.sync, a *_sync intrinsic) of the same
+  // op, which in the chunk kernel they would meet at a different place.  An
+  // op qualifies if its only returns are the block-uniform tick guards, or it
+  // has no barrier at all.
+  static bool divergent_return_before_barrier(const std::string& t) {
+    bool divergent = false;
+    std::istringstream in(t);
+    for (std::string line; std::getline(in, line);) {
+      if (line.find("return;") == std::string::npos) continue;
+      const bool uniform = line.rfind("  if ((i64)rel - ", 0) == 0 || line.rfind("  if (rel < ", 0) == 0 ||
+                           line.rfind("  if (tick < ", 0) == 0;
+      divergent |= !uniform;
+    }
+    if (!divergent) return false;
+    for (const char* b : {"__syncthreads", "_sync(", "b2_block_exclusive_scan", "b2_finalize_spikes", "b2_tile_offsets"})
+      if (t.find(b) != std::string::npos) return true;
+    return false;
+  }
+  std::string gen_chunk_kernel(const std::vector<std::string>& texts) {
+    for (size_t i = 0; i < ops.size(); ++i) {
+      size_t globals = 0;
+      for (size_t at = texts[i].find("__global__"); at != std::string::npos; at = texts[i].find("__global__", at + 1))
+        ++globals;
+      if (globals != 1 || ops[i].block != kThreads || texts[i].find("__device__") != std::string::npos ||
+          divergent_return_before_barrier(texts[i])) {
+        mega_ = false;
+        return "";
+      }
+    }
+    std::ostringstream o;
+    for (size_t i = 0; i < ops.size(); ++i) {
+      std::string t = texts[i];
+      const size_t h = t.find("extern \"C\" __global__ void");
+      const size_t brace = t.find('{', h);
+      t.replace(h, brace - h,
+                "__device__ __forceinline__ void " + ops[i].name + "_m(RunCtl* __restrict__ ctl, u32 k, u32 b2_vb, u32 b2_vgrid) ");
+      replace_all(t, "asm volatile(\"griddepcontrol.wait;\" ::: \"memory\");", "");
+      replace_all(t, "asm volatile(\"griddepcontrol.launch_dependents;\" ::: \"memory\");", "");
+      replace_all(t, "blockIdx.x", "b2_vb");
+      replace_all(t, "gridDim.x", "b2_vgrid");
+      replace_all(t, "__ldg(", "__ldcg(");
+      o << t;
+    }
+    const uint64_t timeout_ns = uint64_t(opt.exchange_timeout_ms) * 1000000ull;
+    o << "extern \"C\" __global__ void __launch_bounds__(" << kThreads << ", " << std::max(1u, min_blocks_)
+      << ") b2_chunk(RunCtl* __restrict__ ctl, u32 k0, u32 n, u32* __restrict__ bar) {\n";
+    o << "  u32 target = 0;\n";
+    o << "  for (u32 k = k0; k < k0 + n; ++k) {\n";
+    for (size_t i = 0; i < ops.size(); ++i) {
+      o << "    for (u32 vb = blockIdx.x; vb < " << ops[i].grid << "u; vb += gridDim.x) " << ops[i].name << "_m(ctl, k, vb, "
+        << ops[i].grid << "u);\n";
+      o << "    target += gridDim.x;\n    b2_grid_barrier(bar, target, ctl, " << timeout_ns << "ull);\n";
+    }
+    o << "  }\n}\n";
+    return o.str();
+  }
+
   bool deferred_pending = false;
 
   void build_plan() {
@@ -3710,7 +3793,9 @@ struct Engine::Impl {
     src << kDeviceLibSource << "\n";
     src << "__constant__ u64 g_ptr[PTR_COUNT_PLACEHOLDER];\n\n";
     int kid = 0;
+    std::vector<std::string> op_text;  // each op's kernel source (for the chunk kernel)
     for (auto& o : specs) {
+      const size_t text_from = kernels.str().size();
       std::string nm = "b2_" + std::to_string(kid++) + "_" + sanitize(o.base);
       switch (o.kind) {
         case OpSpec::Kind::Text:
@@ -3801,7 +3886,9 @@ struct Engine::Impl {
         }
       }
       ops.push_back({nm, nullptr, o.grid, o.block});
+      op_text.push_back(kernels.str().substr(text_from));
     }
+    if (mega_) kernels << gen_chunk_kernel(op_text);
     for (size_t f = 0; f < flushes.size(); ++f) {
       size_t p = flushes[f].pop;
       std::string nm = "b2_flush_" + std::to_string(f) + "_" + sanitize(m.populations[p].name);
@@ -3856,6 +3943,16 @@ struct Engine::Impl {
     if (!ptrs.empty()) B2_CUDA(cudaMemcpy(table, ptrs.data(), ptrs.size() * 8, cudaMemcpyHostToDevice));
     for (auto& op : ops) B2_CUDA(cudaLibraryGetKernel(&op.fn, module, op.name.c_str()));
     for (auto& op : flush_ops) B2_CUDA(cudaLibraryGetKernel(&op.fn, module, op.name.c_str()));
+    if (mega_) {
+      B2_CUDA(cudaLibraryGetKernel(&mega_fn, module, "b2_chunk"));
+      int per_sm = 0;
+      B2_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, reinterpret_cast<const void*>(mega_fn), int(kThreads), 0));
+      int sms = 0;
+      B2_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device));
+      mega_grid = unsigned(std::max(0, per_sm) * sms);
+      check(mega_grid > 0, "the chunk kernel cannot be resident on this device");
+      mega_bar = DeviceBuffer(256);
+    }
   }
   size_t cubin_bytes = 0;
 
@@ -3875,6 +3972,27 @@ struct Engine::Impl {
       cfg.numAttrs = use_pdl_ ? 1 : 0;
       B2_CUDA(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(op.fn), args));
     }
+  }
+
+  // One cooperative launch of the chunk kernel for ticks 0 .. n-1 of the
+  // chunk (the driver refuses the launch if the grid cannot be co-resident,
+  // so the grid barriers cannot wait on a block that never runs).
+  void launch_chunk(uint32_t n) {
+    B2_CUDA(cudaMemsetAsync(mega_bar.ptr, 0, 4, stream));
+    void* ctl_ptr = ctl.ptr;
+    void* bar_ptr = mega_bar.ptr;
+    uint32_t k0 = 0;
+    void* args[] = {&ctl_ptr, &k0, &n, &bar_ptr};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(mega_grid);
+    cfg.blockDim = dim3(kThreads);
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    B2_CUDA(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(mega_fn), args));
   }
 
   void ensure_graph(uint32_t ticks) {
@@ -4054,15 +4172,17 @@ struct Engine::Impl {
         tick_host_ = start_tick + cur_rel;
         B2_CUDA(cudaMemcpyAsync(ctl.ptr, &tick_host_, 8, cudaMemcpyHostToDevice, stream));
         st.h2d_bytes += 8;
-        if (opt.use_graphs && n == opt.chunk_ticks) ensure_graph(n);
+        if (!mega_ && opt.use_graphs && n == opt.chunk_ticks) ensure_graph(n);
         B2_CUDA(cudaEventRecord(ev_start, stream));
-        if (opt.use_graphs && n == opt.chunk_ticks) {
+        if (mega_) {
+          launch_chunk(n);
+        } else if (opt.use_graphs && n == opt.chunk_ticks) {
           B2_CUDA(cudaGraphLaunch(graph_exec, stream));
         } else {
           for (uint32_t k = 0; k < n; ++k) launch_tick(k);
         }
         B2_CUDA(cudaEventRecord(ev_stop, stream));
-        st.kernel_launches += uint64_t(n) * ops.size();
+        st.kernel_launches += mega_ ? 1 : uint64_t(n) * ops.size();
         B2_CUDA(cudaStreamSynchronize(stream));
         float ms = 0.f;
         B2_CUDA(cudaEventElapsedTime(&ms, ev_start, ev_stop));

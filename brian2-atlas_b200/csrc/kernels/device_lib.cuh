@@ -33,6 +33,7 @@ typedef unsigned char u8;
 #define B2_ERR_TIMEDARRAY 0x80u
 #define B2_ERR_CAST 0x100u
 #define B2_ERR_EXCHANGE 0x200u
+#define B2_ERR_BARRIER 0x400u
 
 struct RunCtl {
   u64 tick_base;      // absolute tick of graph step k == 0
@@ -158,7 +159,8 @@ __device__ double b2_binomial_inv(u64 seed, u64 stream, u64 tick, u64 index, u64
 // largest m whose inversion returns at most x (host-built from the loop's
 // own subtractions, non-decreasing), so the result is the number of
 // thresholds below m, and K of them (m above every threshold) is a restart
-// with the next draw.  Every lane reads thr[j] at the same j (a broadcast);
+// with the next draw.  The walk stops at the first threshold at or above m:
+// the lanes still walking all read thr[x] at the same x (a broadcast), and
 // no floating-point operation remains.
 template <u32 K>
 __device__ __forceinline__ double b2_binomial_thr(u64 seed, u64 stream, u64 tick, u64 index, u64 n,
@@ -166,8 +168,7 @@ __device__ __forceinline__ double b2_binomial_thr(u64 seed, u64 stream, u64 tick
   for (u64 draw = 0; draw < (1ull << 16); ++draw) {
     const u64 m = b2_uniform_bits(seed, stream, tick, index, draw);
     u32 x = 0;
-#pragma unroll
-    for (u32 j = 0; j < K; ++j) x += m > thr[j] ? 1u : 0u;
+    while (x < K && m > thr[x]) ++x;
     if (x < K) return (double)(reverse ? n - x : x);
   }
   return 0.0;
@@ -497,6 +498,39 @@ __device__ __forceinline__ u32 b2_ll_wait(const u64* p, u32 tag, u64 timeout_ns,
   }
   err |= B2_ERR_EXCHANGE;
   return 0u;
+}
+
+// Grid-wide barrier of a co-resident (cooperatively launched) grid: every
+// block adds one arrival to *bar and waits until *bar reaches `target` (the
+// barriers passed so far times the grid's blocks).  The arrival is a release
+// (fence, then the add) and the wait an acquire, so everything any block
+// wrote before the barrier is visible to every block after it.  Bounded like
+// the exchange waits: on expiry a block stops waiting and the run reports the
+// error, and once one barrier has expired no later barrier waits.
+__device__ __forceinline__ void b2_grid_barrier(u32* bar, u32 target, RunCtl* ctl, u64 timeout_ns) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    atomicAdd(bar, 1u);
+    u32 v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+    if (v < target) {
+      const u64 t0 = b2_globaltimer();
+      for (u64 it = 0; it < (1ull << 28); ++it) {
+        __nanosleep(32);
+        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(bar) : "memory");
+        if (v >= target) break;
+        if ((it & 15) == 0 &&
+            (b2_globaltimer() - t0 > timeout_ns || (*(volatile const u32*)&ctl->error & B2_ERR_BARRIER) != 0u)) {
+          atomicOr(&ctl->error, B2_ERR_BARRIER);
+          break;
+        }
+      }
+      if (v < target) atomicOr(&ctl->error, B2_ERR_BARRIER);
+    }
+    __threadfence();
+  }
+  __syncthreads();
 }
 
 // Exclusive offsets of the tiles' staged counts for the calling thread's

@@ -464,6 +464,9 @@ struct Engine::Impl {
     // One cooperative launch per chunk runs every tick's kernels as phases
     // separated by grid barriers (same results).
     if (const char* e = std::getenv("B2GPU_MEGA")) mega_ = std::atoi(e) != 0;
+    // __launch_bounds__ blocks-per-SM hint of constant-addend scatter kernels
+    // (0: none).
+    if (const char* e = std::getenv("B2GPU_SCATTER_MINBLOCKS")) scatter_min_blocks_ = unsigned(std::atoi(e));
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -500,6 +503,7 @@ struct Engine::Impl {
   // co-resident grid for their virtual blocks, with a grid barrier after each
   // (B2GPU_MEGA); mega_grid is the launch's block count (0: not available).
   bool mega_ = false;
+  unsigned scatter_min_blocks_ = 0;
   unsigned mega_grid = 0;
   cudaKernel_t mega_fn = nullptr;
   DeviceBuffer mega_bar;
@@ -661,6 +665,7 @@ struct Engine::Impl {
       pd.global_count = def.count;
       pd.replicated = replicable(p);
       pd.lo = pd.replicated ? 0 : part_lo(def.count, rank);
+      check(def.count < UINT32_MAX, "populations must hold fewer than 2^32 - 1 neurons");
       pd.count = pd.replicated ? def.count : part_lo(def.count, rank + 1) - pd.lo;
       const size_t lo = pd.lo, n = pd.count;
       pd.start_tick = start_tick;
@@ -2498,11 +2503,13 @@ struct Engine::Impl {
     for (const auto& ad : pw.atomic_adds) gated |= ad.gated;
     const unsigned U = scatter_unroll_;
     std::ostringstream o;
-    o << ind << "u64 tq[" << U << "];\n" << ind << "bool tv[" << U << "];\n";
+    // target state indices in 32 bits (populations hold fewer than 2^32
+    // neurons; the bias wraps like the 64-bit one)
+    o << ind << "u32 tq[" << U << "];\n" << ind << "bool tv[" << U << "];\n";
     o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) {\n";
     o << ind << "  const u64 q = q0 + threadIdx.x + u * " << kThreads << "ull;\n";
     o << ind << "  tv[u] = q < q1;\n";
-    o << ind << "  tq[u] = tv[u] ? (u64)__ldg(other + q) + " << target_bias(def) << "ull : 0ull;\n" << ind << "}\n";
+    o << ind << "  tq[u] = tv[u] ? __ldg(other + q) + " << uint32_t(target_bias(def)) << "u : 0u;\n" << ind << "}\n";
     if (pw.counted) {
       // counted delivery: one event more for the target (the gate and the
       // map are applied by the target's next dense kernel)
@@ -2540,11 +2547,11 @@ struct Engine::Impl {
     bool gated = false;
     for (const auto& ad : pw.atomic_adds) gated |= ad.gated;
     std::ostringstream o;
-    o << ind << "u64 tq[8];\n" << ind << "bool tv[8];\n";
+    o << ind << "u32 tq[8];\n" << ind << "bool tv[8];\n";
     o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) {\n";
     o << ind << "  const u64 q = q0 + lane + u * 32ull;\n";
     o << ind << "  tv[u] = q < q1;\n";
-    o << ind << "  tq[u] = tv[u] ? (u64)__ldg(other + q) + " << target_bias(def) << "ull : 0ull;\n" << ind << "}\n";
+    o << ind << "  tq[u] = tv[u] ? __ldg(other + q) + " << uint32_t(target_bias(def)) << "u : 0u;\n" << ind << "}\n";
     if (pw.counted) {
       o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) if (tv[u]) atomicAdd("
         << P(pw.count_ptr, "u32") << " + tq[u], 1u);\n";
@@ -2585,7 +2592,7 @@ struct Engine::Impl {
     uint64_t chunks = 1;
     for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + span - 1) / span);
     std::ostringstream o;
-    o << kernel_head(name);
+    o << kernel_head(name, scatter_min_blocks_);
     o << "  if ((i64)rel - " << p0.delay << "ll < 0) return;\n  const u64 te = rel - " << p0.delay << "ull;\n";
     o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
     o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";

@@ -241,3 +241,27 @@ def test_counted_delivery_plan(pkg, monkeypatch):
     src = pkg.codegen(load("brunel_small"))
     names = [n.split("_", 2)[2] for n in re.findall(r"__global__ void __launch_bounds__\([^)]*\) (\w+)", src)]
     assert len([n for n in names if n.endswith("_atomic")]) == 2 and "n_ev" not in src
+
+
+def test_chunk_kernel_plan(pkg, monkeypatch):
+    """B2GPU_MEGA: every kernel of the tick becomes a device function of a
+    virtual block (no programmatic-launch instructions, no hardware block
+    index, loads through L2 rather than the read-only path), called by one
+    cooperative chunk kernel with a grid barrier after each op; a plan with an
+    op that is not a single kernel (two populations stepped by one launch)
+    keeps the per-op kernels."""
+    monkeypatch.setenv("B2GPU_MEGA", "1")
+    src = pkg.codegen(load("cuba_poisson_small"))
+    assert "b2_chunk(" in src
+    chunk = src[src.index("b2_chunk("):]
+    ops = re.findall(r"(b2_\d+_\w+)_m\(ctl, k, vb, (\d+)u\);", chunk)
+    assert [o[0] for o in ops] == kernels(src)[:len(ops)] and len(ops) == 2
+    assert chunk.count("b2_grid_barrier(") == len(ops)
+    for name, _ in ops:
+        body = src[src.index(f"void {name}_m("):]
+        body = body[:body.index("\n}\n")]
+        for banned in ("griddepcontrol", "blockIdx.x", "gridDim.x", "__ldg("):
+            assert banned not in body, (name, banned)
+    assert "b2_chunk(" not in pkg.codegen(load("synapse_updates_small"))
+    monkeypatch.delenv("B2GPU_MEGA")
+    assert "b2_chunk(" not in pkg.codegen(load("cuba_poisson_small"))

@@ -1666,6 +1666,9 @@ struct Engine::Impl {
     // storage type and checked finite like one delivery of the reference's
     // (executor.rs:2166-2251 per event); the gate is the target's
     // not_refractory as stored by the delivering tick's threshold
+    // A finite value plus a constant stays non-finite once it is (inf + w =
+    // inf, NaN + w = NaN), so one finite check after the n applications
+    // flags exactly the runs in which some application was non-finite.
     auto emit_apply = [&](size_t a, const std::string& cond) {
       const PathwayDev* pw = all_applies[a];
       o << "  if (" << cond << "cna" << a << "[kk]) {\n    const u32 n_ev = cna" << a << "[kk];\n";
@@ -1678,9 +1681,14 @@ struct Engine::Impl {
           o << v << " = " << v << " + " << double_literal(ad.addend) << ";";
         else
           o << v << " = (float)((double)" << v << " + " << double_literal(ad.addend) << ");";
-        o << " if (!b2_finite((double)" << v << ")) err |= " << kErrNonfinite << "u; }\n";
+        o << " }\n";
       }
-      o << "    }\n  }\n";
+      o << "    }\n";
+      for (const auto& ad : pw->atomic_adds) {
+        const std::string v = "sv" + std::to_string(ad.state);
+        o << "    if (!b2_finite((double)" << v << ")) err |= " << kErrNonfinite << "u;\n";
+      }
+      o << "  }\n";
     };
     // the previous tick's trailing dense kernel, in its order: its applies,
     // its program, its reset of the lanes that tick fired

@@ -3165,8 +3165,10 @@ struct Engine::Impl {
     o << "  u32 target = 0;\n";
     o << "  for (u32 k = k0; k < k0 + n; ++k) {\n";
     for (size_t i = 0; i < ops.size(); ++i) {
-      o << "    for (u32 vb = blockIdx.x; vb < " << ops[i].grid << "u; vb += gridDim.x) " << ops[i].name << "_m(ctl, k, vb, "
-        << ops[i].grid << "u);\n";
+      // a block barrier between virtual blocks: an op's shared arrays are
+      // reused by the block's next virtual block
+      o << "    for (u32 vb = blockIdx.x; vb < " << ops[i].grid << "u; vb += gridDim.x) { " << ops[i].name
+        << "_m(ctl, k, vb, " << ops[i].grid << "u); __syncthreads(); }\n";
       o << "    target += gridDim.x;\n    b2_grid_barrier(bar, target, ctl, " << timeout_ns << "ull);\n";
     }
     o << "  }\n}\n";

@@ -254,7 +254,7 @@ def test_chunk_kernel_plan(pkg, monkeypatch):
     src = pkg.codegen(load("cuba_poisson_small"))
     assert "b2_chunk(" in src
     chunk = src[src.index("b2_chunk("):]
-    ops = re.findall(r"(b2_\d+_\w+)_m\(ctl, k, vb, (\d+)u\);", chunk)
+    ops = re.findall(r"(b2_\d+_\w+)_m\(ctl, k, vb, (\d+)u\); __syncthreads\(\); \}", chunk)
     assert [o[0] for o in ops] == kernels(src)[:len(ops)] and len(ops) == 2
     assert chunk.count("b2_grid_barrier(") == len(ops)
     for name, _ in ops:

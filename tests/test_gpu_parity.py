@@ -16,7 +16,7 @@ import pytest
 
 from conftest import (GOLDEN, MODELS, encode_model, golden_procedural_initializers, model_file, procedural_variant,
                       run_oracle)
-from b2results import load_model, read_results
+from b2results import describe_difference, load_model, read_results
 
 pytestmark = pytest.mark.gpu
 
@@ -37,8 +37,9 @@ def gpu_run(pkg, model_path, outdir, **kw):
         return eng.stats()
 
 
-def assert_same_files(a, b):
-    assert (a / "results.bin").read_bytes() == (b / "results.bin").read_bytes()
+def assert_same_files(a, b, model=None):
+    same = (a / "results.bin").read_bytes() == (b / "results.bin").read_bytes()
+    assert same, describe_difference(a, b, load_model(model)) if model else "results.bin differs"
     ea, eb = a / "events.bin", b / "events.bin"
     assert ea.exists() == eb.exists()
     if ea.exists():
@@ -66,7 +67,7 @@ def test_exact_models_match_oracle(pkg, oracle, tmp_path, name):
     path = model_file(name, tmp_path)
     gpu_run(pkg, path, tmp_path / "gpu")
     run_oracle(oracle, path, tmp_path / "ref")
-    assert_same_files(tmp_path / "gpu", tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref", path)
 
 
 @pytest.mark.parametrize("expr", ["v_pre", "current_pre"])

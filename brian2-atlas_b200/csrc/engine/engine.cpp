@@ -580,14 +580,20 @@ struct Engine::Impl {
   }
   // Device copy of host bytes.  Callers pad empty arrays to one element so
   // every pointer is valid; the data of an empty std::vector may be null, in
-  // which case the padding is zero-filled instead of copied.
+  // which case the padding is zero-filled instead of copied.  The copy is
+  // complete when this returns: callers pass temporaries, and an
+  // asynchronous copy from pageable memory may still read the host buffer
+  // after the call has returned (seen as another buffer's bytes in a state
+  // array when the temporary's heap block was reused).
   int upload(const void* host, size_t bytes) {
     int k = alloc(bytes);
     if (bytes && !opt.dry_run) {
-      if (host)
+      if (host) {
         B2_CUDA(cudaMemcpyAsync(reinterpret_cast<void*>(ptrs[size_t(k)]), host, bytes, cudaMemcpyHostToDevice, stream));
-      else
+        B2_CUDA(cudaStreamSynchronize(stream));
+      } else {
         B2_CUDA(cudaMemsetAsync(reinterpret_cast<void*>(ptrs[size_t(k)]), 0, bytes, stream));
+      }
     }
     return k;
   }

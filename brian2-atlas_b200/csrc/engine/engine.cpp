@@ -352,6 +352,14 @@ struct Engine::Impl {
     // the pathway's map that many times (StepSpec::applies)
     bool counted = false;
     int count_ptr = -1;
+    // Two counted pathways of one launch may share a u32 counter per target
+    // (16 bits each, this pathway's at count_shift) when each delivers fewer
+    // than 2^16 events to one target in a tick: max_indeg bounds that (the
+    // pathway's largest in-degree; a single delay gives each edge at most
+    // one event per tick).
+    bool count_packed = false;
+    int count_shift = 0;
+    uint64_t max_indeg = UINT64_MAX;
   };
   struct SynDev {
     uint64_t edges = 0;        // global edge count (the `N` of synaptic code)
@@ -467,6 +475,7 @@ struct Engine::Impl {
     // __launch_bounds__ blocks-per-SM hint of constant-addend scatter kernels
     // (0: none).
     if (const char* e = std::getenv("B2GPU_SCATTER_MINBLOCKS")) scatter_min_blocks_ = unsigned(std::atoi(e));
+    if (const char* e = std::getenv("B2GPU_PACK_COUNTS")) pack_counts_ = std::atoi(e) != 0;
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -504,6 +513,7 @@ struct Engine::Impl {
   // (B2GPU_MEGA); mega_grid is the launch's block count (0: not available).
   bool mega_ = false;
   unsigned scatter_min_blocks_ = 0;
+  bool pack_counts_ = true;  // B2GPU_PACK_COUNTS: two counted pathways share 16-bit halves of one counter
   unsigned mega_grid = 0;
   cudaKernel_t mega_fn = nullptr;
   DeviceBuffer mega_bar;
@@ -988,6 +998,12 @@ struct Engine::Impl {
           }
           check(idx.size() <= UINT32_MAX, "explicit edge count must fit u32");
           for (size_t i = 0; i < pd.endpoint_count; ++i) pd.max_row = std::max<uint64_t>(pd.max_row, offs[i + 1] - offs[i]);
+          if (pd.is_pre) {
+            std::vector<uint32_t> indeg(def.target_count, 0);
+            uint64_t most = 0;
+            for (size_t k = 0; k < L; ++k) most = std::max<uint64_t>(most, ++indeg[tgt_h[gid(k)]]);
+            pd.max_indeg = most;
+          }
           pd.offsets = upload(offs.data(), offs.size() * 8);
           pd.row_other = upload(row_other.data(), std::max<size_t>(row_other.size(), 1) * 4);
           if (!identity) pd.row_edge = upload(row_edge.data(), std::max<size_t>(row_edge.size(), 1) * 4);
@@ -1001,6 +1017,8 @@ struct Engine::Impl {
             pd.offsets = proc_off;
             pd.row_other = proc_rows;
             pd.max_row = proc_max_row;
+            pd.max_indeg = topo.kind == b2ir::Topology::Kind::FixedIndegree ? uint64_t(topo.indegree)
+                                                                             : uint64_t(topo.edge_count);
             if (!pd.uniform) pd.row_delay = init_delay;  // row position == edge id
           } else if (opt.dry_run) {
             pd.offsets = alloc(0);
@@ -1677,7 +1695,9 @@ struct Engine::Impl {
     // flags exactly the runs in which some application was non-finite.
     auto emit_apply = [&](size_t a, const std::string& cond) {
       const PathwayDev* pw = all_applies[a];
-      o << "  if (" << cond << "cna" << a << "[kk]) {\n    const u32 n_ev = cna" << a << "[kk];\n";
+      const std::string c = "cna" + std::to_string(a) + "[kk]";
+      o << "  if (" << cond << c << ") {\n    const u32 n_ev = "
+        << (pw->count_packed ? "(" + c + " >> " + std::to_string(pw->count_shift) + ") & 65535u" : c) << ";\n";
       o << "    " << P(pw->count_ptr, "u32") << "[i] = 0u;\n";
       o << "    for (u32 r = 0; r < n_ev; ++r) {\n";
       for (const auto& ad : pw->atomic_adds) {
@@ -2528,7 +2548,7 @@ struct Engine::Impl {
       // counted delivery: one event more for the target (the gate and the
       // map are applied by the target's next dense kernel)
       o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) if (tv[u]) atomicAdd("
-        << P(pw.count_ptr, "u32") << " + tq[u], 1u);\n";
+        << P(pw.count_ptr, "u32") << " + tq[u], " << (1u << pw.count_shift) << "u);\n";
       return o.str();
     }
     if (gated) {
@@ -2568,7 +2588,7 @@ struct Engine::Impl {
     o << ind << "  tq[u] = tv[u] ? __ldg(other + q) + " << uint32_t(target_bias(def)) << "u : 0u;\n" << ind << "}\n";
     if (pw.counted) {
       o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) if (tv[u]) atomicAdd("
-        << P(pw.count_ptr, "u32") << " + tq[u], 1u);\n";
+        << P(pw.count_ptr, "u32") << " + tq[u], " << (1u << pw.count_shift) << "u);\n";
       return o.str();
     }
     if (gated) {
@@ -3629,11 +3649,27 @@ struct Engine::Impl {
         if (wrap)
           for (Flush& f : flushes)
             if (f.pop == T && !fl) fl = &f;
+        std::vector<PathwayDev*> group;
+        for (size_t k = i; k < j; ++k)
+          for (PathwayDev* pw : paths[specs[k].index].pathways) group.push_back(pw);
+        const bool packed = pack_counts_ && group.size() == 2 && group[0]->max_indeg < 65536 &&
+                            group[1]->max_indeg < 65536;
+        int shared_count = -1;
+        if (packed) {
+          shared_count = alloc(std::max<size_t>(pops[T].count, 1) * 4);
+          memset_dev(shared_count, std::max<size_t>(pops[T].count, 1) * 4);
+        }
         for (size_t k = i; k < j; ++k)
           for (PathwayDev* pw : paths[specs[k].index].pathways) {
             pw->counted = true;
-            pw->count_ptr = alloc(std::max<size_t>(pops[T].count, 1) * 4);
-            memset_dev(pw->count_ptr, std::max<size_t>(pops[T].count, 1) * 4);
+            if (packed) {
+              pw->count_ptr = shared_count;
+              pw->count_packed = true;
+              pw->count_shift = pw == group[0] ? 0 : 16;
+            } else {
+              pw->count_ptr = alloc(std::max<size_t>(pops[T].count, 1) * 4);
+              memset_dev(pw->count_ptr, std::max<size_t>(pops[T].count, 1) * 4);
+            }
             if (wrap) {
               steps_[specs[0].index].deferred_applies.push_back(pw);
               fl->applies.push_back(pw);

@@ -1652,7 +1652,12 @@ struct Engine::Impl {
     }
     o << "#pragma unroll 1\n  for (u32 ch = 0; ch < " << chunks << "u; ++ch) {\n";
     // ---- load phase
-    auto ld = [&](int ptr, const char* ct) { return "__ldg(" + P(ptr, ct) + " + i)"; };
+    // Loads of state and of anything an earlier kernel of the tick wrote go
+    // through L2 (ld.global.cg), never the read-only path: with programmatic
+    // dependent launch the kernel is resident before its predecessor ends,
+    // and a read-only (ld.global.nc) load may legally be scheduled ahead of
+    // griddepcontrol.wait, reading the value from before that predecessor.
+    auto ld = [&](int ptr, const char* ct) { return "__ldcg(" + P(ptr, ct) + " + i)"; };
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "  " << ct << " sva" << s << "[" << npt << "];\n";
@@ -1854,26 +1859,13 @@ struct Engine::Impl {
     return o.str();
   }
 
-  // Consumer layout of a tick's list (gen_pop_step leaves it as per-tile
-  // counts and ids): pair p = (rank, tile) in rank-then-tile order, which is
-  // ascending neuron order.  No block waits for another:
-  //  * layout blocks (the first `lb` of the grid) each read every pair's
-  //    count (waiting, bounded, for a peer's tagged word where the list is
-  //    exchanged), scan them into the pairs' offsets, so that position g of
-  //    the list lies in the last pair whose offset is <= g, and copy the list
-  //    into the ring (position g -> thread g of the layout blocks); block 0
-  //    writes tick_start[rel + 1].  Rank order is global order, so an
-  //    exchanged list is ascending without a sort (the reference's MPI path
-  //    sorts the gathered ids, mpi_codegen.py:79-82);
-  //  * `fused`: the delay-0 constant-addend pathways of the stream, whose
-  //    result does not depend on the order of events, are delivered by the
-  //    other blocks straight from the tile lists: block b takes pairs b,
-  //    b + blocks, ... (one count read per pair, all of a block's at once),
-  //    and its warps share the block's work items (id, 256-entry row chunk),
-  //    so the scatter needs no ring read, no prefix over all tiles and no
-  //    kernel boundary of its own.
-  std::string gen_consumer(const std::string& name, int stream_id, const std::vector<PathwayDev*>& fused,
-                           unsigned grid, unsigned lb) {
+  // The layout part of a list consumer: the definitions that read the
+  // tick's per-tile counts and ids (this rank's inbox when the list is
+  // exchanged, else the step's tile_count / stage) and the layout blocks
+  // (the first `lb` blocks of the launch) that lay the list out in the ring
+  // and write tick_start[rel + 1].  Used by gen_consumer and by a scatter
+  // kernel that lays out another tick's list alongside its delivery.
+  std::string emit_list_layout(int stream_id, unsigned lb) {
     const EventStreamDev& es = streams[size_t(stream_id)];
     const PopDev& pd = pops[es.pop];
     const bool remote = es.exchanged;
@@ -1889,12 +1881,8 @@ struct Engine::Impl {
       pairs = tiles_for(pd.count);
     }
     check(pairs <= 8192, "spike list layout: too many tiles");
-    check(lb >= 1 && lb <= grid && (fused.empty() ? lb == grid : grid > lb), "spike list layout: bad grid split");
     const unsigned per = unsigned((pairs + kThreads - 1) / kThreads);
-    constexpr unsigned W = kThreads / 32;
     std::ostringstream o;
-    o << kernel_head(name);
-    o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
     if (remote) {
       // once the run has failed (e.g. an earlier wait expired) later ticks
       // must not wait again: their results are discarded anyway
@@ -1968,6 +1956,51 @@ struct Engine::Impl {
     o << "      if (end - " << floor_of(size_t(stream_id)) << " > " << u64lit(es.cap) << ") err |= " << kErrRing
       << "u;\n    }\n";
     o << "  }\n";
+    return o.str();
+  }
+
+  // Consumer layout of a tick's list (gen_pop_step leaves it as per-tile
+  // counts and ids): pair p = (rank, tile) in rank-then-tile order, which is
+  // ascending neuron order.  No block waits for another:
+  //  * layout blocks (the first `lb` of the grid) each read every pair's
+  //    count (waiting, bounded, for a peer's tagged word where the list is
+  //    exchanged), scan them into the pairs' offsets, so that position g of
+  //    the list lies in the last pair whose offset is <= g, and copy the list
+  //    into the ring (position g -> thread g of the layout blocks); block 0
+  //    writes tick_start[rel + 1].  Rank order is global order, so an
+  //    exchanged list is ascending without a sort (the reference's MPI path
+  //    sorts the gathered ids, mpi_codegen.py:79-82);
+  //  * `fused`: the delay-0 constant-addend pathways of the stream, whose
+  //    result does not depend on the order of events, are delivered by the
+  //    other blocks straight from the tile lists: block b takes pairs b,
+  //    b + blocks, ... (one count read per pair, all of a block's at once),
+  //    and its warps share the block's work items (id, 256-entry row chunk),
+  //    so the scatter needs no ring read, no prefix over all tiles and no
+  //    kernel boundary of its own.
+  std::string gen_consumer(const std::string& name, int stream_id, const std::vector<PathwayDev*>& fused,
+                           unsigned grid, unsigned lb) {
+    const EventStreamDev& es = streams[size_t(stream_id)];
+    const PopDev& pd = pops[es.pop];
+    const bool remote = es.exchanged;
+    const uint64_t timeout_ns = uint64_t(opt.exchange_timeout_ms) * 1000000ull;
+    uint64_t pairs = 0;
+    std::vector<uint64_t> pair_start;  // remote: first pair of each rank
+    if (remote) {
+      for (int q = 0; q < world; ++q) {
+        pair_start.push_back(pairs);
+        pairs += es.x_tiles[size_t(q)];
+      }
+    } else {
+      pairs = tiles_for(pd.count);
+    }
+    check(pairs <= 8192, "spike list layout: too many tiles");
+    check(lb >= 1 && lb <= grid && (fused.empty() ? lb == grid : grid > lb), "spike list layout: bad grid split");
+    const unsigned per = unsigned((pairs + kThreads - 1) / kThreads);
+    constexpr unsigned W = kThreads / 32;
+    std::ostringstream o;
+    o << kernel_head(name);
+    o << "  const u32 lane = threadIdx.x & 31u, warp = threadIdx.x >> 5;\n  (void)lane; (void)warp;\n";
+    o << emit_list_layout(stream_id, lb);
     if (!fused.empty()) {
       // ---- scatter blocks
       const unsigned blocks = grid - lb;
@@ -2553,7 +2586,7 @@ struct Engine::Impl {
     }
     if (gated) {
       o << ind << "u8 tg[" << U << "];\n";
-      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) tg[u] = tv[u] ? __ldg("
+      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) tg[u] = tv[u] ? __ldcg("
         << P(tp.not_refractory, "const u8") << " + tq[u]) : (u8)0;\n";
     }
     o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < " << U << "u; ++u) {\n";
@@ -2593,7 +2626,7 @@ struct Engine::Impl {
     }
     if (gated) {
       o << ind << "u8 tg[8];\n";
-      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) tg[u] = tv[u] ? __ldg("
+      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) tg[u] = tv[u] ? __ldcg("
         << P(tp.not_refractory, "const u8") << " + tq[u]) : (u8)0;\n";
     }
     o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) {\n";
@@ -2639,7 +2672,7 @@ struct Engine::Impl {
     else
       o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
     o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
-    o << "    const u32 s = __ldg(ring + (j & " << u64lit(es.mask) << "));\n";
+    o << "    const u32 s = __ldcg(ring + (j & " << u64lit(es.mask) << "));\n";
     for (size_t k = 0; k < pws.size(); ++k) {
       const PathwayDev& pw = *pws[k];
       const size_t lo = pw.endpoint_start, hi = pw.endpoint_start + pw.endpoint_count;
@@ -2737,7 +2770,7 @@ struct Engine::Impl {
       o << "  const u64 items = (b - a) * " << chunks << "ull;\n";
       o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
       o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
-      o << "    const u32 s = __ldg(ring + (j & " << u64lit(es.mask) << "));\n";
+      o << "    const u32 s = __ldcg(ring + (j & " << u64lit(es.mask) << "));\n";
       if (!full) o << "    if (s < " << lo << "u || s >= " << hi << "u) continue;\n";
       o << "    const u32 ep = s - " << lo << "u;\n    const u64 r0 = __ldg(off + ep), r1 = __ldg(off + ep + 1);\n";
       o << "    if (c == 0 && threadIdx.x == 0) events += r1 - r0;\n";
@@ -2778,7 +2811,7 @@ struct Engine::Impl {
           << es.bm_words << "ull;\n";
         if (smem_bm) {
           o << "  __shared__ u32 s_bm[" << es.bm_words << "];\n";
-          o << "  for (u32 w = threadIdx.x; w < " << es.bm_words << "u; w += blockDim.x) s_bm[w] = __ldg(bmw + w);\n";
+          o << "  for (u32 w = threadIdx.x; w < " << es.bm_words << "u; w += blockDim.x) s_bm[w] = __ldcg(bmw + w);\n";
           o << "  __syncthreads();\n";
         }
       } else {
@@ -2796,10 +2829,10 @@ struct Engine::Impl {
         h << "        bool h = false;\n";
         h << "        if (in[u]) {\n          const u32 s = sv[u] + " << pw.endpoint_start << "u;\n";
         if (pw.uniform) {
-          h << "          h = (" << (smem_bm ? "s_bm[s >> 5]" : "__ldg(bmw + (s >> 5))") << " >> (s & 31u)) & 1u;\n";
+          h << "          h = (" << (smem_bm ? "s_bm[s >> 5]" : "__ldcg(bmw + (s >> 5))") << " >> (s & 31u)) & 1u;\n";
         } else {
           h << "          const u64 lag = __ldg(tdel + " << tb << " + u * 32u + lane);\n";
-          h << "          if (lag <= rel) h = (__ldg(" << bm << " + ((rel - lag) % " << es.bm_slots << "ull) * "
+          h << "          if (lag <= rel) h = (__ldcg(" << bm << " + ((rel - lag) % " << es.bm_slots << "ull) * "
             << es.bm_words << "ull + (s >> 5)) >> (s & 31u)) & 1u;\n";
         }
         h << "        }\n        mk[u] = __ballot_sync(0xffffffffu, h);\n      }\n";

@@ -476,6 +476,7 @@ struct Engine::Impl {
     // (0: none).
     if (const char* e = std::getenv("B2GPU_SCATTER_MINBLOCKS")) scatter_min_blocks_ = unsigned(std::atoi(e));
     if (const char* e = std::getenv("B2GPU_PACK_COUNTS")) pack_counts_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_FUSE_LAYOUT")) fuse_layout_ = std::atoi(e) != 0;
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -514,6 +515,7 @@ struct Engine::Impl {
   bool mega_ = false;
   unsigned scatter_min_blocks_ = 0;
   bool pack_counts_ = true;  // B2GPU_PACK_COUNTS: two counted pathways share 16-bit halves of one counter
+  bool fuse_layout_ = true;  // B2GPU_FUSE_LAYOUT: a layout / receive kernel joins the scatter launch before it
   unsigned mega_grid = 0;
   cudaKernel_t mega_fn = nullptr;
   DeviceBuffer mega_bar;
@@ -591,10 +593,7 @@ struct Engine::Impl {
   // Device copy of host bytes.  Callers pad empty arrays to one element so
   // every pointer is valid; the data of an empty std::vector may be null, in
   // which case the padding is zero-filled instead of copied.  The copy is
-  // complete when this returns: callers pass temporaries, and an
-  // asynchronous copy from pageable memory may still read the host buffer
-  // after the call has returned (seen as another buffer's bytes in a state
-  // array when the temporary's heap block was reused).
+  // complete when this returns, so callers may pass temporaries.
   int upload(const void* host, size_t bytes) {
     int k = alloc(bytes);
     if (bytes && !opt.dry_run) {
@@ -2650,7 +2649,12 @@ struct Engine::Impl {
   // block holds eight independent ring -> row bounds -> row -> update chains,
   // each lane loading its eight entries before applying them); with
   // B2GPU_SCATTER_WARP=0 to whole blocks, one entry per thread.
-  std::string gen_atomic_kernel(const std::string& name, const std::vector<PathwayDev*>& pws) {
+  // With layout_sid >= 0 the launch's first lb blocks lay that stream's list
+  // of this tick out in the ring (emit_list_layout; for a list no kernel of
+  // the tick reads, e.g. config 3's, whose deliveries come 15 ticks later)
+  // while the other blocks deliver: one launch instead of two.
+  std::string gen_atomic_kernel(const std::string& name, const std::vector<PathwayDev*>& pws, int layout_sid = -1,
+                                unsigned lb = 0) {
     const PathwayDev& p0 = *pws.front();
     const EventStreamDev& es = streams[size_t(p0.stream)];
     const size_t endpoint_count = m.populations[p0.endpoint_pop].count;
@@ -2660,6 +2664,12 @@ struct Engine::Impl {
     for (const PathwayDev* pw : pws) chunks = std::max<uint64_t>(chunks, (pw->max_row + span - 1) / span);
     std::ostringstream o;
     o << kernel_head(name, scatter_min_blocks_);
+    if (layout_sid >= 0) {
+      o << emit_list_layout(layout_sid, lb);
+      o << "  else {\n";
+    }
+    // delivery blocks: b2_bid of b2_nblk (the blocks after the layout blocks)
+    o << "  const u32 b2_bid = blockIdx.x - " << lb << "u, b2_nblk = gridDim.x - " << lb << "u;\n";
     o << "  if ((i64)rel - " << p0.delay << "ll < 0) return;\n  const u64 te = rel - " << p0.delay << "ull;\n";
     o << "  const u64* ts = " << P(es.tick_start, "const u64") << ";\n  const u64 a = ts[te], b = ts[te + 1];\n";
     o << "  const u32* ring = " << P(es.ring, "const u32") << ";\n";
@@ -2667,10 +2677,10 @@ struct Engine::Impl {
     for (size_t k = 0; k < pws.size(); ++k) o << "  u64 events" << k << " = 0;\n";
     o << "  const u64 items = (b - a) * " << chunks << "ull;\n";
     if (per_warp)
-      o << "  for (u64 w = (u64)blockIdx.x * " << kThreads / 32 << "u + warp; w < items; w += (u64)gridDim.x * "
+      o << "  for (u64 w = (u64)b2_bid * " << kThreads / 32 << "u + warp; w < items; w += (u64)b2_nblk * "
         << kThreads / 32 << "u) {\n";
     else
-      o << "  for (u64 w = blockIdx.x; w < items; w += gridDim.x) {\n";
+      o << "  for (u64 w = b2_bid; w < items; w += b2_nblk) {\n";
     o << "    const u64 j = a + w / " << chunks << "ull;\n    const u64 c = w % " << chunks << "ull;\n";
     o << "    const u32 s = __ldcg(ring + (j & " << u64lit(es.mask) << "));\n";
     for (size_t k = 0; k < pws.size(); ++k) {
@@ -2692,6 +2702,7 @@ struct Engine::Impl {
     for (size_t k = 0; k < pws.size(); ++k)
       o << "  if (" << (per_warp ? "lane" : "threadIdx.x") << " == 0 && events" << k << ") atomicAdd((unsigned long long*)"
         << P(delivered_ptr, "u64") << " + " << pws[k]->delivered_slot << ", events" << k << ");\n";
+    if (layout_sid >= 0) o << "  }\n";
     o << kernel_tail();
     return o.str();
   }
@@ -3071,6 +3082,7 @@ struct Engine::Impl {
     size_t item = 0;                  // evmon: EventMonitor index within its population
     int reads = -1;                   // Text ops: the event stream whose lists they read
     unsigned lb = 1;                  // list consumers: blocks that lay the list out in the ring
+    int layout_sid = -1;              // Path: a stream whose tick list its first lb blocks lay out
   };
   // Deferred work of a population's last tick that a flush kernel applies at
   // the end of a run or before a state read.
@@ -3855,6 +3867,35 @@ struct Engine::Impl {
         }
       }
     }
+    // A layout or receive kernel right after a constant-addend scatter that
+    // reads older ticks of the lists only: the scatter launch lays the list
+    // out in its first blocks (gen_atomic_kernel) instead.  Neither reads
+    // what the other writes (the layout writes ring positions of this tick
+    // and tick_start[rel + 1]; the scatter reads the lists of ticks at least
+    // one back), and on several GPUs the layout blocks wait for the peers'
+    // lists while the other blocks deliver.
+    if (!no_fuse_ && fuse_layout_) {
+      for (size_t i = 1; i < specs.size();) {
+        OpSpec& prev = specs[i - 1];
+        bool ok = specs[i].text == "exchange" && specs[i].fuse_path < 0 && prev.kind == OpSpec::Kind::Path &&
+                  prev.layout_sid < 0;
+        if (ok) {
+          const auto& pws = paths[prev.index].pathways;
+          ok = !(pws.size() == 1 && pws[0]->mode != PathwayDev::Mode::Atomic);
+          for (const PathwayDev* pw : pws)
+            ok = ok && pw->mode == PathwayDev::Mode::Atomic && pw->uniform && !pw->has_pending && pw->delay > 0;
+        }
+        if (!ok) {
+          ++i;
+          continue;
+        }
+        prev.layout_sid = int(specs[i].index);
+        prev.lb = specs[i].lb;
+        prev.grid += specs[i].lb;
+        prev.base += "_" + specs[i].base;
+        specs.erase(specs.begin() + long(i));
+      }
+    }
     // Consecutive step kernels of different populations touch disjoint state
     // (population code reads and writes only its own population), so one
     // launch steps them all: block ranges dispatch to per-population tiles,
@@ -3972,7 +4013,7 @@ struct Engine::Impl {
             kernels << gen_pathway_kernel(nm, body, *ps.pathways[0]);
           } else {
             nm += "_atomic";
-            kernels << gen_atomic_kernel(nm, ps.pathways);
+            kernels << gen_atomic_kernel(nm, ps.pathways, o.layout_sid, o.layout_sid >= 0 ? o.lb : 0);
           }
           break;
         }

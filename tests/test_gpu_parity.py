@@ -283,6 +283,28 @@ def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, 
         assert_same_files(tmp_path / f"gpu{k}", tmp_path / f"ref{k}")
 
 
+@pytest.mark.parametrize("fuse", ["1", "0"])
+def test_brunel_list_layout_in_the_scatter_launch_matches_oracle(pkg, oracle, tmp_path, monkeypatch, fuse):
+    """A population of more than 1024 tiles gets a layout kernel for its
+    list; when the tick's list is read only 15 ticks later (Brunel), that
+    layout runs in the first blocks of the delayed scatter's launch
+    (fuse=1, the default) or as its own kernel (fuse=0).  40k neurons in
+    tiles of 32 (1250 tiles): byte-identical to the oracle either way."""
+    import importlib
+    monkeypatch.setenv("B2GPU_TILE", "32")
+    monkeypatch.setenv("B2GPU_FUSE_LAYOUT", fuse)
+    synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
+    template = json.loads((MODELS / "brunel_small.json").read_text())
+    path = tmp_path / "brunel_40k.json"
+    path.write_bytes(synthetic.encode(synthetic.brunel_fixed_indegree(template, n=40000, indegree=1000, ticks=200,
+                                                                      seed=23)))
+    src = pkg.codegen(path.read_bytes())
+    assert ("neurons_layout(" in src) == (fuse == "0") and "s_pre[" in src
+    gpu_run(pkg, path, tmp_path / "gpu")
+    run_oracle(oracle, path, tmp_path / "ref")
+    assert_same_files(tmp_path / "gpu", tmp_path / "ref", path)
+
+
 def test_counted_f64_delivery_matches_oracle(pkg, oracle, tmp_path, monkeypatch):
     """Config 2's f64 constant-addend pathways counted per target instead of
     one red.add.f64 per event: the scatters end the tick, so the next tick's

@@ -67,13 +67,22 @@ def test_rank_plans(pkg, world, monkeypatch):
 def test_delayed_receive_moves_after_the_delivery(pkg, tmp_path, monkeypatch):
     """Brunel (one 15-tick delay): no kernel reads the tick's own list (the
     reset runs inside the PoissonInput kernel, on the lanes the threshold
-    just fired), so the receive is the tick's last kernel and the peers'
-    lists travel while the delayed deliveries and the Poisson drive run;
-    with no fusion at all (one kernel per node) it stays right after the
-    step."""
+    just fired), so the receive moves behind the delayed delivery and joins
+    its launch: the scatter's first blocks wait for the peers' lists and lay
+    them out while the others deliver older ticks' spikes
+    (B2GPU_FUSE_LAYOUT=0: a receive kernel of its own at the end of the
+    tick); with no fusion at all (one kernel per node) it stays right after
+    the step."""
     data = (MODELS / "brunel_small.json").read_bytes()
+    src = pkg.codegen(data, rank=1, world_size=4)
+    names = [k.split("_", 2)[2] for k in kernels(src) if not k.startswith("b2_flush_")]
+    assert names[-1].endswith("_atomic") and "neurons_reset" not in names and "neurons_receive" not in names
+    last = src[src.index(kernels(src)[-2] + "("):]
+    assert "b2_ll_wait" in last and "s_pre[" in last and "b2_bid" in last
+    monkeypatch.setenv("B2GPU_FUSE_LAYOUT", "0")
     names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4)) if not k.startswith("b2_flush_")]
-    assert names[-1] == "neurons_receive" and "neurons_reset" not in names
+    assert names[-1] == "neurons_receive"
+    monkeypatch.delenv("B2GPU_FUSE_LAYOUT")
     monkeypatch.setenv("B2GPU_NO_FUSE", "1")
     names = [k.split("_", 2)[2] for k in kernels(pkg.codegen(data, rank=1, world_size=4)) if not k.startswith("b2_flush_")]
     assert names.index("neurons_receive") == names.index("neurons_step") + 1

@@ -477,6 +477,7 @@ struct Engine::Impl {
     if (const char* e = std::getenv("B2GPU_SCATTER_MINBLOCKS")) scatter_min_blocks_ = unsigned(std::atoi(e));
     if (const char* e = std::getenv("B2GPU_PACK_COUNTS")) pack_counts_ = std::atoi(e) != 0;
     if (const char* e = std::getenv("B2GPU_FUSE_LAYOUT")) fuse_layout_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_L2_HINTS")) l2_hints_ = std::atoi(e) != 0;
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -516,6 +517,7 @@ struct Engine::Impl {
   unsigned scatter_min_blocks_ = 0;
   bool pack_counts_ = true;  // B2GPU_PACK_COUNTS: two counted pathways share 16-bit halves of one counter
   bool fuse_layout_ = true;  // B2GPU_FUSE_LAYOUT: a layout / receive kernel joins the scatter launch before it
+  bool l2_hints_ = false;    // B2GPU_L2_HINTS: counted scatters stream rows evict-first, counters evict-last
   unsigned mega_grid = 0;
   cudaKernel_t mega_fn = nullptr;
   DeviceBuffer mega_bar;
@@ -2613,14 +2615,21 @@ struct Engine::Impl {
     bool gated = false;
     for (const auto& ad : pw.atomic_adds) gated |= ad.gated;
     std::ostringstream o;
+    const bool hints = l2_hints_ && pw.counted;
     o << ind << "u32 tq[8];\n" << ind << "bool tv[8];\n";
+    if (hints) o << ind << "const u64 pol_rows = b2_policy_evict_first(), pol_cnt = b2_policy_evict_last();\n";
     o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) {\n";
     o << ind << "  const u64 q = q0 + lane + u * 32ull;\n";
     o << ind << "  tv[u] = q < q1;\n";
-    o << ind << "  tq[u] = tv[u] ? __ldg(other + q) + " << uint32_t(target_bias(def)) << "u : 0u;\n" << ind << "}\n";
+    o << ind << "  tq[u] = tv[u] ? " << (hints ? "b2_ld_rows(other + q, pol_rows)" : "__ldg(other + q)") << " + "
+      << uint32_t(target_bias(def)) << "u : 0u;\n" << ind << "}\n";
     if (pw.counted) {
-      o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) if (tv[u]) atomicAdd("
-        << P(pw.count_ptr, "u32") << " + tq[u], " << (1u << pw.count_shift) << "u);\n";
+      if (hints)
+        o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) if (tv[u]) b2_red_add_hint("
+          << P(pw.count_ptr, "u32") << " + tq[u], " << (1u << pw.count_shift) << "u, pol_cnt);\n";
+      else
+        o << ind << "#pragma unroll\n" << ind << "for (u32 u = 0; u < 8u; ++u) if (tv[u]) atomicAdd("
+          << P(pw.count_ptr, "u32") << " + tq[u], " << (1u << pw.count_shift) << "u);\n";
       return o.str();
     }
     if (gated) {

@@ -500,6 +500,29 @@ __device__ __forceinline__ u32 b2_ll_wait(const u64* p, u32 tag, u64 timeout_ns,
   return 0u;
 }
 
+// L2 eviction priorities for a scatter: row entries are read once per tick
+// (evict first), the per-target counters they index are reused by every
+// event (evict last).
+__device__ __forceinline__ u64 b2_policy_evict_first() {
+  u64 pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+__device__ __forceinline__ u64 b2_policy_evict_last() {
+  u64 pol;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+// Build-time data only (the read-only path).
+__device__ __forceinline__ u32 b2_ld_rows(const u32* p, u64 pol) {
+  u32 v;
+  asm volatile("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ void b2_red_add_hint(u32* p, u32 v, u64 pol) {
+  asm volatile("red.global.add.L2::cache_hint.u32 [%0], %1, %2;" ::"l"(p), "r"(v), "l"(pol) : "memory");
+}
+
 // Grid-wide barrier of a co-resident (cooperatively launched) grid: every
 // block adds one arrival to *bar and waits until *bar reaches `target` (the
 // barriers passed so far times the grid's blocks).  The arrival is a release

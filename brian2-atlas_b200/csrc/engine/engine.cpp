@@ -1670,8 +1670,15 @@ struct Engine::Impl {
     o << "#pragma unroll\n  for (u32 kk = 0; kk < " << npt << "u; ++kk) {\n";
     o << "    const u32 i = tile * " << tile_n << "u + " << slot_off << " + threadIdx.x;\n";
     o << "    if (" << in_tile << "i < " << pd.count << "u) {\n";
-    for (size_t a = 0; a < all_applies.size(); ++a)
-      o << "      cna" << a << "[kk] = __ldcg(" << P(all_applies[a]->count_ptr, "const u32") << " + i);\n";
+    for (size_t a = 0; a < all_applies.size(); ++a) {
+      size_t same = a;  // a packed pathway shares the counter word of an earlier one
+      for (size_t b = 0; b < a; ++b)
+        if (all_applies[b]->count_ptr == all_applies[a]->count_ptr) same = std::min(same, b);
+      if (same < a)
+        o << "      cna" << a << "[kk] = cna" << same << "[kk];\n";
+      else
+        o << "      cna" << a << "[kk] = __ldcg(" << P(all_applies[a]->count_ptr, "const u32") << " + i);\n";
+    }
     for (size_t s : used) {
       const char* ct = storage_ctype(def.states[s].dtype);
       o << "      sva" << s << "[kk] = " << ld(pops[p].states[s].ptr, ct) << ";\n";

@@ -517,7 +517,7 @@ struct Engine::Impl {
   unsigned scatter_min_blocks_ = 0;
   bool pack_counts_ = true;  // B2GPU_PACK_COUNTS: two counted pathways share 16-bit halves of one counter
   bool fuse_layout_ = true;  // B2GPU_FUSE_LAYOUT: a layout / receive kernel joins the scatter launch before it
-  bool l2_hints_ = false;    // B2GPU_L2_HINTS: counted scatters stream rows evict-first, counters evict-last
+  bool l2_hints_ = true;     // B2GPU_L2_HINTS: counted scatters stream rows evict-first, counters evict-last
   unsigned mega_grid = 0;
   cudaKernel_t mega_fn = nullptr;
   DeviceBuffer mega_bar;

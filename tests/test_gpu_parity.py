@@ -262,16 +262,21 @@ def test_bucket_delivery_of_crowded_targets(pkg, tmp_path, monkeypatch):
     assert_same_files(tmp_path / "gpu1", tmp_path / "gpu0")
 
 
-@pytest.mark.parametrize("counted,warp", [("0", "1"), ("1", "1"), ("1", "0")])
-def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, monkeypatch, counted, warp):
+@pytest.mark.parametrize("counted,warp,packed,hints", [("0", "1", "1", "1"), ("1", "1", "1", "1"), ("1", "0", "1", "1"),
+                                                     ("1", "1", "0", "0")])
+def test_brunel_counted_and_atomic_delivery_match_oracle(pkg, oracle, tmp_path, monkeypatch, counted, warp, packed,
+                                                         hints):
     """Brunel's f32 constant-addend pathways delivered by per-event
     compare-and-swap (counted=0) or counted per target and applied by the
     PoissonInput kernel (counted=1, the default), with scatter items per warp
-    (the default) or per block: all byte-identical to the oracle, on the
+    (the default) or per block, E and I counts packed into one counter or
+    not, L2 eviction hints or not: all byte-identical to the oracle, on the
     fixture and on a fixed in-degree variant at 20k neurons."""
     import importlib
     monkeypatch.setenv("B2GPU_COUNTED", counted)
     monkeypatch.setenv("B2GPU_SCATTER_WARP", warp)
+    monkeypatch.setenv("B2GPU_PACK_COUNTS", packed)
+    monkeypatch.setenv("B2GPU_L2_HINTS", hints)
     synthetic = importlib.import_module("brian2-atlas_b200.synthetic")
     template = json.loads((MODELS / "brunel_small.json").read_text())
     big = tmp_path / "brunel_20k.json"

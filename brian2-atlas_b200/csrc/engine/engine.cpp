@@ -478,6 +478,7 @@ struct Engine::Impl {
     if (const char* e = std::getenv("B2GPU_PACK_COUNTS")) pack_counts_ = std::atoi(e) != 0;
     if (const char* e = std::getenv("B2GPU_FUSE_LAYOUT")) fuse_layout_ = std::atoi(e) != 0;
     if (const char* e = std::getenv("B2GPU_L2_HINTS")) l2_hints_ = std::atoi(e) != 0;
+    if (const char* e = std::getenv("B2GPU_SCATTER_BLOCKS")) scatter_blocks_ = unsigned(std::atoi(e));
     // Diagnostic: constant-addend scatter items per block, one row entry per
     // thread, instead of per warp (same results).
     if (const char* e = std::getenv("B2GPU_SCATTER_WARP")) scatter_warp_ = std::atoi(e) != 0;
@@ -517,6 +518,7 @@ struct Engine::Impl {
   unsigned scatter_min_blocks_ = 0;
   bool pack_counts_ = true;  // B2GPU_PACK_COUNTS: two counted pathways share 16-bit halves of one counter
   bool fuse_layout_ = true;  // B2GPU_FUSE_LAYOUT: a layout / receive kernel joins the scatter launch before it
+  unsigned scatter_blocks_ = 0;  // B2GPU_SCATTER_BLOCKS: grid of delayed / unfused scatters (0: 1184)
   bool l2_hints_ = true;     // B2GPU_L2_HINTS: counted scatters stream rows evict-first, counters evict-last
   unsigned mega_grid = 0;
   cudaKernel_t mega_fn = nullptr;
@@ -3620,7 +3622,7 @@ struct Engine::Impl {
           o.index = paths.size();
           o.base = code.name;
           bool serial = pw.mode == PathwayDev::Mode::Serial;
-          o.grid = serial ? 1u : 148u * 8u;
+          o.grid = serial ? 1u : (scatter_blocks_ ? scatter_blocks_ : 148u * 8u);
           o.block = serial ? 32u : kThreads;
           if (pw.mode == PathwayDev::Mode::Targets && !pw.tm_events) {  // tm_warps warps per target
             pw.tm_warps = targets_group(pw);
